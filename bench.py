@@ -1,0 +1,466 @@
+"""Batch-one decode benchmark on B200 -- driver contract.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+Workload (config[3]): the miniMoE-shaped model (12 x 768, 12 heads x 64,
+RMSNorm, RoPE, 8 SwiGLU experts of hidden 768, top-2, vocab 50304, tied LM
+head), random init, bf16, paged KV cache (block 16, direct attention), MoE
+direct.  A 512-token random prompt is prefilled once; one bench STEP is the
+greedy decode of 1024 tokens from that prompt (context 513..1536), replaying
+the captured decode-step CUDA graph once per token.  `value` is decode tokens
+per second over K steps (device time, CUDA events, max over ranks).  The
+per-token weight bytes (219 MB) exceed the 126 MB L2, so every step streams
+from HBM.
+
+`e2e` is the same metric through the public API: ``Model.generate`` from a
+host (pinned) prompt tensor to host output tokens, prefill included.
+
+`--impl reference` times the reference algorithm's CPU path (the oracle
+restatement of ``--moe reference`` with a contiguous fp32 KV cache) on the
+host cores on a bounded sample of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(REPO, "moe-inference-engine_b200"))
+sys.path.insert(0, REPO)
+
+METRIC = "batch-1 decode tok/s (bf16, config[3]: 512-token prompt + 1024 greedy tokens)"
+PROMPT_LEN = 512
+NEW_TOKENS = 1024
+# active weight bytes per token in bf16: 2 B x 109,506,048 active params
+ACTIVE_PARAMS = 109_506_048
+KV_BYTES_PER_CTX = 36_864  # 12 layers x 12 heads x 64 x 2 (K+V) x 2 B
+MOE_LAYER_BYTES = 7_090_176  # router 12,288 + 2 experts x 3 x 1,179,648
+
+
+def peaks():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "MEASURED_PEAKS.json hbm_gbs (measured)"
+    return 6650.0, "fallback 6.65 TB/s"
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled every 200 ms during timing."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (FileNotFoundError, OSError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        mhz, maxes, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                mhz.append(float(parts[1]))
+                maxes.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not mhz:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(mhz), "sm_max_mhz": max(maxes), "reasons": sorted(reasons),
+                "samples": len(mhz)}
+
+
+def build_model(device, dtype, seed=0):
+    from moe_engine.model import Model, baseline_config
+
+    torch.manual_seed(seed)
+    model = Model(baseline_config()).eval().to(device=device, dtype=dtype)
+    g = torch.Generator(device=device).manual_seed(seed)
+    with torch.no_grad():
+        for name, p in model.named_parameters():
+            if name.endswith("norm.weight"):
+                p.fill_(1.0)
+            else:
+                p.copy_(torch.randn(p.shape, generator=g, device=device, dtype=torch.float32) * 0.02)
+    return model
+
+
+def time_graph_calls(fn, calls: int, reps: int = 5):
+    """Average device time of fn() when `calls` launches run back to back in a graph."""
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(3):
+            fn()
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(calls):
+            fn()
+    for _ in range(2):
+        g.replay()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(reps):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / 1e3 / (reps * calls)
+
+
+def kernel_rooflines(model, cache, hbm_peak):
+    """Isolated per-kernel device times (graphs of back-to-back launches)."""
+    from moe_engine import fused_moe, paged_attention
+
+    dev = model.token_embedding.weight.device
+    out = {}
+    # MoE: the 12 layers' experts cycled (working set 340 MB > L2)
+    ws = []
+    xs = torch.randn(12, 768, device=dev, dtype=torch.bfloat16)
+    for blk in model.MoEBlocks:
+        moe = blk.moe
+        s = moe._expert_storage
+        ws.append((moe, s))
+    state = {"i": 0}
+
+    def moe_call():
+        i = state["i"] % 12
+        state["i"] += 1
+        moe, s = ws[i]
+        fused_moe.decode(xs[i].view(1, 1, 768), moe.router.weight, s["w1"], None, s["w2"], None,
+                         router_logits=moe._router_logits, expert_ids=moe._expert_ids,
+                         route_weights=moe._route_weights, hidden=moe._expert_hidden, out=moe._direct_out,
+                         w3_base=s["w3"], sync=moe._sync)
+
+    t = time_graph_calls(moe_call, 240)
+    out["moe_decode"] = {"us": t * 1e6, "bytes": MOE_LAYER_BYTES, "gbs": MOE_LAYER_BYTES / t / 1e9}
+    # attention at ctx 1024 (12 layers cycled, paged bf16)
+    q = torch.randn(1, 12, 1, 64, device=dev, dtype=torch.bfloat16)
+    ctx = 1024
+    st2 = {"i": 0}
+
+    def attn_call():
+        i = st2["i"] % 12
+        st2["i"] += 1
+        paged_attention.decode(q, cache, i, ctx)
+
+    if len(cache.block_table) * cache.allocator.block_size >= ctx:
+        t = time_graph_calls(attn_call, 120)
+        b = ctx * 12 * 64 * 2 * 2
+        out["attn_decode_ctx1024"] = {"us": t * 1e6, "bytes": b, "gbs": b / t / 1e9}
+    for v in out.values():
+        v["frac"] = v["gbs"] / hbm_peak
+    return out
+
+
+def run_b200(args, rank, world, device):
+    from moe_engine import capi
+    from moe_engine.decode import greedy_generate  # noqa: F401  (public path is Model.generate)
+
+    dtype = torch.bfloat16
+    hbm_peak, peak_src = peaks()
+    model = build_model(device, dtype)
+    gen = torch.Generator().manual_seed(3 + rank)
+    prompt = torch.randint(0, 50304, (PROMPT_LEN,), generator=gen)
+    max_blocks = -(-(PROMPT_LEN + NEW_TOKENS) // 16)
+    alloc = model.new_block_allocator(num_blocks=max_blocks + 8, block_size=16, attention_mode="direct")
+    runner = model.decode_runner()
+
+    # prefill once, then the device-resident decode loop
+    cache = alloc.new_cache()
+    with torch.no_grad():
+        logits = model(prompt[None].to(device), cache)
+    first = int(logits[0, -1].float().argmax())
+    P = cache.position
+    cache.reserve(P + NEW_TOKENS)
+    graph = runner.graph_for(cache, P + NEW_TOKENS)
+
+    def reset():
+        runner.token.fill_(first)
+        runner.pos.fill_(P)
+        runner.done.zero_()
+        runner.log_count.zero_()
+
+    def one_step():
+        reset()
+        for _ in range(NEW_TOKENS):
+            graph.replay()
+
+    for _ in range(args.warmup):
+        one_step()
+    torch.cuda.synchronize()
+    runner.check_status()
+
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(device.index or 0) as clocks:
+        e0.record()
+        for _ in range(args.steps):
+            one_step()
+        e1.record()
+        torch.cuda.synchronize()
+    elapsed = e0.elapsed_time(e1) / 1e3
+    if world > 1:
+        t = torch.tensor([elapsed], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        elapsed = float(t)
+        torch.distributed.barrier()
+    runner.check_status()
+    tokens = args.steps * NEW_TOKENS * world
+    value = tokens / elapsed
+
+    # per-token latency distribution (events between replays, separate pass)
+    reset()
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(NEW_TOKENS + 1)]
+    evs[0].record()
+    for i in range(NEW_TOKENS):
+        graph.replay()
+        evs[i + 1].record()
+    torch.cuda.synchronize()
+    per_tok = sorted(evs[i].elapsed_time(evs[i + 1]) for i in range(NEW_TOKENS))
+    p50 = per_tok[len(per_tok) // 2]
+    p99 = per_tok[min(len(per_tok) - 1, int(len(per_tok) * 0.99))]
+
+    # end to end through the public API (host prompt -> host tokens)
+    host_prompt = prompt.clone().pin_memory()
+    e2e_times = []
+    out_len = 0
+    for it in range(max(1, min(args.steps, 3)) + 1):
+        c = alloc.new_cache()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        out = model.generate(host_prompt, max_new_tokens=NEW_TOKENS, temperature=0, cache=c)
+        out_host = out.cpu()
+        t1 = time.perf_counter()
+        c.free()
+        out_len = out_host.shape[1]
+        if it > 0:  # first call warms the graph for this cache
+            e2e_times.append(t1 - t0)
+    new_tokens = out_len - PROMPT_LEN
+    e2e_value = new_tokens / statistics.median(e2e_times)
+    if world > 1:
+        t = torch.tensor([e2e_value], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MIN)
+        e2e_value = float(t) * world
+
+    # rooflines
+    step_s = elapsed / (args.steps * NEW_TOKENS)  # seconds per token on each replica
+    weights_bytes = 2 * ACTIVE_PARAMS
+    mean_ctx = PROMPT_LEN + NEW_TOKENS / 2
+    kv_bytes = KV_BYTES_PER_CTX * mean_ctx
+    k_roof = kernel_rooflines(model, cache, hbm_peak) if rank == 0 else {}
+    dominant = "moe_decode"
+    kr = k_roof.get(dominant, {"us": None, "gbs": None, "frac": None, "bytes": MOE_LAYER_BYTES})
+
+    result = {
+        "metric": METRIC,
+        "value": value,
+        "unit": "tok/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": elapsed / args.steps * 1e3,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (random-init weights N(0,0.02), seeded random prompt ids)",
+        "config": {
+            "workload": "config[3] full-model decode, 512-token prompt + 1024 greedy tokens, paged KV bs16, "
+                        "MoE direct, one CUDA-graph replay per token; step = one 1024-token decode",
+            "model": "miniMoE-shaped 12x768, 12 heads x 64, 8 SwiGLU experts top-2, vocab 50304",
+            "global_batch": world,
+            "seq_len": PROMPT_LEN + NEW_TOKENS,
+            "parallelism": f"replicas x{world}",
+            "l2": "inputs larger than L2 (219 MB of weights per token > 126 MB L2)",
+        },
+        "latency_ms_per_token": {"p50": p50, "p99": p99, "mean": sum(per_tok) / len(per_tok)},
+        "step_roofline": {
+            "bound": "hbm",
+            "weights_bytes_per_token": weights_bytes,
+            "kv_bytes_per_token_mean": kv_bytes,
+            "us_per_token": step_s * 1e6,
+            "achieved_gbs_weights": weights_bytes / step_s / 1e9,
+            "frac_weights_only": weights_bytes / step_s / 1e9 / hbm_peak,
+            "frac_total": (weights_bytes + kv_bytes) / step_s / 1e9 / hbm_peak,
+            "peak_gbs": hbm_peak,
+            "peak_source": peak_src,
+        },
+        "roofline": {
+            "kernel": dominant,
+            "bound": "hbm",
+            "achieved": kr["gbs"],
+            "peak": hbm_peak,
+            "unit": "GB/s",
+            "frac": kr["frac"],
+            "traffic": None,
+            "algorithmic_bytes_per_launch": MOE_LAYER_BYTES,
+            "us_per_launch": kr["us"],
+            "peak_source": peak_src + " (burst copy; kernel timed in isolation)",
+        },
+        "kernels": k_roof,
+        "clocks": clocks.summary(),
+        "e2e": {
+            "value": e2e_value,
+            "unit": "tok/s",
+            "h2d_bytes_per_step": PROMPT_LEN * 8,
+            "d2h_bytes_per_step": (PROMPT_LEN + NEW_TOKENS) * 8,
+            "note": "Model.generate from a pinned host prompt to host tokens, prefill included",
+        },
+        "gpu_launches": args.steps * NEW_TOKENS * (4 * 12 + 1),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = cpu_baseline(seconds=args.cpu_seconds)
+    return result
+
+
+def cpu_baseline(seconds: float = 15.0):
+    """The reference path (--moe reference, contiguous fp32 KV) on the host cores.
+
+    Restated by the oracle (the reference engine cannot run BASELINE's
+    architecture unmodified).  Sample: a 32-token prompt prefill (untimed)
+    then greedy decode steps at context ~33+, timed until `seconds` elapse.
+    """
+    import oracle
+
+    ncores = len(os.sched_getaffinity(0))
+    torch.set_num_threads(ncores)
+    P = oracle.init_params(oracle.BASELINE_ARCH, seed=0)
+    dec = oracle.Decoder(P, oracle.BASELINE_ARCH)
+    prompt = torch.randint(0, 50304, (1, 32), generator=torch.Generator().manual_seed(3))
+    with torch.no_grad():
+        logits = dec.forward(prompt)
+        tok = logits[0, -1].argmax().view(1, 1)
+        times = []
+        t_end = time.perf_counter() + seconds
+        while time.perf_counter() < t_end and len(times) < 256:
+            t0 = time.perf_counter()
+            logits = dec.forward(tok)
+            tok = logits[0, -1].argmax().view(1, 1)
+            times.append(time.perf_counter() - t0)
+    times.sort()
+    return {
+        "value": len(times) / sum(times),
+        "unit": "tok/s",
+        "cores": ncores,
+        "kind": "port",
+        "sample": f"BASELINE arch fp32, 32-token prompt, {len(times)} greedy decode steps "
+                  f"(p50 {times[len(times) // 2] * 1e3:.1f} ms/token)",
+    }
+
+
+def run_reference(args):
+    """--impl reference: the reference algorithm's CPU path (oracle port)."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return None
+    steps_t = []
+    cb = None
+    for _ in range(args.warmup):
+        cpu_baseline(seconds=2.0)
+    for _ in range(args.steps):
+        cb = cpu_baseline(seconds=args.cpu_seconds / max(1, args.steps))
+        steps_t.append(cb["value"])
+    value = statistics.median(steps_t)
+    cb["value"] = value
+    return {
+        "metric": METRIC,
+        "value": value,
+        "unit": "tok/s",
+        "n_gpus": int(os.environ.get("WORLD_SIZE", "1")),
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic",
+        "impl": "reference",
+        "config": {"workload": "config[3]-shaped decode, bounded CPU sample (see cpu_baseline.sample)"},
+        "cpu_baseline": cb,
+        "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be at least 3")
+
+    if args.impl == "reference":
+        res = run_reference(args)
+        if res is not None:
+            print(json.dumps(res), flush=True)
+        return
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                             device_id=device)
+    try:
+        res = run_b200(args, rank, world, device)
+        if rank == 0:
+            print(json.dumps(res), flush=True)
+    finally:
+        if world > 1:
+            torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,307 @@
+/*
+ * mie.h -- C ABI of the B200 (sm_100a) batch-one decode kernels for the
+ * miniMoE engine.  Plain C: device pointers, sizes and a cudaStream_t passed
+ * as void*.  No torch types cross this boundary.
+ *
+ * Every entry point returns an int status (MIE_OK == 0).  Kernels also record
+ * device-side failures (bounded waits that gave up, out-of-range block ids,
+ * positions or expert ids) in an optional device status word, which the host
+ * reads after synchronising; no kernel traps.
+ *
+ * Reference interfaces replaced (paths relative to the reference project):
+ *   mie_moe_route        <- src/moe_engine/fused_moe.py:274-309  (route)
+ *   mie_moe_decode       <- src/moe_engine/fused_moe.py:312-380  (decode)
+ *   mie_attn_decode      <- src/moe_engine/paged_attention.py:113-154 (decode),
+ *                           and the contiguous SDPA decode at model.py:261-266
+ *   mie_qkv_rope_store   <- src/moe_engine/model.py:226-234,247 (QKV projection,
+ *                           head split, cache write) plus the norm at
+ *                           model.py:495 and embedding at model.py:557-558
+ *   mie_proj_residual    <- src/moe_engine/model.py:268-269,495 (out_proj + residual)
+ *   mie_lmhead_argmax    <- src/moe_engine/model.py:564-565,600-603 (final norm,
+ *                           tied LM head, greedy argmax)
+ *   mie_decode_step      <- src/moe_engine/model.py:543-565 (Model.forward for one
+ *                           decode token) as one launch sequence
+ */
+#ifndef MIE_H
+#define MIE_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes */
+enum {
+  MIE_OK = 0,
+  MIE_ERR_INVALID = 1,      /* bad argument (null pointer, bad size, misalignment) */
+  MIE_ERR_UNSUPPORTED = 2,  /* shape / dtype combination has no kernel */
+  MIE_ERR_CUDA = 3,         /* a CUDA runtime call failed */
+  MIE_ERR_TIMEOUT = 4,      /* device: a bounded wait gave up */
+  MIE_ERR_RANGE = 5         /* device: block id / position / expert / token out of range */
+};
+
+/* element types */
+enum { MIE_F32 = 0, MIE_BF16 = 1 };
+/* normalisation applied in a kernel prologue */
+enum { MIE_NORM_NONE = 0, MIE_NORM_RMS = 1, MIE_NORM_LAYER = 2 };
+/* expert activation */
+enum { MIE_ACT_GELU = 0, MIE_ACT_SWIGLU = 1 };
+
+/* Fused top-2 MoE decode: norm -> router GEMV -> top-2 (ties to the lower id)
+ * -> 2-way softmax -> selected experts' up GEMVs + activation -> down GEMVs ->
+ * weighted combine (+ residual).  One persistent launch. */
+typedef struct mie_moe_args {
+  int dtype;              /* weights */
+  int x_dtype;            /* x */
+  int out_dtype;          /* out */
+  int hidden_dim;         /* D */
+  int expert_hidden_dim;  /* Hx */
+  int num_experts;        /* E <= 32 */
+  int top_k;              /* must be 2 */
+  int act;                /* MIE_ACT_* */
+  int norm;               /* MIE_NORM_* applied to x before routing */
+  float eps;
+  const void* x;          /* [D] */
+  const void* norm_w;     /* [D] or NULL */
+  const void* norm_b;     /* [D] or NULL */
+  const void* router_w;   /* [E, D] */
+  const void* w1;         /* [E', Hx, D]: GELU fc1 / SwiGLU gate */
+  const void* b1;         /* [E', Hx] or NULL */
+  const void* w3;         /* [E', Hx, D]: SwiGLU up, NULL for GELU */
+  const void* w2;         /* [E', D, Hx]: down */
+  const void* b2;         /* [E', D] or NULL */
+  float* router_logits;   /* [E] fp32 out, or NULL */
+  int32_t* expert_ids;    /* [2] out, or NULL */
+  float* route_weights;   /* [2] fp32 out, or NULL */
+  float* hidden;          /* scratch [2, Hx] fp32 */
+  void* out;              /* [D]: out = (residual ? x : 0) + moe */
+  int residual;
+  uint32_t* sync;         /* 4 words, zeroed once by the caller, reused forever */
+  int32_t* status;        /* device status word, or NULL */
+  const int32_t* skip;    /* device flag: nonzero -> do nothing; or NULL */
+  int grid;               /* CTAs; 0 = one per SM */
+  int expert_base;        /* expert parallel: weights hold experts [base, base+count) */
+  int expert_count;       /* 0 = all experts local */
+} mie_moe_args;
+
+/* Single-query attention over a paged ([nb, H, bs, hd] per layer) or
+ * contiguous ([H, S, hd] per layer) K/V cache, split-K over KV blocks with a
+ * log-sum-exp merge in the same launch (last CTA per head merges). */
+typedef struct mie_attn_args {
+  int kv_dtype;
+  int q_dtype;
+  int out_dtype;
+  int num_heads;
+  int head_dim;           /* 4..128, multiple of 4 */
+  const void* q;          /* [H, hd] */
+  const void* k;          /* layer base */
+  const void* v;          /* layer base */
+  const int32_t* block_table; /* paged: [>= ceil(ctx/bs)] physical ids; NULL: contiguous */
+  int num_blocks;         /* paged: blocks in the pool (range check) */
+  int block_size;         /* paged: tokens per block; contiguous: tile tokens */
+  int64_t stride_block;   /* elements between blocks (contiguous: block_size*stride_tok) */
+  int64_t stride_head;    /* elements between heads */
+  int64_t stride_tok;     /* elements between tokens (== head_dim) */
+  int ctx_len;            /* context length when ctx_dev is NULL */
+  const int32_t* ctx_dev; /* device position p: ctx = *ctx_dev + ctx_dev_offset */
+  int ctx_dev_offset;
+  int max_ctx;            /* upper bound for ctx (range check) */
+  float scale;            /* softmax scale, normally 1/sqrt(hd) */
+  void* out;              /* [H, hd] */
+  float* partials;        /* scratch [H, max_splits, hd + 2] fp32 */
+  uint32_t* counters;     /* [H], zeroed once by the caller */
+  int splits;             /* KV splits per head (>= 1) */
+  int max_splits;
+  int new_token_last;     /* 1: the last token was written by the preceding kernel */
+  int32_t* status;
+  const int32_t* skip;
+} mie_attn_args;
+
+/* Norm + QKV GEMV + RoPE + K/V store into the cache slot of the device
+ * position.  Optionally gathers the token embedding first (layer 0). */
+typedef struct mie_qkv_args {
+  int dtype;              /* weights / embeddings */
+  int kv_dtype;
+  int hidden_dim;
+  int num_heads;
+  int head_dim;
+  int norm;
+  float eps;
+  const void* norm_w;
+  const void* norm_b;
+  float* x;               /* fp32 residual stream [D] */
+  const float* x_add;     /* pending residual delta [D] or NULL (x := x + x_add) */
+  const void* embedding;  /* [V, D] or NULL; when set x := emb[*token] (+ pos_emb[pos]) */
+  const void* pos_embedding; /* [S, D] or NULL */
+  const int64_t* token;
+  int vocab;
+  const void* w;          /* [3D, D] */
+  const void* b;          /* [3D] or NULL */
+  const float* rope_cos;  /* [S, hd/2] or NULL (no RoPE) */
+  const float* rope_sin;
+  const int32_t* pos;     /* device position of the new token */
+  int max_pos;
+  float* q_out;           /* [H*hd] fp32 */
+  void* k_cache;          /* layer base */
+  void* v_cache;
+  const int32_t* block_table; /* NULL: contiguous */
+  int num_blocks;
+  int block_size;
+  int64_t stride_block;
+  int64_t stride_head;
+  int64_t stride_tok;
+  int32_t* status;
+  const int32_t* skip;
+  int grid;
+} mie_qkv_args;
+
+/* out[r] = (accumulate ? out[r] : 0) + add[r] + W[r,:] . in + b[r]  (fp32 in/out). */
+typedef struct mie_proj_args {
+  int dtype;
+  int rows;
+  int cols;
+  const void* w;
+  const void* b;
+  const float* in;
+  float* out;
+  const float* add;       /* [rows] or NULL */
+  int accumulate;
+  int32_t* status;
+  const int32_t* skip;
+  int grid;
+} mie_proj_args;
+
+/* Final norm + tied LM-head GEMV + argmax (ties to the lower id), with the
+ * step's device-side bookkeeping (next token, position, EOS flag, token log). */
+typedef struct mie_lmhead_args {
+  int dtype;
+  int vocab;
+  int hidden_dim;
+  int norm;
+  float eps;
+  const void* norm_w;
+  const void* norm_b;
+  const float* x;
+  const float* x_add;
+  const void* w;          /* [V, D] */
+  const void* b;          /* [V] or NULL */
+  float* logits;          /* [V] fp32 or NULL */
+  float* partial_val;     /* scratch [grid] */
+  int32_t* partial_idx;   /* scratch [grid] */
+  uint32_t* counter;      /* 1 word, zeroed once */
+  int64_t* token_out;     /* argmax id */
+  int32_t* pos;           /* incremented by one when non-NULL */
+  int64_t* tokens_log;    /* optional append log [log_capacity] */
+  int32_t* log_count;
+  int log_capacity;
+  int32_t* done;          /* set to 1 when the token equals eos_id (if non-NULL) */
+  int eos_id;
+  int32_t* status;
+  const int32_t* skip;
+  int grid;
+} mie_lmhead_args;
+
+/* Per-layer weights and cache bases for mie_decode_step. */
+typedef struct mie_layer_desc {
+  const void* attn_norm_w;
+  const void* attn_norm_b;
+  const void* qkv_w;
+  const void* qkv_b;
+  const void* out_w;
+  const void* out_b;
+  const void* moe_norm_w;
+  const void* moe_norm_b;
+  const void* router_w;
+  const void* w1;
+  const void* b1;
+  const void* w3;
+  const void* w2;
+  const void* b2;
+  void* k_cache;
+  void* v_cache;
+} mie_layer_desc;
+
+/* One whole decode step (all layers + LM head) for one token. */
+typedef struct mie_step_desc {
+  int dtype;
+  int kv_dtype;
+  int num_layers;
+  int hidden_dim;
+  int num_heads;
+  int head_dim;
+  int num_experts;
+  int top_k;
+  int expert_hidden_dim;
+  int vocab;
+  int norm;
+  int act;
+  float eps;
+  float attn_scale;
+  int max_pos;
+  const mie_layer_desc* layers;  /* host array [num_layers] */
+  const void* embedding;
+  const void* pos_embedding;
+  const void* final_norm_w;
+  const void* final_norm_b;
+  const void* lm_bias;
+  const float* rope_cos;
+  const float* rope_sin;
+  const int32_t* block_table;    /* NULL: contiguous cache */
+  int num_blocks;
+  int block_size;
+  int64_t kv_stride_block;
+  int64_t kv_stride_head;
+  int64_t kv_stride_tok;
+  int64_t* token;                /* device: input token, overwritten by the argmax */
+  int32_t* pos;                  /* device: position of the input token */
+  int32_t* done;                 /* device EOS flag or NULL */
+  int eos_id;
+  int64_t* tokens_log;
+  int32_t* log_count;
+  int log_capacity;
+  float* x;                      /* scratch fp32 [D] */
+  float* q;                      /* scratch fp32 [H*hd] */
+  float* attn_out;               /* scratch fp32 [H*hd] */
+  float* moe_hidden;             /* scratch fp32 [2, Hx] */
+  float* moe_partial;            /* expert parallel: MoE contribution [D] or NULL */
+  int expert_base;
+  int expert_count;
+  float* attn_partials;          /* scratch [H, max_splits, hd+2] */
+  uint32_t* attn_counters;       /* [H] zeroed once */
+  uint32_t* moe_sync;            /* [4] zeroed once */
+  float* lm_partial_val;         /* [lm_grid] */
+  int32_t* lm_partial_idx;       /* [lm_grid] */
+  uint32_t* lm_counter;          /* [1] zeroed once */
+  float* logits;                 /* [V] or NULL */
+  int32_t* status;
+  int attn_splits;
+  int max_splits;
+  int lm_grid;                   /* 0 = one per SM */
+  int use_pdl;                   /* programmatic dependent launch between kernels */
+} mie_step_desc;
+
+/* Library management */
+int mie_version(void);
+int mie_init(int device);                 /* set kernel attributes; call before any capture */
+const char* mie_status_string(int code);
+int mie_num_sms(int device);
+
+/* Operators (see the table at the top of this file). */
+int mie_moe_route(const mie_moe_args* a, void* stream);
+int mie_moe_decode(const mie_moe_args* a, void* stream);
+int mie_attn_decode(const mie_attn_args* a, void* stream);
+int mie_qkv_rope_store(const mie_qkv_args* a, void* stream);
+int mie_proj_residual(const mie_proj_args* a, void* stream);
+int mie_lmhead_argmax(const mie_lmhead_args* a, void* stream);
+
+/* Whole-step launchers.  mie_decode_layer / mie_decode_head let a caller put a
+ * collective between a layer's MoE and the next consumer (expert parallel). */
+int mie_decode_step(const mie_step_desc* d, void* stream);
+int mie_decode_layer(const mie_step_desc* d, int layer, void* stream);
+int mie_decode_head(const mie_step_desc* d, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MIE_H */

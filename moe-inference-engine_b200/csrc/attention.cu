@@ -1,0 +1,294 @@
+// Single-query (decode) attention over a paged or contiguous K/V cache, sm_100a.
+//
+// Reference: src/moe_engine/paged_attention.py:47-154 (one Triton program per
+// head looping over 128-token tiles with an online softmax) and the contiguous
+// SDPA decode at src/moe_engine/model.py:261-266.
+//
+// Here the context of every head is split over `splits` CTAs (grid = splits x
+// heads) so all SMs stream K/V.  Each CTA moves whole KV blocks into shared
+// memory with TMA bulk copies (a block of one head is bs*hd contiguous
+// elements in the [nb, H, bs, hd] pool; the contiguous [H, S, hd] layout is
+// the same addressing with an identity block map), keeps an online softmax
+// (running max m, normaliser l, accumulator acc), and writes (m, l, acc).  The
+// last CTA of each head (arrival counter, no spinning) merges the partials
+// with a log-sum-exp rescale and writes the output row.
+//
+// Under programmatic dependent launch the blocks that hold only OLD tokens are
+// fetched before waiting on the producer grid (the QKV kernel that writes the
+// newest token); the block holding the newest token is fetched after.
+#include <utility>
+
+#include "kernels.h"
+#include "stream.cuh"
+
+namespace mie {
+
+namespace {
+
+constexpr int kThreads = 128;
+
+template <typename KV, int HD>
+__global__ void __launch_bounds__(kThreads) attn_decode_kernel(const mie_attn_args a, AttnLayout L) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int h = blockIdx.y, s = blockIdx.x, S = gridDim.x, tid = threadIdx.x;
+  const int bs = a.block_size;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + L.off_bar);
+  KV* kvbuf = reinterpret_cast<KV*>(smem + L.off_kv);
+  float* q_s = reinterpret_cast<float*>(smem + L.off_q);
+  float* p_s = reinterpret_cast<float*>(smem + L.off_p);
+  float* acc_s = reinterpret_cast<float*>(smem + L.off_acc);
+  __shared__ float red[kThreads / 32];
+  __shared__ int last_s;
+  const int stage_tok = L.stage_tokens;
+  const int stage_blocks = stage_tok / bs;
+  const size_t stage_elems = (size_t)2 * stage_tok * HD;  // K then V
+  constexpr bool kBulk = (HD * sizeof(KV)) % 16 == 0;
+
+  // Context length.  ctx_dev is the step's device position, written by an
+  // earlier step's LM-head kernel that completed before this grid's producer
+  // started, so it may be read before pdl_wait().
+  int ctx = a.ctx_dev ? (__ldcg(a.ctx_dev) + a.ctx_dev_offset) : a.ctx_len;
+  if (ctx < 1 || ctx > a.max_ctx) {
+    if (tid == 0 && s == 0) set_status(a.status, MIE_ERR_RANGE);
+    ctx = ctx < 1 ? 1 : a.max_ctx;
+  }
+  const int nblk = (ctx + bs - 1) / bs;
+  int b0, b1;
+  split_range(nblk, s, S, &b0, &b1);
+  const int nst = (b1 - b0 + stage_blocks - 1) / stage_blocks;
+  const int deferred = (a.new_token_last && b1 == nblk && nst > 0) ? nst - 1 : -1;
+
+  auto phys_of = [&](int b) -> int64_t {
+    if (!a.block_table) return b;
+    int p = __ldg(a.block_table + b);
+    if (p < 0 || p >= a.num_blocks) {
+      set_status(a.status, MIE_ERR_RANGE);
+      p = 0;
+    }
+    return p;
+  };
+  auto tile_ptr = [&](const void* base, int64_t phys) {
+    return static_cast<const KV*>(base) + phys * a.stride_block + (int64_t)h * a.stride_head;
+  };
+  // thread 0: start the bulk copies of stage `st` into buffer st % nstage.
+  auto issue = [&](int st) {
+    const int bb = b0 + st * stage_blocks, be = min(b1, bb + stage_blocks);
+    KV* dst = kvbuf + (size_t)(st % L.nstage) * stage_elems;
+    uint32_t total = 0;
+    for (int b = bb; b < be; ++b) total += 2u * (uint32_t)(min(bs, ctx - b * bs) * HD * sizeof(KV));
+    uint64_t* br = &bar[st % L.nstage];
+    mbar_arrive_expect_tx(br, total);
+    for (int b = bb; b < be; ++b) {
+      const int64_t p = phys_of(b);
+      const uint32_t n = (uint32_t)(min(bs, ctx - b * bs) * HD * sizeof(KV));
+      const size_t o = (size_t)(b - bb) * bs * HD;
+      bulk_g2s(dst + o, tile_ptr(a.k, p), n, br);
+      bulk_g2s(dst + (size_t)stage_tok * HD + o, tile_ptr(a.v, p), n, br);
+    }
+  };
+
+  int issued = 0;
+  if (kBulk && tid == 0) {
+    for (int i = 0; i < L.nstage; ++i) mbar_init(&bar[i], 1);
+    fence_barrier_init();
+    for (int st = 0; st < min(L.nstage, nst); ++st)
+      if (st != deferred) issue(st);
+  }
+  __syncthreads();
+
+  pdl_wait();
+  if (skip_requested(a.skip)) {
+    if (kBulk && tid == 0)
+      for (int st = 0; st < min(L.nstage, nst); ++st)
+        if (st != deferred) mbar_wait(&bar[st], 0, a.status);
+    __syncthreads();
+    pdl_trigger();
+    return;
+  }
+  pdl_trigger();
+  if (kBulk && tid == 0 && deferred >= 0 && deferred < L.nstage) issue(deferred);
+  issued = min(L.nstage, nst);
+
+  const float scale = a.scale;
+  for (int d = tid; d < HD; d += kThreads) q_s[d] = load_any(a.q, a.q_dtype, (int64_t)h * HD + d);
+
+  constexpr int G = kThreads / HD > 0 ? kThreads / HD : 1;  // PV token groups
+  const int g = tid / HD, dcol = tid % HD;
+  const bool pv_active = tid < G * HD;
+  float acc = 0.f, m_run = -INFINITY, l_run = 0.f;
+  bool failed = false;
+
+  for (int st = 0; st < nst; ++st) {
+    const int bb = b0 + st * stage_blocks, be = min(b1, bb + stage_blocks);
+    const int t0 = bb * bs, ntok = min(be * bs, ctx) - t0;
+    const KV* kst = kvbuf + (size_t)(st % L.nstage) * stage_elems;
+    const KV* vst = kst + (size_t)stage_tok * HD;
+    if constexpr (kBulk) {
+      if (tid == 0) {
+        while (issued < nst && issued < st + L.nstage) {
+          fence_proxy_async_smem();
+          issue(issued);
+          ++issued;
+        }
+      }
+      const bool ok = mbar_wait(&bar[st % L.nstage], (st / L.nstage) & 1, a.status);
+      if (!__syncthreads_and(ok)) {
+        if (tid == 0)
+          for (int j = st + 1; j < min(nst, st + L.nstage); ++j) mbar_wait(&bar[j % L.nstage], (j / L.nstage) & 1, a.status);
+        failed = true;
+        break;
+      }
+    } else {
+      // Rows too narrow for 16-byte bulk copies: plain loads.
+      KV* kw = const_cast<KV*>(kst);
+      KV* vw = const_cast<KV*>(vst);
+      __syncthreads();
+      for (int i = tid; i < ntok * HD; i += kThreads) {
+        const int t = i / HD, d = i % HD, b = (t0 + t) / bs, slot = (t0 + t) % bs;
+        const int64_t p = phys_of(b);
+        kw[i] = tile_ptr(a.k, p)[(int64_t)slot * a.stride_tok + d];
+        vw[i] = tile_ptr(a.v, p)[(int64_t)slot * a.stride_tok + d];
+      }
+      __syncthreads();
+    }
+
+    // scores
+    float mloc = -INFINITY;
+    for (int t = tid; t < ntok; t += kThreads) {
+      float dot = 0.f;
+      if constexpr (kBulk) {
+        constexpr int VPT = 16 / sizeof(KV);
+        constexpr int NV = HD / VPT;
+        const uint4* kr = reinterpret_cast<const uint4*>(kst + (size_t)t * HD);
+#pragma unroll
+        for (int j = 0; j < NV; ++j) {
+          const int v = (j + t) % NV;  // rotate the start chunk: spreads banks
+          dot = dot_vec(kr[v], q_s + v * VPT, dot, (const KV*)nullptr);
+        }
+      } else {
+#pragma unroll
+        for (int d = 0; d < HD; ++d) dot = fmaf(Elem<KV>::to_f(kst[(size_t)t * HD + d]), q_s[d], dot);
+      }
+      const float sc = dot * scale;
+      p_s[t] = sc;
+      mloc = fmaxf(mloc, sc);
+    }
+    const float m_stage = block_max(mloc, red);
+    const float m_new = fmaxf(m_run, m_stage);
+    const float alpha = (m_run == -INFINITY) ? 0.f : expf(m_run - m_new);
+    float lsum = 0.f;
+    for (int t = tid; t < ntok; t += kThreads) {
+      const float p = expf(p_s[t] - m_new);
+      p_s[t] = p;
+      lsum += p;
+    }
+    const float l_stage = block_sum(lsum, red);  // ends with p_s visible to all
+    l_run = l_run * alpha + l_stage;
+    m_run = m_new;
+    if (pv_active) {
+      acc *= alpha;
+      for (int t = g; t < ntok; t += G) acc = fmaf(p_s[t], Elem<KV>::to_f(vst[(size_t)t * HD + dcol]), acc);
+    }
+    __syncthreads();
+  }
+  if (failed) return;
+
+  // combine the PV token groups
+  if (pv_active) acc_s[g * HD + dcol] = acc;
+  __syncthreads();
+  float* part = a.partials + ((size_t)h * a.max_splits + s) * (HD + 2);
+  for (int d = tid; d < HD; d += kThreads) {
+    float v = 0.f;
+    for (int gg = 0; gg < G; ++gg) v += acc_s[gg * HD + d];
+    if (S == 1)
+      store_any(a.out, a.out_dtype, (int64_t)h * HD + d, v / l_run);
+    else
+      part[2 + d] = v;
+  }
+  if (S == 1) return;
+  if (tid == 0) {
+    part[0] = m_run;
+    part[1] = l_run;
+  }
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) last_s = (atom_add_acq_rel_gpu(a.counters + h, 1u) == (uint32_t)(S - 1));
+  __syncthreads();
+  if (!last_s) return;
+  __threadfence();
+  // log-sum-exp merge of the S partials of this head
+  const float* hp = a.partials + (size_t)h * a.max_splits * (HD + 2);
+  float M = -INFINITY;
+  for (int j = 0; j < S; ++j) M = fmaxf(M, __ldcg(hp + (size_t)j * (HD + 2)));
+  float Lsum = 0.f;
+  for (int j = 0; j < S; ++j) {
+    const float mj = __ldcg(hp + (size_t)j * (HD + 2));
+    if (mj != -INFINITY) Lsum += __ldcg(hp + (size_t)j * (HD + 2) + 1) * expf(mj - M);
+  }
+  for (int d = tid; d < HD; d += kThreads) {
+    float o = 0.f;
+    for (int j = 0; j < S; ++j) {
+      const float mj = __ldcg(hp + (size_t)j * (HD + 2));
+      if (mj != -INFINITY) o += __ldcg(hp + (size_t)j * (HD + 2) + 2 + d) * expf(mj - M);
+    }
+    store_any(a.out, a.out_dtype, (int64_t)h * HD + d, o / Lsum);
+  }
+  if (tid == 0) a.counters[h] = 0u;  // ready for the next launch
+}
+
+template <typename KV>
+void* pick(int hd) {
+  switch (hd) {
+    case 4: return (void*)attn_decode_kernel<KV, 4>;
+    case 8: return (void*)attn_decode_kernel<KV, 8>;
+    case 16: return (void*)attn_decode_kernel<KV, 16>;
+    case 32: return (void*)attn_decode_kernel<KV, 32>;
+    case 64: return (void*)attn_decode_kernel<KV, 64>;
+    case 96: return (void*)attn_decode_kernel<KV, 96>;
+    case 128: return (void*)attn_decode_kernel<KV, 128>;
+    default: return nullptr;
+  }
+}
+
+}  // namespace
+
+AttnLayout attn_layout(const mie_attn_args& a) {
+  const int esz = a.kv_dtype == MIE_BF16 ? 2 : 4;
+  AttnLayout L{};
+  // ~32 KB of K+V per stage, a whole number of blocks (at least one).
+  const int per_tok = 2 * a.head_dim * esz;
+  int st = (32 * 1024 / per_tok) / a.block_size * a.block_size;
+  if (st < a.block_size) st = a.block_size;
+  L.stage_tokens = st;
+  L.nstage = 3;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    off = (off + 127) & ~size_t(127);
+    const size_t at = off;
+    off += bytes;
+    return (uint32_t)at;
+  };
+  L.off_bar = take(sizeof(uint64_t) * L.nstage);
+  L.off_kv = take((size_t)L.nstage * per_tok * st);
+  L.off_q = take(sizeof(float) * a.head_dim);
+  L.off_p = take(sizeof(float) * st);
+  L.off_acc = take(sizeof(float) * (kThreads > a.head_dim ? kThreads : a.head_dim));
+  L.smem = (uint32_t)((off + 127) & ~size_t(127));
+  return L;
+}
+
+int attn_decode_launch(const mie_attn_args& a, const AttnLayout& L, cudaStream_t st, bool pdl) {
+  void* k = a.kv_dtype == MIE_BF16 ? pick<__nv_bfloat16>(a.head_dim) : pick<float>(a.head_dim);
+  if (!k) return MIE_ERR_UNSUPPORTED;
+  using K = void (*)(const mie_attn_args, AttnLayout);
+  return launch(reinterpret_cast<K>(k), dim3(a.splits, a.num_heads), dim3(kThreads), L.smem, st, pdl, a, L);
+}
+
+void attn_set_attributes() {
+  for (int hd : {4, 8, 16, 32, 64, 96, 128}) {
+    cudaFuncSetAttribute(pick<float>(hd), cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
+    cudaFuncSetAttribute(pick<__nv_bfloat16>(hd), cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
+  }
+}
+
+}  // namespace mie

@@ -1,0 +1,413 @@
+// extern "C" entry points of libmie.so (declared in include/mie.h): argument
+// validation, launch geometry, and the decode-step launch sequence.
+#include <mutex>
+
+#include "kernels.h"
+
+namespace mie {
+
+int num_sms() {
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (!cached[dev]) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cached[dev] = n > 0 ? n : 148;
+  }
+  return cached[dev];
+}
+
+namespace {
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+int esize(int dtype) { return dtype == MIE_BF16 ? 2 : 4; }
+bool dtype_ok(int d) { return d == MIE_F32 || d == MIE_BF16; }
+bool rows16(int elems, int dtype) { return ((int64_t)elems * esize(dtype)) % 16 == 0; }
+
+constexpr int kSlotBytes = 16 * 1024;
+
+int check_moe(const mie_moe_args& a, bool route_only) {
+  if (!dtype_ok(a.dtype) || !dtype_ok(a.x_dtype) || (!route_only && !dtype_ok(a.out_dtype))) return MIE_ERR_UNSUPPORTED;
+  if (a.top_k != 2 || a.num_experts < 2 || a.num_experts > 32) return MIE_ERR_UNSUPPORTED;
+  if (a.hidden_dim <= 0 || a.expert_hidden_dim <= 0) return MIE_ERR_INVALID;
+  if (!rows16(a.hidden_dim, a.dtype) || !rows16(a.expert_hidden_dim, a.dtype)) return MIE_ERR_UNSUPPORTED;
+  if ((int64_t)a.expert_hidden_dim * esize(a.dtype) > kSlotBytes) return MIE_ERR_UNSUPPORTED;
+  if ((int64_t)a.hidden_dim * esize(a.dtype) > kSlotBytes) return MIE_ERR_UNSUPPORTED;
+  if (!a.x || !a.router_w || !aligned16(a.router_w)) return MIE_ERR_INVALID;
+  if (a.norm != MIE_NORM_NONE && !a.norm_w) return MIE_ERR_INVALID;
+  if (route_only) return MIE_OK;
+  if (a.act != MIE_ACT_GELU && a.act != MIE_ACT_SWIGLU) return MIE_ERR_UNSUPPORTED;
+  if (!a.w1 || !a.w2 || !aligned16(a.w1) || !aligned16(a.w2)) return MIE_ERR_INVALID;
+  if (a.act == MIE_ACT_SWIGLU && (!a.w3 || !aligned16(a.w3))) return MIE_ERR_INVALID;
+  if (!a.hidden || !a.out || !a.sync) return MIE_ERR_INVALID;
+  if (a.expert_count < 0 || a.expert_base < 0 || a.expert_base + a.expert_count > a.num_experts)
+    return MIE_ERR_INVALID;
+  return MIE_OK;
+}
+
+int run_moe(const mie_moe_args& a, cudaStream_t st, bool pdl, bool route_only) {
+  const int rc = check_moe(a, route_only);
+  if (rc) return rc;
+  int grid = a.grid > 0 ? a.grid : num_sms();
+  if (grid > num_sms()) grid = num_sms();  // grid barrier: all CTAs co-resident
+  if (route_only) grid = 1;
+  MoeLayout L = moe_layout(a, grid, kSlotBytes, 6);
+  L.route_only = route_only ? 1 : 0;
+  if (L.smem > (uint32_t)kMaxDynSmem) return MIE_ERR_UNSUPPORTED;
+  // chunk-list bound (kMaxChunks in moe.cu)
+  const int cap_up = kSlotBytes / (a.hidden_dim * esize(a.dtype));
+  const int cap_dn = kSlotBytes / (a.expert_hidden_dim * esize(a.dtype));
+  const int up = 2 * ((L.max_units + cap_up - 1) / cap_up + 1) * (a.act == MIE_ACT_SWIGLU ? 2 : 1);
+  const int dn = 2 * ((L.max_rows + cap_dn - 1) / cap_dn + 1);
+  if (!route_only && up + dn > 96) return MIE_ERR_UNSUPPORTED;
+  return moe_decode_launch(a, L, grid, st, pdl);
+}
+
+int check_attn(const mie_attn_args& a) {
+  if (!dtype_ok(a.kv_dtype) || !dtype_ok(a.q_dtype) || !dtype_ok(a.out_dtype)) return MIE_ERR_UNSUPPORTED;
+  switch (a.head_dim) {
+    case 4: case 8: case 16: case 32: case 64: case 96: case 128: break;
+    default: return MIE_ERR_UNSUPPORTED;
+  }
+  if (a.num_heads <= 0 || a.block_size <= 0 || a.splits <= 0 || a.splits > a.max_splits) return MIE_ERR_INVALID;
+  if (!a.q || !a.k || !a.v || !a.out) return MIE_ERR_INVALID;
+  if (a.splits > 1 && (!a.partials || !a.counters)) return MIE_ERR_INVALID;
+  if (!a.ctx_dev && (a.ctx_len < 1 || a.ctx_len > a.max_ctx)) return MIE_ERR_INVALID;
+  if (a.stride_tok != a.head_dim) return MIE_ERR_UNSUPPORTED;
+  if (rows16(a.head_dim, a.kv_dtype)) {
+    const int64_t e = esize(a.kv_dtype);
+    if (!aligned16(a.k) || !aligned16(a.v) || (a.stride_block * e) % 16 || (a.stride_head * e) % 16)
+      return MIE_ERR_INVALID;
+  }
+  return MIE_OK;
+}
+
+int run_attn(const mie_attn_args& a, cudaStream_t st, bool pdl) {
+  const int rc = check_attn(a);
+  if (rc) return rc;
+  AttnLayout L = attn_layout(a);
+  if (L.smem > (uint32_t)kMaxDynSmem) return MIE_ERR_UNSUPPORTED;
+  return attn_decode_launch(a, L, st, pdl);
+}
+
+int check_qkv(const mie_qkv_args& a) {
+  if (!dtype_ok(a.dtype) || !dtype_ok(a.kv_dtype)) return MIE_ERR_UNSUPPORTED;
+  if (a.num_heads <= 0 || a.head_dim <= 0 || a.head_dim % 2 || a.num_heads * a.head_dim != a.hidden_dim)
+    return MIE_ERR_INVALID;
+  if (!rows16(a.hidden_dim, a.dtype) || (int64_t)a.hidden_dim * esize(a.dtype) > kSlotBytes) return MIE_ERR_UNSUPPORTED;
+  if (!a.x || !a.w || !aligned16(a.w) || !a.pos || !a.q_out || !a.k_cache || !a.v_cache) return MIE_ERR_INVALID;
+  if (a.embedding && !a.token) return MIE_ERR_INVALID;
+  if (a.norm != MIE_NORM_NONE && !a.norm_w) return MIE_ERR_INVALID;
+  if ((a.rope_cos == nullptr) != (a.rope_sin == nullptr)) return MIE_ERR_INVALID;
+  if (a.block_size <= 0) return MIE_ERR_INVALID;
+  return MIE_OK;
+}
+
+int run_qkv(const mie_qkv_args& a, cudaStream_t st, bool pdl) {
+  const int rc = check_qkv(a);
+  if (rc) return rc;
+  const int U = 3 * a.num_heads * (a.head_dim / 2);
+  int grid = a.grid > 0 ? a.grid : num_sms();
+  if (grid > U) grid = U;
+  GemvLayout L = qkv_layout(a, grid);
+  const int cap = kSlotBytes / (a.hidden_dim * esize(a.dtype));
+  // each CTA: <= (units/(hd/2) + 2) groups x 2 halves x ceil(run/cap) chunks
+  const int per = (L.max_units + cap - 1) / cap + 1;
+  if (2 * per * (L.max_units / (a.head_dim / 2) + 2) > 160) return MIE_ERR_UNSUPPORTED;
+  return qkv_launch(a, L, grid, st, pdl);
+}
+
+int run_proj(const mie_proj_args& a, cudaStream_t st, bool pdl) {
+  if (!dtype_ok(a.dtype)) return MIE_ERR_UNSUPPORTED;
+  if (a.rows <= 0 || a.cols <= 0 || !a.w || !aligned16(a.w) || !a.in || !a.out) return MIE_ERR_INVALID;
+  if (!rows16(a.cols, a.dtype) || (int64_t)a.cols * esize(a.dtype) > kSlotBytes) return MIE_ERR_UNSUPPORTED;
+  int grid = a.grid > 0 ? a.grid : num_sms();
+  if (grid > a.rows) grid = a.rows;
+  GemvLayout L = proj_layout(a, grid);
+  const int cap = kSlotBytes / (a.cols * esize(a.dtype));
+  if ((L.max_units + cap - 1) / cap > 160) return MIE_ERR_UNSUPPORTED;
+  return proj_launch(a, L, grid, st, pdl);
+}
+
+int run_lmhead(const mie_lmhead_args& a, cudaStream_t st, bool pdl) {
+  if (!dtype_ok(a.dtype)) return MIE_ERR_UNSUPPORTED;
+  if (a.vocab <= 0 || a.hidden_dim <= 0 || !a.x || !a.w || !aligned16(a.w)) return MIE_ERR_INVALID;
+  if (!rows16(a.hidden_dim, a.dtype) || (int64_t)a.hidden_dim * esize(a.dtype) > kSlotBytes) return MIE_ERR_UNSUPPORTED;
+  if (!a.partial_val || !a.partial_idx || !a.counter) return MIE_ERR_INVALID;
+  if (a.norm != MIE_NORM_NONE && !a.norm_w) return MIE_ERR_INVALID;
+  int grid = a.grid > 0 ? a.grid : num_sms();
+  if (grid > a.vocab) grid = a.vocab;
+  GemvLayout L = lmhead_layout(a, grid);
+  const int cap = kSlotBytes / (a.hidden_dim * esize(a.dtype));
+  const int rows_max = (a.vocab + grid - 1) / grid + 1;
+  if ((rows_max + cap - 1) / cap > 160) return MIE_ERR_UNSUPPORTED;
+  return lmhead_launch(a, L, grid, st, pdl);
+}
+
+// ---- decode step ---------------------------------------------------------
+
+mie_qkv_args step_qkv(const mie_step_desc& d, int l) {
+  const mie_layer_desc& ly = d.layers[l];
+  mie_qkv_args a = {};
+  a.dtype = d.dtype;
+  a.kv_dtype = d.kv_dtype;
+  a.hidden_dim = d.hidden_dim;
+  a.num_heads = d.num_heads;
+  a.head_dim = d.head_dim;
+  a.norm = d.norm;
+  a.eps = d.eps;
+  a.norm_w = ly.attn_norm_w;
+  a.norm_b = ly.attn_norm_b;
+  a.x = d.x;
+  a.x_add = (l > 0 && d.moe_partial) ? d.moe_partial : nullptr;
+  a.embedding = l == 0 ? d.embedding : nullptr;
+  a.pos_embedding = l == 0 ? d.pos_embedding : nullptr;
+  a.token = d.token;
+  a.vocab = d.vocab;
+  a.w = ly.qkv_w;
+  a.b = ly.qkv_b;
+  a.rope_cos = d.rope_cos;
+  a.rope_sin = d.rope_sin;
+  a.pos = d.pos;
+  a.max_pos = d.max_pos;
+  a.q_out = d.q;
+  a.k_cache = ly.k_cache;
+  a.v_cache = ly.v_cache;
+  a.block_table = d.block_table;
+  a.num_blocks = d.num_blocks;
+  a.block_size = d.block_size;
+  a.stride_block = d.kv_stride_block;
+  a.stride_head = d.kv_stride_head;
+  a.stride_tok = d.kv_stride_tok;
+  a.status = d.status;
+  a.skip = d.done;
+  return a;
+}
+
+mie_attn_args step_attn(const mie_step_desc& d, int l) {
+  const mie_layer_desc& ly = d.layers[l];
+  mie_attn_args a = {};
+  a.kv_dtype = d.kv_dtype;
+  a.q_dtype = MIE_F32;
+  a.out_dtype = MIE_F32;
+  a.num_heads = d.num_heads;
+  a.head_dim = d.head_dim;
+  a.q = d.q;
+  a.k = ly.k_cache;
+  a.v = ly.v_cache;
+  a.block_table = d.block_table;
+  a.num_blocks = d.num_blocks;
+  a.block_size = d.block_size;
+  a.stride_block = d.kv_stride_block;
+  a.stride_head = d.kv_stride_head;
+  a.stride_tok = d.kv_stride_tok;
+  a.ctx_dev = d.pos;
+  a.ctx_dev_offset = 1;
+  a.max_ctx = d.max_pos;
+  a.scale = d.attn_scale;
+  a.out = d.attn_out;
+  a.partials = d.attn_partials;
+  a.counters = d.attn_counters;
+  a.splits = d.attn_splits;
+  a.max_splits = d.max_splits;
+  a.new_token_last = 1;
+  a.status = d.status;
+  a.skip = d.done;
+  return a;
+}
+
+mie_proj_args step_proj(const mie_step_desc& d, int l) {
+  const mie_layer_desc& ly = d.layers[l];
+  mie_proj_args a = {};
+  a.dtype = d.dtype;
+  a.rows = d.hidden_dim;
+  a.cols = d.num_heads * d.head_dim;
+  a.w = ly.out_w;
+  a.b = ly.out_b;
+  a.in = d.attn_out;
+  a.out = d.x;
+  a.add = (l > 0 && d.moe_partial) ? d.moe_partial : nullptr;
+  a.accumulate = 1;
+  a.status = d.status;
+  a.skip = d.done;
+  return a;
+}
+
+mie_moe_args step_moe(const mie_step_desc& d, int l) {
+  const mie_layer_desc& ly = d.layers[l];
+  mie_moe_args a = {};
+  a.dtype = d.dtype;
+  a.x_dtype = MIE_F32;
+  a.out_dtype = MIE_F32;
+  a.hidden_dim = d.hidden_dim;
+  a.expert_hidden_dim = d.expert_hidden_dim;
+  a.num_experts = d.num_experts;
+  a.top_k = d.top_k;
+  a.act = d.act;
+  a.norm = d.norm;
+  a.eps = d.eps;
+  a.x = d.x;
+  a.norm_w = ly.moe_norm_w;
+  a.norm_b = ly.moe_norm_b;
+  a.router_w = ly.router_w;
+  a.w1 = ly.w1;
+  a.b1 = ly.b1;
+  a.w3 = ly.w3;
+  a.w2 = ly.w2;
+  a.b2 = ly.b2;
+  a.hidden = d.moe_hidden;
+  if (d.moe_partial) {
+    a.out = d.moe_partial;
+    a.residual = 0;
+  } else {
+    a.out = d.x;
+    a.residual = 1;
+  }
+  a.sync = d.moe_sync;
+  a.status = d.status;
+  a.skip = d.done;
+  a.expert_base = d.expert_base;
+  a.expert_count = d.expert_count;
+  return a;
+}
+
+mie_lmhead_args step_lmhead(const mie_step_desc& d) {
+  mie_lmhead_args a = {};
+  a.dtype = d.dtype;
+  a.vocab = d.vocab;
+  a.hidden_dim = d.hidden_dim;
+  a.norm = d.norm;
+  a.eps = d.eps;
+  a.norm_w = d.final_norm_w;
+  a.norm_b = d.final_norm_b;
+  a.x = d.x;
+  a.x_add = d.moe_partial;
+  a.w = d.embedding;
+  a.b = d.lm_bias;
+  a.logits = d.logits;
+  a.partial_val = d.lm_partial_val;
+  a.partial_idx = d.lm_partial_idx;
+  a.counter = d.lm_counter;
+  a.token_out = d.token;
+  a.pos = d.pos;
+  a.tokens_log = d.tokens_log;
+  a.log_count = d.log_count;
+  a.log_capacity = d.log_capacity;
+  a.done = d.done;
+  a.eos_id = d.eos_id;
+  a.status = d.status;
+  a.skip = d.done;
+  a.grid = d.lm_grid;
+  return a;
+}
+
+int check_step(const mie_step_desc& d) {
+  if (!d.layers || d.num_layers <= 0 || !d.embedding || !d.token || !d.pos || !d.x || !d.q || !d.attn_out ||
+      !d.moe_hidden || !d.moe_sync || !d.lm_partial_val || !d.lm_partial_idx || !d.lm_counter)
+    return MIE_ERR_INVALID;
+  if (d.attn_splits > 1 && (!d.attn_partials || !d.attn_counters)) return MIE_ERR_INVALID;
+  return MIE_OK;
+}
+
+}  // namespace
+}  // namespace mie
+
+using namespace mie;
+
+extern "C" {
+
+int mie_version(void) { return 1; }
+
+const char* mie_status_string(int code) {
+  switch (code) {
+    case MIE_OK: return "ok";
+    case MIE_ERR_INVALID: return "invalid argument (null pointer, size or alignment)";
+    case MIE_ERR_UNSUPPORTED: return "unsupported shape or dtype for the sm_100a kernels";
+    case MIE_ERR_CUDA: return "CUDA runtime error";
+    case MIE_ERR_TIMEOUT: return "device wait timed out";
+    case MIE_ERR_RANGE: return "device index out of range (block id, position, expert or token)";
+    default: return "unknown status";
+  }
+}
+
+int mie_num_sms(int device) {
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) return -1;
+  return n;
+}
+
+int mie_init(int device) {
+  int cur = 0;
+  if (cudaGetDevice(&cur) != cudaSuccess) return MIE_ERR_CUDA;
+  if (device >= 0 && device != cur) {
+    if (cudaSetDevice(device) != cudaSuccess) return MIE_ERR_CUDA;
+  }
+  moe_set_attributes();
+  attn_set_attributes();
+  gemv_set_attributes();
+  (void)num_sms();
+  const cudaError_t e = cudaGetLastError();
+  if (device >= 0 && device != cur) cudaSetDevice(cur);
+  return e == cudaSuccess ? MIE_OK : MIE_ERR_CUDA;
+}
+
+int mie_moe_route(const mie_moe_args* a, void* stream) {
+  if (!a) return MIE_ERR_INVALID;
+  return run_moe(*a, static_cast<cudaStream_t>(stream), false, true);
+}
+
+int mie_moe_decode(const mie_moe_args* a, void* stream) {
+  if (!a) return MIE_ERR_INVALID;
+  return run_moe(*a, static_cast<cudaStream_t>(stream), false, false);
+}
+
+int mie_attn_decode(const mie_attn_args* a, void* stream) {
+  if (!a) return MIE_ERR_INVALID;
+  return run_attn(*a, static_cast<cudaStream_t>(stream), false);
+}
+
+int mie_qkv_rope_store(const mie_qkv_args* a, void* stream) {
+  if (!a) return MIE_ERR_INVALID;
+  return run_qkv(*a, static_cast<cudaStream_t>(stream), false);
+}
+
+int mie_proj_residual(const mie_proj_args* a, void* stream) {
+  if (!a) return MIE_ERR_INVALID;
+  return run_proj(*a, static_cast<cudaStream_t>(stream), false);
+}
+
+int mie_lmhead_argmax(const mie_lmhead_args* a, void* stream) {
+  if (!a) return MIE_ERR_INVALID;
+  return run_lmhead(*a, static_cast<cudaStream_t>(stream), false);
+}
+
+int mie_decode_layer(const mie_step_desc* d, int l, void* stream) {
+  if (!d || l < 0 || l >= d->num_layers) return MIE_ERR_INVALID;
+  int rc = check_step(*d);
+  if (rc) return rc;
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool pdl = d->use_pdl != 0;
+  if ((rc = run_qkv(step_qkv(*d, l), st, pdl))) return rc;
+  if ((rc = run_attn(step_attn(*d, l), st, pdl))) return rc;
+  if ((rc = run_proj(step_proj(*d, l), st, pdl))) return rc;
+  return run_moe(step_moe(*d, l), st, pdl, false);
+}
+
+int mie_decode_head(const mie_step_desc* d, void* stream) {
+  if (!d) return MIE_ERR_INVALID;
+  const int rc = check_step(*d);
+  if (rc) return rc;
+  return run_lmhead(step_lmhead(*d), static_cast<cudaStream_t>(stream), d->use_pdl != 0);
+}
+
+int mie_decode_step(const mie_step_desc* d, void* stream) {
+  if (!d) return MIE_ERR_INVALID;
+  for (int l = 0; l < d->num_layers; ++l) {
+    const int rc = mie_decode_layer(d, l, stream);
+    if (rc) return rc;
+  }
+  return mie_decode_head(d, stream);
+}
+
+}  // extern "C"

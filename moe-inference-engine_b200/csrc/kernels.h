@@ -1,0 +1,83 @@
+// Internal host-side interface between the kernel files and the C ABI layer.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <utility>
+
+#include "../../include/mie.h"
+
+namespace mie {
+
+// Shared-memory layout of the MoE kernel (byte offsets into dynamic smem).
+struct MoeLayout {
+  uint32_t off_bar, off_ring, off_router, off_x, off_h, off_res, off_chunks, smem;
+  uint32_t slot_bytes;
+  int nslot;
+  int max_units;  // up-phase units per CTA (upper bound)
+  int max_rows;   // down-phase rows per CTA (upper bound)
+  int route_only; // 1: stop after routing (mie_moe_route)
+};
+
+// Shared-memory layout of the single-vector GEMV kernels (QKV, proj, LM head).
+struct GemvLayout {
+  uint32_t off_bar, off_ring, off_x, off_res, off_chunks, smem;
+  uint32_t slot_bytes;
+  int nslot;
+  int max_units;
+};
+
+struct AttnLayout {
+  uint32_t off_bar, off_kv, off_q, off_p, off_acc, smem;
+  int nstage;
+  int stage_tokens;  // tokens per stage (a multiple of block_size)
+};
+
+constexpr int kMaxDynSmem = 227 * 1024;
+
+template <typename Kernel>
+inline void set_max_smem(Kernel k) {
+  cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
+}
+
+// Launch with optional programmatic dependent launch.  Returns MIE_OK or MIE_ERR_CUDA.
+template <typename... KArgs, typename... Args>
+inline int launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, uint32_t smem, cudaStream_t stream, bool pdl,
+                  Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+  return e == cudaSuccess ? MIE_OK : MIE_ERR_CUDA;
+}
+
+// moe.cu
+MoeLayout moe_layout(const mie_moe_args& a, int grid, int slot_bytes, int nslot);
+int moe_decode_launch(const mie_moe_args& a, const MoeLayout& L, int grid, cudaStream_t st, bool pdl);
+void moe_set_attributes();
+
+// attention.cu
+AttnLayout attn_layout(const mie_attn_args& a);
+int attn_decode_launch(const mie_attn_args& a, const AttnLayout& L, cudaStream_t st, bool pdl);
+void attn_set_attributes();
+
+// gemv.cu
+GemvLayout qkv_layout(const mie_qkv_args& a, int grid);
+int qkv_launch(const mie_qkv_args& a, const GemvLayout& L, int grid, cudaStream_t st, bool pdl);
+GemvLayout proj_layout(const mie_proj_args& a, int grid);
+int proj_launch(const mie_proj_args& a, const GemvLayout& L, int grid, cudaStream_t st, bool pdl);
+GemvLayout lmhead_layout(const mie_lmhead_args& a, int grid);
+int lmhead_launch(const mie_lmhead_args& a, const GemvLayout& L, int grid, cudaStream_t st, bool pdl);
+void gemv_set_attributes();
+
+int num_sms();
+
+}  // namespace mie

@@ -1,0 +1,319 @@
+"""Fused decode step: one launch sequence of sm_100a kernels per token.
+
+A decode step of the reference (``Model.forward`` with one token,
+src/moe_engine/model.py:543-565) becomes, per layer,
+
+    qkv   norm -> QKV GEMV -> RoPE -> K/V store at the device position
+    attn  split-K attention over the cache with an in-launch LSE merge
+    proj  out_proj + residual
+    moe   norm -> router -> top-2 -> selected experts -> combine + residual
+
+followed by ``lmhead`` (final norm -> tied LM head -> argmax, position += 1,
+EOS flag, token log).  All launches use programmatic dependent launch so a
+kernel fetches its weights while its predecessor still runs.
+
+The position, the input token and the EOS flag live on the device, so one
+step can be captured once as a CUDA graph and replayed for every token;
+greedy generation replays it in chunks and reads the produced tokens back
+once per chunk (:func:`greedy_generate`).
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+
+import torch
+
+from . import capi
+from .paged_attention import MAX_SPLITS, SUPPORTED_HEAD_DIMS, cache_geometry
+
+EOS_TOKEN_ID = 50256
+CHUNK_STEPS = 64  # graph replays between host reads of the token log
+
+
+def _row_ok(n: int, dtype) -> bool:
+    e = 2 if dtype == torch.bfloat16 else 4
+    return (n * e) % 16 == 0 and n * e <= 16 * 1024
+
+
+class DecodeRunner:
+    """Device state, scratch and step descriptors for one model on one GPU."""
+
+    @staticmethod
+    def supports(model, cache, batch: int) -> bool:
+        cfg = model.config
+        w = model.token_embedding.weight
+        if batch != 1 or w.device.type != "cuda" or not capi.library_available():
+            return False
+        if w.dtype not in (torch.float32, torch.bfloat16):
+            return False
+        if getattr(cache, "attention_mode", "gather") == "gather":
+            return False
+        kv = cache.allocator.k_pool if hasattr(cache, "allocator") else cache.k
+        if kv.dtype != w.dtype or kv.device != w.device:
+            return False
+        if not hasattr(cache, "allocator") and cache.k.shape[1] != 1:
+            return False
+        hd = cfg.head_dim
+        if hd not in SUPPORTED_HEAD_DIMS or cfg.num_heads * hd != cfg.hidden_dim or cfg.top_k != 2:
+            return False
+        if not (_row_ok(cfg.hidden_dim, w.dtype) and _row_ok(cfg.expert_hidden, w.dtype)):
+            return False
+        for block in model.MoEBlocks:
+            if block.moe.mode == "reference" or not block.moe.direct_configuration_supported(1):
+                return False
+        return all(p.dtype == w.dtype and p.device == w.device for p in model.parameters())
+
+    def __init__(self, model, expert_base: int = 0, expert_count: int = 0, moe_partial: bool = False):
+        cfg = model.config
+        self.model = model
+        self.config = cfg
+        dev = model.token_embedding.weight.device
+        self.device = dev
+        self.lib = capi.ensure_init(dev)
+        self.num_sms = self.lib.mie_num_sms(dev.index if dev.index is not None else torch.cuda.current_device())
+        D, H, hd, Hx, V = cfg.hidden_dim, cfg.num_heads, cfg.head_dim, cfg.expert_hidden, cfg.vocab_size
+        f32 = dict(dtype=torch.float32, device=dev)
+        i32 = dict(dtype=torch.int32, device=dev)
+        self.x = torch.zeros(D, **f32)
+        self.q = torch.zeros(H * hd, **f32)
+        self.attn_out = torch.zeros(H * hd, **f32)
+        self.moe_hidden = torch.zeros(2 * Hx, **f32)
+        self.moe_partial = torch.zeros(D, **f32) if moe_partial else None
+        self.expert_base, self.expert_count = expert_base, expert_count
+        self.attn_partials = torch.zeros(H * MAX_SPLITS * (hd + 2), **f32)
+        self.attn_counters = torch.zeros(H, **i32)
+        self.moe_sync = torch.zeros(4, **i32)
+        self.lm_grid = self.num_sms
+        self.lm_partial_val = torch.zeros(self.lm_grid, **f32)
+        self.lm_partial_idx = torch.zeros(self.lm_grid, **i32)
+        self.lm_counter = torch.zeros(1, **i32)
+        self.logits = torch.zeros(V, **f32)
+        self.status = torch.zeros(1, **i32)
+        self.token = torch.zeros(1, dtype=torch.int64, device=dev)
+        self.pos = torch.zeros(1, **i32)
+        self.done = torch.zeros(1, **i32)
+        self.log_capacity = cfg.max_seq_length + 1
+        self.tokens_log = torch.zeros(self.log_capacity, dtype=torch.int64, device=dev)
+        self.log_count = torch.zeros(1, **i32)
+        self._host_state = torch.zeros(2, dtype=torch.int32, pin_memory=True)
+        self._graphs: dict = {}
+        self.use_pdl = True
+
+    # ---- descriptors --------------------------------------------------------
+    def param_signature(self):
+        return tuple(p.data_ptr() for p in self.model.parameters())
+
+    def splits_for(self, max_ctx: int, block_size: int) -> int:
+        nblk = -(-max_ctx // block_size)
+        want = -(-self.num_sms // self.config.num_heads)
+        return max(1, min(want, max(1, -(-nblk // 2)), MAX_SPLITS))
+
+    def _layers(self, cache):
+        m = self.model
+        n_layers = self.config.num_layers
+        arr = (capi.LayerDesc * n_layers)()
+        p = capi.ptr
+        for i, blk in enumerate(m.MoEBlocks):
+            L = arr[i]
+            att, moe = blk.attention, blk.moe
+            s = moe._expert_storage
+            L.attn_norm_w = p(blk.attn_norm.weight)
+            L.attn_norm_b = p(getattr(blk.attn_norm, "bias", None))
+            L.qkv_w = p(att.in_proj_weight)
+            L.qkv_b = p(att.in_proj_bias)
+            L.out_w = p(att.out_proj.weight)
+            L.out_b = p(att.out_proj.bias)
+            L.moe_norm_w = p(blk.moe_norm.weight)
+            L.moe_norm_b = p(getattr(blk.moe_norm, "bias", None))
+            L.router_w = p(moe.router.weight)
+            eb = self.expert_base
+            def view(t):
+                if t is None or not self.expert_count:
+                    return p(t)
+                return t[eb].data_ptr()
+            L.w1, L.b1, L.w3, L.w2, L.b2 = (view(s.get(k)) for k in ("w1", "b1", "w3", "w2", "b2"))
+            k, v, *_ = cache_geometry(cache, i)
+            L.k_cache, L.v_cache = k.data_ptr(), v.data_ptr()
+        return arr
+
+    def make_desc(self, cache, *, logits: bool, graph: bool, splits: int):
+        cfg, m = self.config, self.model
+        w = m.token_embedding.weight
+        d = capi.StepDesc()
+        d.dtype = capi.dtype_code(w.dtype)
+        _, kv0, table, nb, bs, (s_blk, s_head, s_tok), _ = cache_geometry(cache, 0)
+        d.kv_dtype = capi.dtype_code(kv0.dtype)
+        d.num_layers = cfg.num_layers
+        d.hidden_dim = cfg.hidden_dim
+        d.num_heads = cfg.num_heads
+        d.head_dim = cfg.head_dim
+        d.num_experts = cfg.num_experts
+        d.top_k = cfg.top_k
+        d.expert_hidden_dim = cfg.expert_hidden
+        d.vocab = cfg.vocab_size
+        d.norm = capi.MIE_NORM_RMS if cfg.norm == "rms" else capi.MIE_NORM_LAYER
+        d.act = capi.MIE_ACT_SWIGLU if cfg.expert_act == "swiglu" else capi.MIE_ACT_GELU
+        d.eps = cfg.norm_eps
+        d.attn_scale = 1.0 / math.sqrt(cfg.head_dim)
+        if table is not None:
+            d.max_pos = min(cfg.max_seq_length, nb * bs)
+        else:
+            d.max_pos = min(cfg.max_seq_length, cache.k.shape[3])
+        layers = self._layers(cache)
+        d.layers = ctypes.cast(layers, ctypes.c_void_p)
+        d.embedding = w.data_ptr()
+        pe = getattr(m, "positional_embedding", None)
+        d.pos_embedding = capi.ptr(pe.weight) if pe is not None else None
+        d.final_norm_w = capi.ptr(m.final_norm.weight)
+        d.final_norm_b = capi.ptr(getattr(m.final_norm, "bias", None))
+        d.lm_bias = capi.ptr(m.output_projection.bias)
+        if cfg.pos == "rope":
+            d.rope_cos, d.rope_sin = m.rope_cos.data_ptr(), m.rope_sin.data_ptr()
+        d.block_table = capi.ptr(table)
+        d.num_blocks = nb
+        d.block_size = bs
+        d.kv_stride_block, d.kv_stride_head, d.kv_stride_tok = s_blk, s_head, s_tok
+        d.token = self.token.data_ptr()
+        d.pos = self.pos.data_ptr()
+        d.done = self.done.data_ptr() if graph else None
+        d.eos_id = EOS_TOKEN_ID
+        d.tokens_log = self.tokens_log.data_ptr() if graph else None
+        d.log_count = self.log_count.data_ptr() if graph else None
+        d.log_capacity = self.log_capacity
+        d.x = self.x.data_ptr()
+        d.q = self.q.data_ptr()
+        d.attn_out = self.attn_out.data_ptr()
+        d.moe_hidden = self.moe_hidden.data_ptr()
+        d.moe_partial = capi.ptr(self.moe_partial)
+        d.expert_base = self.expert_base
+        d.expert_count = self.expert_count
+        d.attn_partials = self.attn_partials.data_ptr()
+        d.attn_counters = self.attn_counters.data_ptr()
+        d.moe_sync = self.moe_sync.data_ptr()
+        d.lm_partial_val = self.lm_partial_val.data_ptr()
+        d.lm_partial_idx = self.lm_partial_idx.data_ptr()
+        d.lm_counter = self.lm_counter.data_ptr()
+        d.logits = self.logits.data_ptr() if logits else None
+        d.status = self.status.data_ptr()
+        d.attn_splits = splits
+        d.max_splits = MAX_SPLITS
+        d.lm_grid = self.lm_grid
+        d.use_pdl = 1 if self.use_pdl else 0
+        return d, layers
+
+    # ---- execution ------------------------------------------------------------
+    def launch_step(self, desc) -> None:
+        capi.check(self.lib.mie_decode_step(ctypes.byref(desc), capi.stream_handle(self.device)), "mie_decode_step")
+
+    def check_status(self) -> None:
+        """Synchronise and raise if any kernel recorded a device-side failure."""
+        code = int(self.status.item())
+        if code:
+            self.status.zero_()
+            raise capi.KernelError(code, "decode step (device status)")
+
+    @torch.no_grad()
+    def forward_step(self, token_ids: torch.Tensor, cache) -> torch.Tensor:
+        """One eager fused decode step; returns logits [1, 1, V] in the model dtype."""
+        position = cache.position
+        cache.reserve(position + 1)
+        self.token.copy_(token_ids.reshape(1))
+        self.pos.fill_(position)
+        _, _, _, _, bs, _, _ = cache_geometry(cache, 0)
+        desc, layers = self.make_desc(cache, logits=True, graph=False, splits=self.splits_for(position + 1, bs))
+        self.launch_step(desc)
+        del layers
+        cache.position += 1
+        dt = self.model.token_embedding.weight.dtype
+        return self.logits.to(dt, copy=True).view(1, 1, -1)
+
+    def graph_for(self, cache, max_ctx: int):
+        """The captured decode step for ``cache`` (captured on first use)."""
+        _, _, _, _, bs, _, _ = cache_geometry(cache, 0)
+        splits = self.splits_for(max_ctx, bs)
+        k0 = cache_geometry(cache, 0)[0]
+        table = getattr(cache, "block_table_device", None)
+        key = (k0.data_ptr(), None if table is None else table.data_ptr(), splits, self.use_pdl,
+               self.param_signature())
+        hit = self._graphs.get(key)
+        if hit is not None:
+            return hit[0]
+        if len(self._graphs) >= 4:
+            self._graphs.clear()
+        desc, layers = self.make_desc(cache, logits=False, graph=True, splits=splits)
+        # Warm-up with every kernel skipping (done = 1): loads modules, touches
+        # nothing; then capture.
+        self.done.fill_(1)
+        self.launch_step(desc)
+        torch.cuda.current_stream(self.device).synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            rc = self.lib.mie_decode_step(ctypes.byref(desc), capi.stream_handle(self.device))
+        capi.check(rc, "mie_decode_step (capture)")
+        self._graphs[key] = (g, desc, layers)
+        return g
+
+
+@torch.no_grad()
+def greedy_generate(model, token_ids: torch.Tensor, max_new_tokens: int, cache) -> torch.Tensor:
+    """Greedy ``Model.generate`` with the decode step replayed as a CUDA graph.
+
+    Same results and cache effects as the step-by-step loop (model.py:596-621):
+    iteration 0 is the prompt prefill; each further iteration is one graph
+    replay; EOS stops generation on the device (later replays are no-ops) and
+    the loop ends when the context is full.
+    """
+    runner = model.decode_runner()
+    max_seq = model.max_seq_length
+    logits = model(token_ids, cache)  # prefill (position 0)
+    first = int(torch.argmax(logits[0, -1]).item())
+    if first == EOS_TOKEN_ID:
+        return token_ids
+    P = cache.position
+    if P >= max_seq or max_new_tokens == 1:
+        return torch.cat((token_ids, token_ids.new_tensor([[first]])), dim=1)
+    K = min(max_new_tokens - 1, max_seq - P)
+    graph = runner.graph_for(cache, P + K)
+    runner.token.fill_(first)
+    runner.pos.fill_(P)
+    runner.done.zero_()
+    runner.log_count.zero_()
+    produced = 0  # replays issued
+    count = 0
+    exhausted = False
+    paged = hasattr(cache, "allocator")
+    while produced < K:
+        n = min(CHUNK_STEPS, K - produced)
+        if paged:
+            try:
+                cache.reserve(P + produced + n)
+            except RuntimeError:
+                # Reserve what the pool still has, run up to it, then fail like
+                # the step that could not get a block.
+                bs = cache.allocator.block_size
+                while cache.allocator.free_blocks and len(cache.block_table) * bs < P + produced + n:
+                    cache.reserve(len(cache.block_table) * bs + 1)
+                n = len(cache.block_table) * bs - (P + produced)
+                exhausted = True
+        for _ in range(n):
+            graph.replay()
+        produced += n
+        runner._host_state[0:1].copy_(runner.log_count, non_blocking=True)
+        runner._host_state[1:2].copy_(runner.done, non_blocking=True)
+        torch.cuda.current_stream(runner.device).synchronize()
+        count, done = int(runner._host_state[0]), int(runner._host_state[1])
+        if done or exhausted:
+            break
+    runner.check_status()
+    cache.position = P + count
+    if paged:
+        cache._trim(cache.position)
+    new = runner.tokens_log[:count]
+    if count and int(new[-1]) == EOS_TOKEN_ID and int(runner.done.item()):
+        new = new[:-1]
+    elif exhausted and count < K:
+        raise RuntimeError("no free KV cache blocks left")
+    first_t = token_ids.new_tensor([[first]])
+    return torch.cat((token_ids, first_t, new.view(1, -1).to(token_ids.dtype)), dim=1)

@@ -1,0 +1,254 @@
+"""sm_100a kernels vs the CPU oracle (and the reference's golden outputs).
+
+Tolerances (written per test):
+* float32 kernels: the reference's own bars -- router logits atol 2e-5,
+  MoE output atol 3e-4 / rtol 2e-4 (reference tests/test_fused_moe.py:68-127),
+  attention atol 2e-5 / rtol 1e-5 (tests/test_paged_attention.py:74-76);
+* bfloat16 weights / KV with fp32 accumulation, compared with the oracle on
+  the same bf16-rounded inputs: 1e-2, and bf16 output
+  rounding (rtol 1e-2);
+* expert ids: exact, ties to the lower id.
+"""
+
+import os
+import random
+
+import pytest
+import torch
+
+import oracle
+from moe_engine import fused_moe, paged_attention
+from moe_engine.model import BlockAllocator, KVCache, ModelConfig
+from tests.golden import make_golden as mg
+
+pytestmark = pytest.mark.gpu
+GOLDEN = os.path.dirname(mg.__file__)
+DEV = "cuda"
+
+
+def workspaces(E, Hx, D, dtype):
+    f = dict(device=DEV, dtype=torch.float32)
+    return dict(
+        router_logits=torch.empty(E, **f),
+        expert_ids=torch.empty(2, dtype=torch.int32, device=DEV),
+        route_weights=torch.empty(2, **f),
+        hidden=torch.empty(2, Hx, **f),
+        out=torch.empty(D, dtype=dtype, device=DEV),
+    )
+
+
+# ---------------------------------------------------------------------------
+# fused MoE
+# ---------------------------------------------------------------------------
+
+
+def test_moe_gelu_fp32_matches_reference_golden():
+    """Reference production shape (768, 8 experts, GELU 3072, biases), fp32,
+    against outputs of the unmodified reference's _forward_reference."""
+    fx = torch.load(os.path.join(GOLDEN, "reference_moe.pt"))
+    router, w1, b1, w2, b2, xs = (t.to(DEV) for t in mg.moe_weights())
+    ws = workspaces(8, 3072, 768, torch.float32)
+    for i, x in enumerate(xs):
+        out = fused_moe.decode(x.view(1, 1, 768), router, w1, b1, w2, b2, **ws)
+        torch.testing.assert_close(ws["router_logits"].cpu(), fx["router_logits"][i], atol=2e-5, rtol=1e-5)
+        assert ws["expert_ids"].cpu().long().tolist() == fx["expert_ids"][i].tolist()
+        torch.testing.assert_close(ws["route_weights"].cpu(), fx["route_weights"][i], atol=2e-6, rtol=1e-6)
+        torch.testing.assert_close(out.view(768).cpu(), fx["out"][i], atol=3e-4, rtol=2e-4)
+
+
+def swiglu_weights(E=8, D=768, Hx=768, seed=0, dtype=torch.bfloat16):
+    g = torch.Generator().manual_seed(seed)
+    router = torch.randn(E, D, generator=g) * 0.02
+    w1 = torch.randn(E, Hx, D, generator=g) * 0.02
+    w3 = torch.randn(E, Hx, D, generator=g) * 0.02
+    w2 = torch.randn(E, D, Hx, generator=g) * 0.02
+    return [t.to(dtype) for t in (router, w1, w3, w2)]
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_moe_swiglu_matches_oracle(dtype):
+    router, w1, w3, w2 = swiglu_weights(dtype=dtype)
+    ws = workspaces(8, 768, 768, dtype)
+    g = torch.Generator().manual_seed(1)
+    for _ in range(8):
+        x = torch.randn(768, generator=g).to(dtype)
+        out = fused_moe.decode(x.to(DEV).view(1, 1, 768), router.to(DEV), w1.to(DEV), None, w2.to(DEV), None,
+                               w3_base=w3.to(DEV), **ws)
+        want, logits, ids, wts = oracle.moe_decode_stacked(x.float(), router.float(), w1.float(), None,
+                                                           w2.float(), None, w3=w3.float())
+        assert ws["expert_ids"].cpu().long().tolist() == ids.tolist()
+        torch.testing.assert_close(ws["router_logits"].cpu(), logits, atol=2e-5, rtol=1e-5)
+        torch.testing.assert_close(ws["route_weights"].cpu(), wts, atol=2e-6, rtol=1e-5)
+        tol = dict(atol=3e-4, rtol=2e-4) if dtype == torch.float32 else dict(atol=1e-3, rtol=1e-2)
+        torch.testing.assert_close(out.view(768).float().cpu(), want, **tol)
+
+
+@pytest.mark.parametrize("act", ["gelu", "swiglu"])
+def test_every_expert_pointer_works_in_both_routes(act):
+    """Distinct weights per expert; each expert is forced into slot 0 and slot 1."""
+    E, D = 8, 768
+    Hx = 3072 if act == "gelu" else 768
+    g = torch.Generator().manual_seed(2)
+    w1 = torch.randn(E, Hx, D, generator=g) * 0.02
+    w2 = torch.randn(E, D, Hx, generator=g) * 0.02
+    b1 = torch.randn(E, Hx, generator=g) * 0.1 if act == "gelu" else None
+    b2 = torch.randn(E, D, generator=g) * 0.1 if act == "gelu" else None
+    w3 = torch.randn(E, Hx, D, generator=g) * 0.02 if act == "swiglu" else None
+    x = torch.ones(D)
+    ws = workspaces(E, Hx, D, torch.float32)
+    firsts, seconds = [], []
+    dev = lambda t: None if t is None else t.to(DEV)
+    for first in range(E):
+        second = (first + 3) % E
+        logits = -2.0 - 0.1 * torch.arange(E, dtype=torch.float32)
+        logits[first], logits[second] = 1.0, 0.25
+        router = logits[:, None].expand(E, D) / D
+        out = fused_moe.decode(x.to(DEV).view(1, 1, D), router.contiguous().to(DEV), dev(w1), dev(b1), dev(w2),
+                               dev(b2), w3_base=dev(w3), **ws)
+        firsts.append(int(ws["expert_ids"][0]))
+        seconds.append(int(ws["expert_ids"][1]))
+        want = oracle.moe_decode_stacked(x, router, w1, b1, w2, b2, w3=w3)[0]
+        torch.testing.assert_close(out.view(D).cpu(), want, atol=3e-4, rtol=2e-4)
+    assert firsts == list(range(E))
+    assert seconds == [(i + 3) % E for i in range(E)]
+
+
+def test_router_ties_pick_lower_ids():
+    E, D = 8, 768
+    router = torch.zeros(E, D, device=DEV)
+    ws = workspaces(E, 768, D, torch.float32)
+    x = torch.randn(1, 1, D, device=DEV)
+    fused_moe.route(x, router, ws["router_logits"], ws["expert_ids"], ws["route_weights"])
+    assert ws["expert_ids"].tolist() == [0, 1]
+    torch.testing.assert_close(ws["route_weights"].cpu(), torch.tensor([0.5, 0.5]))
+    router[5] = 1e-3
+    router[2] = 1e-3
+    x = torch.ones(1, 1, D, device=DEV)
+    fused_moe.route(x, router, ws["router_logits"], ws["expert_ids"], ws["route_weights"])
+    assert ws["expert_ids"].tolist() == [2, 5]
+
+
+def test_moe_config1_stacked_layers_ids_exact():
+    """12 independent bf16 layers (working set > L2); ids
+    must match the oracle exactly on every call."""
+    layers = [swiglu_weights(seed=100 + l) for l in range(12)]
+    dl = [[t.to(DEV) for t in ly] for ly in layers]
+    ws = workspaces(8, 768, 768, torch.bfloat16)
+    x = torch.randn(768, generator=torch.Generator().manual_seed(1)).to(torch.bfloat16)
+    xd = x.to(DEV).view(1, 1, 768)
+    for rep in range(36):
+        l = rep % 12
+        router, w1, w3, w2 = dl[l]
+        out = fused_moe.decode(xd, router, w1, None, w2, None, w3_base=w3, **ws)
+        want, _, ids, _ = oracle.moe_decode_stacked(x.float(), *[layers[l][0].float()],
+                                                    layers[l][1].float(), None, layers[l][3].float(), None,
+                                                    w3=layers[l][2].float())
+        assert ws["expert_ids"].cpu().long().tolist() == ids.tolist(), rep
+        torch.testing.assert_close(out.view(768).float().cpu(), want, atol=1e-3, rtol=1e-2)
+
+
+def test_moe_rejects_bad_layouts():
+    router, w1, w3, w2 = (t.to(DEV) for t in swiglu_weights(dtype=torch.float32))
+    ws = workspaces(8, 768, 768, torch.float32)
+    x = torch.randn(1, 1, 768, device=DEV)
+    with pytest.raises(ValueError, match="canonical"):
+        fused_moe.decode(x, router, w1[:, :, :512], None, w2, None, w3_base=w3, **ws)
+    with pytest.raises(RuntimeError, match="float32 or bfloat16"):
+        fused_moe.decode(x.double(), router.double(), w1.double(), None, w2.double(), None, w3_base=w3.double(),
+                         **ws)
+
+
+# ---------------------------------------------------------------------------
+# attention
+# ---------------------------------------------------------------------------
+
+
+def filled_paged_cache(H, hd, bs, ctx, max_seq, seed, shuffle, dtype, layers=1):
+    free, k, v, q, nb = mg.attention_inputs(H, hd, bs, ctx, max_seq, seed, shuffle)
+    cfg = ModelConfig(max_seq_length=max_seq, vocab_size=96, num_layers=layers, hidden_dim=H * hd, num_heads=H)
+    alloc = BlockAllocator(cfg, nb, bs, DEV, dtype)
+    alloc.free_blocks = list(free)
+    cache = alloc.new_cache()
+    for layer in range(layers):
+        cache.write(layer, 0, k.to(DEV, dtype), v.to(DEV, dtype))
+    cache.position = ctx
+    return cache, k, v, q
+
+
+def test_attention_matches_reference_golden_paged():
+    """Every golden case of the reference's gather+SDPA oracle (8x96 at
+    ctx 1..1024, shuffled tables; 8x4 at block sizes 4/16/32), fp32."""
+    fx = torch.load(os.path.join(GOLDEN, "reference_attention.pt"))
+    for i in sorted(fx):
+        c = fx[i]
+        cache, k, v, q = filled_paged_cache(c["H"], c["hd"], c["bs"], c["ctx"], c["max_seq"], c["seed"], True,
+                                            torch.float32)
+        assert cache.block_table == c["block_table"].tolist()
+        got = paged_attention.decode(q.to(DEV), cache, 0, c["ctx"])
+        torch.testing.assert_close(got.view(c["H"], c["hd"]).cpu(), c["out"], atol=2e-5, rtol=1e-5,
+                                   msg=lambda m: f"case {i} {c['tag']} ctx {c['ctx']}: {m}")
+
+
+@pytest.mark.parametrize("ctx", [128, 512, 2048, 8192])
+def test_attention_config2_bf16_paged_and_contiguous(ctx):
+    """12 heads x 64, bf16 K/V ~N(0,1), block 16, shuffled
+    table; fp32 accumulate, tolerance 1e-2; contiguous twin on the same K/V."""
+    H, hd, bs = 12, 64, 16
+    cache, k, v, q = filled_paged_cache(H, hd, bs, ctx, 8192, 7 + ctx, True, torch.bfloat16)
+    table = cache.block_table
+    assert any(b != a + 1 for a, b in zip(table, table[1:]))
+    qb = q.to(torch.bfloat16)
+    want = oracle.attention_decode(qb[0, :, 0].float(), k[0].to(torch.bfloat16).float(),
+                                   v[0].to(torch.bfloat16).float())
+    got = paged_attention.decode(qb.to(DEV), cache, 0, ctx)
+    torch.testing.assert_close(got.view(H, hd).float().cpu(), want, atol=1e-2, rtol=1e-2)
+    cfg = ModelConfig(max_seq_length=8192, vocab_size=96, num_layers=1, hidden_dim=H * hd, num_heads=H)
+    cc = KVCache(cfg, 1, DEV, torch.bfloat16)
+    cc.write(0, 0, k.to(DEV, torch.bfloat16), v.to(DEV, torch.bfloat16))
+    got_c = paged_attention.decode(qb.to(DEV), cc, 0, ctx)
+    torch.testing.assert_close(got_c.view(H, hd).float().cpu(), want, atol=1e-2, rtol=1e-2)
+    # fp32 q / out over bf16 K/V: the decode step's configuration
+    got32 = paged_attention.decode(q.to(DEV), cache, 0, ctx, out=torch.empty(H, hd, device=DEV))
+    want32 = oracle.attention_decode(q[0, :, 0], k[0].to(torch.bfloat16).float(), v[0].to(torch.bfloat16).float())
+    torch.testing.assert_close(got32.view(H, hd).cpu(), want32, atol=2e-5, rtol=1e-4)
+
+
+@pytest.mark.parametrize("block_size", [4, 16, 32])
+def test_attention_partial_blocks_fp32(block_size):
+    H, hd = 12, 64
+    for ctx in [1, block_size - 1, block_size, block_size + 1, 3 * block_size + 2, 333]:
+        if ctx < 1:
+            continue
+        cache, k, v, q = filled_paged_cache(H, hd, block_size, ctx, 512, ctx, True, torch.float32)
+        want = oracle.attention_decode(q[0, :, 0], k[0], v[0])
+        got = paged_attention.decode(q.to(DEV), cache, 0, ctx)
+        torch.testing.assert_close(got.view(H, hd).cpu(), want, atol=2e-5, rtol=1e-5)
+
+
+def test_attention_layer_indexing():
+    H, hd = 12, 64
+    cache, _, _, q = filled_paged_cache(H, hd, 16, 40, 256, 3, True, torch.float32, layers=3)
+    # distinct K/V per layer
+    g = torch.Generator().manual_seed(9)
+    for layer in (1, 2):
+        cache.write(layer, 0, torch.randn(1, H, 40, hd, generator=g).to(DEV), torch.randn(1, H, 40, hd, generator=g).to(DEV))
+    qd = q.to(DEV)
+    outs = []
+    for layer in range(3):
+        keys, vals = cache.read(layer, 40)
+        want = oracle.attention_decode(q[0, :, 0], keys[0].cpu(), vals[0].cpu())
+        got = paged_attention.decode(qd, cache, layer, 40).view(H, hd).cpu()
+        torch.testing.assert_close(got, want, atol=2e-5, rtol=1e-5)
+        outs.append(got)
+    assert not torch.allclose(outs[0], outs[1], atol=1e-3)
+
+
+def test_attention_reuses_workspace_across_calls():
+    """The per-head merge counters reset themselves: many calls in a row."""
+    H, hd = 12, 64
+    cache, k, v, q = filled_paged_cache(H, hd, 16, 700, 1024, 11, True, torch.float32)
+    want = oracle.attention_decode(q[0, :, 0], k[0], v[0])
+    qd = q.to(DEV)
+    for _ in range(50):
+        got = paged_attention.decode(qd, cache, 0, 700)
+    torch.testing.assert_close(got.view(H, hd).cpu(), want, atol=2e-5, rtol=1e-5)
