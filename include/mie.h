@@ -285,6 +285,7 @@ typedef struct mie_step_desc {
 int mie_version(void);
 int mie_init(int device);                 /* set kernel attributes; call before any capture */
 const char* mie_status_string(int code);
+const char* mie_last_cuda_error(void);   /* text of the last failed CUDA call on this thread, "" if none */
 int mie_num_sms(int device);
 
 /* Operators (see the table at the top of this file). */

@@ -286,8 +286,8 @@ int attn_decode_launch(const mie_attn_args& a, const AttnLayout& L, cudaStream_t
 
 void attn_set_attributes() {
   for (int hd : {4, 8, 16, 32, 64, 96, 128}) {
-    cudaFuncSetAttribute(pick<float>(hd), cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
-    cudaFuncSetAttribute(pick<__nv_bfloat16>(hd), cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
+    set_max_smem(pick<float>(hd));
+    set_max_smem(pick<__nv_bfloat16>(hd));
   }
 }
 

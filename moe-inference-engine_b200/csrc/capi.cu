@@ -1,10 +1,18 @@
 // extern "C" entry points of libmie.so (declared in include/mie.h): argument
 // validation, launch geometry, and the decode-step launch sequence.
-#include <mutex>
+#include <cstdio>
 
 #include "kernels.h"
 
 namespace mie {
+
+namespace {
+thread_local char g_last_error[256] = "";
+}
+
+void note_cuda_error(cudaError_t e, const char* what) {
+  snprintf(g_last_error, sizeof(g_last_error), "%s: %s (%d)", what, cudaGetErrorString(e), (int)e);
+}
 
 int num_sms() {
   static int cached[64] = {0};
@@ -343,14 +351,18 @@ int mie_init(int device) {
   if (device >= 0 && device != cur) {
     if (cudaSetDevice(device) != cudaSuccess) return MIE_ERR_CUDA;
   }
+  g_last_error[0] = 0;
   moe_set_attributes();
   attn_set_attributes();
   gemv_set_attributes();
   (void)num_sms();
   const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) note_cuda_error(e, "mie_init");
   if (device >= 0 && device != cur) cudaSetDevice(cur);
-  return e == cudaSuccess ? MIE_OK : MIE_ERR_CUDA;
+  return (e == cudaSuccess && g_last_error[0] == 0) ? MIE_OK : MIE_ERR_CUDA;
 }
+
+const char* mie_last_cuda_error(void) { return g_last_error; }
 
 int mie_moe_route(const mie_moe_args* a, void* stream) {
   if (!a) return MIE_ERR_INVALID;

@@ -10,6 +10,9 @@
 
 namespace mie {
 
+// Record a failed CUDA call (readable through mie_last_cuda_error()).
+void note_cuda_error(cudaError_t e, const char* what);
+
 // Shared-memory layout of the MoE kernel (byte offsets into dynamic smem).
 struct MoeLayout {
   uint32_t off_bar, off_ring, off_router, off_x, off_h, off_res, off_chunks, smem;
@@ -34,11 +37,26 @@ struct AttnLayout {
   int stage_tokens;  // tokens per stage (a multiple of block_size)
 };
 
-constexpr int kMaxDynSmem = 227 * 1024;
+// Dynamic shared memory any layout here may use (under the 227 KB opt-in
+// limit minus the kernels' static shared memory).
+constexpr int kMaxDynSmem = 220 * 1024;
 
+// Allow the largest dynamic shared memory the device permits next to the
+// kernel's static shared memory.
 template <typename Kernel>
 inline void set_max_smem(Kernel k) {
-  cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
+  int dev = 0, optin = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  cudaFuncAttributes fa{};
+  cudaError_t e = cudaFuncGetAttributes(&fa, reinterpret_cast<const void*>(k));
+  if (e != cudaSuccess) {
+    note_cuda_error(e, "cudaFuncGetAttributes");
+    return;
+  }
+  e = cudaFuncSetAttribute(reinterpret_cast<const void*>(k), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           optin - (int)fa.sharedSizeBytes);
+  if (e != cudaSuccess) note_cuda_error(e, "cudaFuncSetAttribute(MaxDynamicSharedMemorySize)");
 }
 
 // Launch with optional programmatic dependent launch.  Returns MIE_OK or MIE_ERR_CUDA.
@@ -56,7 +74,11 @@ inline int launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, uint32_t smem
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
   const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
-  return e == cudaSuccess ? MIE_OK : MIE_ERR_CUDA;
+  if (e != cudaSuccess) {
+    note_cuda_error(e, "cudaLaunchKernelEx");
+    return MIE_ERR_CUDA;
+  }
+  return MIE_OK;
 }
 
 // moe.cu

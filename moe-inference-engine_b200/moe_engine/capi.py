@@ -109,6 +109,7 @@ SYMBOLS = {
     "mie_version": ([], ctypes.c_int),
     "mie_init": ([_i], ctypes.c_int),
     "mie_status_string": ([_i], ctypes.c_char_p),
+    "mie_last_cuda_error": ([], ctypes.c_char_p),
     "mie_num_sms": ([_i], ctypes.c_int),
     "mie_moe_route": ([ctypes.POINTER(MoeArgs), _p], ctypes.c_int),
     "mie_moe_decode": ([ctypes.POINTER(MoeArgs), _p], ctypes.c_int),
@@ -131,7 +132,10 @@ class KernelError(RuntimeError):
 
     def __init__(self, code: int, what: str):
         self.code = code
-        super().__init__(f"{what}: {status_string(code)} (status {code})")
+        detail = ""
+        if code == MIE_ERR_CUDA and _lib is not None:
+            detail = " [" + _lib.mie_last_cuda_error().decode() + "]"
+        super().__init__(f"{what}: {status_string(code)} (status {code}){detail}")
 
 
 def library_available() -> bool:
