@@ -204,7 +204,8 @@ def run_b200(args, rank, world, device):
     gen = torch.Generator().manual_seed(3 + rank)
     prompt = torch.randint(0, 50304, (PROMPT_LEN,), generator=gen)
     max_blocks = -(-(PROMPT_LEN + NEW_TOKENS) // 16)
-    alloc = model.new_block_allocator(num_blocks=max_blocks + 8, block_size=16, attention_mode="direct")
+    # room for the device-loop request and one public-API (e2e) request at a time
+    alloc = model.new_block_allocator(num_blocks=2 * max_blocks + 8, block_size=16, attention_mode="direct")
     runner = model.decode_runner()
 
     # prefill once, then the device-resident decode loop

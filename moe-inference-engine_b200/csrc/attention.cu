@@ -47,11 +47,11 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const mie_attn_ar
   // Context length.  ctx_dev is the step's device position, written by an
   // earlier step's LM-head kernel that completed before this grid's producer
   // started, so it may be read before pdl_wait().
+  // Out-of-range values are clamped here and reported only after the skip
+  // flag was read (a skipped step may carry a stale position).
   int ctx = a.ctx_dev ? (__ldcg(a.ctx_dev) + a.ctx_dev_offset) : a.ctx_len;
-  if (ctx < 1 || ctx > a.max_ctx) {
-    if (tid == 0 && s == 0) set_status(a.status, MIE_ERR_RANGE);
-    ctx = ctx < 1 ? 1 : a.max_ctx;
-  }
+  const bool bad_ctx = ctx < 1 || ctx > a.max_ctx;
+  if (bad_ctx) ctx = ctx < 1 ? 1 : a.max_ctx;
   const int nblk = (ctx + bs - 1) / bs;
   int b0, b1;
   split_range(nblk, s, S, &b0, &b1);
@@ -106,6 +106,7 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const mie_attn_ar
     return;
   }
   pdl_trigger();
+  if (bad_ctx && tid == 0 && s == 0) set_status(a.status, MIE_ERR_RANGE);
   if (kBulk && tid == 0 && deferred >= 0 && deferred < L.nstage) issue(deferred);
   issued = min(L.nstage, nst);
 

@@ -246,6 +246,7 @@ class DecodeRunner:
         # Warm-up with every kernel skipping (done = 1): loads modules, touches
         # nothing; then capture.
         self.done.fill_(1)
+        self.pos.zero_()
         self.launch_step(desc)
         torch.cuda.current_stream(self.device).synchronize()
         g = torch.cuda.CUDAGraph()

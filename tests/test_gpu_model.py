@@ -107,6 +107,11 @@ def test_generate_context_limit_and_chunking_on_gpu():
     want = oracle.generate_greedy(P, arch.with_(max_seq_length=150), prompt, 200)
     got = m.generate(prompt, max_new_tokens=200, temperature=0)[0].tolist()
     assert got == want and len(got) == 151
+    # A new cache re-captures the step while the device position still holds
+    # the full context of the previous request: no false range report.
+    again = m.generate(prompt, max_new_tokens=200, temperature=0, cache=m.new_cache())[0].tolist()
+    assert again == want
+    m.decode_runner().check_status()
 
 
 @pytest.mark.parametrize("kind", ["reference", "baseline"])
