@@ -38,7 +38,8 @@ enum {
   MIE_ERR_UNSUPPORTED = 2,  /* shape / dtype combination has no kernel */
   MIE_ERR_CUDA = 3,         /* a CUDA runtime call failed */
   MIE_ERR_TIMEOUT = 4,      /* device: a bounded wait gave up */
-  MIE_ERR_RANGE = 5         /* device: block id / position / expert / token out of range */
+  MIE_ERR_RANGE = 5,        /* device: block id / position / expert / token out of range */
+  MIE_ERR_SCRATCH_LIMIT = 6 /* request larger than the fixed scratch of mie_attn_decode_fixed_scratch */
 };
 
 /* element types */
@@ -292,6 +293,26 @@ int mie_num_sms(int device);
 int mie_moe_route(const mie_moe_args* a, void* stream);
 int mie_moe_decode(const mie_moe_args* a, void* stream);
 int mie_attn_decode(const mie_attn_args* a, void* stream);
+
+/* mie_attn_decode_fixed_scratch -- no counterpart in the reference.
+ *
+ * The same attention decode as mie_attn_decode for callers that cannot
+ * allocate device memory: a host runtime that owns all device memory and gives
+ * its plugins no allocator, or a latency-critical caller that must not call
+ * cudaMalloc / cudaFree (they can synchronise the device).  The caller passes
+ * q, the cache and `out` as usual; a->partials, a->counters and a->max_splits
+ * are ignored.  Split partials and merge counters live in one fixed array
+ * inside libmie.so: 64 counter words + 65,536 floats (256 KB), which every GPU
+ * that loads the library holds until the process exits.  Limits: num_heads <=
+ * 64 and num_heads * splits * (head_dim + 2) <= 65,536; larger requests return
+ * MIE_ERR_SCRATCH_LIMIT and launch nothing.  Nothing is allocated: no
+ * cudaMalloc, cudaFree or allocating library call.  The first call on a device
+ * looks up the array's device address and zeroes its counters
+ * (cudaGetSymbolAddress + cudaMemset, with that device current), so make the
+ * first call on each device before any stream capture.  All calls share the
+ * array and each call returns the counters to zero: calls that overlap on
+ * the GPU (for example on two streams at once) race and corrupt each other. */
+int mie_attn_decode_fixed_scratch(const mie_attn_args* a, void* stream);
 int mie_qkv_rope_store(const mie_qkv_args* a, void* stream);
 int mie_proj_residual(const mie_proj_args* a, void* stream);
 int mie_lmhead_argmax(const mie_lmhead_args* a, void* stream);

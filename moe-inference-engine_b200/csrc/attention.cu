@@ -16,6 +16,7 @@
 // Under programmatic dependent launch the blocks that hold only OLD tokens are
 // fetched before waiting on the producer grid (the QKV kernel that writes the
 // newest token); the block holding the newest token is fetched after.
+#include <mutex>
 #include <utility>
 
 #include "kernels.h"
@@ -290,6 +291,77 @@ void attn_set_attributes() {
     set_max_smem(pick<float>(hd));
     set_max_smem(pick<__nv_bfloat16>(hd));
   }
+}
+
+// ---------------------------------------------------------------------------
+// Fixed-scratch variant (mie_attn_decode_fixed_scratch)
+//
+// Some callers cannot allocate device memory: a host runtime that owns every
+// byte of device memory and offers its plugins no allocator, or a
+// latency-critical caller for which a cudaMalloc / cudaFree (which may
+// synchronise the device) is not acceptable.  For them the split partials and
+// the per-head merge counters live in this file-scope array instead of in
+// caller-provided buffers.  Every GPU that loads the library holds it until
+// the process exits.
+//
+// Layout (32-bit words): [0, kFixedCounters) merge counters, then
+// kFixedPartialFloats floats of partials (num_heads x splits x (head_dim + 2)).
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr int kFixedCounters = 64;                      // max heads
+constexpr int kFixedPartialFloats = 64 * 1024;          // 256 KB of partials
+constexpr int kFixedWords = kFixedCounters + kFixedPartialFloats;
+
+static __device__ __align__(256) uint32_t g_attn_fixed_scratch[kFixedWords];
+
+std::mutex g_fixed_mutex;
+void* g_fixed_addr[64] = {nullptr};  // device address of the array, per device
+
+// Once per device, with that device current: resolve the array's device
+// address (the host symbol is only a stand-in) and zero the counters.
+int fixed_scratch_setup(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= 64) {
+    note_cuda_error(e, "cudaGetDevice");
+    return MIE_ERR_CUDA;
+  }
+  std::lock_guard<std::mutex> lock(g_fixed_mutex);
+  if (!g_fixed_addr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_attn_fixed_scratch);
+    if (e != cudaSuccess) {
+      note_cuda_error(e, "cudaGetSymbolAddress(g_attn_fixed_scratch)");
+      return MIE_ERR_CUDA;
+    }
+    e = cudaMemset(p, 0, sizeof(uint32_t) * kFixedCounters);
+    if (e != cudaSuccess) {
+      note_cuda_error(e, "cudaMemset(fixed-scratch counters)");
+      return MIE_ERR_CUDA;
+    }
+    g_fixed_addr[dev] = p;
+  }
+  *out = g_fixed_addr[dev];
+  return MIE_OK;
+}
+
+}  // namespace
+
+// Point a->partials / a->counters at the fixed array (set up on first use on
+// this device) after checking the request fits it.
+int attn_fixed_scratch_bind(mie_attn_args* a) {
+  if (a->num_heads <= 0 || a->splits <= 0) return MIE_ERR_INVALID;
+  if (a->num_heads > kFixedCounters ||
+      (int64_t)a->num_heads * a->splits * (a->head_dim + 2) > kFixedPartialFloats)
+    return MIE_ERR_SCRATCH_LIMIT;
+  void* base = nullptr;
+  const int rc = fixed_scratch_setup(&base);
+  if (rc) return rc;
+  a->counters = static_cast<uint32_t*>(base);
+  a->partials = reinterpret_cast<float*>(static_cast<uint32_t*>(base) + kFixedCounters);
+  a->max_splits = a->splits;  // partials packed as [heads, splits, head_dim + 2]
+  return MIE_OK;
 }
 
 }  // namespace mie

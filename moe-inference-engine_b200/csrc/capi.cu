@@ -335,6 +335,9 @@ const char* mie_status_string(int code) {
     case MIE_ERR_CUDA: return "CUDA runtime error";
     case MIE_ERR_TIMEOUT: return "device wait timed out";
     case MIE_ERR_RANGE: return "device index out of range (block id, position, expert or token)";
+    case MIE_ERR_SCRATCH_LIMIT:
+      return "request exceeds the fixed scratch of mie_attn_decode_fixed_scratch "
+             "(num_heads <= 64, num_heads * splits * (head_dim + 2) <= 65536)";
     default: return "unknown status";
   }
 }
@@ -377,6 +380,14 @@ int mie_moe_decode(const mie_moe_args* a, void* stream) {
 int mie_attn_decode(const mie_attn_args* a, void* stream) {
   if (!a) return MIE_ERR_INVALID;
   return run_attn(*a, static_cast<cudaStream_t>(stream), false);
+}
+
+int mie_attn_decode_fixed_scratch(const mie_attn_args* a, void* stream) {
+  if (!a) return MIE_ERR_INVALID;
+  mie_attn_args v = *a;
+  const int rc = attn_fixed_scratch_bind(&v);  // partials + counters from the fixed array
+  if (rc) return rc;
+  return run_attn(v, static_cast<cudaStream_t>(stream), false);
 }
 
 int mie_qkv_rope_store(const mie_qkv_args* a, void* stream) {

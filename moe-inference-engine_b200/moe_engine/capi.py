@@ -17,7 +17,7 @@ import torch
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "_native", "libmie.so")
 
-MIE_OK, MIE_ERR_INVALID, MIE_ERR_UNSUPPORTED, MIE_ERR_CUDA, MIE_ERR_TIMEOUT, MIE_ERR_RANGE = range(6)
+MIE_OK, MIE_ERR_INVALID, MIE_ERR_UNSUPPORTED, MIE_ERR_CUDA, MIE_ERR_TIMEOUT, MIE_ERR_RANGE, MIE_ERR_SCRATCH_LIMIT = range(7)
 MIE_F32, MIE_BF16 = 0, 1
 MIE_NORM_NONE, MIE_NORM_RMS, MIE_NORM_LAYER = 0, 1, 2
 MIE_ACT_GELU, MIE_ACT_SWIGLU = 0, 1
@@ -114,6 +114,7 @@ SYMBOLS = {
     "mie_moe_route": ([ctypes.POINTER(MoeArgs), _p], ctypes.c_int),
     "mie_moe_decode": ([ctypes.POINTER(MoeArgs), _p], ctypes.c_int),
     "mie_attn_decode": ([ctypes.POINTER(AttnArgs), _p], ctypes.c_int),
+    "mie_attn_decode_fixed_scratch": ([ctypes.POINTER(AttnArgs), _p], ctypes.c_int),
     "mie_qkv_rope_store": ([ctypes.POINTER(QkvArgs), _p], ctypes.c_int),
     "mie_proj_residual": ([ctypes.POINTER(ProjArgs), _p], ctypes.c_int),
     "mie_lmhead_argmax": ([ctypes.POINTER(LmHeadArgs), _p], ctypes.c_int),
