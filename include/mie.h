@@ -117,6 +117,8 @@ typedef struct mie_attn_args {
   int new_token_last;     /* 1: the last token was written by the preceding kernel */
   int32_t* status;
   const int32_t* skip;
+  int defer_merge;        /* 1: write every split's (m, l, acc) to partials and leave the
+                             merge to the consumer (mie_proj_args.attn_partials) */
 } mie_attn_args;
 
 /* Norm + QKV GEMV + RoPE + K/V store into the cache slot of the device
@@ -171,6 +173,13 @@ typedef struct mie_proj_args {
   int32_t* status;
   const int32_t* skip;
   int grid;
+  /* Optional: build `in` by merging split-K attention partials ([heads, max_splits,
+   * head_dim + 2] as written with mie_attn_args.defer_merge) instead of reading it. */
+  const float* attn_partials;
+  int attn_heads;
+  int attn_head_dim;
+  int attn_splits;
+  int attn_max_splits;
 } mie_proj_args;
 
 /* Final norm + tied LM-head GEMV + argmax (ties to the lower id), with the

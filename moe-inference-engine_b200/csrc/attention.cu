@@ -5,17 +5,21 @@
 // SDPA decode at src/moe_engine/model.py:261-266.
 //
 // Here the context of every head is split over `splits` CTAs (grid = splits x
-// heads) so all SMs stream K/V.  Each CTA moves whole KV blocks into shared
-// memory with TMA bulk copies (a block of one head is bs*hd contiguous
-// elements in the [nb, H, bs, hd] pool; the contiguous [H, S, hd] layout is
-// the same addressing with an identity block map), keeps an online softmax
-// (running max m, normaliser l, accumulator acc), and writes (m, l, acc).  The
-// last CTA of each head (arrival counter, no spinning) merges the partials
-// with a log-sum-exp rescale and writes the output row.
+// heads) so all SMs stream K/V.  A CTA walks its token range in stages of up
+// to 32 KB of K+V: every thread loads its 16-byte pieces of the stage with
+// plain read-only loads into registers (a block of one head is bs*hd
+// contiguous elements in the [nb, H, bs, hd] pool; the contiguous [H, S, hd]
+// layout is the same addressing with an identity block map), stores them to
+// one of two shared-memory buffers, and the next stage's loads are in flight
+// while the current stage is reduced.  An online softmax (running max m,
+// normaliser l, accumulator acc) gives the CTA's (m, l, acc).  The last CTA of
+// each head (arrival counter, no spinning) merges the partials with a
+// log-sum-exp rescale and writes the output row -- or, with defer_merge, the
+// consumer kernel merges them (the decode step's out_proj).
 //
-// Under programmatic dependent launch the blocks that hold only OLD tokens are
-// fetched before waiting on the producer grid (the QKV kernel that writes the
-// newest token); the block holding the newest token is fetched after.
+// Under programmatic dependent launch the stages that hold only OLD tokens are
+// loaded before waiting on the producer grid (the QKV kernel that writes the
+// newest token); the stage holding the newest token is loaded after.
 #include <mutex>
 #include <utility>
 
@@ -27,13 +31,13 @@ namespace mie {
 namespace {
 
 constexpr int kThreads = 128;
+constexpr int kStageVecs = 16;  // 16-byte K/V pieces per thread per stage (32 KB per CTA)
 
 template <typename KV, int HD>
 __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const mie_attn_args a, AttnLayout L) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int h = blockIdx.y, s = blockIdx.x, S = gridDim.x, tid = threadIdx.x;
   const int bs = a.block_size;
-  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + L.off_bar);
   KV* kvbuf = reinterpret_cast<KV*>(smem + L.off_kv);
   float* q_s = reinterpret_cast<float*>(smem + L.off_q);
   float* p_s = reinterpret_cast<float*>(smem + L.off_p);
@@ -43,13 +47,15 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const mie_attn_ar
   const int stage_tok = L.stage_tokens;
   const int stage_blocks = stage_tok / bs;
   const size_t stage_elems = (size_t)2 * stage_tok * HD;  // K then V
-  constexpr bool kBulk = (HD * sizeof(KV)) % 16 == 0;
+  constexpr bool kVec = (HD * sizeof(KV)) % 16 == 0;
+  constexpr int VPT = kVec ? 16 / (int)sizeof(KV) : 1;  // elements per 16-byte piece
+  constexpr int VPH = kVec ? HD / VPT : 1;              // pieces per head row
 
   // Context length.  ctx_dev is the step's device position, written by an
   // earlier step's LM-head kernel that completed before this grid's producer
-  // started, so it may be read before pdl_wait().
-  // Out-of-range values are clamped here and reported only after the skip
-  // flag was read (a skipped step may carry a stale position).
+  // started, so it may be read before pdl_wait().  Out-of-range values are
+  // clamped here and reported only after the skip flag was read (a skipped
+  // step may carry a stale position).
   int ctx = a.ctx_dev ? (__ldcg(a.ctx_dev) + a.ctx_dev_offset) : a.ctx_len;
   const bool bad_ctx = ctx < 1 || ctx > a.max_ctx;
   if (bad_ctx) ctx = ctx < 1 ? 1 : a.max_ctx;
@@ -57,7 +63,9 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const mie_attn_ar
   int b0, b1;
   split_range(nblk, s, S, &b0, &b1);
   const int nst = (b1 - b0 + stage_blocks - 1) / stage_blocks;
-  const int deferred = (a.new_token_last && b1 == nblk && nst > 0) ? nst - 1 : -1;
+  // The stage holding the newest token (always this CTA's last stage) is
+  // loaded only after the producer grid finished.
+  const int nst_pre = (a.new_token_last && b1 == nblk && nst > 0) ? nst - 1 : nst;
 
   auto phys_of = [&](int b) -> int64_t {
     if (!a.block_table) return b;
@@ -71,45 +79,55 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const mie_attn_ar
   auto tile_ptr = [&](const void* base, int64_t phys) {
     return static_cast<const KV*>(base) + phys * a.stride_block + (int64_t)h * a.stride_head;
   };
-  // thread 0: start the bulk copies of stage `st` into buffer st % nstage.
-  auto issue = [&](int st) {
+  auto stage_tokens = [&](int st) {
     const int bb = b0 + st * stage_blocks, be = min(b1, bb + stage_blocks);
-    KV* dst = kvbuf + (size_t)(st % L.nstage) * stage_elems;
-    uint32_t total = 0;
-    for (int b = bb; b < be; ++b) total += 2u * (uint32_t)(min(bs, ctx - b * bs) * HD * sizeof(KV));
-    uint64_t* br = &bar[st % L.nstage];
-    mbar_arrive_expect_tx(br, total);
-    for (int b = bb; b < be; ++b) {
-      const int64_t p = phys_of(b);
-      const uint32_t n = (uint32_t)(min(bs, ctx - b * bs) * HD * sizeof(KV));
-      const size_t o = (size_t)(b - bb) * bs * HD;
-      bulk_g2s(dst + o, tile_ptr(a.k, p), n, br);
-      bulk_g2s(dst + (size_t)stage_tok * HD + o, tile_ptr(a.v, p), n, br);
+    return min(be * bs, ctx) - bb * bs;
+  };
+  // Piece i of stage st: K pieces [0, n), then V pieces [n, 2n), n = tokens x VPH.
+  auto piece_src = [&](int st, int i, int n) -> const uint4* {
+    const int kv = i >= n, i2 = i - kv * n, t = i2 / VPH, sub = i2 - t * VPH;
+    const int tok = (b0 + st * stage_blocks) * bs + t;
+    const KV* base = tile_ptr(kv ? a.v : a.k, phys_of(tok / bs)) + (int64_t)(tok % bs) * a.stride_tok;
+    return reinterpret_cast<const uint4*>(base + sub * VPT);
+  };
+  auto piece_dst = [&](int st, int i, int n) -> uint4* {
+    const int kv = i >= n, i2 = i - kv * n, t = i2 / VPH, sub = i2 - t * VPH;
+    KV* dst = kvbuf + (size_t)(st & 1) * stage_elems + (size_t)kv * stage_tok * HD + (size_t)t * HD + sub * VPT;
+    return reinterpret_cast<uint4*>(dst);
+  };
+  uint4 pend[kStageVecs];
+  auto stage_load = [&](int st) {  // registers <- global
+    const int n = stage_tokens(st) * VPH;
+#pragma unroll
+    for (int m = 0; m < kStageVecs; ++m) {
+      const int i = tid + kThreads * m;
+      if (i < 2 * n) pend[m] = __ldg(piece_src(st, i, n));
+    }
+  };
+  auto stage_store = [&](int st) {  // shared <- registers
+    const int n = stage_tokens(st) * VPH;
+#pragma unroll
+    for (int m = 0; m < kStageVecs; ++m) {
+      const int i = tid + kThreads * m;
+      if (i < 2 * n) *piece_dst(st, i, n) = pend[m];
     }
   };
 
-  int issued = 0;
-  if (kBulk && tid == 0) {
-    for (int i = 0; i < L.nstage; ++i) mbar_init(&bar[i], 1);
-    fence_barrier_init();
-    for (int st = 0; st < min(L.nstage, nst); ++st)
-      if (st != deferred) issue(st);
+  int stored = 0;  // stages [0, stored) are in shared memory
+  if constexpr (kVec) {
+    for (; stored < min(2, nst_pre); ++stored) {
+      stage_load(stored);
+      stage_store(stored);
+    }
   }
-  __syncthreads();
 
   pdl_wait();
   if (skip_requested(a.skip)) {
-    if (kBulk && tid == 0)
-      for (int st = 0; st < min(L.nstage, nst); ++st)
-        if (st != deferred) mbar_wait(&bar[st], 0, a.status);
-    __syncthreads();
     pdl_trigger();
     return;
   }
   pdl_trigger();
   if (bad_ctx && tid == 0 && s == 0) set_status(a.status, MIE_ERR_RANGE);
-  if (kBulk && tid == 0 && deferred >= 0 && deferred < L.nstage) issue(deferred);
-  issued = min(L.nstage, nst);
 
   const float scale = a.scale;
   for (int d = tid; d < HD; d += kThreads) q_s[d] = load_any(a.q, a.q_dtype, (int64_t)h * HD + d);
@@ -118,30 +136,26 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const mie_attn_ar
   const int g = tid / HD, dcol = tid % HD;
   const bool pv_active = tid < G * HD;
   float acc = 0.f, m_run = -INFINITY, l_run = 0.f;
-  bool failed = false;
 
   for (int st = 0; st < nst; ++st) {
-    const int bb = b0 + st * stage_blocks, be = min(b1, bb + stage_blocks);
-    const int t0 = bb * bs, ntok = min(be * bs, ctx) - t0;
-    const KV* kst = kvbuf + (size_t)(st % L.nstage) * stage_elems;
+    const int bb = b0 + st * stage_blocks;
+    const int t0 = bb * bs, ntok = stage_tokens(st);
+    const KV* kst = kvbuf + (size_t)(st & 1) * stage_elems;
     const KV* vst = kst + (size_t)stage_tok * HD;
-    if constexpr (kBulk) {
-      if (tid == 0) {
-        while (issued < nst && issued < st + L.nstage) {
-          fence_proxy_async_smem();
-          issue(issued);
-          ++issued;
-        }
+    bool pending = false;
+    if constexpr (kVec) {
+      if (stored == st) {  // not staged yet (the newest-token stage, or 1-buffer lag)
+        stage_load(st);
+        stage_store(st);
+        ++stored;
       }
-      const bool ok = mbar_wait(&bar[st % L.nstage], (st / L.nstage) & 1, a.status);
-      if (!__syncthreads_and(ok)) {
-        if (tid == 0)
-          for (int j = st + 1; j < min(nst, st + L.nstage); ++j) mbar_wait(&bar[j % L.nstage], (j / L.nstage) & 1, a.status);
-        failed = true;
-        break;
+      __syncthreads();
+      if (stored == st + 1 && st + 1 < nst) {  // next stage in flight while this one is reduced
+        stage_load(st + 1);
+        pending = true;
       }
     } else {
-      // Rows too narrow for 16-byte bulk copies: plain loads.
+      // Rows too narrow for 16-byte pieces: element loads.
       KV* kw = const_cast<KV*>(kst);
       KV* vw = const_cast<KV*>(vst);
       __syncthreads();
@@ -158,13 +172,11 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const mie_attn_ar
     float mloc = -INFINITY;
     for (int t = tid; t < ntok; t += kThreads) {
       float dot = 0.f;
-      if constexpr (kBulk) {
-        constexpr int VPT = 16 / sizeof(KV);
-        constexpr int NV = HD / VPT;
+      if constexpr (kVec) {
         const uint4* kr = reinterpret_cast<const uint4*>(kst + (size_t)t * HD);
 #pragma unroll
-        for (int j = 0; j < NV; ++j) {
-          const int v = (j + t) % NV;  // rotate the start chunk: spreads banks
+        for (int j = 0; j < VPH; ++j) {
+          const int v = (j + t) % VPH;  // rotate the start piece: spreads banks
           dot = dot_vec(kr[v], q_s + v * VPT, dot, (const KV*)nullptr);
         }
       } else {
@@ -191,27 +203,32 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const mie_attn_ar
       acc *= alpha;
       for (int t = g; t < ntok; t += G) acc = fmaf(p_s[t], Elem<KV>::to_f(vst[(size_t)t * HD + dcol]), acc);
     }
-    __syncthreads();
+    __syncthreads();  // buffer (st + 1) & 1 == (st - 1) & 1 is no longer read
+    if (pending) {
+      stage_store(st + 1);
+      ++stored;
+    }
   }
-  if (failed) return;
 
   // combine the PV token groups
   if (pv_active) acc_s[g * HD + dcol] = acc;
   __syncthreads();
+  const bool direct_out = (S == 1 && !a.defer_merge);
   float* part = a.partials + ((size_t)h * a.max_splits + s) * (HD + 2);
   for (int d = tid; d < HD; d += kThreads) {
     float v = 0.f;
     for (int gg = 0; gg < G; ++gg) v += acc_s[gg * HD + d];
-    if (S == 1)
+    if (direct_out)
       store_any(a.out, a.out_dtype, (int64_t)h * HD + d, v / l_run);
     else
       part[2 + d] = v;
   }
-  if (S == 1) return;
+  if (direct_out) return;
   if (tid == 0) {
     part[0] = m_run;
     part[1] = l_run;
   }
+  if (a.defer_merge) return;
   __threadfence();
   __syncthreads();
   if (tid == 0) last_s = (atom_add_acq_rel_gpu(a.counters + h, 1u) == (uint32_t)(S - 1));
@@ -257,12 +274,15 @@ void* pick(int hd) {
 AttnLayout attn_layout(const mie_attn_args& a) {
   const int esz = a.kv_dtype == MIE_BF16 ? 2 : 4;
   AttnLayout L{};
-  // ~32 KB of K+V per stage, a whole number of blocks (at least one).
+  // A stage (K+V) fits the threads' register staging: kStageVecs x 16 B per
+  // thread; a whole number of blocks, at least one (narrow rows load per
+  // element and are not limited by it).
   const int per_tok = 2 * a.head_dim * esz;
-  int st = (32 * 1024 / per_tok) / a.block_size * a.block_size;
+  const int budget = kStageVecs * 16 * kThreads;
+  int st = (budget / per_tok) / a.block_size * a.block_size;
   if (st < a.block_size) st = a.block_size;
   L.stage_tokens = st;
-  L.nstage = 3;
+  L.nstage = 2;
   size_t off = 0;
   auto take = [&](size_t bytes) {
     off = (off + 127) & ~size_t(127);
@@ -270,12 +290,14 @@ AttnLayout attn_layout(const mie_attn_args& a) {
     off += bytes;
     return (uint32_t)at;
   };
-  L.off_bar = take(sizeof(uint64_t) * L.nstage);
+  L.off_bar = take(16);
   L.off_kv = take((size_t)L.nstage * per_tok * st);
   L.off_q = take(sizeof(float) * a.head_dim);
   L.off_p = take(sizeof(float) * st);
   L.off_acc = take(sizeof(float) * (kThreads > a.head_dim ? kThreads : a.head_dim));
   L.smem = (uint32_t)((off + 127) & ~size_t(127));
+  // One block of K+V must fit the per-thread register staging (16-byte rows).
+  if ((a.head_dim * esz) % 16 == 0 && per_tok * st > budget) L.smem = 0xffffffffu;  // -> unsupported
   return L;
 }
 

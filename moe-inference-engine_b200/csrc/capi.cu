@@ -33,15 +33,14 @@ int esize(int dtype) { return dtype == MIE_BF16 ? 2 : 4; }
 bool dtype_ok(int d) { return d == MIE_F32 || d == MIE_BF16; }
 bool rows16(int elems, int dtype) { return ((int64_t)elems * esize(dtype)) % 16 == 0; }
 
-constexpr int kSlotBytes = 16 * 1024;
+constexpr int kMaxRowElems = 16 * 1024;  // longest weight row (elements) the kernels accept
 
 int check_moe(const mie_moe_args& a, bool route_only) {
   if (!dtype_ok(a.dtype) || !dtype_ok(a.x_dtype) || (!route_only && !dtype_ok(a.out_dtype))) return MIE_ERR_UNSUPPORTED;
   if (a.top_k != 2 || a.num_experts < 2 || a.num_experts > 32) return MIE_ERR_UNSUPPORTED;
   if (a.hidden_dim <= 0 || a.expert_hidden_dim <= 0) return MIE_ERR_INVALID;
   if (!rows16(a.hidden_dim, a.dtype) || !rows16(a.expert_hidden_dim, a.dtype)) return MIE_ERR_UNSUPPORTED;
-  if ((int64_t)a.expert_hidden_dim * esize(a.dtype) > kSlotBytes) return MIE_ERR_UNSUPPORTED;
-  if ((int64_t)a.hidden_dim * esize(a.dtype) > kSlotBytes) return MIE_ERR_UNSUPPORTED;
+  if (a.expert_hidden_dim > kMaxRowElems || a.hidden_dim > kMaxRowElems) return MIE_ERR_UNSUPPORTED;
   if (!a.x || !a.router_w || !aligned16(a.router_w)) return MIE_ERR_INVALID;
   if (a.norm != MIE_NORM_NONE && !a.norm_w) return MIE_ERR_INVALID;
   if (route_only) return MIE_OK;
@@ -60,15 +59,9 @@ int run_moe(const mie_moe_args& a, cudaStream_t st, bool pdl, bool route_only) {
   int grid = a.grid > 0 ? a.grid : num_sms();
   if (grid > num_sms()) grid = num_sms();  // grid barrier: all CTAs co-resident
   if (route_only) grid = 1;
-  MoeLayout L = moe_layout(a, grid, kSlotBytes, 6);
+  MoeLayout L = moe_layout(a, grid, 0, 0);
   L.route_only = route_only ? 1 : 0;
   if (L.smem > (uint32_t)kMaxDynSmem) return MIE_ERR_UNSUPPORTED;
-  // chunk-list bound (kMaxChunks in moe.cu)
-  const int cap_up = kSlotBytes / (a.hidden_dim * esize(a.dtype));
-  const int cap_dn = kSlotBytes / (a.expert_hidden_dim * esize(a.dtype));
-  const int up = 2 * ((L.max_units + cap_up - 1) / cap_up + 1) * (a.act == MIE_ACT_SWIGLU ? 2 : 1);
-  const int dn = 2 * ((L.max_rows + cap_dn - 1) / cap_dn + 1);
-  if (!route_only && up + dn > 96) return MIE_ERR_UNSUPPORTED;
   return moe_decode_launch(a, L, grid, st, pdl);
 }
 
@@ -103,7 +96,7 @@ int check_qkv(const mie_qkv_args& a) {
   if (!dtype_ok(a.dtype) || !dtype_ok(a.kv_dtype)) return MIE_ERR_UNSUPPORTED;
   if (a.num_heads <= 0 || a.head_dim <= 0 || a.head_dim % 2 || a.num_heads * a.head_dim != a.hidden_dim)
     return MIE_ERR_INVALID;
-  if (!rows16(a.hidden_dim, a.dtype) || (int64_t)a.hidden_dim * esize(a.dtype) > kSlotBytes) return MIE_ERR_UNSUPPORTED;
+  if (!rows16(a.hidden_dim, a.dtype) || a.hidden_dim > kMaxRowElems) return MIE_ERR_UNSUPPORTED;
   if (!a.x || !a.w || !aligned16(a.w) || !a.pos || !a.q_out || !a.k_cache || !a.v_cache) return MIE_ERR_INVALID;
   if (a.embedding && !a.token) return MIE_ERR_INVALID;
   if (a.norm != MIE_NORM_NONE && !a.norm_w) return MIE_ERR_INVALID;
@@ -119,37 +112,35 @@ int run_qkv(const mie_qkv_args& a, cudaStream_t st, bool pdl) {
   int grid = a.grid > 0 ? a.grid : num_sms();
   if (grid > U) grid = U;
   GemvLayout L = qkv_layout(a, grid);
-  const int cap = kSlotBytes / (a.hidden_dim * esize(a.dtype));
-  // each CTA: <= (units/(hd/2) + 2) groups x 2 halves x ceil(run/cap) chunks
-  const int per = (L.max_units + cap - 1) / cap + 1;
-  if (2 * per * (L.max_units / (a.head_dim / 2) + 2) > 160) return MIE_ERR_UNSUPPORTED;
   return qkv_launch(a, L, grid, st, pdl);
 }
 
 int run_proj(const mie_proj_args& a, cudaStream_t st, bool pdl) {
   if (!dtype_ok(a.dtype)) return MIE_ERR_UNSUPPORTED;
-  if (a.rows <= 0 || a.cols <= 0 || !a.w || !aligned16(a.w) || !a.in || !a.out) return MIE_ERR_INVALID;
-  if (!rows16(a.cols, a.dtype) || (int64_t)a.cols * esize(a.dtype) > kSlotBytes) return MIE_ERR_UNSUPPORTED;
+  if (a.rows <= 0 || a.cols <= 0 || !a.w || !aligned16(a.w) || !a.out) return MIE_ERR_INVALID;
+  if (a.attn_partials) {
+    if (a.attn_heads <= 0 || a.attn_heads > 64 || a.attn_splits <= 0 || a.attn_splits > 64 ||
+        a.attn_splits > a.attn_max_splits || a.attn_heads * a.attn_head_dim != a.cols)
+      return MIE_ERR_INVALID;
+  } else if (!a.in) {
+    return MIE_ERR_INVALID;
+  }
+  if (!rows16(a.cols, a.dtype) || a.cols > kMaxRowElems) return MIE_ERR_UNSUPPORTED;
   int grid = a.grid > 0 ? a.grid : num_sms();
   if (grid > a.rows) grid = a.rows;
   GemvLayout L = proj_layout(a, grid);
-  const int cap = kSlotBytes / (a.cols * esize(a.dtype));
-  if ((L.max_units + cap - 1) / cap > 160) return MIE_ERR_UNSUPPORTED;
   return proj_launch(a, L, grid, st, pdl);
 }
 
 int run_lmhead(const mie_lmhead_args& a, cudaStream_t st, bool pdl) {
   if (!dtype_ok(a.dtype)) return MIE_ERR_UNSUPPORTED;
   if (a.vocab <= 0 || a.hidden_dim <= 0 || !a.x || !a.w || !aligned16(a.w)) return MIE_ERR_INVALID;
-  if (!rows16(a.hidden_dim, a.dtype) || (int64_t)a.hidden_dim * esize(a.dtype) > kSlotBytes) return MIE_ERR_UNSUPPORTED;
+  if (!rows16(a.hidden_dim, a.dtype) || a.hidden_dim > kMaxRowElems) return MIE_ERR_UNSUPPORTED;
   if (!a.partial_val || !a.partial_idx || !a.counter) return MIE_ERR_INVALID;
   if (a.norm != MIE_NORM_NONE && !a.norm_w) return MIE_ERR_INVALID;
   int grid = a.grid > 0 ? a.grid : num_sms();
   if (grid > a.vocab) grid = a.vocab;
   GemvLayout L = lmhead_layout(a, grid);
-  const int cap = kSlotBytes / (a.hidden_dim * esize(a.dtype));
-  const int rows_max = (a.vocab + grid - 1) / grid + 1;
-  if ((rows_max + cap - 1) / cap > 160) return MIE_ERR_UNSUPPORTED;
   return lmhead_launch(a, L, grid, st, pdl);
 }
 
@@ -222,6 +213,7 @@ mie_attn_args step_attn(const mie_step_desc& d, int l) {
   a.new_token_last = 1;
   a.status = d.status;
   a.skip = d.done;
+  a.defer_merge = 1;  // proj_kernel merges the split partials
   return a;
 }
 
@@ -234,6 +226,11 @@ mie_proj_args step_proj(const mie_step_desc& d, int l) {
   a.w = ly.out_w;
   a.b = ly.out_b;
   a.in = d.attn_out;
+  a.attn_partials = d.attn_partials;
+  a.attn_heads = d.num_heads;
+  a.attn_head_dim = d.head_dim;
+  a.attn_splits = d.attn_splits;
+  a.attn_max_splits = d.max_splits;
   a.out = d.x;
   a.add = (l > 0 && d.moe_partial) ? d.moe_partial : nullptr;
   a.accumulate = 1;

@@ -149,26 +149,44 @@ __device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t* p, uint32_t v
   return old;
 }
 
-// Grid-wide barrier for a grid whose CTAs are all co-resident (grid <= SMs and
-// one CTA per SM fits).  state[0] counts arrivals, state[1] is a generation.
-// Bounded: a CTA that waits longer than kWaitLimitNs records MIE_ERR_TIMEOUT and
-// returns false.  Returns true on success (same value in every thread).
-__device__ __forceinline__ bool grid_barrier(uint32_t* state, uint32_t nblocks, int32_t* status) {
+__device__ __forceinline__ uint64_t ld_relaxed_u64(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint64_t ld_acquire_u64(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void red_release_add_u64(uint64_t* p, uint64_t v) {
+  asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+// Grid-wide barrier for a grid whose CTAs are all co-resident (grid <= SMs, one
+// CTA per SM fits), on a 64-bit counter that only grows: each launch adds
+// exactly gridDim.x arrivals, and every launch sharing the counter uses the
+// same grid size.  grid_sync_target (thread 0, any time before this CTA
+// arrives, e.g. before the PDL wait) gives the value the counter holds once all
+// CTAs of this launch arrived: fewer than gridDim.x arrivals of this launch can
+// precede the read, so rounding down to a multiple of gridDim.x finds the
+// launch's base.  Arrival is one fire-and-forget release add; waiting polls with
+// acquire loads.  Bounded: a CTA that waits longer than kWaitLimitNs records
+// MIE_ERR_TIMEOUT and returns false (the counter is then no longer aligned and
+// must be zeroed by the host before the next launch).
+__device__ __forceinline__ uint64_t grid_sync_target(const uint64_t* ctr, uint32_t nblocks) {
+  return (ld_relaxed_u64(ctr) / nblocks + 1) * nblocks;
+}
+__device__ __forceinline__ bool grid_sync(uint64_t* ctr, uint64_t target, int32_t* status) {
   __shared__ int ok_s;
   __syncthreads();
   if (threadIdx.x == 0) {
     int ok = 1;
     __threadfence();
-    const uint32_t gen = ld_acquire_gpu(state + 1);
-    const uint32_t prev = atom_add_acq_rel_gpu(state, 1u);
-    if (prev == nblocks - 1) {
-      state[0] = 0u;
-      __threadfence();
-      st_release_gpu(state + 1, gen + 1u);
-    } else {
+    red_release_add_u64(ctr, 1ull);
+    if (ld_acquire_u64(ctr) < target) {
       const unsigned long long t0 = global_ns();
-      while (ld_acquire_gpu(state + 1) == gen) {
-        __nanosleep(32);
+      while (ld_acquire_u64(ctr) < target) {
         if (global_ns() - t0 > kWaitLimitNs) {
           ok = 0;
           set_status(status, MIE_ERR_TIMEOUT);
@@ -176,7 +194,6 @@ __device__ __forceinline__ bool grid_barrier(uint32_t* state, uint32_t nblocks, 
         }
       }
     }
-    __threadfence();
     ok_s = ok;
   }
   __syncthreads();

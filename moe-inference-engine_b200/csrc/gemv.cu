@@ -4,15 +4,17 @@
 //                    k / v into the cache slot of the device position
 //                    (reference: src/moe_engine/model.py:226-234,247,495,557-558;
 //                    the paged slot math of model.py:145-147,167-178).
-//  * proj_kernel     out += W in + b (out_proj + residual, model.py:268-269,495).
+//  * proj_kernel     out += W in + b (out_proj + residual, model.py:268-269,495),
+//                    optionally merging split-K attention partials into `in`.
 //  * lmhead_kernel   final norm -> tied LM head [V, D] -> argmax (ties -> lower
 //                    id) + the step's device bookkeeping (model.py:562-565,
 //                    600-603,615).
 //
-// All three stream their weight rows with the TMA bulk ring of stream.cuh.
-// Weights do not depend on the producer grid, so the first ring slots are
-// filled BEFORE griddepcontrol.wait: under programmatic dependent launch the
-// weight fetch overlaps the previous kernel.
+// A warp owns whole weight rows and loads them straight into registers
+// (stream.cuh).  Rows are static, so each warp's first rows are requested
+// BEFORE griddepcontrol.wait: under programmatic dependent launch the weight
+// fetch overlaps the previous kernel.  The LM head keeps the next batch of
+// rows in flight while it reduces the current one.
 #include <utility>
 
 #include "kernels.h"
@@ -22,26 +24,12 @@ namespace mie {
 
 namespace {
 
-constexpr int kMaxChunks = 160;
-constexpr int kThreads = 256;
+// Attention merge in proj_kernel: heads x splits weights in static shared memory.
+constexpr int kMaxMergeHeads = 64;
+constexpr int kMaxMergeSplits = 64;
 
-struct GemvSmem {
-  Ring R;
-  float* xs;
-  float* res;
-  Chunk* chunks;
-};
-
-__device__ __forceinline__ GemvSmem gemv_smem(uint8_t* smem, const GemvLayout& L) {
-  GemvSmem g;
-  g.R.bar = reinterpret_cast<uint64_t*>(smem + L.off_bar);
-  g.R.data = smem + L.off_ring;
-  g.R.nslot = L.nslot;
-  g.R.slot_bytes = L.slot_bytes;
-  g.xs = reinterpret_cast<float*>(smem + L.off_x);
-  g.res = reinterpret_cast<float*>(smem + L.off_res);
-  g.chunks = reinterpret_cast<Chunk*>(smem + L.off_chunks);
-  return g;
+__device__ __forceinline__ const uint4* row_ptr(const void* base, int64_t row, int64_t row_bytes) {
+  return reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(base) + row * row_bytes);
 }
 
 // ---------------------------------------------------------------------------
@@ -49,58 +37,42 @@ __device__ __forceinline__ GemvSmem gemv_smem(uint8_t* smem, const GemvLayout& L
 // ---------------------------------------------------------------------------
 // Work unit = one RoPE pair of one head of one section (q, k or v): rows
 // (h*hd + i) and (h*hd + i + hd/2) of that section, i < hd/2.  A CTA owns a
-// contiguous unit range, i.e. for each (section, head) it touches two
-// contiguous row runs, so no weight repacking is needed.
-enum : uint8_t { kTagFirstHalf = 0, kTagSecondHalf = 1 };
-
+// contiguous unit range; warp w takes units u0 + w, u0 + w + nwarps, ...
+// Both rows of a unit are reduced by the same warp, so lane 0 applies RoPE and
+// stores without any exchange.
 template <typename W>
-__global__ void __launch_bounds__(kThreads) qkv_kernel(const mie_qkv_args a, GemvLayout L) {
-  extern __shared__ __align__(128) uint8_t smem[];
-  GemvSmem S = gemv_smem(smem, L);
-  __shared__ float red[kThreads / 32];
-  __shared__ int n_s;
+__global__ void __launch_bounds__(512) qkv_kernel(const mie_qkv_args a, GemvLayout L) {
+  extern __shared__ __align__(16) float xs[];  // [D]
+  __shared__ float red[16];
   __shared__ int pos_s;
-  __shared__ int64_t slot_off_s;
+  __shared__ int64_t slot_off_s, tok_s;
+  constexpr int PV = Elem<W>::kPerVec;
   const int D = a.hidden_dim, H = a.num_heads, hd = a.head_dim, half = hd / 2;
   const int U = 3 * H * half;
-  const int G = gridDim.x, c = blockIdx.x, tid = threadIdx.x;
+  const int G = gridDim.x, c = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int NW = blockDim.x >> 5;
   int u0, u1;
   split_range(U, c, G, &u0, &u1);
   const int nu = u1 - u0;
-  float* resA = S.res;
-  float* resB = S.res + L.max_units;
-  const uint64_t pol = policy_evict_first();
-  const uint32_t row_bytes = (uint32_t)(D * sizeof(W));
-  const int cap = (int)(L.slot_bytes / row_bytes);
+  const int nvec = D / PV;
+  const int64_t row_bytes = (int64_t)D * sizeof(W);
+  const bool one_seg = nvec <= Seg<W>::kVecs;
+  auto unit_rows = [&](int u, int64_t* ra) {
+    const int grp = u / half, i = u - grp * half, sec = grp / H, h = grp - sec * H;
+    *ra = (int64_t)sec * D + (int64_t)h * hd + i;
+  };
 
-  if (tid == 0) {
-    ring_init(S.R);
-    int n = 0;
-    bool ok = true;
-    for (int u = u0; u < u1;) {
-      const int grp = u / half, i0 = u - grp * half;
-      const int i1 = min(half, i0 + (u1 - u));
-      const int sec = grp / H, h = grp - sec * H;
-      const int64_t base = (int64_t)sec * D + (int64_t)h * hd;
-      ok &= push_rows(S.chunks, &n, kMaxChunks, a.w, base + i0, i1 - i0, row_bytes, cap, kTagFirstHalf, 0, u - u0);
-      ok &= push_rows(S.chunks, &n, kMaxChunks, a.w, base + half + i0, i1 - i0, row_bytes, cap, kTagSecondHalf, 0,
-                      u - u0);
-      u += i1 - i0;
-    }
-    if (!ok) {
-      set_status(a.status, MIE_ERR_INVALID);
-      n = 0;
-    }
-    n_s = n;
-    for (int i = 0; i < min(n, S.R.nslot); ++i) ring_issue(S.R, S.chunks[i], i, pol);
+  // First unit of this warp: both rows requested before the PDL wait.
+  RowRegs<W> wa, wb;
+  if (one_seg && warp < nu) {
+    int64_t ra;
+    unit_rows(u0 + warp, &ra);
+    row_load<W>(wa, row_ptr(a.w, ra, row_bytes), nvec, 0);
+    row_load<W>(wb, row_ptr(a.w, ra + half, row_bytes), nvec, 0);
   }
-  __syncthreads();
-  const int n = n_s;
 
   pdl_wait();
   if (skip_requested(a.skip)) {
-    if (tid == 0) ring_drain(S.R, 0, min(n, S.R.nslot), a.status);
-    __syncthreads();
     pdl_trigger();
     return;
   }
@@ -124,14 +96,7 @@ __global__ void __launch_bounds__(kThreads) qkv_kernel(const mie_qkv_args a, Gem
     }
     pos_s = p;
     slot_off_s = blk * a.stride_block + (int64_t)(p % a.block_size) * a.stride_tok;
-  }
-  __syncthreads();
-  const int pos = pos_s;
-
-  // input vector: x, or the token embedding (+ learned position) for layer 0
-  if (a.embedding) {
-    __shared__ int64_t tok_s;
-    if (tid == 0) {
+    if (a.embedding) {
       int64_t t = __ldcg(a.token);
       if (t < 0 || t >= a.vocab) {
         set_status(a.status, MIE_ERR_RANGE);
@@ -139,53 +104,65 @@ __global__ void __launch_bounds__(kThreads) qkv_kernel(const mie_qkv_args a, Gem
       }
       tok_s = t;
     }
-    __syncthreads();
+  }
+  __syncthreads();
+  const int pos = pos_s;
+
+  // input vector: x, or the token embedding (+ learned position) for layer 0
+  if (a.embedding) {
     const int64_t tok = tok_s;
     for (int i = tid; i < D; i += blockDim.x) {
       float v = load_any(a.embedding, a.dtype, tok * D + i);
       if (a.pos_embedding) v += load_any(a.pos_embedding, a.dtype, (int64_t)pos * D + i);
-      S.xs[i] = v;
-      if (c == 0) a.x[i] = v;  // residual stream starts at the embedding
+      xs[i] = v;
+      if (c == 0) a.x[i] = v;  // the residual stream starts at the embedding
     }
-    __syncthreads();
-    load_and_norm(S.xs, S.xs, MIE_F32, nullptr, D, a.norm, a.eps, a.norm_w, a.norm_b, a.dtype, red);
+    load_and_norm(xs, nullptr, MIE_F32, nullptr, D, a.norm, a.eps, a.norm_w, a.norm_b, a.dtype, red);
   } else {
-    load_and_norm(S.xs, a.x, MIE_F32, a.x_add, D, a.norm, a.eps, a.norm_w, a.norm_b, a.dtype, red);
+    load_and_norm(xs, a.x, MIE_F32, a.x_add, D, a.norm, a.eps, a.norm_w, a.norm_b, a.dtype, red);
   }
+  float xr[Seg<W>::kNV * PV];
+  load_x_regs<W>(xr, xs, nvec);
 
-  const bool ok = ring_consume(S.R, S.chunks, n, min(n, S.R.nslot), pol, a.status,
-                               [&](int, const Chunk& ch, const uint8_t* s) {
-                                 float* dst = ch.tag == kTagFirstHalf ? resA : resB;
-                                 chunk_dot_rows<W>(s, ch.rows, D, S.xs, [&](int r, float v) { dst[ch.out + r] = v; });
-                               });
-  if (!ok) return;
-
-  // epilogue: bias, RoPE on q / k, stores
   const int64_t slot_off = slot_off_s;
-  for (int k = tid; k < nu; k += blockDim.x) {
-    const int u = u0 + k, grp = u / half, i = u - grp * half;
-    const int sec = grp / H, h = grp - sec * H;
-    const int64_t ra = (int64_t)sec * D + (int64_t)h * hd + i;
-    float x1 = resA[k], x2 = resB[k];
-    if (a.b) {
-      x1 += load_any(a.b, a.dtype, ra);
-      x2 += load_any(a.b, a.dtype, ra + half);
-    }
-    if (sec < 2 && a.rope_cos) {
-      const float cs = a.rope_cos[(int64_t)pos * half + i], sn = a.rope_sin[(int64_t)pos * half + i];
-      const float y1 = x1 * cs - x2 * sn;
-      const float y2 = x2 * cs + x1 * sn;
-      x1 = y1;
-      x2 = y2;
-    }
-    if (sec == 0) {
-      a.q_out[h * hd + i] = x1;
-      a.q_out[h * hd + i + half] = x2;
+  for (int k = warp; k < nu; k += NW) {
+    const int u = u0 + k;
+    int64_t ra;
+    unit_rows(u, &ra);
+    float x1, x2;
+    if (one_seg) {
+      if (k != warp) {
+        row_load<W>(wa, row_ptr(a.w, ra, row_bytes), nvec, 0);
+        row_load<W>(wb, row_ptr(a.w, ra + half, row_bytes), nvec, 0);
+      }
+      x1 = warp_sum(row_dot_regs<W>(wa, xr));
+      x2 = warp_sum(row_dot_regs<W>(wb, xr));
     } else {
-      void* cache = sec == 1 ? a.k_cache : a.v_cache;
-      const int64_t o = slot_off + (int64_t)h * a.stride_head;
-      store_any(cache, a.kv_dtype, o + i, x1);
-      store_any(cache, a.kv_dtype, o + i + half, x2);
+      x1 = warp_row_dot<W>(row_ptr(a.w, ra, row_bytes), nvec, xs);
+      x2 = warp_row_dot<W>(row_ptr(a.w, ra + half, row_bytes), nvec, xs);
+    }
+    if (lane == 0) {
+      const int grp = u / half, i = u - grp * half, sec = grp / H, h = grp - sec * H;
+      if (a.b) {
+        x1 += load_any(a.b, a.dtype, ra);
+        x2 += load_any(a.b, a.dtype, ra + half);
+      }
+      if (sec < 2 && a.rope_cos) {
+        const float cs = a.rope_cos[(int64_t)pos * half + i], sn = a.rope_sin[(int64_t)pos * half + i];
+        const float y1 = x1 * cs - x2 * sn;
+        const float y2 = x2 * cs + x1 * sn;
+        x1 = y1;
+        x2 = y2;
+      }
+      if (sec == 0) {
+        a.q_out[h * hd + i] = x1;
+        a.q_out[h * hd + i + half] = x2;
+      } else {
+        void* cache = sec == 1 ? a.k_cache : a.v_cache;
+        const int64_t o = slot_off + (int64_t)h * a.stride_head;
+        store_any(cache, a.kv_dtype, o + i, x1);
+        store_any(cache, a.kv_dtype, o + i + half, x2);
+      }
     }
   }
 }
@@ -194,51 +171,78 @@ __global__ void __launch_bounds__(kThreads) qkv_kernel(const mie_qkv_args a, Gem
 // out_proj (+ residual): out[r] = (acc ? out[r] : 0) + add[r] + W[r].in + b[r]
 // ---------------------------------------------------------------------------
 template <typename W>
-__global__ void __launch_bounds__(kThreads) proj_kernel(const mie_proj_args a, GemvLayout L) {
-  extern __shared__ __align__(128) uint8_t smem[];
-  GemvSmem S = gemv_smem(smem, L);
-  __shared__ int n_s;
-  const int G = gridDim.x, c = blockIdx.x, tid = threadIdx.x;
+__global__ void __launch_bounds__(256) proj_kernel(const mie_proj_args a, GemvLayout L) {
+  extern __shared__ __align__(16) float xs[];  // [cols]
+  __shared__ float w_s[kMaxMergeHeads * kMaxMergeSplits];
+  constexpr int PV = Elem<W>::kPerVec;
+  const int G = gridDim.x, c = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int NW = blockDim.x >> 5;
   int r0, r1;
   split_range(a.rows, c, G, &r0, &r1);
-  const uint64_t pol = policy_evict_first();
-  const uint32_t row_bytes = (uint32_t)(a.cols * sizeof(W));
-  const int cap = (int)(L.slot_bytes / row_bytes);
-  if (tid == 0) {
-    ring_init(S.R);
-    int n = 0;
-    if (!push_rows(S.chunks, &n, kMaxChunks, a.w, r0, r1 - r0, row_bytes, cap, 0, 0, 0)) {
-      set_status(a.status, MIE_ERR_INVALID);
-      n = 0;
-    }
-    n_s = n;
-    for (int i = 0; i < min(n, S.R.nslot); ++i) ring_issue(S.R, S.chunks[i], i, pol);
-  }
-  __syncthreads();
-  const int n = n_s;
+  const int nr = r1 - r0;
+  const int nvec = a.cols / PV;
+  const int64_t row_bytes = (int64_t)a.cols * sizeof(W);
+  const bool one_seg = nvec <= Seg<W>::kVecs;
+
+  RowRegs<W> wr;
+  if (one_seg && warp < nr) row_load<W>(wr, row_ptr(a.w, r0 + warp, row_bytes), nvec, 0);
+
   pdl_wait();
   if (skip_requested(a.skip)) {
-    if (tid == 0) ring_drain(S.R, 0, min(n, S.R.nslot), a.status);
-    __syncthreads();
     pdl_trigger();
     return;
   }
   pdl_trigger();
-  for (int i = tid; i < a.cols; i += blockDim.x) S.xs[i] = a.in[i];
+  if (a.attn_partials) {
+    // Input = attention output, merged here from the split-K partials
+    // (m, l, acc[hd]) of every head: o = sum_s acc_s e^(m_s - M) / sum_s l_s e^(m_s - M).
+    const int H = a.attn_heads, hd = a.attn_head_dim, Sp = a.attn_splits;
+    auto part = [&](int h, int s) { return a.attn_partials + ((size_t)h * a.attn_max_splits + s) * (hd + 2); };
+    for (int h = warp; h < H; h += NW) {
+      float m[2], l[2];
+      for (int k = 0; k < 2; ++k) {
+        const int s = lane + 32 * k;
+        m[k] = s < Sp ? __ldcg(part(h, s)) : -INFINITY;
+        l[k] = s < Sp ? __ldcg(part(h, s) + 1) : 0.f;
+      }
+      const float M = warp_max(fmaxf(m[0], m[1]));
+      float e[2];
+      for (int k = 0; k < 2; ++k) e[k] = m[k] == -INFINITY ? 0.f : expf(m[k] - M);
+      const float Lsum = warp_sum(l[0] * e[0] + l[1] * e[1]);
+      for (int k = 0; k < 2; ++k) {
+        const int s = lane + 32 * k;
+        if (s < Sp) w_s[h * kMaxMergeSplits + s] = e[k] / Lsum;
+      }
+    }
+    __syncthreads();
+    for (int i = tid; i < H * hd; i += blockDim.x) {
+      const int h = i / hd, d = i - h * hd;
+      float o = 0.f;
+      for (int s = 0; s < Sp; ++s) o = fmaf(w_s[h * kMaxMergeSplits + s], __ldcg(part(h, s) + 2 + d), o);
+      xs[i] = o;
+    }
+  } else {
+    for (int i = tid; i < a.cols; i += blockDim.x) xs[i] = __ldcg(a.in + i);
+  }
   __syncthreads();
-  const bool ok = ring_consume(S.R, S.chunks, n, min(n, S.R.nslot), pol, a.status,
-                               [&](int, const Chunk& ch, const uint8_t* s) {
-                                 chunk_dot_rows<W>(s, ch.rows, a.cols, S.xs,
-                                                   [&](int r, float v) { S.res[ch.out + r] = v; });
-                               });
-  if (!ok) return;
-  for (int k = tid; k < r1 - r0; k += blockDim.x) {
+  float xr[Seg<W>::kNV * PV];
+  if (one_seg) load_x_regs<W>(xr, xs, nvec);
+
+  for (int k = warp; k < nr; k += NW) {
     const int r = r0 + k;
-    float y = S.res[k];
-    if (a.b) y += load_any(a.b, a.dtype, r);
-    if (a.add) y += a.add[r];
-    if (a.accumulate) y += a.out[r];
-    a.out[r] = y;
+    float y;
+    if (one_seg) {
+      if (k != warp) row_load<W>(wr, row_ptr(a.w, r, row_bytes), nvec, 0);
+      y = warp_sum(row_dot_regs<W>(wr, xr));
+    } else {
+      y = warp_row_dot<W>(row_ptr(a.w, r, row_bytes), nvec, xs);
+    }
+    if (lane == 0) {
+      if (a.b) y += load_any(a.b, a.dtype, r);
+      if (a.add) y += __ldcg(a.add + r);
+      if (a.accumulate) y += __ldcg(a.out + r);
+      a.out[r] = y;
+    }
   }
 }
 
@@ -249,58 +253,83 @@ __device__ __forceinline__ bool better(float v, int i, float bv, int bi) {
   return v > bv || (v == bv && i < bi);
 }
 
+// Rows per batch per warp: the next batch's loads are in flight while the
+// current one is reduced (2 x 6 16-byte vectors per lane either way).
 template <typename W>
-__global__ void __launch_bounds__(kThreads) lmhead_kernel(const mie_lmhead_args a, GemvLayout L) {
-  extern __shared__ __align__(128) uint8_t smem[];
-  GemvSmem S = gemv_smem(smem, L);
-  __shared__ float red[kThreads / 32];
-  __shared__ float wbest_v[kThreads / 32];
-  __shared__ int wbest_i[kThreads / 32];
-  __shared__ int n_s, last_s;
+struct LmBatch {
+  static constexpr int kRows = sizeof(W) == 2 ? 2 : 1;
+};
+
+template <typename W>
+__global__ void __launch_bounds__(512) lmhead_kernel(const mie_lmhead_args a, GemvLayout L) {
+  extern __shared__ __align__(16) float xs[];  // [D]
+  __shared__ float red[16];
+  __shared__ float wbest_v[16];
+  __shared__ int wbest_i[16];
+  __shared__ int last_s;
+  constexpr int PV = Elem<W>::kPerVec;
+  constexpr int RB = LmBatch<W>::kRows;
   const int D = a.hidden_dim;
   const int G = gridDim.x, c = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int NW = blockDim.x >> 5;
   int r0, r1;
   split_range(a.vocab, c, G, &r0, &r1);
-  const uint64_t pol = policy_evict_first();
-  const uint32_t row_bytes = (uint32_t)(D * sizeof(W));
-  const int cap = (int)(L.slot_bytes / row_bytes);
-  if (tid == 0) {
-    ring_init(S.R);
-    int n = 0;
-    if (!push_rows(S.chunks, &n, kMaxChunks, a.w, r0, r1 - r0, row_bytes, cap, 0, 0, r0)) {
-      set_status(a.status, MIE_ERR_INVALID);
-      n = 0;
-    }
-    n_s = n;
-    for (int i = 0; i < min(n, S.R.nslot); ++i) ring_issue(S.R, S.chunks[i], i, pol);
+  const int nvec = D / PV;
+  const int64_t row_bytes = (int64_t)D * sizeof(W);
+  const bool one_seg = nvec <= Seg<W>::kVecs;
+  // this warp's rows: r0 + warp + NW * k, k < nmine (ascending)
+  const int nmine = (r1 - r0 - warp + NW - 1) / NW > 0 ? (r1 - r0 - warp + NW - 1) / NW : 0;
+  auto row_of = [&](int k) { return r0 + warp + NW * k; };
+
+  RowRegs<W> cur[RB], nxt[RB];
+  if (one_seg) {
+#pragma unroll
+    for (int r = 0; r < RB; ++r)
+      if (r < nmine) row_load<W>(cur[r], row_ptr(a.w, row_of(r), row_bytes), nvec, 0);
   }
-  __syncthreads();
-  const int n = n_s;
+
   pdl_wait();
   if (skip_requested(a.skip)) {
-    if (tid == 0) ring_drain(S.R, 0, min(n, S.R.nslot), a.status);
-    __syncthreads();
     pdl_trigger();
     return;
   }
   pdl_trigger();
-  load_and_norm(S.xs, a.x, MIE_F32, a.x_add, D, a.norm, a.eps, a.norm_w, a.norm_b, a.dtype, red);
+  load_and_norm(xs, a.x, MIE_F32, a.x_add, D, a.norm, a.eps, a.norm_w, a.norm_b, a.dtype, red);
 
   float best_v = -INFINITY;  // per warp, valid on lane 0
   int best_i = 0x7fffffff;
-  const bool ok = ring_consume(S.R, S.chunks, n, min(n, S.R.nslot), pol, a.status,
-                               [&](int, const Chunk& ch, const uint8_t* s) {
-                                 chunk_dot_rows<W>(s, ch.rows, D, S.xs, [&](int r, float v) {
-                                   const int row = ch.out + r;
-                                   if (a.b) v += load_any(a.b, a.dtype, row);
-                                   if (a.logits) a.logits[row] = v;
-                                   if (better(v, row, best_v, best_i)) {
-                                     best_v = v;
-                                     best_i = row;
-                                   }
-                                 });
-                               });
-  if (!ok) return;
+  auto emit = [&](int row, float v) {
+    if (a.b) v += load_any(a.b, a.dtype, row);
+    if (a.logits) a.logits[row] = v;
+    if (better(v, row, best_v, best_i)) {
+      best_v = v;
+      best_i = row;
+    }
+  };
+  if (one_seg) {
+    float xr[Seg<W>::kNV * PV];
+    load_x_regs<W>(xr, xs, nvec);
+    for (int kb = 0; kb < nmine; kb += RB) {
+#pragma unroll
+      for (int r = 0; r < RB; ++r)
+        if (kb + RB + r < nmine) row_load<W>(nxt[r], row_ptr(a.w, row_of(kb + RB + r), row_bytes), nvec, 0);
+#pragma unroll
+      for (int r = 0; r < RB; ++r) {
+        if (kb + r < nmine) {
+          const float v = warp_sum(row_dot_regs<W>(cur[r], xr));
+          if (lane == 0) emit(row_of(kb + r), v);
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < RB; ++r) cur[r] = nxt[r];
+    }
+  } else {
+    for (int k = 0; k < nmine; ++k) {
+      const float v = warp_row_dot<W>(row_ptr(a.w, row_of(k), row_bytes), nvec, xs);
+      if (lane == 0) emit(row_of(k), v);
+    }
+  }
+
   if (lane == 0) {
     wbest_v[warp] = best_v;
     wbest_i[warp] = best_i;
@@ -309,7 +338,7 @@ __global__ void __launch_bounds__(kThreads) lmhead_kernel(const mie_lmhead_args 
   if (tid == 0) {
     float bv = -INFINITY;
     int bi = 0x7fffffff;
-    for (int w = 0; w < (int)(blockDim.x >> 5); ++w)
+    for (int w = 0; w < NW; ++w)
       if (better(wbest_v[w], wbest_i[w], bv, bi)) {
         bv = wbest_v[w];
         bi = wbest_i[w];
@@ -339,7 +368,7 @@ __global__ void __launch_bounds__(kThreads) lmhead_kernel(const mie_lmhead_args 
   if (a.token_out) *a.token_out = bi;
   if (a.pos) *a.pos = __ldcg(a.pos) + 1;
   if (a.tokens_log && a.log_count) {
-    const int k = *a.log_count;
+    const int k = __ldcg(a.log_count);
     if (k < a.log_capacity) a.tokens_log[k] = bi;
     *a.log_count = k + 1;
   }
@@ -348,54 +377,30 @@ __global__ void __launch_bounds__(kThreads) lmhead_kernel(const mie_lmhead_args 
   *a.counter = 0u;
 }
 
-size_t align128(size_t v) { return (v + 127) & ~size_t(127); }
-
-GemvLayout gemv_layout(int units_per_cta_max, int vec_len, int slot_bytes, int nslot, int res_arrays) {
+GemvLayout vec_layout(int vec_len) {
   GemvLayout L{};
-  L.nslot = nslot;
-  L.slot_bytes = (uint32_t)slot_bytes;
-  L.max_units = units_per_cta_max;
-  size_t off = 0;
-  auto take = [&](size_t bytes) {
-    off = align128(off);
-    const size_t at = off;
-    off += bytes;
-    return (uint32_t)at;
-  };
-  L.off_bar = take(sizeof(uint64_t) * nslot);
-  L.off_ring = take((size_t)nslot * slot_bytes);
-  L.off_x = take(sizeof(float) * vec_len);
-  L.off_res = take(sizeof(float) * (size_t)res_arrays * units_per_cta_max);
-  L.off_chunks = take(sizeof(Chunk) * kMaxChunks);
-  L.smem = (uint32_t)align128(off);
+  L.smem = (uint32_t)(sizeof(float) * ((vec_len + 3) & ~3));
   return L;
 }
 
 }  // namespace
 
-GemvLayout qkv_layout(const mie_qkv_args& a, int grid) {
-  const int U = 3 * a.num_heads * (a.head_dim / 2);
-  return gemv_layout((U + grid - 1) / grid + 1, a.hidden_dim, 16 * 1024, 4, 2);
-}
+GemvLayout qkv_layout(const mie_qkv_args& a, int) { return vec_layout(a.hidden_dim); }
 int qkv_launch(const mie_qkv_args& a, const GemvLayout& L, int grid, cudaStream_t st, bool pdl) {
   auto k = a.dtype == MIE_BF16 ? qkv_kernel<__nv_bfloat16> : qkv_kernel<float>;
-  return launch(k, dim3(grid), dim3(kThreads), L.smem, st, pdl, a, L);
+  return launch(k, dim3(grid), dim3(512), L.smem, st, pdl, a, L);
 }
 
-GemvLayout proj_layout(const mie_proj_args& a, int grid) {
-  return gemv_layout((a.rows + grid - 1) / grid + 1, a.cols, 16 * 1024, 2, 1);
-}
+GemvLayout proj_layout(const mie_proj_args& a, int) { return vec_layout(a.cols); }
 int proj_launch(const mie_proj_args& a, const GemvLayout& L, int grid, cudaStream_t st, bool pdl) {
   auto k = a.dtype == MIE_BF16 ? proj_kernel<__nv_bfloat16> : proj_kernel<float>;
-  return launch(k, dim3(grid), dim3(kThreads), L.smem, st, pdl, a, L);
+  return launch(k, dim3(grid), dim3(256), L.smem, st, pdl, a, L);
 }
 
-GemvLayout lmhead_layout(const mie_lmhead_args& a, int grid) {
-  return gemv_layout(1, a.hidden_dim, 16 * 1024, 6, 1);
-}
+GemvLayout lmhead_layout(const mie_lmhead_args& a, int) { return vec_layout(a.hidden_dim); }
 int lmhead_launch(const mie_lmhead_args& a, const GemvLayout& L, int grid, cudaStream_t st, bool pdl) {
   auto k = a.dtype == MIE_BF16 ? lmhead_kernel<__nv_bfloat16> : lmhead_kernel<float>;
-  return launch(k, dim3(grid), dim3(kThreads), L.smem, st, pdl, a, L);
+  return launch(k, dim3(grid), dim3(512), L.smem, st, pdl, a, L);
 }
 
 void gemv_set_attributes() {

@@ -15,20 +15,16 @@ void note_cuda_error(cudaError_t e, const char* what);
 
 // Shared-memory layout of the MoE kernel (byte offsets into dynamic smem).
 struct MoeLayout {
-  uint32_t off_bar, off_ring, off_router, off_x, off_h, off_res, off_chunks, smem;
-  uint32_t slot_bytes;
-  int nslot;
-  int max_units;  // up-phase units per CTA (upper bound)
-  int max_rows;   // down-phase rows per CTA (upper bound)
-  int route_only; // 1: stop after routing (mie_moe_route)
+  uint32_t off_h, off_res;  // offsets in floats: expert activations [2, Hx], down results [2, max_rows]
+  uint32_t smem;            // dynamic shared memory bytes
+  int max_rows;             // down-phase rows per CTA (upper bound)
+  int route_only;           // 1: stop after routing (mie_moe_route)
 };
 
-// Shared-memory layout of the single-vector GEMV kernels (QKV, proj, LM head).
+// Shared-memory layout of the single-vector GEMV kernels (QKV, proj, LM head):
+// only the fp32 input vector lives in dynamic shared memory.
 struct GemvLayout {
-  uint32_t off_bar, off_ring, off_x, off_res, off_chunks, smem;
-  uint32_t slot_bytes;
-  int nslot;
-  int max_units;
+  uint32_t smem;
 };
 
 struct AttnLayout {

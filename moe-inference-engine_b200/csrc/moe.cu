@@ -4,18 +4,20 @@
 // W1 + activation, selected W2 + weighted combine; src/moe_engine/fused_moe.py
 // :120-262) with ONE persistent launch:
 //
-//   prologue (every CTA, redundantly): x -> norm -> router GEMV (8 x D) ->
-//       top-2 by repeated argmax (ties -> lower id) -> 2-way softmax.
-//   up phase: the 2 x Hx hidden units of the two selected experts are split
-//       evenly over the grid; each CTA streams only its rows of W1 (and W3 for
-//       SwiGLU) with TMA bulk copies and writes h = act(W1 x + b1) (* W3 x).
-//   grid barrier (bounded; the down-phase weights were prefetched before it).
-//   down phase: the D output rows are split over the grid; each CTA streams
-//       its rows of both selected experts' W2 and writes
+//   prologue (every CTA, redundantly): x -> norm -> router GEMV (E x D) ->
+//       top-2 by repeated argmax (ties -> lower id) -> 2-way softmax.  The
+//       router rows are loaded into registers before the PDL wait.
+//   right after routing every warp requests its up rows (W1 [, W3]) of the two
+//       selected experts AND its down rows (W2), all at once, into registers.
+//   up phase: the 2 x Hx hidden units are split evenly over the grid; a warp
+//       reduces its unit's rows and writes h = act(W1 x + b1) (* W3 x).
+//   grid barrier (monotonic counter).
+//   down phase: the D output rows (x 2 experts) are split over the grid; a
+//       warp dots its (already loaded) W2 row with h; the CTA combines
 //       out = (x) + sum_r w_r (W2[e_r] h_r + b2[e_r]).
 //
 // Only the selected experts' bytes are read: router + 2 x (W1 [, W3], W2).
-// The reduction order is fixed, so results are bit-reproducible.
+// Every reduction has a fixed order, so results are bit-reproducible.
 #include "kernels.h"
 #include "stream.cuh"
 
@@ -23,74 +25,62 @@ namespace mie {
 
 namespace {
 
-enum : uint8_t { kTagUpA = 0, kTagUpB = 1, kTagDown = 2 };
-constexpr int kMaxChunks = 96;
+constexpr int kThreads = 512;
+constexpr int kWarps = kThreads / 32;
 
 __device__ __forceinline__ float gelu_erf(float v) { return 0.5f * v * (1.0f + erff(v * 0.7071067811865476f)); }
 __device__ __forceinline__ float silu(float v) { return v / (1.0f + expf(-v)); }
 
-template <typename W>
-__global__ void __launch_bounds__(256) moe_decode_kernel(const mie_moe_args a, MoeLayout L) {
-  extern __shared__ __align__(128) uint8_t smem[];
-  const int D = a.hidden_dim, Hx = a.expert_hidden_dim, E = a.num_experts;
-  const int G = gridDim.x, c = blockIdx.x, tid = threadIdx.x;
-  const bool swiglu = a.act == MIE_ACT_SWIGLU;
+__device__ __forceinline__ const uint4* row_ptr(const void* base, int64_t row, int64_t row_bytes) {
+  return reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(base) + row * row_bytes);
+}
 
-  Ring R;
-  R.bar = reinterpret_cast<uint64_t*>(smem + L.off_bar);
-  R.data = smem + L.off_ring;
-  R.nslot = L.nslot;
-  R.slot_bytes = L.slot_bytes;
-  uint64_t* router_bar = reinterpret_cast<uint64_t*>(smem + L.off_bar) + L.nslot;
-  W* router_s = reinterpret_cast<W*>(smem + L.off_router);
-  float* xs = reinterpret_cast<float*>(smem + L.off_x);
-  float* hs = reinterpret_cast<float*>(smem + L.off_h);       // [2, Hx]
-  float* resA = reinterpret_cast<float*>(smem + L.off_res);   // up results (gate / fc1)
-  float* resB = resA + L.max_units;                           // up results (up)
-  float* resD = resB + L.max_units;                           // down results [2][max_rows]
-  Chunk* chunks = reinterpret_cast<Chunk*>(smem + L.off_chunks);
-  __shared__ float red[8];
+template <typename W>
+__global__ void __launch_bounds__(kThreads) moe_decode_kernel(const mie_moe_args a, MoeLayout L) {
+  extern __shared__ __align__(16) float smem_f[];
+  constexpr int PV = Elem<W>::kPerVec;
+  const int D = a.hidden_dim, Hx = a.expert_hidden_dim, E = a.num_experts;
+  const int G = gridDim.x, c = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const bool swiglu = a.act == MIE_ACT_SWIGLU;
+  float* xs = smem_f;                 // [D] normalised input
+  float* hs = xs + L.off_h;           // [2, Hx] expert activations
+  float* resD = xs + L.off_res;       // [2, max_rows] down-projection results
+  __shared__ float red[kWarps];
   __shared__ float logits_s[32];
   __shared__ int ids_s[2];
   __shared__ float wts_s[2];
-  __shared__ int nchunk_s, first_down_s, issued_s;
+  __shared__ uint64_t target_s;
 
-  const uint64_t pol = policy_evict_first();
-  const uint32_t router_bytes = (uint32_t)(E * D * sizeof(W));
-  if (tid == 0) {
-    ring_init(R);
-    mbar_init(router_bar, 1);
-    fence_barrier_init();
-    // Router weights are static: fetch them before waiting on the producer grid.
-    mbar_arrive_expect_tx(router_bar, router_bytes);
-    for (uint32_t off = 0; off < router_bytes; off += kBulkMax)
-      bulk_g2s(reinterpret_cast<uint8_t*>(router_s) + off, static_cast<const uint8_t*>(a.router_w) + off,
-               min(kBulkMax, router_bytes - off), router_bar);
+  uint64_t* ctr = reinterpret_cast<uint64_t*>(a.sync);
+  const int nvec_d = D / PV, nvec_h = Hx / PV;  // vectors per up row / per down row
+  const int64_t rb_d = (int64_t)D * sizeof(W), rb_h = (int64_t)Hx * sizeof(W);
+  const bool up_regs = nvec_d <= Seg<W>::kVecs;  // one segment: keep rows in registers
+  const bool dn_regs = nvec_h <= Seg<W>::kVecs;
+
+  // Router rows are static: request them before waiting on the producer grid.
+  RowRegs<W> rr[2];
+  if (up_regs) {
+    for (int k = 0; k < 2; ++k)
+      if (warp + kWarps * k < E) row_load<W>(rr[k], row_ptr(a.router_w, warp + kWarps * k, rb_d), nvec_d, 0);
   }
-  __syncthreads();
+  if (tid == 0 && !L.route_only) target_s = grid_sync_target(ctr, (uint32_t)G);
 
   pdl_wait();
   if (skip_requested(a.skip)) {
-    if (tid == 0) mbar_wait(router_bar, 0, a.status);
-    __syncthreads();
     pdl_trigger();
     return;
   }
 
   // ---- prologue: norm + router + top-2 (identical in every CTA) ----
   load_and_norm(xs, a.x, a.x_dtype, nullptr, D, a.norm, a.eps, a.norm_w, a.norm_b, a.dtype, red);
-  const bool rok = mbar_wait(router_bar, 0, a.status);
-  if (!__syncthreads_and(rok)) return;
-  {
-    const int lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
-    constexpr int PV = Elem<W>::kPerVec;
-    const int nvec = D / PV;
-    for (int e = warp; e < E; e += nw) {
-      const uint4* row = reinterpret_cast<const uint4*>(router_s) + (size_t)e * nvec;
-      float acc = 0.f;
-      for (int v = lane; v < nvec; v += kWarp) acc = dot_vec(row[v], xs + v * PV, acc, (const W*)nullptr);
-      acc = warp_sum(acc);
-      if (lane == 0) logits_s[e] = acc;
+  float xr[Seg<W>::kNV * PV];
+  if (up_regs) load_x_regs<W>(xr, xs, nvec_d);
+  for (int k = 0; k < 2; ++k) {
+    const int e = warp + kWarps * k;
+    if (e < E) {
+      const float v = up_regs ? warp_sum(row_dot_regs<W>(rr[k], xr))
+                              : warp_row_dot<W>(row_ptr(a.router_w, e, rb_d), nvec_d, xs);
+      if (lane == 0) logits_s[e] = v;
     }
   }
   __syncthreads();
@@ -129,95 +119,99 @@ __global__ void __launch_bounds__(256) moe_decode_kernel(const mie_moe_args a, M
     return;
   }
 
-  // ---- chunk list: up rows of both selected experts, then down rows ----
+  // ---- this CTA's work: up units [u0, u1), down rows [r0, r1) x 2 experts ----
   const int ebase = a.expert_base;
   const int ecount = a.expert_count > 0 ? a.expert_count : E;
-  const uint32_t row_up = (uint32_t)(D * sizeof(W));
-  const uint32_t row_dn = (uint32_t)(Hx * sizeof(W));
-  const int cap_up = (int)(R.slot_bytes / row_up);
-  const int cap_dn = (int)(R.slot_bytes / row_dn);
   int u0, u1, r0, r1;
   split_range(2 * Hx, c, G, &u0, &u1);
   split_range(D, c, G, &r0, &r1);
-  bool local[2];
+  const int nu = u1 - u0, nr = r1 - r0;
   int le[2];
+  bool local[2];
   for (int r = 0; r < 2; ++r) {
     le[r] = ids_s[r] - ebase;
     local[r] = le[r] >= 0 && le[r] < ecount;
   }
-  if (tid == 0) {
-    int n = 0;
-    bool ok = true;
-    for (int r = 0; r < 2; ++r) {
-      // units of slot r inside [u0, u1)
-      const int lo = max(u0, r * Hx), hi = min(u1, (r + 1) * Hx);
-      if (lo >= hi || !local[r]) continue;
-      const int64_t erow = (int64_t)le[r] * Hx;
-      ok &= push_rows(chunks, &n, kMaxChunks, a.w1, erow + (lo - r * Hx), hi - lo, row_up, cap_up, kTagUpA,
-                      (uint8_t)r, lo - u0);
-      if (swiglu)
-        ok &= push_rows(chunks, &n, kMaxChunks, a.w3, erow + (lo - r * Hx), hi - lo, row_up, cap_up, kTagUpB,
-                        (uint8_t)r, lo - u0);
-    }
-    first_down_s = n;
-    for (int r = 0; r < 2; ++r) {
-      if (r1 <= r0 || !local[r]) continue;
-      ok &= push_rows(chunks, &n, kMaxChunks, a.w2, (int64_t)le[r] * D + r0, r1 - r0, row_dn, cap_dn, kTagDown,
-                      (uint8_t)r, 0);
-    }
-    if (!ok) {
-      set_status(a.status, MIE_ERR_INVALID);
-      n = 0;
-      first_down_s = 0;
-    }
-    nchunk_s = n;
-    const int first = min(n, R.nslot);
-    for (int i = 0; i < first; ++i) ring_issue(R, chunks[i], i, pol);
-    issued_s = first;
-  }
-  for (int i = tid; i < 2 * L.max_rows; i += blockDim.x) resD[i] = 0.f;
-  __syncthreads();
-  const int n = nchunk_s, first_down = first_down_s;
-
-  bool synced = false;
-  auto finish_up_and_sync = [&]() {
-    // h for this CTA's units -> global scratch, then the grid barrier.
-    for (int k = tid; k < u1 - u0; k += blockDim.x) {
-      const int u = u0 + k, r = u / Hx, j = u - r * Hx;
-      if (!local[r]) continue;
-      float pre = resA[k];
-      if (a.b1) pre += load_any(a.b1, a.dtype, (int64_t)le[r] * Hx + j);
-      const float h = swiglu ? silu(pre) * resB[k] : gelu_erf(pre);
-      a.hidden[(int64_t)r * Hx + j] = h;
-    }
-    const bool ok = grid_barrier(a.sync, (uint32_t)G, a.status);
-    synced = true;
-    pdl_trigger();
-    if (ok)
-      for (int i = tid; i < 2 * Hx; i += blockDim.x) hs[i] = __ldcg(a.hidden + i);
-    __syncthreads();
+  // unit k (of this CTA) -> slot r, hidden index j
+  auto unit = [&](int k, int* r, int* j) {
+    const int u = u0 + k;
+    *r = u / Hx;
+    *j = u - *r * Hx;
   };
+  // down pair p -> slot r = p / nr, output row r0 + p % nr
+  auto pair_slot = [&](int p) { return p / nr; };
 
-  const bool ok = ring_consume(R, chunks, n, issued_s, pol, a.status, [&](int i, const Chunk& ch, const uint8_t* s) {
-    if (i == first_down && !synced) finish_up_and_sync();
-    if (ch.tag == kTagDown) {
-      float* dst = resD + ch.sub * L.max_rows;
-      chunk_dot_rows<W>(s, ch.rows, Hx, hs + ch.sub * Hx, [&](int row, float v) { dst[ch.out + row] = v; });
+  // Request the first up unit and the first down pair of this warp together.
+  RowRegs<W> wg, wu, wd;
+  int r_first, j_first;
+  const bool up0 = warp < nu;
+  if (up0) unit(warp, &r_first, &j_first);
+  const bool up0_ok = up0 && local[r_first];
+  if (up_regs && up0_ok) {
+    const int64_t row = (int64_t)le[r_first] * Hx + j_first;
+    row_load<W>(wg, row_ptr(a.w1, row, rb_d), nvec_d, 0);
+    if (swiglu) row_load<W>(wu, row_ptr(a.w3, row, rb_d), nvec_d, 0);
+  }
+  const int np = 2 * nr;
+  const bool dn0 = warp < np && local[pair_slot(warp)];
+  if (dn_regs && dn0) {
+    const int r = pair_slot(warp);
+    row_load<W>(wd, row_ptr(a.w2, (int64_t)le[r] * D + r0 + warp % nr, rb_h), nvec_h, 0);
+  }
+
+  // ---- up phase ----
+  for (int k = warp; k < nu; k += kWarps) {
+    int r, j;
+    unit(k, &r, &j);
+    if (!local[r]) continue;
+    const int64_t row = (int64_t)le[r] * Hx + j;
+    float g, u = 0.f;
+    if (up_regs) {
+      if (k != warp) {
+        row_load<W>(wg, row_ptr(a.w1, row, rb_d), nvec_d, 0);
+        if (swiglu) row_load<W>(wu, row_ptr(a.w3, row, rb_d), nvec_d, 0);
+      }
+      g = warp_sum(row_dot_regs<W>(wg, xr));
+      if (swiglu) u = warp_sum(row_dot_regs<W>(wu, xr));
     } else {
-      float* dst = (ch.tag == kTagUpA ? resA : resB);
-      chunk_dot_rows<W>(s, ch.rows, D, xs, [&](int row, float v) { dst[ch.out + row] = v; });
+      g = warp_row_dot<W>(row_ptr(a.w1, row, rb_d), nvec_d, xs);
+      if (swiglu) u = warp_row_dot<W>(row_ptr(a.w3, row, rb_d), nvec_d, xs);
     }
-  });
-  if (!synced) finish_up_and_sync();
+    if (lane == 0) {
+      if (a.b1) g += load_any(a.b1, a.dtype, row);
+      a.hidden[(int64_t)r * Hx + j] = swiglu ? silu(g) * u : gelu_erf(g);
+    }
+  }
+
+  // ---- grid barrier: every CTA's h is in global memory ----
+  const bool ok = grid_sync(ctr, target_s, a.status);
+  pdl_trigger();
   if (!ok) return;
+  for (int i = tid; i < 2 * Hx; i += blockDim.x) hs[i] = __ldcg(a.hidden + i);
+  __syncthreads();
+
+  // ---- down phase ----
+  for (int p = warp; p < np; p += kWarps) {
+    const int r = pair_slot(p), row = r0 + p % nr;
+    if (!local[r]) continue;
+    float v;
+    if (dn_regs) {
+      if (p != warp) row_load<W>(wd, row_ptr(a.w2, (int64_t)le[r] * D + row, rb_h), nvec_h, 0);
+      v = warp_sum(row_dot<W>(wd, hs + (size_t)r * Hx, nvec_h, 0));
+    } else {
+      v = warp_row_dot<W>(row_ptr(a.w2, (int64_t)le[r] * D + row, rb_h), nvec_h, hs + (size_t)r * Hx);
+    }
+    if (lane == 0) resD[p] = v;
+  }
+  __syncthreads();
 
   // ---- epilogue: weighted combine (+ residual) for rows [r0, r1) ----
-  for (int k = tid; k < r1 - r0; k += blockDim.x) {
+  for (int k = tid; k < nr; k += blockDim.x) {
     const int row = r0 + k;
     float y = 0.f;
     for (int r = 0; r < 2; ++r) {
       if (!local[r]) continue;
-      float v = resD[r * L.max_rows + k];
+      float v = resD[r * nr + k];
       if (a.b2) v += load_any(a.b2, a.dtype, (int64_t)le[r] * D + row);
       y = fmaf(wts_s[r], v, y);
     }
@@ -228,35 +222,21 @@ __global__ void __launch_bounds__(256) moe_decode_kernel(const mie_moe_args a, M
 
 }  // namespace
 
-MoeLayout moe_layout(const mie_moe_args& a, int grid, int slot_bytes, int nslot) {
-  const int wsz = a.dtype == MIE_BF16 ? 2 : 4;
+MoeLayout moe_layout(const mie_moe_args& a, int grid, int, int) {
   MoeLayout L{};
-  L.nslot = nslot;
-  L.slot_bytes = (uint32_t)slot_bytes;
-  L.max_units = (2 * a.expert_hidden_dim + grid - 1) / grid + 1;
   L.max_rows = (a.hidden_dim + grid - 1) / grid + 1;
-  size_t off = 0;
-  auto take = [&](size_t bytes) {
-    off = (off + 127) & ~size_t(127);
-    const size_t at = off;
-    off += bytes;
-    return (uint32_t)at;
-  };
-  L.off_bar = take(sizeof(uint64_t) * (nslot + 1));
-  L.off_ring = take((size_t)nslot * slot_bytes);
-  L.off_router = take((size_t)a.num_experts * a.hidden_dim * wsz);
-  L.off_x = take(sizeof(float) * a.hidden_dim);
-  L.off_h = take(sizeof(float) * 2 * a.expert_hidden_dim);
-  L.off_res = take(sizeof(float) * (2 * L.max_units + 2 * L.max_rows));
-  L.off_chunks = take(sizeof(Chunk) * kMaxChunks);
-  L.smem = (uint32_t)((off + 127) & ~size_t(127));
+  const uint32_t d4 = (uint32_t)((a.hidden_dim + 3) & ~3);
+  const uint32_t h4 = (uint32_t)((2 * a.expert_hidden_dim + 3) & ~3);
+  L.off_h = d4;                 // offsets in floats
+  L.off_res = d4 + h4;
+  L.smem = (L.off_res + 2 * (uint32_t)L.max_rows) * (uint32_t)sizeof(float);
   return L;
 }
 
 int moe_decode_launch(const mie_moe_args& a, const MoeLayout& L, int grid, cudaStream_t st, bool pdl) {
   void (*k)(const mie_moe_args, MoeLayout) =
       a.dtype == MIE_BF16 ? moe_decode_kernel<__nv_bfloat16> : moe_decode_kernel<float>;
-  return launch(k, dim3(grid), dim3(256), L.smem, st, pdl, a, L);
+  return launch(k, dim3(grid), dim3(kThreads), L.smem, st, pdl, a, L);
 }
 
 void moe_set_attributes() {

@@ -1,137 +1,114 @@
-// Row-chunk streaming for the M=1 GEMV kernels.
+// Register-staged row loads for the M=1 GEMV kernels.
 //
-// Every GEMV here reads each weight row exactly once.  A CTA owns a list of
-// "chunks" (runs of consecutive rows, contiguous in HBM); one thread moves each
-// chunk into a shared-memory ring slot with cp.async.bulk (TMA bulk copy,
-// completion counted in bytes on the slot's mbarrier) and all warps consume
-// the slot (one warp per row, 16-byte vector loads from shared memory, a
-// shuffle reduction per row).  Keeping `nslot` chunks in flight per SM hides
-// HBM latency with a single issuing thread.
+// Every GEMV here reads each weight row exactly once.  A warp owns whole rows:
+// lane l loads 16-byte vectors l, l+32, l+64, ... of a row with plain
+// read-only 128-bit loads straight into registers, then forms the dot product
+// with the fp32 input vector and reduces it with shuffles.  A warp issues the
+// loads of several rows before it uses any of them, so each SM keeps tens of
+// KB in flight without shared-memory staging, async-copy units or barriers.
+// Rows whose weights do not depend on the producer grid are loaded before the
+// kernel waits on it (programmatic dependent launch), i.e. while the previous
+// kernel still runs.
+//
+// A row is processed in segments of 768 elements (3 vectors per lane for
+// bf16, 6 for fp32); longer rows loop over segments.
 #pragma once
+
+#include <cstdio>
 
 #include "common.cuh"
 
 namespace mie {
 
-struct Chunk {
-  const uint8_t* src;  // first byte of the first row (16-byte aligned)
-  uint32_t bytes;      // rows * row_bytes (multiple of 16)
-  uint16_t rows;
-  uint8_t tag;         // kernel-defined meaning
-  uint8_t sub;         // kernel-defined (e.g. top-k slot)
-  int32_t out;         // kernel-defined output index of the first row
+// 16-byte vectors per lane per row segment (a segment = 768 elements).
+template <typename W>
+struct Seg {
+  static constexpr int kNV = 768 / (kWarp * Elem<W>::kPerVec);  // bf16: 3, fp32: 6
+  static constexpr int kVecs = kNV * kWarp;                      // vectors per segment
 };
 
-struct Ring {
-  uint64_t* bar;  // [nslot] mbarriers (count 1, tx-counted)
-  uint8_t* data;  // nslot * slot_bytes, 128-byte aligned
-  int nslot;
-  uint32_t slot_bytes;
-  __device__ __forceinline__ uint8_t* slot(int i) const { return data + (size_t)i * slot_bytes; }
+template <typename W>
+struct RowRegs {
+  uint4 w[Seg<W>::kNV];
 };
 
-// thread 0: initialise the ring's barriers (call before __syncthreads()).
-__device__ __forceinline__ void ring_init(const Ring& R) {
-  for (int s = 0; s < R.nslot; ++s) mbar_init(&R.bar[s], 1);
-  fence_barrier_init();
-}
+__device__ __forceinline__ uint4 ld_weights(const uint4* p) { return __ldg(p); }
 
-// thread 0: start the copy of chunk i into slot i % nslot.
-__device__ __forceinline__ void ring_issue(const Ring& R, const Chunk& c, int i, uint64_t policy) {
-  const int s = i % R.nslot;
-  uint64_t* bar = &R.bar[s];
-  mbar_arrive_expect_tx(bar, c.bytes);
-  uint8_t* dst = R.slot(s);
-  for (uint32_t off = 0; off < c.bytes; off += kBulkMax) {
-    const uint32_t n = (c.bytes - off) < kBulkMax ? (c.bytes - off) : kBulkMax;
-    bulk_g2s_stream(dst + off, c.src + off, n, bar, policy);
+// Load segment `seg` of a row (nvec 16-byte vectors) into this lane's registers.
+template <typename W>
+__device__ __forceinline__ void row_load(RowRegs<W>& r, const uint4* row, int nvec, int seg) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int j = 0; j < Seg<W>::kNV; ++j) {
+    const int v = seg * Seg<W>::kVecs + lane + kWarp * j;
+    r.w[j] = v < nvec ? ld_weights(row + v) : make_uint4(0u, 0u, 0u, 0u);
   }
 }
 
-// thread 0: wait (bounded) for chunks [from, to) that were issued but will not
-// be consumed, so no bulk copy is still writing shared memory at exit.
-__device__ __forceinline__ void ring_drain(const Ring& R, int from, int to, int32_t* status) {
-  for (int i = from; i < to; ++i) mbar_wait(&R.bar[i % R.nslot], (i / R.nslot) & 1, status);
-}
-
-// Consume chunks [0, n) in order.  `issued` chunks were started already
-// (issued <= nslot); later ones are started as slots free up.  process(i,
-// chunk, slot_ptr) is called by every thread.  Returns false if a wait gave up
-// (after draining what is still in flight).
-template <typename Process>
-__device__ __forceinline__ bool ring_consume(const Ring& R, const Chunk* chunks, int n, int issued,
-                                             uint64_t policy, int32_t* status, Process&& process) {
-  for (int i = 0; i < n; ++i) {
-    if (threadIdx.x == 0) {
-      // Top up the ring: chunk i must have been issued before we wait on it.
-      while (issued < n && issued < i + R.nslot) {
-        if (issued >= R.nslot) fence_proxy_async_smem();
-        ring_issue(R, chunks[issued], issued, policy);
-        ++issued;
-      }
-    }
-    const int s = i % R.nslot;
-    const bool ok = mbar_wait(&R.bar[s], (i / R.nslot) & 1, status);
-    if (!__syncthreads_and(ok)) {
-      if (threadIdx.x == 0) ring_drain(R, i + 1, min(n, i + R.nslot), status);
-      return false;
-    }
-    process(i, chunks[i], R.slot(s));
-    __syncthreads();
-  }
-  return true;
-}
-
-// Dot every row of a chunk (rows x row_elems elements of W, row-major in
-// shared memory) with the fp32 vector `vec` (shared memory).  One warp per row;
-// emit(row, value) runs on lane 0 of the warp that owns the row.
-template <typename W, typename Emit>
-__device__ __forceinline__ void chunk_dot_rows(const uint8_t* slot, int rows, int row_elems,
-                                               const float* __restrict__ vec, Emit&& emit) {
+// This lane's partial dot of a loaded segment with the fp32 vector xs (shared).
+template <typename W>
+__device__ __forceinline__ float row_dot(const RowRegs<W>& r, const float* __restrict__ xs, int nvec, int seg,
+                                         float acc = 0.f) {
   constexpr int PV = Elem<W>::kPerVec;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  const int nvec = row_elems / PV;
-  for (int r = warp; r < rows; r += nw) {
-    const uint4* row = reinterpret_cast<const uint4*>(slot) + (size_t)r * nvec;
-    float acc = 0.f;
-    for (int v = lane; v < nvec; v += kWarp) acc = dot_vec(row[v], vec + v * PV, acc, (const W*)nullptr);
-    acc = warp_sum(acc);
-    if (lane == 0) emit(r, acc);
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int j = 0; j < Seg<W>::kNV; ++j) {
+    const int v = seg * Seg<W>::kVecs + lane + kWarp * j;
+    if (v < nvec) acc = dot_vec(r.w[j], xs + v * PV, acc, (const W*)nullptr);
+  }
+  return acc;
+}
+
+// Same with x already held in registers (segment 0 of xs, see load_x_regs).
+template <typename W>
+__device__ __forceinline__ float row_dot_regs(const RowRegs<W>& r, const float* xr) {
+  constexpr int PV = Elem<W>::kPerVec;
+  float acc = 0.f;
+#pragma unroll
+  for (int j = 0; j < Seg<W>::kNV; ++j) acc = dot_vec(r.w[j], xr + j * PV, acc, (const W*)nullptr);
+  return acc;
+}
+
+// xr[j*PV + e] = xs[(lane + 32 j) * PV + e] for segment 0 (zero past nvec).
+template <typename W>
+__device__ __forceinline__ void load_x_regs(float* xr, const float* xs, int nvec) {
+  constexpr int PV = Elem<W>::kPerVec;
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int j = 0; j < Seg<W>::kNV; ++j) {
+    const int v = lane + kWarp * j;
+#pragma unroll
+    for (int e = 0; e < PV; ++e) xr[j * PV + e] = v < nvec ? xs[v * PV + e] : 0.f;
   }
 }
 
-// Split [begin, end) rows starting at `base` (row_bytes each) into chunks of
-// at most `cap` rows, appending to chunks[*n].  Returns false on overflow.
-__device__ __forceinline__ bool push_rows(Chunk* chunks, int* n, int max_chunks, const void* base,
-                                          int64_t row_begin, int rows, uint32_t row_bytes, int cap,
-                                          uint8_t tag, uint8_t sub, int32_t out) {
-  const uint8_t* p = static_cast<const uint8_t*>(base) + row_begin * (int64_t)row_bytes;
-  for (int r = 0; r < rows; r += cap) {
-    if (*n >= max_chunks) return false;
-    const int k = (rows - r) < cap ? (rows - r) : cap;
-    Chunk c;
-    c.src = p + (int64_t)r * row_bytes;
-    c.bytes = (uint32_t)k * row_bytes;
-    c.rows = (uint16_t)k;
-    c.tag = tag;
-    c.sub = sub;
-    c.out = out + r;
-    chunks[(*n)++] = c;
+// Full dot of one row with xs (any length), loads issued segment by segment.
+template <typename W>
+__device__ __forceinline__ float warp_row_dot(const uint4* row, int nvec, const float* xs) {
+  const int nseg = (nvec + Seg<W>::kVecs - 1) / Seg<W>::kVecs;
+  float acc = 0.f;
+  for (int s = 0; s < nseg; ++s) {
+    RowRegs<W> r;
+    row_load<W>(r, row, nvec, s);
+    acc = row_dot<W>(r, xs, nvec, s, acc);
   }
-  return true;
+  return warp_sum(acc);
 }
 
 // Input-vector prologue shared by the QKV, MoE and LM-head kernels:
 // xs[i] = (x[i] (+ add[i])) then optional RMSNorm / LayerNorm with weight w
-// (and bias b).  Deterministic: every CTA computes bit-identical values.
-// `red` needs blockDim.x/32 floats.
+// (and bias b).  x is a global pointer (read through L2: it was written by an
+// earlier grid), or nullptr when xs already holds the input.  Deterministic:
+// every CTA computes bit-identical values.  `red` needs blockDim.x/32 floats.
 __device__ __forceinline__ void load_and_norm(float* xs, const void* x, int x_dtype, const float* add, int D,
                                               int norm, float eps, const void* w, const void* b, int w_dtype,
                                               float* red) {
-  for (int i = threadIdx.x; i < D; i += blockDim.x) {
-    float v = load_any(x, x_dtype, i);
-    if (add) v += add[i];
-    xs[i] = v;
+  if (x) {
+    for (int i = threadIdx.x; i < D; i += blockDim.x) {
+      float v = x_dtype == MIE_F32 ? __ldcg(static_cast<const float*>(x) + i) : load_any(x, x_dtype, i);
+      if (add) v += __ldcg(add + i);
+      xs[i] = v;
+    }
   }
   __syncthreads();
   if (norm == MIE_NORM_RMS) {

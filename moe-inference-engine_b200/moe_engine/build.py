@@ -49,9 +49,11 @@ def build(force: bool = False, verbose: bool = False) -> str:
         return OUT
     os.makedirs(OUT_DIR, exist_ok=True)
     tmp = OUT + ".tmp"
+    # MIE_NVCC_FLAGS adds flags, e.g. "-DMIE_DEBUG_CHECKS" for the self-checking build.
+    extra = os.environ.get("MIE_NVCC_FLAGS", "").split()
     cmd = [
         nvcc(), *ARCH_FLAGS, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-shared",
-        "-I", INCLUDE, "-o", tmp, *[os.path.join(CSRC, s) for s in SOURCES],
+        *extra, "-I", INCLUDE, "-o", tmp, *[os.path.join(CSRC, s) for s in SOURCES],
     ]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")

@@ -44,7 +44,7 @@ class AttnArgs(ctypes.Structure):
         ("block_size", _i), ("stride_block", _i64), ("stride_head", _i64), ("stride_tok", _i64),
         ("ctx_len", _i), ("ctx_dev", _p), ("ctx_dev_offset", _i), ("max_ctx", _i), ("scale", _f),
         ("out", _p), ("partials", _p), ("counters", _p), ("splits", _i), ("max_splits", _i),
-        ("new_token_last", _i), ("status", _p), ("skip", _p),
+        ("new_token_last", _i), ("status", _p), ("skip", _p), ("defer_merge", _i),
     ]
 
 
@@ -64,6 +64,8 @@ class ProjArgs(ctypes.Structure):
     _fields_ = [
         ("dtype", _i), ("rows", _i), ("cols", _i), ("w", _p), ("b", _p), ("in_", _p),
         ("out", _p), ("add", _p), ("accumulate", _i), ("status", _p), ("skip", _p), ("grid", _i),
+        ("attn_partials", _p), ("attn_heads", _i), ("attn_head_dim", _i), ("attn_splits", _i),
+        ("attn_max_splits", _i),
     ]
 
 
