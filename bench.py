@@ -216,6 +216,8 @@ def run_b200(args, rank, world, device):
     P = cache.position
     cache.reserve(P + NEW_TOKENS)
     graph = runner.graph_for(cache, P + NEW_TOKENS)
+    # one persistent launch per token, else 4 launches per layer + the LM head
+    launches_per_token = 1 if runner.uses_persistent(cache) else 4 * 12 + 1
 
     def reset():
         runner.token.fill_(first)
@@ -351,7 +353,7 @@ def run_b200(args, rank, world, device):
             "d2h_bytes_per_step": (PROMPT_LEN + NEW_TOKENS) * 8,
             "note": "Model.generate from a pinned host prompt to host tokens, prefill included",
         },
-        "gpu_launches": args.steps * NEW_TOKENS * (4 * 12 + 1),
+        "gpu_launches": args.steps * NEW_TOKENS * launches_per_token,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(seconds=args.cpu_seconds)

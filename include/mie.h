@@ -20,7 +20,8 @@
  *   mie_lmhead_argmax    <- src/moe_engine/model.py:564-565,600-603 (final norm,
  *                           tied LM head, greedy argmax)
  *   mie_decode_step      <- src/moe_engine/model.py:543-565 (Model.forward for one
- *                           decode token) as one launch sequence
+ *                           decode token) as one launch sequence, or as one
+ *                           persistent launch (mie_step_scratch_bytes)
  */
 #ifndef MIE_H
 #define MIE_H
@@ -289,6 +290,12 @@ typedef struct mie_step_desc {
   int max_splits;
   int lm_grid;                   /* 0 = one per SM */
   int use_pdl;                   /* programmatic dependent launch between kernels */
+  /* Persistent step: when non-NULL, mie_decode_step runs the whole step as ONE
+   * launch of one CTA per SM whose phases exchange their results through this
+   * buffer (see mie_step_scratch_bytes).  Zeroed by the caller once, reused
+   * for every step; zero it again after a step reported a device failure. */
+  uint64_t* step_scratch;
+  int64_t step_scratch_bytes;
 } mie_step_desc;
 
 /* Library management */
@@ -327,8 +334,16 @@ int mie_proj_residual(const mie_proj_args* a, void* stream);
 int mie_lmhead_argmax(const mie_lmhead_args* a, void* stream);
 
 /* Whole-step launchers.  mie_decode_layer / mie_decode_head let a caller put a
- * collective between a layer's MoE and the next consumer (expert parallel). */
+ * collective between a layer's MoE and the next consumer (expert parallel).
+ * mie_decode_step runs the persistent single-launch step when d->step_scratch
+ * is set (MIE_ERR_UNSUPPORTED when the shapes have no persistent kernel), else
+ * the per-op launch sequence. */
 int mie_decode_step(const mie_step_desc* d, void* stream);
+/* Bytes of d->step_scratch the persistent step needs for this description on
+ * the current device (> 0), or -status when the persistent step does not
+ * support it (hidden_dim and expert_hidden_dim <= 768, head_dim <= 128, no
+ * expert parallelism, num_layers <= 48).  Launches nothing. */
+int64_t mie_step_scratch_bytes(const mie_step_desc* d);
 int mie_decode_layer(const mie_step_desc* d, int layer, void* stream);
 int mie_decode_head(const mie_step_desc* d, void* stream);
 

@@ -307,6 +307,35 @@ mie_lmhead_args step_lmhead(const mie_step_desc& d) {
   return a;
 }
 
+// Persistent step: geometry for this device plus the checks the per-op
+// launchers would otherwise make (alignment of every weight row base and of
+// the K/V caches, which the kernel copies in 16-byte units).
+int persistent_geometry(const mie_step_desc& d, StepGeom* g) {
+  if (!d.layers || !d.embedding || !d.token || !d.pos || !d.x || !d.lm_partial_val || !d.lm_partial_idx ||
+      !d.lm_counter)
+    return MIE_ERR_INVALID;
+  const int rc = step_geometry(d, num_sms(), g);
+  if (rc) return rc;
+  if (d.norm != MIE_NORM_NONE && !d.final_norm_w) return MIE_ERR_INVALID;
+  if ((d.rope_cos == nullptr) != (d.rope_sin == nullptr)) return MIE_ERR_INVALID;
+  if (d.block_size <= 0 || d.max_pos <= 0) return MIE_ERR_INVALID;
+  if (!aligned16(d.embedding) || (d.final_norm_w && !aligned16(d.final_norm_w)) ||
+      (d.final_norm_b && !aligned16(d.final_norm_b)))
+    return MIE_ERR_INVALID;
+  for (int l = 0; l < d.num_layers; ++l) {
+    const mie_layer_desc& y = d.layers[l];
+    if (!y.qkv_w || !y.out_w || !y.router_w || !y.w1 || !y.w2 || !y.k_cache || !y.v_cache) return MIE_ERR_INVALID;
+    if (d.act == MIE_ACT_SWIGLU && !y.w3) return MIE_ERR_INVALID;
+    if (d.norm == MIE_NORM_NONE || !y.attn_norm_w || !y.moe_norm_w) return MIE_ERR_UNSUPPORTED;
+    if (!aligned16(y.qkv_w) || !aligned16(y.out_w) || !aligned16(y.router_w) || !aligned16(y.w1) ||
+        !aligned16(y.w2) || (y.w3 && !aligned16(y.w3)) || !aligned16(y.k_cache) || !aligned16(y.v_cache) ||
+        !aligned16(y.attn_norm_w) || !aligned16(y.moe_norm_w) || (y.attn_norm_b && !aligned16(y.attn_norm_b)) ||
+        (y.moe_norm_b && !aligned16(y.moe_norm_b)))
+      return MIE_ERR_INVALID;
+  }
+  return MIE_OK;
+}
+
 int check_step(const mie_step_desc& d) {
   if (!d.layers || d.num_layers <= 0 || !d.embedding || !d.token || !d.pos || !d.x || !d.q || !d.attn_out ||
       !d.moe_hidden || !d.moe_sync || !d.lm_partial_val || !d.lm_partial_idx || !d.lm_counter)
@@ -355,6 +384,7 @@ int mie_init(int device) {
   moe_set_attributes();
   attn_set_attributes();
   gemv_set_attributes();
+  step_set_attributes();
   (void)num_sms();
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) note_cuda_error(e, "mie_init");
@@ -423,11 +453,26 @@ int mie_decode_head(const mie_step_desc* d, void* stream) {
 
 int mie_decode_step(const mie_step_desc* d, void* stream) {
   if (!d) return MIE_ERR_INVALID;
+  if (d->step_scratch) {
+    StepGeom g;
+    const int rc = persistent_geometry(*d, &g);
+    if (rc) return rc;
+    if (d->step_scratch_bytes < g.words * (int64_t)sizeof(uint64_t)) return MIE_ERR_INVALID;
+    return step_launch(*d, g, d->step_scratch, static_cast<cudaStream_t>(stream));
+  }
   for (int l = 0; l < d->num_layers; ++l) {
     const int rc = mie_decode_layer(d, l, stream);
     if (rc) return rc;
   }
   return mie_decode_head(d, stream);
+}
+
+int64_t mie_step_scratch_bytes(const mie_step_desc* d) {
+  if (!d) return -MIE_ERR_INVALID;
+  StepGeom g;
+  const int rc = persistent_geometry(*d, &g);
+  if (rc) return -(int64_t)rc;
+  return g.words * (int64_t)sizeof(uint64_t);
 }
 
 }  // extern "C"

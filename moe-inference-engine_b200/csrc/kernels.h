@@ -37,6 +37,42 @@ struct AttnLayout {
 // limit minus the kernels' static shared memory).
 constexpr int kMaxDynSmem = 220 * 1024;
 
+// ---- persistent decode step (step.cu) ----
+constexpr int kStepThreads = 512;                   // one CTA of 16 warps per SM
+constexpr int kMaxStepLayers = 48;                  // layer descriptors carried in the launch parameters
+constexpr uint32_t kStepKvChunkBytes = 32 * 1024;   // K+V of one split staged in shared memory at a time
+constexpr int kStepHeadStagesMax = 8;               // LM-head ring stages
+constexpr uint32_t kStepMaxSmem = 224 * 1024;       // dynamic shared memory of the step kernel (static: < 3 KB)
+
+// Geometry of one persistent step launch: exchange-buffer offsets (64-bit
+// words into the caller's scratch) and the shared-memory layout (bytes).
+struct StepGeom {
+  uint64_t* ll;   // scratch base
+  int64_t words;  // scratch size in 64-bit words
+  int64_t off_a[2], off_b[2], off_c[2], off_d[2], off_e[2];
+  int G;          // CTAs (one per SM)
+  int S;          // attention splits per head
+  int natt;       // attention CTAs (num_heads * S)
+  int chunk_tok;  // K/V tokens per shared-memory chunk
+  int q_stage;    // q rows of the head staged in shared memory (the rest are read from global memory)
+  int moe_staged; // 1: the selected experts' rows are staged in shared memory
+  int nr_max;     // out_proj / down rows of one CTA (upper bound)
+  int head_rows, head_stages;  // LM-head ring: rows per stage, stages
+  // shared memory (byte offsets): fp32 vectors (x, normalised x, x_mid, expert
+  // activations, attention output, q + this CTA's k / v values, scratch,
+  // scores), the attention norm weights, the attention staging area sm_qw ..
+  // sm_kv + K/V chunk (reused as the LM-head ring), and sm_moe (out_proj rows,
+  // router, MoE norm weights; after routing the selected experts' rows)
+  uint32_t sm_x, sm_xn, sm_xm, sm_h, sm_o, sm_qk, sm_acc, sm_sc, sm_anw;
+  uint32_t sm_qw, sm_kvw, sm_kv, sm_moe, smem;
+};
+
+struct StepParams {
+  mie_step_desc d;  // d.layers is not used on the device
+  StepGeom g;
+  mie_layer_desc layers[kMaxStepLayers];
+};
+
 // Allow the largest dynamic shared memory the device permits next to the
 // kernel's static shared memory.
 template <typename Kernel>
@@ -96,6 +132,11 @@ int proj_launch(const mie_proj_args& a, const GemvLayout& L, int grid, cudaStrea
 GemvLayout lmhead_layout(const mie_lmhead_args& a, int grid);
 int lmhead_launch(const mie_lmhead_args& a, const GemvLayout& L, int grid, cudaStream_t st, bool pdl);
 void gemv_set_attributes();
+
+// step.cu
+int step_geometry(const mie_step_desc& d, int grid, StepGeom* g);
+int step_launch(const mie_step_desc& d, const StepGeom& g, uint64_t* scratch, cudaStream_t st);
+void step_set_attributes();
 
 int num_sms();
 

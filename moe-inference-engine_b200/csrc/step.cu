@@ -1,0 +1,1184 @@
+// Persistent decode step: the whole batch-one decode step (all layers + LM
+// head) in ONE launch of one CTA per SM, sm_100a.
+//
+// The per-op launch sequence (qkv -> attention -> out_proj -> MoE per layer,
+// LM head at the end; src/moe_engine/model.py:543-565 of the reference) pays a
+// launch, a prologue and a grid-wide drain per kernel.  Here every CTA walks
+// the same program of phases and the phases hand their results to each other
+// through small "LL" exchanges in global memory: every value travels as one
+// 64-bit word {f32 value, u32 tag} written with a single 64-bit store, and a
+// consumer polls the words it needs until their tag equals the tag of the
+// current (step, layer).  A word is complete the moment its tag is visible, so
+// no fence, counter or grid barrier is needed.
+//
+// Phases of layer l (G CTAs; the first H*S CTAs are attention CTAs, CTA
+// (h, s) = split s of head h):
+//
+//   ATT    every CTA: x (exchange A, or the token embedding for l = 0) ->
+//          norm.  Attention CTAs compute q_h (all hd rows of head h) locally,
+//          plus their share of the new token's k (RoPE pairs) and v rows,
+//          which they store into the cache slot of the position.  Online
+//          softmax over the split's share of the OLD tokens, and the split's
+//          share of q.k_new.  -> exchange B: (m, l, q.k_new part, acc).
+//   MERGE  attention CTAs: the S entries of their head -> log-sum-exp merge
+//          with the new token as one more term -> o_h for their v dims ->
+//          exchange C.
+//   PROJ   every CTA: its rows of out_proj + bias + residual -> exchange D
+//          (x_mid).
+//   UP     every CTA: x_mid -> norm -> router -> top-2 (ties to the lower id)
+//          -> 2-way softmax -> its up units (gate [+ up] rows) of the two
+//          selected experts: h = act(...) -> exchange E.
+//   DOWN   every CTA: its output rows: x_mid + sum_k w_k (W2_k h_k + b2_k) ->
+//          exchange A of layer l + 1.
+//
+// Then HEAD: x_L -> final norm -> tied LM head rows -> per-CTA argmax -> the
+// last CTA to arrive reduces the CTA results and does the step's device
+// bookkeeping (next token, position + 1, token log, EOS flag, step counter).
+//
+// Weights and old K/V never travel through registers ahead of time: they are
+// staged in shared memory by bulk copies (cp.async.bulk, completion counted on
+// an mbarrier) issued long before they are needed -- layer l + 1's attention
+// inputs right after layer l's attention, layer l + 1's out_proj rows, router
+// rows and norm weights right after layer l's down projection, the selected
+// experts' rows right after routing, the LM-head rows through a ring.  Every
+// GEMV then runs from shared memory.
+//
+// The code is organised for the instruction cache: one decode step runs every
+// phase of every layer, so the code of one layer should stay resident.  The
+// phases are thin sequences of calls to a few shared routines (exchange
+// receive, norm, GEMV over staged rows, attention core), and loops that need
+// no unrolling are not unrolled.
+//
+// Exchange buffers are reused every second layer (A, B, C, D, E each have two
+// copies, by layer parity).  A CTA writes a buffer of layer l + 2 only after it
+// consumed exchange D of layer l + 1, to which every CTA contributed after it
+// finished reading layer l's copy, so a copy is never overwritten while read.
+// Every wait is bounded (kWaitLimitNs); a CTA that gives up records
+// MIE_ERR_TIMEOUT, raises the abort word so the others stop waiting, waits
+// (bounded) for its own bulk copies still in flight, and leaves.  After that
+// the host must zero the scratch before the next step.
+//
+// Every reduction has a fixed order: results are bit-reproducible run to run.
+#include "kernels.h"
+#include "stream.cuh"
+
+namespace mie {
+
+namespace {
+
+constexpr int kST = kStepThreads;
+constexpr int kSW = kST / 32;
+
+// scratch header words
+constexpr int kHdrStep = 0;   // completed steps (the step counter)
+constexpr int kHdrAbort = 1;  // nonzero: a CTA gave up waiting
+
+#ifdef MIE_STEP_STAMPS
+// Phase timestamps for performance analysis builds only: [CTA][layer][point].
+constexpr int kStampLayers = kMaxStepLayers + 1, kStampPoints = 32;
+__device__ unsigned long long g_step_stamps[160 * kStampLayers * kStampPoints];
+#define STEP_STAMP(l, k) \
+  do { \
+    if (threadIdx.x == 0) g_step_stamps[(blockIdx.x * kStampLayers + (l)) * kStampPoints + (k)] = global_ns(); \
+  } while (0)
+#else
+#define STEP_STAMP(l, k) \
+  do { \
+  } while (0)
+#endif
+
+// ---------------------------------------------------------------------------
+// Exchange words
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void ll_put(uint64_t* p, float v, uint32_t tag) {
+  const uint64_t w = ((uint64_t)tag << 32) | (uint64_t)__float_as_uint(v);
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ uint64_t ll_ld(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint32_t ll_tag(uint64_t w) { return (uint32_t)(w >> 32); }
+__device__ __forceinline__ float ll_val(uint64_t w) { return __uint_as_float((uint32_t)w); }
+
+// Slow path of a wait, every 64 polls: true when another CTA raised the abort
+// word or this wait has run for kWaitLimitNs (then MIE_ERR_TIMEOUT is
+// recorded and the abort word raised).
+__device__ __noinline__ bool ll_give_up(uint64_t* hdr, int32_t* status, unsigned long long* t0) {
+  if (ll_ld(hdr + kHdrAbort)) return true;
+  const unsigned long long t = global_ns();
+  if (!*t0) {
+    *t0 = t;
+    return false;
+  }
+  if (t - *t0 <= kWaitLimitNs) return false;
+  set_status(status, MIE_ERR_TIMEOUT);
+  atomicExch(reinterpret_cast<unsigned long long*>(hdr + kHdrAbort), 1ull);
+  return true;
+}
+
+// Receive n exchange words: dst[i] = value of buf[idx(i)] (idx(i) = i when
+// gather is null, else gather[i]) once its tag equals `tag`.  Thread t owns
+// words t, t + kST, ...; all of its pending words are polled again together,
+// so a thread sees its last word one load round trip after it landed.  Called
+// by every thread; true for all of them, or false for all when a wait gave up.
+__device__ __noinline__ bool recv(const uint64_t* buf, int n, uint32_t tag, float* dst, const int* gather,
+                                  uint64_t* hdr, int32_t* status) {
+  int bad = 0;
+#pragma unroll 1
+  for (int i0 = threadIdx.x; i0 < n && !bad; i0 += kST * 4) {
+    uint64_t w[4];
+    int at[4];
+    unsigned need = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int i = i0 + kST * j;
+      at[j] = i < n ? (gather ? gather[i] : i) : 0;
+      if (i < n) {
+        w[j] = ll_ld(buf + at[j]);
+        need |= 1u << j;
+      }
+    }
+    unsigned long long t0 = 0;
+#pragma unroll 1
+    for (int it = 1;; ++it) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if ((need >> j & 1u) && ll_tag(w[j]) == tag) {
+          dst[i0 + kST * j] = ll_val(w[j]);
+          need &= ~(1u << j);
+        }
+      }
+      if (!need) break;
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (need >> j & 1u) w[j] = ll_ld(buf + at[j]);
+      if ((it & 63) == 0 && ll_give_up(hdr, status, &t0)) {
+        bad = 1;
+        break;
+      }
+    }
+  }
+  return __syncthreads_or(bad) == 0;
+}
+
+// ---------------------------------------------------------------------------
+// Small helpers
+// ---------------------------------------------------------------------------
+// Contiguous share of `total` items for CTA `c` of `g` in 32-bit arithmetic
+// (total * g < 2^32, checked on the host).
+__device__ __forceinline__ void split32(int total, int c, int g, int* begin, int* end) {
+  *begin = (int)(((uint32_t)total * (uint32_t)c) / (uint32_t)g);
+  *end = (int)(((uint32_t)total * (uint32_t)(c + 1)) / (uint32_t)g);
+}
+// Typed element load (the step kernel knows its weight type at compile time).
+template <typename T>
+__device__ __forceinline__ float ldw(const void* p, int64_t i) {
+  return Elem<T>::to_f(static_cast<const T*>(p)[i]);
+}
+__device__ __forceinline__ const uint4* rowp(const void* base, int64_t row, int64_t row_bytes) {
+  return reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(base) + row * row_bytes);
+}
+__device__ __forceinline__ float gelu_erf(float v) { return 0.5f * v * (1.0f + erff(v * 0.7071067811865476f)); }
+__device__ __forceinline__ float silu(float v) { return v / (1.0f + expf(-v)); }
+__device__ __forceinline__ bool better(float v, int i, float bv, int bi) {
+  return v > bv || (v == bv && i < bi);
+}
+
+// ---------------------------------------------------------------------------
+// Per-step state shared by the phases (shared memory of each CTA).
+// ---------------------------------------------------------------------------
+struct StepCtx {
+  int pos;        // position of the input token
+  int stop;       // nonzero: skip the step (EOS reached or bad input)
+  uint32_t step;  // this step's number (tags)
+  int64_t tok;    // input token
+  int64_t slot;   // cache offset (elements) of the new token's slot, head 0
+  int sel[2];     // selected experts of the current layer
+  float wts[2];   // their gate weights
+  float m, l;     // attention: running max and normaliser of this split
+  int last;       // this CTA finished the LM head last
+};
+__shared__ StepCtx cx_s;
+__shared__ float red_s[kSW];
+__shared__ int gat_s[kST];  // merge: exchange word index of each received value
+__shared__ float bestv_s[kSW];
+__shared__ int besti_s[kSW];
+// mbarriers of the bulk-copy staging, with per-barrier counts of armed and
+// completed phases (a wait uses parity = completed & 1).
+constexpr int kBarAtt = 0, kBarKv = 1, kBarSide = 2, kBarMoe = 3, kBarHead = 4;
+constexpr int kNumBars = kBarHead + kStepHeadStagesMax;
+__shared__ __align__(8) uint64_t bars_s[kNumBars];
+__shared__ uint32_t bar_armed_s[kNumBars], bar_done_s[kNumBars];
+extern __shared__ __align__(128) uint8_t sm[];
+
+__device__ __forceinline__ uint32_t tag_of(int l) { return (cx_s.step << 8) | (uint32_t)l; }
+template <typename T>
+__device__ __forceinline__ T* smem_at(uint32_t off) {
+  return reinterpret_cast<T*>(sm + off);
+}
+
+// ---------------------------------------------------------------------------
+// Bulk-copy staging
+// ---------------------------------------------------------------------------
+// Arm barrier b for `bytes` of bulk copies (one thread, before its copies).
+__device__ __forceinline__ void bar_arm(int b, uint32_t bytes) {
+  bar_armed_s[b] += 1;
+  mbar_arrive_expect_tx(&bars_s[b], bytes);
+}
+// Bulk copy global -> shared counted on barrier b (16-byte aligned, size a
+// multiple of 16), in pieces of at most 64 KB.
+__device__ __noinline__ void bulk_copy(void* dst, const void* src, uint32_t bytes, int b) {
+#pragma unroll 1
+  for (uint32_t o = 0; o < bytes; o += 65536u)
+    bulk_g2s(static_cast<uint8_t*>(dst) + o, static_cast<const uint8_t*>(src) + o, min(65536u, bytes - o),
+             &bars_s[b]);
+}
+// Every thread: wait for the oldest armed phase of barrier b (bounded).
+__device__ __noinline__ bool bar_wait(int b, uint64_t* hdr, int32_t* status) {
+  const bool ok = mbar_wait(&bars_s[b], bar_done_s[b] & 1u, status);
+  if (!ok) atomicExch(reinterpret_cast<unsigned long long*>(hdr + kHdrAbort), 1ull);
+  const int bad = __syncthreads_or(!ok);
+  if (threadIdx.x == 0) bar_done_s[b] += 1;
+  return !bad;
+}
+// Before leaving early: wait (bounded) for every armed copy not waited for,
+// so no bulk copy lands in shared memory after the CTA left.
+__device__ __noinline__ void drain_copies() {
+  if (threadIdx.x != 0) return;
+#pragma unroll 1
+  for (int b = 0; b < kNumBars; ++b)
+    while (bar_done_s[b] < bar_armed_s[b]) {
+      mbar_wait(&bars_s[b], bar_done_s[b] & 1u, nullptr);
+      bar_done_s[b] += 1;
+    }
+}
+
+// Work split of the attention CTAs (CTA (h, s) = split s of head h).
+struct AttSplit {
+  bool att;
+  int h, s, p0, nkp, v0, nvd, t0, t1;
+};
+__device__ __forceinline__ AttSplit att_split(const StepGeom& g, int hd, int pos) {
+  AttSplit a;
+  const int c = blockIdx.x, S = g.S;
+  a.att = c < g.natt;
+  a.h = a.att ? c / S : 0;
+  a.s = a.att ? c % S : 0;
+  int p1, v1;
+  split32(hd / 2, a.s, S, &a.p0, &p1);  // k RoPE pairs
+  split32(hd, a.s, S, &a.v0, &v1);      // v rows / output dims
+  split32(pos, a.s, S, &a.t0, &a.t1);   // old tokens
+  a.nkp = a.att ? p1 - a.p0 : 0;
+  a.nvd = a.att ? v1 - a.v0 : 0;
+  if (!a.att) a.t0 = a.t1 = 0;
+  return a;
+}
+
+// K/V of tokens [ta, ta + n) of head h -> shared memory (K then V), counted
+// on barrier b.  Warp 0 calls this; lane 0 arms, the lanes issue one copy per
+// (block, K or V) segment.
+template <typename KV>
+__device__ __noinline__ void kv_issue(const mie_step_desc& d, const StepGeom& g, const mie_layer_desc& ly, int h,
+                                      int ta, int n, int b) {
+  const int lane = threadIdx.x & 31, hd = d.head_dim, bs = d.block_size;
+  if (lane == 0) bar_arm(b, (uint32_t)(2 * n * hd * sizeof(KV)));
+  __syncwarp();
+  KV* dst = smem_at<KV>(g.sm_kv);
+  const int b0 = ta / bs, b1 = (ta + n - 1) / bs;
+#pragma unroll 1
+  for (int bi = b0 + lane; bi <= b1; bi += 32) {
+    const int tb = max(ta, bi * bs), te = min(ta + n, (bi + 1) * bs);
+    int64_t blk = bi;
+    if (d.block_table) {
+      const int pb = __ldg(d.block_table + bi);
+      if (pb < 0 || pb >= d.num_blocks) set_status(d.status, MIE_ERR_RANGE);
+      blk = (pb < 0 || pb >= d.num_blocks) ? 0 : pb;
+    }
+    const int64_t off = blk * d.kv_stride_block + (int64_t)h * d.kv_stride_head + (int64_t)(tb % bs) * d.kv_stride_tok;
+    const uint32_t bytes = (uint32_t)((te - tb) * hd * sizeof(KV));
+    bulk_copy(dst + (size_t)(tb - ta) * hd, static_cast<const KV*>(ly.k_cache) + off, bytes, b);
+    bulk_copy(dst + (size_t)g.chunk_tok * hd + (size_t)(tb - ta) * hd, static_cast<const KV*>(ly.v_cache) + off,
+              bytes, b);
+  }
+}
+
+// Norm weight (and bias) of D elements -> shared memory (one thread).
+__device__ __forceinline__ void norm_copy(void* dst, const void* w, const void* b, uint32_t rb, int bar) {
+  bulk_copy(dst, w, rb, bar);
+  if (b) bulk_copy(static_cast<uint8_t*>(dst) + rb, b, rb, bar);
+}
+
+// Stage layer l's attention inputs (warp 0): the attention norm weights; for
+// attention CTAs also q rows [0, q_stage) of the head, this CTA's k / v rows
+// (k pair first halves, second halves, v rows) and the first chunk of its old
+// tokens' K/V.
+template <typename W, typename KV>
+__device__ __noinline__ void att_issue(const StepParams& P, int l) {
+  const mie_step_desc& d = P.d;
+  const StepGeom& g = P.g;
+  const mie_layer_desc& ly = P.layers[l];
+  const int hd = d.head_dim, half = hd / 2, D = d.hidden_dim, lane = threadIdx.x & 31;
+  const AttSplit a = att_split(g, hd, cx_s.pos);
+  const uint32_t rb = (uint32_t)(D * sizeof(W));
+  if (lane == 0) {
+    fence_proxy_async_smem();  // earlier generic reads of these buffers before the async writes
+    const uint32_t nrows = a.att ? (uint32_t)(g.q_stage + 2 * a.nkp + a.nvd) : 0u;
+    bar_arm(kBarAtt, nrows * rb + (ly.attn_norm_b ? 2 : 1) * rb);
+    norm_copy(smem_at<uint8_t>(g.sm_anw), ly.attn_norm_w, ly.attn_norm_b, rb, kBarAtt);
+    if (a.att) {
+      const uint8_t* w = static_cast<const uint8_t*>(ly.qkv_w);
+      uint8_t* qs = smem_at<uint8_t>(g.sm_qw);
+      uint8_t* ks = smem_at<uint8_t>(g.sm_kvw);
+      bulk_copy(qs, w + (size_t)a.h * hd * rb, g.q_stage * rb, kBarAtt);
+      const size_t kbase = (size_t)(D + a.h * hd + a.p0) * rb, vbase = (size_t)(2 * D + a.h * hd + a.v0) * rb;
+      bulk_copy(ks, w + kbase, a.nkp * rb, kBarAtt);
+      bulk_copy(ks + (size_t)a.nkp * rb, w + kbase + (size_t)half * rb, a.nkp * rb, kBarAtt);
+      bulk_copy(ks + (size_t)2 * a.nkp * rb, w + vbase, a.nvd * rb, kBarAtt);
+    }
+  }
+  const int n0 = min(g.chunk_tok, a.t1 - a.t0);
+  if (n0 > 0) kv_issue<KV>(d, g, ly, a.h, a.t0, n0, kBarKv);
+}
+
+// Stage layer l's out_proj rows of this CTA, the router and the MoE norm
+// weights -- or, for l == num_layers, the final norm weights (one thread).
+template <typename W>
+__device__ __noinline__ void side_issue(const StepParams& P, int l) {
+  const mie_step_desc& d = P.d;
+  const StepGeom& g = P.g;
+  const int D = d.hidden_dim, E = d.num_experts;
+  const uint32_t rb = (uint32_t)(D * sizeof(W));
+  uint8_t* dst = smem_at<uint8_t>(g.sm_moe);
+  fence_proxy_async_smem();
+  if (l == d.num_layers) {
+    bar_arm(kBarSide, (d.final_norm_b ? 2 : 1) * rb);
+    norm_copy(dst, d.final_norm_w, d.final_norm_b, rb, kBarSide);
+    return;
+  }
+  const mie_layer_desc& ly = P.layers[l];
+  int r0, r1;
+  split32(D, blockIdx.x, gridDim.x, &r0, &r1);
+  bar_arm(kBarSide, (uint32_t)(r1 - r0 + E + (ly.moe_norm_b ? 2 : 1)) * rb);
+  bulk_copy(dst, static_cast<const uint8_t*>(ly.out_w) + (size_t)r0 * rb, (r1 - r0) * rb, kBarSide);
+  bulk_copy(dst + (size_t)g.nr_max * rb, ly.router_w, E * rb, kBarSide);
+  norm_copy(dst + (size_t)(g.nr_max + E) * rb, ly.moe_norm_w, ly.moe_norm_b, rb, kBarSide);
+}
+
+// Stages [first, first + count) of this CTA's LM-head rows (one thread) into
+// the ring in the attention staging area.
+template <typename W>
+__device__ __noinline__ void head_issue(const StepParams& P, int first, int count) {
+  const mie_step_desc& d = P.d;
+  const StepGeom& g = P.g;
+  int v0h, v1h;
+  split32(d.vocab, blockIdx.x, gridDim.x, &v0h, &v1h);
+  const uint32_t rb = (uint32_t)(d.hidden_dim * sizeof(W));
+  const int nst = (v1h - v0h + g.head_rows - 1) / g.head_rows;
+  fence_proxy_async_smem();
+#pragma unroll 1
+  for (int i = first; i < first + count && i < nst; ++i) {
+    const int slot = i % g.head_stages;
+    const int r0 = v0h + i * g.head_rows, nrw = min(g.head_rows, v1h - r0);
+    bar_arm(kBarHead + slot, nrw * rb);
+    bulk_copy(smem_at<uint8_t>(g.sm_qw) + (size_t)slot * g.head_rows * rb,
+              static_cast<const uint8_t*>(d.embedding) + (size_t)r0 * rb, nrw * rb, kBarHead + slot);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Compute routines (shared by all phases)
+// ---------------------------------------------------------------------------
+// out = norm(in) with weight w (and bias b, LayerNorm) staged in shared memory
+// as W; in, out in shared memory (may alias).  Ends with a barrier.
+template <typename W>
+__device__ __noinline__ void norm_smem(float* out, const float* in, int D, int norm, float eps, const W* w,
+                                       const W* b) {
+  __syncthreads();
+  float s1 = 0.f, s2 = 0.f;
+#pragma unroll 1
+  for (int i = threadIdx.x; i < D; i += kST) {
+    const float v = in[i];
+    s1 += v;
+    s2 = fmaf(v, v, s2);
+  }
+  if (norm == MIE_NORM_RMS) {
+    const float rs = rsqrtf(block_sum(s2, red_s) / (float)D + eps);
+#pragma unroll 1
+    for (int i = threadIdx.x; i < D; i += kST) out[i] = (in[i] * rs) * Elem<W>::to_f(w[i]);
+  } else if (norm == MIE_NORM_LAYER) {
+    const float mean = block_sum(s1, red_s) / (float)D;
+    float v = 0.f;
+#pragma unroll 1
+    for (int i = threadIdx.x; i < D; i += kST) {
+      const float t = in[i] - mean;
+      v = fmaf(t, t, v);
+    }
+    const float rs = rsqrtf(block_sum(v, red_s) / (float)D + eps);
+#pragma unroll 1
+    for (int i = threadIdx.x; i < D; i += kST) {
+      float y = (in[i] - mean) * rs * Elem<W>::to_f(w[i]);
+      if (b) y += Elem<W>::to_f(b[i]);
+      out[i] = y;
+    }
+  } else if (out != in) {
+#pragma unroll 1
+    for (int i = threadIdx.x; i < D; i += kST) out[i] = in[i];
+  }
+  __syncthreads();
+}
+
+// out[r] = rows[r] . x for r < n: rows of nvec 16-byte vectors (row stride
+// nvec) in shared memory -- or, when grows is set, in global memory -- and x
+// (shared memory, fp32).  Warp w forms rows w, w + kSW, ...  No barrier.
+template <typename W>
+__device__ __noinline__ void gemv(const uint4* rows, const uint4* grows, int n, int nvec, const float* x,
+                                  float* out) {
+  constexpr int PV = Elem<W>::kPerVec;
+  const int lane = threadIdx.x & 31;
+  if ((threadIdx.x >> 5) >= n) return;  // no rows for this warp
+  float xr[Seg<W>::kNV * PV];
+  load_x_regs<W>(xr, x, nvec);
+#pragma unroll 1
+  for (int r = threadIdx.x >> 5; r < n; r += kSW) {
+    RowRegs<W> w;
+#pragma unroll
+    for (int j = 0; j < Seg<W>::kNV; ++j) {
+      const int v = lane + kWarp * j;
+      w.w[j] = v < nvec ? (grows ? __ldg(grows + (size_t)r * nvec + v) : rows[(size_t)r * nvec + v])
+                        : make_uint4(0u, 0u, 0u, 0u);
+    }
+    const float s = warp_sum(row_dot_regs<W>(w, xr));
+    if (lane == 0) out[r] = s;
+  }
+}
+
+// Online softmax of q over K/V chunks of this split's old tokens [t0, t1)
+// (the first chunk was staged with the layer's attention inputs).  Leaves
+// the split's running max / normaliser in cx_s.m / cx_s.l and the PV group
+// partials in ab[0, kST).
+template <typename KV>
+__device__ __noinline__ bool att_core(const StepParams& P, int l, int h, int t0, int t1, const float* q, float* sc,
+                                      float* ab) {
+  const mie_step_desc& d = P.d;
+  const StepGeom& g = P.g;
+  const int tid = threadIdx.x, hd = d.head_dim, chunk = g.chunk_tok;
+  constexpr int VPT = 16 / (int)sizeof(KV);
+  const int VPH = hd / VPT, Gp = kST / hd, gi = tid / hd, dcol = tid - gi * hd;
+  const KV* ks = smem_at<const KV>(g.sm_kv);
+  const KV* vs = ks + (size_t)chunk * hd;
+  const float scale = d.attn_scale;
+  float m_run = -INFINITY, l_run = 0.f, acc = 0.f;
+  const int nchunks = (t1 - t0 + chunk - 1) / chunk;
+#pragma unroll 1
+  for (int ci = 0; ci < nchunks; ++ci) {
+    const int ta = t0 + ci * chunk, n = min(chunk, t1 - ta);
+    if (ci > 0) {
+      __syncthreads();  // previous chunk no longer read
+      if (tid < 32) {
+        if (tid == 0) fence_proxy_async_smem();
+        __syncwarp();
+        kv_issue<KV>(d, g, P.layers[l], h, ta, n, kBarKv);
+      }
+    }
+    if (!bar_wait(kBarKv, g.ll, d.status)) return false;
+    float mloc = -INFINITY;
+#pragma unroll 1
+    for (int t = tid; t < n; t += kST) {
+      const uint4* kr = reinterpret_cast<const uint4*>(ks + (size_t)t * hd);
+      float dot = 0.f;
+#pragma unroll 1
+      for (int jj = 0; jj < VPH; ++jj) {
+        const int j = (jj + t) & (VPH - 1);  // rotate the start piece: spreads banks (VPH a power of 2)
+        dot = dot_vec(kr[j], q + j * VPT, dot, (const KV*)nullptr);
+      }
+      const float v = dot * scale;
+      sc[t] = v;
+      mloc = fmaxf(mloc, v);
+    }
+    const float mn = fmaxf(m_run, block_max(mloc, red_s));
+    const float alpha = m_run == -INFINITY ? 0.f : expf(m_run - mn);
+    float ls = 0.f;
+#pragma unroll 1
+    for (int t = tid; t < n; t += kST) {
+      const float pr = expf(sc[t] - mn);
+      sc[t] = pr;
+      ls += pr;
+    }
+    l_run = l_run * alpha + block_sum(ls, red_s);  // every thread passed a barrier after the sc writes
+    m_run = mn;
+    if (gi < Gp) {
+      acc *= alpha;
+#pragma unroll 1
+      for (int t = gi; t < n; t += Gp) acc = fmaf(sc[t], Elem<KV>::to_f(vs[(size_t)t * hd + dcol]), acc);
+    }
+  }
+  __syncthreads();
+  ab[tid] = gi < Gp ? acc : 0.f;
+  if (tid == 0) {
+    cx_s.m = m_run;
+    cx_s.l = l_run;
+  }
+  return true;
+}
+
+// ---------------------------------------------------------------------------
+// ATT + MERGE of layer l (see the file comment).
+// ---------------------------------------------------------------------------
+template <typename W, typename KV>
+__device__ __noinline__ bool att_phase(const StepParams& P, int l) {
+  const mie_step_desc& d = P.d;
+  const StepGeom& g = P.g;
+  const mie_layer_desc& ly = P.layers[l];
+  constexpr int PV = Elem<W>::kPerVec;
+  const int tid = threadIdx.x;
+  const int D = d.hidden_dim, hd = d.head_dim, half = hd / 2, nvD = D / PV;
+  uint64_t* ll = g.ll;
+  const uint32_t tag = tag_of(l);
+  const int par = l & 1;
+  float* xs = smem_at<float>(g.sm_x);
+  float* xn = smem_at<float>(g.sm_xn);
+  const int pos = cx_s.pos;
+  const AttSplit a = att_split(g, hd, pos);
+  const int S = g.S, nkv = 2 * a.nkp + a.nvd;
+  STEP_STAMP(l, 0);
+
+  // ---- x: token embedding (layer 0) or exchange A; norm ----
+  if (l == 0) {
+    const int64_t tok = cx_s.tok;
+#pragma unroll 1
+    for (int i = tid; i < D; i += kST) {
+      float v = ldw<W>(d.embedding, tok * D + i);
+      if (d.pos_embedding) v += ldw<W>(d.pos_embedding, (int64_t)pos * D + i);
+      xs[i] = v;
+    }
+  } else if (!recv(ll + g.off_a[par], D, tag, xs, nullptr, ll, d.status)) {
+    return false;
+  }
+  STEP_STAMP(l, 1);
+  if (!bar_wait(kBarAtt, ll, d.status)) return false;
+  const W* nw = smem_at<const W>(g.sm_anw);
+  norm_smem<W>(xn, xs, D, d.norm, d.eps, nw, ly.attn_norm_b ? nw + D : nullptr);
+  STEP_STAMP(l, 2);
+  if (!a.att) {
+    // CTAs without attention work stage the next layer's attention norm
+    // weights (or their first LM-head rows) here
+    if (tid < 32) {
+      if (l + 1 < d.num_layers)
+        att_issue<W, KV>(P, l + 1);
+      else if (tid == 0)
+        head_issue<W>(P, 0, g.head_stages);
+    }
+    return true;
+  }
+
+  // ---- q rows of head h and this CTA's k / v rows: qk[0, hd) = q, qk[hd, hd + nkv) = k, v ----
+  float* qk = smem_at<float>(g.sm_qk);
+  gemv<W>(smem_at<const uint4>(g.sm_qw), nullptr, g.q_stage, nvD, xn, qk);
+  if (g.q_stage < hd)
+    gemv<W>(nullptr, rowp(ly.qkv_w, (int64_t)a.h * hd + g.q_stage, (int64_t)nvD * 16), hd - g.q_stage, nvD, xn,
+            qk + g.q_stage);
+  gemv<W>(smem_at<const uint4>(g.sm_kvw), nullptr, nkv, nvD, xn, qk + hd);
+  __syncthreads();
+  STEP_STAMP(l, 3);
+  // bias; RoPE of q (pairs j, j + hd/2) and of this CTA's k pairs; k / v
+  // rounded to the cache type and stored into the slot of the new token
+  float* kv = qk + hd;
+  if (ly.qkv_b) {
+    if (tid < hd) qk[tid] += ldw<W>(ly.qkv_b, (int64_t)a.h * hd + tid);
+    if (tid >= 128 && tid < 128 + nkv) {
+      const int k = tid - 128;
+      const int64_t row = k < a.nkp       ? (int64_t)D + a.h * hd + a.p0 + k
+                          : k < 2 * a.nkp ? (int64_t)D + a.h * hd + half + a.p0 + (k - a.nkp)
+                                          : 2 * (int64_t)D + a.h * hd + a.v0 + (k - 2 * a.nkp);
+      kv[k] += ldw<W>(ly.qkv_b, row);
+    }
+    __syncthreads();
+  }
+  const float* cs = d.rope_cos ? d.rope_cos + (int64_t)pos * half : nullptr;
+  const float* sn = d.rope_sin ? d.rope_sin + (int64_t)pos * half : nullptr;
+  if (cs && tid < half) {
+    const float x1 = qk[tid], x2 = qk[tid + half], cv = cs[tid], sv = sn[tid];
+    qk[tid] = x1 * cv - x2 * sv;
+    qk[tid + half] = x2 * cv + x1 * sv;
+  }
+  const int64_t slot = cx_s.slot + (int64_t)a.h * d.kv_stride_head;
+  if (tid >= 128 && tid < 128 + a.nkp) {
+    const int k = tid - 128, i = a.p0 + k;
+    float x1 = kv[k], x2 = kv[a.nkp + k];
+    if (cs) {
+      const float y1 = x1 * cs[i] - x2 * sn[i];
+      const float y2 = x2 * cs[i] + x1 * sn[i];
+      x1 = y1;
+      x2 = y2;
+    }
+    const KV k1 = Elem<KV>::from_f(x1), k2 = Elem<KV>::from_f(x2);
+    KV* kc = static_cast<KV*>(ly.k_cache);
+    kc[slot + i] = k1;
+    kc[slot + i + half] = k2;
+    kv[k] = Elem<KV>::to_f(k1);
+    kv[a.nkp + k] = Elem<KV>::to_f(k2);
+  } else if (tid >= 256 && tid < 256 + a.nvd) {
+    const int k = tid - 256;
+    const KV vv = Elem<KV>::from_f(kv[2 * a.nkp + k]);
+    static_cast<KV*>(ly.v_cache)[slot + a.v0 + k] = vv;
+    kv[2 * a.nkp + k] = Elem<KV>::to_f(vv);
+  }
+  __syncthreads();
+  STEP_STAMP(l, 4);
+
+  // ---- attention over the old tokens ----
+  float* ab = smem_at<float>(g.sm_acc);
+  if (!att_core<KV>(P, l, a.h, a.t0, a.t1, qk, smem_at<float>(g.sm_sc), ab)) return false;
+  __syncthreads();  // staged rows, K/V and ab complete
+  STEP_STAMP(l, 5);
+  // stage the next layer's attention inputs (or the first LM-head rows)
+  if (tid < 32) {
+    if (l + 1 < d.num_layers)
+      att_issue<W, KV>(P, l + 1);
+    else if (tid == 0)
+      head_issue<W>(P, 0, g.head_stages);
+  }
+  uint64_t* be = ll + g.off_b[par] + (int64_t)(a.h * S + a.s) * (3 + hd);
+  const int Gp = kST / hd;
+  if (tid < hd) {
+    float s = 0.f;
+#pragma unroll 1
+    for (int k = 0; k < Gp; ++k) s += ab[k * hd + tid];
+    ll_put(be + 3 + tid, s, tag);
+  } else if (tid == hd) {
+    // this CTA's share of q . k_new (k rounded to the cache type)
+    float sp = 0.f;
+#pragma unroll 1
+    for (int k = 0; k < a.nkp; ++k) {
+      sp = fmaf(qk[a.p0 + k], kv[k], sp);
+      sp = fmaf(qk[a.p0 + k + half], kv[a.nkp + k], sp);
+    }
+    ll_put(be + 0, cx_s.m, tag);
+    ll_put(be + 1, cx_s.l, tag);
+    ll_put(be + 2, sp, tag);
+  }
+  STEP_STAMP(l, 6);
+
+  // ---- MERGE: ab[0, 3S) = (m, l, sp) of every split, ab[3S, 3S + S nvd) = acc of my dims ----
+  if (a.nvd == 0) return true;
+  const int nm = 3 * S, nvd = a.nvd, nwords = nm + S * nvd;
+#pragma unroll 1
+  for (int i = tid; i < nwords; i += kST) {
+    int at;
+    if (i < nm) {
+      at = (i / 3) * (3 + hd) + (i % 3);
+    } else {
+      const int j = i - nm, sp = j / nvd;
+      at = sp * (3 + hd) + 3 + a.v0 + (j - sp * nvd);
+    }
+    gat_s[i] = at;
+  }
+  __syncthreads();  // gather indices ready, ab (PV groups) fully read
+  if (!recv(ll + g.off_b[par] + (int64_t)a.h * S * (3 + hd), nwords, tag, ab, gat_s, ll, d.status)) return false;
+  STEP_STAMP(l, 7);
+  if (tid < nvd) {
+    const float scale = d.attn_scale;
+    float spn = 0.f;
+#pragma unroll 1
+    for (int k = 0; k < S; ++k) spn += ab[3 * k + 2];
+    const float snew = spn * scale;
+    float M = snew;
+#pragma unroll 1
+    for (int k = 0; k < S; ++k) M = fmaxf(M, ab[3 * k]);
+    const float wn = expf(snew - M);
+    float den = wn, num = wn * kv[2 * a.nkp + tid];
+#pragma unroll 1
+    for (int k = 0; k < S; ++k) {
+      const float mk = ab[3 * k];
+      if (mk == -INFINITY) continue;
+      const float wk = expf(mk - M);
+      den = fmaf(ab[3 * k + 1], wk, den);
+      num = fmaf(ab[nm + k * nvd + tid], wk, num);
+    }
+    ll_put(ll + g.off_c[par] + (int64_t)a.h * hd + a.v0 + tid, num / den, tag);
+  }
+  return true;
+}
+
+// ---------------------------------------------------------------------------
+// PROJ: x_mid rows = x + out_proj(o) (+ bias) -> exchange D.
+// ---------------------------------------------------------------------------
+template <typename W>
+__device__ __noinline__ bool proj_phase(const StepParams& P, int l) {
+  const mie_step_desc& d = P.d;
+  const StepGeom& g = P.g;
+  const mie_layer_desc& ly = P.layers[l];
+  constexpr int PV = Elem<W>::kPerVec;
+  const int tid = threadIdx.x, D = d.hidden_dim, nvD = D / PV;
+  uint64_t* ll = g.ll;
+  const uint32_t tag = tag_of(l);
+  int r0, r1;
+  split32(D, blockIdx.x, gridDim.x, &r0, &r1);
+  const int nr = r1 - r0;
+  float* ob = smem_at<float>(g.sm_o);
+  float* ab = smem_at<float>(g.sm_acc);
+  if (!recv(ll + g.off_c[l & 1], D, tag, ob, nullptr, ll, d.status)) return false;
+  STEP_STAMP(l, 8);
+  if (!bar_wait(kBarSide, ll, d.status)) return false;
+  gemv<W>(smem_at<const uint4>(g.sm_moe), nullptr, nr, nvD, ob, ab);
+  __syncthreads();
+  if (tid < nr) {
+    const int r = r0 + tid;
+    float y = ab[tid];
+    if (ly.out_b) y += ldw<W>(ly.out_b, r);
+    ll_put(ll + g.off_d[l & 1] + r, smem_at<float>(g.sm_x)[r] + y, tag);
+  }
+  STEP_STAMP(l, 9);
+  return true;
+}
+
+// ---------------------------------------------------------------------------
+// UP + DOWN: x_mid -> norm -> router -> top-2 -> selected experts -> x of
+// layer l + 1 (exchange A).  bf16 weights: the selected experts' rows of this
+// CTA are bulk-copied into shared memory right after routing; fp32 weights:
+// read from global memory by the GEMV.
+// ---------------------------------------------------------------------------
+template <typename W>
+__device__ __noinline__ bool moe_phase(const StepParams& P, int l) {
+  const mie_step_desc& d = P.d;
+  const StepGeom& g = P.g;
+  const mie_layer_desc& ly = P.layers[l];
+  constexpr int PV = Elem<W>::kPerVec;
+  constexpr bool kStaged = sizeof(W) == 2;
+  const int tid = threadIdx.x;
+  const int D = d.hidden_dim, Hx = d.expert_hidden_dim, E = d.num_experts, nvD = D / PV, nvH = Hx / PV;
+  const int64_t rbD = (int64_t)D * sizeof(W), rbH = (int64_t)Hx * sizeof(W);
+  const bool swiglu = d.act == MIE_ACT_SWIGLU;
+  const int nmat = swiglu ? 2 : 1;
+  uint64_t* ll = g.ll;
+  const uint32_t tag = tag_of(l);
+  const int par = l & 1;
+  float* xm = smem_at<float>(g.sm_xm);
+  float* xn = smem_at<float>(g.sm_xn);
+  float* hb = smem_at<float>(g.sm_h);
+  float* ab = smem_at<float>(g.sm_acc);
+  uint8_t* ms = smem_at<uint8_t>(g.sm_moe);
+  int u0, u1, r0, r1;
+  split32(2 * Hx, blockIdx.x, gridDim.x, &u0, &u1);  // up units
+  split32(D, blockIdx.x, gridDim.x, &r0, &r1);       // output rows
+  const int nu = u1 - u0, nr = r1 - r0;
+
+  if (!recv(ll + g.off_d[par], D, tag, xm, nullptr, ll, d.status)) return false;
+  STEP_STAMP(l, 10);
+  const W* nw = reinterpret_cast<const W*>(ms + (size_t)(g.nr_max + E) * rbD);
+  norm_smem<W>(xn, xm, D, d.norm, d.eps, nw, ly.moe_norm_b ? nw + D : nullptr);
+  gemv<W>(reinterpret_cast<const uint4*>(ms + (size_t)g.nr_max * rbD), nullptr, E, nvD, xn, ab);
+  __syncthreads();
+  if (tid == 0) {
+    // repeated argmax, strict '>' over ascending ids: ties keep the lower id
+    int i0 = 0;
+#pragma unroll 1
+    for (int e = 1; e < E; ++e)
+      if (ab[e] > ab[i0]) i0 = e;
+    int i1 = i0 == 0 ? 1 : 0;
+#pragma unroll 1
+    for (int e = 0; e < E; ++e)
+      if (e != i0 && ab[e] > ab[i1]) i1 = e;
+    const float e1 = expf(ab[i1] - ab[i0]);
+    cx_s.sel[0] = i0;
+    cx_s.sel[1] = i1;
+    cx_s.wts[0] = 1.0f / (1.0f + e1);
+    cx_s.wts[1] = e1 / (1.0f + e1);
+    if constexpr (kStaged) {
+      // the selected experts' rows of this CTA -> shared memory (over the
+      // out_proj / router / norm rows, all read by now): gate rows of units
+      // [u0, u1), up rows (SwiGLU), down rows (slot 0 then slot 1)
+      fence_proxy_async_smem();
+      bar_arm(kBarMoe, (uint32_t)(nmat * nu * rbD + 2 * nr * rbH));
+#pragma unroll 1
+      for (int m = 0; m < nmat; ++m) {
+        const uint8_t* w = static_cast<const uint8_t*>(m ? ly.w3 : ly.w1);
+#pragma unroll 1
+        for (int k = 0; k < 2; ++k) {
+          const int ua = max(u0, k * Hx), ub = min(u1, (k + 1) * Hx);
+          if (ub > ua)
+            bulk_copy(ms + (size_t)(m * nu + ua - u0) * rbD, w + ((size_t)(k ? i1 : i0) * Hx + ua - k * Hx) * rbD,
+                      (uint32_t)((ub - ua) * rbD), kBarMoe);
+        }
+      }
+#pragma unroll 1
+      for (int k = 0; k < 2; ++k)
+        bulk_copy(ms + (size_t)nmat * nu * rbD + (size_t)k * nr * rbH,
+                  static_cast<const uint8_t*>(ly.w2) + ((size_t)(k ? i1 : i0) * D + r0) * rbH, (uint32_t)(nr * rbH),
+                  kBarMoe);
+    }
+  }
+  __syncthreads();
+  STEP_STAMP(l, 11);
+  const int sel0 = cx_s.sel[0], sel1 = cx_s.sel[1];
+  // up units: gate (and up) rows -> ab[0, nmat * nu)
+  if constexpr (kStaged) {
+    if (!bar_wait(kBarMoe, ll, d.status)) return false;
+    gemv<W>(reinterpret_cast<const uint4*>(ms), nullptr, nmat * nu, nvD, xn, ab);
+  } else {
+#pragma unroll 1
+    for (int m = 0; m < nmat; ++m) {
+      const void* w = m ? ly.w3 : ly.w1;
+#pragma unroll 1
+      for (int k = 0; k < 2; ++k) {
+        const int ua = max(u0, k * Hx), ub = min(u1, (k + 1) * Hx);
+        if (ub > ua)
+          gemv<W>(nullptr, rowp(w, (int64_t)(k ? sel1 : sel0) * Hx + ua - k * Hx, rbD), ub - ua, nvD, xn,
+                  ab + m * nu + (ua - u0));
+      }
+    }
+  }
+  __syncthreads();
+  if (tid < nu) {
+    const int u = u0 + tid, k = u / Hx;
+    const int64_t row = (int64_t)(k ? sel1 : sel0) * Hx + (u - k * Hx);
+    float gv = ab[tid];
+    if (ly.b1) gv += ldw<W>(ly.b1, row);
+    ll_put(ll + g.off_e[par] + u, swiglu ? silu(gv) * ab[nu + tid] : gelu_erf(gv), tag);
+  }
+  STEP_STAMP(l, 12);
+
+  // ---- DOWN ----
+  if (!recv(ll + g.off_e[par], 2 * Hx, tag, hb, nullptr, ll, d.status)) return false;
+  STEP_STAMP(l, 13);
+#pragma unroll 1
+  for (int k = 0; k < 2; ++k) {
+    if constexpr (kStaged)
+      gemv<W>(reinterpret_cast<const uint4*>(ms + (size_t)nmat * nu * rbD + (size_t)k * nr * rbH), nullptr, nr, nvH,
+              hb + (size_t)k * Hx, ab + k * nr);
+    else
+      gemv<W>(nullptr, rowp(ly.w2, (int64_t)(k ? sel1 : sel0) * D + r0, rbH), nr, nvH, hb + (size_t)k * Hx,
+              ab + k * nr);
+  }
+  __syncthreads();
+  // stage the next layer's out_proj / router / norm rows (or the final norm)
+  if (tid == 0) side_issue<W>(P, l + 1);
+  if (tid < nr) {
+    const int r = r0 + tid;
+    float y = xm[r];
+#pragma unroll 1
+    for (int k = 0; k < 2; ++k) {
+      float v = ab[k * nr + tid];
+      if (ly.b2) v += ldw<W>(ly.b2, (int64_t)(k ? sel1 : sel0) * D + r);
+      y = fmaf(cx_s.wts[k], v, y);
+    }
+    ll_put(ll + g.off_a[(l + 1) & 1] + r, y, tag_of(l + 1));
+    if (l == d.num_layers - 1) d.x[r] = y;
+  }
+  STEP_STAMP(l, 14);
+  return true;
+}
+
+// ---------------------------------------------------------------------------
+// HEAD: x_L -> final norm -> tied LM head -> argmax + device bookkeeping.
+// The CTA's vocab rows stream through a ring of head_stages stages of
+// head_rows rows in the attention staging area; the first stages were
+// requested during the last layer's attention.
+// ---------------------------------------------------------------------------
+template <typename W>
+__device__ __noinline__ bool head_phase(const StepParams& P) {
+  const mie_step_desc& d = P.d;
+  const StepGeom& g = P.g;
+  constexpr int PV = Elem<W>::kPerVec;
+  const int G = gridDim.x, c = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int D = d.hidden_dim, nvD = D / PV, V = d.vocab, Lnum = d.num_layers;
+  uint64_t* ll = g.ll;
+  float* xs = smem_at<float>(g.sm_x);
+  float* xn = smem_at<float>(g.sm_xn);
+  float* ab = smem_at<float>(g.sm_acc);
+  STEP_STAMP(Lnum, 0);
+  int v0h, v1h;
+  split32(V, c, G, &v0h, &v1h);
+  const int nst = (v1h - v0h + g.head_rows - 1) / g.head_rows;
+  if (!recv(ll + g.off_a[Lnum & 1], D, tag_of(Lnum), xs, nullptr, ll, d.status)) return false;
+  STEP_STAMP(Lnum, 1);
+  if (!bar_wait(kBarSide, ll, d.status)) return false;
+  const W* nw = smem_at<const W>(g.sm_moe);
+  norm_smem<W>(xn, xs, D, d.norm, d.eps, nw, d.final_norm_b ? nw + D : nullptr);
+  float best_v = -INFINITY;
+  int best_i = 0x7fffffff;
+#pragma unroll 1
+  for (int i = 0; i < nst; ++i) {
+    const int slot = i % g.head_stages;
+    if (!bar_wait(kBarHead + slot, ll, d.status)) return false;
+    const int r0 = v0h + i * g.head_rows, nrw = min(g.head_rows, v1h - r0);
+    gemv<W>(smem_at<const uint4>(g.sm_qw) + (size_t)slot * g.head_rows * nvD, nullptr, nrw, nvD, xn, ab);
+    __syncthreads();  // stage no longer read, ab complete
+    if (tid == 0 && i + g.head_stages < nst) head_issue<W>(P, i + g.head_stages, 1);
+    if (tid < nrw) {
+      float v = ab[tid];
+      const int row = r0 + tid;
+      if (d.lm_bias) v += ldw<W>(d.lm_bias, row);
+      if (d.logits) d.logits[row] = v;
+      if (better(v, row, best_v, best_i)) {
+        best_v = v;
+        best_i = row;
+      }
+    }
+  }
+  STEP_STAMP(Lnum, 2);
+  // CTA argmax: (value, lower index) is a total order, so the reduction
+  // order does not change the result
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best_v, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, best_i, o);
+    if (better(ov, oi, best_v, best_i)) {
+      best_v = ov;
+      best_i = oi;
+    }
+  }
+  if (lane == 0) {
+    bestv_s[warp] = best_v;
+    besti_s[warp] = best_i;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+#pragma unroll 1
+    for (int w = 0; w < kSW; ++w)
+      if (better(bestv_s[w], besti_s[w], bv, bi)) {
+        bv = bestv_s[w];
+        bi = besti_s[w];
+      }
+    d.lm_partial_val[c] = bv;
+    d.lm_partial_idx[c] = bi;
+    __threadfence();
+    cx_s.last = atom_add_acq_rel_gpu(d.lm_counter, 1u) == (uint32_t)(G - 1);
+  }
+  __syncthreads();
+  if (!cx_s.last || warp != 0) return true;
+  __threadfence();
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+#pragma unroll 1
+  for (int j = lane; j < G; j += 32) {
+    const float v = __ldcg(d.lm_partial_val + j);
+    const int i = __ldcg(d.lm_partial_idx + j);
+    if (better(v, i, bv, bi)) {
+      bv = v;
+      bi = i;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (better(ov, oi, bv, bi)) {
+      bv = ov;
+      bi = oi;
+    }
+  }
+  if (lane != 0) return true;
+  if (bi < 0 || bi >= V) {  // every logit NaN
+    set_status(d.status, MIE_ERR_RANGE);
+    bi = 0;
+  }
+  *d.token = bi;
+  *d.pos = cx_s.pos + 1;
+  if (d.tokens_log && d.log_count) {
+    const int k = __ldcg(d.log_count);
+    if (k < d.log_capacity) d.tokens_log[k] = bi;
+    *d.log_count = k + 1;
+  }
+  if (d.done && bi == d.eos_id) *d.done = 1;
+  *d.lm_counter = 0u;
+  __threadfence();
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(ll + kHdrStep), "l"((uint64_t)cx_s.step) : "memory");
+  return true;
+}
+
+template <typename W, typename KV>
+__global__ void __launch_bounds__(kST, 1) step_kernel(const __grid_constant__ StepParams P) {
+  const mie_step_desc& d = P.d;
+  // ---- step prologue: position, token, cache slot of the new token ----
+  if (threadIdx.x == 0) {
+    const int c = blockIdx.x;
+    int stop = d.done ? __ldcg(d.done) : 0;
+    cx_s.step = (uint32_t)ll_ld(P.g.ll + kHdrStep) + 1u;
+    const int p = __ldcg(d.pos);
+    const int64_t t = __ldcg(d.token);
+    if (!stop && (p < 0 || p >= d.max_pos || t < 0 || t >= d.vocab)) {
+      if (c == 0) set_status(d.status, MIE_ERR_RANGE);
+      stop = 1;
+    }
+    int64_t blk = stop ? 0 : p / d.block_size;
+    if (!stop && d.block_table) {
+      const int pb = __ldcg(d.block_table + blk);
+      if (pb < 0 || pb >= d.num_blocks) {
+        if (c == 0) set_status(d.status, MIE_ERR_RANGE);
+        stop = 1;
+      }
+      blk = pb;
+    }
+    cx_s.pos = p;
+    cx_s.tok = t;
+    cx_s.slot = stop ? 0 : blk * d.kv_stride_block + (int64_t)(p % d.block_size) * d.kv_stride_tok;
+    cx_s.stop = stop;
+#pragma unroll 1
+    for (int b = 0; b < kNumBars; ++b) {
+      mbar_init(&bars_s[b], 1);
+      bar_armed_s[b] = bar_done_s[b] = 0;
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (cx_s.stop) return;
+  if (threadIdx.x < 32) {
+    att_issue<W, KV>(P, 0);
+    if (threadIdx.x == 0) side_issue<W>(P, 0);
+  }
+  bool ok = true;
+#pragma unroll 1
+  for (int l = 0; l < d.num_layers && ok; ++l)
+    ok = att_phase<W, KV>(P, l) && proj_phase<W>(P, l) && moe_phase<W>(P, l);
+  if (ok) ok = head_phase<W>(P);
+  if (!ok) drain_copies();
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// Host side: validation, geometry, launch.
+// ---------------------------------------------------------------------------
+int step_geometry(const mie_step_desc& d, int grid, StepGeom* g) {
+  if (d.num_layers <= 0 || d.num_layers > kMaxStepLayers) return MIE_ERR_UNSUPPORTED;
+  if (d.dtype != MIE_F32 && d.dtype != MIE_BF16) return MIE_ERR_UNSUPPORTED;
+  if (d.kv_dtype != MIE_F32 && d.kv_dtype != MIE_BF16) return MIE_ERR_UNSUPPORTED;
+  const int esz = d.dtype == MIE_BF16 ? 2 : 4, kvsz = d.kv_dtype == MIE_BF16 ? 2 : 4;
+  const int D = d.hidden_dim, H = d.num_heads, hd = d.head_dim, Hx = d.expert_hidden_dim, E = d.num_experts;
+  if (D <= 0 || H <= 0 || hd <= 0 || Hx <= 0 || H * hd != D || hd % 2) return MIE_ERR_UNSUPPORTED;
+  // rows live in one register segment of a warp: at most 768 elements
+  if (D > 768 || Hx > 768 || (D * esz) % 16 || (Hx * esz) % 16) return MIE_ERR_UNSUPPORTED;
+  // head_dim: 16-byte K/V pieces, a power-of-two count of them per row, and
+  // whole PV groups of the CTA's threads
+  const int vph = hd * kvsz / 16;
+  if (hd > 128 || (hd * kvsz) % 16 || (vph & (vph - 1)) || kStepThreads % hd) return MIE_ERR_UNSUPPORTED;
+  if (d.top_k != 2 || E < 2 || E > 32) return MIE_ERR_UNSUPPORTED;
+  if (d.act != MIE_ACT_GELU && d.act != MIE_ACT_SWIGLU) return MIE_ERR_UNSUPPORTED;
+  if (d.moe_partial || (d.expert_count && d.expert_count != E) || d.expert_base)
+    return MIE_ERR_UNSUPPORTED;  // expert parallel runs layer by layer
+  if (d.kv_stride_tok != hd || (d.kv_stride_block * kvsz) % 16 || (d.kv_stride_head * kvsz) % 16)
+    return MIE_ERR_UNSUPPORTED;
+  if (grid < H || grid < 2) return MIE_ERR_UNSUPPORTED;
+  // work splits use 32-bit products (total * grid < 2^32)
+  if ((int64_t)d.vocab * grid >= (1ll << 32) || (int64_t)d.max_pos * grid >= (1ll << 32)) return MIE_ERR_UNSUPPORTED;
+  if (d.lm_grid < grid) return MIE_ERR_INVALID;  // per-CTA argmax results
+  StepGeom& G = *g;
+  G = StepGeom{};
+  G.G = grid;
+  G.S = grid / H;
+  G.natt = G.S * H;
+  // exchange buffers (64-bit words), two copies each
+  int64_t off = 8;  // header
+  auto take = [&](int64_t words) {
+    const int64_t at = off;
+    off += (words + 1) & ~int64_t(1);
+    return at;
+  };
+  for (int p = 0; p < 2; ++p) {
+    G.off_a[p] = take(D);
+    G.off_b[p] = take((int64_t)H * G.S * (3 + hd));
+    G.off_c[p] = take(D);
+    G.off_d[p] = take(D);
+    G.off_e[p] = take(2 * (int64_t)Hx);
+  }
+  G.words = off;
+  // work per CTA (upper bounds)
+  const int kvw_max = 2 * ((hd / 2 + G.S - 1) / G.S) + (hd + G.S - 1) / G.S;  // k + v rows of one split
+  const int merge_words = 3 * G.S + G.S * ((hd + G.S - 1) / G.S);
+  G.nr_max = (D + grid - 1) / grid;
+  const int nu_max = (2 * Hx + grid - 1) / grid;
+  const int nmat = d.act == MIE_ACT_SWIGLU ? 2 : 1;
+  // per-thread epilogues and the merge gather index table hold one item per thread
+  if (merge_words > kStepThreads || 2 * G.nr_max > kStepThreads || nmat * nu_max > kStepThreads ||
+      kvw_max > 128 || hd > 128)
+    return MIE_ERR_UNSUPPORTED;
+  // shared memory: vectors, then the staging areas
+  const uint32_t rbD = (uint32_t)(D * esz), rbH = (uint32_t)(Hx * esz);
+  uint32_t so = 0;
+  auto stake = [&](uint32_t bytes) {
+    so = (so + 127) & ~127u;
+    const uint32_t at = so;
+    so += bytes;
+    return at;
+  };
+  G.sm_x = stake(4 * D);
+  G.sm_xn = stake(4 * D);
+  G.sm_xm = stake(4 * D);
+  G.sm_h = stake(8 * Hx);
+  G.sm_o = stake(4 * D);
+  G.sm_qk = stake(4 * (hd + kvw_max));
+  int abw = kStepThreads;
+  if (E > abw) abw = E;
+  G.sm_acc = stake(4 * abw);
+  G.chunk_tok = (int)(kStepKvChunkBytes / (2 * hd * kvsz));
+  G.sm_sc = stake(4 * G.chunk_tok);
+  G.sm_anw = stake(2 * rbD);
+  const uint32_t base = (so + 127) & ~127u;
+  const uint32_t chunk_bytes = (uint32_t)(2 * G.chunk_tok * hd * kvsz);
+  const uint32_t att_min = (uint32_t)kvw_max * rbD + chunk_bytes + 3 * 128;
+  const uint32_t side_bytes = (uint32_t)(G.nr_max + E + 2) * rbD;
+  const uint32_t moe_bytes = (uint32_t)(nmat * nu_max) * rbD + 2u * G.nr_max * rbH;
+  const uint32_t region2 = (esz == 2 && moe_bytes > side_bytes) ? moe_bytes : side_bytes;
+  if (base + att_min + region2 > kStepMaxSmem) return MIE_ERR_UNSUPPORTED;
+  const uint32_t avail = kStepMaxSmem - base - region2 - att_min;
+  // bf16 weights: all q rows of the head staged (and the selected experts'
+  // rows, see moe_phase); fp32 weights: as many q rows as fit.
+  const uint32_t q = avail / rbD;
+  G.q_stage = q < (uint32_t)hd ? (int)q : hd;
+  if (esz == 2 && G.q_stage < hd) return MIE_ERR_UNSUPPORTED;
+  G.moe_staged = esz == 2 ? 1 : 0;
+  G.sm_qw = stake((uint32_t)G.q_stage * rbD);
+  G.sm_kvw = stake((uint32_t)kvw_max * rbD);
+  G.sm_kv = stake(chunk_bytes);
+  const uint32_t att_bytes = G.sm_kv + chunk_bytes - G.sm_qw;
+  G.sm_moe = stake(region2);
+  G.smem = (so + 127) & ~127u;
+  if (G.smem > kStepMaxSmem) return MIE_ERR_UNSUPPORTED;
+  G.head_rows = kStepThreads / 32;
+  const uint32_t stage_bytes = (uint32_t)G.head_rows * rbD;
+  G.head_stages = (int)(att_bytes / stage_bytes);
+  if (G.head_stages > kStepHeadStagesMax) G.head_stages = kStepHeadStagesMax;
+  if (G.head_stages < 2) return MIE_ERR_UNSUPPORTED;
+  return MIE_OK;
+}
+
+int step_launch(const mie_step_desc& d, const StepGeom& g, uint64_t* scratch, cudaStream_t st) {
+  StepParams p;
+  p.d = d;
+  p.g = g;
+  p.g.ll = scratch;
+  for (int l = 0; l < d.num_layers; ++l) p.layers[l] = d.layers[l];
+  p.d.layers = nullptr;
+  void (*k)(const StepParams);
+#ifdef MIE_STEP_STAMPS
+  if (d.num_layers + 1 > kStampLayers || g.G > 160) return MIE_ERR_UNSUPPORTED;
+#endif
+  if (d.dtype == MIE_BF16)
+    k = d.kv_dtype == MIE_BF16 ? step_kernel<__nv_bfloat16, __nv_bfloat16> : step_kernel<__nv_bfloat16, float>;
+  else
+    k = d.kv_dtype == MIE_BF16 ? step_kernel<float, __nv_bfloat16> : step_kernel<float, float>;
+  return launch(k, dim3(g.G), dim3(kStepThreads), g.smem, st, false, p);
+}
+
+#ifdef MIE_STEP_STAMPS
+// Copy the phase timestamps of the last step to the host (analysis builds).
+extern "C" int mie_debug_step_stamps(unsigned long long* host, int64_t count) {
+  return cudaMemcpyFromSymbol(host, g_step_stamps, sizeof(unsigned long long) * (size_t)count) == cudaSuccess
+             ? MIE_OK
+             : MIE_ERR_CUDA;
+}
+#endif
+
+void step_set_attributes() {
+  set_max_smem(step_kernel<__nv_bfloat16, __nv_bfloat16>);
+  set_max_smem(step_kernel<__nv_bfloat16, float>);
+  set_max_smem(step_kernel<float, __nv_bfloat16>);
+  set_max_smem(step_kernel<float, float>);
+}
+
+}  // namespace mie

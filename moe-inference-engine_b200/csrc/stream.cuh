@@ -69,7 +69,12 @@ __device__ __forceinline__ float row_dot_regs(const RowRegs<W>& r, const float* 
   return acc;
 }
 
-// xr[j*PV + e] = xs[(lane + 32 j) * PV + e] for segment 0 (zero past nvec).
+// xr[j*PV + e] = xs[(lane + 32 j) * PV + e] for segment 0 (zero past nvec);
+// xs 16-byte aligned in shared memory.  16-byte loads.  For bf16 rows a lane
+// needs 32 bytes of x (two 16-byte halves); lanes 4-7 of every quarter-warp
+// read their halves in the opposite order to lanes 0-3, so each 16-byte load
+// instruction of a quarter-warp touches eight distinct bank groups (no bank
+// conflicts; in natural order lanes i and i + 4 would collide).
 template <typename W>
 __device__ __forceinline__ void load_x_regs(float* xr, const float* xs, int nvec) {
   constexpr int PV = Elem<W>::kPerVec;
@@ -77,8 +82,29 @@ __device__ __forceinline__ void load_x_regs(float* xr, const float* xs, int nvec
 #pragma unroll
   for (int j = 0; j < Seg<W>::kNV; ++j) {
     const int v = lane + kWarp * j;
-#pragma unroll
-    for (int e = 0; e < PV; ++e) xr[j * PV + e] = v < nvec ? xs[v * PV + e] : 0.f;
+    if constexpr (PV == 4) {
+      const float4 a = v < nvec ? *reinterpret_cast<const float4*>(xs + v * 4) : make_float4(0.f, 0.f, 0.f, 0.f);
+      xr[j * 4 + 0] = a.x;
+      xr[j * 4 + 1] = a.y;
+      xr[j * 4 + 2] = a.z;
+      xr[j * 4 + 3] = a.w;
+    } else {
+      const int h0 = (lane >> 2) & 1;
+      float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
+      if (v < nvec) {
+        a = *reinterpret_cast<const float4*>(xs + v * 8 + 4 * h0);
+        b = *reinterpret_cast<const float4*>(xs + v * 8 + 4 * (1 - h0));
+      }
+      const float4 lo = h0 ? b : a, hi = h0 ? a : b;
+      xr[j * 8 + 0] = lo.x;
+      xr[j * 8 + 1] = lo.y;
+      xr[j * 8 + 2] = lo.z;
+      xr[j * 8 + 3] = lo.w;
+      xr[j * 8 + 4] = hi.x;
+      xr[j * 8 + 5] = hi.y;
+      xr[j * 8 + 6] = hi.z;
+      xr[j * 8 + 7] = hi.w;
+    }
   }
 }
 

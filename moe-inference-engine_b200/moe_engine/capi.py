@@ -102,7 +102,7 @@ class StepDesc(ctypes.Structure):
         ("expert_base", _i), ("expert_count", _i), ("attn_partials", _p), ("attn_counters", _p),
         ("moe_sync", _p), ("lm_partial_val", _p), ("lm_partial_idx", _p), ("lm_counter", _p),
         ("logits", _p), ("status", _p), ("attn_splits", _i), ("max_splits", _i), ("lm_grid", _i),
-        ("use_pdl", _i),
+        ("use_pdl", _i), ("step_scratch", _p), ("step_scratch_bytes", _i64),
     ]
 
 
@@ -123,6 +123,7 @@ SYMBOLS = {
     "mie_decode_step": ([ctypes.POINTER(StepDesc), _p], ctypes.c_int),
     "mie_decode_layer": ([ctypes.POINTER(StepDesc), _i, _p], ctypes.c_int),
     "mie_decode_head": ([ctypes.POINTER(StepDesc), _p], ctypes.c_int),
+    "mie_step_scratch_bytes": ([ctypes.POINTER(StepDesc)], ctypes.c_int64),
 }
 
 _lib = None

@@ -22,6 +22,7 @@ from __future__ import annotations
 
 import ctypes
 import math
+import os
 
 import torch
 
@@ -100,6 +101,10 @@ class DecodeRunner:
         self._host_state = torch.zeros(2, dtype=torch.int32, pin_memory=True)
         self._graphs: dict = {}
         self.use_pdl = True
+        # Persistent step (one launch per token) whenever the shapes allow it;
+        # MIE_PERSISTENT=0 selects the per-op launch sequence.
+        self.persistent = os.environ.get("MIE_PERSISTENT", "1") != "0"
+        self.step_scratch = None  # int64 words, zeroed once
 
     # ---- descriptors --------------------------------------------------------
     def param_signature(self):
@@ -201,7 +206,23 @@ class DecodeRunner:
         d.max_splits = MAX_SPLITS
         d.lm_grid = self.lm_grid
         d.use_pdl = 1 if self.use_pdl else 0
+        d.step_scratch = None
+        d.step_scratch_bytes = 0
+        if self.persistent:
+            with torch.cuda.device(self.device):
+                need = int(self.lib.mie_step_scratch_bytes(ctypes.byref(d)))
+            if need > 0:
+                if self.step_scratch is None or self.step_scratch.numel() * 8 < need:
+                    self.step_scratch = torch.zeros(-(-need // 8), dtype=torch.int64, device=self.device)
+                d.step_scratch = self.step_scratch.data_ptr()
+                d.step_scratch_bytes = self.step_scratch.numel() * 8
         return d, layers
+
+    def uses_persistent(self, cache) -> bool:
+        """True when decode steps for ``cache`` run as one persistent launch."""
+        _, _, _, _, bs, _, _ = cache_geometry(cache, 0)
+        desc, _ = self.make_desc(cache, logits=False, graph=True, splits=self.splits_for(bs, bs))
+        return bool(desc.step_scratch)
 
     # ---- execution ------------------------------------------------------------
     def launch_step(self, desc) -> None:
@@ -212,6 +233,10 @@ class DecodeRunner:
         code = int(self.status.item())
         if code:
             self.status.zero_()
+            # a step that gave up leaves exchange words and counters mid-step
+            if self.step_scratch is not None:
+                self.step_scratch.zero_()
+            self.lm_counter.zero_()
             raise capi.KernelError(code, "decode step (device status)")
 
     @torch.no_grad()
@@ -236,7 +261,7 @@ class DecodeRunner:
         k0 = cache_geometry(cache, 0)[0]
         table = getattr(cache, "block_table_device", None)
         key = (k0.data_ptr(), None if table is None else table.data_ptr(), splits, self.use_pdl,
-               self.param_signature())
+               self.persistent, self.param_signature())
         hit = self._graphs.get(key)
         if hit is not None:
             return hit[0]

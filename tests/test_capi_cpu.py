@@ -28,7 +28,7 @@ STRUCTS = {
 
 def declared_functions():
     text = open(HEADER).read()
-    return sorted(set(re.findall(r"^\s*(?:int|const char\*)\s+(mie_\w+)\s*\(", text, re.M)))
+    return sorted(set(re.findall(r"^\s*(?:int|int64_t|const char\*)\s+(mie_\w+)\s*\(", text, re.M)))
 
 
 def c_field_names(struct_name):

@@ -184,3 +184,37 @@ def test_module_level_direct_paths_match_reference_mode():
                 steps.append(m(x[:, t : t + 1], cache)[:, -1])
         out[mode] = torch.stack(steps, 1)
     torch.testing.assert_close(out["direct"], out["reference"], atol=1e-4, rtol=1e-4)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_persistent_step_is_used_and_agrees_with_launch_sequence(baseline_params, dtype):
+    """The single-launch step and the per-op launch sequence compute the same
+    step: hidden states agree to rounding, greedy tokens are identical."""
+    m = baseline_model(baseline_params, dtype)
+    runner = m.decode_runner()
+    assert runner.uses_persistent(m.new_cache())
+    prompt = torch.randint(0, 50304, (24,), generator=torch.Generator().manual_seed(9))
+    xs = {}
+    for persistent in (True, False):
+        runner.persistent = persistent
+        cache = m.new_block_allocator(num_blocks=64, block_size=16, attention_mode="direct").new_cache()
+        hs = []
+        with torch.no_grad():
+            m(prompt[None].to(DEV), cache)
+            tok = torch.tensor([[17]], device=DEV)
+            for _ in range(6):
+                logits = m(tok, cache)
+                hs.append(runner.x.clone())
+                tok = logits[0, -1].float().argmax().view(1, 1)
+        xs[persistent] = torch.stack(hs)
+        runner.check_status()
+    runner.persistent = True
+    rel = (xs[True] - xs[False]).norm() / xs[False].norm()
+    assert rel < (5e-3 if dtype == torch.bfloat16 else 1e-5), float(rel)
+    gen = {}
+    for persistent in (True, False):
+        runner.persistent = persistent
+        gen[persistent] = m.generate(prompt, max_new_tokens=40, temperature=0)
+    runner.persistent = True
+    assert torch.equal(gen[True], gen[False])
+    runner.check_status()
