@@ -199,10 +199,13 @@ struct StepCtx {
   float wts[2];   // their gate weights
   float m, l;     // attention: running max and normaliser of this split
   int last;       // this CTA finished the LM head last
+  int blk0;       // first cache block of this CTA's old tokens (blk_s[0])
 };
+constexpr int kStepBlkCache = 64;  // block ids of a split cached per step
 __shared__ StepCtx cx_s;
 __shared__ float red_s[kSW];
 __shared__ int gat_s[kST];  // merge: exchange word index of each received value
+__shared__ int blk_s[kStepBlkCache];  // physical block ids of this CTA's old tokens
 __shared__ float bestv_s[kSW];
 __shared__ int besti_s[kSW];
 // mbarriers of the bulk-copy staging, with per-barrier counts of armed and
@@ -277,8 +280,9 @@ __device__ __forceinline__ AttSplit att_split(const StepGeom& g, int hd, int pos
 }
 
 // K/V of tokens [ta, ta + n) of head h -> shared memory (K then V), counted
-// on barrier b.  Warp 0 calls this; lane 0 arms, the lanes issue one copy per
-// (block, K or V) segment.
+// on barrier b.  One warp calls this; its lane 0 arms, the lanes issue one
+// copy per (block, K or V) segment.  Block ids of this CTA's first
+// kStepBlkCache blocks come from the per-step copy in shared memory.
 template <typename KV>
 __device__ __noinline__ void kv_issue(const mie_step_desc& d, const StepGeom& g, const mie_layer_desc& ly, int h,
                                       int ta, int n, int b) {
@@ -292,7 +296,8 @@ __device__ __noinline__ void kv_issue(const mie_step_desc& d, const StepGeom& g,
     const int tb = max(ta, bi * bs), te = min(ta + n, (bi + 1) * bs);
     int64_t blk = bi;
     if (d.block_table) {
-      const int pb = __ldg(d.block_table + bi);
+      const int k = bi - cx_s.blk0;
+      const int pb = (k >= 0 && k < kStepBlkCache) ? blk_s[k] : __ldg(d.block_table + bi);
       if (pb < 0 || pb >= d.num_blocks) set_status(d.status, MIE_ERR_RANGE);
       blk = (pb < 0 || pb >= d.num_blocks) ? 0 : pb;
     }
@@ -440,17 +445,37 @@ __device__ __noinline__ void gemv(const uint4* rows, const uint4* grows, int n, 
   if ((threadIdx.x >> 5) >= n) return;  // no rows for this warp
   float xr[Seg<W>::kNV * PV];
   load_x_regs<W>(xr, x, nvec);
+  // Two rows per iteration and one partial sum per 16-byte vector: the FMA
+  // chains and the two shuffle reductions are independent of each other.
 #pragma unroll 1
-  for (int r = threadIdx.x >> 5; r < n; r += kSW) {
-    RowRegs<W> w;
+  for (int r = threadIdx.x >> 5; r < n; r += 2 * kSW) {
+    const int r2 = r + kSW;
+    const bool two = r2 < n;
+    uint4 wa[Seg<W>::kNV], wb[Seg<W>::kNV];
 #pragma unroll
     for (int j = 0; j < Seg<W>::kNV; ++j) {
       const int v = lane + kWarp * j;
-      w.w[j] = v < nvec ? (grows ? __ldg(grows + (size_t)r * nvec + v) : rows[(size_t)r * nvec + v])
-                        : make_uint4(0u, 0u, 0u, 0u);
+      const bool ok = v < nvec;
+      wa[j] = ok ? (grows ? __ldg(grows + (size_t)r * nvec + v) : rows[(size_t)r * nvec + v])
+                 : make_uint4(0u, 0u, 0u, 0u);
+      wb[j] = (ok && two) ? (grows ? __ldg(grows + (size_t)r2 * nvec + v) : rows[(size_t)r2 * nvec + v])
+                          : make_uint4(0u, 0u, 0u, 0u);
     }
-    const float s = warp_sum(row_dot_regs<W>(w, xr));
-    if (lane == 0) out[r] = s;
+    float sa = 0.f, sb = 0.f;
+#pragma unroll
+    for (int j = 0; j < Seg<W>::kNV; ++j) {
+      sa += dot_vec(wa[j], xr + j * PV, 0.f, (const W*)nullptr);
+      sb += dot_vec(wb[j], xr + j * PV, 0.f, (const W*)nullptr);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      sa += __shfl_xor_sync(0xffffffffu, sa, o);
+      sb += __shfl_xor_sync(0xffffffffu, sb, o);
+    }
+    if (lane == 0) {
+      out[r] = sa;
+      if (two) out[r2] = sb;
+    }
   }
 }
 
@@ -633,13 +658,6 @@ __device__ __noinline__ bool att_phase(const StepParams& P, int l) {
   if (!att_core<KV>(P, l, a.h, a.t0, a.t1, qk, smem_at<float>(g.sm_sc), ab)) return false;
   __syncthreads();  // staged rows, K/V and ab complete
   STEP_STAMP(l, 5);
-  // stage the next layer's attention inputs (or the first LM-head rows)
-  if (tid < 32) {
-    if (l + 1 < d.num_layers)
-      att_issue<W, KV>(P, l + 1);
-    else if (tid == 0)
-      head_issue<W>(P, 0, g.head_stages);
-  }
   uint64_t* be = ll + g.off_b[par] + (int64_t)(a.h * S + a.s) * (3 + hd);
   const int Gp = kST / hd;
   if (tid < hd) {
@@ -658,6 +676,14 @@ __device__ __noinline__ bool att_phase(const StepParams& P, int l) {
     ll_put(be + 0, cx_s.m, tag);
     ll_put(be + 1, cx_s.l, tag);
     ll_put(be + 2, sp, tag);
+  }
+  // then stage the next layer's attention inputs (or the first LM-head rows)
+  // from the last warp, which holds no merge words
+  if (tid >= kST - 32) {
+    if (l + 1 < d.num_layers)
+      att_issue<W, KV>(P, l + 1);
+    else if (tid == kST - 32)
+      head_issue<W>(P, 0, g.head_stages);
   }
   STEP_STAMP(l, 6);
 
@@ -853,8 +879,6 @@ __device__ __noinline__ bool moe_phase(const StepParams& P, int l) {
               ab + k * nr);
   }
   __syncthreads();
-  // stage the next layer's out_proj / router / norm rows (or the final norm)
-  if (tid == 0) side_issue<W>(P, l + 1);
   if (tid < nr) {
     const int r = r0 + tid;
     float y = xm[r];
@@ -867,6 +891,9 @@ __device__ __noinline__ bool moe_phase(const StepParams& P, int l) {
     ll_put(ll + g.off_a[(l + 1) & 1] + r, y, tag_of(l + 1));
     if (l == d.num_layers - 1) d.x[r] = y;
   }
+  // then stage the next layer's out_proj / router / norm rows (or the final
+  // norm) from a thread without an output row
+  if (tid == kST - 1) side_issue<W>(P, l + 1);
   STEP_STAMP(l, 14);
   return true;
 }
@@ -1027,6 +1054,16 @@ __global__ void __launch_bounds__(kST, 1) step_kernel(const __grid_constant__ St
   }
   __syncthreads();
   if (cx_s.stop) return;
+  {
+    // physical block ids of this CTA's old tokens, the same for every layer
+    const AttSplit a = att_split(P.g, d.head_dim, cx_s.pos);
+    const int b0 = a.t0 / d.block_size;
+    if (threadIdx.x == 0) cx_s.blk0 = b0;
+    if (d.block_table && threadIdx.x < kStepBlkCache && a.t1 > a.t0 &&
+        b0 + (int)threadIdx.x <= (a.t1 - 1) / d.block_size)
+      blk_s[threadIdx.x] = __ldcg(d.block_table + b0 + threadIdx.x);
+    __syncthreads();
+  }
   if (threadIdx.x < 32) {
     att_issue<W, KV>(P, 0);
     if (threadIdx.x == 0) side_issue<W>(P, 0);
@@ -1139,7 +1176,9 @@ int step_geometry(const mie_step_desc& d, int grid, StepGeom* g) {
   G.sm_moe = stake(region2);
   G.smem = (so + 127) & ~127u;
   if (G.smem > kStepMaxSmem) return MIE_ERR_UNSUPPORTED;
-  G.head_rows = kStepThreads / 32;
+  // two rows per warp per stage when three such stages fit, else one
+  G.head_rows = 2 * (kStepThreads / 32);
+  if (att_bytes / ((uint32_t)G.head_rows * rbD) < 3) G.head_rows = kStepThreads / 32;
   const uint32_t stage_bytes = (uint32_t)G.head_rows * rbD;
   G.head_stages = (int)(att_bytes / stage_bytes);
   if (G.head_stages > kStepHeadStagesMax) G.head_stages = kStepHeadStagesMax;
