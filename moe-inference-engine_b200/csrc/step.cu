@@ -81,7 +81,14 @@ __device__ unsigned long long g_step_stamps[160 * kStampLayers * kStampPoints];
   do { \
     if (threadIdx.x == 0) g_step_stamps[(blockIdx.x * kStampLayers + (l)) * kStampPoints + (k)] = global_ns(); \
   } while (0)
+#define STEP_STAMP_T(l, k, t) \
+  do { \
+    if (threadIdx.x == (t)) g_step_stamps[(blockIdx.x * kStampLayers + (l)) * kStampPoints + (k)] = global_ns(); \
+  } while (0)
 #else
+#define STEP_STAMP_T(l, k, t) \
+  do { \
+  } while (0)
 #define STEP_STAMP(l, k) \
   do { \
   } while (0)
@@ -315,36 +322,42 @@ __device__ __forceinline__ void norm_copy(void* dst, const void* w, const void* 
   if (b) bulk_copy(static_cast<uint8_t*>(dst) + rb, b, rb, bar);
 }
 
-// Stage layer l's attention inputs (warp 0): the attention norm weights; for
-// attention CTAs also q rows [0, q_stage) of the head, this CTA's k / v rows
-// (k pair first halves, second halves, v rows) and the first chunk of its old
-// tokens' K/V.
-template <typename W, typename KV>
-__device__ __noinline__ void att_issue(const StepParams& P, int l) {
+// Stage layer l's attention weights (lane 0 of the calling warp): the
+// attention norm weights; for attention CTAs also q rows [0, q_stage) of the
+// head and this CTA's k / v rows (k pair first halves, second halves, v rows).
+template <typename W>
+__device__ __noinline__ void att_issue_rows(const StepParams& P, int l) {
   const mie_step_desc& d = P.d;
   const StepGeom& g = P.g;
   const mie_layer_desc& ly = P.layers[l];
-  const int hd = d.head_dim, half = hd / 2, D = d.hidden_dim, lane = threadIdx.x & 31;
+  const int hd = d.head_dim, half = hd / 2, D = d.hidden_dim;
   const AttSplit a = att_split(g, hd, cx_s.pos);
   const uint32_t rb = (uint32_t)(D * sizeof(W));
-  if (lane == 0) {
-    fence_proxy_async_smem();  // earlier generic reads of these buffers before the async writes
-    const uint32_t nrows = a.att ? (uint32_t)(g.q_stage + 2 * a.nkp + a.nvd) : 0u;
-    bar_arm(kBarAtt, nrows * rb + (ly.attn_norm_b ? 2 : 1) * rb);
-    norm_copy(smem_at<uint8_t>(g.sm_anw), ly.attn_norm_w, ly.attn_norm_b, rb, kBarAtt);
-    if (a.att) {
-      const uint8_t* w = static_cast<const uint8_t*>(ly.qkv_w);
-      uint8_t* qs = smem_at<uint8_t>(g.sm_qw);
-      uint8_t* ks = smem_at<uint8_t>(g.sm_kvw);
-      bulk_copy(qs, w + (size_t)a.h * hd * rb, g.q_stage * rb, kBarAtt);
-      const size_t kbase = (size_t)(D + a.h * hd + a.p0) * rb, vbase = (size_t)(2 * D + a.h * hd + a.v0) * rb;
-      bulk_copy(ks, w + kbase, a.nkp * rb, kBarAtt);
-      bulk_copy(ks + (size_t)a.nkp * rb, w + kbase + (size_t)half * rb, a.nkp * rb, kBarAtt);
-      bulk_copy(ks + (size_t)2 * a.nkp * rb, w + vbase, a.nvd * rb, kBarAtt);
-    }
-  }
+  fence_proxy_async_smem();  // earlier generic reads of these buffers before the async writes
+  const uint32_t nrows = a.att ? (uint32_t)(g.q_stage + 2 * a.nkp + a.nvd) : 0u;
+  bar_arm(kBarAtt, nrows * rb + (ly.attn_norm_b ? 2 : 1) * rb);
+  norm_copy(smem_at<uint8_t>(g.sm_anw), ly.attn_norm_w, ly.attn_norm_b, rb, kBarAtt);
+  if (!a.att) return;
+  const uint8_t* w = static_cast<const uint8_t*>(ly.qkv_w);
+  uint8_t* qs = smem_at<uint8_t>(g.sm_qw);
+  uint8_t* ks = smem_at<uint8_t>(g.sm_kvw);
+  bulk_copy(qs, w + (size_t)a.h * hd * rb, g.q_stage * rb, kBarAtt);
+  const size_t kbase = (size_t)(D + a.h * hd + a.p0) * rb, vbase = (size_t)(2 * D + a.h * hd + a.v0) * rb;
+  bulk_copy(ks, w + kbase, a.nkp * rb, kBarAtt);
+  bulk_copy(ks + (size_t)a.nkp * rb, w + kbase + (size_t)half * rb, a.nkp * rb, kBarAtt);
+  bulk_copy(ks + (size_t)2 * a.nkp * rb, w + vbase, a.nvd * rb, kBarAtt);
+}
+
+// Stage the first K/V chunk of this CTA's old tokens of layer l (whole warp).
+template <typename KV>
+__device__ __noinline__ void att_issue_kv(const StepParams& P, int l) {
+  const StepGeom& g = P.g;
+  const AttSplit a = att_split(g, P.d.head_dim, cx_s.pos);
   const int n0 = min(g.chunk_tok, a.t1 - a.t0);
-  if (n0 > 0) kv_issue<KV>(d, g, ly, a.h, a.t0, n0, kBarKv);
+  if (n0 <= 0) return;
+  if ((threadIdx.x & 31) == 0) fence_proxy_async_smem();
+  __syncwarp();
+  kv_issue<KV>(P.d, g, P.layers[l], a.h, a.t0, n0, kBarKv);
 }
 
 // Stage layer l's out_proj rows of this CTA, the router and the MoE norm
@@ -435,31 +448,35 @@ __device__ __noinline__ void norm_smem(float* out, const float* in, int D, int n
 }
 
 // out[r] = rows[r] . x for r < n: rows of nvec 16-byte vectors (row stride
-// nvec) in shared memory -- or, when grows is set, in global memory -- and x
-// (shared memory, fp32).  Warp w forms rows w, w + kSW, ...  No barrier.
-template <typename W>
-__device__ __noinline__ void gemv(const uint4* rows, const uint4* grows, int n, int nvec, const float* x,
-                                  float* out) {
+// nvec) in shared memory (kGlobal false) or global memory, x an fp32 vector
+// in shared memory.  Warp w forms rows w, w + kSW, ...: two rows per
+// iteration and one partial sum per 16-byte vector, so the FMA chains and the
+// two shuffle reductions are independent of each other.  No barrier.
+template <typename W, bool kGlobal>
+__device__ __noinline__ void gemv(const uint4* rows, int n, int nvec, const float* x, float* out) {
   constexpr int PV = Elem<W>::kPerVec;
   const int lane = threadIdx.x & 31;
   if ((threadIdx.x >> 5) >= n) return;  // no rows for this warp
   float xr[Seg<W>::kNV * PV];
   load_x_regs<W>(xr, x, nvec);
-  // Two rows per iteration and one partial sum per 16-byte vector: the FMA
-  // chains and the two shuffle reductions are independent of each other.
 #pragma unroll 1
   for (int r = threadIdx.x >> 5; r < n; r += 2 * kSW) {
     const int r2 = r + kSW;
     const bool two = r2 < n;
+    const uint4* ra = rows + (size_t)r * nvec;
+    const uint4* rb = rows + (size_t)(two ? r2 : r) * nvec;
     uint4 wa[Seg<W>::kNV], wb[Seg<W>::kNV];
 #pragma unroll
     for (int j = 0; j < Seg<W>::kNV; ++j) {
       const int v = lane + kWarp * j;
-      const bool ok = v < nvec;
-      wa[j] = ok ? (grows ? __ldg(grows + (size_t)r * nvec + v) : rows[(size_t)r * nvec + v])
-                 : make_uint4(0u, 0u, 0u, 0u);
-      wb[j] = (ok && two) ? (grows ? __ldg(grows + (size_t)r2 * nvec + v) : rows[(size_t)r2 * nvec + v])
-                          : make_uint4(0u, 0u, 0u, 0u);
+      const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+      if constexpr (kGlobal) {
+        wa[j] = v < nvec ? __ldg(ra + v) : z;
+        wb[j] = v < nvec ? __ldg(rb + v) : z;
+      } else {
+        wa[j] = v < nvec ? ra[v] : z;
+        wb[j] = v < nvec ? rb[v] : z;
+      }
     }
     float sa = 0.f, sb = 0.f;
 #pragma unroll
@@ -477,6 +494,14 @@ __device__ __noinline__ void gemv(const uint4* rows, const uint4* grows, int n, 
       if (two) out[r2] = sb;
     }
   }
+}
+template <typename W>
+__device__ __forceinline__ void gemv_smem(const uint4* rows, int n, int nvec, const float* x, float* out) {
+  gemv<W, false>(rows, n, nvec, x, out);
+}
+template <typename W>
+__device__ __forceinline__ void gemv_global(const uint4* rows, int n, int nvec, const float* x, float* out) {
+  gemv<W, true>(rows, n, nvec, x, out);
 }
 
 // Online softmax of q over K/V chunks of this split's old tokens [t0, t1)
@@ -586,25 +611,19 @@ __device__ __noinline__ bool att_phase(const StepParams& P, int l) {
   const W* nw = smem_at<const W>(g.sm_anw);
   norm_smem<W>(xn, xs, D, d.norm, d.eps, nw, ly.attn_norm_b ? nw + D : nullptr);
   STEP_STAMP(l, 2);
-  if (!a.att) {
-    // CTAs without attention work stage the next layer's attention norm
-    // weights (or their first LM-head rows) here
-    if (tid < 32) {
-      if (l + 1 < d.num_layers)
-        att_issue<W, KV>(P, l + 1);
-      else if (tid == 0)
-        head_issue<W>(P, 0, g.head_stages);
-    }
-    return true;
-  }
+  if (!a.att) return true;
 
   // ---- q rows of head h and this CTA's k / v rows: qk[0, hd) = q, qk[hd, hd + nkv) = k, v ----
   float* qk = smem_at<float>(g.sm_qk);
-  gemv<W>(smem_at<const uint4>(g.sm_qw), nullptr, g.q_stage, nvD, xn, qk);
-  if (g.q_stage < hd)
-    gemv<W>(nullptr, rowp(ly.qkv_w, (int64_t)a.h * hd + g.q_stage, (int64_t)nvD * 16), hd - g.q_stage, nvD, xn,
-            qk + g.q_stage);
-  gemv<W>(smem_at<const uint4>(g.sm_kvw), nullptr, nkv, nvD, xn, qk + hd);
+  if (g.q_stage == hd && g.sm_kvw == g.sm_qw + (uint32_t)(hd * nvD * 16)) {
+    gemv_smem<W>(smem_at<const uint4>(g.sm_qw), hd + nkv, nvD, xn, qk);  // q and k / v rows are adjacent
+  } else {
+    gemv_smem<W>(smem_at<const uint4>(g.sm_qw), g.q_stage, nvD, xn, qk);
+    if (g.q_stage < hd)
+      gemv_global<W>(rowp(ly.qkv_w, (int64_t)a.h * hd + g.q_stage, (int64_t)nvD * 16), hd - g.q_stage, nvD, xn,
+                     qk + g.q_stage);
+    gemv_smem<W>(smem_at<const uint4>(g.sm_kvw), nkv, nvD, xn, qk + hd);
+  }
   __syncthreads();
   STEP_STAMP(l, 3);
   // bias; RoPE of q (pairs j, j + hd/2) and of this CTA's k pairs; k / v
@@ -677,14 +696,6 @@ __device__ __noinline__ bool att_phase(const StepParams& P, int l) {
     ll_put(be + 1, cx_s.l, tag);
     ll_put(be + 2, sp, tag);
   }
-  // then stage the next layer's attention inputs (or the first LM-head rows)
-  // from the last warp, which holds no merge words
-  if (tid >= kST - 32) {
-    if (l + 1 < d.num_layers)
-      att_issue<W, KV>(P, l + 1);
-    else if (tid == kST - 32)
-      head_issue<W>(P, 0, g.head_stages);
-  }
   STEP_STAMP(l, 6);
 
   // ---- MERGE: ab[0, 3S) = (m, l, sp) of every split, ab[3S, 3S + S nvd) = acc of my dims ----
@@ -704,34 +715,43 @@ __device__ __noinline__ bool att_phase(const StepParams& P, int l) {
   __syncthreads();  // gather indices ready, ab (PV groups) fully read
   if (!recv(ll + g.off_b[par] + (int64_t)a.h * S * (3 + hd), nwords, tag, ab, gat_s, ll, d.status)) return false;
   STEP_STAMP(l, 7);
-  if (tid < nvd) {
-    const float scale = d.attn_scale;
-    float spn = 0.f;
+  if (tid < 32) {
+    // warp 0: split weights w_k = e^(m_k - M) with the new token as one more
+    // term (score q.k_new, value v_new); lane k holds splits k, k + 32, ...
+    float sp = 0.f, mx = -INFINITY;
 #pragma unroll 1
-    for (int k = 0; k < S; ++k) spn += ab[3 * k + 2];
-    const float snew = spn * scale;
-    float M = snew;
-#pragma unroll 1
-    for (int k = 0; k < S; ++k) M = fmaxf(M, ab[3 * k]);
-    const float wn = expf(snew - M);
-    float den = wn, num = wn * kv[2 * a.nkp + tid];
-#pragma unroll 1
-    for (int k = 0; k < S; ++k) {
-      const float mk = ab[3 * k];
-      if (mk == -INFINITY) continue;
-      const float wk = expf(mk - M);
-      den = fmaf(ab[3 * k + 1], wk, den);
-      num = fmaf(ab[nm + k * nvd + tid], wk, num);
+    for (int k = tid; k < S; k += 32) {
+      sp += ab[3 * k + 2];
+      mx = fmaxf(mx, ab[3 * k]);
     }
-    ll_put(ll + g.off_c[par] + (int64_t)a.h * hd + a.v0 + tid, num / den, tag);
+    const float snew = warp_sum(sp) * d.attn_scale;
+    const float M = fmaxf(warp_max(mx), snew);
+    float lw = 0.f;
+#pragma unroll 1
+    for (int k = tid; k < S; k += 32) {
+      const float mk = ab[3 * k];
+      const float wk = mk == -INFINITY ? 0.f : expf(mk - M);
+      gat_s[k] = __float_as_int(wk);
+      lw = fmaf(ab[3 * k + 1], wk, lw);
+    }
+    const float wn = expf(snew - M);
+    const float den = warp_sum(lw) + wn;
+    __syncwarp();
+    if (tid < nvd) {
+      float num = wn * kv[2 * a.nkp + tid];
+#pragma unroll 1
+      for (int k = 0; k < S; ++k) num = fmaf(ab[nm + k * nvd + tid], __int_as_float(gat_s[k]), num);
+      ll_put(ll + g.off_c[par] + (int64_t)a.h * hd + a.v0 + tid, num / den, tag);
+    }
   }
+  STEP_STAMP(l, 15);
   return true;
 }
 
 // ---------------------------------------------------------------------------
 // PROJ: x_mid rows = x + out_proj(o) (+ bias) -> exchange D.
 // ---------------------------------------------------------------------------
-template <typename W>
+template <typename W, typename KV>
 __device__ __noinline__ bool proj_phase(const StepParams& P, int l) {
   const mie_step_desc& d = P.d;
   const StepGeom& g = P.g;
@@ -745,10 +765,25 @@ __device__ __noinline__ bool proj_phase(const StepParams& P, int l) {
   const int nr = r1 - r0;
   float* ob = smem_at<float>(g.sm_o);
   float* ab = smem_at<float>(g.sm_acc);
+  // While o is on its way: stage the next layer's attention inputs (the
+  // attention staging area is free since this layer's attention), or the
+  // first LM-head rows after the last layer.
+  const int warp = tid >> 5;
+  STEP_STAMP_T(l, 16, kST - 32);
+  if (warp == kSW - 1 && (tid & 31) == 0) {
+    if (l + 1 < d.num_layers)
+      att_issue_rows<W>(P, l + 1);
+    else
+      head_issue<W>(P, 0, g.head_stages);
+  } else if (warp == kSW - 2 && l + 1 < d.num_layers) {
+    att_issue_kv<KV>(P, l + 1);
+  }
+  STEP_STAMP_T(l, 17, kST - 32);
+  STEP_STAMP(l, 18);
   if (!recv(ll + g.off_c[l & 1], D, tag, ob, nullptr, ll, d.status)) return false;
   STEP_STAMP(l, 8);
   if (!bar_wait(kBarSide, ll, d.status)) return false;
-  gemv<W>(smem_at<const uint4>(g.sm_moe), nullptr, nr, nvD, ob, ab);
+  gemv_smem<W>(smem_at<const uint4>(g.sm_moe), nr, nvD, ob, ab);
   __syncthreads();
   if (tid < nr) {
     const int r = r0 + tid;
@@ -795,45 +830,69 @@ __device__ __noinline__ bool moe_phase(const StepParams& P, int l) {
   STEP_STAMP(l, 10);
   const W* nw = reinterpret_cast<const W*>(ms + (size_t)(g.nr_max + E) * rbD);
   norm_smem<W>(xn, xm, D, d.norm, d.eps, nw, ly.moe_norm_b ? nw + D : nullptr);
-  gemv<W>(reinterpret_cast<const uint4*>(ms + (size_t)g.nr_max * rbD), nullptr, E, nvD, xn, ab);
+  gemv_smem<W>(reinterpret_cast<const uint4*>(ms + (size_t)g.nr_max * rbD), E, nvD, xn, ab);
   __syncthreads();
-  if (tid == 0) {
-    // repeated argmax, strict '>' over ascending ids: ties keep the lower id
-    int i0 = 0;
-#pragma unroll 1
-    for (int e = 1; e < E; ++e)
-      if (ab[e] > ab[i0]) i0 = e;
-    int i1 = i0 == 0 ? 1 : 0;
-#pragma unroll 1
-    for (int e = 0; e < E; ++e)
-      if (e != i0 && ab[e] > ab[i1]) i1 = e;
-    const float e1 = expf(ab[i1] - ab[i0]);
-    cx_s.sel[0] = i0;
-    cx_s.sel[1] = i1;
-    cx_s.wts[0] = 1.0f / (1.0f + e1);
-    cx_s.wts[1] = e1 / (1.0f + e1);
+  if (tid < 32) {
+    // top-2 over the router logits in warp 0 (lane e holds expert e):
+    // largest logit, ties to the lower id -- the same choice as a repeated
+    // argmax scanning ascending ids with a strict '>'
+    const float v = tid < E ? ab[tid] : -INFINITY;
+    float bv = v;
+    int bi = tid < E ? tid : 0x7fffffff;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (better(ov, oi, bv, bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    const int i0 = bi;
+    float cv = (tid < E && tid != i0) ? v : -INFINITY;
+    int ci = (tid < E && tid != i0) ? tid : 0x7fffffff;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, cv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, ci, o);
+      if (better(ov, oi, cv, ci)) {
+        cv = ov;
+        ci = oi;
+      }
+    }
+    const int i1 = ci;
+    if (tid == 0) {
+      const float e1 = expf(cv - bv);
+      cx_s.sel[0] = i0;
+      cx_s.sel[1] = i1;
+      cx_s.wts[0] = 1.0f / (1.0f + e1);
+      cx_s.wts[1] = e1 / (1.0f + e1);
+    }
     if constexpr (kStaged) {
       // the selected experts' rows of this CTA -> shared memory (over the
       // out_proj / router / norm rows, all read by now): gate rows of units
-      // [u0, u1), up rows (SwiGLU), down rows (slot 0 then slot 1)
-      fence_proxy_async_smem();
-      bar_arm(kBarMoe, (uint32_t)(nmat * nu * rbD + 2 * nr * rbH));
-#pragma unroll 1
-      for (int m = 0; m < nmat; ++m) {
-        const uint8_t* w = static_cast<const uint8_t*>(m ? ly.w3 : ly.w1);
-#pragma unroll 1
-        for (int k = 0; k < 2; ++k) {
-          const int ua = max(u0, k * Hx), ub = min(u1, (k + 1) * Hx);
-          if (ub > ua)
-            bulk_copy(ms + (size_t)(m * nu + ua - u0) * rbD, w + ((size_t)(k ? i1 : i0) * Hx + ua - k * Hx) * rbD,
-                      (uint32_t)((ub - ua) * rbD), kBarMoe);
-        }
+      // [u0, u1), up rows (SwiGLU), down rows (slot 0 then slot 1); lane c
+      // issues copy c
+      if (tid == 0) {
+        fence_proxy_async_smem();
+        bar_arm(kBarMoe, (uint32_t)(nmat * nu * rbD + 2 * nr * rbH));
       }
-#pragma unroll 1
-      for (int k = 0; k < 2; ++k)
+      __syncwarp();
+      if (tid < 2 * nmat) {
+        const int m = tid >> 1, k = tid & 1;
+        const uint8_t* w = static_cast<const uint8_t*>(m ? ly.w3 : ly.w1);
+        const int ua = max(u0, k * Hx), ub = min(u1, (k + 1) * Hx);
+        fence_proxy_async_smem();
+        if (ub > ua)
+          bulk_copy(ms + (size_t)(m * nu + ua - u0) * rbD, w + ((size_t)(k ? i1 : i0) * Hx + ua - k * Hx) * rbD,
+                    (uint32_t)((ub - ua) * rbD), kBarMoe);
+      } else if (tid >= 8 && tid < 10) {
+        const int k = tid - 8;
+        fence_proxy_async_smem();
         bulk_copy(ms + (size_t)nmat * nu * rbD + (size_t)k * nr * rbH,
                   static_cast<const uint8_t*>(ly.w2) + ((size_t)(k ? i1 : i0) * D + r0) * rbH, (uint32_t)(nr * rbH),
                   kBarMoe);
+      }
     }
   }
   __syncthreads();
@@ -842,7 +901,7 @@ __device__ __noinline__ bool moe_phase(const StepParams& P, int l) {
   // up units: gate (and up) rows -> ab[0, nmat * nu)
   if constexpr (kStaged) {
     if (!bar_wait(kBarMoe, ll, d.status)) return false;
-    gemv<W>(reinterpret_cast<const uint4*>(ms), nullptr, nmat * nu, nvD, xn, ab);
+    gemv_smem<W>(reinterpret_cast<const uint4*>(ms), nmat * nu, nvD, xn, ab);
   } else {
 #pragma unroll 1
     for (int m = 0; m < nmat; ++m) {
@@ -851,8 +910,8 @@ __device__ __noinline__ bool moe_phase(const StepParams& P, int l) {
       for (int k = 0; k < 2; ++k) {
         const int ua = max(u0, k * Hx), ub = min(u1, (k + 1) * Hx);
         if (ub > ua)
-          gemv<W>(nullptr, rowp(w, (int64_t)(k ? sel1 : sel0) * Hx + ua - k * Hx, rbD), ub - ua, nvD, xn,
-                  ab + m * nu + (ua - u0));
+          gemv_global<W>(rowp(w, (int64_t)(k ? sel1 : sel0) * Hx + ua - k * Hx, rbD), ub - ua, nvD, xn,
+                         ab + m * nu + (ua - u0));
       }
     }
   }
@@ -872,11 +931,11 @@ __device__ __noinline__ bool moe_phase(const StepParams& P, int l) {
 #pragma unroll 1
   for (int k = 0; k < 2; ++k) {
     if constexpr (kStaged)
-      gemv<W>(reinterpret_cast<const uint4*>(ms + (size_t)nmat * nu * rbD + (size_t)k * nr * rbH), nullptr, nr, nvH,
-              hb + (size_t)k * Hx, ab + k * nr);
+      gemv_smem<W>(reinterpret_cast<const uint4*>(ms + (size_t)nmat * nu * rbD + (size_t)k * nr * rbH), nr, nvH,
+                   hb + (size_t)k * Hx, ab + k * nr);
     else
-      gemv<W>(nullptr, rowp(ly.w2, (int64_t)(k ? sel1 : sel0) * D + r0, rbH), nr, nvH, hb + (size_t)k * Hx,
-              ab + k * nr);
+      gemv_global<W>(rowp(ly.w2, (int64_t)(k ? sel1 : sel0) * D + r0, rbH), nr, nvH, hb + (size_t)k * Hx,
+                     ab + k * nr);
   }
   __syncthreads();
   if (tid < nr) {
@@ -931,7 +990,7 @@ __device__ __noinline__ bool head_phase(const StepParams& P) {
     const int slot = i % g.head_stages;
     if (!bar_wait(kBarHead + slot, ll, d.status)) return false;
     const int r0 = v0h + i * g.head_rows, nrw = min(g.head_rows, v1h - r0);
-    gemv<W>(smem_at<const uint4>(g.sm_qw) + (size_t)slot * g.head_rows * nvD, nullptr, nrw, nvD, xn, ab);
+    gemv_smem<W>(smem_at<const uint4>(g.sm_qw) + (size_t)slot * g.head_rows * nvD, nrw, nvD, xn, ab);
     __syncthreads();  // stage no longer read, ab complete
     if (tid == 0 && i + g.head_stages < nst) head_issue<W>(P, i + g.head_stages, 1);
     if (tid < nrw) {
@@ -1064,14 +1123,13 @@ __global__ void __launch_bounds__(kST, 1) step_kernel(const __grid_constant__ St
       blk_s[threadIdx.x] = __ldcg(d.block_table + b0 + threadIdx.x);
     __syncthreads();
   }
-  if (threadIdx.x < 32) {
-    att_issue<W, KV>(P, 0);
-    if (threadIdx.x == 0) side_issue<W>(P, 0);
-  }
+  if (threadIdx.x == 0) att_issue_rows<W>(P, 0);
+  if (threadIdx.x >= 32 && threadIdx.x < 64) att_issue_kv<KV>(P, 0);
+  if (threadIdx.x == 64) side_issue<W>(P, 0);
   bool ok = true;
 #pragma unroll 1
   for (int l = 0; l < d.num_layers && ok; ++l)
-    ok = att_phase<W, KV>(P, l) && proj_phase<W>(P, l) && moe_phase<W>(P, l);
+    ok = att_phase<W, KV>(P, l) && proj_phase<W, KV>(P, l) && moe_phase<W>(P, l);
   if (ok) ok = head_phase<W>(P);
   if (!ok) drain_copies();
 }
