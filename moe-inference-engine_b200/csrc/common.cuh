@@ -270,6 +270,13 @@ __device__ __forceinline__ uint64_t policy_evict_first() {
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
   return p;
 }
+// L2 policy for data reread every decode step and small enough to stay in L2
+// (the LM head): kept in preference to streamed data.
+__device__ __forceinline__ uint64_t policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
 
 // Largest chunk one bulk copy moves here (bytes); larger ranges are split.
 constexpr uint32_t kBulkMax = 1u << 16;

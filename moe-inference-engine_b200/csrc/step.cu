@@ -217,7 +217,7 @@ __shared__ float bestv_s[kSW];
 __shared__ int besti_s[kSW];
 // mbarriers of the bulk-copy staging, with per-barrier counts of armed and
 // completed phases (a wait uses parity = completed & 1).
-constexpr int kBarAtt = 0, kBarKv = 1, kBarSide = 2, kBarMoe = 3, kBarHead = 4;
+constexpr int kBarAtt = 0, kBarKv = 1, kBarSide = 2, kBarMoe = 3, kBarDown = 4, kBarHead = 5;
 constexpr int kNumBars = kBarHead + kStepHeadStagesMax;
 __shared__ __align__(8) uint64_t bars_s[kNumBars];
 __shared__ uint32_t bar_armed_s[kNumBars], bar_done_s[kNumBars];
@@ -238,12 +238,16 @@ __device__ __forceinline__ void bar_arm(int b, uint32_t bytes) {
   mbar_arrive_expect_tx(&bars_s[b], bytes);
 }
 // Bulk copy global -> shared counted on barrier b (16-byte aligned, size a
-// multiple of 16), in pieces of at most 64 KB.
-__device__ __noinline__ void bulk_copy(void* dst, const void* src, uint32_t bytes, int b) {
+// multiple of 16), in pieces of at most 64 KB.  Everything a step streams
+// once (layer weights, K/V) is marked evict-first in L2; `keep` (the tied LM
+// head, 77 MB for the miniMoE vocabulary) is marked evict-last, so it can
+// stay in the 126 MB L2 from one decode step to the next.
+__device__ __noinline__ void bulk_copy(void* dst, const void* src, uint32_t bytes, int b, bool keep = false) {
+  const uint64_t pol = keep ? policy_evict_last() : policy_evict_first();
 #pragma unroll 1
   for (uint32_t o = 0; o < bytes; o += 65536u)
-    bulk_g2s(static_cast<uint8_t*>(dst) + o, static_cast<const uint8_t*>(src) + o, min(65536u, bytes - o),
-             &bars_s[b]);
+    bulk_g2s_stream(static_cast<uint8_t*>(dst) + o, static_cast<const uint8_t*>(src) + o, min(65536u, bytes - o),
+                    &bars_s[b], pol);
 }
 // Every thread: wait for the oldest armed phase of barrier b (bounded).
 __device__ __noinline__ bool bar_wait(int b, uint64_t* hdr, int32_t* status) {
@@ -401,7 +405,7 @@ __device__ __noinline__ void head_issue(const StepParams& P, int first, int coun
     const int r0 = v0h + i * g.head_rows, nrw = min(g.head_rows, v1h - r0);
     bar_arm(kBarHead + slot, nrw * rb);
     bulk_copy(smem_at<uint8_t>(g.sm_qw) + (size_t)slot * g.head_rows * rb,
-              static_cast<const uint8_t*>(d.embedding) + (size_t)r0 * rb, nrw * rb, kBarHead + slot);
+              static_cast<const uint8_t*>(d.embedding) + (size_t)r0 * rb, nrw * rb, kBarHead + slot, true);
   }
 }
 
@@ -875,7 +879,8 @@ __device__ __noinline__ bool moe_phase(const StepParams& P, int l) {
       // issues copy c
       if (tid == 0) {
         fence_proxy_async_smem();
-        bar_arm(kBarMoe, (uint32_t)(nmat * nu * rbD + 2 * nr * rbH));
+        bar_arm(kBarMoe, (uint32_t)(nmat * nu * rbD));  // up rows
+        bar_arm(kBarDown, (uint32_t)(2 * nr * rbH));    // down rows, needed after exchange E
       }
       __syncwarp();
       if (tid < 2 * nmat) {
@@ -891,7 +896,7 @@ __device__ __noinline__ bool moe_phase(const StepParams& P, int l) {
         fence_proxy_async_smem();
         bulk_copy(ms + (size_t)nmat * nu * rbD + (size_t)k * nr * rbH,
                   static_cast<const uint8_t*>(ly.w2) + ((size_t)(k ? i1 : i0) * D + r0) * rbH, (uint32_t)(nr * rbH),
-                  kBarMoe);
+                  kBarDown);
       }
     }
   }
@@ -928,6 +933,9 @@ __device__ __noinline__ bool moe_phase(const StepParams& P, int l) {
   // ---- DOWN ----
   if (!recv(ll + g.off_e[par], 2 * Hx, tag, hb, nullptr, ll, d.status)) return false;
   STEP_STAMP(l, 13);
+  if constexpr (kStaged) {
+    if (!bar_wait(kBarDown, ll, d.status)) return false;
+  }
 #pragma unroll 1
   for (int k = 0; k < 2; ++k) {
     if constexpr (kStaged)
