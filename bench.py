@@ -295,8 +295,20 @@ def run_b200(args, rank, world, device):
     mean_ctx = PROMPT_LEN + NEW_TOKENS / 2
     kv_bytes = KV_BYTES_PER_CTX * mean_ctx
     k_roof = kernel_rooflines(model, cache, hbm_peak) if rank == 0 else {}
-    dominant = "moe_decode"
-    kr = k_roof.get(dominant, {"us": None, "gbs": None, "frac": None, "bytes": MOE_LAYER_BYTES})
+    persistent = launches_per_token == 1
+    # dominant kernel: the persistent step kernel (one launch per token) or,
+    # on the per-op path, the fused MoE kernel timed in isolation
+    if persistent:
+        dominant = "step_kernel (persistent decode step, one launch per token)"
+        step_bytes = weights_bytes + kv_bytes
+        kr = {"us": step_s * 1e6, "gbs": step_bytes / step_s / 1e9, "bytes": step_bytes}
+        kr["frac"] = kr["gbs"] / hbm_peak
+        roof_note = ("per-launch average of the graph-replayed step over the timed region (CUDA events); "
+                     "algorithmic bytes = active bf16 weights + the K/V bytes at the mean context")
+    else:
+        dominant = "moe_decode"
+        kr = k_roof.get(dominant, {"us": None, "gbs": None, "frac": None, "bytes": MOE_LAYER_BYTES})
+        roof_note = "fused MoE kernel timed in isolation (graph of 240 launches over 12 layers' experts)"
 
     result = {
         "metric": METRIC,
@@ -340,9 +352,10 @@ def run_b200(args, rank, world, device):
             "unit": "GB/s",
             "frac": kr["frac"],
             "traffic": None,
-            "algorithmic_bytes_per_launch": MOE_LAYER_BYTES,
+            "algorithmic_bytes_per_launch": kr["bytes"],
             "us_per_launch": kr["us"],
-            "peak_source": peak_src + " (burst copy; kernel timed in isolation)",
+            "peak_source": peak_src,
+            "note": roof_note,
         },
         "kernels": k_roof,
         "clocks": clocks.summary(),
@@ -364,8 +377,9 @@ def cpu_baseline(seconds: float = 15.0):
     """The reference path (--moe reference, contiguous fp32 KV) on the host cores.
 
     Restated by the oracle (the reference engine cannot run BASELINE's
-    architecture unmodified).  Sample: a 32-token prompt prefill (untimed)
-    then greedy decode steps at context ~33+, timed until `seconds` elapse.
+    architecture unmodified).  Sample: the config[3] 512-token prompt prefill
+    (untimed) then greedy decode steps at context 513+, timed until `seconds`
+    elapse.
     """
     import oracle
 
@@ -373,7 +387,7 @@ def cpu_baseline(seconds: float = 15.0):
     torch.set_num_threads(ncores)
     P = oracle.init_params(oracle.BASELINE_ARCH, seed=0)
     dec = oracle.Decoder(P, oracle.BASELINE_ARCH)
-    prompt = torch.randint(0, 50304, (1, 32), generator=torch.Generator().manual_seed(3))
+    prompt = torch.randint(0, 50304, (1, PROMPT_LEN), generator=torch.Generator().manual_seed(3))
     with torch.no_grad():
         logits = dec.forward(prompt)
         tok = logits[0, -1].argmax().view(1, 1)
@@ -390,7 +404,7 @@ def cpu_baseline(seconds: float = 15.0):
         "unit": "tok/s",
         "cores": ncores,
         "kind": "port",
-        "sample": f"BASELINE arch fp32, 32-token prompt, {len(times)} greedy decode steps "
+        "sample": f"BASELINE arch fp32, {PROMPT_LEN}-token prompt, {len(times)} greedy decode steps "
                   f"(p50 {times[len(times) // 2] * 1e3:.1f} ms/token)",
     }
 
@@ -428,6 +442,33 @@ def run_reference(args):
     }
 
 
+def run_profile(steps: int):
+    """Profiling workload (``--profile N``): the bench's model, prompt and paged
+    cache, then N decode steps replayed from the captured graph; no timing.
+    Kept small so an ncu capture of one step launch ends quickly."""
+    device = torch.device("cuda", 0)
+    model = build_model(device, torch.bfloat16)
+    prompt = torch.randint(0, 50304, (PROMPT_LEN,), generator=torch.Generator().manual_seed(3))
+    alloc = model.new_block_allocator(num_blocks=-(-(PROMPT_LEN + steps) // 16) + 8, block_size=16,
+                                      attention_mode="direct")
+    cache = alloc.new_cache()
+    runner = model.decode_runner()
+    with torch.no_grad():
+        logits = model(prompt[None].to(device), cache)
+    P = cache.position
+    cache.reserve(P + steps)
+    graph = runner.graph_for(cache, P + steps)
+    runner.token.fill_(int(logits[0, -1].float().argmax()))
+    runner.pos.fill_(P)
+    runner.done.zero_()
+    runner.log_count.zero_()
+    for _ in range(steps):
+        graph.replay()
+    torch.cuda.synchronize()
+    runner.check_status()
+    print(json.dumps({"profile_steps": steps, "tokens": int(runner.log_count.item())}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -436,7 +477,12 @@ def main():
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--profile", type=int, default=0, metavar="N",
+                    help="profiling workload: N decode steps after the prompt, no timing")
     args = ap.parse_args()
+    if args.profile:
+        run_profile(args.profile)
+        return
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
 
