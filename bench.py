@@ -442,6 +442,60 @@ def run_reference(args):
     }
 
 
+def run_expert_parallel(args, rank, world, device):
+    """config[4b]: one request decoded with the 8 experts of every layer split
+    8/N over the N ranks and an NCCL all-reduce of the MoE partial per layer.
+    ``value`` = decode tok/s of the single stream (= aggregate: all ranks serve
+    the same request); device time, CUDA events, max over ranks."""
+    from moe_engine.expert_parallel import ExpertParallelDecoder
+
+    model = build_model(device, torch.bfloat16)
+    prompt = torch.randint(0, 50304, (PROMPT_LEN,), generator=torch.Generator().manual_seed(3))
+    max_blocks = -(-(PROMPT_LEN + NEW_TOKENS) // 16)
+    alloc = model.new_block_allocator(num_blocks=max_blocks + 8, block_size=16, attention_mode="direct")
+    ep = ExpertParallelDecoder(model)
+    times = []
+    produced = 0
+    for it in range(args.warmup + args.steps):
+        cache = alloc.new_cache()
+        _, first = ep.prefill(prompt, cache)
+        torch.distributed.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        new = ep.decode(first, NEW_TOKENS, cache)
+        e1.record()
+        torch.cuda.synchronize()
+        cache.free()
+        if it >= args.warmup:
+            times.append(e0.elapsed_time(e1) / 1e3)
+            produced += int(new.numel())
+    t = torch.tensor([sum(times)], device=device)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    elapsed = float(t)
+    value = produced / elapsed
+    return {
+        "metric": METRIC + " -- expert parallel",
+        "value": value,
+        "unit": "tok/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": elapsed / args.steps * 1e3,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (random-init weights N(0,0.02), seeded random prompt ids)",
+        "config": {"workload": "config[4b] expert parallel: config[3] request, experts split %d/%d per rank, "
+                               "NCCL all-reduce of the fp32 [768] MoE partial per layer, layer-by-layer launches"
+                               % (model.config.num_experts // world, model.config.num_experts),
+                   "parallelism": f"ep{world}"},
+        "per_stream_tok_s": value,
+        "aggregate_tok_s": value,
+    }
+
+
 def run_profile(steps: int):
     """Profiling workload (``--profile N``): the bench's model, prompt and paged
     cache, then N decode steps replayed from the captured graph; no timing.
@@ -477,6 +531,8 @@ def main():
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--mode", choices=["replicas", "ep"], default="replicas",
+                    help="N>1: independent replicas (default) or one request expert parallel")
     ap.add_argument("--profile", type=int, default=0, metavar="N",
                     help="profiling workload: N decode steps after the prompt, no timing")
     args = ap.parse_args()
@@ -503,7 +559,12 @@ def main():
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                              device_id=device)
     try:
-        res = run_b200(args, rank, world, device)
+        if args.mode == "ep":
+            if world < 2:
+                ap.error("--mode ep needs torchrun with 2 or more ranks")
+            res = run_expert_parallel(args, rank, world, device)
+        else:
+            res = run_b200(args, rank, world, device)
         if rank == 0:
             print(json.dumps(res), flush=True)
     finally:

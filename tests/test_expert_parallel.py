@@ -1,0 +1,121 @@
+"""Expert-parallel decode (config[4b]): experts split over ranks, the MoE
+output completed by an all-reduce of per-rank partials.
+
+* CPU (gloo, 2 and 4 ranks): the decomposition the product relies on -- each
+  rank's weighted sum over the selected experts it owns, summed over ranks,
+  equals the full MoE output of the oracle; and the expert shard arithmetic.
+* GPU (NCCL, 2 ranks, needs 2 GPUs): expert-parallel greedy decode of the
+  BASELINE model in fp32 gives the same tokens as the oracle and as the
+  single-GPU path.
+"""
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+import oracle
+from moe_engine.expert_parallel import expert_shard
+
+
+def free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def test_expert_shard():
+    assert [expert_shard(8, r, 2) for r in range(2)] == [(0, 4), (4, 4)]
+    assert [expert_shard(8, r, 8) for r in range(8)] == [(r, 1) for r in range(8)]
+    assert expert_shard(8, 0, 1) == (0, 8)
+    with pytest.raises(ValueError):
+        expert_shard(8, 0, 3)
+    with pytest.raises(ValueError):
+        expert_shard(8, 2, 2)
+
+
+def _decomposition_worker(rank, world, port, out):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        arch = oracle.BASELINE_ARCH.with_(num_layers=1, vocab_size=64, max_seq_length=8, hidden_dim=64,
+                                          num_heads=4, expert_hidden_dim=48)
+        P = oracle.init_params(arch, seed=7)
+        x = torch.randn(1, 1, arch.hidden_dim, generator=torch.Generator().manual_seed(8))
+        full, (logits, ids, weights) = oracle.moe_forward(x, P, 0, arch)
+        base, count = expert_shard(arch.num_experts, rank, world)
+        part = torch.zeros(arch.hidden_dim)
+        for slot in range(ids.shape[-1]):
+            e = int(ids.view(-1)[slot])
+            if base <= e < base + count:
+                part += weights.view(-1)[slot] * oracle.expert_forward(x.view(1, -1), P, f"MoEBlocks.0.moe.experts.{e}.",
+                                                                       arch).view(-1)
+        dist.all_reduce(part)
+        if rank == 0:
+            out.put((part, full.view(-1)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_partials_all_reduced_equal_full_moe(world):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    procs = [ctx.Process(target=_decomposition_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    part, full = q.get(timeout=120)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    torch.testing.assert_close(part, full, atol=1e-6, rtol=1e-5)
+
+
+def _ep_gpu_worker(rank, world, port, out):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    import datetime
+
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=dev)
+    try:
+        from moe_engine.expert_parallel import ExpertParallelDecoder
+        from moe_engine.model import Model, baseline_config
+        from tests.helpers import engine_state_dict
+
+        P = oracle.init_params(oracle.BASELINE_ARCH, seed=0)
+        m = Model(baseline_config()).eval()
+        m.load_state_dict(engine_state_dict(P))
+        m = m.to(dev, torch.float32)
+        prompt = torch.randint(0, 50304, (16,), generator=torch.Generator().manual_seed(0))
+        alloc = m.new_block_allocator(num_blocks=8, block_size=16, attention_mode="direct")
+        ep = ExpertParallelDecoder(m)
+        got = ep.generate(prompt, 24, alloc.new_cache())[0].tolist()
+        single = m.generate(prompt, max_new_tokens=24, temperature=0)[0].tolist() if rank == 0 else None
+        if rank == 0:
+            out.put((got, single, oracle.generate_greedy(P, oracle.BASELINE_ARCH, prompt, 24)))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="expert parallel needs 2 GPUs")
+def test_expert_parallel_greedy_matches_oracle_and_single_gpu():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    procs = [ctx.Process(target=_ep_gpu_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got, single, want = q.get(timeout=600)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert got == want
+    assert got == single
