@@ -58,6 +58,7 @@ struct StepGeom {
   int moe_staged; // 1: the selected experts' rows are staged in shared memory
   int nr_max;     // out_proj / down rows of one CTA (upper bound)
   int head_rows, head_stages;  // LM-head ring: rows per stage, stages
+  int head_early;               // ring stages inside the attention staging area
   // shared memory (byte offsets): fp32 vectors (x, normalised x, x_mid, expert
   // activations, attention output, q + this CTA's k / v values, scratch,
   // scores), the attention norm weights, the attention staging area sm_qw ..

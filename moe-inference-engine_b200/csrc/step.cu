@@ -365,7 +365,8 @@ __device__ __noinline__ void att_issue_kv(const StepParams& P, int l) {
 }
 
 // Stage layer l's out_proj rows of this CTA, the router and the MoE norm
-// weights -- or, for l == num_layers, the final norm weights (one thread).
+// weights -- or, for l == num_layers, the final norm weights, into the
+// attention norm slot (one thread).
 template <typename W>
 __device__ __noinline__ void side_issue(const StepParams& P, int l) {
   const mie_step_desc& d = P.d;
@@ -376,7 +377,7 @@ __device__ __noinline__ void side_issue(const StepParams& P, int l) {
   fence_proxy_async_smem();
   if (l == d.num_layers) {
     bar_arm(kBarSide, (d.final_norm_b ? 2 : 1) * rb);
-    norm_copy(dst, d.final_norm_w, d.final_norm_b, rb, kBarSide);
+    norm_copy(smem_at<uint8_t>(g.sm_anw), d.final_norm_w, d.final_norm_b, rb, kBarSide);
     return;
   }
   const mie_layer_desc& ly = P.layers[l];
@@ -389,7 +390,7 @@ __device__ __noinline__ void side_issue(const StepParams& P, int l) {
 }
 
 // Stages [first, first + count) of this CTA's LM-head rows (one thread) into
-// the ring in the attention staging area.
+// the ring, which spans the attention staging area and the expert area.
 template <typename W>
 __device__ __noinline__ void head_issue(const StepParams& P, int first, int count) {
   const mie_step_desc& d = P.d;
@@ -457,12 +458,15 @@ __device__ __noinline__ void norm_smem(float* out, const float* in, int D, int n
 // iteration and one partial sum per 16-byte vector, so the FMA chains and the
 // two shuffle reductions are independent of each other.  No barrier.
 template <typename W, bool kGlobal>
-__device__ __noinline__ void gemv(const uint4* rows, int n, int nvec, const float* x, float* out) {
+__device__ __noinline__ void gemv(const uint4* rows, int n, int nvec, const float* x, float* out,
+                                  const float* x1 = nullptr, int split = 0) {
   constexpr int PV = Elem<W>::kPerVec;
   const int lane = threadIdx.x & 31;
   if ((threadIdx.x >> 5) >= n) return;  // no rows for this warp
+  // rows [split, n) dot x1 instead of x (n <= kSW: one row per warp)
+  const float* xb = (x1 && (int)(threadIdx.x >> 5) >= split) ? x1 : x;
   float xr[Seg<W>::kNV * PV];
-  load_x_regs<W>(xr, x, nvec);
+  load_x_regs<W>(xr, xb, nvec);
 #pragma unroll 1
   for (int r = threadIdx.x >> 5; r < n; r += 2 * kSW) {
     const int r2 = r + kSW;
@@ -500,8 +504,9 @@ __device__ __noinline__ void gemv(const uint4* rows, int n, int nvec, const floa
   }
 }
 template <typename W>
-__device__ __forceinline__ void gemv_smem(const uint4* rows, int n, int nvec, const float* x, float* out) {
-  gemv<W, false>(rows, n, nvec, x, out);
+__device__ __forceinline__ void gemv_smem(const uint4* rows, int n, int nvec, const float* x, float* out,
+                                          const float* x1 = nullptr, int split = 0) {
+  gemv<W, false>(rows, n, nvec, x, out, x1, split);
 }
 template <typename W>
 __device__ __forceinline__ void gemv_global(const uint4* rows, int n, int nvec, const float* x, float* out) {
@@ -541,13 +546,25 @@ __device__ __noinline__ bool att_core(const StepParams& P, int l, int h, int t0,
 #pragma unroll 1
     for (int t = tid; t < n; t += kST) {
       const uint4* kr = reinterpret_cast<const uint4*>(ks + (size_t)t * hd);
-      float dot = 0.f;
+      // four independent partial dots; the start piece rotates with t, which
+      // spreads the threads of a warp over the banks (VPH a power of 2)
+      float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
+      int jj = 0;
 #pragma unroll 1
-      for (int jj = 0; jj < VPH; ++jj) {
-        const int j = (jj + t) & (VPH - 1);  // rotate the start piece: spreads banks (VPH a power of 2)
-        dot = dot_vec(kr[j], q + j * VPT, dot, (const KV*)nullptr);
+      for (; jj + 4 <= VPH; jj += 4) {
+        const int j0 = (jj + t) & (VPH - 1), j1 = (jj + 1 + t) & (VPH - 1);
+        const int j2 = (jj + 2 + t) & (VPH - 1), j3 = (jj + 3 + t) & (VPH - 1);
+        d0 = dot_vec(kr[j0], q + j0 * VPT, d0, (const KV*)nullptr);
+        d1 = dot_vec(kr[j1], q + j1 * VPT, d1, (const KV*)nullptr);
+        d2 = dot_vec(kr[j2], q + j2 * VPT, d2, (const KV*)nullptr);
+        d3 = dot_vec(kr[j3], q + j3 * VPT, d3, (const KV*)nullptr);
       }
-      const float v = dot * scale;
+#pragma unroll 1
+      for (; jj < VPH; ++jj) {
+        const int j = (jj + t) & (VPH - 1);
+        d0 = dot_vec(kr[j], q + j * VPT, d0, (const KV*)nullptr);
+      }
+      const float v = ((d0 + d1) + (d2 + d3)) * scale;
       sc[t] = v;
       mloc = fmaxf(mloc, v);
     }
@@ -563,9 +580,19 @@ __device__ __noinline__ bool att_core(const StepParams& P, int l, int h, int t0,
     l_run = l_run * alpha + block_sum(ls, red_s);  // every thread passed a barrier after the sc writes
     m_run = mn;
     if (gi < Gp) {
-      acc *= alpha;
+      // four independent accumulation chains over this group's tokens
+      float a1 = 0.f, a2 = 0.f, a3 = 0.f, a0 = 0.f;
+      int t = gi;
 #pragma unroll 1
-      for (int t = gi; t < n; t += Gp) acc = fmaf(sc[t], Elem<KV>::to_f(vs[(size_t)t * hd + dcol]), acc);
+      for (; t + 3 * Gp < n; t += 4 * Gp) {
+        a0 = fmaf(sc[t], Elem<KV>::to_f(vs[(size_t)t * hd + dcol]), a0);
+        a1 = fmaf(sc[t + Gp], Elem<KV>::to_f(vs[(size_t)(t + Gp) * hd + dcol]), a1);
+        a2 = fmaf(sc[t + 2 * Gp], Elem<KV>::to_f(vs[(size_t)(t + 2 * Gp) * hd + dcol]), a2);
+        a3 = fmaf(sc[t + 3 * Gp], Elem<KV>::to_f(vs[(size_t)(t + 3 * Gp) * hd + dcol]), a3);
+      }
+#pragma unroll 1
+      for (; t < n; t += Gp) a0 = fmaf(sc[t], Elem<KV>::to_f(vs[(size_t)t * hd + dcol]), a0);
+      acc = fmaf(acc, alpha, (a0 + a1) + (a2 + a3));
     }
   }
   __syncthreads();
@@ -778,7 +805,7 @@ __device__ __noinline__ bool proj_phase(const StepParams& P, int l) {
     if (l + 1 < d.num_layers)
       att_issue_rows<W>(P, l + 1);
     else
-      head_issue<W>(P, 0, g.head_stages);
+      head_issue<W>(P, 0, g.head_early);  // stages clear of the expert area
   } else if (warp == kSW - 2 && l + 1 < d.num_layers) {
     att_issue_kv<KV>(P, l + 1);
   }
@@ -936,6 +963,11 @@ __device__ __noinline__ bool moe_phase(const StepParams& P, int l) {
   if constexpr (kStaged) {
     if (!bar_wait(kBarDown, ll, d.status)) return false;
   }
+  if (kStaged && 2 * nr <= kSW) {
+    // both slots' down rows (adjacent in shared memory) in one pass: rows
+    // [0, nr) dot h of slot 0, rows [nr, 2 nr) dot h of slot 1
+    gemv_smem<W>(reinterpret_cast<const uint4*>(ms + (size_t)nmat * nu * rbD), 2 * nr, nvH, hb, ab, hb + Hx, nr);
+  } else {
 #pragma unroll 1
   for (int k = 0; k < 2; ++k) {
     if constexpr (kStaged)
@@ -944,6 +976,7 @@ __device__ __noinline__ bool moe_phase(const StepParams& P, int l) {
     else
       gemv_global<W>(rowp(ly.w2, (int64_t)(k ? sel1 : sel0) * D + r0, rbH), nr, nvH, hb + (size_t)k * Hx,
                      ab + k * nr);
+  }
   }
   __syncthreads();
   if (tid < nr) {
@@ -960,7 +993,12 @@ __device__ __noinline__ bool moe_phase(const StepParams& P, int l) {
   }
   // then stage the next layer's out_proj / router / norm rows (or the final
   // norm) from a thread without an output row
-  if (tid == kST - 1) side_issue<W>(P, l + 1);
+  if (tid == kST - 1) {
+    side_issue<W>(P, l + 1);
+    // after the last layer the expert area is free: the remaining first stages
+    // of the LM-head ring
+    if (l + 1 == d.num_layers) head_issue<W>(P, g.head_early, g.head_stages - g.head_early);
+  }
   STEP_STAMP(l, 14);
   return true;
 }
@@ -968,8 +1006,8 @@ __device__ __noinline__ bool moe_phase(const StepParams& P, int l) {
 // ---------------------------------------------------------------------------
 // HEAD: x_L -> final norm -> tied LM head -> argmax + device bookkeeping.
 // The CTA's vocab rows stream through a ring of head_stages stages of
-// head_rows rows in the attention staging area; the first stages were
-// requested during the last layer's attention.
+// head_rows rows over the attention and expert staging areas; the first
+// stages were requested during the last layer.
 // ---------------------------------------------------------------------------
 template <typename W>
 __device__ __noinline__ bool head_phase(const StepParams& P) {
@@ -989,7 +1027,7 @@ __device__ __noinline__ bool head_phase(const StepParams& P) {
   if (!recv(ll + g.off_a[Lnum & 1], D, tag_of(Lnum), xs, nullptr, ll, d.status)) return false;
   STEP_STAMP(Lnum, 1);
   if (!bar_wait(kBarSide, ll, d.status)) return false;
-  const W* nw = smem_at<const W>(g.sm_moe);
+  const W* nw = smem_at<const W>(g.sm_anw);
   norm_smem<W>(xn, xs, D, d.norm, d.eps, nw, d.final_norm_b ? nw + D : nullptr);
   float best_v = -INFINITY;
   int best_i = 0x7fffffff;
@@ -1243,12 +1281,18 @@ int step_geometry(const mie_step_desc& d, int grid, StepGeom* g) {
   G.smem = (so + 127) & ~127u;
   if (G.smem > kStepMaxSmem) return MIE_ERR_UNSUPPORTED;
   // two rows per warp per stage when three such stages fit, else one
-  G.head_rows = 2 * (kStepThreads / 32);
-  if (att_bytes / ((uint32_t)G.head_rows * rbD) < 3) G.head_rows = kStepThreads / 32;
+  // LM-head ring over [sm_qw, end): the largest stage of 4, 2 or 1 rows per
+  // warp that still gives two stages; the first head_early stages lie in the
+  // attention area and can be requested before the last layer's MoE is done
+  const uint32_t ring_bytes = G.smem - G.sm_qw;
+  G.head_rows = 4 * (kStepThreads / 32);
+  while (G.head_rows > kStepThreads / 32 && ring_bytes / ((uint32_t)G.head_rows * rbD) < 2) G.head_rows /= 2;
   const uint32_t stage_bytes = (uint32_t)G.head_rows * rbD;
-  G.head_stages = (int)(att_bytes / stage_bytes);
+  G.head_stages = (int)(ring_bytes / stage_bytes);
   if (G.head_stages > kStepHeadStagesMax) G.head_stages = kStepHeadStagesMax;
   if (G.head_stages < 2) return MIE_ERR_UNSUPPORTED;
+  G.head_early = (int)(att_bytes / stage_bytes);
+  if (G.head_early > G.head_stages) G.head_early = G.head_stages;
   return MIE_OK;
 }
 
