@@ -125,35 +125,36 @@ __device__ __noinline__ bool ll_give_up(uint64_t* hdr, int32_t* status, unsigned
   return true;
 }
 
-// Receive n exchange words: dst[i] = value of buf[idx(i)] (idx(i) = i when
-// gather is null, else gather[i]) once its tag equals `tag`.  Thread t owns
-// words t, t + kST, ...; all of its pending words are polled again together,
-// so a thread sees its last word one load round trip after it landed.  Called
-// by every thread; true for all of them, or false for all when a wait gave up.
-__device__ __noinline__ bool recv(const uint64_t* buf, int n, uint32_t tag, float* dst, const int* gather,
-                                  uint64_t* hdr, int32_t* status) {
-  int bad = 0;
+// The polling part of recv, without the closing barrier: 1 when a wait gave
+// up.  With s2 set, *s2 = sum of squares of this thread's words in index
+// order (t, t + NT, ...), the order a strided loop over dst would use.  Run
+// by threads [0, NT).
+template <int NT = kST>
+__device__ __forceinline__ int recv_poll(const uint64_t* buf, int n, uint32_t tag, float* dst, const int* gather,
+                                         uint64_t* hdr, int32_t* status, float* s2) {
+  float acc = 0.f;
 #pragma unroll 1
-  for (int i0 = threadIdx.x; i0 < n && !bad; i0 += kST * 4) {
+  for (int i0 = threadIdx.x; i0 < n; i0 += NT * 4) {
     uint64_t w[4];
     int at[4];
     unsigned need = 0;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      const int i = i0 + kST * j;
+      const int i = i0 + NT * j;
       at[j] = i < n ? (gather ? gather[i] : i) : 0;
       if (i < n) {
         w[j] = ll_ld(buf + at[j]);
         need |= 1u << j;
       }
     }
+    const unsigned all = need;
     unsigned long long t0 = 0;
 #pragma unroll 1
     for (int it = 1;; ++it) {
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         if ((need >> j & 1u) && ll_tag(w[j]) == tag) {
-          dst[i0 + kST * j] = ll_val(w[j]);
+          dst[i0 + NT * j] = ll_val(w[j]);
           need &= ~(1u << j);
         }
       }
@@ -161,13 +162,29 @@ __device__ __noinline__ bool recv(const uint64_t* buf, int n, uint32_t tag, floa
 #pragma unroll
       for (int j = 0; j < 4; ++j)
         if (need >> j & 1u) w[j] = ll_ld(buf + at[j]);
-      if ((it & 63) == 0 && ll_give_up(hdr, status, &t0)) {
-        bad = 1;
-        break;
-      }
+      if ((it & 63) == 0 && ll_give_up(hdr, status, &t0)) return 1;
+    }
+    if (s2) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (all >> j & 1u) {
+          const float v = ll_val(w[j]);
+          acc = fmaf(v, v, acc);
+        }
     }
   }
-  return __syncthreads_or(bad) == 0;
+  if (s2) *s2 = acc;
+  return 0;
+}
+
+// Receive n exchange words: dst[i] = value of buf[idx(i)] (idx(i) = i when
+// gather is null, else gather[i]) once its tag equals `tag`.  Thread t owns
+// words t, t + kST, ...; all of its pending words are polled again together,
+// so a thread sees its last word one load round trip after it landed.  Called
+// by every thread; true for all of them, or false for all when a wait gave up.
+__device__ __noinline__ bool recv(const uint64_t* buf, int n, uint32_t tag, float* dst, const int* gather,
+                                  uint64_t* hdr, int32_t* status) {
+  return __syncthreads_or(recv_poll(buf, n, tag, dst, gather, hdr, status, nullptr)) == 0;
 }
 
 // ---------------------------------------------------------------------------
@@ -202,8 +219,6 @@ struct StepCtx {
   uint32_t step;  // this step's number (tags)
   int64_t tok;    // input token
   int64_t slot;   // cache offset (elements) of the new token's slot, head 0
-  int sel[2];     // selected experts of the current layer
-  float wts[2];   // their gate weights
   float m, l;     // attention: running max and normaliser of this split
   int last;       // this CTA finished the LM head last
   int blk0;       // first cache block of this CTA's old tokens (blk_s[0])
@@ -256,6 +271,40 @@ __device__ __noinline__ bool bar_wait(int b, uint64_t* hdr, int32_t* status) {
   const int bad = __syncthreads_or(!ok);
   if (threadIdx.x == 0) bar_done_s[b] += 1;
   return !bad;
+}
+// PROJ runs on threads [0, kProjThreads): the last two warps issue the next
+// layer's bulk copies meanwhile, which can take microseconds when the copy
+// engine is busy, and join at the phase's closing barrier.
+constexpr int kProjThreads = kST - 64;
+// Threads [0, kProjThreads): receive n exchange words into dst and wait
+// (bounded) for the copies of barrier b; one named barrier (id 1) over those
+// threads closes both.  True for all of them, or false for all when a wait
+// gave up.
+__device__ __noinline__ bool recv_part(const uint64_t* buf, int n, uint32_t tag, float* dst, int b, uint64_t* hdr,
+                                       int32_t* status) {
+  int bad = recv_poll<kProjThreads>(buf, n, tag, dst, nullptr, hdr, status, nullptr);
+  bool waited = false;
+  if (!bad) {
+    waited = mbar_wait(&bars_s[b], bar_done_s[b] & 1u, status);
+    if (!waited) {
+      atomicExch(reinterpret_cast<unsigned long long*>(hdr + kHdrAbort), 1ull);
+      bad = 1;
+    }
+  }
+  uint32_t any;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 q, %1, 0;\n\tbarrier.red.or.pred p, 1, %2, q;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(any)
+      : "r"(bad), "n"(kProjThreads)
+      : "memory");
+  if (any) return false;
+  if (waited && threadIdx.x == 0) bar_done_s[b] += 1;
+  return true;
+}
+// Barrier over threads [0, kProjThreads) (named barrier 1).
+__device__ __forceinline__ void bar_sync_part() {
+  asm volatile("bar.sync 1, %0;" ::"n"(kProjThreads) : "memory");
 }
 // Before leaving early: wait (bounded) for every armed copy not waited for,
 // so no bulk copy lands in shared memory after the CTA left.
@@ -326,30 +375,41 @@ __device__ __forceinline__ void norm_copy(void* dst, const void* w, const void* 
   if (b) bulk_copy(static_cast<uint8_t*>(dst) + rb, b, rb, bar);
 }
 
-// Stage layer l's attention weights (lane 0 of the calling warp): the
-// attention norm weights; for attention CTAs also q rows [0, q_stage) of the
-// head and this CTA's k / v rows (k pair first halves, second halves, v rows).
+// Stage layer l's attention weights (whole calling warp: lane 0 arms the
+// barrier, lanes 0-4 issue one copy each): the attention norm weights; for
+// attention CTAs also q rows [0, q_stage) of the head and this CTA's k / v
+// rows (k pair first halves, second halves, v rows).
 template <typename W>
 __device__ __noinline__ void att_issue_rows(const StepParams& P, int l) {
   const mie_step_desc& d = P.d;
   const StepGeom& g = P.g;
   const mie_layer_desc& ly = P.layers[l];
+  const int lane = threadIdx.x & 31;
   const int hd = d.head_dim, half = hd / 2, D = d.hidden_dim;
   const AttSplit a = att_split(g, hd, cx_s.pos);
   const uint32_t rb = (uint32_t)(D * sizeof(W));
-  fence_proxy_async_smem();  // earlier generic reads of these buffers before the async writes
-  const uint32_t nrows = a.att ? (uint32_t)(g.q_stage + 2 * a.nkp + a.nvd) : 0u;
-  bar_arm(kBarAtt, nrows * rb + (ly.attn_norm_b ? 2 : 1) * rb);
-  norm_copy(smem_at<uint8_t>(g.sm_anw), ly.attn_norm_w, ly.attn_norm_b, rb, kBarAtt);
-  if (!a.att) return;
+  if (lane == 0) {
+    fence_proxy_async_smem();  // earlier generic reads of these buffers before the async writes
+    const uint32_t nrows = a.att ? (uint32_t)(g.q_stage + 2 * a.nkp + a.nvd) : 0u;
+    bar_arm(kBarAtt, nrows * rb + (ly.attn_norm_b ? 2 : 1) * rb);
+  }
+  __syncwarp();
+  // one copy per lane: norm weights, q rows, k (both RoPE halves), v
+  if (lane > 4 || (lane > 0 && !a.att)) return;
+  fence_proxy_async_smem();
   const uint8_t* w = static_cast<const uint8_t*>(ly.qkv_w);
-  uint8_t* qs = smem_at<uint8_t>(g.sm_qw);
   uint8_t* ks = smem_at<uint8_t>(g.sm_kvw);
-  bulk_copy(qs, w + (size_t)a.h * hd * rb, g.q_stage * rb, kBarAtt);
   const size_t kbase = (size_t)(D + a.h * hd + a.p0) * rb, vbase = (size_t)(2 * D + a.h * hd + a.v0) * rb;
-  bulk_copy(ks, w + kbase, a.nkp * rb, kBarAtt);
-  bulk_copy(ks + (size_t)a.nkp * rb, w + kbase + (size_t)half * rb, a.nkp * rb, kBarAtt);
-  bulk_copy(ks + (size_t)2 * a.nkp * rb, w + vbase, a.nvd * rb, kBarAtt);
+  if (lane == 0)
+    norm_copy(smem_at<uint8_t>(g.sm_anw), ly.attn_norm_w, ly.attn_norm_b, rb, kBarAtt);
+  else if (lane == 1)
+    bulk_copy(smem_at<uint8_t>(g.sm_qw), w + (size_t)a.h * hd * rb, g.q_stage * rb, kBarAtt);
+  else if (lane == 2)
+    bulk_copy(ks, w + kbase, a.nkp * rb, kBarAtt);
+  else if (lane == 3)
+    bulk_copy(ks + (size_t)a.nkp * rb, w + kbase + (size_t)half * rb, a.nkp * rb, kBarAtt);
+  else
+    bulk_copy(ks + (size_t)2 * a.nkp * rb, w + vbase, a.nvd * rb, kBarAtt);
 }
 
 // Stage the first K/V chunk of this CTA's old tokens of layer l (whole warp).
@@ -414,7 +474,7 @@ __device__ __noinline__ void head_issue(const StepParams& P, int first, int coun
 // Compute routines (shared by all phases)
 // ---------------------------------------------------------------------------
 // out = norm(in) with weight w (and bias b, LayerNorm) staged in shared memory
-// as W; in, out in shared memory (may alias).  Ends with a barrier.
+// as W; in, out fp32 vectors in shared memory (may alias).  Ends with a barrier.
 template <typename W>
 __device__ __noinline__ void norm_smem(float* out, const float* in, int D, int norm, float eps, const W* w,
                                        const W* b) {
@@ -452,57 +512,108 @@ __device__ __noinline__ void norm_smem(float* out, const float* in, int D, int n
   __syncthreads();
 }
 
+// dst = the D words of exchange buffer buf (tag `tag`), out = norm(dst) with
+// weight w (bias b) in shared memory; with bar >= 0 the bulk copies of
+// barrier bar (the weights) are waited for as well.  RMSNorm folds the sum of
+// squares into the receive: one barrier covers the receive, the copy wait and
+// the cross-warp partials, a second one the output.  Same arithmetic, in the
+// same order, as recv + bar_wait + norm_smem (the path other norms take).
+template <typename W>
+__device__ __noinline__ bool recv_norm(const uint64_t* buf, int D, uint32_t tag, float* dst, float* out, int bar,
+                                       int norm, float eps, const W* w, const W* b, uint64_t* hdr,
+                                       int32_t* status) {
+  if (norm != MIE_NORM_RMS) {
+    if (!recv(buf, D, tag, dst, nullptr, hdr, status)) return false;
+    if (bar >= 0 && !bar_wait(bar, hdr, status)) return false;
+    norm_smem<W>(out, dst, D, norm, eps, w, b);
+    return true;
+  }
+  float s2;
+  int bad = recv_poll(buf, D, tag, dst, nullptr, hdr, status, &s2);
+  s2 = warp_sum(s2);
+  if ((threadIdx.x & 31) == 0) red_s[threadIdx.x >> 5] = s2;  // last read of red_s: behind a barrier
+  bool waited = false;
+  if (bar >= 0 && !bad) {
+    waited = mbar_wait(&bars_s[bar], bar_done_s[bar] & 1u, status);
+    if (!waited) {
+      atomicExch(reinterpret_cast<unsigned long long*>(hdr + kHdrAbort), 1ull);
+      bad = 1;
+    }
+  }
+  if (__syncthreads_or(bad)) return false;
+  if (waited && threadIdx.x == 0) bar_done_s[bar] += 1;
+  float t = 0.f;
+#pragma unroll
+  for (int i = 0; i < kSW; ++i) t += red_s[i];
+  const float rs = rsqrtf(t / (float)D + eps);
+#pragma unroll 1
+  for (int i = threadIdx.x; i < D; i += kST) out[i] = (dst[i] * rs) * Elem<W>::to_f(w[i]);
+  __syncthreads();
+  return true;
+}
+
+// Rows w, w + kSW, ... of warp w, R rows per iteration (one partial sum per
+// 16-byte vector and row; the R shuffle reductions interleave).
+template <typename W, bool kGlobal, int R>
+__device__ __forceinline__ void gemv_rows(const uint4* rows, int n, int nvec, const float* xr, float* out) {
+  constexpr int PV = Elem<W>::kPerVec, NV = Seg<W>::kNV;
+  const int lane = threadIdx.x & 31;
+  const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll 1
+  for (int r = threadIdx.x >> 5; r < n; r += R * kSW) {
+    uint4 w[R][NV];
+#pragma unroll
+    for (int k = 0; k < R; ++k) {
+      const int rk = r + k * kSW < n ? r + k * kSW : r;
+      const uint4* rp = rows + (size_t)rk * nvec;
+#pragma unroll
+      for (int j = 0; j < NV; ++j) {
+        const int v = lane + kWarp * j;
+        if constexpr (kGlobal)
+          w[k][j] = v < nvec ? __ldg(rp + v) : z;
+        else
+          w[k][j] = v < nvec ? rp[v] : z;
+      }
+    }
+    float sum[R];
+#pragma unroll
+    for (int k = 0; k < R; ++k) {
+      sum[k] = 0.f;
+#pragma unroll
+      for (int j = 0; j < NV; ++j) sum[k] += dot_vec(w[k][j], xr + j * PV, 0.f, (const W*)nullptr);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+      for (int k = 0; k < R; ++k) sum[k] += __shfl_xor_sync(0xffffffffu, sum[k], o);
+    }
+    if (lane == 0) {
+#pragma unroll
+      for (int k = 0; k < R; ++k)
+        if (r + k * kSW < n) out[r + k * kSW] = sum[k];
+    }
+  }
+}
+
+// ---- fp32 rows: CUDA-core GEMV ----
 // out[r] = rows[r] . x for r < n: rows of nvec 16-byte vectors (row stride
 // nvec) in shared memory (kGlobal false) or global memory, x an fp32 vector
-// in shared memory.  Warp w forms rows w, w + kSW, ...: two rows per
-// iteration and one partial sum per 16-byte vector, so the FMA chains and the
-// two shuffle reductions are independent of each other.  No barrier.
+// in shared memory (rows [split, n) dot x1 when x1 is set, n <= kSW).  Warp w
+// forms rows w, w + kSW, ...: two rows per iteration and one partial sum per
+// 16-byte vector, so the FMA chains and the two shuffle reductions are
+// independent of each other.  No barrier.
 template <typename W, bool kGlobal>
 __device__ __noinline__ void gemv(const uint4* rows, int n, int nvec, const float* x, float* out,
                                   const float* x1 = nullptr, int split = 0) {
   constexpr int PV = Elem<W>::kPerVec;
-  const int lane = threadIdx.x & 31;
   if ((threadIdx.x >> 5) >= n) return;  // no rows for this warp
   // rows [split, n) dot x1 instead of x (n <= kSW: one row per warp)
   const float* xb = (x1 && (int)(threadIdx.x >> 5) >= split) ? x1 : x;
   float xr[Seg<W>::kNV * PV];
   load_x_regs<W>(xr, xb, nvec);
-#pragma unroll 1
-  for (int r = threadIdx.x >> 5; r < n; r += 2 * kSW) {
-    const int r2 = r + kSW;
-    const bool two = r2 < n;
-    const uint4* ra = rows + (size_t)r * nvec;
-    const uint4* rb = rows + (size_t)(two ? r2 : r) * nvec;
-    uint4 wa[Seg<W>::kNV], wb[Seg<W>::kNV];
-#pragma unroll
-    for (int j = 0; j < Seg<W>::kNV; ++j) {
-      const int v = lane + kWarp * j;
-      const uint4 z = make_uint4(0u, 0u, 0u, 0u);
-      if constexpr (kGlobal) {
-        wa[j] = v < nvec ? __ldg(ra + v) : z;
-        wb[j] = v < nvec ? __ldg(rb + v) : z;
-      } else {
-        wa[j] = v < nvec ? ra[v] : z;
-        wb[j] = v < nvec ? rb[v] : z;
-      }
-    }
-    float sa = 0.f, sb = 0.f;
-#pragma unroll
-    for (int j = 0; j < Seg<W>::kNV; ++j) {
-      sa += dot_vec(wa[j], xr + j * PV, 0.f, (const W*)nullptr);
-      sb += dot_vec(wb[j], xr + j * PV, 0.f, (const W*)nullptr);
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      sa += __shfl_xor_sync(0xffffffffu, sa, o);
-      sb += __shfl_xor_sync(0xffffffffu, sb, o);
-    }
-    if (lane == 0) {
-      out[r] = sa;
-      if (two) out[r2] = sb;
-    }
-  }
+  gemv_rows<W, kGlobal, 2>(rows, n, nvec, xr, out);
 }
+
 template <typename W>
 __device__ __forceinline__ void gemv_smem(const uint4* rows, int n, int nvec, const float* x, float* out,
                                           const float* x1 = nullptr, int split = 0) {
@@ -626,6 +737,7 @@ __device__ __noinline__ bool att_phase(const StepParams& P, int l) {
   STEP_STAMP(l, 0);
 
   // ---- x: token embedding (layer 0) or exchange A; norm ----
+  const W* nw = smem_at<const W>(g.sm_anw);
   if (l == 0) {
     const int64_t tok = cx_s.tok;
 #pragma unroll 1
@@ -634,13 +746,12 @@ __device__ __noinline__ bool att_phase(const StepParams& P, int l) {
       if (d.pos_embedding) v += ldw<W>(d.pos_embedding, (int64_t)pos * D + i);
       xs[i] = v;
     }
-  } else if (!recv(ll + g.off_a[par], D, tag, xs, nullptr, ll, d.status)) {
+    if (!bar_wait(kBarAtt, ll, d.status)) return false;
+    norm_smem<W>(xn, xs, D, d.norm, d.eps, nw, ly.attn_norm_b ? nw + D : nullptr);
+  } else if (!recv_norm<W>(ll + g.off_a[par], D, tag, xs, xn, kBarAtt, d.norm, d.eps, nw,
+                           ly.attn_norm_b ? nw + D : nullptr, ll, d.status)) {
     return false;
   }
-  STEP_STAMP(l, 1);
-  if (!bar_wait(kBarAtt, ll, d.status)) return false;
-  const W* nw = smem_at<const W>(g.sm_anw);
-  norm_smem<W>(xn, xs, D, d.norm, d.eps, nw, ly.attn_norm_b ? nw + D : nullptr);
   STEP_STAMP(l, 2);
   if (!a.att) return true;
 
@@ -650,9 +761,10 @@ __device__ __noinline__ bool att_phase(const StepParams& P, int l) {
     gemv_smem<W>(smem_at<const uint4>(g.sm_qw), hd + nkv, nvD, xn, qk);  // q and k / v rows are adjacent
   } else {
     gemv_smem<W>(smem_at<const uint4>(g.sm_qw), g.q_stage, nvD, xn, qk);
-    if (g.q_stage < hd)
-      gemv_global<W>(rowp(ly.qkv_w, (int64_t)a.h * hd + g.q_stage, (int64_t)nvD * 16), hd - g.q_stage, nvD, xn,
-                     qk + g.q_stage);
+    if constexpr (sizeof(W) == 4)  // bf16: every q row is staged (checked on the host)
+      if (g.q_stage < hd)
+        gemv_global<W>(rowp(ly.qkv_w, (int64_t)a.h * hd + g.q_stage, (int64_t)nvD * 16), hd - g.q_stage, nvD, xn,
+                       qk + g.q_stage);
     gemv_smem<W>(smem_at<const uint4>(g.sm_kvw), nkv, nvD, xn, qk + hd);
   }
   __syncthreads();
@@ -748,31 +860,35 @@ __device__ __noinline__ bool att_phase(const StepParams& P, int l) {
   STEP_STAMP(l, 7);
   if (tid < 32) {
     // warp 0: split weights w_k = e^(m_k - M) with the new token as one more
-    // term (score q.k_new, value v_new); lane k holds splits k, k + 32, ...
+    // term (score q.k_new, value v_new), M the largest score; lane k forms
+    // w_k of splits k, k + 32, ... (S broadcast reads for M), then lane d < nvd
+    // the output of dim v0 + d, summing the splits in order
     float sp = 0.f, mx = -INFINITY;
-#pragma unroll 1
-    for (int k = tid; k < S; k += 32) {
+#pragma unroll 4
+    for (int k = 0; k < S; ++k) {
       sp += ab[3 * k + 2];
       mx = fmaxf(mx, ab[3 * k]);
     }
-    const float snew = warp_sum(sp) * d.attn_scale;
-    const float M = fmaxf(warp_max(mx), snew);
-    float lw = 0.f;
+    const float snew = sp * d.attn_scale;
+    const float M = fmaxf(mx, snew);
+    float* wk = smem_at<float>(g.sm_sc);  // scores scratch, free after the attention core
 #pragma unroll 1
     for (int k = tid; k < S; k += 32) {
       const float mk = ab[3 * k];
-      const float wk = mk == -INFINITY ? 0.f : expf(mk - M);
-      gat_s[k] = __float_as_int(wk);
-      lw = fmaf(ab[3 * k + 1], wk, lw);
+      wk[k] = mk == -INFINITY ? 0.f : expf(mk - M);
     }
-    const float wn = expf(snew - M);
-    const float den = warp_sum(lw) + wn;
     __syncwarp();
     if (tid < nvd) {
-      float num = wn * kv[2 * a.nkp + tid];
-#pragma unroll 1
-      for (int k = 0; k < S; ++k) num = fmaf(ab[nm + k * nvd + tid], __int_as_float(gat_s[k]), num);
-      ll_put(ll + g.off_c[par] + (int64_t)a.h * hd + a.v0 + tid, num / den, tag);
+      const float wn = expf(snew - M);
+      float den = 0.f, num = 0.f;
+#pragma unroll 4
+      for (int k = 0; k < S; ++k) {
+        const float w = wk[k];
+        den = fmaf(ab[3 * k + 1], w, den);
+        num = fmaf(ab[nm + k * nvd + tid], w, num);
+      }
+      num = fmaf(wn, kv[2 * a.nkp + tid], num);
+      ll_put(ll + g.off_c[par] + (int64_t)a.h * hd + a.v0 + tid, num / (den + wn), tag);
     }
   }
   STEP_STAMP(l, 15);
@@ -801,21 +917,27 @@ __device__ __noinline__ bool proj_phase(const StepParams& P, int l) {
   // first LM-head rows after the last layer.
   const int warp = tid >> 5;
   STEP_STAMP_T(l, 16, kST - 32);
-  if (warp == kSW - 1 && (tid & 31) == 0) {
-    if (l + 1 < d.num_layers)
-      att_issue_rows<W>(P, l + 1);
-    else
-      head_issue<W>(P, 0, g.head_early);  // stages clear of the expert area
-  } else if (warp == kSW - 2 && l + 1 < d.num_layers) {
-    att_issue_kv<KV>(P, l + 1);
+  if (tid >= kProjThreads) {
+    // the last two warps: copy issue only; they meet the others at the next
+    // phase's first barrier
+    if (warp == kSW - 1) {
+      if (l + 1 < d.num_layers)
+        att_issue_rows<W>(P, l + 1);
+      else if ((tid & 31) == 0)
+        head_issue<W>(P, 0, g.head_early);  // stages clear of the expert area
+    } else if (l + 1 < d.num_layers) {
+      att_issue_kv<KV>(P, l + 1);
+    }
+    STEP_STAMP_T(l, 17, kST - 32);
+    return true;
   }
-  STEP_STAMP_T(l, 17, kST - 32);
   STEP_STAMP(l, 18);
-  if (!recv(ll + g.off_c[l & 1], D, tag, ob, nullptr, ll, d.status)) return false;
+  // a failed wait raised the abort word: the next receive then fails for
+  // every thread of every CTA, so no barrier is needed to agree here
+  if (!recv_part(ll + g.off_c[l & 1], D, tag, ob, kBarSide, ll, d.status)) return true;
   STEP_STAMP(l, 8);
-  if (!bar_wait(kBarSide, ll, d.status)) return false;
-  gemv_smem<W>(smem_at<const uint4>(g.sm_moe), nr, nvD, ob, ab);
-  __syncthreads();
+  gemv_smem<W>(smem_at<const uint4>(g.sm_moe), nr, nvD, ob, ab);  // nr <= 14 rows: warps < 14
+  bar_sync_part();
   if (tid < nr) {
     const int r = r0 + tid;
     float y = ab[tid];
@@ -857,58 +979,45 @@ __device__ __noinline__ bool moe_phase(const StepParams& P, int l) {
   split32(D, blockIdx.x, gridDim.x, &r0, &r1);       // output rows
   const int nu = u1 - u0, nr = r1 - r0;
 
-  if (!recv(ll + g.off_d[par], D, tag, xm, nullptr, ll, d.status)) return false;
-  STEP_STAMP(l, 10);
   const W* nw = reinterpret_cast<const W*>(ms + (size_t)(g.nr_max + E) * rbD);
-  norm_smem<W>(xn, xm, D, d.norm, d.eps, nw, ly.moe_norm_b ? nw + D : nullptr);
+  if (!recv_norm<W>(ll + g.off_d[par], D, tag, xm, xn, -1, d.norm, d.eps, nw, ly.moe_norm_b ? nw + D : nullptr, ll,
+                    d.status))
+    return false;
+  STEP_STAMP(l, 10);
   gemv_smem<W>(reinterpret_cast<const uint4*>(ms + (size_t)g.nr_max * rbD), E, nvD, xn, ab);
   __syncthreads();
-  if (tid < 32) {
-    // top-2 over the router logits in warp 0 (lane e holds expert e):
-    // largest logit, ties to the lower id -- the same choice as a repeated
-    // argmax scanning ascending ids with a strict '>'
-    const float v = tid < E ? ab[tid] : -INFINITY;
-    float bv = v;
-    int bi = tid < E ? tid : 0x7fffffff;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-      if (better(ov, oi, bv, bi)) {
-        bv = ov;
-        bi = oi;
-      }
+  // top-2 over the router logits, by every thread (E broadcast reads, no
+  // exchange): largest logit, ties to the lower id -- a repeated argmax
+  // scanning ascending ids with a strict '>' -- and the softmax of the pair
+  int sel0 = 0;
+  float bv = ab[0];
+#pragma unroll 1
+  for (int e = 1; e < E; ++e)
+    if (ab[e] > bv) {
+      bv = ab[e];
+      sel0 = e;
     }
-    const int i0 = bi;
-    float cv = (tid < E && tid != i0) ? v : -INFINITY;
-    int ci = (tid < E && tid != i0) ? tid : 0x7fffffff;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, cv, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, ci, o);
-      if (better(ov, oi, cv, ci)) {
-        cv = ov;
-        ci = oi;
-      }
+  int sel1 = sel0 == 0 ? 1 : 0;
+  float cv = ab[sel1];
+#pragma unroll 1
+  for (int e = sel1 + 1; e < E; ++e)
+    if (e != sel0 && ab[e] > cv) {
+      cv = ab[e];
+      sel1 = e;
     }
-    const int i1 = ci;
+  const float e1 = expf(cv - bv);
+  const float wt0 = 1.0f / (1.0f + e1), wt1 = e1 / (1.0f + e1);
+  if constexpr (kStaged) {
+    // the selected experts' rows of this CTA -> shared memory (over the
+    // out_proj / router / norm rows, all read by now): gate rows of units
+    // [u0, u1), up rows (SwiGLU), down rows (slot 0 then slot 1); thread c of
+    // warp 0 issues copy c after thread 0 armed the barriers
     if (tid == 0) {
-      const float e1 = expf(cv - bv);
-      cx_s.sel[0] = i0;
-      cx_s.sel[1] = i1;
-      cx_s.wts[0] = 1.0f / (1.0f + e1);
-      cx_s.wts[1] = e1 / (1.0f + e1);
+      fence_proxy_async_smem();
+      bar_arm(kBarMoe, (uint32_t)(nmat * nu * rbD));  // up rows
+      bar_arm(kBarDown, (uint32_t)(2 * nr * rbH));    // down rows, needed after exchange E
     }
-    if constexpr (kStaged) {
-      // the selected experts' rows of this CTA -> shared memory (over the
-      // out_proj / router / norm rows, all read by now): gate rows of units
-      // [u0, u1), up rows (SwiGLU), down rows (slot 0 then slot 1); lane c
-      // issues copy c
-      if (tid == 0) {
-        fence_proxy_async_smem();
-        bar_arm(kBarMoe, (uint32_t)(nmat * nu * rbD));  // up rows
-        bar_arm(kBarDown, (uint32_t)(2 * nr * rbH));    // down rows, needed after exchange E
-      }
+    if (tid < 32) {
       __syncwarp();
       if (tid < 2 * nmat) {
         const int m = tid >> 1, k = tid & 1;
@@ -916,20 +1025,18 @@ __device__ __noinline__ bool moe_phase(const StepParams& P, int l) {
         const int ua = max(u0, k * Hx), ub = min(u1, (k + 1) * Hx);
         fence_proxy_async_smem();
         if (ub > ua)
-          bulk_copy(ms + (size_t)(m * nu + ua - u0) * rbD, w + ((size_t)(k ? i1 : i0) * Hx + ua - k * Hx) * rbD,
+          bulk_copy(ms + (size_t)(m * nu + ua - u0) * rbD, w + ((size_t)(k ? sel1 : sel0) * Hx + ua - k * Hx) * rbD,
                     (uint32_t)((ub - ua) * rbD), kBarMoe);
       } else if (tid >= 8 && tid < 10) {
         const int k = tid - 8;
         fence_proxy_async_smem();
         bulk_copy(ms + (size_t)nmat * nu * rbD + (size_t)k * nr * rbH,
-                  static_cast<const uint8_t*>(ly.w2) + ((size_t)(k ? i1 : i0) * D + r0) * rbH, (uint32_t)(nr * rbH),
-                  kBarDown);
+                  static_cast<const uint8_t*>(ly.w2) + ((size_t)(k ? sel1 : sel0) * D + r0) * rbH,
+                  (uint32_t)(nr * rbH), kBarDown);
       }
     }
   }
-  __syncthreads();
   STEP_STAMP(l, 11);
-  const int sel0 = cx_s.sel[0], sel1 = cx_s.sel[1];
   // up units: gate (and up) rows -> ab[0, nmat * nu)
   if constexpr (kStaged) {
     if (!bar_wait(kBarMoe, ll, d.status)) return false;
@@ -960,8 +1067,13 @@ __device__ __noinline__ bool moe_phase(const StepParams& P, int l) {
   // ---- DOWN ----
   if (!recv(ll + g.off_e[par], 2 * Hx, tag, hb, nullptr, ll, d.status)) return false;
   STEP_STAMP(l, 13);
+  // the next layer's out_proj / router / norm rows go over the consumed up
+  // rows while the down GEMV runs (warps < 2 nr), issued by the last thread,
+  // when they fit there; else after the down GEMV
+  const bool side_now = kStaged && l + 1 < d.num_layers && g.nr_max + E + 2 <= nmat * nu && 2 * nr < kSW;
   if constexpr (kStaged) {
     if (!bar_wait(kBarDown, ll, d.status)) return false;
+    if (side_now && tid == kST - 1) side_issue<W>(P, l + 1);
   }
   if (kStaged && 2 * nr <= kSW) {
     // both slots' down rows (adjacent in shared memory) in one pass: rows
@@ -969,14 +1081,14 @@ __device__ __noinline__ bool moe_phase(const StepParams& P, int l) {
     gemv_smem<W>(reinterpret_cast<const uint4*>(ms + (size_t)nmat * nu * rbD), 2 * nr, nvH, hb, ab, hb + Hx, nr);
   } else {
 #pragma unroll 1
-  for (int k = 0; k < 2; ++k) {
-    if constexpr (kStaged)
-      gemv_smem<W>(reinterpret_cast<const uint4*>(ms + (size_t)nmat * nu * rbD + (size_t)k * nr * rbH), nr, nvH,
-                   hb + (size_t)k * Hx, ab + k * nr);
-    else
-      gemv_global<W>(rowp(ly.w2, (int64_t)(k ? sel1 : sel0) * D + r0, rbH), nr, nvH, hb + (size_t)k * Hx,
-                     ab + k * nr);
-  }
+    for (int k = 0; k < 2; ++k) {
+      if constexpr (kStaged)
+        gemv_smem<W>(reinterpret_cast<const uint4*>(ms + (size_t)nmat * nu * rbD + (size_t)k * nr * rbH), nr, nvH,
+                     hb + (size_t)k * Hx, ab + k * nr);
+      else
+        gemv_global<W>(rowp(ly.w2, (int64_t)(k ? sel1 : sel0) * D + r0, rbH), nr, nvH, hb + (size_t)k * Hx,
+                       ab + k * nr);
+    }
   }
   __syncthreads();
   if (tid < nr) {
@@ -986,14 +1098,14 @@ __device__ __noinline__ bool moe_phase(const StepParams& P, int l) {
     for (int k = 0; k < 2; ++k) {
       float v = ab[k * nr + tid];
       if (ly.b2) v += ldw<W>(ly.b2, (int64_t)(k ? sel1 : sel0) * D + r);
-      y = fmaf(cx_s.wts[k], v, y);
+      y = fmaf(k ? wt1 : wt0, v, y);
     }
     ll_put(ll + g.off_a[(l + 1) & 1] + r, y, tag_of(l + 1));
     if (l == d.num_layers - 1) d.x[r] = y;
   }
-  // then stage the next layer's out_proj / router / norm rows (or the final
-  // norm) from a thread without an output row
-  if (tid == kST - 1) {
+  // else stage the next layer's out_proj / router / norm rows (or the final
+  // norm) now, from a thread without an output row
+  if (tid == kST - 1 && !side_now) {
     side_issue<W>(P, l + 1);
     // after the last layer the expert area is free: the remaining first stages
     // of the LM-head ring
@@ -1024,11 +1136,11 @@ __device__ __noinline__ bool head_phase(const StepParams& P) {
   int v0h, v1h;
   split32(V, c, G, &v0h, &v1h);
   const int nst = (v1h - v0h + g.head_rows - 1) / g.head_rows;
-  if (!recv(ll + g.off_a[Lnum & 1], D, tag_of(Lnum), xs, nullptr, ll, d.status)) return false;
-  STEP_STAMP(Lnum, 1);
-  if (!bar_wait(kBarSide, ll, d.status)) return false;
   const W* nw = smem_at<const W>(g.sm_anw);
-  norm_smem<W>(xn, xs, D, d.norm, d.eps, nw, d.final_norm_b ? nw + D : nullptr);
+  if (!recv_norm<W>(ll + g.off_a[Lnum & 1], D, tag_of(Lnum), xs, xn, kBarSide, d.norm, d.eps, nw,
+                    d.final_norm_b ? nw + D : nullptr, ll, d.status))
+    return false;
+  STEP_STAMP(Lnum, 1);
   float best_v = -INFINITY;
   int best_i = 0x7fffffff;
 #pragma unroll 1
@@ -1169,7 +1281,7 @@ __global__ void __launch_bounds__(kST, 1) step_kernel(const __grid_constant__ St
       blk_s[threadIdx.x] = __ldcg(d.block_table + b0 + threadIdx.x);
     __syncthreads();
   }
-  if (threadIdx.x == 0) att_issue_rows<W>(P, 0);
+  if (threadIdx.x < 32) att_issue_rows<W>(P, 0);
   if (threadIdx.x >= 32 && threadIdx.x < 64) att_issue_kv<KV>(P, 0);
   if (threadIdx.x == 64) side_issue<W>(P, 0);
   bool ok = true;
@@ -1238,6 +1350,8 @@ int step_geometry(const mie_step_desc& d, int grid, StepGeom* g) {
   if (merge_words > kStepThreads || 2 * G.nr_max > kStepThreads || nmat * nu_max > kStepThreads ||
       kvw_max > 128 || hd > 128)
     return MIE_ERR_UNSUPPORTED;
+  // out_proj rows of a CTA: one per warp of the PROJ threads
+  if (G.nr_max > kProjThreads / 32) return MIE_ERR_UNSUPPORTED;
   // shared memory: vectors, then the staging areas
   const uint32_t rbD = (uint32_t)(D * esz), rbH = (uint32_t)(Hx * esz);
   uint32_t so = 0;
@@ -1258,6 +1372,7 @@ int step_geometry(const mie_step_desc& d, int grid, StepGeom* g) {
   G.sm_acc = stake(4 * abw);
   G.chunk_tok = (int)(kStepKvChunkBytes / (2 * hd * kvsz));
   G.sm_sc = stake(4 * G.chunk_tok);
+  if (G.S > G.chunk_tok) return MIE_ERR_UNSUPPORTED;  // the merge's split weights live in the scores scratch
   G.sm_anw = stake(2 * rbD);
   const uint32_t base = (so + 127) & ~127u;
   const uint32_t chunk_bytes = (uint32_t)(2 * G.chunk_tok * hd * kvsz);
