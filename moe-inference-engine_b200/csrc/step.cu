@@ -891,6 +891,9 @@ __device__ __noinline__ bool att_phase(const StepParams& P, int l) {
       ll_put(ll + g.off_c[par] + (int64_t)a.h * hd + a.v0 + tid, num / (den + wn), tag);
     }
   }
+  // the PROJ threads start polling o only after this CTA's merge: polls
+  // issued early only load the lines the producers are about to write
+  if (tid < kProjThreads) bar_sync_part();
   STEP_STAMP(l, 15);
   return true;
 }
