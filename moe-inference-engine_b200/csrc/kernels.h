@@ -42,7 +42,7 @@ constexpr int kStepThreads = 512;                   // one CTA of 16 warps per S
 constexpr int kMaxStepLayers = 48;                  // layer descriptors carried in the launch parameters
 constexpr uint32_t kStepKvChunkBytes = 32 * 1024;   // K+V of one split staged in shared memory at a time
 constexpr int kStepHeadStagesMax = 8;               // LM-head ring stages
-constexpr uint32_t kStepMaxSmem = 224 * 1024;       // dynamic shared memory of the step kernel (static: < 3 KB)
+constexpr uint32_t kStepMaxSmem = 223 * 1024;       // dynamic shared memory of the step kernel (static: < 4 KB)
 
 // Geometry of one persistent step launch: exchange-buffer offsets (64-bit
 // words into the caller's scratch) and the shared-memory layout (bytes).

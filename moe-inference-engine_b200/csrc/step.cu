@@ -225,6 +225,27 @@ struct StepCtx {
 };
 constexpr int kStepBlkCache = 64;  // block ids of a split cached per step
 __shared__ StepCtx cx_s;
+// The launch parameters the phases read, copied to shared memory at the
+// start (a read of a kernel parameter through a reference costs ~250 cycles,
+// a shared-memory read ~30): the step descriptor, the geometry and a window
+// of kLayerSlots layer descriptors -- layer l in slot l % kLayerSlots; the
+// descriptor of layer l + 2 is copied during layer l.
+struct StepShared {
+  mie_step_desc d;
+  StepGeom g;
+};
+constexpr int kLayerSlots = 4;
+__shared__ StepShared ps_s;
+__shared__ mie_layer_desc lay_s[kLayerSlots];
+__device__ __forceinline__ const mie_layer_desc& layer_at(int l) { return lay_s[l & (kLayerSlots - 1)]; }
+// Copy layer l's descriptor into its slot (threads [first, first + 16)).
+__device__ __forceinline__ void layer_fetch(const StepParams& P, int l, int first) {
+  constexpr int kWords = (int)(sizeof(mie_layer_desc) / 8);
+  const int i = (int)threadIdx.x - first;
+  if (i >= 0 && i < kWords)
+    reinterpret_cast<uint64_t*>(&lay_s[l & (kLayerSlots - 1)])[i] =
+        reinterpret_cast<const uint64_t*>(&P.layers[l])[i];
+}
 __shared__ float red_s[kSW];
 __shared__ int gat_s[kST];  // merge: exchange word index of each received value
 __shared__ int blk_s[kStepBlkCache];  // physical block ids of this CTA's old tokens
@@ -381,9 +402,9 @@ __device__ __forceinline__ void norm_copy(void* dst, const void* w, const void* 
 // rows (k pair first halves, second halves, v rows).
 template <typename W>
 __device__ __noinline__ void att_issue_rows(const StepParams& P, int l) {
-  const mie_step_desc& d = P.d;
-  const StepGeom& g = P.g;
-  const mie_layer_desc& ly = P.layers[l];
+  const mie_step_desc& d = ps_s.d;
+  const StepGeom& g = ps_s.g;
+  const mie_layer_desc& ly = layer_at(l);
   const int lane = threadIdx.x & 31;
   const int hd = d.head_dim, half = hd / 2, D = d.hidden_dim;
   const AttSplit a = att_split(g, hd, cx_s.pos);
@@ -415,13 +436,13 @@ __device__ __noinline__ void att_issue_rows(const StepParams& P, int l) {
 // Stage the first K/V chunk of this CTA's old tokens of layer l (whole warp).
 template <typename KV>
 __device__ __noinline__ void att_issue_kv(const StepParams& P, int l) {
-  const StepGeom& g = P.g;
-  const AttSplit a = att_split(g, P.d.head_dim, cx_s.pos);
+  const StepGeom& g = ps_s.g;
+  const AttSplit a = att_split(g, ps_s.d.head_dim, cx_s.pos);
   const int n0 = min(g.chunk_tok, a.t1 - a.t0);
   if (n0 <= 0) return;
   if ((threadIdx.x & 31) == 0) fence_proxy_async_smem();
   __syncwarp();
-  kv_issue<KV>(P.d, g, P.layers[l], a.h, a.t0, n0, kBarKv);
+  kv_issue<KV>(ps_s.d, g, layer_at(l), a.h, a.t0, n0, kBarKv);
 }
 
 // Stage layer l's out_proj rows of this CTA, the router and the MoE norm
@@ -429,8 +450,8 @@ __device__ __noinline__ void att_issue_kv(const StepParams& P, int l) {
 // attention norm slot (one thread).
 template <typename W>
 __device__ __noinline__ void side_issue(const StepParams& P, int l) {
-  const mie_step_desc& d = P.d;
-  const StepGeom& g = P.g;
+  const mie_step_desc& d = ps_s.d;
+  const StepGeom& g = ps_s.g;
   const int D = d.hidden_dim, E = d.num_experts;
   const uint32_t rb = (uint32_t)(D * sizeof(W));
   uint8_t* dst = smem_at<uint8_t>(g.sm_moe);
@@ -440,7 +461,7 @@ __device__ __noinline__ void side_issue(const StepParams& P, int l) {
     norm_copy(smem_at<uint8_t>(g.sm_anw), d.final_norm_w, d.final_norm_b, rb, kBarSide);
     return;
   }
-  const mie_layer_desc& ly = P.layers[l];
+  const mie_layer_desc& ly = layer_at(l);
   int r0, r1;
   split32(D, blockIdx.x, gridDim.x, &r0, &r1);
   bar_arm(kBarSide, (uint32_t)(r1 - r0 + E + (ly.moe_norm_b ? 2 : 1)) * rb);
@@ -453,8 +474,8 @@ __device__ __noinline__ void side_issue(const StepParams& P, int l) {
 // the ring, which spans the attention staging area and the expert area.
 template <typename W>
 __device__ __noinline__ void head_issue(const StepParams& P, int first, int count) {
-  const mie_step_desc& d = P.d;
-  const StepGeom& g = P.g;
+  const mie_step_desc& d = ps_s.d;
+  const StepGeom& g = ps_s.g;
   int v0h, v1h;
   split32(d.vocab, blockIdx.x, gridDim.x, &v0h, &v1h);
   const uint32_t rb = (uint32_t)(d.hidden_dim * sizeof(W));
@@ -631,8 +652,8 @@ __device__ __forceinline__ void gemv_global(const uint4* rows, int n, int nvec, 
 template <typename KV>
 __device__ __noinline__ bool att_core(const StepParams& P, int l, int h, int t0, int t1, const float* q, float* sc,
                                       float* ab) {
-  const mie_step_desc& d = P.d;
-  const StepGeom& g = P.g;
+  const mie_step_desc& d = ps_s.d;
+  const StepGeom& g = ps_s.g;
   const int tid = threadIdx.x, hd = d.head_dim, chunk = g.chunk_tok;
   constexpr int VPT = 16 / (int)sizeof(KV);
   const int VPH = hd / VPT, Gp = kST / hd, gi = tid / hd, dcol = tid - gi * hd;
@@ -649,7 +670,7 @@ __device__ __noinline__ bool att_core(const StepParams& P, int l, int h, int t0,
       if (tid < 32) {
         if (tid == 0) fence_proxy_async_smem();
         __syncwarp();
-        kv_issue<KV>(d, g, P.layers[l], h, ta, n, kBarKv);
+        kv_issue<KV>(d, g, layer_at(l), h, ta, n, kBarKv);
       }
     }
     if (!bar_wait(kBarKv, g.ll, d.status)) return false;
@@ -720,9 +741,9 @@ __device__ __noinline__ bool att_core(const StepParams& P, int l, int h, int t0,
 // ---------------------------------------------------------------------------
 template <typename W, typename KV>
 __device__ __noinline__ bool att_phase(const StepParams& P, int l) {
-  const mie_step_desc& d = P.d;
-  const StepGeom& g = P.g;
-  const mie_layer_desc& ly = P.layers[l];
+  const mie_step_desc& d = ps_s.d;
+  const StepGeom& g = ps_s.g;
+  const mie_layer_desc& ly = layer_at(l);
   constexpr int PV = Elem<W>::kPerVec;
   const int tid = threadIdx.x;
   const int D = d.hidden_dim, hd = d.head_dim, half = hd / 2, nvD = D / PV;
@@ -903,9 +924,9 @@ __device__ __noinline__ bool att_phase(const StepParams& P, int l) {
 // ---------------------------------------------------------------------------
 template <typename W, typename KV>
 __device__ __noinline__ bool proj_phase(const StepParams& P, int l) {
-  const mie_step_desc& d = P.d;
-  const StepGeom& g = P.g;
-  const mie_layer_desc& ly = P.layers[l];
+  const mie_step_desc& d = ps_s.d;
+  const StepGeom& g = ps_s.g;
+  const mie_layer_desc& ly = layer_at(l);
   constexpr int PV = Elem<W>::kPerVec;
   const int tid = threadIdx.x, D = d.hidden_dim, nvD = D / PV;
   uint64_t* ll = g.ll;
@@ -928,8 +949,9 @@ __device__ __noinline__ bool proj_phase(const StepParams& P, int l) {
         att_issue_rows<W>(P, l + 1);
       else if ((tid & 31) == 0)
         head_issue<W>(P, 0, g.head_early);  // stages clear of the expert area
-    } else if (l + 1 < d.num_layers) {
-      att_issue_kv<KV>(P, l + 1);
+    } else {
+      if (l + 1 < d.num_layers) att_issue_kv<KV>(P, l + 1);
+      if (l + 2 < d.num_layers) layer_fetch(P, l + 2, kST - 64);  // into the slot of layer l - 2
     }
     STEP_STAMP_T(l, 17, kST - 32);
     return true;
@@ -959,9 +981,9 @@ __device__ __noinline__ bool proj_phase(const StepParams& P, int l) {
 // ---------------------------------------------------------------------------
 template <typename W>
 __device__ __noinline__ bool moe_phase(const StepParams& P, int l) {
-  const mie_step_desc& d = P.d;
-  const StepGeom& g = P.g;
-  const mie_layer_desc& ly = P.layers[l];
+  const mie_step_desc& d = ps_s.d;
+  const StepGeom& g = ps_s.g;
+  const mie_layer_desc& ly = layer_at(l);
   constexpr int PV = Elem<W>::kPerVec;
   constexpr bool kStaged = sizeof(W) == 2;
   const int tid = threadIdx.x;
@@ -1058,6 +1080,8 @@ __device__ __noinline__ bool moe_phase(const StepParams& P, int l) {
     }
   }
   __syncthreads();
+  const bool side_now = kStaged && l + 1 < d.num_layers && g.nr_max + E + 2 <= nmat * nu;
+  if (side_now && tid == kST - 1) side_issue<W>(P, l + 1);
   if (tid < nu) {
     const int u = u0 + tid, k = u / Hx;
     const int64_t row = (int64_t)(k ? sel1 : sel0) * Hx + (u - k * Hx);
@@ -1073,10 +1097,8 @@ __device__ __noinline__ bool moe_phase(const StepParams& P, int l) {
   // the next layer's out_proj / router / norm rows go over the consumed up
   // rows while the down GEMV runs (warps < 2 nr), issued by the last thread,
   // when they fit there; else after the down GEMV
-  const bool side_now = kStaged && l + 1 < d.num_layers && g.nr_max + E + 2 <= nmat * nu && 2 * nr < kSW;
   if constexpr (kStaged) {
     if (!bar_wait(kBarDown, ll, d.status)) return false;
-    if (side_now && tid == kST - 1) side_issue<W>(P, l + 1);
   }
   if (kStaged && 2 * nr <= kSW) {
     // both slots' down rows (adjacent in shared memory) in one pass: rows
@@ -1126,8 +1148,8 @@ __device__ __noinline__ bool moe_phase(const StepParams& P, int l) {
 // ---------------------------------------------------------------------------
 template <typename W>
 __device__ __noinline__ bool head_phase(const StepParams& P) {
-  const mie_step_desc& d = P.d;
-  const StepGeom& g = P.g;
+  const mie_step_desc& d = ps_s.d;
+  const StepGeom& g = ps_s.g;
   constexpr int PV = Elem<W>::kPerVec;
   const int G = gridDim.x, c = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int D = d.hidden_dim, nvD = D / PV, V = d.vocab, Lnum = d.num_layers;
@@ -1240,12 +1262,27 @@ __device__ __noinline__ bool head_phase(const StepParams& P) {
 
 template <typename W, typename KV>
 __global__ void __launch_bounds__(kST, 1) step_kernel(const __grid_constant__ StepParams P) {
-  const mie_step_desc& d = P.d;
+  {
+    // parameters -> shared memory: descriptor and geometry, layers 0 .. 3
+    constexpr int kWords = (int)(sizeof(StepShared) / 8);
+    static_assert(sizeof(mie_step_desc) % 8 == 0 && sizeof(StepGeom) % 8 == 0, "8-byte words");
+    const int i = threadIdx.x;
+    if (i < kWords) {
+      const uint64_t* src = i < (int)(sizeof(mie_step_desc) / 8)
+                                ? reinterpret_cast<const uint64_t*>(&P.d) + i
+                                : reinterpret_cast<const uint64_t*>(&P.g) + (i - (int)(sizeof(mie_step_desc) / 8));
+      reinterpret_cast<uint64_t*>(&ps_s)[i] = *src;
+    }
+#pragma unroll 1
+    for (int l = 0; l < kLayerSlots && l < P.d.num_layers; ++l) layer_fetch(P, l, 128 + 16 * l);
+    __syncthreads();
+  }
+  const mie_step_desc& d = ps_s.d;
   // ---- step prologue: position, token, cache slot of the new token ----
   if (threadIdx.x == 0) {
     const int c = blockIdx.x;
     int stop = d.done ? __ldcg(d.done) : 0;
-    cx_s.step = (uint32_t)ll_ld(P.g.ll + kHdrStep) + 1u;
+    cx_s.step = (uint32_t)ll_ld(ps_s.g.ll + kHdrStep) + 1u;
     const int p = __ldcg(d.pos);
     const int64_t t = __ldcg(d.token);
     if (!stop && (p < 0 || p >= d.max_pos || t < 0 || t >= d.vocab)) {
@@ -1276,7 +1313,7 @@ __global__ void __launch_bounds__(kST, 1) step_kernel(const __grid_constant__ St
   if (cx_s.stop) return;
   {
     // physical block ids of this CTA's old tokens, the same for every layer
-    const AttSplit a = att_split(P.g, d.head_dim, cx_s.pos);
+    const AttSplit a = att_split(ps_s.g, d.head_dim, cx_s.pos);
     const int b0 = a.t0 / d.block_size;
     if (threadIdx.x == 0) cx_s.blk0 = b0;
     if (d.block_table && threadIdx.x < kStepBlkCache && a.t1 > a.t0 &&
