@@ -22,6 +22,10 @@
  *   mie_decode_step      <- src/moe_engine/model.py:543-565 (Model.forward for one
  *                           decode token) as one launch sequence, or as one
  *                           persistent launch (mie_step_scratch_bytes)
+ *   mie_gemm             <- the prompt prefill's projections: F.linear of the
+ *                           QKV and out projections (model.py:226-234,268) and
+ *                           the expert matmuls of the reference MoE loop
+ *                           (model.py:443-461), on the tcgen05 tensor cores
  */
 #ifndef MIE_H
 #define MIE_H
@@ -298,6 +302,39 @@ typedef struct mie_step_desc {
   int64_t step_scratch_bytes;
 } mie_step_desc;
 
+/* Prefill GEMM on the tcgen05 tensor cores: C = A . B^T with A [M, K] and
+ * B [N, K] bf16 row-major (rows of K elements), fp32 accumulation, then one of
+ * the epilogues below.  K a multiple of 64, N a multiple of 128, rows 16-byte
+ * aligned.  Grouped form (groups > 1 or counts set): group g uses A rows
+ * [g a_group_rows, ..), B rows [g b_group_rows, ..) and C rows
+ * [g c_group_rows, ..); only its first counts[g] rows (a device array; M when
+ * counts is NULL, at most M) are computed and stored. */
+enum {
+  MIE_GEMM_F32 = 0,    /* C fp32 */
+  MIE_GEMM_BF16 = 1,   /* C bf16 */
+  MIE_GEMM_RESID = 2,  /* C fp32 = resid + A.B^T (resid may alias C) */
+  MIE_GEMM_SWIGLU = 3  /* B = gate rows, b2 = up rows; N counts gate + up
+                          columns; C bf16 [.., N / 2] = silu(A.B^T) * (A.B2^T) */
+};
+typedef struct mie_gemm_args {
+  const void* a;        /* bf16 */
+  int64_t lda;          /* elements */
+  const void* b;        /* bf16 */
+  const void* b2;       /* bf16, MIE_GEMM_SWIGLU only */
+  int64_t ldb;          /* elements, b and b2 */
+  int64_t b_rows;       /* rows of b (and b2) over all groups */
+  void* c;
+  int64_t ldc;          /* elements */
+  const float* resid;   /* MIE_GEMM_RESID */
+  int64_t ldr;
+  const int32_t* counts;  /* grouped: valid rows per group (device) or NULL */
+  int M, N, K;
+  int epilogue;
+  int groups;
+  int a_group_rows, b_group_rows, c_group_rows;
+  int32_t* status;      /* optional device status word */
+} mie_gemm_args;
+
 /* Library management */
 int mie_version(void);
 int mie_init(int device);                 /* set kernel attributes; call before any capture */
@@ -346,6 +383,9 @@ int mie_decode_step(const mie_step_desc* d, void* stream);
 int64_t mie_step_scratch_bytes(const mie_step_desc* d);
 int mie_decode_layer(const mie_step_desc* d, int layer, void* stream);
 int mie_decode_head(const mie_step_desc* d, void* stream);
+
+/* Prefill GEMM (see mie_gemm_args). */
+int mie_gemm(const mie_gemm_args* a, void* stream);
 
 #ifdef __cplusplus
 }

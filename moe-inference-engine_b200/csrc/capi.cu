@@ -385,6 +385,7 @@ int mie_init(int device) {
   attn_set_attributes();
   gemv_set_attributes();
   step_set_attributes();
+  gemm_set_attributes();
   (void)num_sms();
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) note_cuda_error(e, "mie_init");
@@ -430,6 +431,11 @@ int mie_proj_residual(const mie_proj_args* a, void* stream) {
 int mie_lmhead_argmax(const mie_lmhead_args* a, void* stream) {
   if (!a) return MIE_ERR_INVALID;
   return run_lmhead(*a, static_cast<cudaStream_t>(stream), false);
+}
+
+int mie_gemm(const mie_gemm_args* a, void* stream) {
+  if (!a) return MIE_ERR_INVALID;
+  return gemm_run(*a, static_cast<cudaStream_t>(stream));
 }
 
 int mie_decode_layer(const mie_step_desc* d, int l, void* stream) {

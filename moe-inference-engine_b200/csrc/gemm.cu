@@ -1,0 +1,355 @@
+// Tensor-core GEMM for the prompt prefill: C = A . B^T with A [M, K] and
+// B [N, K] bf16, both K-major (row-major rows of K elements), on the
+// 5th-generation tensor cores.  At a prompt of a few hundred tokens every
+// projection of a layer is an M = T problem where tensor cores matter (the
+// decode step, M = 1, stays on CUDA cores).
+//
+// One CTA computes one 128 x BN tile:
+//   warp 0      one thread streams K-slices of A and B into shared memory with
+//               tiled TMA loads (128-byte swizzle), a ring of kStages stages;
+//   warp 1      allocates the TMEM accumulator (BN fp32 columns x 128 lanes)
+//               and one thread issues tcgen05.mma (M 128, N BN, K 16) four
+//               times per 64-wide K-slice, releasing each stage with
+//               tcgen05.commit to the stage's "empty" mbarrier;
+//   warps 2-5   wait for the final commit, read the accumulator with
+//               tcgen05.ld (warp w reads TMEM lanes 32 (w % 4) ...) and apply
+//               the epilogue: fp32 / bf16 store, fp32 residual add, SwiGLU of
+//               a gate half and an up half of the tile.
+// Grouped mode (blockIdx.z = group, e.g. an expert): A, B and C rows are
+// offset by a per-group stride and rows at or past the group's count (read on
+// the device) are neither computed into C nor stored.
+//
+// Every wait is bounded (kWaitLimitNs); a CTA that gives up records
+// MIE_ERR_TIMEOUT, skips its remaining work and still frees its TMEM.
+#include <cuda.h>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace mie {
+namespace {
+
+constexpr int kGemmThreads = 192;  // 6 warps
+constexpr int kBM = 128, kBK = 64;
+constexpr int kStages = 4;
+constexpr uint32_t kTileABytes = kBM * kBK * 2;  // 16 KB
+
+// ---- tcgen05 / TMA primitives ----
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t cols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+               "r"(cols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_free(uint32_t taddr, uint32_t cols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(cols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+// D (TMEM) = A (smem) . B (smem)^T (+ D when accumulate)
+__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                       uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrive on `bar` once every tcgen05.mma issued so far by this thread completed.
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+// 32 consecutive fp32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Shared-memory matrix descriptor of a K-major tile written by a 128-byte
+// swizzled TMA load: rows of 128 bytes, 8-row swizzle atoms 1024 bytes apart
+// (stride byte offset), leading byte offset unused (16 bytes), version 1,
+// layout SWIZZLE_128B.  The tile base is 1024-byte aligned; the k-th 16-wide
+// K step starts 32 k bytes further.
+__device__ __forceinline__ uint64_t sw128_desc(const void* tile, uint32_t k_bytes) {
+  const uint32_t addr = smem_u32(tile) + k_bytes;
+  uint64_t d = (uint64_t)((addr >> 4) & 0x3fffu);
+  d |= (uint64_t)1u << 16;            // leading byte offset (16 B, unused here)
+  d |= (uint64_t)(1024u >> 4) << 32;  // stride byte offset
+  d |= (uint64_t)1u << 46;            // descriptor version (sm_100)
+  d |= (uint64_t)2u << 61;            // SWIZZLE_128B
+  return d;
+}
+// Instruction descriptor: kind::f16, bf16 A and B, fp32 D, both K-major,
+// M = 128, N = n.
+__host__ __device__ constexpr uint32_t idesc_bf16(int n) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
+}
+
+__device__ __forceinline__ float silu_f(float v) { return v / (1.0f + expf(-v)); }
+
+template <int BN, int EPI>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                const __grid_constant__ CUtensorMap map_b2, const GemmArgs args) {
+  constexpr uint32_t kTileBBytes = (uint32_t)BN * kBK * 2;
+  constexpr uint32_t kStageBytes = kTileABytes + kTileBBytes;
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t full_bar[kStages], empty_bar[kStages], acc_bar;
+  __shared__ uint32_t tmem_s;
+  __shared__ int bad_s;
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = blockIdx.z;
+  const int rows = args.counts ? min(__ldg(args.counts + g), args.M) : args.M;
+  const int m0 = blockIdx.x * kBM, n0 = blockIdx.y * BN;
+  if (m0 >= rows) return;  // whole CTA: past this group's rows
+  const int a_row0 = g * args.a_group_rows + m0;
+  const int b_row0 = g * args.b_group_rows + (EPI == kEpiSwiGLU ? n0 / 2 : n0);
+  const int nk = args.K / kBK;
+
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    mbar_init(&acc_bar, 1);
+    bad_s = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(&tmem_s, (uint32_t)BN);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_s;
+
+  if (warp == 0 && lane == 0) {
+    // ---- TMA producer ----
+    for (int k = 0; k < nk; ++k) {
+      const int s = k % kStages, use = k / kStages;
+      if (use > 0 && !mbar_wait(&empty_bar[s], (uint32_t)((use - 1) & 1), args.status)) {
+        bad_s = 1;
+        break;
+      }
+      uint8_t* sa = smem + (size_t)s * kStageBytes;
+      uint8_t* sb = sa + kTileABytes;
+      mbar_arrive_expect_tx(&full_bar[s], kStageBytes);
+      tma_load_2d(sa, &map_a, k * kBK, a_row0, &full_bar[s]);
+      if constexpr (EPI == kEpiSwiGLU) {
+        // gate rows then up rows of the same BN / 2 units
+        tma_load_2d(sb, &map_b, k * kBK, b_row0, &full_bar[s]);
+        tma_load_2d(sb + kTileBBytes / 2, &map_b2, k * kBK, b_row0, &full_bar[s]);
+      } else {
+        tma_load_2d(sb, &map_b, k * kBK, b_row0, &full_bar[s]);
+      }
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ---- MMA issuer ----
+    constexpr uint32_t idesc = idesc_bf16(BN);
+    bool ok = true;
+    for (int k = 0; k < nk && ok; ++k) {
+      const int s = k % kStages, use = k / kStages;
+      if (!mbar_wait(&full_bar[s], (uint32_t)(use & 1), args.status)) {
+        bad_s = 1;
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint8_t* sa = smem + (size_t)s * kStageBytes;
+      const uint8_t* sb = sa + kTileABytes;
+#pragma unroll
+      for (int kk = 0; kk < kBK / 16; ++kk)
+        tc_mma(tmem, sw128_desc(sa, 32u * kk), sw128_desc(sb, 32u * kk), idesc, (k | kk) ? 1u : 0u);
+      tc_commit(&empty_bar[s]);  // the stage is free once these MMAs have read it
+    }
+    tc_commit(&acc_bar);  // accumulator complete (also after a failed wait: nothing in flight is left)
+  } else if (warp >= 2) {
+    // ---- epilogue: TMEM lanes 32 q .. 32 q + 31 = tile rows ----
+    const int q = warp & 3;
+    const bool ok = mbar_wait(&acc_bar, 0u, args.status);
+    tc_fence_after();
+    const int r = q * 32 + lane;
+    const int row = m0 + r;
+    const int64_t crow = (int64_t)g * args.c_group_rows + row;
+    if (ok && !bad_s) {
+      const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16);
+      if constexpr (EPI == kEpiSwiGLU) {
+        // columns [0, BN/2): gate, [BN/2, BN): up of the same units
+#pragma unroll 1
+        for (int c = 0; c < BN / 2; c += 32) {
+          float gv[32], uv[32];
+          tmem_ld32(tbase + c, gv);
+          tmem_ld32(tbase + BN / 2 + c, uv);
+          if (row < rows) {
+            __nv_bfloat16* out = static_cast<__nv_bfloat16*>(args.c) + crow * args.ldc + n0 / 2 + c;
+#pragma unroll
+            for (int i = 0; i < 32; i += 2)
+              *reinterpret_cast<__nv_bfloat162*>(out + i) =
+                  __floats2bfloat162_rn(silu_f(gv[i]) * uv[i], silu_f(gv[i + 1]) * uv[i + 1]);
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          float v[32];
+          tmem_ld32(tbase + c, v);
+          if (row < rows) {
+            if constexpr (EPI == kEpiBF16) {
+              __nv_bfloat16* out = static_cast<__nv_bfloat16*>(args.c) + crow * args.ldc + n0 + c;
+#pragma unroll
+              for (int i = 0; i < 32; i += 2)
+                *reinterpret_cast<__nv_bfloat162*>(out + i) = __floats2bfloat162_rn(v[i], v[i + 1]);
+            } else {
+              float* out = static_cast<float*>(args.c) + crow * args.ldc + n0 + c;
+              if constexpr (EPI == kEpiResid) {
+                const float* res = args.resid + crow * args.ldr + n0 + c;
+#pragma unroll
+                for (int i = 0; i < 32; i += 4) {
+                  const float4 rv = *reinterpret_cast<const float4*>(res + i);
+                  *reinterpret_cast<float4*>(out + i) =
+                      make_float4(rv.x + v[i], rv.y + v[i + 1], rv.z + v[i + 2], rv.w + v[i + 3]);
+                }
+              } else {
+#pragma unroll
+                for (int i = 0; i < 32; i += 4)
+                  *reinterpret_cast<float4*>(out + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+              }
+            }
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_free(tmem, (uint32_t)BN);
+  }
+}
+
+// ---- host: tensor maps ----
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// 2-D bf16 tensor [rows, cols] (row stride ld elements), box box_rows x 64,
+// 128-byte swizzle; reads past `rows` return zeros.
+int make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return MIE_ERR_CUDA;
+  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+  const cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? MIE_OK : MIE_ERR_INVALID;
+}
+
+template <int BN, int EPI>
+constexpr uint32_t gemm_smem() {
+  return 1024 + kStages * (kTileABytes + (uint32_t)BN * kBK * 2);
+}
+
+template <int BN, int EPI>
+int gemm_launch_t(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& b2, const GemmArgs& args,
+                  int groups, cudaStream_t st) {
+  const dim3 grid((unsigned)((args.M + kBM - 1) / kBM), (unsigned)(args.N / BN), (unsigned)groups);
+  return launch(gemm_kernel<BN, EPI>, grid, dim3(kGemmThreads), gemm_smem<BN, EPI>(), st, false, a, b, b2, args);
+}
+
+}  // namespace
+
+void gemm_set_attributes() {
+  cudaFuncSetAttribute(gemm_kernel<128, kEpiF32>, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm_smem<128, kEpiF32>());
+  cudaFuncSetAttribute(gemm_kernel<128, kEpiBF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       gemm_smem<128, kEpiBF16>());
+  cudaFuncSetAttribute(gemm_kernel<128, kEpiResid>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       gemm_smem<128, kEpiResid>());
+  cudaFuncSetAttribute(gemm_kernel<128, kEpiSwiGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       gemm_smem<128, kEpiSwiGLU>());
+}
+
+// C[g] = A[g] . B[g]^T for the groups of a (see mie_gemm_args).
+int gemm_run(const mie_gemm_args& a, cudaStream_t st) {
+  if (a.M <= 0 || a.N <= 0 || a.K <= 0 || a.K % kBK || a.N % 128 || a.groups <= 0) return MIE_ERR_UNSUPPORTED;
+  if (!a.a || !a.b || !a.c || (a.epilogue == kEpiSwiGLU && !a.b2) || (a.epilogue == kEpiResid && !a.resid) ||
+      a.epilogue < kEpiF32 || a.epilogue > kEpiSwiGLU)
+    return MIE_ERR_INVALID;
+  const bool grouped = a.groups > 1 || a.counts;
+  if (grouped && (a.a_group_rows < a.M || a.c_group_rows < a.M)) return MIE_ERR_INVALID;
+  const uintptr_t al = reinterpret_cast<uintptr_t>(a.a) | reinterpret_cast<uintptr_t>(a.b) |
+                       reinterpret_cast<uintptr_t>(a.b2) | (uintptr_t)(a.lda * 2) | (uintptr_t)(a.ldb * 2);
+  if (al % 16 || a.lda < a.K || a.ldb < a.K) return MIE_ERR_INVALID;
+  const int out_cols = a.epilogue == kEpiSwiGLU ? a.N / 2 : a.N;
+  if (a.ldc < out_cols || (a.epilogue == kEpiResid && a.ldr < a.N)) return MIE_ERR_INVALID;
+  // epilogue stores: 16-byte fp32 vectors, 4-byte bf16 pairs
+  const bool f32_out = a.epilogue == kEpiF32 || a.epilogue == kEpiResid;
+  const uintptr_t cal = reinterpret_cast<uintptr_t>(a.c) | reinterpret_cast<uintptr_t>(a.resid) |
+                        (uintptr_t)(a.ldc * (f32_out ? 4 : 2)) | (uintptr_t)(a.ldr * 4);
+  if (cal % (f32_out ? 16 : 4)) return MIE_ERR_INVALID;
+  const int64_t a_rows = grouped ? (int64_t)a.groups * a.a_group_rows : a.M;
+  CUtensorMap ma, mb, mb2;
+  const int box_b = a.epilogue == kEpiSwiGLU ? 64 : 128;
+  int rc = make_map(&ma, a.a, a_rows, a.K, a.lda, kBM);
+  if (rc == MIE_OK) rc = make_map(&mb, a.b, a.b_rows, a.K, a.ldb, box_b);
+  if (rc == MIE_OK) rc = make_map(&mb2, a.epilogue == kEpiSwiGLU ? a.b2 : a.b, a.b_rows, a.K, a.ldb, box_b);
+  if (rc != MIE_OK) return rc;
+  GemmArgs g{};
+  g.M = a.M;
+  g.N = a.N;
+  g.K = a.K;
+  g.c = a.c;
+  g.ldc = a.ldc;
+  g.resid = a.resid;
+  g.ldr = a.ldr;
+  g.counts = a.counts;
+  g.a_group_rows = grouped ? a.a_group_rows : 0;
+  g.b_group_rows = grouped ? a.b_group_rows : 0;
+  g.c_group_rows = grouped ? a.c_group_rows : 0;
+  g.status = a.status;
+  switch (a.epilogue) {
+    case kEpiF32:
+      return gemm_launch_t<128, kEpiF32>(ma, mb, mb2, g, a.groups, st);
+    case kEpiBF16:
+      return gemm_launch_t<128, kEpiBF16>(ma, mb, mb2, g, a.groups, st);
+    case kEpiResid:
+      return gemm_launch_t<128, kEpiResid>(ma, mb, mb2, g, a.groups, st);
+    default:
+      return gemm_launch_t<128, kEpiSwiGLU>(ma, mb, mb2, g, a.groups, st);
+  }
+}
+
+}  // namespace mie

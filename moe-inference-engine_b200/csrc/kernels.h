@@ -139,6 +139,22 @@ int step_geometry(const mie_step_desc& d, int grid, StepGeom* g);
 int step_launch(const mie_step_desc& d, const StepGeom& g, uint64_t* scratch, cudaStream_t st);
 void step_set_attributes();
 
+// gemm.cu (prefill GEMM on the tensor cores)
+enum { kEpiF32 = MIE_GEMM_F32, kEpiBF16 = MIE_GEMM_BF16, kEpiResid = MIE_GEMM_RESID, kEpiSwiGLU = MIE_GEMM_SWIGLU };
+// Device-side arguments of one GEMM launch (the tensor maps travel separately).
+struct GemmArgs {
+  int M, N, K;
+  void* c;
+  int64_t ldc;
+  const float* resid;
+  int64_t ldr;
+  const int32_t* counts;
+  int a_group_rows, b_group_rows, c_group_rows;
+  int32_t* status;
+};
+int gemm_run(const mie_gemm_args& a, cudaStream_t st);
+void gemm_set_attributes();
+
 int num_sms();
 
 }  // namespace mie

@@ -106,6 +106,18 @@ class StepDesc(ctypes.Structure):
     ]
 
 
+GEMM_F32, GEMM_BF16, GEMM_RESID, GEMM_SWIGLU = 0, 1, 2, 3
+
+
+class GemmArgs(ctypes.Structure):
+    _fields_ = [
+        ("a", _p), ("lda", _i64), ("b", _p), ("b2", _p), ("ldb", _i64), ("b_rows", _i64), ("c", _p),
+        ("ldc", _i64), ("resid", _p), ("ldr", _i64), ("counts", _p), ("M", _i), ("N", _i), ("K", _i),
+        ("epilogue", _i), ("groups", _i), ("a_group_rows", _i), ("b_group_rows", _i),
+        ("c_group_rows", _i), ("status", _p),
+    ]
+
+
 # Every symbol include/mie.h declares, with its ctypes argument types.
 SYMBOLS = {
     "mie_version": ([], ctypes.c_int),
@@ -124,6 +136,7 @@ SYMBOLS = {
     "mie_decode_layer": ([ctypes.POINTER(StepDesc), _i, _p], ctypes.c_int),
     "mie_decode_head": ([ctypes.POINTER(StepDesc), _p], ctypes.c_int),
     "mie_step_scratch_bytes": ([ctypes.POINTER(StepDesc)], ctypes.c_int64),
+    "mie_gemm": ([ctypes.POINTER(GemmArgs), _p], ctypes.c_int),
 }
 
 _lib = None
