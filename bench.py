@@ -271,7 +271,7 @@ def run_b200(args, rank, world, device):
     host_prompt = prompt.clone().pin_memory()
     e2e_times = []
     out_len = 0
-    for it in range(max(1, min(args.steps, 3)) + 1):
+    for it in range(max(1, min(args.steps, 5)) + 1):
         c = alloc.new_cache()
         torch.cuda.synchronize()
         t0 = time.perf_counter()

@@ -26,6 +26,11 @@
  *                           QKV and out projections (model.py:226-234,268) and
  *                           the expert matmuls of the reference MoE loop
  *                           (model.py:443-461), on the tcgen05 tensor cores
+ *   mie_prefill_norm     <- model.py:491-492,557-558 (embedding + norms, T tokens)
+ *   mie_prefill_rope_kv  <- model.py:226-247 (head split, RoPE, cache write)
+ *   mie_prefill_route    <- model.py:443-452 (fp32 router, top-2, softmax) plus
+ *                           the per-expert token selection of the loop
+ *   mie_prefill_combine  <- model.py:453-461 (weighted index_add_ of expert outputs)
  */
 #ifndef MIE_H
 #define MIE_H
@@ -335,6 +340,74 @@ typedef struct mie_gemm_args {
   int32_t* status;      /* optional device status word */
 } mie_gemm_args;
 
+/* Prefill per-token kernels (one warp per token; residual stream fp32, GEMM
+ * operands bf16; weights bf16; hidden_dim a multiple of 32, at most 1024). */
+typedef struct mie_prefill_norm_args {
+  int tokens;
+  int hidden_dim;
+  int norm;                  /* MIE_NORM_RMS or MIE_NORM_LAYER */
+  float eps;
+  const int64_t* ids;        /* optional: first x[t] = embedding[ids[t]] (+ pos_embedding[pos0 + t]) */
+  const void* embedding;     /* bf16 [vocab, hidden_dim] */
+  const void* pos_embedding; /* bf16 [max_pos, hidden_dim] or NULL */
+  int pos0;
+  float* x;                  /* fp32 [tokens, hidden_dim] residual stream */
+  const void* w;             /* bf16 norm weight */
+  const void* b;             /* bf16 norm bias (LayerNorm) or NULL */
+  void* out;                 /* bf16 [tokens, hidden_dim] */
+} mie_prefill_norm_args;
+
+typedef struct mie_prefill_rope_args {
+  int tokens;
+  int num_heads;
+  int head_dim;
+  int pos0;                  /* position of token 0 */
+  const float* qkv;          /* fp32 [tokens, 3 * hidden]: q | k | v */
+  const float* rope_cos;     /* fp32 [max_pos, head_dim / 2], or NULL (no RoPE) */
+  const float* rope_sin;
+  void* q_out;               /* bf16 [num_heads, tokens, head_dim] */
+  void* k_out;
+  void* v_out;
+  void* k_cache;             /* bf16 cache of this layer */
+  void* v_cache;
+  const int32_t* block_table;  /* paged cache; NULL: contiguous (block_size = max positions) */
+  int block_size;
+  int64_t kv_stride_block;   /* elements */
+  int64_t kv_stride_head;
+  int64_t kv_stride_tok;
+} mie_prefill_rope_args;
+
+typedef struct mie_prefill_route_args {
+  int tokens;
+  int hidden_dim;
+  int num_experts;           /* 2 .. 32, top-2 */
+  int group_rows;            /* rows reserved per expert in `gathered` (>= tokens) */
+  const void* x;             /* bf16 [tokens, hidden_dim], normalised: the rows gathered */
+  const float* x_res;        /* fp32 [tokens, hidden_dim] residual stream; the router
+                                reads norm(x_res) in fp32 */
+  int norm;                  /* MIE_NORM_RMS or MIE_NORM_LAYER */
+  float eps;
+  const void* norm_w;        /* bf16 */
+  const void* norm_b;        /* bf16 or NULL */
+  const void* router_w;      /* bf16 [num_experts, hidden_dim] */
+  float* logits;             /* optional fp32 [tokens, num_experts] */
+  int32_t* counts;           /* [num_experts] rows per expert; zero on entry */
+  float* weights;            /* [tokens, 2] softmax of the two selected logits */
+  int32_t* ids_out;          /* [tokens, 2] selected experts (ties -> lower id) */
+  int32_t* rows_out;         /* [tokens, 2] row of the token's copy in `gathered` */
+  void* gathered;            /* bf16 [num_experts * group_rows, hidden_dim] */
+} mie_prefill_route_args;
+
+typedef struct mie_prefill_combine_args {
+  int tokens;
+  int hidden_dim;
+  float* x;                  /* fp32 [tokens, hidden_dim], updated in place */
+  const float* y;            /* fp32 expert outputs, rows as in rows[] */
+  int64_t ldy;
+  const float* weights;      /* [tokens, 2] */
+  const int32_t* rows;       /* [tokens, 2] */
+} mie_prefill_combine_args;
+
 /* Library management */
 int mie_version(void);
 int mie_init(int device);                 /* set kernel attributes; call before any capture */
@@ -384,8 +457,12 @@ int64_t mie_step_scratch_bytes(const mie_step_desc* d);
 int mie_decode_layer(const mie_step_desc* d, int layer, void* stream);
 int mie_decode_head(const mie_step_desc* d, void* stream);
 
-/* Prefill GEMM (see mie_gemm_args). */
+/* Prefill GEMM (see mie_gemm_args) and per-token kernels. */
 int mie_gemm(const mie_gemm_args* a, void* stream);
+int mie_prefill_norm(const mie_prefill_norm_args* a, void* stream);
+int mie_prefill_rope_kv(const mie_prefill_rope_args* a, void* stream);
+int mie_prefill_route(const mie_prefill_route_args* a, void* stream);
+int mie_prefill_combine(const mie_prefill_combine_args* a, void* stream);
 
 #ifdef __cplusplus
 }

@@ -438,6 +438,19 @@ int mie_gemm(const mie_gemm_args* a, void* stream) {
   return gemm_run(*a, static_cast<cudaStream_t>(stream));
 }
 
+int mie_prefill_norm(const mie_prefill_norm_args* a, void* stream) {
+  return a ? prefill_norm(*a, static_cast<cudaStream_t>(stream)) : MIE_ERR_INVALID;
+}
+int mie_prefill_rope_kv(const mie_prefill_rope_args* a, void* stream) {
+  return a ? prefill_rope_kv(*a, static_cast<cudaStream_t>(stream)) : MIE_ERR_INVALID;
+}
+int mie_prefill_route(const mie_prefill_route_args* a, void* stream) {
+  return a ? prefill_route(*a, static_cast<cudaStream_t>(stream)) : MIE_ERR_INVALID;
+}
+int mie_prefill_combine(const mie_prefill_combine_args* a, void* stream) {
+  return a ? prefill_combine(*a, static_cast<cudaStream_t>(stream)) : MIE_ERR_INVALID;
+}
+
 int mie_decode_layer(const mie_step_desc* d, int l, void* stream) {
   if (!d || l < 0 || l >= d->num_layers) return MIE_ERR_INVALID;
   int rc = check_step(*d);

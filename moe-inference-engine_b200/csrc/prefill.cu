@@ -1,0 +1,260 @@
+// Prompt prefill: the per-token kernels around the tensor-core GEMMs
+// (csrc/gemm.cu).  One warp per token everywhere; the residual stream x stays
+// fp32, GEMM operands are bf16.
+//
+//   prefill_norm      x[t] = embedding[id] (+ learned position) when ids are
+//                     given; out[t] = norm(x[t]) as bf16        (model.py:491-492,557-558)
+//   prefill_rope_kv   q / k / v rows of the QKV GEMM -> RoPE on q and k ->
+//                     [H, T, hd] bf16 operands for the attention and the K/V
+//                     cache slots of positions pos0 + t (paged through the
+//                     block table, or contiguous)             (model.py:226-247)
+//   prefill_route     router logits (fp32, from the fp32 residual normalised
+//                     again here), top-2 with ties to the lower id,
+//                     softmax of the two logits; each token's row is copied to
+//                     the next free row of both selected experts' groups
+//                     (counts[e] grows by atomics: the order of the rows in a
+//                     group varies, each row's result does not)  (model.py:443-452)
+//   prefill_combine   x[t] += w0 y[row0] + w1 y[row1] in that order (model.py:453-461)
+#include "common.cuh"
+#include "kernels.h"
+
+namespace mie {
+namespace {
+
+constexpr int kPfThreads = 256;  // 8 warps, one token each
+constexpr int kPfWarps = kPfThreads / 32;
+constexpr int kPfMaxDim = 1024;  // hidden_dim: at most 32 elements per lane
+
+__device__ __forceinline__ float bf(const __nv_bfloat16* p, int64_t i) { return __bfloat162float(p[i]); }
+
+__global__ void __launch_bounds__(kPfThreads) prefill_norm_kernel(const mie_prefill_norm_args a) {
+  const int t = blockIdx.x * kPfWarps + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (t >= a.tokens) return;
+  const int D = a.hidden_dim;
+  float* xr = a.x + (int64_t)t * D;
+  float v[kPfMaxDim / 32];
+  const int per = D / 32;
+  if (a.ids) {
+    const int64_t id = a.ids[t];
+    const __nv_bfloat16* e = static_cast<const __nv_bfloat16*>(a.embedding) + id * D;
+    const __nv_bfloat16* pe =
+        a.pos_embedding ? static_cast<const __nv_bfloat16*>(a.pos_embedding) + (int64_t)(a.pos0 + t) * D : nullptr;
+#pragma unroll 4
+    for (int j = 0; j < per; ++j) {
+      const int i = lane + 32 * j;
+      float y = bf(e, i);
+      if (pe) y += bf(pe, i);
+      v[j] = y;
+      xr[i] = y;
+    }
+  } else {
+#pragma unroll 4
+    for (int j = 0; j < per; ++j) v[j] = xr[lane + 32 * j];
+  }
+  const __nv_bfloat16* w = static_cast<const __nv_bfloat16*>(a.w);
+  const __nv_bfloat16* b = static_cast<const __nv_bfloat16*>(a.b);
+  __nv_bfloat16* out = static_cast<__nv_bfloat16*>(a.out) + (int64_t)t * D;
+  float mean = 0.f, rs;
+  if (a.norm == MIE_NORM_LAYER) {
+    float s = 0.f;
+    for (int j = 0; j < per; ++j) s += v[j];
+    mean = warp_sum(s) / (float)D;
+    float q = 0.f;
+    for (int j = 0; j < per; ++j) q = fmaf(v[j] - mean, v[j] - mean, q);
+    rs = rsqrtf(warp_sum(q) / (float)D + a.eps);
+  } else {
+    float q = 0.f;
+    for (int j = 0; j < per; ++j) q = fmaf(v[j], v[j], q);
+    rs = rsqrtf(warp_sum(q) / (float)D + a.eps);
+  }
+#pragma unroll 4
+  for (int j = 0; j < per; ++j) {
+    const int i = lane + 32 * j;
+    float y = (v[j] - mean) * rs * bf(w, i);
+    if (b) y += bf(b, i);
+    out[i] = __float2bfloat16_rn(y);
+  }
+}
+
+// One warp per (token, head): hd / 2 RoPE pairs of q and k, hd values of v.
+__global__ void __launch_bounds__(kPfThreads) prefill_rope_kv_kernel(const mie_prefill_rope_args a) {
+  const int item = blockIdx.x * kPfWarps + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (item >= a.tokens * a.num_heads) return;
+  const int t = item / a.num_heads, h = item - t * a.num_heads;
+  const int hd = a.head_dim, half = hd / 2, D = a.num_heads * hd;
+  const int p = a.pos0 + t;
+  const float* row = a.qkv + (int64_t)t * 3 * D;
+  const float* qr = row + h * hd;
+  const float* kr = row + D + h * hd;
+  const float* vr = row + 2 * D + h * hd;
+  const int64_t o = ((int64_t)h * a.tokens + t) * hd;  // [H, T, hd]
+  __nv_bfloat16* qo = static_cast<__nv_bfloat16*>(a.q_out) + o;
+  __nv_bfloat16* ko = static_cast<__nv_bfloat16*>(a.k_out) + o;
+  __nv_bfloat16* vo = static_cast<__nv_bfloat16*>(a.v_out) + o;
+  int64_t blk = p / a.block_size;
+  if (a.block_table) blk = a.block_table[blk];
+  const int64_t slot = blk * a.kv_stride_block + (int64_t)h * a.kv_stride_head + (int64_t)(p % a.block_size) * a.kv_stride_tok;
+  __nv_bfloat16* kc = static_cast<__nv_bfloat16*>(a.k_cache) + slot;
+  __nv_bfloat16* vc = static_cast<__nv_bfloat16*>(a.v_cache) + slot;
+  const float* cs = a.rope_cos ? a.rope_cos + (int64_t)p * half : nullptr;
+  const float* sn = a.rope_sin ? a.rope_sin + (int64_t)p * half : nullptr;
+  for (int j = lane; j < half; j += 32) {
+    float q1 = qr[j], q2 = qr[j + half], k1 = kr[j], k2 = kr[j + half];
+    if (cs) {
+      const float c = cs[j], s = sn[j];
+      const float a1 = q1 * c - q2 * s, a2 = q2 * c + q1 * s;
+      const float b1 = k1 * c - k2 * s, b2 = k2 * c + k1 * s;
+      q1 = a1;
+      q2 = a2;
+      k1 = b1;
+      k2 = b2;
+    }
+    qo[j] = __float2bfloat16_rn(q1);
+    qo[j + half] = __float2bfloat16_rn(q2);
+    const __nv_bfloat16 e1 = __float2bfloat16_rn(k1), e2 = __float2bfloat16_rn(k2);
+    ko[j] = e1;
+    ko[j + half] = e2;
+    kc[j] = e1;
+    kc[j + half] = e2;
+  }
+  for (int j = lane; j < hd; j += 32) {
+    const __nv_bfloat16 e = __float2bfloat16_rn(vr[j]);
+    vo[j] = e;
+    vc[j] = e;
+  }
+}
+
+__device__ __forceinline__ bool better(float v, int i, float bv, int bi) { return v > bv || (v == bv && i < bi); }
+
+__global__ void __launch_bounds__(kPfThreads) prefill_route_kernel(const mie_prefill_route_args a) {
+  const int t = blockIdx.x * kPfWarps + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (t >= a.tokens) return;
+  const int D = a.hidden_dim, E = a.num_experts, per = D / 32;
+  const __nv_bfloat16* xr = static_cast<const __nv_bfloat16*>(a.x) + (int64_t)t * D;
+  const __nv_bfloat16* rw = static_cast<const __nv_bfloat16*>(a.router_w);
+  // the router sees the normalised residual in fp32 (the bf16 copy feeds the
+  // expert GEMMs): routing decisions as close to an fp32 forward as possible
+  float xv[kPfMaxDim / 32];
+  const float* xf = a.x_res + (int64_t)t * D;
+#pragma unroll 4
+  for (int j = 0; j < per; ++j) xv[j] = xf[lane + 32 * j];
+  {
+    const __nv_bfloat16* nw = static_cast<const __nv_bfloat16*>(a.norm_w);
+    const __nv_bfloat16* nb = static_cast<const __nv_bfloat16*>(a.norm_b);
+    float mean = 0.f, q = 0.f;
+    if (a.norm == MIE_NORM_LAYER) {
+      float sm = 0.f;
+      for (int j = 0; j < per; ++j) sm += xv[j];
+      mean = warp_sum(sm) / (float)D;
+      for (int j = 0; j < per; ++j) q = fmaf(xv[j] - mean, xv[j] - mean, q);
+    } else {
+      for (int j = 0; j < per; ++j) q = fmaf(xv[j], xv[j], q);
+    }
+    const float rs = rsqrtf(warp_sum(q) / (float)D + a.eps);
+    for (int j = 0; j < per; ++j) {
+      const int i = lane + 32 * j;
+      float y = (xv[j] - mean) * rs * bf(nw, i);
+      if (nb) y += bf(nb, i);
+      xv[j] = y;
+    }
+  }
+  // lane e ends up holding logit e (E <= 32)
+  float mine = -INFINITY;
+  for (int e = 0; e < E; ++e) {
+    float s = 0.f;
+    for (int j = 0; j < per; ++j) s = fmaf(xv[j], bf(rw, (int64_t)e * D + lane + 32 * j), s);
+    s = warp_sum(s);
+    if (lane == e) mine = s;
+  }
+  if (a.logits && lane < E) a.logits[(int64_t)t * E + lane] = mine;
+  float bv = lane < E ? mine : -INFINITY;
+  int bi = lane < E ? lane : 0x7fffffff;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (better(ov, oi, bv, bi)) {
+      bv = ov;
+      bi = oi;
+    }
+  }
+  const int i0 = bi;
+  float cv = (lane < E && lane != i0) ? mine : -INFINITY;
+  int ci = (lane < E && lane != i0) ? lane : 0x7fffffff;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, cv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, ci, o);
+    if (better(ov, oi, cv, ci)) {
+      cv = ov;
+      ci = oi;
+    }
+  }
+  const int i1 = ci;
+  int r0 = 0, r1 = 0;
+  if (lane == 0) {
+    const float e1 = expf(cv - bv);
+    a.weights[2 * t] = 1.0f / (1.0f + e1);
+    a.weights[2 * t + 1] = e1 / (1.0f + e1);
+    a.ids_out[2 * t] = i0;
+    a.ids_out[2 * t + 1] = i1;
+    r0 = i0 * a.group_rows + atomicAdd(a.counts + i0, 1);
+    r1 = i1 * a.group_rows + atomicAdd(a.counts + i1, 1);
+    a.rows_out[2 * t] = r0;
+    a.rows_out[2 * t + 1] = r1;
+  }
+  r0 = __shfl_sync(0xffffffffu, r0, 0);
+  r1 = __shfl_sync(0xffffffffu, r1, 0);
+  __nv_bfloat16* g0 = static_cast<__nv_bfloat16*>(a.gathered) + (int64_t)r0 * D;
+  __nv_bfloat16* g1 = static_cast<__nv_bfloat16*>(a.gathered) + (int64_t)r1 * D;
+  for (int j = 0; j < per; ++j) {
+    const int i = lane + 32 * j;
+    g0[i] = xr[i];
+    g1[i] = xr[i];
+  }
+}
+
+__global__ void __launch_bounds__(kPfThreads) prefill_combine_kernel(const mie_prefill_combine_args a) {
+  const int t = blockIdx.x * kPfWarps + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (t >= a.tokens) return;
+  const int D = a.hidden_dim;
+  const float w0 = a.weights[2 * t], w1 = a.weights[2 * t + 1];
+  const float* y0 = a.y + (int64_t)a.rows[2 * t] * a.ldy;
+  const float* y1 = a.y + (int64_t)a.rows[2 * t + 1] * a.ldy;
+  float* xr = a.x + (int64_t)t * D;
+  for (int i = lane; i < D; i += 32) xr[i] = fmaf(w1, y1[i], fmaf(w0, y0[i], xr[i]));
+}
+
+unsigned grid_for(int items) { return (unsigned)((items + kPfWarps - 1) / kPfWarps); }
+
+}  // namespace
+
+int prefill_norm(const mie_prefill_norm_args& a, cudaStream_t st) {
+  if (a.tokens <= 0 || a.hidden_dim <= 0 || a.hidden_dim % 32 || a.hidden_dim > kPfMaxDim || !a.x || !a.w ||
+      !a.out || (a.ids && !a.embedding))
+    return MIE_ERR_INVALID;
+  return launch(prefill_norm_kernel, dim3(grid_for(a.tokens)), dim3(kPfThreads), 0, st, false, a);
+}
+
+int prefill_rope_kv(const mie_prefill_rope_args& a, cudaStream_t st) {
+  if (a.tokens <= 0 || a.num_heads <= 0 || a.head_dim <= 0 || a.head_dim % 2 || !a.qkv || !a.q_out || !a.k_out ||
+      !a.v_out || !a.k_cache || !a.v_cache || a.block_size <= 0 || (a.rope_cos && !a.rope_sin))
+    return MIE_ERR_INVALID;
+  return launch(prefill_rope_kv_kernel, dim3(grid_for(a.tokens * a.num_heads)), dim3(kPfThreads), 0, st, false, a);
+}
+
+int prefill_route(const mie_prefill_route_args& a, cudaStream_t st) {
+  if (a.tokens <= 0 || a.hidden_dim % 32 || a.hidden_dim > kPfMaxDim || a.num_experts < 2 || a.num_experts > 32 ||
+      a.group_rows < a.tokens || !a.x || !a.x_res || !a.norm_w || !a.router_w || !a.counts || !a.weights ||
+      !a.ids_out || !a.rows_out || !a.gathered)
+    return MIE_ERR_INVALID;
+  return launch(prefill_route_kernel, dim3(grid_for(a.tokens)), dim3(kPfThreads), 0, st, false, a);
+}
+
+int prefill_combine(const mie_prefill_combine_args& a, cudaStream_t st) {
+  if (a.tokens <= 0 || a.hidden_dim <= 0 || !a.x || !a.y || !a.weights || !a.rows || a.ldy < a.hidden_dim)
+    return MIE_ERR_INVALID;
+  return launch(prefill_combine_kernel, dim3(grid_for(a.tokens)), dim3(kPfThreads), 0, st, false, a);
+}
+
+}  // namespace mie

@@ -118,6 +118,38 @@ class GemmArgs(ctypes.Structure):
     ]
 
 
+class PrefillNormArgs(ctypes.Structure):
+    _fields_ = [
+        ("tokens", _i), ("hidden_dim", _i), ("norm", _i), ("eps", _f), ("ids", _p), ("embedding", _p),
+        ("pos_embedding", _p), ("pos0", _i), ("x", _p), ("w", _p), ("b", _p), ("out", _p),
+    ]
+
+
+class PrefillRopeArgs(ctypes.Structure):
+    _fields_ = [
+        ("tokens", _i), ("num_heads", _i), ("head_dim", _i), ("pos0", _i), ("qkv", _p), ("rope_cos", _p),
+        ("rope_sin", _p), ("q_out", _p), ("k_out", _p), ("v_out", _p), ("k_cache", _p), ("v_cache", _p),
+        ("block_table", _p), ("block_size", _i), ("kv_stride_block", _i64), ("kv_stride_head", _i64),
+        ("kv_stride_tok", _i64),
+    ]
+
+
+class PrefillRouteArgs(ctypes.Structure):
+    _fields_ = [
+        ("tokens", _i), ("hidden_dim", _i), ("num_experts", _i), ("group_rows", _i), ("x", _p),
+        ("x_res", _p), ("norm", _i), ("eps", _f), ("norm_w", _p), ("norm_b", _p),
+        ("router_w", _p), ("logits", _p), ("counts", _p), ("weights", _p), ("ids_out", _p),
+        ("rows_out", _p), ("gathered", _p),
+    ]
+
+
+class PrefillCombineArgs(ctypes.Structure):
+    _fields_ = [
+        ("tokens", _i), ("hidden_dim", _i), ("x", _p), ("y", _p), ("ldy", _i64), ("weights", _p),
+        ("rows", _p),
+    ]
+
+
 # Every symbol include/mie.h declares, with its ctypes argument types.
 SYMBOLS = {
     "mie_version": ([], ctypes.c_int),
@@ -137,6 +169,10 @@ SYMBOLS = {
     "mie_decode_head": ([ctypes.POINTER(StepDesc), _p], ctypes.c_int),
     "mie_step_scratch_bytes": ([ctypes.POINTER(StepDesc)], ctypes.c_int64),
     "mie_gemm": ([ctypes.POINTER(GemmArgs), _p], ctypes.c_int),
+    "mie_prefill_norm": ([ctypes.POINTER(PrefillNormArgs), _p], ctypes.c_int),
+    "mie_prefill_rope_kv": ([ctypes.POINTER(PrefillRopeArgs), _p], ctypes.c_int),
+    "mie_prefill_route": ([ctypes.POINTER(PrefillRouteArgs), _p], ctypes.c_int),
+    "mie_prefill_combine": ([ctypes.POINTER(PrefillCombineArgs), _p], ctypes.c_int),
 }
 
 _lib = None

@@ -632,6 +632,7 @@ class Model(nn.Module):
         result = super()._apply(fn, recurse=recurse)
         self._build_rope(self.token_embedding.weight.device)
         self._decode_runner = None
+        self._prefill_runner = None
         return result
 
     @property
@@ -663,6 +664,22 @@ class Model(nn.Module):
             self._decode_runner = DecodeRunner(self)
         return self._decode_runner
 
+    def prefill_runner(self):
+        """The tensor-core prompt prefill of this model (created on first use)."""
+        from .prefill import PrefillRunner
+
+        if getattr(self, "_prefill_runner", None) is None:
+            self._prefill_runner = PrefillRunner(self)
+        return self._prefill_runner
+
+    def prefill_supported(self, cache, token_ids) -> bool:
+        """Whether a prompt prefill can run on the sm_100a kernels (bf16 weights
+        and cache, SwiGLU experts, no biases, MoE mode not "reference",
+        attention mode not "gather")."""
+        from .prefill import PrefillRunner
+
+        return PrefillRunner.supports(self, cache, token_ids)
+
     def fused_decode_supported(self, cache, batch: int) -> bool:
         """Whether a one-token decode step can run as the fused kernel sequence."""
         from .decode import DecodeRunner
@@ -682,6 +699,8 @@ class Model(nn.Module):
                 block.moe.preflight_direct_decode(batch_size=batch)
             if self.fused_decode_supported(cache, batch):
                 return self.decode_runner().forward_step(token_ids, cache)
+        if position == 0 and seq_len > 1 and self.prefill_supported(cache, token_ids):
+            return self.prefill_runner().run(token_ids, cache)
 
         pos = torch.arange(position, position + seq_len, device=token_ids.device)
         x = self.token_embedding(token_ids)

@@ -60,3 +60,139 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, out: torch.Tensor | None = None, e
     lib = capi.ensure_init(a.device)
     capi.check(lib.mie_gemm(ctypes.byref(args), capi.stream_handle(a.device)), "mie_gemm")
     return out
+
+
+def _kv_layout(cache, layer: int):
+    """(k, v tensors of this layer, block table or None, block size, strides
+    block / head / token) for the K/V slots the prefill writes."""
+    if hasattr(cache, "allocator"):
+        al = cache.allocator
+        k, v = al.k_pool[layer], al.v_pool[layer]  # [blocks, H, bs, hd]
+        return k, v, cache.block_table_device, al.block_size, k.stride(0), k.stride(1), k.stride(2)
+    k, v = cache.k[layer, 0], cache.v[layer, 0]  # [H, max_seq, hd]
+    return k, v, None, k.shape[1], 0, k.stride(0), k.stride(1)
+
+
+class PrefillRunner:
+    """Prompt prefill of a bf16 model on the sm_100a kernels.
+
+    Per layer: norm -> QKV GEMM -> RoPE + K/V cache write -> causal attention
+    (PyTorch SDPA over the fresh K/V, as the reference's prefill fast path,
+    model.py:252-256) -> out_proj GEMM + residual -> norm -> router, top-2 and
+    per-expert row gather -> grouped SwiGLU up GEMM -> grouped down GEMM ->
+    weighted combine.  Then the final norm and the tied LM head GEMM for every
+    position.  The residual stream stays fp32.
+    """
+
+    @staticmethod
+    def supports(model, cache, token_ids) -> bool:
+        cfg = model.config
+        w = model.token_embedding.weight
+        if token_ids.dim() != 2 or token_ids.shape[0] != 1 or token_ids.shape[1] < 2 or cache.position != 0:
+            return False
+        if w.device.type != "cuda" or w.dtype != torch.bfloat16 or not capi.library_available():
+            return False
+        if getattr(cache, "attention_mode", "gather") == "gather":
+            return False
+        kv = cache.allocator.k_pool if hasattr(cache, "allocator") else cache.k
+        if kv.dtype != torch.bfloat16 or kv.device != w.device:
+            return False
+        if not hasattr(cache, "allocator") and cache.k.shape[1] != 1:
+            return False
+        D, Hx, V = cfg.hidden_dim, cfg.expert_hidden, cfg.vocab_size
+        if cfg.expert_act != "swiglu" or cfg.bias or cfg.top_k != 2 or not 2 <= cfg.num_experts <= 32:
+            return False
+        if D % 128 or D > 1024 or Hx % 64 or V % 128 or cfg.num_heads * cfg.head_dim != D:
+            return False
+        if any(block.moe.mode == "reference" for block in model.MoEBlocks):
+            return False
+        return all(p.dtype == torch.bfloat16 and p.device == w.device for p in model.parameters())
+
+    def __init__(self, model):
+        self.model = model
+        self.cfg = model.config
+        self.device = model.token_embedding.weight.device
+        self.lib = capi.ensure_init(self.device)
+
+    def _call(self, name, args):
+        capi.check(getattr(self.lib, name)(ctypes.byref(args), capi.stream_handle(self.device)), name)
+
+    def _norm(self, x, w, b, out, tokens, ids=None):
+        cfg = self.cfg
+        m = self.model
+        args = capi.PrefillNormArgs(
+            tokens=tokens, hidden_dim=cfg.hidden_dim, norm=capi.MIE_NORM_RMS if cfg.norm == "rms" else capi.MIE_NORM_LAYER,
+            eps=cfg.norm_eps, ids=capi.ptr(ids), embedding=m.token_embedding.weight.data_ptr(),
+            pos_embedding=m.positional_embedding.weight.data_ptr() if cfg.pos == "learned" else None, pos0=0,
+            x=x.data_ptr(), w=w.data_ptr(), b=capi.ptr(b), out=out.data_ptr(),
+        )
+        self._call("mie_prefill_norm", args)
+
+    @torch.no_grad()
+    def run(self, token_ids: torch.Tensor, cache) -> torch.Tensor:
+        """Prefill ``token_ids`` [1, T] into the empty ``cache``; returns the
+        logits [1, T, vocab] (model dtype) like ``Model.forward``."""
+        cfg, m, dev = self.cfg, self.model, self.device
+        T = token_ids.shape[1]
+        D, H, hd, E, Hx, V = cfg.hidden_dim, cfg.num_heads, cfg.head_dim, cfg.num_experts, cfg.expert_hidden, cfg.vocab_size
+        if hasattr(cache, "allocator"):
+            cache.reserve(T)
+        ids = token_ids[0].to(dev, torch.int64).contiguous()
+        lo, hi = torch.aminmax(ids)
+        if int(lo) < 0 or int(hi) >= V:  # the embedding gather reads row ids[t]
+            raise IndexError(f"token id outside [0, {V})")
+        bf, f32, i32 = dict(dtype=torch.bfloat16, device=dev), dict(dtype=torch.float32, device=dev), dict(
+            dtype=torch.int32, device=dev)
+        x = torch.empty(T, D, **f32)
+        xn = torch.empty(T, D, **bf)
+        qkv = torch.empty(T, 3 * D, **f32)
+        q, k, v = (torch.empty(H, T, hd, **bf) for _ in range(3))
+        o = torch.empty(T, D, **bf)
+        counts = torch.zeros(E, **i32)
+        wts = torch.empty(T, 2, **f32)
+        sel = torch.empty(T, 2, **i32)
+        rows = torch.empty(T, 2, **i32)
+        cap = T
+        gathered = torch.empty(E * cap, D, **bf)
+        hbuf = torch.empty(E * cap, Hx, **bf)
+        ybuf = torch.empty(E * cap, D, **f32)
+        rope = m.rope
+        for i, block in enumerate(m.MoEBlocks):
+            att, moe = block.attention, block.moe
+            an = block.attn_norm
+            self._norm(x, an.weight, getattr(an, "bias", None), xn, T, ids=ids if i == 0 else None)
+            gemm(xn, att.in_proj_weight, out=qkv)
+            kc, vc, table, bs, sb, sh, st = _kv_layout(cache, i)
+            self._call("mie_prefill_rope_kv", capi.PrefillRopeArgs(
+                tokens=T, num_heads=H, head_dim=hd, pos0=0, qkv=qkv.data_ptr(),
+                rope_cos=rope[0].data_ptr() if rope else None, rope_sin=rope[1].data_ptr() if rope else None,
+                q_out=q.data_ptr(), k_out=k.data_ptr(), v_out=v.data_ptr(), k_cache=kc.data_ptr(),
+                v_cache=vc.data_ptr(), block_table=capi.ptr(table), block_size=bs, kv_stride_block=sb,
+                kv_stride_head=sh, kv_stride_tok=st))
+            attn = torch.nn.functional.scaled_dot_product_attention(q[None], k[None], v[None], is_causal=True)
+            o.copy_(attn[0].transpose(0, 1).reshape(T, D))
+            gemm(o, att.out_proj.weight, out=x, epilogue=capi.GEMM_RESID, resid=x)
+            mn = block.moe_norm
+            self._norm(x, mn.weight, getattr(mn, "bias", None), xn, T)
+            counts.zero_()
+            self._call("mie_prefill_route", capi.PrefillRouteArgs(
+                tokens=T, hidden_dim=D, num_experts=E, group_rows=cap, x=xn.data_ptr(), x_res=x.data_ptr(),
+                norm=capi.MIE_NORM_RMS if cfg.norm == "rms" else capi.MIE_NORM_LAYER, eps=cfg.norm_eps,
+                norm_w=mn.weight.data_ptr(), norm_b=capi.ptr(getattr(mn, "bias", None)),
+                router_w=moe.router.weight.data_ptr(), logits=None, counts=counts.data_ptr(),
+                weights=wts.data_ptr(), ids_out=sel.data_ptr(), rows_out=rows.data_ptr(),
+                gathered=gathered.data_ptr()))
+            s = moe._expert_storage
+            w1, w3, w2 = s["w1"].view(E * Hx, D), s["w3"].view(E * Hx, D), s["w2"].view(E * D, Hx)
+            gemm(gathered, w1, b2=w3, out=hbuf, epilogue=capi.GEMM_SWIGLU, counts=counts, groups=E, rows=cap,
+                 a_group_rows=cap, b_group_rows=Hx, c_group_rows=cap)
+            gemm(hbuf, w2, out=ybuf, counts=counts, groups=E, rows=cap, a_group_rows=cap, b_group_rows=D,
+                 c_group_rows=cap)
+            self._call("mie_prefill_combine", capi.PrefillCombineArgs(
+                tokens=T, hidden_dim=D, x=x.data_ptr(), y=ybuf.data_ptr(), ldy=ybuf.stride(0),
+                weights=wts.data_ptr(), rows=rows.data_ptr()))
+        fn = m.final_norm
+        self._norm(x, fn.weight, getattr(fn, "bias", None), xn, T)
+        logits = gemm(xn, m.token_embedding.weight)
+        cache.position += T
+        return logits.to(torch.bfloat16).view(1, T, V)
