@@ -523,6 +523,23 @@ def run_profile(steps: int):
     print(json.dumps({"profile_steps": steps, "tokens": int(runner.log_count.item())}), flush=True)
 
 
+def run_profile_prefill(reps: int):
+    """Profiling workload (``--profile-prefill N``): the bench's model and
+    512-token prompt prefilled N times into fresh paged caches (tensor-core
+    GEMMs of the prefill); no timing."""
+    device = torch.device("cuda", 0)
+    model = build_model(device, torch.bfloat16)
+    prompt = torch.randint(0, 50304, (PROMPT_LEN,), generator=torch.Generator().manual_seed(3))
+    alloc = model.new_block_allocator(num_blocks=-(-PROMPT_LEN // 16) + 8, block_size=16, attention_mode="direct")
+    for _ in range(reps):
+        cache = alloc.new_cache()
+        with torch.no_grad():
+            model(prompt[None].to(device), cache)
+        cache.free()
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_prefill": reps, "prompt": PROMPT_LEN}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -535,9 +552,14 @@ def main():
                     help="N>1: independent replicas (default) or one request expert parallel")
     ap.add_argument("--profile", type=int, default=0, metavar="N",
                     help="profiling workload: N decode steps after the prompt, no timing")
+    ap.add_argument("--profile-prefill", type=int, default=0, metavar="N",
+                    help="profiling workload: N prefills of the 512-token prompt, no timing")
     args = ap.parse_args()
     if args.profile:
         run_profile(args.profile)
+        return
+    if args.profile_prefill:
+        run_profile_prefill(args.profile_prefill)
         return
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")

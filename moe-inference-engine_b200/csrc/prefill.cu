@@ -32,47 +32,56 @@ __global__ void __launch_bounds__(kPfThreads) prefill_norm_kernel(const mie_pref
   if (t >= a.tokens) return;
   const int D = a.hidden_dim;
   float* xr = a.x + (int64_t)t * D;
-  float v[kPfMaxDim / 32];
+  constexpr int kPer = kPfMaxDim / 32;
+  float v[kPer];
   const int per = D / 32;
   if (a.ids) {
     const int64_t id = a.ids[t];
     const __nv_bfloat16* e = static_cast<const __nv_bfloat16*>(a.embedding) + id * D;
     const __nv_bfloat16* pe =
         a.pos_embedding ? static_cast<const __nv_bfloat16*>(a.pos_embedding) + (int64_t)(a.pos0 + t) * D : nullptr;
-#pragma unroll 4
-    for (int j = 0; j < per; ++j) {
-      const int i = lane + 32 * j;
-      float y = bf(e, i);
-      if (pe) y += bf(pe, i);
-      v[j] = y;
-      xr[i] = y;
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      if (j < per) {
+        const int i = lane + 32 * j;
+        float y = bf(e, i);
+        if (pe) y += bf(pe, i);
+        v[j] = y;
+        xr[i] = y;
+      }
     }
   } else {
-#pragma unroll 4
-    for (int j = 0; j < per; ++j) v[j] = xr[lane + 32 * j];
+#pragma unroll
+    for (int j = 0; j < kPer; ++j)
+      if (j < per) v[j] = xr[lane + 32 * j];
   }
   const __nv_bfloat16* w = static_cast<const __nv_bfloat16*>(a.w);
   const __nv_bfloat16* b = static_cast<const __nv_bfloat16*>(a.b);
   __nv_bfloat16* out = static_cast<__nv_bfloat16*>(a.out) + (int64_t)t * D;
-  float mean = 0.f, rs;
+  float mean = 0.f, q = 0.f;
   if (a.norm == MIE_NORM_LAYER) {
-    float s = 0.f;
-    for (int j = 0; j < per; ++j) s += v[j];
-    mean = warp_sum(s) / (float)D;
-    float q = 0.f;
-    for (int j = 0; j < per; ++j) q = fmaf(v[j] - mean, v[j] - mean, q);
-    rs = rsqrtf(warp_sum(q) / (float)D + a.eps);
+    float sm = 0.f;
+#pragma unroll
+    for (int j = 0; j < kPer; ++j)
+      if (j < per) sm += v[j];
+    mean = warp_sum(sm) / (float)D;
+#pragma unroll
+    for (int j = 0; j < kPer; ++j)
+      if (j < per) q = fmaf(v[j] - mean, v[j] - mean, q);
   } else {
-    float q = 0.f;
-    for (int j = 0; j < per; ++j) q = fmaf(v[j], v[j], q);
-    rs = rsqrtf(warp_sum(q) / (float)D + a.eps);
+#pragma unroll
+    for (int j = 0; j < kPer; ++j)
+      if (j < per) q = fmaf(v[j], v[j], q);
   }
-#pragma unroll 4
-  for (int j = 0; j < per; ++j) {
-    const int i = lane + 32 * j;
-    float y = (v[j] - mean) * rs * bf(w, i);
-    if (b) y += bf(b, i);
-    out[i] = __float2bfloat16_rn(y);
+  const float rs = rsqrtf(warp_sum(q) / (float)D + a.eps);
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    if (j < per) {
+      const int i = lane + 32 * j;
+      float y = (v[j] - mean) * rs * bf(w, i);
+      if (b) y += bf(b, i);
+      out[i] = __float2bfloat16_rn(y);
+    }
   }
 }
 
@@ -134,35 +143,47 @@ __global__ void __launch_bounds__(kPfThreads) prefill_route_kernel(const mie_pre
   const __nv_bfloat16* rw = static_cast<const __nv_bfloat16*>(a.router_w);
   // the router sees the normalised residual in fp32 (the bf16 copy feeds the
   // expert GEMMs): routing decisions as close to an fp32 forward as possible
-  float xv[kPfMaxDim / 32];
+  constexpr int kPer = kPfMaxDim / 32;
+  float xv[kPer];
   const float* xf = a.x_res + (int64_t)t * D;
-#pragma unroll 4
-  for (int j = 0; j < per; ++j) xv[j] = xf[lane + 32 * j];
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) xv[j] = j < per ? xf[lane + 32 * j] : 0.f;
   {
     const __nv_bfloat16* nw = static_cast<const __nv_bfloat16*>(a.norm_w);
     const __nv_bfloat16* nb = static_cast<const __nv_bfloat16*>(a.norm_b);
     float mean = 0.f, q = 0.f;
     if (a.norm == MIE_NORM_LAYER) {
       float sm = 0.f;
-      for (int j = 0; j < per; ++j) sm += xv[j];
+#pragma unroll
+      for (int j = 0; j < kPer; ++j) sm += xv[j];
       mean = warp_sum(sm) / (float)D;
-      for (int j = 0; j < per; ++j) q = fmaf(xv[j] - mean, xv[j] - mean, q);
+#pragma unroll
+      for (int j = 0; j < kPer; ++j)
+        if (j < per) q = fmaf(xv[j] - mean, xv[j] - mean, q);
     } else {
-      for (int j = 0; j < per; ++j) q = fmaf(xv[j], xv[j], q);
+#pragma unroll
+      for (int j = 0; j < kPer; ++j) q = fmaf(xv[j], xv[j], q);
     }
     const float rs = rsqrtf(warp_sum(q) / (float)D + a.eps);
-    for (int j = 0; j < per; ++j) {
-      const int i = lane + 32 * j;
-      float y = (xv[j] - mean) * rs * bf(nw, i);
-      if (nb) y += bf(nb, i);
-      xv[j] = y;
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      if (j < per) {
+        const int i = lane + 32 * j;
+        float y = (xv[j] - mean) * rs * bf(nw, i);
+        if (nb) y += bf(nb, i);
+        xv[j] = y;
+      }
     }
   }
   // lane e ends up holding logit e (E <= 32)
   float mine = -INFINITY;
+#pragma unroll 1
   for (int e = 0; e < E; ++e) {
+    const __nv_bfloat16* we = rw + (int64_t)e * D + lane;
     float s = 0.f;
-    for (int j = 0; j < per; ++j) s = fmaf(xv[j], bf(rw, (int64_t)e * D + lane + 32 * j), s);
+#pragma unroll
+    for (int j = 0; j < kPer; ++j)
+      if (j < per) s = fmaf(xv[j], bf(we, 32 * j), s);
     s = warp_sum(s);
     if (lane == e) mine = s;
   }
@@ -207,6 +228,7 @@ __global__ void __launch_bounds__(kPfThreads) prefill_route_kernel(const mie_pre
   r1 = __shfl_sync(0xffffffffu, r1, 0);
   __nv_bfloat16* g0 = static_cast<__nv_bfloat16*>(a.gathered) + (int64_t)r0 * D;
   __nv_bfloat16* g1 = static_cast<__nv_bfloat16*>(a.gathered) + (int64_t)r1 * D;
+#pragma unroll 4
   for (int j = 0; j < per; ++j) {
     const int i = lane + 32 * j;
     g0[i] = xr[i];
@@ -221,8 +243,19 @@ __global__ void __launch_bounds__(kPfThreads) prefill_combine_kernel(const mie_p
   const float w0 = a.weights[2 * t], w1 = a.weights[2 * t + 1];
   const float* y0 = a.y + (int64_t)a.rows[2 * t] * a.ldy;
   const float* y1 = a.y + (int64_t)a.rows[2 * t + 1] * a.ldy;
-  float* xr = a.x + (int64_t)t * D;
-  for (int i = lane; i < D; i += 32) xr[i] = fmaf(w1, y1[i], fmaf(w0, y0[i], xr[i]));
+  float4* xr = reinterpret_cast<float4*>(a.x + (int64_t)t * D);
+  const float4* a0 = reinterpret_cast<const float4*>(y0);
+  const float4* a1 = reinterpret_cast<const float4*>(y1);
+#pragma unroll 2
+  for (int i = lane; i < D / 4; i += 32) {
+    const float4 u = a0[i], v = a1[i];
+    float4 x = xr[i];
+    x.x = fmaf(w1, v.x, fmaf(w0, u.x, x.x));
+    x.y = fmaf(w1, v.y, fmaf(w0, u.y, x.y));
+    x.z = fmaf(w1, v.z, fmaf(w0, u.z, x.z));
+    x.w = fmaf(w1, v.w, fmaf(w0, u.w, x.w));
+    xr[i] = x;
+  }
 }
 
 unsigned grid_for(int items) { return (unsigned)((items + kPfWarps - 1) / kPfWarps); }
@@ -252,7 +285,8 @@ int prefill_route(const mie_prefill_route_args& a, cudaStream_t st) {
 }
 
 int prefill_combine(const mie_prefill_combine_args& a, cudaStream_t st) {
-  if (a.tokens <= 0 || a.hidden_dim <= 0 || !a.x || !a.y || !a.weights || !a.rows || a.ldy < a.hidden_dim)
+  if (a.tokens <= 0 || a.hidden_dim <= 0 || a.hidden_dim % 4 || a.ldy % 4 || !a.x || !a.y || !a.weights || !a.rows ||
+      a.ldy < a.hidden_dim || (reinterpret_cast<uintptr_t>(a.x) | reinterpret_cast<uintptr_t>(a.y)) % 16)
     return MIE_ERR_INVALID;
   return launch(prefill_combine_kernel, dim3(grid_for(a.tokens)), dim3(kPfThreads), 0, st, false, a);
 }
