@@ -632,7 +632,10 @@ __device__ __noinline__ void gemv(const uint4* rows, int n, int nvec, const floa
   const float* xb = (x1 && (int)(threadIdx.x >> 5) >= split) ? x1 : x;
   float xr[Seg<W>::kNV * PV];
   load_x_regs<W>(xr, xb, nvec);
-  gemv_rows<W, kGlobal, 2>(rows, n, nvec, xr, out);
+  if (Seg<W>::kNV <= 3 && n == 4 * kSW)
+    gemv_rows<W, kGlobal, Seg<W>::kNV <= 3 ? 4 : 2>(rows, n, nvec, xr, out);  // LM-head stages: 4 rows per warp
+  else
+    gemv_rows<W, kGlobal, 2>(rows, n, nvec, xr, out);
 }
 
 template <typename W>
