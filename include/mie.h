@@ -318,8 +318,9 @@ enum {
   MIE_GEMM_F32 = 0,    /* C fp32 */
   MIE_GEMM_BF16 = 1,   /* C bf16 */
   MIE_GEMM_RESID = 2,  /* C fp32 = resid + A.B^T (resid may alias C) */
-  MIE_GEMM_SWIGLU = 3  /* B = gate rows, b2 = up rows; N counts gate + up
+  MIE_GEMM_SWIGLU = 3, /* B = gate rows, b2 = up rows; N counts gate + up
                           columns; C bf16 [.., N / 2] = silu(A.B^T) * (A.B2^T) */
+  MIE_GEMM_GELU = 4    /* C bf16 = gelu_erf(A.B^T + bias) */
 };
 typedef struct mie_gemm_args {
   const void* a;        /* bf16 */
@@ -338,6 +339,9 @@ typedef struct mie_gemm_args {
   int groups;
   int a_group_rows, b_group_rows, c_group_rows;
   int32_t* status;      /* optional device status word */
+  const void* bias;     /* optional bf16 per-column bias (all but SwiGLU); group g
+                           uses bias + g * bias_group_stride */
+  int64_t bias_group_stride;
 } mie_gemm_args;
 
 /* Prefill per-token kernels (one warp per token; residual stream fp32, GEMM

@@ -13,8 +13,9 @@
 //               tcgen05.commit to the stage's "empty" mbarrier;
 //   warps 2-5   wait for the final commit, read the accumulator with
 //               tcgen05.ld (warp w reads TMEM lanes 32 (w % 4) ...) and apply
-//               the epilogue: fp32 / bf16 store, fp32 residual add, SwiGLU of
-//               a gate half and an up half of the tile.
+//               the epilogue: optional per-column bias, then fp32 / bf16
+//               store, fp32 residual add, GELU (erf), or SwiGLU of a gate half
+//               and an up half of the tile.
 // Grouped mode (blockIdx.z = group, e.g. an expert): A, B and C rows are
 // offset by a per-group stride and rows at or past the group's count (read on
 // the device) are neither computed into C nor stored.
@@ -104,6 +105,7 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int n) {
 }
 
 __device__ __forceinline__ float silu_f(float v) { return v / (1.0f + expf(-v)); }
+__device__ __forceinline__ float gelu_f(float v) { return 0.5f * v * (1.0f + erff(v * 0.7071067811865476f)); }
 
 template <int BN, int EPI>
 __global__ void __launch_bounds__(kGemmThreads, 1)
@@ -207,12 +209,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
         }
       } else {
+        const __nv_bfloat16* bias = args.bias ? args.bias + (int64_t)g * args.bias_group_stride + n0 : nullptr;
 #pragma unroll 1
         for (int c = 0; c < BN; c += 32) {
           float v[32];
           tmem_ld32(tbase + c, v);
+          if (bias) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] += __bfloat162float(bias[c + i]);
+          }
           if (row < rows) {
-            if constexpr (EPI == kEpiBF16) {
+            if constexpr (EPI == kEpiBF16 || EPI == kEpiGelu) {
+              if constexpr (EPI == kEpiGelu) {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) v[i] = gelu_f(v[i]);
+              }
               __nv_bfloat16* out = static_cast<__nv_bfloat16*>(args.c) + crow * args.ldc + n0 + c;
 #pragma unroll
               for (int i = 0; i < 32; i += 2)
@@ -300,13 +311,15 @@ void gemm_set_attributes() {
                        gemm_smem<128, kEpiResid>());
   cudaFuncSetAttribute(gemm_kernel<128, kEpiSwiGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        gemm_smem<128, kEpiSwiGLU>());
+  cudaFuncSetAttribute(gemm_kernel<128, kEpiGelu>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       gemm_smem<128, kEpiGelu>());
 }
 
 // C[g] = A[g] . B[g]^T for the groups of a (see mie_gemm_args).
 int gemm_run(const mie_gemm_args& a, cudaStream_t st) {
   if (a.M <= 0 || a.N <= 0 || a.K <= 0 || a.K % kBK || a.N % 128 || a.groups <= 0) return MIE_ERR_UNSUPPORTED;
-  if (!a.a || !a.b || !a.c || (a.epilogue == kEpiSwiGLU && !a.b2) || (a.epilogue == kEpiResid && !a.resid) ||
-      a.epilogue < kEpiF32 || a.epilogue > kEpiSwiGLU)
+  if (!a.a || !a.b || !a.c || (a.epilogue == kEpiSwiGLU && (!a.b2 || a.bias)) ||
+      (a.epilogue == kEpiResid && !a.resid) || a.epilogue < kEpiF32 || a.epilogue > kEpiGelu)
     return MIE_ERR_INVALID;
   const bool grouped = a.groups > 1 || a.counts;
   if (grouped && (a.a_group_rows < a.M || a.c_group_rows < a.M)) return MIE_ERR_INVALID;
@@ -316,7 +329,7 @@ int gemm_run(const mie_gemm_args& a, cudaStream_t st) {
   const int out_cols = a.epilogue == kEpiSwiGLU ? a.N / 2 : a.N;
   if (a.ldc < out_cols || (a.epilogue == kEpiResid && a.ldr < a.N)) return MIE_ERR_INVALID;
   // epilogue stores: 16-byte fp32 vectors, 4-byte bf16 pairs
-  const bool f32_out = a.epilogue == kEpiF32 || a.epilogue == kEpiResid;
+  const bool f32_out = a.epilogue == kEpiF32 || a.epilogue == kEpiResid;  // else bf16 out
   const uintptr_t cal = reinterpret_cast<uintptr_t>(a.c) | reinterpret_cast<uintptr_t>(a.resid) |
                         (uintptr_t)(a.ldc * (f32_out ? 4 : 2)) | (uintptr_t)(a.ldr * 4);
   if (cal % (f32_out ? 16 : 4)) return MIE_ERR_INVALID;
@@ -340,6 +353,8 @@ int gemm_run(const mie_gemm_args& a, cudaStream_t st) {
   g.b_group_rows = grouped ? a.b_group_rows : 0;
   g.c_group_rows = grouped ? a.c_group_rows : 0;
   g.status = a.status;
+  g.bias = static_cast<const __nv_bfloat16*>(a.bias);
+  g.bias_group_stride = grouped ? a.bias_group_stride : 0;
   switch (a.epilogue) {
     case kEpiF32:
       return gemm_launch_t<128, kEpiF32>(ma, mb, mb2, g, a.groups, st);
@@ -347,6 +362,8 @@ int gemm_run(const mie_gemm_args& a, cudaStream_t st) {
       return gemm_launch_t<128, kEpiBF16>(ma, mb, mb2, g, a.groups, st);
     case kEpiResid:
       return gemm_launch_t<128, kEpiResid>(ma, mb, mb2, g, a.groups, st);
+    case kEpiGelu:
+      return gemm_launch_t<128, kEpiGelu>(ma, mb, mb2, g, a.groups, st);
     default:
       return gemm_launch_t<128, kEpiSwiGLU>(ma, mb, mb2, g, a.groups, st);
   }

@@ -2,6 +2,7 @@
 #pragma once
 
 #include <cuda_runtime.h>
+#include <cuda_bf16.h>
 #include <stdint.h>
 
 #include <utility>
@@ -140,7 +141,13 @@ int step_launch(const mie_step_desc& d, const StepGeom& g, uint64_t* scratch, cu
 void step_set_attributes();
 
 // gemm.cu (prefill GEMM on the tensor cores)
-enum { kEpiF32 = MIE_GEMM_F32, kEpiBF16 = MIE_GEMM_BF16, kEpiResid = MIE_GEMM_RESID, kEpiSwiGLU = MIE_GEMM_SWIGLU };
+enum {
+  kEpiF32 = MIE_GEMM_F32,
+  kEpiBF16 = MIE_GEMM_BF16,
+  kEpiResid = MIE_GEMM_RESID,
+  kEpiSwiGLU = MIE_GEMM_SWIGLU,
+  kEpiGelu = MIE_GEMM_GELU
+};
 // Device-side arguments of one GEMM launch (the tensor maps travel separately).
 struct GemmArgs {
   int M, N, K;
@@ -151,6 +158,8 @@ struct GemmArgs {
   const int32_t* counts;
   int a_group_rows, b_group_rows, c_group_rows;
   int32_t* status;
+  const __nv_bfloat16* bias;
+  int64_t bias_group_stride;
 };
 int gemm_run(const mie_gemm_args& a, cudaStream_t st);
 void gemm_set_attributes();

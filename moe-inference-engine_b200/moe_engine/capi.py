@@ -106,7 +106,7 @@ class StepDesc(ctypes.Structure):
     ]
 
 
-GEMM_F32, GEMM_BF16, GEMM_RESID, GEMM_SWIGLU = 0, 1, 2, 3
+GEMM_F32, GEMM_BF16, GEMM_RESID, GEMM_SWIGLU, GEMM_GELU = 0, 1, 2, 3, 4
 
 
 class GemmArgs(ctypes.Structure):
@@ -114,7 +114,7 @@ class GemmArgs(ctypes.Structure):
         ("a", _p), ("lda", _i64), ("b", _p), ("b2", _p), ("ldb", _i64), ("b_rows", _i64), ("c", _p),
         ("ldc", _i64), ("resid", _p), ("ldr", _i64), ("counts", _p), ("M", _i), ("N", _i), ("K", _i),
         ("epilogue", _i), ("groups", _i), ("a_group_rows", _i), ("b_group_rows", _i),
-        ("c_group_rows", _i), ("status", _p),
+        ("c_group_rows", _i), ("status", _p), ("bias", _p), ("bias_group_stride", _i64),
     ]
 
 

@@ -21,7 +21,8 @@ from . import capi
 def gemm(a: torch.Tensor, b: torch.Tensor, *, out: torch.Tensor | None = None, epilogue: int = capi.GEMM_F32,
          b2: torch.Tensor | None = None, resid: torch.Tensor | None = None, counts: torch.Tensor | None = None,
          groups: int = 1, rows: int | None = None, a_group_rows: int = 0, b_group_rows: int = 0,
-         c_group_rows: int = 0, status: torch.Tensor | None = None) -> torch.Tensor:
+         c_group_rows: int = 0, status: torch.Tensor | None = None, bias: torch.Tensor | None = None,
+         bias_group_stride: int = 0) -> torch.Tensor:
     """C = A . B^T on the tensor cores (see ``mie_gemm_args`` in include/mie.h).
 
     ``a`` [rows, K] and ``b`` [N, K] (``b2`` [N, K] gate/up pair for SwiGLU,
@@ -31,6 +32,8 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, out: torch.Tensor | None = None, e
     """
     if a.dtype != torch.bfloat16 or b.dtype != torch.bfloat16:
         raise ValueError("mie_gemm takes bf16 operands")
+    if bias is not None and (bias.dtype != torch.bfloat16 or not bias.is_contiguous()):
+        raise ValueError("mie_gemm takes a contiguous bf16 bias")
     if a.dim() != 2 or b.dim() != 2 or a.stride(1) != 1 or b.stride(1) != 1:
         raise ValueError("mie_gemm takes row-major 2-D operands")
     K = a.shape[1]
@@ -48,14 +51,15 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, out: torch.Tensor | None = None, e
         out_cols = N
     if out is None:
         out_rows = groups * c_group_rows if grouped else M
-        dt = torch.bfloat16 if epilogue in (capi.GEMM_BF16, capi.GEMM_SWIGLU) else torch.float32
+        dt = torch.bfloat16 if epilogue in (capi.GEMM_BF16, capi.GEMM_SWIGLU, capi.GEMM_GELU) else torch.float32
         out = torch.empty(out_rows, out_cols, device=a.device, dtype=dt)
     args = capi.GemmArgs(
         a=a.data_ptr(), lda=a.stride(0), b=b.data_ptr(), b2=capi.ptr(b2), ldb=b.stride(0),
         b_rows=b.shape[0], c=out.data_ptr(), ldc=out.stride(0), resid=capi.ptr(resid),
         ldr=resid.stride(0) if resid is not None else 0, counts=capi.ptr(counts), M=M, N=N, K=K,
         epilogue=epilogue, groups=groups, a_group_rows=a_group_rows, b_group_rows=b_group_rows,
-        c_group_rows=c_group_rows, status=capi.ptr(status),
+        c_group_rows=c_group_rows, status=capi.ptr(status), bias=capi.ptr(bias),
+        bias_group_stride=bias_group_stride,
     )
     lib = capi.ensure_init(a.device)
     capi.check(lib.mie_gemm(ctypes.byref(args), capi.stream_handle(a.device)), "mie_gemm")
@@ -76,12 +80,14 @@ def _kv_layout(cache, layer: int):
 class PrefillRunner:
     """Prompt prefill of a bf16 model on the sm_100a kernels.
 
-    Per layer: norm -> QKV GEMM -> RoPE + K/V cache write -> causal attention
-    (PyTorch SDPA over the fresh K/V, as the reference's prefill fast path,
-    model.py:252-256) -> out_proj GEMM + residual -> norm -> router, top-2 and
-    per-expert row gather -> grouped SwiGLU up GEMM -> grouped down GEMM ->
-    weighted combine.  Then the final norm and the tied LM head GEMM for every
-    position.  The residual stream stays fp32.
+    Per layer: norm -> QKV GEMM (+ bias) -> RoPE + K/V cache write -> causal
+    attention (PyTorch SDPA over the fresh K/V, as the reference's prefill
+    fast path, model.py:252-256) -> out_proj GEMM (+ bias) + residual -> norm
+    -> router, top-2 and per-expert row gather -> grouped up GEMM (SwiGLU, or
+    bias + GELU) -> grouped down GEMM (+ bias) -> weighted combine.  Then the
+    final norm and the tied LM head GEMM (+ bias) for every position.  The
+    residual stream stays fp32.  Both the BASELINE architecture and the
+    reference's own (LayerNorm, learned positions, biased GELU experts).
     """
 
     @staticmethod
@@ -100,9 +106,11 @@ class PrefillRunner:
         if not hasattr(cache, "allocator") and cache.k.shape[1] != 1:
             return False
         D, Hx, V = cfg.hidden_dim, cfg.expert_hidden, cfg.vocab_size
-        if cfg.expert_act != "swiglu" or cfg.bias or cfg.top_k != 2 or not 2 <= cfg.num_experts <= 32:
+        if cfg.top_k != 2 or not 2 <= cfg.num_experts <= 32:
             return False
-        if D % 128 or D > 1024 or Hx % 64 or V % 128 or cfg.num_heads * cfg.head_dim != D:
+        # GEMM shapes: K a multiple of 64, N a multiple of 128 (SwiGLU: 2 Hx)
+        hx_align = 64 if cfg.expert_act == "swiglu" else 128
+        if D % 128 or D > 1024 or Hx % hx_align or V % 128 or cfg.num_heads * cfg.head_dim != D:
             return False
         if any(block.moe.mode == "reference" for block in model.MoEBlocks):
             return False
@@ -161,7 +169,7 @@ class PrefillRunner:
             att, moe = block.attention, block.moe
             an = block.attn_norm
             self._norm(x, an.weight, getattr(an, "bias", None), xn, T, ids=ids if i == 0 else None)
-            gemm(xn, att.in_proj_weight, out=qkv)
+            gemm(xn, att.in_proj_weight, out=qkv, bias=att.in_proj_bias)
             kc, vc, table, bs, sb, sh, st = _kv_layout(cache, i)
             self._call("mie_prefill_rope_kv", capi.PrefillRopeArgs(
                 tokens=T, num_heads=H, head_dim=hd, pos0=0, qkv=qkv.data_ptr(),
@@ -171,7 +179,7 @@ class PrefillRunner:
                 kv_stride_head=sh, kv_stride_tok=st))
             attn = torch.nn.functional.scaled_dot_product_attention(q[None], k[None], v[None], is_causal=True)
             o.copy_(attn[0].transpose(0, 1).reshape(T, D))
-            gemm(o, att.out_proj.weight, out=x, epilogue=capi.GEMM_RESID, resid=x)
+            gemm(o, att.out_proj.weight, out=x, epilogue=capi.GEMM_RESID, resid=x, bias=att.out_proj.bias)
             mn = block.moe_norm
             self._norm(x, mn.weight, getattr(mn, "bias", None), xn, T)
             counts.zero_()
@@ -183,16 +191,23 @@ class PrefillRunner:
                 weights=wts.data_ptr(), ids_out=sel.data_ptr(), rows_out=rows.data_ptr(),
                 gathered=gathered.data_ptr()))
             s = moe._expert_storage
-            w1, w3, w2 = s["w1"].view(E * Hx, D), s["w3"].view(E * Hx, D), s["w2"].view(E * D, Hx)
-            gemm(gathered, w1, b2=w3, out=hbuf, epilogue=capi.GEMM_SWIGLU, counts=counts, groups=E, rows=cap,
-                 a_group_rows=cap, b_group_rows=Hx, c_group_rows=cap)
-            gemm(hbuf, w2, out=ybuf, counts=counts, groups=E, rows=cap, a_group_rows=cap, b_group_rows=D,
-                 c_group_rows=cap)
+            w1, w2 = s["w1"].view(E * Hx, D), s["w2"].view(E * D, Hx)
+            grouped = dict(counts=counts, groups=E, rows=cap, a_group_rows=cap, c_group_rows=cap)
+            if "w3" in s:
+                gemm(gathered, w1, b2=s["w3"].view(E * Hx, D), out=hbuf, epilogue=capi.GEMM_SWIGLU,
+                     b_group_rows=Hx, **grouped)
+            else:
+                b1 = s.get("b1")
+                gemm(gathered, w1, out=hbuf, epilogue=capi.GEMM_GELU, b_group_rows=Hx,
+                     bias=b1.reshape(-1) if b1 is not None else None, bias_group_stride=Hx, **grouped)
+            b2 = s.get("b2")
+            gemm(hbuf, w2, out=ybuf, b_group_rows=D, bias=b2.reshape(-1) if b2 is not None else None,
+                 bias_group_stride=D, **grouped)
             self._call("mie_prefill_combine", capi.PrefillCombineArgs(
                 tokens=T, hidden_dim=D, x=x.data_ptr(), y=ybuf.data_ptr(), ldy=ybuf.stride(0),
                 weights=wts.data_ptr(), rows=rows.data_ptr()))
         fn = m.final_norm
         self._norm(x, fn.weight, getattr(fn, "bias", None), xn, T)
-        logits = gemm(xn, m.token_embedding.weight)
+        logits = gemm(xn, m.token_embedding.weight, bias=m.output_projection.bias)
         cache.position += T
         return logits.to(torch.bfloat16).view(1, T, V)

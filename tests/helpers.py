@@ -49,3 +49,32 @@ def make_pair(kind: str = "reference", seed: int = 0, device="cpu", dtype=torch.
 def load_into(model: Model, P: dict) -> Model:
     model.load_state_dict(engine_state_dict(P))
     return model
+
+
+def oracle_prefill_with_margins(P: dict, arch, ids: torch.Tensor, kv_dtype=torch.bfloat16):
+    """The oracle's prompt forward (as ``oracle.Decoder.forward`` from an empty
+    cache) returning (logits [T, vocab], margin [T]): per position the
+    smallest gap, over the layers, between the router's second and third
+    logits -- below ~1e-3 a bf16 computation of the same layer may select
+    another expert pair."""
+    from oracle import minimoe as om
+
+    ids = ids.long().reshape(1, -1)
+    T = ids.shape[1]
+    positions = torch.arange(T)
+    cos = sin = None
+    if arch.pos == "rope":
+        cos, sin = om.rope_tables(arch.max_seq_length, arch.head_dim, arch.rope_base)
+    x = om._embed(P, arch, ids, positions)
+    margin = torch.full((T,), float("inf"))
+    for layer in range(arch.num_layers):
+        h = om.norm(x, P, f"MoEBlocks.{layer}.attn_norm", arch)
+        q, k, v = om._qkv(h, P, layer, arch, positions, cos, sin)
+        k, v = k.to(kv_dtype).float(), v.to(kv_dtype).float()
+        x = x + om._out_proj(om.attention(q, k, v, causal=T > 1), P, layer, arch)
+        h = om.norm(x, P, f"MoEBlocks.{layer}.moe_norm", arch)
+        out, (logits, _, _) = om.moe_forward(h, P, layer, arch)
+        top = logits.sort(dim=-1, descending=True).values
+        margin = torch.minimum(margin, top[:, 1] - top[:, 2])
+        x = x + out
+    return om._lm_head(x, P, arch)[0], margin

@@ -106,3 +106,33 @@ def test_rejects_bad_shapes():
         gemm(a, b[:, :700].contiguous())
     with pytest.raises(Exception):
         gemm(a[:, :96].contiguous(), b[:, :96].contiguous())  # K not a multiple of 64
+
+
+def test_bias_and_gelu_epilogues():
+    a, b = operands(200, 3072, 768, seed=7)
+    bias = (0.1 * torch.randn(3072, generator=torch.Generator().manual_seed(8))).to(DEV, torch.bfloat16)
+    out = gemm(a, b, bias=bias)
+    h = gemm(a, b, bias=bias, epilogue=capi.GEMM_GELU)
+    torch.cuda.synchronize()
+    want = ref(a, b) + bias.float()
+    torch.testing.assert_close(out, want, atol=1e-3, rtol=1e-3)
+    torch.testing.assert_close(h.float(), torch.nn.functional.gelu(want), atol=2e-2, rtol=1e-2)
+
+
+def test_grouped_gelu_with_per_group_bias():
+    """The GELU expert up projection of the reference architecture: hidden 3072,
+    one bias row per expert."""
+    E, cap, H, K = 3, 128, 3072, 768
+    g = torch.Generator().manual_seed(9)
+    a = torch.randn(E * cap, K, generator=g).to(DEV, torch.bfloat16)
+    w1 = (0.02 * torch.randn(E * H, K, generator=g)).to(DEV, torch.bfloat16)
+    b1 = (0.1 * torch.randn(E, H, generator=g)).to(DEV, torch.bfloat16)
+    counts = torch.tensor([100, 0, 128], dtype=torch.int32, device=DEV)
+    h = torch.zeros(E * cap, H, device=DEV, dtype=torch.bfloat16)
+    gemm(a, w1, out=h, epilogue=capi.GEMM_GELU, counts=counts, groups=E, rows=cap, a_group_rows=cap,
+         b_group_rows=H, c_group_rows=cap, bias=b1.reshape(-1), bias_group_stride=H)
+    torch.cuda.synchronize()
+    for e in range(E):
+        n = int(counts[e])
+        want = torch.nn.functional.gelu(ref(a[e * cap:e * cap + n], w1[e * H:(e + 1) * H]) + b1[e].float())
+        torch.testing.assert_close(h[e * cap:e * cap + n].float(), want, atol=2e-2, rtol=1e-2)

@@ -4,12 +4,14 @@ attention) against the CPU oracle and against the PyTorch module path.
 
 * logits of the prompt positions against the oracle run on the same
   bf16-rounded weights with a bf16 K/V cache (relative error, Frobenius over
-  the vocabulary): median below 1e-2, at least 85 % of the positions within
-  2e-2 (the bf16 decode step's tolerance) and every one within 0.15.  The
-  GEMM operands are bf16, so router logits move by ~1e-3; where the oracle's
-  second and third logits lie closer than that (measured at a 40-token
-  prompt: margins of 3e-4 to 3e-3 at 4 of 480 routing decisions) the token
-  takes another expert and its logits move by ~7 %;
+  the vocabulary): within 2e-2 (the bf16 decode step's tolerance) at every
+  position whose router margins are clear (second minus third logit above
+  5e-3 in every layer), median below 1e-2 over all positions.  The GEMM
+  operands are bf16, so router logits move by ~1e-3; where the oracle's second
+  and third logits lie closer than that (measured at a 40-token prompt:
+  margins of 3e-4 to 3e-3 at 4 of 480 routing decisions) the token takes
+  another expert and its logits move by ~7 % (BASELINE) -- not a defect of
+  the kernels but of comparing discrete choices at a tie;
 * the K/V cache the prefill writes equals the module path's: layer 0
   elementwise within 2e-2 (bf16 rounding of differently ordered fp32 sums; the
   module path also rounds q / k to bf16 before RoPE), every layer for at least
@@ -23,7 +25,7 @@ import torch
 
 import oracle
 from moe_engine.model import Model, baseline_config
-from tests.helpers import engine_state_dict
+from tests.helpers import engine_state_dict, oracle_prefill_with_margins
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
@@ -53,12 +55,12 @@ def test_prefill_logits_match_oracle(params, model, n):
     with torch.no_grad():
         got = model(p[None].to(DEV), cache)[0].float().cpu()
     assert cache.position == n
-    dec = oracle.Decoder(oracle.round_params(params, torch.bfloat16), oracle.BASELINE_ARCH, kv_dtype=torch.bfloat16)
-    want = dec.forward(p[None])[0]
+    want, margin = oracle_prefill_with_margins(oracle.round_params(params, torch.bfloat16), oracle.BASELINE_ARCH, p)
     rel = (got - want).norm(dim=-1) / want.norm(dim=-1)
+    clear = margin > 5e-3  # positions whose routing no bf16 rounding can flip
+    assert float(clear.float().mean()) > 0.5  # most positions are checked at 2e-2
+    assert float(rel[clear].max()) < 2e-2, rel
     assert float(rel.median()) < 1e-2, rel
-    assert float((rel < 2e-2).float().mean()) >= 0.85, rel
-    assert float(rel.max()) < 0.15, rel
 
 
 def test_prefill_cache_matches_module_path(model):
