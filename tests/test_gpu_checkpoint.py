@@ -55,6 +55,7 @@ def test_fp32_greedy_tokens_equal_oracle(params, ckpt_path):
     assert (cfg.norm, cfg.pos, cfg.expert_act, cfg.expert_hidden, cfg.head_dim) == ("layer", "learned", "gelu",
                                                                                       3072, 96)
     p = prompt(16)
+    assert model.fused_decode_supported(model.new_cache(), 1)  # decode on the sm_100a kernels
     got = model.generate(p, max_new_tokens=32, temperature=0)[0].tolist()
     want = oracle.generate_greedy(params, ARCH, p, 32)
     assert got == want
