@@ -38,6 +38,10 @@ sys.path.insert(0, os.path.join(REPO, "moe-inference-engine_b200"))
 sys.path.insert(0, REPO)
 
 METRIC = "batch-1 decode tok/s (bf16, config[3]: 512-token prompt + 1024 greedy tokens)"
+# ncu capture of one persistent step launch (--profile 12, 7th step, context 518):
+# dram__bytes_read.sum + dram__bytes_write.sum
+STEP_CAPTURE_DRAM_BYTES = 238.227968e6 + 3.871232e6
+STEP_CAPTURE_CTX = 518
 PROMPT_LEN = 512
 NEW_TOKENS = 1024
 # active weight bytes per token in bf16: 2 B x 109,506,048 active params
@@ -298,13 +302,21 @@ def run_b200(args, rank, world, device):
     persistent = launches_per_token == 1
     # dominant kernel: the persistent step kernel (one launch per token) or,
     # on the per-op path, the fused MoE kernel timed in isolation
+    traffic = None
     if persistent:
         dominant = "step_kernel (persistent decode step, one launch per token)"
         step_bytes = weights_bytes + kv_bytes
         kr = {"us": step_s * 1e6, "gbs": step_bytes / step_s / 1e9, "bytes": step_bytes}
         kr["frac"] = kr["gbs"] / hbm_peak
+        # DRAM bytes of one step launch from the ncu capture summarised in
+        # profiles/step_kernel_persistent_decode.md (context 518), scaled to the
+        # mean context: the same ratio to the algorithmic bytes
+        cap_traffic, cap_alg = STEP_CAPTURE_DRAM_BYTES, weights_bytes + KV_BYTES_PER_CTX * STEP_CAPTURE_CTX
+        traffic = step_bytes * cap_traffic / cap_alg
         roof_note = ("per-launch average of the graph-replayed step over the timed region (CUDA events); "
-                     "algorithmic bytes = active bf16 weights + the K/V bytes at the mean context")
+                     "algorithmic bytes = active bf16 weights + the K/V bytes at the mean context; traffic = "
+                     f"ncu dram read+write of one launch at context {STEP_CAPTURE_CTX} "
+                     f"({cap_traffic / 1e6:.1f} MB), scaled to the mean context by the algorithmic bytes")
     else:
         dominant = "moe_decode"
         kr = k_roof.get(dominant, {"us": None, "gbs": None, "frac": None, "bytes": MOE_LAYER_BYTES})
@@ -351,7 +363,7 @@ def run_b200(args, rank, world, device):
             "peak": hbm_peak,
             "unit": "GB/s",
             "frac": kr["frac"],
-            "traffic": None,
+            "traffic": traffic,
             "algorithmic_bytes_per_launch": kr["bytes"],
             "us_per_launch": kr["us"],
             "peak_source": peak_src,
