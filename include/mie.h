@@ -305,6 +305,16 @@ typedef struct mie_step_desc {
    * for every step; zero it again after a step reported a device failure. */
   uint64_t* step_scratch;
   int64_t step_scratch_bytes;
+  /* Sampling instead of greedy argmax (model.py:604-613), persistent step only
+   * (the per-op launch sequence returns MIE_ERR_UNSUPPORTED for it): with
+   * sample_temperature > 0 the token is drawn from softmax(logits / T),
+   * restricted to the logits >= the sample_top_k-th largest when
+   * 0 < sample_top_k <= 64 (all logits when sample_top_k <= 0), by the
+   * Gumbel-max rule with a counter-based random stream keyed by
+   * (*sample_seed, position, token id). */
+  float sample_temperature;
+  int sample_top_k;
+  const uint64_t* sample_seed;  /* device word, read every step */
 } mie_step_desc;
 
 /* Prefill GEMM on the tcgen05 tensor cores: C = A . B^T with A [M, K] and

@@ -465,6 +465,7 @@ int mie_decode_layer(const mie_step_desc* d, int l, void* stream) {
 
 int mie_decode_head(const mie_step_desc* d, void* stream) {
   if (!d) return MIE_ERR_INVALID;
+  if (d->sample_temperature > 0.f) return MIE_ERR_UNSUPPORTED;  // the device sampler is in the persistent step
   const int rc = check_step(*d);
   if (rc) return rc;
   return run_lmhead(step_lmhead(*d), static_cast<cudaStream_t>(stream), d->use_pdl != 0);
@@ -479,6 +480,7 @@ int mie_decode_step(const mie_step_desc* d, void* stream) {
     if (d->step_scratch_bytes < g.words * (int64_t)sizeof(uint64_t)) return MIE_ERR_INVALID;
     return step_launch(*d, g, d->step_scratch, static_cast<cudaStream_t>(stream));
   }
+  if (d->sample_temperature > 0.f) return MIE_ERR_UNSUPPORTED;  // before any launch
   for (int l = 0; l < d->num_layers; ++l) {
     const int rc = mie_decode_layer(d, l, stream);
     if (rc) return rc;

@@ -44,6 +44,8 @@ constexpr int kMaxStepLayers = 48;                  // layer descriptors carried
 constexpr uint32_t kStepKvChunkBytes = 32 * 1024;   // K+V of one split staged in shared memory at a time
 constexpr int kStepHeadStagesMax = 8;               // LM-head ring stages
 constexpr uint32_t kStepMaxSmem = 223 * 1024;       // dynamic shared memory of the step kernel (static: < 4 KB)
+constexpr int kStepTopKMax = 64;                    // largest top_k of the device sampler
+constexpr int kStepHeadRowsMax = 512;               // LM-head rows of one CTA the top-k sampler sorts
 
 // Geometry of one persistent step launch: exchange-buffer offsets (64-bit
 // words into the caller's scratch) and the shared-memory layout (bytes).
@@ -51,6 +53,7 @@ struct StepGeom {
   uint64_t* ll;   // scratch base
   int64_t words;  // scratch size in 64-bit words
   int64_t off_a[2], off_b[2], off_c[2], off_d[2], off_e[2];
+  int64_t off_cand;  // sampling with top-k: kStepTopKMax candidates per CTA
   int G;          // CTAs (one per SM)
   int S;          // attention splits per head
   int natt;       // attention CTAs (num_heads * S)

@@ -251,6 +251,56 @@ __shared__ int gat_s[kST];  // merge: exchange word index of each received value
 __shared__ int blk_s[kStepBlkCache];  // physical block ids of this CTA's old tokens
 __shared__ float bestv_s[kSW];
 __shared__ int besti_s[kSW];
+
+// ---------------------------------------------------------------------------
+// Device sampler (temperature > 0).  Gumbel-max: argmax_i (l_i / T + G_i) with
+// G_i = -log(-log U_i) draws i with probability softmax(l / T)_i; U_i comes
+// from the SplitMix64 finaliser (Steele, Lea, Flood 2014) of (seed, position,
+// token id), so a step's draw is reproducible and independent of the grid.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float gumbel(uint64_t seed, int pos, int row) {
+  uint64_t z = seed + 0x9E3779B97F4A7C15ull * (((uint64_t)(uint32_t)pos << 32) + (uint64_t)(uint32_t)row + 1u);
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  z ^= z >> 31;
+  const float u = ((float)(z >> 40) + 0.5f) * (1.0f / 16777216.0f);  // (0, 1)
+  return -logf(-logf(u));
+}
+// Sort key of (logit, token): descending key order = larger logit first, then
+// lower token id; 0 sorts below every real logit.
+__device__ __forceinline__ uint64_t logit_key(float v, int row) {
+  uint32_t b = __float_as_uint(v);
+  b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  return ((uint64_t)b << 32) | (uint64_t)(0xFFFFFFFFu - (uint32_t)row);
+}
+__device__ __forceinline__ float key_logit(uint64_t k) {
+  uint32_t b = (uint32_t)(k >> 32);
+  b = (b & 0x80000000u) ? (b & 0x7FFFFFFFu) : ~b;
+  return __uint_as_float(b);
+}
+__device__ __forceinline__ int key_row(uint64_t k) { return (int)(0xFFFFFFFFu - (uint32_t)k); }
+// Descending bitonic sort of keys[0, n) in shared memory (n a power of two),
+// by the whole CTA; ends with a barrier.
+__device__ __noinline__ void sort_keys_desc(uint64_t* keys, int n) {
+  __syncthreads();
+#pragma unroll 1
+  for (int size = 2; size <= n; size <<= 1) {
+#pragma unroll 1
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+#pragma unroll 1
+      for (int t = threadIdx.x; t < n / 2; t += kST) {
+        const int i = 2 * t - (t & (stride - 1)), j = i + stride;  // pair (i, j), i has bit `stride` clear
+        const bool desc = (i & size) == 0;
+        const uint64_t a = keys[i], b = keys[j];
+        if ((a < b) == desc) {
+          keys[i] = b;
+          keys[j] = a;
+        }
+      }
+      __syncthreads();
+    }
+  }
+}
 // mbarriers of the bulk-copy staging, with per-barrier counts of armed and
 // completed phases (a wait uses parity = completed & 1).
 constexpr int kBarAtt = 0, kBarKv = 1, kBarSide = 2, kBarMoe = 3, kBarDown = 4, kBarHead = 5;
@@ -1149,6 +1199,101 @@ __device__ __noinline__ bool moe_phase(const StepParams& P, int l) {
 // head_rows rows over the attention and expert staging areas; the first
 // stages were requested during the last layer.
 // ---------------------------------------------------------------------------
+// Last CTA of the LM head: publish the step's token (device state, token
+// log, EOS flag) and reset the head's counter for the next step (one thread).
+__device__ __noinline__ void head_finish(int bi) {
+  const mie_step_desc& d = ps_s.d;
+  if (bi < 0 || bi >= d.vocab) {  // every logit NaN
+    set_status(d.status, MIE_ERR_RANGE);
+    bi = 0;
+  }
+  *d.token = bi;
+  *d.pos = cx_s.pos + 1;
+  if (d.tokens_log && d.log_count) {
+    const int k = __ldcg(d.log_count);
+    if (k < d.log_capacity) d.tokens_log[k] = bi;
+    *d.log_count = k + 1;
+  }
+  if (d.done && bi == d.eos_id) *d.done = 1;
+  *d.lm_counter = 0u;
+  __threadfence();
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(ps_s.g.ll + kHdrStep), "l"((uint64_t)cx_s.step)
+               : "memory");
+}
+
+// Sampling with top-k (model.py:604-613): this CTA's logits (headv_s) sorted,
+// its top_k candidates published; the last CTA sorts all candidates, keeps
+// the logits >= the top_k-th largest and draws among them by Gumbel-max.
+__device__ __noinline__ bool head_sample_topk(int v0h, int v1h, uint64_t seed, float inv_t) {
+  const mie_step_desc& d = ps_s.d;
+  const StepGeom& g = ps_s.g;
+  const int tid = threadIdx.x, c = blockIdx.x, G = gridDim.x, K = d.sample_top_k, n = v1h - v0h;
+  uint64_t* keys = smem_at<uint64_t>(g.sm_qw);  // the LM-head ring: every stage consumed
+  const float* headv = smem_at<const float>(g.sm_h);  // this CTA's logits (the h vector is free in the head)
+  __syncthreads();
+#pragma unroll 1
+  for (int i = tid; i < kStepHeadRowsMax; i += kST) keys[i] = i < n ? logit_key(headv[i], v0h + i) : 0ull;
+  sort_keys_desc(keys, kStepHeadRowsMax);
+  uint64_t* cand = g.ll + g.off_cand + (int64_t)c * kStepTopKMax;
+  if (tid < K) cand[tid] = keys[tid];
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    cx_s.last = atom_add_acq_rel_gpu(d.lm_counter, 1u) == (uint32_t)(G - 1);
+  }
+  __syncthreads();
+  if (!cx_s.last) return true;
+  __threadfence();
+  const int m = G * K;
+  int n2 = 1;
+  while (n2 < m) n2 <<= 1;
+#pragma unroll 1
+  for (int i = tid; i < n2; i += kST)
+    keys[i] = i < m ? __ldcg(g.ll + g.off_cand + (int64_t)(i / K) * kStepTopKMax + i % K) : 0ull;
+  sort_keys_desc(keys, n2);
+  const float theta = key_logit(keys[K - 1]);
+  float best_v = -INFINITY;
+  int best_i = 0x7fffffff;
+#pragma unroll 1
+  for (int i = tid; i < m; i += kST) {
+    const uint64_t k = keys[i];
+    const float v = key_logit(k);
+    if (k == 0ull || !(v >= theta)) continue;
+    const int row = key_row(k);
+    const float sc = v * inv_t + gumbel(seed, cx_s.pos, row);
+    if (better(sc, row, best_v, best_i)) {
+      best_v = sc;
+      best_i = row;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best_v, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, best_i, o);
+    if (better(ov, oi, best_v, best_i)) {
+      best_v = ov;
+      best_i = oi;
+    }
+  }
+  if ((tid & 31) == 0) {
+    bestv_s[tid >> 5] = best_v;
+    besti_s[tid >> 5] = best_i;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+#pragma unroll 1
+    for (int w = 0; w < kSW; ++w)
+      if (better(bestv_s[w], besti_s[w], bv, bi)) {
+        bv = bestv_s[w];
+        bi = besti_s[w];
+      }
+    head_finish(bi);
+  }
+  return true;
+}
+
 template <typename W>
 __device__ __noinline__ bool head_phase(const StepParams& P) {
   const mie_step_desc& d = ps_s.d;
@@ -1169,6 +1314,11 @@ __device__ __noinline__ bool head_phase(const StepParams& P) {
                     d.final_norm_b ? nw + D : nullptr, ll, d.status))
     return false;
   STEP_STAMP(Lnum, 1);
+  // greedy (temperature 0): argmax of the logits; sampling: argmax of
+  // logit / T + Gumbel noise over every token, or the top-k sampler
+  const bool sample = d.sample_temperature > 0.f, topk = sample && d.sample_top_k > 0;
+  const uint64_t seed = sample ? __ldcg(reinterpret_cast<const unsigned long long*>(d.sample_seed)) : 0ull;
+  const float inv_t = sample ? 1.0f / d.sample_temperature : 0.f;
   float best_v = -INFINITY;
   int best_i = 0x7fffffff;
 #pragma unroll 1
@@ -1184,13 +1334,19 @@ __device__ __noinline__ bool head_phase(const StepParams& P) {
       const int row = r0 + tid;
       if (d.lm_bias) v += ldw<W>(d.lm_bias, row);
       if (d.logits) d.logits[row] = v;
-      if (better(v, row, best_v, best_i)) {
-        best_v = v;
-        best_i = row;
+      if (topk) {
+        smem_at<float>(g.sm_h)[row - v0h] = v;
+      } else {
+        const float sc = sample ? v * inv_t + gumbel(seed, cx_s.pos, row) : v;
+        if (better(sc, row, best_v, best_i)) {
+          best_v = sc;
+          best_i = row;
+        }
       }
     }
   }
   STEP_STAMP(Lnum, 2);
+  if (topk) return head_sample_topk(v0h, v1h, seed, inv_t);
   // CTA argmax: (value, lower index) is a total order, so the reduction
   // order does not change the result
 #pragma unroll
@@ -1244,22 +1400,7 @@ __device__ __noinline__ bool head_phase(const StepParams& P) {
       bi = oi;
     }
   }
-  if (lane != 0) return true;
-  if (bi < 0 || bi >= V) {  // every logit NaN
-    set_status(d.status, MIE_ERR_RANGE);
-    bi = 0;
-  }
-  *d.token = bi;
-  *d.pos = cx_s.pos + 1;
-  if (d.tokens_log && d.log_count) {
-    const int k = __ldcg(d.log_count);
-    if (k < d.log_capacity) d.tokens_log[k] = bi;
-    *d.log_count = k + 1;
-  }
-  if (d.done && bi == d.eos_id) *d.done = 1;
-  *d.lm_counter = 0u;
-  __threadfence();
-  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(ll + kHdrStep), "l"((uint64_t)cx_s.step) : "memory");
+  if (lane == 0) head_finish(bi);
   return true;
 }
 
@@ -1363,6 +1504,11 @@ int step_geometry(const mie_step_desc& d, int grid, StepGeom* g) {
   // work splits use 32-bit products (total * grid < 2^32)
   if ((int64_t)d.vocab * grid >= (1ll << 32) || (int64_t)d.max_pos * grid >= (1ll << 32)) return MIE_ERR_UNSUPPORTED;
   if (d.lm_grid < grid) return MIE_ERR_INVALID;  // per-CTA argmax results
+  if (d.sample_temperature > 0.f) {  // device sampler
+    if (!d.sample_seed || d.sample_top_k > kStepTopKMax) return MIE_ERR_UNSUPPORTED;
+    if (d.sample_top_k > 0 && ((d.vocab + grid - 1) / grid > kStepHeadRowsMax || 2 * d.expert_hidden_dim < kStepHeadRowsMax))
+      return MIE_ERR_UNSUPPORTED;  // the CTA's logits live in the h vector's shared memory
+  }
   StepGeom& G = *g;
   G = StepGeom{};
   G.G = grid;
@@ -1382,6 +1528,7 @@ int step_geometry(const mie_step_desc& d, int grid, StepGeom* g) {
     G.off_d[p] = take(D);
     G.off_e[p] = take(2 * (int64_t)Hx);
   }
+  G.off_cand = take((int64_t)grid * kStepTopKMax);
   G.words = off;
   // work per CTA (upper bounds)
   const int kvw_max = 2 * ((hd / 2 + G.S - 1) / G.S) + (hd + G.S - 1) / G.S;  // k + v rows of one split
@@ -1450,6 +1597,12 @@ int step_geometry(const mie_step_desc& d, int grid, StepGeom* g) {
   if (G.head_stages > kStepHeadStagesMax) G.head_stages = kStepHeadStagesMax;
   if (G.head_stages < 2) return MIE_ERR_UNSUPPORTED;
   G.head_early = (int)(att_bytes / stage_bytes);
+  // the top-k sampler sorts the candidates of every CTA in the ring area
+  if (d.sample_temperature > 0.f && d.sample_top_k > 0) {
+    uint32_t n2 = 1;
+    while (n2 < (uint32_t)(grid * d.sample_top_k) || n2 < (uint32_t)kStepHeadRowsMax) n2 <<= 1;
+    if ((uint64_t)n2 * 8u > ring_bytes) return MIE_ERR_UNSUPPORTED;
+  }
   if (G.head_early > G.head_stages) G.head_early = G.head_stages;
   return MIE_OK;
 }

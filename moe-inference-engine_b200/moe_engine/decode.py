@@ -25,6 +25,7 @@ import math
 import os
 
 import torch
+import torch.nn.functional as F
 
 from . import capi
 from .paged_attention import MAX_SPLITS, SUPPORTED_HEAD_DIMS, cache_geometry
@@ -99,6 +100,7 @@ class DecodeRunner:
         self.tokens_log = torch.zeros(self.log_capacity, dtype=torch.int64, device=dev)
         self.log_count = torch.zeros(1, **i32)
         self._host_state = torch.zeros(2, dtype=torch.int32, pin_memory=True)
+        self.sample_seed = torch.zeros(1, dtype=torch.int64, device=dev)  # device sampler stream
         self._graphs: dict = {}
         self.use_pdl = True
         # Persistent step (one launch per token) whenever the shapes allow it;
@@ -143,7 +145,9 @@ class DecodeRunner:
             L.k_cache, L.v_cache = k.data_ptr(), v.data_ptr()
         return arr
 
-    def make_desc(self, cache, *, logits: bool, graph: bool, splits: int):
+    def make_desc(self, cache, *, logits: bool, graph: bool, splits: int, sample=(0.0, 0)):
+        """Step descriptor; ``sample`` = (temperature, top_k) selects the device
+        sampler (persistent step only) instead of the greedy argmax."""
         cfg, m = self.config, self.model
         w = m.token_embedding.weight
         d = capi.StepDesc()
@@ -206,6 +210,9 @@ class DecodeRunner:
         d.max_splits = MAX_SPLITS
         d.lm_grid = self.lm_grid
         d.use_pdl = 1 if self.use_pdl else 0
+        d.sample_temperature = float(sample[0])
+        d.sample_top_k = int(sample[1])
+        d.sample_seed = self.sample_seed.data_ptr()
         d.step_scratch = None
         d.step_scratch_bytes = 0
         if self.persistent:
@@ -254,20 +261,29 @@ class DecodeRunner:
         dt = self.model.token_embedding.weight.dtype
         return self.logits.to(dt, copy=True).view(1, 1, -1)
 
-    def graph_for(self, cache, max_ctx: int):
+    def supports_sampling(self, cache, temperature: float, top_k) -> bool:
+        """Whether decode steps for ``cache`` can sample on the device."""
+        if temperature <= 0 or (top_k is not None and top_k > 64):
+            return False
+        _, _, _, _, bs, _, _ = cache_geometry(cache, 0)
+        desc, _ = self.make_desc(cache, logits=False, graph=True, splits=self.splits_for(bs, bs),
+                                 sample=(temperature, top_k or 0))
+        return bool(desc.step_scratch)
+
+    def graph_for(self, cache, max_ctx: int, sample=(0.0, 0)):
         """The captured decode step for ``cache`` (captured on first use)."""
         _, _, _, _, bs, _, _ = cache_geometry(cache, 0)
         splits = self.splits_for(max_ctx, bs)
         k0 = cache_geometry(cache, 0)[0]
         table = getattr(cache, "block_table_device", None)
         key = (k0.data_ptr(), None if table is None else table.data_ptr(), splits, self.use_pdl,
-               self.persistent, self.param_signature())
+               self.persistent, self.param_signature(), tuple(sample))
         hit = self._graphs.get(key)
         if hit is not None:
             return hit[0]
         if len(self._graphs) >= 4:
             self._graphs.clear()
-        desc, layers = self.make_desc(cache, logits=False, graph=True, splits=splits)
+        desc, layers = self.make_desc(cache, logits=False, graph=True, splits=splits, sample=sample)
         # Warm-up with every kernel skipping (done = 1): loads modules, touches
         # nothing; then capture.
         self.done.fill_(1)
@@ -283,25 +299,45 @@ class DecodeRunner:
 
 
 @torch.no_grad()
-def greedy_generate(model, token_ids: torch.Tensor, max_new_tokens: int, cache) -> torch.Tensor:
-    """Greedy ``Model.generate`` with the decode step replayed as a CUDA graph.
+def sample_logits(logits: torch.Tensor, temperature: float, top_k) -> torch.Tensor:
+    """The reference's sampling of one position's logits (model.py:604-613)."""
+    logits = logits.float() / temperature
+    if top_k is not None:
+        k = min(top_k, logits.size(-1))
+        values, _ = torch.topk(logits, k)
+        logits[logits < values[..., [-1]]] = -float("inf")
+    return torch.multinomial(F.softmax(logits, dim=-1), num_samples=1)
+
+
+def greedy_generate(model, token_ids: torch.Tensor, max_new_tokens: int, cache, temperature: float = 0.0,
+                    top_k=None) -> torch.Tensor:
+    """``Model.generate`` with the decode step replayed as a CUDA graph.
 
     Same results and cache effects as the step-by-step loop (model.py:596-621):
     iteration 0 is the prompt prefill; each further iteration is one graph
     replay; EOS stops generation on the device (later replays are no-ops) and
-    the loop ends when the context is full.
+    the loop ends when the context is full.  With temperature > 0 the first
+    token is sampled from the prefill logits as the reference does and every
+    later one by the step kernel's device sampler, its random stream seeded
+    from torch's default generator (so torch.manual_seed makes a run
+    reproducible).
     """
     runner = model.decode_runner()
     max_seq = model.max_seq_length
     logits = model(token_ids, cache)  # prefill (position 0)
-    first = int(torch.argmax(logits[0, -1]).item())
+    if temperature > 0:
+        first = int(sample_logits(logits[0, -1], temperature, top_k).item())
+        runner.sample_seed.fill_(int(torch.randint(0, 2**62, (1,)).item()))
+    else:
+        first = int(torch.argmax(logits[0, -1]).item())
+    sample = (float(temperature), int(top_k or 0)) if temperature > 0 else (0.0, 0)
     if first == EOS_TOKEN_ID:
         return token_ids
     P = cache.position
     if P >= max_seq or max_new_tokens == 1:
         return torch.cat((token_ids, token_ids.new_tensor([[first]])), dim=1)
     K = min(max_new_tokens - 1, max_seq - P)
-    graph = runner.graph_for(cache, P + K)
+    graph = runner.graph_for(cache, P + K, sample=sample)
     runner.token.fill_(first)
     runner.pos.fill_(P)
     runner.done.zero_()

@@ -749,6 +749,12 @@ class Model(nn.Module):
             from .decode import greedy_generate
 
             return greedy_generate(self, token_ids, max_new_tokens, cache)
+        if (temperature > 0 and self.fused_decode_supported(cache, 1)
+                and self.decode_runner().supports_sampling(cache, temperature, top_k)):
+            from .decode import greedy_generate
+
+            # sampling on the device: the step kernel draws every token after the first
+            return greedy_generate(self, token_ids, max_new_tokens, cache, temperature=temperature, top_k=top_k)
 
         x = token_ids
         step_input = token_ids
