@@ -115,18 +115,11 @@ class ClockSampler:
 
 
 def build_model(device, dtype, seed=0):
-    from moe_engine.model import Model, baseline_config
+    from moe_engine.model import Model, baseline_config, random_init_
 
     torch.manual_seed(seed)
     model = Model(baseline_config()).eval().to(device=device, dtype=dtype)
-    g = torch.Generator(device=device).manual_seed(seed)
-    with torch.no_grad():
-        for name, p in model.named_parameters():
-            if name.endswith("norm.weight"):
-                p.fill_(1.0)
-            else:
-                p.copy_(torch.randn(p.shape, generator=g, device=device, dtype=torch.float32) * 0.02)
-    return model
+    return random_init_(model, seed)
 
 
 def time_graph_calls(fn, calls: int, reps: int = 5):

@@ -601,6 +601,24 @@ class TransformerMoEBlock(nn.Module):
         return x
 
 
+@torch.no_grad()
+def random_init_(model: "Model", seed: int = 0) -> "Model":
+    """Seeded random weights on the model's device: every matrix N(0, 0.02)
+    from one generator in ``named_parameters`` order, norm weights 1, ``*bias``
+    parameters 0 (the BASELINE configs are random-init from seed 0; no
+    checkpoint is involved)."""
+    device = model.token_embedding.weight.device
+    g = torch.Generator(device=device).manual_seed(seed)
+    for name, p in model.named_parameters():
+        if name.endswith("norm.weight"):
+            p.fill_(1.0)
+        elif name.endswith("bias"):
+            p.zero_()
+        else:
+            p.copy_(torch.randn(p.shape, generator=g, device=device, dtype=torch.float32) * 0.02)
+    return model
+
+
 class Model(nn.Module):
     def __init__(self, config: ModelConfig):
         super().__init__()
