@@ -315,6 +315,12 @@ typedef struct mie_step_desc {
   float sample_temperature;
   int sample_top_k;
   const uint64_t* sample_seed;  /* device word, read every step */
+  /* Persistent step: when non-NULL (with log_count), a step whose *log_count
+   * has reached *step_limit changes nothing, like a step after EOS -- so a
+   * graph of several step launches decodes at most *step_limit tokens.  With
+   * use_pdl the launch is programmatic-dependent: the next step's CTAs stage
+   * their first weights while this step's last CTA finishes the LM head. */
+  const int32_t* step_limit;
 } mie_step_desc;
 
 /* Prefill GEMM on the tcgen05 tensor cores: C = A . B^T with A [M, K] and

@@ -125,9 +125,11 @@ __device__ __forceinline__ bool skip_requested(const int32_t* skip) {
 // Block until the preceding grid in the stream completed and its memory is
 // visible.  A no-op when the kernel was launched without the PDL attribute.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-// Allow the next grid in the stream to start launching.  Every kernel here
-// calls this only after its own pdl_wait (and after any grid-wide barrier), so
-// at most one dependent grid is ever resident ahead of a running one.
+// Allow the next grid in the stream to start launching.  The per-op kernels
+// call this only after their own pdl_wait (and after any grid-wide barrier),
+// so at most one dependent grid is ever resident ahead of a running one.  The
+// persistent step calls it first thing: its CTAs fill an SM each, so the next
+// step's CTAs only take SMs this grid has left.
 __device__ __forceinline__ void pdl_trigger() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }

@@ -222,6 +222,7 @@ struct StepCtx {
   float m, l;     // attention: running max and normaliser of this split
   int last;       // this CTA finished the LM head last
   int blk0;       // first cache block of this CTA's old tokens (blk_s[0])
+  int log_k;      // *log_count at the start of the step
 };
 constexpr int kStepBlkCache = 64;  // block ids of a split cached per step
 __shared__ StepCtx cx_s;
@@ -1210,7 +1211,7 @@ __device__ __noinline__ void head_finish(int bi) {
   *d.token = bi;
   *d.pos = cx_s.pos + 1;
   if (d.tokens_log && d.log_count) {
-    const int k = __ldcg(d.log_count);
+    const int k = cx_s.log_k;  // read at the start of the step; only this step writes it
     if (k < d.log_capacity) d.tokens_log[k] = bi;
     *d.log_count = k + 1;
   }
@@ -1374,7 +1375,7 @@ __device__ __noinline__ bool head_phase(const StepParams& P) {
       }
     d.lm_partial_val[c] = bv;
     d.lm_partial_idx[c] = bi;
-    __threadfence();
+    // the release half of the atomic orders this thread's two stores before it
     cx_s.last = atom_add_acq_rel_gpu(d.lm_counter, 1u) == (uint32_t)(G - 1);
   }
   __syncthreads();
@@ -1382,14 +1383,23 @@ __device__ __noinline__ bool head_phase(const StepParams& P) {
   __threadfence();
   float bv = -INFINITY;
   int bi = 0x7fffffff;
+  // eight partials per lane per round, loaded before any is compared
 #pragma unroll 1
-  for (int j = lane; j < G; j += 32) {
-    const float v = __ldcg(d.lm_partial_val + j);
-    const int i = __ldcg(d.lm_partial_idx + j);
-    if (better(v, i, bv, bi)) {
-      bv = v;
-      bi = i;
+  for (int j0 = lane; j0 < G; j0 += 8 * 32) {
+    float v[8];
+    int ix[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int j = j0 + 32 * k;
+      v[k] = j < G ? __ldcg(d.lm_partial_val + j) : -INFINITY;
+      ix[k] = j < G ? __ldcg(d.lm_partial_idx + j) : 0x7fffffff;
     }
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      if (better(v[k], ix[k], bv, bi)) {
+        bv = v[k];
+        bi = ix[k];
+      }
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
@@ -1401,11 +1411,17 @@ __device__ __noinline__ bool head_phase(const StepParams& P) {
     }
   }
   if (lane == 0) head_finish(bi);
+  STEP_STAMP(Lnum, 5);
   return true;
 }
 
 template <typename W, typename KV>
 __global__ void __launch_bounds__(kST, 1) step_kernel(const __grid_constant__ StepParams P) {
+  STEP_STAMP(P.d.num_layers, 3);
+  // Under programmatic dependent launch the next step's CTAs may take each SM
+  // this grid's CTAs leave (one CTA fills an SM, so none starts earlier); they
+  // stage their first weights, then wait for this grid to complete.
+  pdl_trigger();
   {
     // parameters -> shared memory: descriptor and geometry, layers 0 .. 3
     constexpr int kWords = (int)(sizeof(StepShared) / 8);
@@ -1419,16 +1435,39 @@ __global__ void __launch_bounds__(kST, 1) step_kernel(const __grid_constant__ St
     }
 #pragma unroll 1
     for (int l = 0; l < kLayerSlots && l < P.d.num_layers; ++l) layer_fetch(P, l, 128 + 16 * l);
+    if (threadIdx.x == 0) {
+      cx_s.pos = 0;
+#pragma unroll 1
+      for (int b = 0; b < kNumBars; ++b) {
+        mbar_init(&bars_s[b], 1);
+        bar_armed_s[b] = bar_done_s[b] = 0;
+      }
+      fence_barrier_init();
+    }
     __syncthreads();
   }
   const mie_step_desc& d = ps_s.d;
-  // ---- step prologue: position, token, cache slot of the new token ----
+  // layer 0's q / k / v rows, out_proj rows, router and norm weights depend on
+  // the CTA alone, not on the step's state: staged before the wait
+  if (threadIdx.x < 32) att_issue_rows<W>(P, 0);
+  if (threadIdx.x == 64) side_issue<W>(P, 0);
+  // the previous step's writes (token, position, cache, exchange words, step
+  // header) are visible from here on
+  pdl_wait();
+  // ---- step prologue: position, token, cache slot of the new token; the
+  // state words are loaded together (one round trip), the block ids of this
+  // CTA's old tokens alongside the new token's block ----
   if (threadIdx.x == 0) {
     const int c = blockIdx.x;
-    int stop = d.done ? __ldcg(d.done) : 0;
-    cx_s.step = (uint32_t)ll_ld(ps_s.g.ll + kHdrStep) + 1u;
+    const int done_v = d.done ? __ldcg(d.done) : 0;
+    const int lc = d.log_count ? __ldcg(d.log_count) : 0;
+    const int lim = d.step_limit ? __ldcg(d.step_limit) : 0;
+    const uint64_t hstep = ll_ld(ps_s.g.ll + kHdrStep);
     const int p = __ldcg(d.pos);
     const int64_t t = __ldcg(d.token);
+    int stop = done_v || (d.step_limit && d.log_count && lc >= lim);
+    cx_s.step = (uint32_t)hstep + 1u;
+    cx_s.log_k = lc;
     if (!stop && (p < 0 || p >= d.max_pos || t < 0 || t >= d.vocab)) {
       if (c == 0) set_status(d.status, MIE_ERR_RANGE);
       stop = 1;
@@ -1445,29 +1484,25 @@ __global__ void __launch_bounds__(kST, 1) step_kernel(const __grid_constant__ St
     cx_s.pos = p;
     cx_s.tok = t;
     cx_s.slot = stop ? 0 : blk * d.kv_stride_block + (int64_t)(p % d.block_size) * d.kv_stride_tok;
+    cx_s.blk0 = stop ? 0 : att_split(ps_s.g, d.head_dim, p).t0 / d.block_size;
     cx_s.stop = stop;
-#pragma unroll 1
-    for (int b = 0; b < kNumBars; ++b) {
-      mbar_init(&bars_s[b], 1);
-      bar_armed_s[b] = bar_done_s[b] = 0;
+  } else if (d.block_table && threadIdx.x <= kStepBlkCache) {
+    // physical block ids of this CTA's old tokens, the same for every layer
+    // (blk_s[i] by thread i + 1); a position out of range stops the step
+    const int p = __ldcg(d.pos), i = threadIdx.x - 1;
+    if (p >= 0 && p < d.max_pos) {
+      const AttSplit a = att_split(ps_s.g, d.head_dim, p);
+      const int b0 = a.t0 / d.block_size;
+      if (a.t1 > a.t0 && b0 + i <= (a.t1 - 1) / d.block_size) blk_s[i] = __ldcg(d.block_table + b0 + i);
     }
-    fence_barrier_init();
   }
   __syncthreads();
-  if (cx_s.stop) return;
-  {
-    // physical block ids of this CTA's old tokens, the same for every layer
-    const AttSplit a = att_split(ps_s.g, d.head_dim, cx_s.pos);
-    const int b0 = a.t0 / d.block_size;
-    if (threadIdx.x == 0) cx_s.blk0 = b0;
-    if (d.block_table && threadIdx.x < kStepBlkCache && a.t1 > a.t0 &&
-        b0 + (int)threadIdx.x <= (a.t1 - 1) / d.block_size)
-      blk_s[threadIdx.x] = __ldcg(d.block_table + b0 + threadIdx.x);
-    __syncthreads();
+  if (cx_s.stop) {
+    drain_copies();
+    return;
   }
-  if (threadIdx.x < 32) att_issue_rows<W>(P, 0);
+  STEP_STAMP(d.num_layers, 4);
   if (threadIdx.x >= 32 && threadIdx.x < 64) att_issue_kv<KV>(P, 0);
-  if (threadIdx.x == 64) side_issue<W>(P, 0);
   bool ok = true;
 #pragma unroll 1
   for (int l = 0; l < d.num_layers && ok; ++l)
@@ -1622,7 +1657,7 @@ int step_launch(const mie_step_desc& d, const StepGeom& g, uint64_t* scratch, cu
     k = d.kv_dtype == MIE_BF16 ? step_kernel<__nv_bfloat16, __nv_bfloat16> : step_kernel<__nv_bfloat16, float>;
   else
     k = d.kv_dtype == MIE_BF16 ? step_kernel<float, __nv_bfloat16> : step_kernel<float, float>;
-  return launch(k, dim3(g.G), dim3(kStepThreads), g.smem, st, false, p);
+  return launch(k, dim3(g.G), dim3(kStepThreads), g.smem, st, d.use_pdl != 0, p);
 }
 
 #ifdef MIE_STEP_STAMPS

@@ -31,7 +31,12 @@ from . import capi
 from .paged_attention import MAX_SPLITS, SUPPORTED_HEAD_DIMS, cache_geometry
 
 EOS_TOKEN_ID = 50256
-CHUNK_STEPS = 64  # graph replays between host reads of the token log
+CHUNK_STEPS = 64  # decode steps between host reads of the token log
+# Persistent step: launches captured per graph.  Consecutive launches are
+# programmatic-dependent, so each step's CTAs stage their first weights while
+# the previous step's last CTA finishes; a device step limit stops the extra
+# launches of the last graph of a chunk.
+GRAPH_STEPS = 8
 
 
 def _row_ok(n: int, dtype) -> bool:
@@ -101,6 +106,7 @@ class DecodeRunner:
         self.log_count = torch.zeros(1, **i32)
         self._host_state = torch.zeros(2, dtype=torch.int32, pin_memory=True)
         self.sample_seed = torch.zeros(1, dtype=torch.int64, device=dev)  # device sampler stream
+        self.step_limit = torch.zeros(1, **i32)  # multi-step graphs: tokens to log before steps stop
         self._graphs: dict = {}
         self.use_pdl = True
         # Persistent step (one launch per token) whenever the shapes allow it;
@@ -145,9 +151,10 @@ class DecodeRunner:
             L.k_cache, L.v_cache = k.data_ptr(), v.data_ptr()
         return arr
 
-    def make_desc(self, cache, *, logits: bool, graph: bool, splits: int, sample=(0.0, 0)):
+    def make_desc(self, cache, *, logits: bool, graph: bool, splits: int, sample=(0.0, 0), limit: bool = False):
         """Step descriptor; ``sample`` = (temperature, top_k) selects the device
-        sampler (persistent step only) instead of the greedy argmax."""
+        sampler (persistent step only) instead of the greedy argmax; ``limit``
+        makes steps stop once ``log_count`` reaches ``step_limit``."""
         cfg, m = self.config, self.model
         w = m.token_embedding.weight
         d = capi.StepDesc()
@@ -213,6 +220,7 @@ class DecodeRunner:
         d.sample_temperature = float(sample[0])
         d.sample_top_k = int(sample[1])
         d.sample_seed = self.sample_seed.data_ptr()
+        d.step_limit = self.step_limit.data_ptr() if limit and graph else None
         d.step_scratch = None
         d.step_scratch_bytes = 0
         if self.persistent:
@@ -230,6 +238,12 @@ class DecodeRunner:
         _, _, _, _, bs, _, _ = cache_geometry(cache, 0)
         desc, _ = self.make_desc(cache, logits=False, graph=True, splits=self.splits_for(bs, bs))
         return bool(desc.step_scratch)
+
+    def steps_per_graph(self, cache) -> int:
+        """Decode steps one graph of :meth:`graph_for` may hold for ``cache``:
+        GRAPH_STEPS for the persistent step (which honours ``step_limit``),
+        else 1."""
+        return GRAPH_STEPS if self.uses_persistent(cache) else 1
 
     # ---- execution ------------------------------------------------------------
     def launch_step(self, desc) -> None:
@@ -270,20 +284,28 @@ class DecodeRunner:
                                  sample=(temperature, top_k or 0))
         return bool(desc.step_scratch)
 
-    def graph_for(self, cache, max_ctx: int, sample=(0.0, 0)):
-        """The captured decode step for ``cache`` (captured on first use)."""
+    def graph_for(self, cache, max_ctx: int, sample=(0.0, 0), steps: int = 1):
+        """The captured decode step for ``cache`` (captured on first use).
+
+        With ``steps`` > 1 the graph holds that many step launches (persistent
+        step only, see :meth:`steps_per_graph`) and every replay decodes up to
+        ``steps`` tokens: the caller sets ``step_limit`` to the ``log_count``
+        at which steps stop."""
         _, _, _, _, bs, _, _ = cache_geometry(cache, 0)
         splits = self.splits_for(max_ctx, bs)
         k0 = cache_geometry(cache, 0)[0]
         table = getattr(cache, "block_table_device", None)
         key = (k0.data_ptr(), None if table is None else table.data_ptr(), splits, self.use_pdl,
-               self.persistent, self.param_signature(), tuple(sample))
+               self.persistent, self.param_signature(), tuple(sample), steps)
         hit = self._graphs.get(key)
         if hit is not None:
             return hit[0]
         if len(self._graphs) >= 4:
             self._graphs.clear()
-        desc, layers = self.make_desc(cache, logits=False, graph=True, splits=splits, sample=sample)
+        desc, layers = self.make_desc(cache, logits=False, graph=True, splits=splits, sample=sample,
+                                      limit=steps > 1)
+        if steps > 1 and not desc.step_scratch:
+            raise ValueError("several steps per graph need the persistent step")
         # Warm-up with every kernel skipping (done = 1): loads modules, touches
         # nothing; then capture.
         self.done.fill_(1)
@@ -292,7 +314,10 @@ class DecodeRunner:
         torch.cuda.current_stream(self.device).synchronize()
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g):
-            rc = self.lib.mie_decode_step(ctypes.byref(desc), capi.stream_handle(self.device))
+            for _ in range(steps):
+                rc = self.lib.mie_decode_step(ctypes.byref(desc), capi.stream_handle(self.device))
+                if rc:
+                    break
         capi.check(rc, "mie_decode_step (capture)")
         self._graphs[key] = (g, desc, layers)
         return g
@@ -337,12 +362,13 @@ def greedy_generate(model, token_ids: torch.Tensor, max_new_tokens: int, cache, 
     if P >= max_seq or max_new_tokens == 1:
         return torch.cat((token_ids, token_ids.new_tensor([[first]])), dim=1)
     K = min(max_new_tokens - 1, max_seq - P)
-    graph = runner.graph_for(cache, P + K, sample=sample)
+    M = runner.steps_per_graph(cache)
+    graph = runner.graph_for(cache, P + K, sample=sample, steps=M)
     runner.token.fill_(first)
     runner.pos.fill_(P)
     runner.done.zero_()
     runner.log_count.zero_()
-    produced = 0  # replays issued
+    produced = 0  # steps issued
     count = 0
     exhausted = False
     paged = hasattr(cache, "allocator")
@@ -359,7 +385,9 @@ def greedy_generate(model, token_ids: torch.Tensor, max_new_tokens: int, cache, 
                     cache.reserve(len(cache.block_table) * bs + 1)
                 n = len(cache.block_table) * bs - (P + produced)
                 exhausted = True
-        for _ in range(n):
+        if M > 1:
+            runner.step_limit.fill_(produced + n)
+        for _ in range(-(-n // M)):
             graph.replay()
         produced += n
         runner._host_state[0:1].copy_(runner.log_count, non_blocking=True)

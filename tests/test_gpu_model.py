@@ -218,3 +218,47 @@ def test_persistent_step_is_used_and_agrees_with_launch_sequence(baseline_params
     runner.persistent = True
     assert torch.equal(gen[True], gen[False])
     runner.check_status()
+
+
+def test_multi_step_graph_honours_step_limit(baseline_params):
+    """A graph of several programmatic-dependent step launches decodes exactly
+    ``step_limit`` tokens (the extra launches change nothing) and the same
+    tokens as eager steps; generate's chunks end mid-graph."""
+    m = baseline_model(baseline_params, torch.bfloat16)
+    runner = m.decode_runner()
+    prompt = torch.randint(0, 50304, (24,), generator=torch.Generator().manual_seed(12))
+    eager = m.new_cache()
+    with torch.no_grad():
+        logits = m(prompt[None].to(DEV), eager)
+        seq = []
+        for _ in range(21):
+            t = int(logits[0, -1].float().argmax())
+            seq.append(t)
+            logits = m(torch.tensor([[t]], device=DEV), eager)
+    got = m.generate(prompt, max_new_tokens=21, temperature=0)[0, 24:].tolist()
+    assert got == seq
+
+    alloc = m.new_block_allocator(num_blocks=8, block_size=16, attention_mode="direct")
+    cache = alloc.new_cache()
+    with torch.no_grad():
+        m(prompt[None].to(DEV), cache)
+    P = cache.position
+    cache.reserve(P + 16)
+    M = runner.steps_per_graph(cache)
+    assert M > 1
+    graph = runner.graph_for(cache, P + 16, steps=M)
+    runner.token.fill_(seq[0])
+    runner.pos.fill_(P)
+    runner.done.zero_()
+    runner.log_count.zero_()
+    runner.step_limit.fill_(5)
+    graph.replay()
+    torch.cuda.synchronize()
+    assert int(runner.log_count) == 5 and int(runner.pos) == P + 5
+    runner.step_limit.fill_(16)
+    for _ in range(-(-11 // M)):
+        graph.replay()
+    torch.cuda.synchronize()
+    runner.check_status()
+    assert int(runner.log_count) == 16 and int(runner.pos) == P + 16
+    assert runner.tokens_log[:16].tolist() == seq[1:17]
