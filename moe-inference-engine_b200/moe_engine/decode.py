@@ -104,7 +104,8 @@ class DecodeRunner:
         self.log_capacity = cfg.max_seq_length + 1
         self.tokens_log = torch.zeros(self.log_capacity, dtype=torch.int64, device=dev)
         self.log_count = torch.zeros(1, **i32)
-        self._host_state = torch.zeros(2, dtype=torch.int32, pin_memory=True)
+        # (log_count, done) after each queued chunk of steps; two chunks in flight
+        self._host_states = [torch.zeros(2, dtype=torch.int32, pin_memory=True) for _ in range(2)]
         self.sample_seed = torch.zeros(1, dtype=torch.int64, device=dev)  # device sampler stream
         self.step_limit = torch.zeros(1, **i32)  # multi-step graphs: tokens to log before steps stop
         self._graphs: dict = {}
@@ -372,30 +373,52 @@ def greedy_generate(model, token_ids: torch.Tensor, max_new_tokens: int, cache, 
     count = 0
     exhausted = False
     paged = hasattr(cache, "allocator")
-    while produced < K:
-        n = min(CHUNK_STEPS, K - produced)
-        if paged:
-            try:
-                cache.reserve(P + produced + n)
-            except RuntimeError:
-                # Reserve what the pool still has, run up to it, then fail like
-                # the step that could not get a block.
-                bs = cache.allocator.block_size
-                while cache.allocator.free_blocks and len(cache.block_table) * bs < P + produced + n:
-                    cache.reserve(len(cache.block_table) * bs + 1)
-                n = len(cache.block_table) * bs - (P + produced)
-                exhausted = True
-        if M > 1:
-            runner.step_limit.fill_(produced + n)
-        for _ in range(-(-n // M)):
-            graph.replay()
-        produced += n
-        runner._host_state[0:1].copy_(runner.log_count, non_blocking=True)
-        runner._host_state[1:2].copy_(runner.done, non_blocking=True)
-        torch.cuda.current_stream(runner.device).synchronize()
-        count, done = int(runner._host_state[0]), int(runner._host_state[1])
-        if done or exhausted:
+    if paged:
+        try:
+            # the whole request at once: the block table (whose update waits
+            # for the stream) is not touched while steps are queued
+            cache.reserve(P + K)
+        except RuntimeError:
+            pass  # chunk by chunk below, as far as the pool goes
+    stream = torch.cuda.current_stream(runner.device)
+    inflight = []  # (host state slot, event) per queued chunk, oldest first
+    slot = 0
+    while True:
+        # keep two chunks queued, so the GPU never waits for this loop
+        while produced < K and not exhausted and len(inflight) < 2:
+            n = min(CHUNK_STEPS, K - produced)
+            if paged and len(cache.block_table) * cache.allocator.block_size < P + produced + n:
+                try:
+                    cache.reserve(P + produced + n)
+                except RuntimeError:
+                    # Reserve what the pool still has, run up to it, then fail
+                    # like the step that could not get a block.
+                    bs = cache.allocator.block_size
+                    while cache.allocator.free_blocks and len(cache.block_table) * bs < P + produced + n:
+                        cache.reserve(len(cache.block_table) * bs + 1)
+                    n = len(cache.block_table) * bs - (P + produced)
+                    exhausted = True
+            if n <= 0:
+                break
+            if M > 1:
+                runner.step_limit.fill_(produced + n)
+            for _ in range(-(-n // M)):
+                graph.replay()
+            produced += n
+            state = runner._host_states[slot]
+            slot ^= 1
+            state[0:1].copy_(runner.log_count, non_blocking=True)
+            state[1:2].copy_(runner.done, non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(stream)
+            inflight.append((state, ev))
+        if not inflight:
             break
+        state, ev = inflight.pop(0)
+        ev.synchronize()
+        count, done = int(state[0]), int(state[1])
+        if done:
+            break  # a chunk still queued runs as no-op steps
     runner.check_status()
     cache.position = P + count
     if paged:
