@@ -280,6 +280,12 @@ __device__ __forceinline__ uint64_t policy_evict_last() {
   return p;
 }
 
+// Bulk prefetch of [src, src + bytes) into L2 (no completion to wait for);
+// src 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 // Largest chunk one bulk copy moves here (bytes); larger ranges are split.
 constexpr uint32_t kBulkMax = 1u << 16;
 

@@ -45,6 +45,7 @@ constexpr uint32_t kStepKvChunkBytes = 32 * 1024;   // K+V of one split staged i
 constexpr int kStepHeadStagesMax = 8;               // LM-head ring stages
 constexpr uint32_t kStepMaxSmem = 223 * 1024;       // dynamic shared memory of the step kernel (static: < 4 KB)
 constexpr int kStepTopKMax = 64;                    // largest top_k of the device sampler
+constexpr int kStepMaxExpertHidden = 4096;          // expert hidden size of the persistent step
 constexpr int kStepHeadRowsMax = 512;               // LM-head rows of one CTA the top-k sampler sorts
 
 // Geometry of one persistent step launch: exchange-buffer offsets (64-bit
@@ -60,6 +61,7 @@ struct StepGeom {
   int chunk_tok;  // K/V tokens per shared-memory chunk
   int q_stage;    // q rows of the head staged in shared memory (the rest are read from global memory)
   int moe_staged; // 1: the selected experts' rows are staged in shared memory
+  int wide;       // 1: the wide kernel variant (any head_dim piece count, long expert rows)
   int nr_max;     // out_proj / down rows of one CTA (upper bound)
   int head_rows, head_stages;  // LM-head ring: rows per stage, stages
   int head_early;               // ring stages inside the attention staging area

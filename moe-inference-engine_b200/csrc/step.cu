@@ -466,7 +466,14 @@ __device__ __noinline__ void att_issue_rows(const StepParams& P, int l) {
     bar_arm(kBarAtt, nrows * rb + (ly.attn_norm_b ? 2 : 1) * rb);
   }
   __syncwarp();
-  // one copy per lane: norm weights, q rows, k (both RoPE halves), v
+  // one copy per lane: norm weights, q rows, k (both RoPE halves), v; lane 5
+  // prefetches the q rows that are not staged into L2
+  if (lane == 5 && a.att && g.q_stage < hd) {
+    const uint8_t* q0 = static_cast<const uint8_t*>(ly.qkv_w) + ((size_t)a.h * hd + g.q_stage) * rb;
+#pragma unroll 1
+    for (uint32_t o = 0, nb = (uint32_t)(hd - g.q_stage) * rb; o < nb; o += kBulkMax)
+      bulk_prefetch_l2(q0 + o, min(kBulkMax, nb - o));
+  }
   if (lane > 4 || (lane > 0 && !a.att)) return;
   fence_proxy_async_smem();
   const uint8_t* w = static_cast<const uint8_t*>(ly.qkv_w);
@@ -667,6 +674,50 @@ __device__ __forceinline__ void gemv_rows(const uint4* rows, int n, int nvec, co
   }
 }
 
+// Rows longer than one register segment (nvec > Seg<W>::kVecs: the expert
+// down rows of a large expert hidden size, read from global memory; staged
+// rows are never that long): one row per warp per iteration,
+// segment by segment, the next segment's weights loaded before the current
+// one is multiplied; one partial sum per 16-byte vector as in gemv_rows.
+template <typename W, bool kGlobal>
+__device__ __noinline__ void gemv_seg(const uint4* rows, int n, int nvec, const float* x, float* out,
+                                      const float* x1, int split) {
+  constexpr int PV = Elem<W>::kPerVec, NV = Seg<W>::kNV, SV = Seg<W>::kVecs;
+  const int lane = threadIdx.x & 31;
+  const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+  const auto load = [&](const uint4* rp, int s0, uint4* w) {
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int v = s0 + lane + kWarp * j;
+      if constexpr (kGlobal)
+        w[j] = v < nvec ? __ldg(rp + v) : z;
+      else
+        w[j] = v < nvec ? rp[v] : z;
+    }
+  };
+#pragma unroll 1
+  for (int r = threadIdx.x >> 5; r < n; r += kSW) {
+    const float* xb = (x1 && r >= split) ? x1 : x;
+    const uint4* rp = rows + (size_t)r * nvec;
+    uint4 w[NV], wn[NV];
+    load(rp, 0, w);
+    float sum = 0.f;
+#pragma unroll 1
+    for (int s0 = 0; s0 < nvec; s0 += SV) {
+      if (s0 + SV < nvec) load(rp, s0 + SV, wn);
+      float xr[NV * PV];
+      load_x_regs<W>(xr, xb + (size_t)s0 * PV, nvec - s0);
+#pragma unroll
+      for (int j = 0; j < NV; ++j) sum += dot_vec(w[j], xr + j * PV, 0.f, (const W*)nullptr);
+#pragma unroll
+      for (int j = 0; j < NV; ++j) w[j] = wn[j];
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if (lane == 0) out[r] = sum;
+  }
+}
+
 // ---- fp32 rows: CUDA-core GEMV ----
 // out[r] = rows[r] . x for r < n: rows of nvec 16-byte vectors (row stride
 // nvec) in shared memory (kGlobal false) or global memory, x an fp32 vector
@@ -703,14 +754,16 @@ __device__ __forceinline__ void gemv_global(const uint4* rows, int n, int nvec, 
 // (the first chunk was staged with the layer's attention inputs).  Leaves
 // the split's running max / normaliser in cx_s.m / cx_s.l and the PV group
 // partials in ab[0, kST).
-template <typename KV>
+template <typename KV, bool kWide>
 __device__ __noinline__ bool att_core(const StepParams& P, int l, int h, int t0, int t1, const float* q, float* sc,
                                       float* ab) {
   const mie_step_desc& d = ps_s.d;
   const StepGeom& g = ps_s.g;
   const int tid = threadIdx.x, hd = d.head_dim, chunk = g.chunk_tok;
   constexpr int VPT = 16 / (int)sizeof(KV);
+  // PV: Gp groups of hd threads (threads past Gp * hd idle)
   const int VPH = hd / VPT, Gp = kST / hd, gi = tid / hd, dcol = tid - gi * hd;
+  // kWide: any piece count (else a power of two)
   const KV* ks = smem_at<const KV>(g.sm_kv);
   const KV* vs = ks + (size_t)chunk * hd;
   const float scale = d.attn_scale;
@@ -733,13 +786,17 @@ __device__ __noinline__ bool att_core(const StepParams& P, int l, int h, int t0,
     for (int t = tid; t < n; t += kST) {
       const uint4* kr = reinterpret_cast<const uint4*>(ks + (size_t)t * hd);
       // four independent partial dots; the start piece rotates with t, which
-      // spreads the threads of a warp over the banks (VPH a power of 2)
+      // spreads the threads of a warp over the banks
       float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
+      // piece (jj + t) mod VPH: a mask for a power of two, else a wrap of
+      // jj + (t mod VPH) < 2 VPH
+      const int rot = kWide ? t % VPH : t;
+      const auto wrap = [VPH](int j) { return kWide ? (j >= VPH ? j - VPH : j) : (j & (VPH - 1)); };
       int jj = 0;
 #pragma unroll 1
       for (; jj + 4 <= VPH; jj += 4) {
-        const int j0 = (jj + t) & (VPH - 1), j1 = (jj + 1 + t) & (VPH - 1);
-        const int j2 = (jj + 2 + t) & (VPH - 1), j3 = (jj + 3 + t) & (VPH - 1);
+        const int j0 = wrap(jj + rot), j1 = wrap(jj + 1 + rot);
+        const int j2 = wrap(jj + 2 + rot), j3 = wrap(jj + 3 + rot);
         d0 = dot_vec(kr[j0], q + j0 * VPT, d0, (const KV*)nullptr);
         d1 = dot_vec(kr[j1], q + j1 * VPT, d1, (const KV*)nullptr);
         d2 = dot_vec(kr[j2], q + j2 * VPT, d2, (const KV*)nullptr);
@@ -747,7 +804,7 @@ __device__ __noinline__ bool att_core(const StepParams& P, int l, int h, int t0,
       }
 #pragma unroll 1
       for (; jj < VPH; ++jj) {
-        const int j = (jj + t) & (VPH - 1);
+        const int j = wrap(jj + rot);
         d0 = dot_vec(kr[j], q + j * VPT, d0, (const KV*)nullptr);
       }
       const float v = ((d0 + d1) + (d2 + d3)) * scale;
@@ -793,7 +850,7 @@ __device__ __noinline__ bool att_core(const StepParams& P, int l, int h, int t0,
 // ---------------------------------------------------------------------------
 // ATT + MERGE of layer l (see the file comment).
 // ---------------------------------------------------------------------------
-template <typename W, typename KV>
+template <typename W, typename KV, bool kWide>
 __device__ __noinline__ bool att_phase(const StepParams& P, int l) {
   const mie_step_desc& d = ps_s.d;
   const StepGeom& g = ps_s.g;
@@ -836,7 +893,9 @@ __device__ __noinline__ bool att_phase(const StepParams& P, int l) {
     gemv_smem<W>(smem_at<const uint4>(g.sm_qw), hd + nkv, nvD, xn, qk);  // q and k / v rows are adjacent
   } else {
     gemv_smem<W>(smem_at<const uint4>(g.sm_qw), g.q_stage, nvD, xn, qk);
-    if constexpr (sizeof(W) == 4)  // bf16: every q row is staged (checked on the host)
+    // the q rows that did not fit in shared memory (prefetched into L2 with
+    // the staging); bf16 weights in the narrow geometry stage every q row
+    if constexpr (sizeof(W) == 4 || kWide)
       if (g.q_stage < hd)
         gemv_global<W>(rowp(ly.qkv_w, (int64_t)a.h * hd + g.q_stage, (int64_t)nvD * 16), hd - g.q_stage, nvD, xn,
                        qk + g.q_stage);
@@ -892,7 +951,7 @@ __device__ __noinline__ bool att_phase(const StepParams& P, int l) {
 
   // ---- attention over the old tokens ----
   float* ab = smem_at<float>(g.sm_acc);
-  if (!att_core<KV>(P, l, a.h, a.t0, a.t1, qk, smem_at<float>(g.sm_sc), ab)) return false;
+  if (!att_core<KV, kWide>(P, l, a.h, a.t0, a.t1, qk, smem_at<float>(g.sm_sc), ab)) return false;
   __syncthreads();  // staged rows, K/V and ab complete
   STEP_STAMP(l, 5);
   uint64_t* be = ll + g.off_b[par] + (int64_t)(a.h * S + a.s) * (3 + hd);
@@ -1027,19 +1086,55 @@ __device__ __noinline__ bool proj_phase(const StepParams& P, int l) {
   return true;
 }
 
+// Warp 0 of a wide-geometry CTA, right after routing: the selected experts'
+// rows of this CTA -- gate (and up) rows of its units [u0, u1), down rows of
+// its output rows -- prefetched into L2 for the GEMVs that read them from
+// global memory (lanes 0-3: up rows of each matrix and slot; lanes 8-9: down
+// rows of each slot).
+template <typename W>
+__device__ __noinline__ void moe_prefetch(int l, int sel0, int sel1) {
+  const mie_step_desc& d = ps_s.d;
+  const mie_layer_desc& ly = layer_at(l);
+  const int tid = threadIdx.x, D = d.hidden_dim, Hx = d.expert_hidden_dim;
+  const int nmat = d.act == MIE_ACT_SWIGLU ? 2 : 1;
+  const uint32_t rbD = (uint32_t)(D * sizeof(W)), rbH = (uint32_t)(Hx * sizeof(W));
+  const uint8_t* src = nullptr;
+  uint32_t nb = 0;
+  if (tid < 2 * nmat) {
+    int u0, u1;
+    split32(2 * Hx, blockIdx.x, gridDim.x, &u0, &u1);
+    const int m = tid >> 1, k = tid & 1;
+    const int ua = max(u0, k * Hx), ub = min(u1, (k + 1) * Hx);
+    if (ub > ua) {
+      src = static_cast<const uint8_t*>(m ? ly.w3 : ly.w1) + ((size_t)(k ? sel1 : sel0) * Hx + ua - k * Hx) * rbD;
+      nb = (uint32_t)(ub - ua) * rbD;
+    }
+  } else if (tid >= 8 && tid < 10) {
+    int r0, r1;
+    split32(D, blockIdx.x, gridDim.x, &r0, &r1);
+    const int k = tid - 8;
+    src = static_cast<const uint8_t*>(ly.w2) + ((size_t)(k ? sel1 : sel0) * D + r0) * rbH;
+    nb = (uint32_t)(r1 - r0) * rbH;
+  }
+#pragma unroll 1
+  for (uint32_t o = 0; o < nb; o += kBulkMax) bulk_prefetch_l2(src + o, min(kBulkMax, nb - o));
+}
+
 // ---------------------------------------------------------------------------
 // UP + DOWN: x_mid -> norm -> router -> top-2 -> selected experts -> x of
 // layer l + 1 (exchange A).  bf16 weights: the selected experts' rows of this
 // CTA are bulk-copied into shared memory right after routing; fp32 weights:
-// read from global memory by the GEMV.
+// read from global memory by the GEMV.  kWide (shapes whose expert rows do not
+// fit in shared memory): read from global memory after an L2 prefetch, down
+// rows longer than one register segment multiplied segment by segment.
 // ---------------------------------------------------------------------------
-template <typename W>
+template <typename W, bool kWide>
 __device__ __noinline__ bool moe_phase(const StepParams& P, int l) {
   const mie_step_desc& d = ps_s.d;
   const StepGeom& g = ps_s.g;
   const mie_layer_desc& ly = layer_at(l);
   constexpr int PV = Elem<W>::kPerVec;
-  constexpr bool kStaged = sizeof(W) == 2;
+  constexpr bool kStaged = sizeof(W) == 2 && !kWide;
   const int tid = threadIdx.x;
   const int D = d.hidden_dim, Hx = d.expert_hidden_dim, E = d.num_experts, nvD = D / PV, nvH = Hx / PV;
   const int64_t rbD = (int64_t)D * sizeof(W), rbH = (int64_t)Hx * sizeof(W);
@@ -1115,6 +1210,9 @@ __device__ __noinline__ bool moe_phase(const StepParams& P, int l) {
       }
     }
   }
+  if constexpr (kWide) {
+    if (tid < 32) moe_prefetch<W>(l, sel0, sel1);
+  }
   STEP_STAMP(l, 11);
   // up units: gate (and up) rows -> ab[0, nmat * nu)
   if constexpr (kStaged) {
@@ -1164,6 +1262,9 @@ __device__ __noinline__ bool moe_phase(const StepParams& P, int l) {
       if constexpr (kStaged)
         gemv_smem<W>(reinterpret_cast<const uint4*>(ms + (size_t)nmat * nu * rbD + (size_t)k * nr * rbH), nr, nvH,
                      hb + (size_t)k * Hx, ab + k * nr);
+      else if (kWide && nvH > Seg<W>::kVecs)  // rows longer than one register segment
+        gemv_seg<W, true>(rowp(ly.w2, (int64_t)(k ? sel1 : sel0) * D + r0, rbH), nr, nvH, hb + (size_t)k * Hx,
+                          ab + k * nr, nullptr, 0);
       else
         gemv_global<W>(rowp(ly.w2, (int64_t)(k ? sel1 : sel0) * D + r0, rbH), nr, nvH, hb + (size_t)k * Hx,
                        ab + k * nr);
@@ -1415,7 +1516,7 @@ __device__ __noinline__ bool head_phase(const StepParams& P) {
   return true;
 }
 
-template <typename W, typename KV>
+template <typename W, typename KV, bool kWide>
 __global__ void __launch_bounds__(kST, 1) step_kernel(const __grid_constant__ StepParams P) {
   STEP_STAMP(P.d.num_layers, 3);
   // Under programmatic dependent launch the next step's CTAs may take each SM
@@ -1506,7 +1607,7 @@ __global__ void __launch_bounds__(kST, 1) step_kernel(const __grid_constant__ St
   bool ok = true;
 #pragma unroll 1
   for (int l = 0; l < d.num_layers && ok; ++l)
-    ok = att_phase<W, KV>(P, l) && proj_phase<W, KV>(P, l) && moe_phase<W>(P, l);
+    ok = att_phase<W, KV, kWide>(P, l) && proj_phase<W, KV>(P, l) && moe_phase<W, kWide>(P, l);
   if (ok) ok = head_phase<W>(P);
   if (!ok) drain_copies();
 }
@@ -1523,12 +1624,17 @@ int step_geometry(const mie_step_desc& d, int grid, StepGeom* g) {
   const int esz = d.dtype == MIE_BF16 ? 2 : 4, kvsz = d.kv_dtype == MIE_BF16 ? 2 : 4;
   const int D = d.hidden_dim, H = d.num_heads, hd = d.head_dim, Hx = d.expert_hidden_dim, E = d.num_experts;
   if (D <= 0 || H <= 0 || hd <= 0 || Hx <= 0 || H * hd != D || hd % 2) return MIE_ERR_UNSUPPORTED;
-  // rows live in one register segment of a warp: at most 768 elements
-  if (D > 768 || Hx > 768 || (D * esz) % 16 || (Hx * esz) % 16) return MIE_ERR_UNSUPPORTED;
-  // head_dim: 16-byte K/V pieces, a power-of-two count of them per row, and
-  // whole PV groups of the CTA's threads
+  // x lives in one register segment of a warp (at most 768 elements); expert
+  // down rows longer than that are multiplied segment by segment (wide)
+  if (D > 768 || Hx > kStepMaxExpertHidden || (D * esz) % 16 || (Hx * esz) % 16) return MIE_ERR_UNSUPPORTED;
+  // head_dim: whole 16-byte K/V pieces
+  if (hd > 128 || (hd * kvsz) % 16) return MIE_ERR_UNSUPPORTED;
+  // The narrow geometry: a power-of-two count of K/V pieces per head row,
+  // whole PV groups of the CTA's threads, expert rows of one register segment
+  // (and for bf16 weights every q row and the selected experts' rows staged in
+  // shared memory, checked below).  Other shapes run the wide kernel variant.
   const int vph = hd * kvsz / 16;
-  if (hd > 128 || (hd * kvsz) % 16 || (vph & (vph - 1)) || kStepThreads % hd) return MIE_ERR_UNSUPPORTED;
+  bool wide = (vph & (vph - 1)) != 0 || kStepThreads % hd != 0 || Hx > 768;
   if (d.top_k != 2 || E < 2 || E > 32) return MIE_ERR_UNSUPPORTED;
   if (d.act != MIE_ACT_GELU && d.act != MIE_ACT_SWIGLU) return MIE_ERR_UNSUPPORTED;
   if (d.moe_partial || (d.expert_count && d.expert_count != E) || d.expert_base)
@@ -1604,15 +1710,20 @@ int step_geometry(const mie_step_desc& d, int grid, StepGeom* g) {
   const uint32_t att_min = (uint32_t)kvw_max * rbD + chunk_bytes + 3 * 128;
   const uint32_t side_bytes = (uint32_t)(G.nr_max + E + 2) * rbD;
   const uint32_t moe_bytes = (uint32_t)(nmat * nu_max) * rbD + 2u * G.nr_max * rbH;
-  const uint32_t region2 = (esz == 2 && moe_bytes > side_bytes) ? moe_bytes : side_bytes;
+  // bf16 weights, narrow: the selected experts' rows are staged in shared
+  // memory beside every q row of the head.  Wide (and fp32 weights): the
+  // expert GEMVs read their rows from global memory (after an L2 prefetch in
+  // the wide variant) and as many q rows as fit are staged, the rest read
+  // from L2 likewise.
+  const uint32_t moe_region = moe_bytes > side_bytes ? moe_bytes : side_bytes;
+  if (esz == 2 && base + att_min + moe_region + (uint32_t)hd * rbD > kStepMaxSmem) wide = true;
+  G.wide = wide ? 1 : 0;
+  G.moe_staged = esz == 2 && !wide ? 1 : 0;
+  const uint32_t region2 = G.moe_staged ? moe_region : side_bytes;
   if (base + att_min + region2 > kStepMaxSmem) return MIE_ERR_UNSUPPORTED;
   const uint32_t avail = kStepMaxSmem - base - region2 - att_min;
-  // bf16 weights: all q rows of the head staged (and the selected experts'
-  // rows, see moe_phase); fp32 weights: as many q rows as fit.
   const uint32_t q = avail / rbD;
   G.q_stage = q < (uint32_t)hd ? (int)q : hd;
-  if (esz == 2 && G.q_stage < hd) return MIE_ERR_UNSUPPORTED;
-  G.moe_staged = esz == 2 ? 1 : 0;
   G.sm_qw = stake((uint32_t)G.q_stage * rbD);
   G.sm_kvw = stake((uint32_t)kvw_max * rbD);
   G.sm_kv = stake(chunk_bytes);
@@ -1653,10 +1764,18 @@ int step_launch(const mie_step_desc& d, const StepGeom& g, uint64_t* scratch, cu
 #ifdef MIE_STEP_STAMPS
   if (d.num_layers + 1 > kStampLayers || g.G > 160) return MIE_ERR_UNSUPPORTED;
 #endif
-  if (d.dtype == MIE_BF16)
-    k = d.kv_dtype == MIE_BF16 ? step_kernel<__nv_bfloat16, __nv_bfloat16> : step_kernel<__nv_bfloat16, float>;
-  else
-    k = d.kv_dtype == MIE_BF16 ? step_kernel<float, __nv_bfloat16> : step_kernel<float, float>;
+  using bf16 = __nv_bfloat16;
+  if (d.dtype == MIE_BF16) {
+    if (g.wide)
+      k = d.kv_dtype == MIE_BF16 ? step_kernel<bf16, bf16, true> : step_kernel<bf16, float, true>;
+    else
+      k = d.kv_dtype == MIE_BF16 ? step_kernel<bf16, bf16, false> : step_kernel<bf16, float, false>;
+  } else {
+    if (g.wide)
+      k = d.kv_dtype == MIE_BF16 ? step_kernel<float, bf16, true> : step_kernel<float, float, true>;
+    else
+      k = d.kv_dtype == MIE_BF16 ? step_kernel<float, bf16, false> : step_kernel<float, float, false>;
+  }
   return launch(k, dim3(g.G), dim3(kStepThreads), g.smem, st, d.use_pdl != 0, p);
 }
 
@@ -1670,10 +1789,15 @@ extern "C" int mie_debug_step_stamps(unsigned long long* host, int64_t count) {
 #endif
 
 void step_set_attributes() {
-  set_max_smem(step_kernel<__nv_bfloat16, __nv_bfloat16>);
-  set_max_smem(step_kernel<__nv_bfloat16, float>);
-  set_max_smem(step_kernel<float, __nv_bfloat16>);
-  set_max_smem(step_kernel<float, float>);
+  using bf16 = __nv_bfloat16;
+  set_max_smem(step_kernel<bf16, bf16, false>);
+  set_max_smem(step_kernel<bf16, float, false>);
+  set_max_smem(step_kernel<float, bf16, false>);
+  set_max_smem(step_kernel<float, float, false>);
+  set_max_smem(step_kernel<bf16, bf16, true>);
+  set_max_smem(step_kernel<bf16, float, true>);
+  set_max_smem(step_kernel<float, bf16, true>);
+  set_max_smem(step_kernel<float, float, true>);
 }
 
 }  // namespace mie

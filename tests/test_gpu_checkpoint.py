@@ -8,6 +8,10 @@ format ({"model": state_dict, "model_config": dict, ...}) and loaded with
 
 * fp32: greedy tokens identical to the oracle (itself pinned against the
   unmodified reference engine, tests/test_oracle_golden.py);
+* the decode step runs as the persistent step's wide variant (head_dim 96:
+  twelve 16-byte K/V pieces per row; expert rows of 3072 read from global
+  memory, down rows in register segments): hidden states within rounding of
+  the per-op launch sequence, greedy tokens identical to it;
 * bf16: the kernel prefill's logits against the oracle on bf16-rounded
   weights -- within 2e-2 at every position with clear router margins, median
   below 1e-2 (a position at a router near-tie takes another expert pair; with
@@ -56,6 +60,7 @@ def test_fp32_greedy_tokens_equal_oracle(params, ckpt_path):
                                                                                       3072, 96)
     p = prompt(16)
     assert model.fused_decode_supported(model.new_cache(), 1)  # decode on the sm_100a kernels
+    assert model.decode_runner().uses_persistent(model.new_cache())  # the wide persistent step
     got = model.generate(p, max_new_tokens=32, temperature=0)[0].tolist()
     want = oracle.generate_greedy(params, ARCH, p, 32)
     assert got == want
@@ -81,3 +86,41 @@ def test_bf16_engine_decode_runs_after_kernel_prefill(ckpt_path):
     p = prompt(40, seed=14)
     out = model.generate(p, max_new_tokens=16, temperature=0)
     assert out.shape == (1, 56) and torch.equal(out[0, :40].cpu(), p)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_persistent_wide_step_agrees_with_launch_sequence(ckpt_path, dtype):
+    model, _, _ = load_engine_model(ckpt_path, DEV, dtype=dtype)
+    runner = model.decode_runner()
+    assert runner.uses_persistent(model.new_cache())
+    p = prompt(24, seed=15)
+    xs = {}
+    for persistent in (True, False):
+        runner.persistent = persistent
+        cache = model.new_block_allocator(num_blocks=64, block_size=16, attention_mode="direct").new_cache()
+        hs = []
+        with torch.no_grad():
+            model(p[None].to(DEV), cache)
+            tok = torch.tensor([[17]], device=DEV)
+            for _ in range(6):
+                logits = model(tok, cache)
+                hs.append(runner.x.clone())
+                tok = logits[0, -1].float().argmax().view(1, 1)
+        xs[persistent] = torch.stack(hs)
+        runner.check_status()
+    runner.persistent = True
+    rel = (xs[True] - xs[False]).norm() / xs[False].norm()
+    assert rel < (5e-3 if dtype == torch.bfloat16 else 1e-5), float(rel)
+    gen = {}
+    for persistent in (True, False):
+        runner.persistent = persistent
+        gen[persistent] = model.generate(p, max_new_tokens=24, temperature=0)
+    runner.persistent = True
+    assert torch.equal(gen[True], gen[False])
+    if dtype == torch.bfloat16:  # the device sampler on the wide variant
+        torch.manual_seed(1)
+        a = model.generate(p, max_new_tokens=12, temperature=0.8, top_k=50)
+        torch.manual_seed(1)
+        b = model.generate(p, max_new_tokens=12, temperature=0.8, top_k=50)
+        assert torch.equal(a, b) and a.shape == (1, 36)
+    runner.check_status()
