@@ -62,6 +62,7 @@ struct StepGeom {
   int q_stage;    // q rows of the head staged in shared memory (the rest are read from global memory)
   int moe_staged; // 1: the selected experts' rows are staged in shared memory
   int wide;       // 1: the wide kernel variant (any head_dim piece count, long expert rows)
+  int head_bias_smem;  // 1: the CTA's LM-head bias values fit in the h vector's shared memory
   int nr_max;     // out_proj / down rows of one CTA (upper bound)
   int head_rows, head_stages;  // LM-head ring: rows per stage, stages
   int head_early;               // ring stages inside the attention staging area
@@ -144,6 +145,9 @@ void gemv_set_attributes();
 int step_geometry(const mie_step_desc& d, int grid, StepGeom* g);
 int step_launch(const mie_step_desc& d, const StepGeom& g, uint64_t* scratch, cudaStream_t st);
 void step_set_attributes();
+// step_wide.cu (the wide variant of the persistent step, its own translation unit)
+int step_launch_wide(const StepParams& p, cudaStream_t st);
+void step_set_attributes_wide();
 
 // gemm.cu (prefill GEMM on the tensor cores)
 enum {

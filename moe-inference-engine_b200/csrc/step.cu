@@ -868,6 +868,21 @@ __device__ __noinline__ bool att_phase(const StepParams& P, int l) {
   const int S = g.S, nkv = 2 * a.nkp + a.nvd;
   STEP_STAMP(l, 0);
 
+  // wide: this thread's q / k / v bias, loaded while x arrives (added after
+  // the GEMVs)
+  float qkv_bias = 0.f;
+  if constexpr (kWide) {
+    if (ly.qkv_b && a.att) {
+      if (tid < hd) qkv_bias = ldw<W>(ly.qkv_b, (int64_t)a.h * hd + tid);
+      if (tid >= 128 && tid < 128 + nkv) {
+        const int k = tid - 128;
+        const int64_t row = k < a.nkp       ? (int64_t)D + a.h * hd + a.p0 + k
+                            : k < 2 * a.nkp ? (int64_t)D + a.h * hd + half + a.p0 + (k - a.nkp)
+                                            : 2 * (int64_t)D + a.h * hd + a.v0 + (k - 2 * a.nkp);
+        qkv_bias = ldw<W>(ly.qkv_b, row);
+      }
+    }
+  }
   // ---- x: token embedding (layer 0) or exchange A; norm ----
   const W* nw = smem_at<const W>(g.sm_anw);
   if (l == 0) {
@@ -906,7 +921,11 @@ __device__ __noinline__ bool att_phase(const StepParams& P, int l) {
   // bias; RoPE of q (pairs j, j + hd/2) and of this CTA's k pairs; k / v
   // rounded to the cache type and stored into the slot of the new token
   float* kv = qk + hd;
-  if (ly.qkv_b) {
+  if (kWide && ly.qkv_b) {
+    if (tid < hd) qk[tid] += qkv_bias;
+    if (tid >= 128 && tid < 128 + nkv) kv[tid - 128] += qkv_bias;
+    __syncthreads();
+  } else if (ly.qkv_b) {
     if (tid < hd) qk[tid] += ldw<W>(ly.qkv_b, (int64_t)a.h * hd + tid);
     if (tid >= 128 && tid < 128 + nkv) {
       const int k = tid - 128;
@@ -1035,7 +1054,7 @@ __device__ __noinline__ bool att_phase(const StepParams& P, int l) {
 // ---------------------------------------------------------------------------
 // PROJ: x_mid rows = x + out_proj(o) (+ bias) -> exchange D.
 // ---------------------------------------------------------------------------
-template <typename W, typename KV>
+template <typename W, typename KV, bool kWide>
 __device__ __noinline__ bool proj_phase(const StepParams& P, int l) {
   const mie_step_desc& d = ps_s.d;
   const StepGeom& g = ps_s.g;
@@ -1072,6 +1091,8 @@ __device__ __noinline__ bool proj_phase(const StepParams& P, int l) {
   STEP_STAMP(l, 18);
   // a failed wait raised the abort word: the next receive then fails for
   // every thread of every CTA, so no barrier is needed to agree here
+  // wide: the bias of this thread's row, loaded while o arrives
+  const float out_bias = kWide && ly.out_b && tid < nr ? ldw<W>(ly.out_b, r0 + tid) : 0.f;
   if (!recv_part(ll + g.off_c[l & 1], D, tag, ob, kBarSide, ll, d.status)) return true;
   STEP_STAMP(l, 8);
   gemv_smem<W>(smem_at<const uint4>(g.sm_moe), nr, nvD, ob, ab);  // nr <= 14 rows: warps < 14
@@ -1079,7 +1100,10 @@ __device__ __noinline__ bool proj_phase(const StepParams& P, int l) {
   if (tid < nr) {
     const int r = r0 + tid;
     float y = ab[tid];
-    if (ly.out_b) y += ldw<W>(ly.out_b, r);
+    if (kWide)
+      y += out_bias;
+    else if (ly.out_b)
+      y += ldw<W>(ly.out_b, r);
     ll_put(ll + g.off_d[l & 1] + r, smem_at<float>(g.sm_x)[r] + y, tag);
   }
   STEP_STAMP(l, 9);
@@ -1396,7 +1420,7 @@ __device__ __noinline__ bool head_sample_topk(int v0h, int v1h, uint64_t seed, f
   return true;
 }
 
-template <typename W>
+template <typename W, bool kWide>
 __device__ __noinline__ bool head_phase(const StepParams& P) {
   const mie_step_desc& d = ps_s.d;
   const StepGeom& g = ps_s.g;
@@ -1412,6 +1436,14 @@ __device__ __noinline__ bool head_phase(const StepParams& P) {
   split32(V, c, G, &v0h, &v1h);
   const int nst = (v1h - v0h + g.head_rows - 1) / g.head_rows;
   const W* nw = smem_at<const W>(g.sm_anw);
+  // wide: the LM-head bias of this CTA's vocab rows into the h vector's
+  // shared memory (free in the head) while x arrives; the top-k sampler's
+  // logits later overwrite each entry after its own bias was read
+  float* hbias = smem_at<float>(g.sm_h);
+  const bool bias_smem = kWide && d.lm_bias && g.head_bias_smem;
+  if (bias_smem)
+#pragma unroll 1
+    for (int i = tid; i < v1h - v0h; i += kST) hbias[i] = ldw<W>(d.lm_bias, v0h + i);
   if (!recv_norm<W>(ll + g.off_a[Lnum & 1], D, tag_of(Lnum), xs, xn, kBarSide, d.norm, d.eps, nw,
                     d.final_norm_b ? nw + D : nullptr, ll, d.status))
     return false;
@@ -1434,7 +1466,10 @@ __device__ __noinline__ bool head_phase(const StepParams& P) {
     if (tid < nrw) {
       float v = ab[tid];
       const int row = r0 + tid;
-      if (d.lm_bias) v += ldw<W>(d.lm_bias, row);
+      if (bias_smem)
+        v += hbias[row - v0h];
+      else if (d.lm_bias)
+        v += ldw<W>(d.lm_bias, row);
       if (d.logits) d.logits[row] = v;
       if (topk) {
         smem_at<float>(g.sm_h)[row - v0h] = v;
@@ -1607,8 +1642,8 @@ __global__ void __launch_bounds__(kST, 1) step_kernel(const __grid_constant__ St
   bool ok = true;
 #pragma unroll 1
   for (int l = 0; l < d.num_layers && ok; ++l)
-    ok = att_phase<W, KV, kWide>(P, l) && proj_phase<W, KV>(P, l) && moe_phase<W, kWide>(P, l);
-  if (ok) ok = head_phase<W>(P);
+    ok = att_phase<W, KV, kWide>(P, l) && proj_phase<W, KV, kWide>(P, l) && moe_phase<W, kWide>(P, l);
+  if (ok) ok = head_phase<W, kWide>(P);
   if (!ok) drain_copies();
 }
 
@@ -1617,6 +1652,7 @@ __global__ void __launch_bounds__(kST, 1) step_kernel(const __grid_constant__ St
 // ---------------------------------------------------------------------------
 // Host side: validation, geometry, launch.
 // ---------------------------------------------------------------------------
+#ifndef MIE_STEP_WIDE_TU
 int step_geometry(const mie_step_desc& d, int grid, StepGeom* g) {
   if (d.num_layers <= 0 || d.num_layers > kMaxStepLayers) return MIE_ERR_UNSUPPORTED;
   if (d.dtype != MIE_F32 && d.dtype != MIE_BF16) return MIE_ERR_UNSUPPORTED;
@@ -1718,6 +1754,8 @@ int step_geometry(const mie_step_desc& d, int grid, StepGeom* g) {
   const uint32_t moe_region = moe_bytes > side_bytes ? moe_bytes : side_bytes;
   if (esz == 2 && base + att_min + moe_region + (uint32_t)hd * rbD > kStepMaxSmem) wide = true;
   G.wide = wide ? 1 : 0;
+  // the CTA's LM-head bias values fit in the h vector's shared memory
+  G.head_bias_smem = (d.vocab + grid - 1) / grid <= 2 * Hx ? 1 : 0;
   G.moe_staged = esz == 2 && !wide ? 1 : 0;
   const uint32_t region2 = G.moe_staged ? moe_region : side_bytes;
   if (base + att_min + region2 > kStepMaxSmem) return MIE_ERR_UNSUPPORTED;
@@ -1764,18 +1802,12 @@ int step_launch(const mie_step_desc& d, const StepGeom& g, uint64_t* scratch, cu
 #ifdef MIE_STEP_STAMPS
   if (d.num_layers + 1 > kStampLayers || g.G > 160) return MIE_ERR_UNSUPPORTED;
 #endif
+  if (g.wide) return step_launch_wide(p, st);
   using bf16 = __nv_bfloat16;
-  if (d.dtype == MIE_BF16) {
-    if (g.wide)
-      k = d.kv_dtype == MIE_BF16 ? step_kernel<bf16, bf16, true> : step_kernel<bf16, float, true>;
-    else
-      k = d.kv_dtype == MIE_BF16 ? step_kernel<bf16, bf16, false> : step_kernel<bf16, float, false>;
-  } else {
-    if (g.wide)
-      k = d.kv_dtype == MIE_BF16 ? step_kernel<float, bf16, true> : step_kernel<float, float, true>;
-    else
-      k = d.kv_dtype == MIE_BF16 ? step_kernel<float, bf16, false> : step_kernel<float, float, false>;
-  }
+  if (d.dtype == MIE_BF16)
+    k = d.kv_dtype == MIE_BF16 ? step_kernel<bf16, bf16, false> : step_kernel<bf16, float, false>;
+  else
+    k = d.kv_dtype == MIE_BF16 ? step_kernel<float, bf16, false> : step_kernel<float, float, false>;
   return launch(k, dim3(g.G), dim3(kStepThreads), g.smem, st, d.use_pdl != 0, p);
 }
 
@@ -1794,10 +1826,40 @@ void step_set_attributes() {
   set_max_smem(step_kernel<bf16, float, false>);
   set_max_smem(step_kernel<float, bf16, false>);
   set_max_smem(step_kernel<float, float, false>);
+  step_set_attributes_wide();
+}
+
+#else
+// The wide kernel variant is compiled in its own translation unit
+// (step_wide.cu includes this file with MIE_STEP_WIDE_TU defined): sharing
+// the out-of-line device functions with it would change their register
+// allocation in the narrow variant.
+int step_launch_wide(const StepParams& p, cudaStream_t st) {
+  void (*k)(const StepParams);
+  using bf16 = __nv_bfloat16;
+  if (p.d.dtype == MIE_BF16)
+    k = p.d.kv_dtype == MIE_BF16 ? step_kernel<bf16, bf16, true> : step_kernel<bf16, float, true>;
+  else
+    k = p.d.kv_dtype == MIE_BF16 ? step_kernel<float, bf16, true> : step_kernel<float, float, true>;
+  return launch(k, dim3(p.g.G), dim3(kStepThreads), p.g.smem, st, p.d.use_pdl != 0, p);
+}
+
+void step_set_attributes_wide() {
+  using bf16 = __nv_bfloat16;
   set_max_smem(step_kernel<bf16, bf16, true>);
   set_max_smem(step_kernel<bf16, float, true>);
   set_max_smem(step_kernel<float, bf16, true>);
   set_max_smem(step_kernel<float, float, true>);
 }
+
+#ifdef MIE_STEP_STAMPS
+extern "C" int mie_debug_step_stamps_wide(unsigned long long* host, int64_t count) {
+  return cudaMemcpyFromSymbol(host, g_step_stamps, sizeof(unsigned long long) * (size_t)count) == cudaSuccess
+             ? MIE_OK
+             : MIE_ERR_CUDA;
+}
+#endif
+
+#endif  // MIE_STEP_WIDE_TU
 
 }  // namespace mie
