@@ -248,6 +248,7 @@ __device__ __forceinline__ void layer_fetch(const StepParams& P, int l, int firs
         reinterpret_cast<const uint64_t*>(&P.layers[l])[i];
 }
 __shared__ float red_s[kSW];
+__shared__ float red2_s[kSW];  // the attention core's sum (its max uses red_s): one barrier each
 __shared__ int gat_s[kST];  // merge: exchange word index of each received value
 __shared__ int blk_s[kStepBlkCache];  // physical block ids of this CTA's old tokens
 __shared__ float bestv_s[kSW];
@@ -780,10 +781,15 @@ __device__ __noinline__ bool att_core(const StepParams& P, int l, int h, int t0,
         kv_issue<KV>(d, g, layer_at(l), h, ta, n, kBarKv);
       }
     }
-    if (!bar_wait(kBarKv, g.ll, d.status)) return false;
+    STEP_STAMP(l, 19);
+    // every thread waits for the chunk's copies itself; whether all waits
+    // succeeded is agreed at the barrier of the max below
+    const bool kv_ok = mbar_wait(&bars_s[kBarKv], bar_done_s[kBarKv] & 1u, d.status);
+    if (!kv_ok) atomicExch(reinterpret_cast<unsigned long long*>(g.ll + kHdrAbort), 1ull);
+    STEP_STAMP(l, 20);
     float mloc = -INFINITY;
 #pragma unroll 1
-    for (int t = tid; t < n; t += kST) {
+    for (int t = kv_ok ? tid : n; t < n; t += kST) {
       const uint4* kr = reinterpret_cast<const uint4*>(ks + (size_t)t * hd);
       // four independent partial dots; the start piece rotates with t, which
       // spreads the threads of a warp over the banks
@@ -811,7 +817,18 @@ __device__ __noinline__ bool att_core(const StepParams& P, int l, int h, int t0,
       sc[t] = v;
       mloc = fmaxf(mloc, v);
     }
-    const float mn = fmaxf(m_run, block_max(mloc, red_s));
+    STEP_STAMP(l, 21);
+    // block max (red_s) and block sum (red2_s) in the order of block_max /
+    // block_sum; each buffer is rewritten only after later barriers
+    mloc = warp_max(mloc);
+    if ((tid & 31) == 0) red_s[tid >> 5] = mloc;
+    if (__syncthreads_or(!kv_ok)) return false;
+    if (tid == 0) bar_done_s[kBarKv] += 1;
+    float bmax = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < kSW; ++i) bmax = fmaxf(bmax, red_s[i]);
+    const float mn = fmaxf(m_run, bmax);
+    STEP_STAMP(l, 22);
     const float alpha = m_run == -INFINITY ? 0.f : expf(m_run - mn);
     float ls = 0.f;
 #pragma unroll 1
@@ -820,8 +837,15 @@ __device__ __noinline__ bool att_core(const StepParams& P, int l, int h, int t0,
       sc[t] = pr;
       ls += pr;
     }
-    l_run = l_run * alpha + block_sum(ls, red_s);  // every thread passed a barrier after the sc writes
+    ls = warp_sum(ls);
+    if ((tid & 31) == 0) red2_s[tid >> 5] = ls;
+    __syncthreads();  // also orders the sc writes before the PV reads
+    float bsum = 0.f;
+#pragma unroll
+    for (int i = 0; i < kSW; ++i) bsum += red2_s[i];
+    l_run = l_run * alpha + bsum;
     m_run = mn;
+    STEP_STAMP(l, 23);
     if (gi < Gp) {
       // four independent accumulation chains over this group's tokens
       float a1 = 0.f, a2 = 0.f, a3 = 0.f, a0 = 0.f;
@@ -837,8 +861,10 @@ __device__ __noinline__ bool att_core(const StepParams& P, int l, int h, int t0,
       for (; t < n; t += Gp) a0 = fmaf(sc[t], Elem<KV>::to_f(vs[(size_t)t * hd + dcol]), a0);
       acc = fmaf(acc, alpha, (a0 + a1) + (a2 + a3));
     }
+    STEP_STAMP(l, 24);
   }
   __syncthreads();
+  STEP_STAMP(l, 25);
   ab[tid] = gi < Gp ? acc : 0.f;
   if (tid == 0) {
     cx_s.m = m_run;
