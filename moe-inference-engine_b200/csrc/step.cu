@@ -737,6 +737,10 @@ __device__ __noinline__ void gemv(const uint4* rows, int n, int nvec, const floa
   load_x_regs<W>(xr, xb, nvec);
   if (Seg<W>::kNV <= 3 && n == 4 * kSW)
     gemv_rows<W, kGlobal, Seg<W>::kNV <= 3 ? 4 : 2>(rows, n, nvec, xr, out);  // LM-head stages: 4 rows per warp
+#ifdef MIE_STEP_WIDE_TU
+  else if (Seg<W>::kNV <= 3 && n == 3 * kSW)
+    gemv_rows<W, kGlobal, Seg<W>::kNV <= 3 ? 3 : 2>(rows, n, nvec, xr, out);  // wide LM-head stages of 48 rows
+#endif
   else
     gemv_rows<W, kGlobal, 2>(rows, n, nvec, xr, out);
 }
@@ -1801,6 +1805,8 @@ int step_geometry(const mie_step_desc& d, int grid, StepGeom* g) {
   // attention area and can be requested before the last layer's MoE is done
   const uint32_t ring_bytes = G.smem - G.sm_qw;
   G.head_rows = 4 * (kStepThreads / 32);
+  // the wide variant also has stages of three rows per warp (bf16)
+  if (wide && esz == 2 && ring_bytes / ((uint32_t)G.head_rows * rbD) < 2) G.head_rows = 3 * (kStepThreads / 32);
   while (G.head_rows > kStepThreads / 32 && ring_bytes / ((uint32_t)G.head_rows * rbD) < 2) G.head_rows /= 2;
   const uint32_t stage_bytes = (uint32_t)G.head_rows * rbD;
   G.head_stages = (int)(ring_bytes / stage_bytes);
