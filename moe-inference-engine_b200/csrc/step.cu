@@ -677,12 +677,14 @@ __device__ __forceinline__ void gemv_rows(const uint4* rows, int n, int nvec, co
 
 // Rows longer than one register segment (nvec > Seg<W>::kVecs: the expert
 // down rows of a large expert hidden size, read from global memory; staged
-// rows are never that long): one row per warp per iteration,
-// segment by segment, the next segment's weights loaded before the current
-// one is multiplied; one partial sum per 16-byte vector as in gemv_rows.
+// rows are never that long): out[r] = row r . x for r < n, rows [0, split)
+// from rows0 dotted with x0, rows [split, n) from rows1 with x1 (both slots'
+// rows in one pass).  One row per warp per iteration, segment by segment, the
+// next segment's weights loaded before the current one is multiplied; one
+// partial sum per 16-byte vector as in gemv_rows.
 template <typename W, bool kGlobal>
-__device__ __noinline__ void gemv_seg(const uint4* rows, int n, int nvec, const float* x, float* out,
-                                      const float* x1, int split) {
+__device__ __noinline__ void gemv_seg(const uint4* rows0, const uint4* rows1, int split, int n, int nvec,
+                                      const float* x0, const float* x1, float* out) {
   constexpr int PV = Elem<W>::kPerVec, NV = Seg<W>::kNV, SV = Seg<W>::kVecs;
   const int lane = threadIdx.x & 31;
   const uint4 z = make_uint4(0u, 0u, 0u, 0u);
@@ -698,8 +700,8 @@ __device__ __noinline__ void gemv_seg(const uint4* rows, int n, int nvec, const 
   };
 #pragma unroll 1
   for (int r = threadIdx.x >> 5; r < n; r += kSW) {
-    const float* xb = (x1 && r >= split) ? x1 : x;
-    const uint4* rp = rows + (size_t)r * nvec;
+    const float* xb = r < split ? x0 : x1;
+    const uint4* rp = r < split ? rows0 + (size_t)r * nvec : rows1 + (size_t)(r - split) * nvec;
     uint4 w[NV], wn[NV];
     load(rp, 0, w);
     float sum = 0.f;
@@ -1310,15 +1312,16 @@ __device__ __noinline__ bool moe_phase(const StepParams& P, int l) {
     // both slots' down rows (adjacent in shared memory) in one pass: rows
     // [0, nr) dot h of slot 0, rows [nr, 2 nr) dot h of slot 1
     gemv_smem<W>(reinterpret_cast<const uint4*>(ms + (size_t)nmat * nu * rbD), 2 * nr, nvH, hb, ab, hb + Hx, nr);
+  } else if (kWide && nvH > Seg<W>::kVecs) {
+    // rows longer than one register segment, both slots in one pass
+    gemv_seg<W, true>(rowp(ly.w2, (int64_t)sel0 * D + r0, rbH), rowp(ly.w2, (int64_t)sel1 * D + r0, rbH), nr, 2 * nr,
+                      nvH, hb, hb + Hx, ab);
   } else {
 #pragma unroll 1
     for (int k = 0; k < 2; ++k) {
       if constexpr (kStaged)
         gemv_smem<W>(reinterpret_cast<const uint4*>(ms + (size_t)nmat * nu * rbD + (size_t)k * nr * rbH), nr, nvH,
                      hb + (size_t)k * Hx, ab + k * nr);
-      else if (kWide && nvH > Seg<W>::kVecs)  // rows longer than one register segment
-        gemv_seg<W, true>(rowp(ly.w2, (int64_t)(k ? sel1 : sel0) * D + r0, rbH), nr, nvH, hb + (size_t)k * Hx,
-                          ab + k * nr, nullptr, 0);
       else
         gemv_global<W>(rowp(ly.w2, (int64_t)(k ? sel1 : sel0) * D + r0, rbH), nr, nvH, hb + (size_t)k * Hx,
                        ab + k * nr);
