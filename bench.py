@@ -307,9 +307,9 @@ def run_b200(args, rank, world, device):
         step_bytes = weights_bytes + kv_bytes
         kr = {"us": step_s * 1e6, "gbs": step_bytes / step_s / 1e9, "bytes": step_bytes}
         kr["frac"] = kr["gbs"] / hbm_peak
-        # DRAM bytes of one step launch from the ncu capture summarised in
-        # profiles/step_kernel_persistent_decode.md (context 518), scaled to the
-        # mean context: the same ratio to the algorithmic bytes
+        # DRAM bytes of one step launch measured by ncu at context
+        # STEP_CAPTURE_CTX (dram__bytes_read.sum + dram__bytes_write.sum),
+        # scaled to the mean context: the same ratio to the algorithmic bytes
         cap_traffic, cap_alg = STEP_CAPTURE_DRAM_BYTES, weights_bytes + KV_BYTES_PER_CTX * STEP_CAPTURE_CTX
         traffic = step_bytes * cap_traffic / cap_alg
         roof_note = ("per-launch average of the graph-replayed step over the timed region (CUDA events); "

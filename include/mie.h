@@ -451,11 +451,15 @@ int mie_attn_decode(const mie_attn_args* a, void* stream);
  * inside libmie.so: 64 counter words + 65,536 floats (256 KB), which every GPU
  * that loads the library holds until the process exits.  Limits: num_heads <=
  * 64 and num_heads * splits * (head_dim + 2) <= 65,536; larger requests return
- * MIE_ERR_SCRATCH_LIMIT and launch nothing.  Nothing is allocated: no
- * cudaMalloc, cudaFree or allocating library call.  The first call on a device
- * looks up the array's device address and zeroes its counters
- * (cudaGetSymbolAddress + cudaMemset, with that device current), so make the
- * first call on each device before any stream capture.  All calls share the
+ * MIE_ERR_SCRATCH_LIMIT and launch nothing; a->defer_merge must be 0 (the
+ * partials would stay in the library's array, where no consumer can read them:
+ * MIE_ERR_INVALID).  The request is validated before the size limit is checked,
+ * so a malformed request returns MIE_ERR_INVALID / MIE_ERR_UNSUPPORTED as with
+ * mie_attn_decode.  Nothing is allocated: no cudaMalloc, cudaFree or allocating
+ * library call.  The first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress, with that device current) and zeroes its counters with
+ * cudaMemsetAsync on the caller's stream, so make the first call on each device
+ * before any stream capture.  All calls share the
  * array and each call returns the counters to zero: calls that overlap on
  * the GPU (for example on two streams at once) race and corrupt each other. */
 int mie_attn_decode_fixed_scratch(const mie_attn_args* a, void* stream);

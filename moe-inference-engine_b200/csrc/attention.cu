@@ -341,8 +341,10 @@ std::mutex g_fixed_mutex;
 void* g_fixed_addr[64] = {nullptr};  // device address of the array, per device
 
 // Once per device, with that device current: resolve the array's device
-// address (the host symbol is only a stand-in) and zero the counters.
-int fixed_scratch_setup(void** out) {
+// address (the host symbol is only a stand-in) and zero the counters on the
+// caller's stream, so the clear is ordered before this call's launch whatever
+// kind of stream the caller uses.
+int fixed_scratch_setup(void** out, cudaStream_t st) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess || dev < 0 || dev >= 64) {
@@ -357,9 +359,9 @@ int fixed_scratch_setup(void** out) {
       note_cuda_error(e, "cudaGetSymbolAddress(g_attn_fixed_scratch)");
       return MIE_ERR_CUDA;
     }
-    e = cudaMemset(p, 0, sizeof(uint32_t) * kFixedCounters);
+    e = cudaMemsetAsync(p, 0, sizeof(uint32_t) * kFixedCounters, st);
     if (e != cudaSuccess) {
-      note_cuda_error(e, "cudaMemset(fixed-scratch counters)");
+      note_cuda_error(e, "cudaMemsetAsync(fixed-scratch counters)");
       return MIE_ERR_CUDA;
     }
     g_fixed_addr[dev] = p;
@@ -371,14 +373,15 @@ int fixed_scratch_setup(void** out) {
 }  // namespace
 
 // Point a->partials / a->counters at the fixed array (set up on first use on
-// this device) after checking the request fits it.
-int attn_fixed_scratch_bind(mie_attn_args* a) {
+// this device) after checking the request fits it.  The caller has validated
+// everything else about the request.
+int attn_fixed_scratch_bind(mie_attn_args* a, cudaStream_t st) {
   if (a->num_heads <= 0 || a->splits <= 0) return MIE_ERR_INVALID;
   if (a->num_heads > kFixedCounters ||
       (int64_t)a->num_heads * a->splits * (a->head_dim + 2) > kFixedPartialFloats)
     return MIE_ERR_SCRATCH_LIMIT;
   void* base = nullptr;
-  const int rc = fixed_scratch_setup(&base);
+  const int rc = fixed_scratch_setup(&base, st);
   if (rc) return rc;
   a->counters = static_cast<uint32_t*>(base);
   a->partials = reinterpret_cast<float*>(static_cast<uint32_t*>(base) + kFixedCounters);

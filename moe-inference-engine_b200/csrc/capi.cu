@@ -65,15 +65,18 @@ int run_moe(const mie_moe_args& a, cudaStream_t st, bool pdl, bool route_only) {
   return moe_decode_launch(a, L, grid, st, pdl);
 }
 
-int check_attn(const mie_attn_args& a) {
+// with_scratch false: the request is checked without its partials / counters /
+// max_splits (the fixed-scratch entry point supplies those itself).
+int check_attn(const mie_attn_args& a, bool with_scratch = true) {
   if (!dtype_ok(a.kv_dtype) || !dtype_ok(a.q_dtype) || !dtype_ok(a.out_dtype)) return MIE_ERR_UNSUPPORTED;
   switch (a.head_dim) {
     case 4: case 8: case 16: case 32: case 64: case 96: case 128: break;
     default: return MIE_ERR_UNSUPPORTED;
   }
-  if (a.num_heads <= 0 || a.block_size <= 0 || a.splits <= 0 || a.splits > a.max_splits) return MIE_ERR_INVALID;
+  if (a.num_heads <= 0 || a.block_size <= 0 || a.splits <= 0) return MIE_ERR_INVALID;
+  if (with_scratch && a.splits > a.max_splits) return MIE_ERR_INVALID;
   if (!a.q || !a.k || !a.v || !a.out) return MIE_ERR_INVALID;
-  if (a.splits > 1 && (!a.partials || !a.counters)) return MIE_ERR_INVALID;
+  if (with_scratch && a.splits > 1 && (!a.partials || !a.counters)) return MIE_ERR_INVALID;
   if (!a.ctx_dev && (a.ctx_len < 1 || a.ctx_len > a.max_ctx)) return MIE_ERR_INVALID;
   if (a.stride_tok != a.head_dim) return MIE_ERR_UNSUPPORTED;
   if (rows16(a.head_dim, a.kv_dtype)) {
@@ -412,10 +415,17 @@ int mie_attn_decode(const mie_attn_args* a, void* stream) {
 
 int mie_attn_decode_fixed_scratch(const mie_attn_args* a, void* stream) {
   if (!a) return MIE_ERR_INVALID;
-  mie_attn_args v = *a;
-  const int rc = attn_fixed_scratch_bind(&v);  // partials + counters from the fixed array
+  // the partials of a deferred merge would stay in the library's array, where
+  // no consumer can read them: refused
+  if (a->defer_merge) return MIE_ERR_INVALID;
+  // the request itself first, then the size limit, then the one-time set-up
+  int rc = check_attn(*a, false);
   if (rc) return rc;
-  return run_attn(v, static_cast<cudaStream_t>(stream), false);
+  mie_attn_args v = *a;
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  rc = attn_fixed_scratch_bind(&v, st);  // partials + counters from the fixed array
+  if (rc) return rc;
+  return run_attn(v, st, false);
 }
 
 int mie_qkv_rope_store(const mie_qkv_args* a, void* stream) {

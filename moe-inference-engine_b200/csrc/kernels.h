@@ -130,7 +130,7 @@ void moe_set_attributes();
 AttnLayout attn_layout(const mie_attn_args& a);
 int attn_decode_launch(const mie_attn_args& a, const AttnLayout& L, cudaStream_t st, bool pdl);
 void attn_set_attributes();
-int attn_fixed_scratch_bind(mie_attn_args* a);
+int attn_fixed_scratch_bind(mie_attn_args* a, cudaStream_t st);
 
 // gemv.cu
 GemvLayout qkv_layout(const mie_qkv_args& a, int grid);

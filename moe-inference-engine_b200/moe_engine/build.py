@@ -45,24 +45,41 @@ def up_to_date() -> bool:
 
 
 def build(force: bool = False, verbose: bool = False) -> str:
+    """Compile every source to an object file (in parallel), then link the
+    shared library; returns its path."""
     if not force and up_to_date():
         return OUT
+    from concurrent.futures import ThreadPoolExecutor
+
     os.makedirs(OUT_DIR, exist_ok=True)
+    obj_dir = os.path.join(OUT_DIR, "obj")
+    os.makedirs(obj_dir, exist_ok=True)
     tmp = OUT + ".tmp"
     # MIE_NVCC_FLAGS adds flags, e.g. "-DMIE_DEBUG_CHECKS" for the self-checking build.
     extra = os.environ.get("MIE_NVCC_FLAGS", "").split()
-    cmd = [
-        nvcc(), *ARCH_FLAGS, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-shared",
-        *extra, "-I", INCLUDE, "-o", tmp, *[os.path.join(CSRC, s) for s in SOURCES],
-    ]
+    common = [nvcc(), *ARCH_FLAGS, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", *extra, "-I", INCLUDE]
     if verbose:
-        cmd.insert(1, "-Xptxas=-v")
-        print(" ".join(cmd))
-    res = subprocess.run(cmd, capture_output=True, text=True)
+        common.insert(1, "-Xptxas=-v")
+
+    def compile_one(src: str):
+        obj = os.path.join(obj_dir, os.path.splitext(src)[0] + ".o")
+        cmd = [*common, "-c", "-o", obj, os.path.join(CSRC, src)]
+        return obj, subprocess.run(cmd, capture_output=True, text=True)
+
+    with ThreadPoolExecutor(max_workers=max(1, min(len(SOURCES), os.cpu_count() or 1))) as pool:
+        results = list(pool.map(compile_one, SOURCES))
+    objs = []
+    for (obj, res), src in zip(results, SOURCES):
+        if res.returncode != 0:
+            raise RuntimeError(f"nvcc failed on {src} ({res.returncode}):\n{res.stdout}\n{res.stderr}")
+        if verbose:
+            print(src, res.stderr)
+        objs.append(obj)
+    res = subprocess.run([nvcc(), *ARCH_FLAGS, "-shared", "-o", tmp, *objs], capture_output=True, text=True)
     if res.returncode != 0:
-        raise RuntimeError(f"nvcc failed ({res.returncode}):\n{res.stdout}\n{res.stderr}")
-    if verbose:
-        print(res.stderr)
+        raise RuntimeError(f"nvcc link failed ({res.returncode}):\n{res.stdout}\n{res.stderr}")
+    for obj in objs:
+        os.remove(obj)
     os.replace(tmp, OUT)
     return OUT
 

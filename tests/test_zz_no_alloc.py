@@ -7,13 +7,15 @@ cudaFree, because those calls can synchronise the device.  For them,
 mie_attn_decode_fixed_scratch keeps the split-K partials and merge counters in
 one fixed array inside libmie.so (64 counters + 65,536 floats).
 
-These tests call it through the C ABI and require its output to match
-mie_attn_decode (the entry point with caller-provided scratch) on the same
+These tests call it through the C ABI and require its output to equal
+mie_attn_decode's (the entry point with caller-provided scratch) on the same
 inputs, on two calls in a row (the second call reuses the array the first one
-left behind).  The tolerance is the attention tolerance used by the other GPU
-tests (atol 2e-5 / rtol 1e-5 for fp32, 1e-2 for bf16).  A request larger than
-the array must be refused before anything is launched.  This file is named so
-that pytest collects it last.
+left behind).  Both entry points launch the same kernel with the same splits and
+the same merge order, so the outputs must be bitwise identical: a tolerance
+could hide a wrong partials stride.  A request larger than the array, or one
+that asks for a deferred merge, must be refused before anything is launched,
+and a malformed request gets the same error as from mie_attn_decode.  This file
+is named so that pytest collects it last.
 """
 
 import ctypes
@@ -76,13 +78,12 @@ def test_fixed_scratch_matches_allocating_entry_point_twice(dtype):
     capi.check(lib.mie_attn_decode(ctypes.byref(attn_args(cache, q, ctx, want, splits, partials, counters)), stream),
                "mie_attn_decode")
 
-    tol = dict(atol=2e-5, rtol=1e-5) if dtype == torch.float32 else dict(atol=1e-2, rtol=1e-2)
     for call in range(2):
         got = torch.full((H, hd), float("nan"), dtype=dtype, device=DEV)
         a = attn_args(cache, q, ctx, got, splits)  # no scratch pointers passed
         capi.check(lib.mie_attn_decode_fixed_scratch(ctypes.byref(a), stream), "mie_attn_decode_fixed_scratch")
         torch.cuda.synchronize()
-        torch.testing.assert_close(got.float(), want.float(), **tol, msg=lambda m: f"call {call}: {m}")
+        assert torch.equal(got, want), f"call {call}: max |diff| {float((got.float() - want.float()).abs().max())}"
 
 
 def test_fixed_scratch_refuses_requests_beyond_its_size():
@@ -100,3 +101,25 @@ def test_fixed_scratch_refuses_requests_beyond_its_size():
     torch.cuda.synchronize()
     assert torch.count_nonzero(out) == 0  # nothing was launched
     assert b"fixed scratch" in lib.mie_status_string(capi.MIE_ERR_SCRATCH_LIMIT)
+
+
+def test_fixed_scratch_refuses_deferred_merge_and_malformed_requests():
+    lib = capi.ensure_init(torch.device(DEV))
+    cache, q, ctx = paged_inputs(torch.float32, ctx=64)
+    H, hd = q.shape
+    stream = capi.stream_handle(torch.device(DEV))
+    out = torch.zeros(H, hd, device=DEV)
+    a = attn_args(cache, q, ctx, out, splits=2)
+    a.defer_merge = 1  # partials would stay in the library's array
+    assert lib.mie_attn_decode_fixed_scratch(ctypes.byref(a), stream) == capi.MIE_ERR_INVALID
+    a = attn_args(cache, q, ctx, out, splits=2)
+    a.q = None  # malformed: the same error as the allocating entry point, not a size error
+    assert lib.mie_attn_decode_fixed_scratch(ctypes.byref(a), stream) == capi.MIE_ERR_INVALID
+    a = attn_args(cache, q, ctx, out, splits=2)
+    a.head_dim = 48  # unsupported head size
+    assert lib.mie_attn_decode_fixed_scratch(ctypes.byref(a), stream) == capi.MIE_ERR_UNSUPPORTED
+    a = attn_args(cache, q, ctx, out, splits=2)
+    a.num_heads, a.q = 65, None  # malformed AND beyond the array: the request check comes first
+    assert lib.mie_attn_decode_fixed_scratch(ctypes.byref(a), stream) == capi.MIE_ERR_INVALID
+    torch.cuda.synchronize()
+    assert torch.count_nonzero(out) == 0  # nothing was launched
