@@ -321,6 +321,17 @@ typedef struct mie_step_desc {
    * use_pdl the launch is programmatic-dependent: the next step's CTAs stage
    * their first weights while this step's last CTA finishes the LM head. */
   const int32_t* step_limit;
+  /* Persistent step: every wait on another CTA's result or on a bulk copy
+   * gives up after this many nanoseconds (0: the default, 200 ms); the step
+   * then ends with MIE_ERR_TIMEOUT in *status and the caller zeroes
+   * step_scratch before the next step. */
+  int64_t wait_limit_ns;
+  /* Persistent step: when non-NULL, the step starts only once *start_gate is
+   * nonzero -- a flag written by another stream, a peer GPU or the host
+   * through mapped memory, for a step queued ahead of the input it reads.  A
+   * gate still closed after wait_limit_ns ends the step with MIE_ERR_TIMEOUT
+   * before it changes anything. */
+  const int32_t* start_gate;
 } mie_step_desc;
 
 /* Prefill GEMM on the tcgen05 tensor cores: C = A . B^T with A [M, K] and

@@ -491,6 +491,7 @@ int mie_decode_step(const mie_step_desc* d, void* stream) {
     return step_launch(*d, g, d->step_scratch, static_cast<cudaStream_t>(stream));
   }
   if (d->sample_temperature > 0.f) return MIE_ERR_UNSUPPORTED;  // before any launch
+  if (d->start_gate) return MIE_ERR_UNSUPPORTED;  // the start gate is a persistent-step feature
   for (int l = 0; l < d->num_layers; ++l) {
     const int rc = mie_decode_layer(d, l, stream);
     if (rc) return rc;

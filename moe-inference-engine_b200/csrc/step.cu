@@ -94,6 +94,9 @@ __device__ unsigned long long g_step_stamps[160 * kStampLayers * kStampPoints];
   } while (0)
 #endif
 
+// Limit of every wait of this step (ns), set in the step prologue.
+__shared__ unsigned long long wait_ns_s;
+
 // ---------------------------------------------------------------------------
 // Exchange words
 // ---------------------------------------------------------------------------
@@ -119,7 +122,7 @@ __device__ __noinline__ bool ll_give_up(uint64_t* hdr, int32_t* status, unsigned
     *t0 = t;
     return false;
   }
-  if (t - *t0 <= kWaitLimitNs) return false;
+  if (t - *t0 <= wait_ns_s) return false;
   set_status(status, MIE_ERR_TIMEOUT);
   atomicExch(reinterpret_cast<unsigned long long*>(hdr + kHdrAbort), 1ull);
   return true;
@@ -339,7 +342,7 @@ __device__ __noinline__ void bulk_copy(void* dst, const void* src, uint32_t byte
 }
 // Every thread: wait for the oldest armed phase of barrier b (bounded).
 __device__ __noinline__ bool bar_wait(int b, uint64_t* hdr, int32_t* status) {
-  const bool ok = mbar_wait(&bars_s[b], bar_done_s[b] & 1u, status);
+  const bool ok = mbar_wait(&bars_s[b], bar_done_s[b] & 1u, status, wait_ns_s);
   if (!ok) atomicExch(reinterpret_cast<unsigned long long*>(hdr + kHdrAbort), 1ull);
   const int bad = __syncthreads_or(!ok);
   if (threadIdx.x == 0) bar_done_s[b] += 1;
@@ -358,7 +361,7 @@ __device__ __noinline__ bool recv_part(const uint64_t* buf, int n, uint32_t tag,
   int bad = recv_poll<kProjThreads>(buf, n, tag, dst, nullptr, hdr, status, nullptr);
   bool waited = false;
   if (!bad) {
-    waited = mbar_wait(&bars_s[b], bar_done_s[b] & 1u, status);
+    waited = mbar_wait(&bars_s[b], bar_done_s[b] & 1u, status, wait_ns_s);
     if (!waited) {
       atomicExch(reinterpret_cast<unsigned long long*>(hdr + kHdrAbort), 1ull);
       bad = 1;
@@ -614,7 +617,7 @@ __device__ __noinline__ bool recv_norm(const uint64_t* buf, int D, uint32_t tag,
   if ((threadIdx.x & 31) == 0) red_s[threadIdx.x >> 5] = s2;  // last read of red_s: behind a barrier
   bool waited = false;
   if (bar >= 0 && !bad) {
-    waited = mbar_wait(&bars_s[bar], bar_done_s[bar] & 1u, status);
+    waited = mbar_wait(&bars_s[bar], bar_done_s[bar] & 1u, status, wait_ns_s);
     if (!waited) {
       atomicExch(reinterpret_cast<unsigned long long*>(hdr + kHdrAbort), 1ull);
       bad = 1;
@@ -790,7 +793,7 @@ __device__ __noinline__ bool att_core(const StepParams& P, int l, int h, int t0,
     STEP_STAMP(l, 19);
     // every thread waits for the chunk's copies itself; whether all waits
     // succeeded is agreed at the barrier of the max below
-    const bool kv_ok = mbar_wait(&bars_s[kBarKv], bar_done_s[kBarKv] & 1u, d.status);
+    const bool kv_ok = mbar_wait(&bars_s[kBarKv], bar_done_s[kBarKv] & 1u, d.status, wait_ns_s);
     if (!kv_ok) atomicExch(reinterpret_cast<unsigned long long*>(g.ll + kHdrAbort), 1ull);
     STEP_STAMP(l, 20);
     float mloc = -INFINITY;
@@ -1584,6 +1587,17 @@ __device__ __noinline__ bool head_phase(const StepParams& P) {
   return true;
 }
 
+// Wait (bounded by limit_ns) until the start gate *gate is nonzero; false when
+// it stayed closed.  Acquire: what the gate's writer wrote before opening it is
+// visible afterwards.
+__device__ __noinline__ bool gate_open(const int32_t* gate, unsigned long long limit_ns) {
+  const unsigned long long t0 = global_ns();
+#pragma unroll 1
+  while (ld_acquire_gpu(reinterpret_cast<const uint32_t*>(gate)) == 0u)
+    if (global_ns() - t0 > limit_ns) return false;
+  return true;
+}
+
 template <typename W, typename KV, bool kWide>
 __global__ void __launch_bounds__(kST, 1) step_kernel(const __grid_constant__ StepParams P) {
   STEP_STAMP(P.d.num_layers, 3);
@@ -1635,6 +1649,11 @@ __global__ void __launch_bounds__(kST, 1) step_kernel(const __grid_constant__ St
     const int p = __ldcg(d.pos);
     const int64_t t = __ldcg(d.token);
     int stop = done_v || (d.step_limit && d.log_count && lc >= lim);
+    wait_ns_s = d.wait_limit_ns > 0 ? (unsigned long long)d.wait_limit_ns : kWaitLimitNs;
+    if (!stop && d.start_gate && !gate_open(d.start_gate, wait_ns_s)) {
+      set_status(d.status, MIE_ERR_TIMEOUT);  // the gate stayed closed: the step changes nothing
+      stop = 1;
+    }
     cx_s.step = (uint32_t)hstep + 1u;
     cx_s.log_k = lc;
     if (!stop && (p < 0 || p >= d.max_pos || t < 0 || t >= d.vocab)) {

@@ -103,7 +103,8 @@ class StepDesc(ctypes.Structure):
         ("moe_sync", _p), ("lm_partial_val", _p), ("lm_partial_idx", _p), ("lm_counter", _p),
         ("logits", _p), ("status", _p), ("attn_splits", _i), ("max_splits", _i), ("lm_grid", _i),
         ("use_pdl", _i), ("step_scratch", _p), ("step_scratch_bytes", _i64), ("sample_temperature", _f),
-        ("sample_top_k", _i), ("sample_seed", _p), ("step_limit", _p),
+        ("sample_top_k", _i), ("sample_seed", _p), ("step_limit", _p), ("wait_limit_ns", _i64),
+        ("start_gate", _p),
     ]
 
 

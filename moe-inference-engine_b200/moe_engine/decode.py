@@ -114,6 +114,11 @@ class DecodeRunner:
         # MIE_PERSISTENT=0 selects the per-op launch sequence.
         self.persistent = os.environ.get("MIE_PERSISTENT", "1") != "0"
         self.step_scratch = None  # int64 words, zeroed once
+        # Persistent step: limit of every device-side wait (0: the library's
+        # default, 200 ms) and an optional start gate (an int32 device flag the
+        # step waits for before it reads its input).
+        self.wait_limit_ns = 0
+        self.start_gate = None
 
     # ---- descriptors --------------------------------------------------------
     def param_signature(self):
@@ -224,6 +229,8 @@ class DecodeRunner:
         d.step_limit = self.step_limit.data_ptr() if limit and graph else None
         d.step_scratch = None
         d.step_scratch_bytes = 0
+        d.wait_limit_ns = int(self.wait_limit_ns)
+        d.start_gate = capi.ptr(self.start_gate)
         if self.persistent:
             with torch.cuda.device(self.device):
                 need = int(self.lib.mie_step_scratch_bytes(ctypes.byref(d)))

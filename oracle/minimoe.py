@@ -402,7 +402,9 @@ class Decoder:
 
     ``kv_dtype`` rounds cached K/V the way a cache of that dtype stores them
     (bf16 for the bf16 kernels).  ``record`` keeps per-layer residual streams
-    of the last forward for hidden-state comparisons.
+    of the last forward for hidden-state comparisons, and per layer the router
+    gap of the last position (second minus third largest logit): below ~1e-3 a
+    bf16 computation of the same layer may select another expert pair.
     """
 
     def __init__(self, P: dict, arch: Arch, kv_dtype=torch.float32, max_seq=None):
@@ -429,6 +431,7 @@ class Decoder:
         positions = torch.arange(pos0, pos0 + T)
         x = _embed(P, arch, ids, positions)
         self.hidden = []
+        self.router_gap = []
         for layer in range(arch.num_layers):
             h = norm(x, P, f"MoEBlocks.{layer}.attn_norm", arch)
             q, k, v = _qkv(h, P, layer, arch, positions, self.cos, self.sin)
@@ -439,9 +442,12 @@ class Decoder:
             a = attention(q, keys, vals, causal=T > 1, q_offset=pos0)
             x = x + _out_proj(a, P, layer, arch)
             h = norm(x, P, f"MoEBlocks.{layer}.moe_norm", arch)
-            x = x + moe_forward(h, P, layer, arch)[0]
+            out, (logits, _, _) = moe_forward(h, P, layer, arch)
+            x = x + out
             if record:
                 self.hidden.append(x[0, -1].clone())
+                top = logits[-1].sort(descending=True).values
+                self.router_gap.append(float(top[arch.top_k - 1] - top[arch.top_k]))
         self.position += T
         return _lm_head(x, P, arch)
 

@@ -78,3 +78,27 @@ def oracle_prefill_with_margins(P: dict, arch, ids: torch.Tensor, kv_dtype=torch
         margin = torch.minimum(margin, top[:, 1] - top[:, 2])
         x = x + out
     return om._lm_head(x, P, arch)[0], margin
+
+
+def baseline_bf16_model(max_seq: int = 1536, num_layers: int = 12, seed: int = 0, device="cuda"):
+    """(bf16 engine model on `device`, fp32 oracle params, oracle arch) of the
+    BASELINE architecture with `num_layers` layers and context `max_seq`."""
+    arch = oracle.BASELINE_ARCH.with_(max_seq_length=max_seq, num_layers=num_layers)
+    P = oracle.init_params(arch, seed=seed)
+    from moe_engine.model import baseline_config
+
+    m = Model(baseline_config(max_seq_length=max_seq, num_layers=num_layers)).eval()
+    m.load_state_dict(engine_state_dict(P))
+    return m.to(device, torch.bfloat16), P, arch
+
+
+def shuffled_paged_cache(m: Model, max_seq: int, shuffle_seed: int = 0):
+    """A fresh paged cache (block 16, direct attention) whose free list is
+    shuffled, so logical blocks map to scattered physical blocks."""
+    import random
+
+    alloc = m.new_block_allocator(num_blocks=-(-max_seq // 16) + 8, block_size=16, attention_mode="direct")
+    free = list(alloc.free_blocks)
+    random.Random(shuffle_seed).shuffle(free)
+    alloc.free_blocks = free
+    return alloc.new_cache()
