@@ -332,7 +332,14 @@ typedef struct mie_step_desc {
    * gate still closed after wait_limit_ns ends the step with MIE_ERR_TIMEOUT
    * before it changes anything. */
   const int32_t* start_gate;
+  /* Which persistent step kernel runs the step (step_scratch set):
+   * MIE_STEP_AUTO picks the cluster kernel when it takes the shapes, else the
+   * one-CTA-per-SM kernel; the other two force one (MIE_ERR_UNSUPPORTED when
+   * the forced kernel cannot take the shapes). */
+  int step_kernel;
 } mie_step_desc;
+
+enum { MIE_STEP_AUTO = 0, MIE_STEP_FLAT = 1, MIE_STEP_CLUSTER = 2 };
 
 /* Prefill GEMM on the tcgen05 tensor cores: C = A . B^T with A [M, K] and
  * B [N, K] bf16 row-major (rows of K elements), fp32 accumulation, then one of
@@ -489,6 +496,13 @@ int mie_decode_step(const mie_step_desc* d, void* stream);
  * support it (hidden_dim and expert_hidden_dim <= 768, head_dim <= 128, no
  * expert parallelism, num_layers <= 48).  Launches nothing. */
 int64_t mie_step_scratch_bytes(const mie_step_desc* d);
+/* Which persistent kernel mie_decode_step would run for this description on
+ * the current device: MIE_STEP_CLUSTER (clusters of 6 CTAs; bf16, head_dim
+ * 64, RMSNorm, RoPE, SwiGLU, no biases, greedy) or MIE_STEP_FLAT (one CTA per
+ * SM; every other supported shape), or -status.  Launches nothing.  No
+ * counterpart in the reference (its decode step is a sequence of Python-level
+ * ops, src/moe_engine/model.py:543-565). */
+int mie_step_kernel_of(const mie_step_desc* d);
 int mie_decode_layer(const mie_step_desc* d, int layer, void* stream);
 int mie_decode_head(const mie_step_desc* d, void* stream);
 

@@ -310,14 +310,34 @@ mie_lmhead_args step_lmhead(const mie_step_desc& d) {
   return a;
 }
 
+// The persistent kernel that runs a step and its geometry.
+struct StepPlan {
+  int cluster;  // 1: the cluster step (cg), 0: the one-CTA-per-SM step (g)
+  StepGeom g;
+  CGeom cg;
+  int64_t words() const { return cluster ? cg.words : g.words; }
+};
+
 // Persistent step: geometry for this device plus the checks the per-op
 // launchers would otherwise make (alignment of every weight row base and of
-// the K/V caches, which the kernel copies in 16-byte units).
-int persistent_geometry(const mie_step_desc& d, StepGeom* g) {
+// the K/V caches, which the kernel copies in 16-byte units).  The cluster
+// step runs every step whose shapes it takes, unless d.step_kernel forces
+// the one-CTA-per-SM step.
+int persistent_geometry(const mie_step_desc& d, StepPlan* plan) {
   if (!d.layers || !d.embedding || !d.token || !d.pos || !d.x || !d.lm_partial_val || !d.lm_partial_idx ||
       !d.lm_counter)
     return MIE_ERR_INVALID;
-  const int rc = step_geometry(d, num_sms(), g);
+  if (d.step_kernel < MIE_STEP_AUTO || d.step_kernel > MIE_STEP_CLUSTER) return MIE_ERR_INVALID;
+  plan->cluster = 0;
+  int rc = MIE_ERR_UNSUPPORTED;
+  if (d.step_kernel != MIE_STEP_FLAT) {
+    rc = cstep_geometry(d, &plan->cg);
+    if (rc == MIE_OK)
+      plan->cluster = 1;
+    else if (d.step_kernel == MIE_STEP_CLUSTER)
+      return rc;
+  }
+  if (!plan->cluster) rc = step_geometry(d, num_sms(), &plan->g);
   if (rc) return rc;
   if (d.norm != MIE_NORM_NONE && !d.final_norm_w) return MIE_ERR_INVALID;
   if ((d.rope_cos == nullptr) != (d.rope_sin == nullptr)) return MIE_ERR_INVALID;
@@ -388,6 +408,7 @@ int mie_init(int device) {
   attn_set_attributes();
   gemv_set_attributes();
   step_set_attributes();
+  cstep_set_attributes();
   gemm_set_attributes();
   (void)num_sms();
   const cudaError_t e = cudaGetLastError();
@@ -484,11 +505,12 @@ int mie_decode_head(const mie_step_desc* d, void* stream) {
 int mie_decode_step(const mie_step_desc* d, void* stream) {
   if (!d) return MIE_ERR_INVALID;
   if (d->step_scratch) {
-    StepGeom g;
-    const int rc = persistent_geometry(*d, &g);
+    StepPlan plan;
+    const int rc = persistent_geometry(*d, &plan);
     if (rc) return rc;
-    if (d->step_scratch_bytes < g.words * (int64_t)sizeof(uint64_t)) return MIE_ERR_INVALID;
-    return step_launch(*d, g, d->step_scratch, static_cast<cudaStream_t>(stream));
+    if (d->step_scratch_bytes < plan.words() * (int64_t)sizeof(uint64_t)) return MIE_ERR_INVALID;
+    if (plan.cluster) return cstep_launch(*d, plan.cg, d->step_scratch, static_cast<cudaStream_t>(stream));
+    return step_launch(*d, plan.g, d->step_scratch, static_cast<cudaStream_t>(stream));
   }
   if (d->sample_temperature > 0.f) return MIE_ERR_UNSUPPORTED;  // before any launch
   if (d->start_gate) return MIE_ERR_UNSUPPORTED;  // the start gate is a persistent-step feature
@@ -499,12 +521,20 @@ int mie_decode_step(const mie_step_desc* d, void* stream) {
   return mie_decode_head(d, stream);
 }
 
+int mie_step_kernel_of(const mie_step_desc* d) {
+  if (!d) return -MIE_ERR_INVALID;
+  StepPlan plan;
+  const int rc = persistent_geometry(*d, &plan);
+  if (rc) return -rc;
+  return plan.cluster ? MIE_STEP_CLUSTER : MIE_STEP_FLAT;
+}
+
 int64_t mie_step_scratch_bytes(const mie_step_desc* d) {
   if (!d) return -MIE_ERR_INVALID;
-  StepGeom g;
-  const int rc = persistent_geometry(*d, &g);
+  StepPlan plan;
+  const int rc = persistent_geometry(*d, &plan);
   if (rc) return -(int64_t)rc;
-  return g.words * (int64_t)sizeof(uint64_t);
+  return plan.words() * (int64_t)sizeof(uint64_t);
 }
 
 }  // extern "C"

@@ -81,6 +81,39 @@ struct StepParams {
   mie_layer_desc layers[kMaxStepLayers];
 };
 
+// ---- persistent decode step on thread-block clusters (step_cluster.cu) ----
+constexpr int kStepCluster = 6;   // CTAs per cluster = attention splits per head
+constexpr int kClusterHeadDim = 64;  // head_dim of the cluster step
+
+// Geometry of one cluster-step launch: exchange-buffer offsets (64-bit words
+// into the caller's scratch) and the shared-memory layout (bytes).
+struct CGeom {
+  uint64_t* ll;   // scratch base
+  int64_t words;  // scratch size in 64-bit words
+  int64_t off_x[2], off_p[2], off_h[2];  // x of a layer [D], out_proj partials [H, D], expert hidden [2 Hx]
+  int G, NC;      // CTAs, clusters (G = NC * kStepCluster)
+  int chunk_tok;  // K/V tokens per shared-memory chunk
+  int np_max, nv_max;  // RoPE pairs / v rows of one split (upper bounds)
+  int orows;      // out_proj rows of one split (upper bound)
+  int nu_max, nr_max;  // up units / down rows of one CTA (upper bounds)
+  int head_rows, head_stages;  // LM-head ring
+  // staging regions: A (q/k/v rows, then the selected experts' gate/up rows),
+  // K (K then V chunk), O (out_proj tile), D (down rows), R (router + norms)
+  uint32_t sm_a, sm_k, sm_o, sm_d, sm_r;
+  // fp32 vectors: x, normalised x, x_mid [2][D], x_mid square sums [2][CS],
+  // gathered q / k_new / v_new [2][3][hd], merge partials [2][CS][hd + 4],
+  // own q/k/v GEMV results, scores, scratch, expert hidden [2 Hx], received
+  // partials [H + 1][orows], merged o [hd]
+  uint32_t sm_x, sm_xn, sm_xm, sm_ss, sm_g, sm_mg, sm_qkv, sm_sc, sm_ab, sm_h, sm_pr, sm_ov;
+  uint32_t smem;
+};
+
+struct CStepParams {
+  mie_step_desc d;  // d.layers is not used on the device
+  CGeom g;
+  mie_layer_desc layers[kMaxStepLayers];
+};
+
 // Allow the largest dynamic shared memory the device permits next to the
 // kernel's static shared memory.
 template <typename Kernel>
@@ -145,6 +178,10 @@ void gemv_set_attributes();
 int step_geometry(const mie_step_desc& d, int grid, StepGeom* g);
 int step_launch(const mie_step_desc& d, const StepGeom& g, uint64_t* scratch, cudaStream_t st);
 void step_set_attributes();
+// step_cluster.cu: MIE_OK when the cluster step takes `d` (and fills *g)
+int cstep_geometry(const mie_step_desc& d, CGeom* g);
+int cstep_launch(const mie_step_desc& d, const CGeom& g, uint64_t* scratch, cudaStream_t st);
+void cstep_set_attributes();
 // step_wide.cu (the wide variant of the persistent step, its own translation unit)
 int step_launch_wide(const StepParams& p, cudaStream_t st);
 void step_set_attributes_wide();

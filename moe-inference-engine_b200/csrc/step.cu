@@ -59,6 +59,7 @@
 // the host must zero the scratch before the next step.
 //
 // Every reduction has a fixed order: results are bit-reproducible run to run.
+#include "exchange.cuh"
 #include "kernels.h"
 #include "stream.cuh"
 
@@ -100,18 +101,6 @@ __shared__ unsigned long long wait_ns_s;
 // ---------------------------------------------------------------------------
 // Exchange words
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ void ll_put(uint64_t* p, float v, uint32_t tag) {
-  const uint64_t w = ((uint64_t)tag << 32) | (uint64_t)__float_as_uint(v);
-  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
-}
-__device__ __forceinline__ uint64_t ll_ld(const uint64_t* p) {
-  uint64_t v;
-  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ uint32_t ll_tag(uint64_t w) { return (uint32_t)(w >> 32); }
-__device__ __forceinline__ float ll_val(uint64_t w) { return __uint_as_float((uint32_t)w); }
-
 // Slow path of a wait, every 64 polls: true when another CTA raised the abort
 // word or this wait has run for kWaitLimitNs (then MIE_ERR_TIMEOUT is
 // recorded and the abort word raised).

@@ -1,0 +1,1362 @@
+// Persistent decode step on thread-block clusters, sm_100a.
+//
+// The whole batch-one decode step (all layers + LM head) in ONE launch, like
+// the one-CTA-per-SM step of step.cu, but laid out on clusters of
+// kStepCluster (6) CTAs so that the work that stays inside one attention head
+// synchronises through distributed shared memory (a cluster barrier, ~0.25 us
+// on B200) instead of device-wide exchanges (~1.1 us each), and so that no
+// CTA repeats another's work.  Shapes: bf16 weights and cache, head_dim 64,
+// hidden <= 768, RMSNorm, RoPE, SwiGLU experts, top-2, no biases, greedy
+// argmax -- the BASELINE miniMoE family; the dataflow is the reference's
+// decode step (src/moe_engine/model.py:494-498, 543-565).
+//
+// Grid: NC clusters (as many as the GPU holds at once: 22 on a 148-SM B200,
+// 132 CTAs), 512 threads per CTA.  Cluster h < num_heads is head h's
+// attention group; CTA s of it is split s of the head's old tokens and owns
+// RoPE pairs / v rows / out_proj rows share s of the head.
+//
+// Per layer l (tags (step << 8) | l on every exchange word):
+//
+//   ATT (attention clusters)
+//     x <- exchange X (or the token embedding at l = 0); RMSNorm
+//     this CTA's q and k rows (whole RoPE pairs) and v rows from shared
+//       memory; RoPE; k, v rounded to the cache type and stored into the
+//       position's cache slot; q, k_new, v_new sent to every CTA of the
+//       cluster (DSMEM) -- cluster barrier 1
+//     online softmax over this split's old tokens (staged K/V chunk)
+//     (m, l, acc) sent to every CTA of the cluster -- cluster barrier 2
+//     every CTA merges the head (log-sum-exp, the new token as one more
+//       term) -> o_h [hd]; its out_proj rows times o_h (a TMA tile of
+//       out_proj's columns of head h) -> exchange P[h] (the head's partial
+//       of out_proj . o)
+//   MOE (every cluster)
+//     CTA s receives rows share s of P (every head) and of x, sums them
+//       (x_mid = x + sum_h P[h]) and sends its rows and their square sum to
+//       every CTA of the cluster -- cluster barrier 3
+//     RMSNorm -> router -> top-2 (ties to the lower id) -> 2-way softmax
+//     the selected experts' gate/up rows of this CTA's units and down rows of
+//       its output rows are bulk-copied into shared memory
+//     up units: silu(gate) * up -> exchange H
+//     down rows of both slots . h + residual -> exchange X of layer l + 1
+//
+// HEAD: x_L -> final norm -> this CTA's tied LM-head rows (a ring of bulk
+// copies) -> argmax -> the last CTA reduces the CTA results and does the
+// step's device bookkeeping (token, position + 1, token log, EOS flag).
+//
+// Weights never pass through registers ahead of use: every GEMV reads rows
+// that bulk copies (cp.async.bulk / cp.async.bulk.tensor, no multicast) put
+// in shared memory earlier -- the next layer's q/k/v rows right after this
+// layer's up GEMV, its K/V chunk right after this layer's attention, its
+// out_proj tile right after this layer's out_proj, its router and norm
+// weights right after this layer's routing.
+//
+// Buffer reuse.  Device-wide exchange buffers alternate by layer parity; a
+// copy is rewritten two layers later only after every CTA consumed it (the
+// data dependencies of the layer in between order the reads first).  The
+// cluster gather buffers alternate by layer parity as well, and every remote
+// write happens just before a cluster barrier that every CTA of the cluster
+// passes after its last read of the previous use.
+//
+// Failure.  Every wait is bounded (mie_step_desc.wait_limit_ns).  A CTA that
+// gives up records MIE_ERR_TIMEOUT and raises the abort word; from then on it
+// runs the step's program without waiting, computing or writing -- but it
+// still takes every cluster barrier, so no CTA of its cluster is ever left
+// waiting at one -- drains its bulk copies and leaves.  The host zeroes the
+// scratch before the next step.
+//
+// Every reduction has a fixed order: results are bit-reproducible, and every
+// CTA that computes a value redundantly (x_mid, the router's choice, o_h)
+// computes the same bits.
+#include <mutex>
+
+#include "exchange.cuh"
+#include "kernels.h"
+#include "stream.cuh"
+
+namespace mie {
+
+namespace {
+
+using bf16 = __nv_bfloat16;
+constexpr int kT = kStepThreads;      // 512 threads
+constexpr int kW = kT / 32;           // 16 warps
+constexpr int kCS = kStepCluster;     // CTAs per cluster
+constexpr int kHd = kClusterHeadDim;  // head_dim
+constexpr int kPV = 8;                // bf16 elements per 16-byte vector
+constexpr int kMg = kHd + 4;          // merge partial: acc [hd], m, l (padded)
+
+constexpr int kHdrStep = 0, kHdrAbort = 1;  // scratch header words
+
+// mbarriers: A (q/k/v rows, then the selected experts' gate/up rows), K (K/V
+// chunk), O (out_proj tile), R (router + norm weights), D (down rows), then
+// the LM-head ring stages
+constexpr int kBA = 0, kBK = 1, kBO = 2, kBR = 3, kBD = 4, kBH = 5;
+constexpr int kNB = kBH + kStepHeadStagesMax;
+constexpr int kBlkCache = 64;  // block ids of a split cached per step
+
+#ifdef MIE_STEP_STAMPS
+constexpr int kStampLayers = kMaxStepLayers + 1, kStampPoints = 32;
+__device__ unsigned long long g_cstep_stamps[160 * kStampLayers * kStampPoints];
+// SM cycle counter (clock64): durations inside one CTA are exact
+#define CSTAMP(l, k)                                                                                   \
+  do {                                                                                                 \
+    if (threadIdx.x == 0) g_cstep_stamps[(blockIdx.x * kStampLayers + (l)) * kStampPoints + (k)] = clock64(); \
+  } while (0)
+#else
+#define CSTAMP(l, k) \
+  do {               \
+  } while (0)
+#endif
+
+struct CCtx {
+  int pos;        // position of the input token
+  int stop;       // nonzero: skip the step (EOS reached, step limit, bad input)
+  uint32_t step;  // this step's number (tags)
+  int64_t tok;    // input token
+  int64_t slot;   // cache offset of the new token's slot (head 0)
+  int last;       // this CTA finished the LM head last
+  int blk0;       // first cache block of this CTA's old tokens
+  int log_k;      // *log_count at the start of the step
+  int sel0, sel1; // the layer's experts
+  float wt0, wt1; // and their weights
+  float snew;     // scale * q . k_new
+};
+__shared__ CCtx cx;
+__shared__ unsigned long long lim_s;  // limit of every wait (ns)
+struct CShared {
+  mie_step_desc d;
+  CGeom g;
+};
+__shared__ CShared ps;
+constexpr int kLaySlots = 4;
+__shared__ mie_layer_desc lay_s[kLaySlots];
+__shared__ float red_s[kW], red2_s[kW];
+__shared__ int blk_s[kBlkCache];
+__shared__ float bestv_s[kW];
+__shared__ int besti_s[kW];
+__shared__ __align__(8) uint64_t bars_s[kNB];
+__shared__ uint32_t armed_s[kNB], done_s[kNB];
+extern __shared__ __align__(128) uint8_t sm[];
+
+template <typename T>
+__device__ __forceinline__ T* at(uint32_t off) {
+  return reinterpret_cast<T*>(sm + off);
+}
+__device__ __forceinline__ const mie_layer_desc& layer_at(int l) { return lay_s[l & (kLaySlots - 1)]; }
+__device__ __forceinline__ uint32_t tag_of(int l) { return (cx.step << 8) | (uint32_t)l; }
+__device__ __forceinline__ void split32(int total, int c, int g, int* b, int* e) {
+  *b = (int)(((uint32_t)total * (uint32_t)c) / (uint32_t)g);
+  *e = (int)(((uint32_t)total * (uint32_t)(c + 1)) / (uint32_t)g);
+}
+__device__ __forceinline__ float silu(float v) { return v / (1.0f + expf(-v)); }
+__device__ __forceinline__ bool better(float v, int i, float bv, int bi) { return v > bv || (v == bv && i < bi); }
+__device__ __forceinline__ void raise_abort() {
+  atomicExch(reinterpret_cast<unsigned long long*>(ps.g.ll + kHdrAbort), 1ull);
+}
+__device__ __forceinline__ void layer_fetch(const CStepParams& P, int l, int first) {
+  constexpr int kWords = (int)(sizeof(mie_layer_desc) / 8);
+  const int i = (int)threadIdx.x - first;
+  if (i >= 0 && i < kWords)
+    reinterpret_cast<uint64_t*>(&lay_s[l & (kLaySlots - 1)])[i] = reinterpret_cast<const uint64_t*>(&P.layers[l])[i];
+}
+
+// ---------------------------------------------------------------------------
+// Bounded waits.  Each returns a CTA-uniform verdict: true when `ok` was
+// true and every thread's wait succeeded; a CTA that is no longer ok skips
+// the wait (but still takes the block barrier).
+// ---------------------------------------------------------------------------
+// Slow path of a poll, every 64 rounds: true when another CTA raised the
+// abort word or this wait ran out (then MIE_ERR_TIMEOUT, abort raised).
+__device__ __noinline__ bool give_up(unsigned long long* t0) {
+  if (ll_ld(ps.g.ll + kHdrAbort)) return true;
+  const unsigned long long t = global_ns();
+  if (!*t0) {
+    *t0 = t;
+    return false;
+  }
+  if (t - *t0 <= lim_s) return false;
+  set_status(ps.d.status, MIE_ERR_TIMEOUT);
+  raise_abort();
+  return true;
+}
+
+// Poll n exchange words: dst[i] = value of buf[src(i)] once its tag equals
+// `tag`.  Thread t owns words t, t + kT, ... in groups of four polled
+// together.  1 when this thread gave up.
+template <typename Src>
+__device__ __forceinline__ int poll(const uint64_t* buf, int n, uint32_t tag, float* dst, Src src) {
+  unsigned long long t0 = 0;
+#pragma unroll 1
+  for (int i0 = threadIdx.x; i0 < n; i0 += 4 * kT) {
+    uint64_t w[4];
+    int a[4];
+    unsigned need = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int i = i0 + j * kT;
+      a[j] = i < n ? src(i) : 0;
+      if (i < n) {
+        w[j] = ll_ld(buf + a[j]);
+        need |= 1u << j;
+      }
+    }
+#pragma unroll 1
+    for (int it = 1;; ++it) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if ((need >> j & 1u) && ll_tag(w[j]) == tag) {
+          dst[i0 + j * kT] = ll_val(w[j]);
+          need &= ~(1u << j);
+        }
+      if (!need) break;
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (need >> j & 1u) w[j] = ll_ld(buf + a[j]);
+      if ((it & 63) == 0 && give_up(&t0)) return 1;
+    }
+  }
+  return 0;
+}
+struct Ident {
+  __device__ __forceinline__ int operator()(int i) const { return i; }
+};
+
+// Every thread: wait (bounded) for the oldest armed phase of mbarrier b.
+__device__ __noinline__ bool bwait(bool ok, int b) {
+  bool mine = true;
+  if (ok) {
+    mine = mbar_wait(&bars_s[b], done_s[b] & 1u, ps.d.status, lim_s);
+    if (!mine) raise_abort();
+  }
+  const int bad = __syncthreads_or(!mine);
+  if (ok && mine && threadIdx.x == 0) done_s[b] += 1;  // the phase completed
+  return ok && !bad;
+}
+
+// Before leaving: wait (bounded) for every armed copy not waited for, so no
+// bulk copy lands in shared memory after the CTA left.
+__device__ __noinline__ void drain_copies() {
+  __syncthreads();
+  if (threadIdx.x != 0) return;
+#pragma unroll 1
+  for (int b = 0; b < kNB; ++b)
+    while (done_s[b] < armed_s[b]) {
+      mbar_wait(&bars_s[b], done_s[b] & 1u, nullptr);
+      done_s[b] += 1;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Staging.  Every region is filled by ALL threads of the CTA with 16-byte
+// cp.async copies (thread t copies chunks t, t + kT, ...), each thread then
+// arrives on the region's mbarrier (count kT) once its own copies have
+// landed (cp.async.mbarrier.arrive.noinc).  Issuing costs every thread a few
+// instructions; a bulk (TMA) copy instead holds its issuing thread for about
+// 0.4 us when every SM issues at once, which put the copy issue on the
+// critical path.  Called under CTA-uniform conditions only: every thread
+// must arrive exactly once per phase.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void cp16(void* dst, const void* src, uint64_t pol) {
+  asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src),
+               "l"(pol)
+               : "memory");
+}
+// Every thread: `bytes` (a multiple of 16) from src to dst, chunk j by thread j mod kT.
+__device__ __forceinline__ void stage(void* dst, const void* src, uint32_t bytes, uint64_t pol) {
+#pragma unroll 1
+  for (uint32_t o = threadIdx.x * 16u; o < bytes; o += kT * 16u)
+    cp16(static_cast<uint8_t*>(dst) + o, static_cast<const uint8_t*>(src) + o, pol);
+}
+// Every thread, after its copies of one phase of barrier b: arrive when they land.
+__device__ __forceinline__ void stage_done(int b) {
+  if (threadIdx.x == 0) armed_s[b] += 1;
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(&bars_s[b])) : "memory");
+}
+
+struct Split {
+  int h, s;        // head (cluster), split (rank)
+  int p0, np;      // RoPE pairs [p0, p0 + np)
+  int v0, nv;      // v rows
+  int t0, t1;      // old tokens
+  int r0, nr;      // out_proj rows
+};
+__device__ __forceinline__ Split split_of(int pos) {
+  Split a;
+  a.h = blockIdx.x / kCS;
+  a.s = blockIdx.x % kCS;
+  int e;
+  split32(kHd / 2, a.s, kCS, &a.p0, &e);
+  a.np = e - a.p0;
+  split32(kHd, a.s, kCS, &a.v0, &e);
+  a.nv = e - a.v0;
+  split32(pos, a.s, kCS, &a.t0, &a.t1);
+  split32(ps.d.hidden_dim, a.s, kCS, &a.r0, &e);
+  a.nr = e - a.r0;
+  return a;
+}
+
+// Layer l's q/k/v rows of this split -> region A: q pair first halves, second
+// halves, k pair first halves, second halves, v rows.
+__device__ __noinline__ void issue_qkv(int l) {
+  const mie_step_desc& d = ps.d;
+  const Split a = split_of(cx.pos);
+  const int D = d.hidden_dim;
+  const uint32_t rb = (uint32_t)D * 2u;
+  const uint8_t* w = static_cast<const uint8_t*>(layer_at(l).qkv_w);
+  uint8_t* dst = at<uint8_t>(ps.g.sm_a);
+  const int64_t base = (int64_t)a.h * kHd;
+  const uint64_t pol = policy_evict_first();
+#pragma unroll 1
+  for (int k = 0; k < 4; ++k) {
+    const int64_t row = (k >= 2 ? D : 0) + base + (k & 1) * (kHd / 2) + a.p0;
+    stage(dst + (size_t)k * a.np * rb, w + row * rb, (uint32_t)a.np * rb, pol);
+  }
+  stage(dst + (size_t)4 * a.np * rb, w + (2 * (int64_t)D + base + a.v0) * rb, (uint32_t)a.nv * rb, pol);
+  stage_done(kBA);
+}
+
+// Layer l's out_proj tile of this split -> region O: rows [r0, r0 + nr),
+// the hd columns of head h (row r of the tile at r * hd elements).
+__device__ __noinline__ void issue_otile(int l) {
+  const Split a = split_of(cx.pos);
+  const int D = ps.d.hidden_dim;
+  const bf16* w = static_cast<const bf16*>(layer_at(l).out_w) + (int64_t)a.r0 * D + a.h * kHd;
+  bf16* dst = at<bf16>(ps.g.sm_o);
+  const uint64_t pol = policy_evict_first();
+  constexpr int kPieces = kHd / kPV;  // 16-byte pieces per tile row
+#pragma unroll 1
+  for (int j = threadIdx.x; j < a.nr * kPieces; j += kT) {
+    const int r = j / kPieces, q = j - r * kPieces;
+    cp16(dst + (size_t)r * kHd + q * kPV, w + (int64_t)r * D + q * kPV, pol);
+  }
+  stage_done(kBO);
+}
+
+// Layer l's router rows and both norm weights -> region R, or for l ==
+// num_layers the final norm weights.
+__device__ __noinline__ void issue_side(int l) {
+  const mie_step_desc& d = ps.d;
+  const uint32_t rb = (uint32_t)d.hidden_dim * 2u;
+  uint8_t* dst = at<uint8_t>(ps.g.sm_r);
+  const uint64_t pol = policy_evict_first();
+  if (l == d.num_layers) {
+    stage(dst + (size_t)d.num_experts * rb, d.final_norm_w, rb, pol);
+  } else {
+    const mie_layer_desc& ly = layer_at(l);
+    stage(dst, ly.router_w, (uint32_t)d.num_experts * rb, pol);
+    stage(dst + (size_t)d.num_experts * rb, ly.attn_norm_w, rb, pol);
+    stage(dst + (size_t)(d.num_experts + 1) * rb, ly.moe_norm_w, rb, pol);
+  }
+  stage_done(kBR);
+}
+
+// K/V of tokens [ta, ta + n) of head h, layer l -> region K (K rows, then V
+// rows at chunk_tok): 16-byte piece j of the n K rows then of the n V rows,
+// each through the block table.
+__device__ __noinline__ void issue_kv(int l, int h, int ta, int n) {
+  const mie_step_desc& d = ps.d;
+  const mie_layer_desc& ly = layer_at(l);
+  const int bs = d.block_size;
+  constexpr int kPieces = kHd / kPV;
+  bf16* dst = at<bf16>(ps.g.sm_k);
+  const uint64_t pol = policy_evict_first();
+  const int total = 2 * n * kPieces;
+#pragma unroll 1
+  for (int j = threadIdx.x; j < total; j += kT) {
+    const int v = j >= n * kPieces;
+    const int jj = j - v * n * kPieces, t = jj / kPieces, q = jj - t * kPieces;
+    const int tok = ta + t, bi = tok / bs;
+    int64_t blk = bi;
+    if (d.block_table) {
+      const int k = bi - cx.blk0;
+      const int pb = (k >= 0 && k < kBlkCache) ? blk_s[k] : __ldg(d.block_table + bi);
+      if (pb < 0 || pb >= d.num_blocks) set_status(d.status, MIE_ERR_RANGE);
+      blk = (pb < 0 || pb >= d.num_blocks) ? 0 : pb;
+    }
+    const int64_t off =
+        blk * d.kv_stride_block + (int64_t)h * d.kv_stride_head + (int64_t)(tok % bs) * d.kv_stride_tok + q * kPV;
+    cp16(dst + (size_t)v * ps.g.chunk_tok * kHd + (size_t)t * kHd + q * kPV,
+         static_cast<const bf16*>(v ? ly.v_cache : ly.k_cache) + off, pol);
+  }
+  stage_done(kBK);
+}
+
+// The selected experts' rows of this CTA: gate rows then up rows of its units
+// -> region A (barrier A), down rows of its output rows, slot 0 then slot 1 ->
+// region D (barrier D).
+__device__ __noinline__ void issue_experts(int l, int sel0, int sel1) {
+  const mie_step_desc& d = ps.d;
+  const CGeom& g = ps.g;
+  const mie_layer_desc& ly = layer_at(l);
+  const int D = d.hidden_dim, Hx = d.expert_hidden_dim;
+  const uint32_t rbD = (uint32_t)D * 2u, rbH = (uint32_t)Hx * 2u;
+  int u0, u1, r0, r1;
+  split32(2 * Hx, blockIdx.x, g.G, &u0, &u1);
+  split32(D, blockIdx.x, g.G, &r0, &r1);
+  const int nu = u1 - u0, nr = r1 - r0;
+  const uint64_t pol = policy_evict_first();
+#pragma unroll 1
+  for (int m = 0; m < 2; ++m) {
+    const uint8_t* w = static_cast<const uint8_t*>(m ? ly.w3 : ly.w1);
+#pragma unroll 1
+    for (int k = 0; k < 2; ++k) {
+      const int ua = max(u0, k * Hx), ub = min(u1, (k + 1) * Hx);
+      if (ub > ua)
+        stage(at<uint8_t>(g.sm_a) + (size_t)(m * nu + ua - u0) * rbD,
+              w + ((size_t)(k ? sel1 : sel0) * Hx + ua - k * Hx) * rbD, (uint32_t)(ub - ua) * rbD, pol);
+    }
+  }
+  stage_done(kBA);
+#pragma unroll 1
+  for (int k = 0; k < 2; ++k)
+    stage(at<uint8_t>(g.sm_d) + (size_t)k * nr * rbH,
+          static_cast<const uint8_t*>(ly.w2) + ((size_t)(k ? sel1 : sel0) * D + r0) * rbH, (uint32_t)nr * rbH, pol);
+  stage_done(kBD);
+}
+
+// LM-head stages [first, first + count) of this CTA's vocab rows into the
+// ring over regions A..D; the rows stay in L2 preferentially (evict-last),
+// since every step reads them again.
+__device__ __noinline__ void issue_head(int first, int count) {
+  const mie_step_desc& d = ps.d;
+  const CGeom& g = ps.g;
+  int v0, v1;
+  split32(d.vocab, blockIdx.x, g.G, &v0, &v1);
+  const uint32_t rb = (uint32_t)d.hidden_dim * 2u;
+  const int nst = (v1 - v0 + g.head_rows - 1) / g.head_rows;
+  const uint64_t pol = policy_evict_last();
+#pragma unroll 1
+  for (int i = first; i < first + count && i < nst; ++i) {
+    const int slot = i % g.head_stages;
+    const int r0 = v0 + i * g.head_rows, n = min(g.head_rows, v1 - r0);
+    stage(at<uint8_t>(g.sm_a) + (size_t)slot * g.head_rows * rb,
+          static_cast<const uint8_t*>(d.embedding) + (size_t)r0 * rb, (uint32_t)n * rb, pol);
+    stage_done(kBH + slot);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Compute routines
+// ---------------------------------------------------------------------------
+// out[r] = rows[r] . x for r < n: bf16 rows of nvec 16-byte vectors (<= 96)
+// staged in shared memory, x fp32 in shared memory (rows [split, n) dot x1
+// when x1 is set).  Warp w forms rows w, w + kW, ...: R rows per iteration,
+// one partial sum per 16-byte vector and row.  No barrier.
+template <int R>
+__device__ __forceinline__ void gemv_rows(const uint4* rows, int n, int nvec, const float* xr, const float* xr1,
+                                          int split, float* out) {
+  constexpr int NV = Seg<bf16>::kNV;
+  const int lane = threadIdx.x & 31;
+  const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll 1
+  for (int r = threadIdx.x >> 5; r < n; r += R * kW) {
+    uint4 w[R][NV];
+#pragma unroll
+    for (int k = 0; k < R; ++k) {
+      const int rk = r + k * kW < n ? r + k * kW : r;
+      const uint4* rp = rows + (size_t)rk * nvec;
+#pragma unroll
+      for (int j = 0; j < NV; ++j) {
+        const int v = lane + kWarp * j;
+        w[k][j] = v < nvec ? rp[v] : z;
+      }
+    }
+    float sum[R];
+#pragma unroll
+    for (int k = 0; k < R; ++k) {
+      const float* x = (xr1 && r + k * kW >= split) ? xr1 : xr;
+      sum[k] = 0.f;
+#pragma unroll
+      for (int j = 0; j < NV; ++j) sum[k] += dot_vec(w[k][j], x + j * kPV, 0.f, (const bf16*)nullptr);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+      for (int k = 0; k < R; ++k) sum[k] += __shfl_xor_sync(0xffffffffu, sum[k], o);
+    }
+    if (lane == 0) {
+#pragma unroll
+      for (int k = 0; k < R; ++k)
+        if (r + k * kW < n) out[r + k * kW] = sum[k];
+    }
+  }
+}
+// GEMV of n staged rows (rows [split, n) dot x1 when x1 is set).
+__device__ __noinline__ void gemv(const uint4* rows, int n, int nvec, const float* x, float* out,
+                                  const float* x1 = nullptr, int split = 0) {
+  constexpr int NV = Seg<bf16>::kNV;
+  if ((int)(threadIdx.x >> 5) >= n) return;
+  float xr[NV * kPV];
+  load_x_regs<bf16>(xr, x, nvec);
+  if (x1) {
+    float xr1[NV * kPV];
+    load_x_regs<bf16>(xr1, x1, nvec);
+    gemv_rows<2>(rows, n, nvec, xr, xr1, split, out);
+  } else if (n > 2 * kW) {
+    gemv_rows<3>(rows, n, nvec, xr, nullptr, 0, out);  // up to 48 rows in one pass
+  } else {
+    gemv_rows<2>(rows, n, nvec, xr, nullptr, 0, out);
+  }
+}
+
+// RMSNorm of D fp32 values: out = in * rsqrt(mean(in^2) + eps) * w (w bf16 in
+// shared memory); the sum of squares in a fixed order.  Ends with a barrier.
+__device__ __noinline__ void rms_norm(float* out, const float* in, int D, float eps, const bf16* w) {
+  float s2 = 0.f;
+#pragma unroll 1
+  for (int i = threadIdx.x; i < D; i += kT) s2 = fmaf(in[i], in[i], s2);
+  s2 = warp_sum(s2);
+  if ((threadIdx.x & 31) == 0) red_s[threadIdx.x >> 5] = s2;
+  __syncthreads();
+  float t = 0.f;
+#pragma unroll
+  for (int i = 0; i < kW; ++i) t += red_s[i];
+  const float rs = rsqrtf(t / (float)D + eps);
+#pragma unroll 1
+  for (int i = threadIdx.x; i < D; i += kT) out[i] = (in[i] * rs) * __bfloat162float(w[i]);
+  __syncthreads();
+}
+
+// Online softmax of q over this split's old tokens [t0, t1) in chunks of
+// chunk_tok (the first chunk was staged ahead).  Leaves (acc [hd], m, l) at
+// `res` (acc, then m, l).  q fp32 in shared memory.
+__device__ __noinline__ bool att_core(bool ok, int l, int h, int t0, int t1, const float* q, float* res) {
+  const mie_step_desc& d = ps.d;
+  const CGeom& g = ps.g;
+  const int tid = threadIdx.x, chunk = g.chunk_tok;
+  constexpr int VPH = kHd / kPV;           // 16-byte pieces per K row
+  constexpr int Gp = kT / kHd;             // PV groups
+  const int gi = tid / kHd, dc = tid % kHd;
+  const bf16* ks = at<const bf16>(g.sm_k);
+  const bf16* vs = ks + (size_t)chunk * kHd;
+  float* sc = at<float>(g.sm_sc);
+  float* pv = at<float>(g.sm_ab);  // [Gp][hd]
+  const float scale = d.attn_scale;
+  float m_run = -INFINITY, l_run = 0.f, acc = 0.f;
+  const int nch = (t1 - t0 + chunk - 1) / chunk;
+#pragma unroll 1
+  for (int ci = 0; ci < nch; ++ci) {
+    const int ta = t0 + ci * chunk, n = min(chunk, t1 - ta);
+    if (ci > 0) {
+      __syncthreads();  // the previous chunk is no longer read
+      if (ok) issue_kv(l, h, ta, n);
+    }
+    ok = bwait(ok, kBK);
+    CSTAMP(l, 16);
+    float mloc = -INFINITY;
+    if (ok) {
+#pragma unroll 1
+      for (int t = tid; t < n; t += kT) {
+        const uint4* kr = reinterpret_cast<const uint4*>(ks + (size_t)t * kHd);
+        // the start piece rotates with t: the threads of a warp read distinct banks
+        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll
+        for (int jj = 0; jj < VPH; jj += 4) {
+          const int j0 = (jj + t) & (VPH - 1), j1 = (jj + 1 + t) & (VPH - 1);
+          const int j2 = (jj + 2 + t) & (VPH - 1), j3 = (jj + 3 + t) & (VPH - 1);
+          a0 = dot_vec(kr[j0], q + j0 * kPV, a0, (const bf16*)nullptr);
+          a1 = dot_vec(kr[j1], q + j1 * kPV, a1, (const bf16*)nullptr);
+          a2 = dot_vec(kr[j2], q + j2 * kPV, a2, (const bf16*)nullptr);
+          a3 = dot_vec(kr[j3], q + j3 * kPV, a3, (const bf16*)nullptr);
+        }
+        const float v = ((a0 + a1) + (a2 + a3)) * scale;
+        sc[t] = v;
+        mloc = fmaxf(mloc, v);
+      }
+    }
+    mloc = warp_max(mloc);
+    if ((tid & 31) == 0) red_s[tid >> 5] = mloc;
+    __syncthreads();
+    float bmax = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < kW; ++i) bmax = fmaxf(bmax, red_s[i]);
+    const float mn = fmaxf(m_run, bmax);
+    CSTAMP(l, 17);
+    const float alpha = m_run == -INFINITY ? 0.f : expf(m_run - mn);
+    float ls = 0.f;
+    if (ok) {
+#pragma unroll 1
+      for (int t = tid; t < n; t += kT) {
+        const float p = expf(sc[t] - mn);
+        sc[t] = p;
+        ls += p;
+      }
+    }
+    ls = warp_sum(ls);
+    if ((tid & 31) == 0) red2_s[tid >> 5] = ls;
+    __syncthreads();  // also orders the probabilities before the PV reads
+    float bsum = 0.f;
+#pragma unroll
+    for (int i = 0; i < kW; ++i) bsum += red2_s[i];
+    l_run = l_run * alpha + bsum;
+    m_run = mn;
+    CSTAMP(l, 18);
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+    if (ok) {
+      int t = gi;
+#pragma unroll 1
+      for (; t + 3 * Gp < n; t += 4 * Gp) {
+        a0 = fmaf(sc[t], __bfloat162float(vs[(size_t)t * kHd + dc]), a0);
+        a1 = fmaf(sc[t + Gp], __bfloat162float(vs[(size_t)(t + Gp) * kHd + dc]), a1);
+        a2 = fmaf(sc[t + 2 * Gp], __bfloat162float(vs[(size_t)(t + 2 * Gp) * kHd + dc]), a2);
+        a3 = fmaf(sc[t + 3 * Gp], __bfloat162float(vs[(size_t)(t + 3 * Gp) * kHd + dc]), a3);
+      }
+#pragma unroll 1
+      for (; t < n; t += Gp) a0 = fmaf(sc[t], __bfloat162float(vs[(size_t)t * kHd + dc]), a0);
+    }
+    acc = fmaf(acc, alpha, (a0 + a1) + (a2 + a3));
+    CSTAMP(l, 19);
+  }
+  __syncthreads();  // every chunk read (the K/V region may be restaged), scores scratch free
+  pv[gi * kHd + dc] = acc;
+  __syncthreads();
+  if (tid < kHd) {
+    float s = 0.f;
+#pragma unroll
+    for (int k = 0; k < Gp; ++k) s += pv[k * kHd + tid];
+    res[tid] = s;
+  } else if (tid == kHd) {
+    res[kHd] = m_run;
+    res[kHd + 1] = l_run;
+  }
+  __syncthreads();
+  return ok;
+}
+
+// ---------------------------------------------------------------------------
+// ATT: attention of layer l for the attention clusters (see the file comment)
+// ---------------------------------------------------------------------------
+__device__ __noinline__ bool att_phase(const CStepParams& P, int l, bool ok) {
+  const mie_step_desc& d = ps.d;
+  const CGeom& g = ps.g;
+  const mie_layer_desc& ly = layer_at(l);
+  const int tid = threadIdx.x, D = d.hidden_dim, nvD = D / kPV, par = l & 1;
+  const uint32_t tag = tag_of(l);
+  const int pos = cx.pos;
+  const Split a = split_of(pos);
+  float* xs = at<float>(g.sm_x);
+  float* xn = at<float>(g.sm_xn);
+  const uint32_t rbD = (uint32_t)D * 2u;
+  CSTAMP(l, 0);
+  // ---- x: the token embedding (layer 0) or exchange X ----
+  if (l == 0) {
+    const bf16* e = static_cast<const bf16*>(d.embedding) + cx.tok * D;
+#pragma unroll 1
+    for (int i = tid; i < D; i += kT) xs[i] = __bfloat162float(e[i]);
+    __syncthreads();
+  } else {
+    int bad = 0;
+    if (ok) bad = poll(g.ll + g.off_x[par], D, tag, xs, Ident{});
+    ok = !__syncthreads_or(bad) && ok;
+  }
+  CSTAMP(l, 1);
+  ok = bwait(ok, kBR);  // the layer's norm weights (and router)
+  CSTAMP(l, 12);
+  rms_norm(xn, xs, D, d.eps, at<const bf16>(g.sm_r) + (size_t)d.num_experts * D);
+  // ---- this split's q, k, v rows ----
+  ok = bwait(ok, kBA);
+  CSTAMP(l, 14);
+  float* qo = at<float>(g.sm_qkv);
+  const int nrows = 4 * a.np + a.nv;
+  if (ok) gemv(at<const uint4>(g.sm_a), nrows, nvD, xn, qo);
+  __syncthreads();
+  CSTAMP(l, 2);
+  // ---- RoPE, cache store, send q / k_new / v_new to every CTA of the cluster ----
+  float* gq = at<float>(g.sm_g) + (size_t)par * 3 * kHd;  // [q | k | v] of this layer parity
+  const float* cs = d.rope_cos + (int64_t)pos * (kHd / 2);
+  const float* sn = d.rope_sin + (int64_t)pos * (kHd / 2);
+  const int64_t slot = cx.slot + (int64_t)a.h * d.kv_stride_head;
+  if (ok) {
+    int dim = -1, dim2 = -1;
+    float v1 = 0.f, v2 = 0.f;
+    if (tid < a.np) {  // q pair
+      const int i = a.p0 + tid;
+      const float x1 = qo[tid], x2 = qo[a.np + tid];
+      v1 = x1 * cs[i] - x2 * sn[i];
+      v2 = x2 * cs[i] + x1 * sn[i];
+      dim = i;
+      dim2 = i + kHd / 2;
+    } else if (tid >= 64 && tid < 64 + a.np) {  // k pair: rounded to the cache type, stored
+      const int k = tid - 64, i = a.p0 + k;
+      const float x1 = qo[2 * a.np + k], x2 = qo[3 * a.np + k];
+      const bf16 k1 = __float2bfloat16_rn(x1 * cs[i] - x2 * sn[i]);
+      const bf16 k2 = __float2bfloat16_rn(x2 * cs[i] + x1 * sn[i]);
+      bf16* kc = static_cast<bf16*>(ly.k_cache);
+      kc[slot + i] = k1;
+      kc[slot + i + kHd / 2] = k2;
+      v1 = __bfloat162float(k1);
+      v2 = __bfloat162float(k2);
+      dim = kHd + i;
+      dim2 = kHd + i + kHd / 2;
+    } else if (tid >= 128 && tid < 128 + a.nv) {  // v row
+      const int k = tid - 128, i = a.v0 + k;
+      const bf16 vv = __float2bfloat16_rn(qo[4 * a.np + k]);
+      static_cast<bf16*>(ly.v_cache)[slot + i] = vv;
+      v1 = __bfloat162float(vv);
+      dim = 2 * kHd + i;
+    }
+    if (dim >= 0) {
+#pragma unroll 1
+      for (int r = 0; r < kCS; ++r) {
+        dsmem_st(dsmem_addr(gq + dim, (uint32_t)r), v1);
+        if (dim2 >= 0) dsmem_st(dsmem_addr(gq + dim2, (uint32_t)r), v2);
+      }
+    }
+  }
+  CSTAMP(l, 15);
+  cluster_sync_all();  // cluster barrier 1: q, k_new, v_new of the head complete in every CTA
+
+  CSTAMP(l, 3);
+  // scale * q . k_new (warp 15, beside the attention core's first loads)
+  if (tid >= kT - 32) {
+    const int lane = tid & 31;
+    float p = gq[lane] * gq[kHd + lane] + gq[lane + 32] * gq[kHd + lane + 32];
+    p = warp_sum(p);
+    if (lane == 0) cx.snew = p * d.attn_scale;
+  }
+  // ---- attention over the old tokens ----
+  float* mg = at<float>(g.sm_mg) + (size_t)par * kCS * kMg;  // [CS][acc, m, l]
+  float* mine = at<float>(g.sm_ov);                          // this split's result, then o
+  ok = att_core(ok, l, a.h, a.t0, a.t1, gq, mine);
+  CSTAMP(l, 4);
+  // the next layer's first K/V chunk (region K is free)
+  if (ok && l + 1 < d.num_layers) {
+    const int n0 = min(g.chunk_tok, a.t1 - a.t0);
+    if (n0 > 0) issue_kv(l + 1, a.h, a.t0, n0);
+  }
+  CSTAMP(l, 21);
+  if (ok && tid < kHd + 2) {
+    const float v = mine[tid];
+    float* dst = mg + (size_t)a.s * kMg + tid;
+#pragma unroll 1
+    for (int r = 0; r < kCS; ++r) dsmem_st(dsmem_addr(dst, (uint32_t)r), v);
+  }
+  CSTAMP(l, 22);
+  cluster_sync_all();  // cluster barrier 2: every split's (acc, m, l)
+  CSTAMP(l, 5);
+  // ---- merge: o_h = (sum_s e^(m_s - M) acc_s + e^(s_new - M) v_new) / (sum_s e^(m_s - M) l_s + e^(s_new - M)) ----
+  float* ov = mine;  // [hd]: the split result is no longer needed
+  if (tid < kHd) {
+    const float snew = cx.snew;
+    float M = snew;
+#pragma unroll
+    for (int s = 0; s < kCS; ++s) M = fmaxf(M, mg[s * kMg + kHd]);
+    const float wn = expf(snew - M);
+    float num = wn * gq[2 * kHd + tid], den = wn;
+#pragma unroll
+    for (int s = 0; s < kCS; ++s) {
+      const float ms = mg[s * kMg + kHd];
+      const float w = ms == -INFINITY ? 0.f : expf(ms - M);
+      num = fmaf(w, mg[s * kMg + tid], num);
+      den = fmaf(w, mg[s * kMg + kHd + 1], den);
+    }
+    ov[tid] = num / den;
+  }
+  __syncthreads();
+  CSTAMP(l, 23);
+  // ---- out_proj partial of head h: rows [r0, r0 + nr) . o_h -> exchange P[h] ----
+  ok = bwait(ok, kBO);
+  CSTAMP(l, 24);
+  if (ok) {
+    // 8 lanes per row (8 bf16 each), 4 rows per warp per pass
+    const int lane = tid & 31, sub = lane >> 3, e = lane & 7;
+    const uint4* tile = at<const uint4>(g.sm_o);
+    float o8[kPV];
+#pragma unroll
+    for (int j = 0; j < kPV; ++j) o8[j] = ov[e * kPV + j];
+    uint64_t* pw = g.ll + g.off_p[par] + (int64_t)a.h * D + a.r0;
+    // every lane of a warp takes the same number of passes (the shuffles)
+#pragma unroll 1
+    for (int rw = (tid >> 5) * 4; rw < a.nr; rw += kW * 4) {
+      const int r = rw + sub;
+      float s = r < a.nr ? dot_vec(tile[r * (kHd / kPV) + e], o8, 0.f, (const bf16*)nullptr) : 0.f;
+      s += __shfl_xor_sync(0xffffffffu, s, 4);
+      s += __shfl_xor_sync(0xffffffffu, s, 2);
+      s += __shfl_xor_sync(0xffffffffu, s, 1);
+      if (e == 0 && r < a.nr) ll_put(pw + r, s, tag);
+    }
+  }
+  __syncthreads();  // the tile is no longer read
+  CSTAMP(l, 25);
+  if (ok && l + 1 < d.num_layers) issue_otile(l + 1);
+  CSTAMP(l, 6);
+  return ok;
+}
+
+// ---------------------------------------------------------------------------
+// MOE: x_mid, routing, the two selected experts, x of layer l + 1
+// ---------------------------------------------------------------------------
+__device__ __noinline__ bool moe_phase(const CStepParams& P, int l, bool ok, bool att) {
+  const mie_step_desc& d = ps.d;
+  const CGeom& g = ps.g;
+  const int tid = threadIdx.x, D = d.hidden_dim, Hx = d.expert_hidden_dim, E = d.num_experts, H = d.num_heads;
+  const int nvD = D / kPV, nvH = Hx / kPV, par = l & 1;
+  const uint32_t tag = tag_of(l);
+  const Split a = split_of(cx.pos);
+  float* xs = at<float>(g.sm_x);
+  float* xn = at<float>(g.sm_xn);
+  float* xm = at<float>(g.sm_xm) + (size_t)par * D;
+  float* ssb = at<float>(g.sm_ss) + (size_t)par * kCS;
+  float* pr = at<float>(g.sm_pr);  // [H][nr] partials, then [nr] x rows (non-attention CTAs)
+  float* ab = at<float>(g.sm_ab);
+  float* hb = at<float>(g.sm_h);
+  // ---- receive rows [r0, r0 + nr) of every head's partial (and of x) ----
+  const int nr = a.nr, r0 = a.r0;
+  const bool need_x = !att && l > 0;
+  {
+    const int n = H * nr + (need_x ? nr : 0);
+    const uint64_t* pb = g.ll + g.off_p[par];
+    const int64_t xoff = g.off_x[par] - g.off_p[par];
+    int bad = 0;
+    if (ok)
+      bad = poll(pb, n, tag, pr, [=](int i) -> int {
+        if (i < H * nr) {
+          const int h = i / nr;
+          return h * D + r0 + (i - h * nr);
+        }
+        return (int)xoff + r0 + (i - H * nr);
+      });
+    if (!att && l == 0) {
+      const bf16* e = static_cast<const bf16*>(d.embedding) + cx.tok * D;
+      for (int i = tid; i < nr; i += kT) pr[H * nr + i] = __bfloat162float(e[r0 + i]);
+    }
+    ok = !__syncthreads_or(bad) && ok;
+  }
+  CSTAMP(l, 26);
+  // ---- x_mid rows and their square sum -> every CTA of the cluster ----
+  float v = 0.f;
+  if (tid < nr) {
+    v = att ? xs[r0 + tid] : pr[H * nr + tid];
+#pragma unroll 1
+    for (int h = 0; h < H; ++h) v += pr[h * nr + tid];
+  }
+  float s2 = warp_sum(v * v);  // rows beyond nr contribute 0
+  if ((tid & 31) == 0) red_s[tid >> 5] = s2;
+  __syncthreads();
+  if (ok) {
+    if (tid < nr) {
+#pragma unroll 1
+      for (int r = 0; r < kCS; ++r) dsmem_st(dsmem_addr(xm + r0 + tid, (uint32_t)r), v);
+    } else if (tid >= kT - 32 && tid - (kT - 32) < kCS) {
+      float t = 0.f;
+#pragma unroll
+      for (int i = 0; i < kW; ++i) t += red_s[i];
+      dsmem_st(dsmem_addr(ssb + a.s, (uint32_t)(tid - (kT - 32))), t);
+    }
+  }
+  CSTAMP(l, 27);
+  cluster_sync_all();  // cluster barrier 3: x_mid complete in every CTA
+  CSTAMP(l, 7);
+  // ---- RMSNorm (square sums of the cluster's shares, in rank order), router, top-2 ----
+  if (!att) ok = bwait(ok, kBR);
+  const bf16* rw = at<const bf16>(g.sm_r);
+  {
+    float t = 0.f;
+#pragma unroll
+    for (int s = 0; s < kCS; ++s) t += ssb[s];
+    const float rs = rsqrtf(t / (float)D + d.eps);
+    const bf16* nw = rw + (size_t)(E + 1) * D;
+#pragma unroll 1
+    for (int i = tid; i < D; i += kT) xn[i] = (xm[i] * rs) * __bfloat162float(nw[i]);
+  }
+  __syncthreads();
+  CSTAMP(l, 28);
+  if (ok) gemv(reinterpret_cast<const uint4*>(rw), E, nvD, xn, ab);
+  __syncthreads();
+  CSTAMP(l, 29);
+  // top-2 in registers, every thread: scanning ascending ids with strict
+  // comparisons keeps the lower id on ties -- the repeated argmax of the
+  // reference's router (src/moe_engine/fused_moe.py:143-150)
+  int sel0 = 0, sel1 = 1;
+  float bv = -INFINITY, cv = -INFINITY;
+#pragma unroll 1
+  for (int e0 = 0; e0 < E; e0 += 4) {
+    const float4 q4 = *reinterpret_cast<const float4*>(ab + e0);
+    const float v4[4] = {q4.x, q4.y, q4.z, q4.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int e = e0 + j;
+      const float x = e < E ? v4[j] : -INFINITY;
+      if (x > bv) {
+        cv = bv;
+        sel1 = sel0;
+        bv = x;
+        sel0 = e;
+      } else if (x > cv) {
+        cv = x;
+        sel1 = e;
+      }
+    }
+  }
+  const float e1 = expf(cv - bv);
+  const float wt0 = 1.0f / (1.0f + e1), wt1 = e1 / (1.0f + e1);
+  __syncthreads();  // router rows and norm weights read: region R may be restaged
+  CSTAMP(l, 30);
+  if (ok) {
+    issue_experts(l, sel0, sel1);
+    issue_side(l + 1);  // the next layer's router + norms, or the final norm
+  }
+  CSTAMP(l, 8);
+  // ---- up units: silu(gate) * up -> exchange H ----
+  int u0, u1, q0, q1;
+  split32(2 * Hx, blockIdx.x, g.G, &u0, &u1);
+  split32(D, blockIdx.x, g.G, &q0, &q1);
+  const int nu = u1 - u0, nq = q1 - q0;
+  ok = bwait(ok, kBA);
+  CSTAMP(l, 31);
+  if (ok) gemv(at<const uint4>(g.sm_a), 2 * nu, nvD, xn, ab);
+  __syncthreads();  // region A no longer read
+  if (ok && tid < nu) ll_put(g.ll + g.off_h[par] + u0 + tid, silu(ab[tid]) * ab[nu + tid], tag);
+  if (ok && att && l + 1 < d.num_layers) issue_qkv(l + 1);  // the next layer's q/k/v rows
+  CSTAMP(l, 9);
+  // ---- down rows of both slots . h + residual -> exchange X of layer l + 1 ----
+  {
+    int bad = 0;
+    if (ok) bad = poll(g.ll + g.off_h[par], 2 * Hx, tag, hb, Ident{});
+    ok = !__syncthreads_or(bad) && ok;
+  }
+  CSTAMP(l, 10);
+  ok = bwait(ok, kBD);
+  if (ok) gemv(at<const uint4>(g.sm_d), 2 * nq, nvH, hb, ab, hb + Hx, nq);
+  __syncthreads();  // region D no longer read
+  if (ok && tid < nq) {
+    const int r = q0 + tid;
+    const float y = fmaf(wt1, ab[nq + tid], fmaf(wt0, ab[tid], xm[r]));
+    ll_put(g.ll + g.off_x[(l + 1) & 1] + r, y, tag_of(l + 1));
+    if (l == d.num_layers - 1) d.x[r] = y;
+  }
+  // after the last layer every staging region but R is free: the first LM-head stages
+  if (ok && l == d.num_layers - 1) issue_head(0, g.head_stages);
+  if (tid == 0) {
+    cx.sel0 = sel0;
+    cx.sel1 = sel1;
+  }
+  CSTAMP(l, 11);
+  return ok;
+}
+
+// ---------------------------------------------------------------------------
+// HEAD: final norm -> tied LM head -> argmax + device bookkeeping
+// ---------------------------------------------------------------------------
+__device__ __noinline__ void head_finish(int bi) {
+  const mie_step_desc& d = ps.d;
+  if (bi < 0 || bi >= d.vocab) {  // every logit NaN
+    set_status(d.status, MIE_ERR_RANGE);
+    bi = 0;
+  }
+  *d.token = bi;
+  *d.pos = cx.pos + 1;
+  if (d.tokens_log && d.log_count) {
+    const int k = cx.log_k;
+    if (k < d.log_capacity) d.tokens_log[k] = bi;
+    *d.log_count = k + 1;
+  }
+  if (d.done && bi == d.eos_id) *d.done = 1;
+  *d.lm_counter = 0u;
+  __threadfence();
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(ps.g.ll + kHdrStep), "l"((uint64_t)cx.step) : "memory");
+}
+
+__device__ __noinline__ bool head_phase(bool ok) {
+  const mie_step_desc& d = ps.d;
+  const CGeom& g = ps.g;
+  const int G = g.G, c = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int D = d.hidden_dim, nvD = D / kPV, L = d.num_layers;
+  float* xs = at<float>(g.sm_x);
+  float* xn = at<float>(g.sm_xn);
+  float* ab = at<float>(g.sm_ab);
+  CSTAMP(L, 0);
+  {
+    int bad = 0;
+    if (ok) bad = poll(g.ll + g.off_x[L & 1], D, tag_of(L), xs, Ident{});
+    ok = !__syncthreads_or(bad) && ok;
+  }
+  ok = bwait(ok, kBR);  // the final norm weights
+  rms_norm(xn, xs, D, d.eps, at<const bf16>(g.sm_r) + (size_t)d.num_experts * D);
+  CSTAMP(L, 1);
+  int v0, v1;
+  split32(d.vocab, c, G, &v0, &v1);
+  const int nst = (v1 - v0 + g.head_rows - 1) / g.head_rows;
+  float best_v = -INFINITY;
+  int best_i = 0x7fffffff;
+#pragma unroll 1
+  for (int i = 0; i < nst; ++i) {
+    const int slot = i % g.head_stages;
+    ok = bwait(ok, kBH + slot);
+    const int r0 = v0 + i * g.head_rows, n = min(g.head_rows, v1 - r0);
+    if (ok) gemv(at<const uint4>(g.sm_a) + (size_t)slot * g.head_rows * nvD, n, nvD, xn, ab);
+    __syncthreads();  // stage no longer read, ab complete
+    if (ok && i + g.head_stages < nst) issue_head(i + g.head_stages, 1);
+    if (tid < n) {
+      const float v = ab[tid];
+      const int row = r0 + tid;
+      if (d.logits) d.logits[row] = v;
+      if (better(v, row, best_v, best_i)) {
+        best_v = v;
+        best_i = row;
+      }
+    }
+  }
+  CSTAMP(L, 2);
+  if (!ok) return false;
+  // CTA argmax: (value, lower index) is a total order
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best_v, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, best_i, o);
+    if (better(ov, oi, best_v, best_i)) {
+      best_v = ov;
+      best_i = oi;
+    }
+  }
+  if (lane == 0) {
+    bestv_s[warp] = best_v;
+    besti_s[warp] = best_i;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+#pragma unroll 1
+    for (int w = 0; w < kW; ++w)
+      if (better(bestv_s[w], besti_s[w], bv, bi)) {
+        bv = bestv_s[w];
+        bi = besti_s[w];
+      }
+    d.lm_partial_val[c] = bv;
+    d.lm_partial_idx[c] = bi;
+    cx.last = atom_add_acq_rel_gpu(d.lm_counter, 1u) == (uint32_t)(G - 1);
+  }
+  __syncthreads();
+  if (!cx.last || warp != 0) return true;
+  __threadfence();
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+#pragma unroll 1
+  for (int j0 = lane; j0 < G; j0 += 8 * 32) {
+    float v[8];
+    int ix[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int j = j0 + 32 * k;
+      v[k] = j < G ? __ldcg(d.lm_partial_val + j) : -INFINITY;
+      ix[k] = j < G ? __ldcg(d.lm_partial_idx + j) : 0x7fffffff;
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      if (better(v[k], ix[k], bv, bi)) {
+        bv = v[k];
+        bi = ix[k];
+      }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (better(ov, oi, bv, bi)) {
+      bv = ov;
+      bi = oi;
+    }
+  }
+  if (lane == 0) head_finish(bi);
+  CSTAMP(L, 5);
+  return true;
+}
+
+// Wait (bounded) until the start gate is nonzero (acquire); false when it
+// stayed closed.
+__device__ __noinline__ bool gate_open(const int32_t* gate, unsigned long long limit_ns) {
+  const unsigned long long t0 = global_ns();
+#pragma unroll 1
+  while (ld_acquire_gpu(reinterpret_cast<const uint32_t*>(gate)) == 0u)
+    if (global_ns() - t0 > limit_ns) return false;
+  return true;
+}
+
+__global__ void __launch_bounds__(kT, 1) cstep_kernel(const __grid_constant__ CStepParams P) {
+  CSTAMP(P.d.num_layers, 3);
+  // under programmatic dependent launch the next step's CTAs may take the SMs
+  // this grid's CTAs leave; they stage their first weights, then wait
+  pdl_trigger();
+  {
+    constexpr int kWords = (int)(sizeof(CShared) / 8);
+    static_assert(sizeof(mie_step_desc) % 8 == 0 && sizeof(CGeom) % 8 == 0, "8-byte words");
+    const int i = threadIdx.x;
+    if (i < kWords) {
+      const uint64_t* src = i < (int)(sizeof(mie_step_desc) / 8)
+                                ? reinterpret_cast<const uint64_t*>(&P.d) + i
+                                : reinterpret_cast<const uint64_t*>(&P.g) + (i - (int)(sizeof(mie_step_desc) / 8));
+      reinterpret_cast<uint64_t*>(&ps)[i] = *src;
+    }
+#pragma unroll 1
+    for (int l = 0; l < kLaySlots && l < P.d.num_layers; ++l) layer_fetch(P, l, 128 + 16 * l);
+    if (threadIdx.x == 0) {
+      cx.pos = 0;
+#pragma unroll 1
+      for (int b = 0; b < kNB; ++b) {
+        mbar_init(&bars_s[b], kT);  // every thread arrives once per phase
+        armed_s[b] = done_s[b] = 0;
+      }
+      fence_barrier_init();
+    }
+    __syncthreads();
+  }
+  const mie_step_desc& d = ps.d;
+  const bool att = (int)(blockIdx.x / kCS) < d.num_heads;
+  // layer 0's q/k/v rows, out_proj tile, router and norm weights depend on the
+  // CTA alone: staged before the wait (the row splits do not depend on pos)
+  if (att) {
+    issue_qkv(0);
+    issue_otile(0);
+  }
+  issue_side(0);
+  // the previous step's writes are visible from here on
+  pdl_wait();
+  bool ok = true;
+  if (threadIdx.x == 0) {
+    const int done_v = d.done ? __ldcg(d.done) : 0;
+    const int lc = d.log_count ? __ldcg(d.log_count) : 0;
+    const int lim = d.step_limit ? __ldcg(d.step_limit) : 0;
+    const uint64_t hstep = ll_ld(ps.g.ll + kHdrStep);
+    const int p = __ldcg(d.pos);
+    const int64_t t = __ldcg(d.token);
+    int stop = done_v || (d.step_limit && d.log_count && lc >= lim);
+    lim_s = d.wait_limit_ns > 0 ? (unsigned long long)d.wait_limit_ns : kWaitLimitNs;
+    cx.step = (uint32_t)hstep + 1u;
+    cx.log_k = lc;
+    if (!stop && (p < 0 || p >= d.max_pos || t < 0 || t >= d.vocab)) {
+      if (blockIdx.x == 0) set_status(d.status, MIE_ERR_RANGE);
+      stop = 1;
+    }
+    int64_t blk = stop ? 0 : p / d.block_size;
+    if (!stop && d.block_table) {
+      const int pb = __ldcg(d.block_table + blk);
+      if (pb < 0 || pb >= d.num_blocks) {
+        if (blockIdx.x == 0) set_status(d.status, MIE_ERR_RANGE);
+        stop = 1;
+      }
+      blk = pb;
+    }
+    cx.pos = p;
+    cx.tok = t;
+    cx.slot = stop ? 0 : blk * d.kv_stride_block + (int64_t)(p % d.block_size) * d.kv_stride_tok;
+    cx.blk0 = 0;
+    if (!stop) {
+      int t0, t1;
+      split32(p, (int)(blockIdx.x % kCS), kCS, &t0, &t1);
+      cx.blk0 = t0 / d.block_size;
+    }
+    cx.stop = stop;
+  } else if (d.block_table && threadIdx.x <= kBlkCache) {
+    // physical block ids of this split's old tokens, the same for every layer
+    const int p = __ldcg(d.pos), i = threadIdx.x - 1;
+    if (p >= 0 && p < d.max_pos) {
+      int t0, t1;
+      split32(p, (int)(blockIdx.x % kCS), kCS, &t0, &t1);
+      const int b0 = t0 / d.block_size;
+      if (t1 > t0 && b0 + i <= (t1 - 1) / d.block_size) blk_s[i] = __ldcg(d.block_table + b0 + i);
+    }
+  }
+  __syncthreads();
+  // the stop decision reads the same device state in every CTA: grid-uniform
+  if (cx.stop) {
+    drain_copies();
+    return;
+  }
+  // a closed start gate ends this CTA's part of the step; it still takes every
+  // cluster barrier
+  if (d.start_gate) {
+    __shared__ int gate_ok;
+    if (threadIdx.x == 0) {
+      gate_ok = gate_open(d.start_gate, lim_s) ? 1 : 0;
+      if (!gate_ok) set_status(d.status, MIE_ERR_TIMEOUT);
+    }
+    __syncthreads();
+    ok = gate_ok != 0;
+  }
+  CSTAMP(d.num_layers, 4);
+  if (ok && att) {
+    const Split a = split_of(cx.pos);
+    const int n0 = min(ps.g.chunk_tok, a.t1 - a.t0);
+    if (n0 > 0) issue_kv(0, a.h, a.t0, n0);
+  }
+#pragma unroll 1
+  for (int l = 0; l < d.num_layers; ++l) {
+    if (threadIdx.x >= 448 && l + 2 < d.num_layers && l + 2 >= kLaySlots) layer_fetch(P, l + 2, 448);
+    if (att) ok = att_phase(P, l, ok);
+    ok = moe_phase(P, l, ok, att);
+  }
+  head_phase(ok);
+  drain_copies();
+}
+
+// ---- host side ----
+std::mutex g_cluster_mutex;
+int g_max_clusters[64] = {0};  // per device: clusters of the kernel that fit at once (0: not queried)
+
+}  // namespace
+
+int cstep_geometry(const mie_step_desc& d, CGeom* out) {
+  // MIE_STEP_AUTO selects the one-CTA-per-SM step while it is the faster one
+  if (d.step_kernel != MIE_STEP_CLUSTER) return MIE_ERR_UNSUPPORTED;
+  if (d.dtype != MIE_BF16 || d.kv_dtype != MIE_BF16) return MIE_ERR_UNSUPPORTED;
+  if (d.norm != MIE_NORM_RMS || d.act != MIE_ACT_SWIGLU || d.top_k != 2) return MIE_ERR_UNSUPPORTED;
+  if (d.head_dim != kHd || d.num_heads * kHd != d.hidden_dim) return MIE_ERR_UNSUPPORTED;
+  const int D = d.hidden_dim, Hx = d.expert_hidden_dim, E = d.num_experts, H = d.num_heads;
+  if (D > 768 || D % kPV || Hx > 768 || Hx % kPV || Hx <= 0 || E < 2 || E > 32) return MIE_ERR_UNSUPPORTED;
+  if (d.num_layers <= 0 || d.num_layers > kMaxStepLayers) return MIE_ERR_UNSUPPORTED;
+  if (!d.rope_cos || !d.rope_sin || d.pos_embedding || d.lm_bias || d.final_norm_b) return MIE_ERR_UNSUPPORTED;
+  if (d.sample_temperature > 0.f) return MIE_ERR_UNSUPPORTED;  // the device sampler runs on the flat step
+  if (d.moe_partial || (d.expert_count && d.expert_count != E) || d.expert_base) return MIE_ERR_UNSUPPORTED;
+  if (d.kv_stride_tok != kHd || (d.kv_stride_block * 2) % 16 || (d.kv_stride_head * 2) % 16)
+    return MIE_ERR_UNSUPPORTED;
+  for (int l = 0; l < d.num_layers; ++l) {
+    const mie_layer_desc& y = d.layers[l];
+    if (y.qkv_b || y.out_b || y.b1 || y.b2 || y.attn_norm_b || y.moe_norm_b || !y.w3) return MIE_ERR_UNSUPPORTED;
+  }
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return MIE_ERR_CUDA;
+  CGeom& g = *out;
+  g = CGeom{};
+  // shared memory layout
+  const uint32_t rbD = (uint32_t)D * 2u, rbH = (uint32_t)Hx * 2u;
+  g.np_max = (kHd / 2 + kCS - 1) / kCS;
+  g.nv_max = (kHd + kCS - 1) / kCS;
+  g.orows = (D + kCS - 1) / kCS;
+  g.chunk_tok = 256;
+  uint32_t so = 0;
+  auto stake = [&](uint32_t bytes) {
+    so = (so + 127) & ~127u;
+    const uint32_t at = so;
+    so += bytes;
+    return at;
+  };
+  // the grid size decides the expert shares; start from the cached cluster count
+  int nc;
+  {
+    std::lock_guard<std::mutex> lock(g_cluster_mutex);
+    nc = g_max_clusters[dev];
+  }
+  if (nc <= 0) return MIE_ERR_UNSUPPORTED;  // cstep_set_attributes found no room for the kernel
+  if (nc > 40) nc = 40;
+  if (nc < H) return MIE_ERR_UNSUPPORTED;  // one cluster per head
+  g.NC = nc;
+  g.G = nc * kCS;
+  if ((int64_t)d.vocab * g.G >= (1ll << 32) || (int64_t)d.max_pos * kCS >= (1ll << 32)) return MIE_ERR_UNSUPPORTED;
+  if (d.lm_grid < g.G) return MIE_ERR_INVALID;
+  g.nu_max = (2 * Hx + g.G - 1) / g.G;
+  g.nr_max = (D + g.G - 1) / g.G;
+  if (2 * g.nu_max > kT || g.nu_max > kT || (H + 1) * g.orows > 6 * kT) return MIE_ERR_UNSUPPORTED;
+  const uint32_t a_bytes = (uint32_t)max(4 * g.np_max + g.nv_max, 2 * g.nu_max) * rbD;
+  g.sm_a = stake(a_bytes);
+  g.sm_k = stake((uint32_t)(2 * g.chunk_tok * kHd * 2));
+  g.sm_o = stake((uint32_t)(g.orows * kHd * 2));
+  g.sm_d = stake(2u * (uint32_t)g.nr_max * rbH);
+  g.sm_r = stake((uint32_t)(E + 2) * rbD);
+  g.sm_x = stake(4u * D);
+  g.sm_xn = stake(4u * D);
+  g.sm_xm = stake(8u * D);
+  g.sm_ss = stake(8u * kCS);
+  g.sm_g = stake(2u * 3u * kHd * 4u);
+  g.sm_mg = stake(2u * kCS * kMg * 4u);
+  g.sm_qkv = stake((uint32_t)(4 * g.np_max + g.nv_max) * 4u);
+  g.sm_sc = stake((uint32_t)g.chunk_tok * 4u);
+  g.sm_ab = stake(4u * (uint32_t)max(kT, max(E, 2 * g.nu_max)));
+  g.sm_h = stake(8u * Hx);
+  g.sm_pr = stake((uint32_t)(H + 1) * g.orows * 4u);
+  g.sm_ov = stake((kHd + 4) * 4u);
+  g.smem = (so + 127) & ~127u;
+  if (g.smem > kStepMaxSmem) return MIE_ERR_UNSUPPORTED;
+  // LM-head ring over regions A..D: stages of 32 rows (two per warp)
+  g.head_rows = 2 * kW;
+  const uint32_t ring = g.sm_r - g.sm_a;
+  g.head_stages = (int)(ring / ((uint32_t)g.head_rows * rbD));
+  if (g.head_stages > kStepHeadStagesMax) g.head_stages = kStepHeadStagesMax;
+  if (g.head_stages < 2) return MIE_ERR_UNSUPPORTED;
+  // exchange words, two copies each
+  int64_t off = 8;
+  auto take = [&](int64_t words) {
+    const int64_t at = off;
+    off += (words + 1) & ~int64_t(1);
+    return at;
+  };
+  for (int p = 0; p < 2; ++p) {
+    g.off_x[p] = take(D);
+    g.off_p[p] = take((int64_t)H * D);
+    g.off_h[p] = take(2 * (int64_t)Hx);
+  }
+  g.words = off;
+  return MIE_OK;
+}
+
+int cstep_launch(const mie_step_desc& d, const CGeom& g, uint64_t* scratch, cudaStream_t st) {
+  static CStepParams p;  // large: not on the stack (launches are made from one host thread at a time)
+  static std::mutex m;
+  std::lock_guard<std::mutex> lock(m);
+  p.d = d;
+  p.g = g;
+  p.g.ll = scratch;
+  for (int l = 0; l < d.num_layers; ++l) p.layers[l] = d.layers[l];
+  p.d.layers = nullptr;
+#ifdef MIE_STEP_STAMPS
+  if (d.num_layers + 1 > kStampLayers || g.G > 160) return MIE_ERR_UNSUPPORTED;
+#endif
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)g.G);
+  cfg.blockDim = dim3(kT);
+  cfg.dynamicSmemBytes = g.smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = kCS;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = d.use_pdl ? 2 : 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, cstep_kernel, p);
+  if (e != cudaSuccess) {
+    note_cuda_error(e, "cudaLaunchKernelEx(cluster step)");
+    return MIE_ERR_CUDA;
+  }
+  return MIE_OK;
+}
+
+// Once per device (from mie_init): the shared-memory attribute, then how many
+// clusters of the kernel the device holds at once with its largest shared
+// memory footprint.
+void cstep_set_attributes() {
+  set_max_smem(cstep_kernel);
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(kCS * 8);
+  cfg.blockDim = dim3(kT);
+  cfg.dynamicSmemBytes = kStepMaxSmem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = kCS;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  const cudaError_t e = cudaOccupancyMaxActiveClusters(&n, cstep_kernel, &cfg);
+  if (e != cudaSuccess) {
+    note_cuda_error(e, "cudaOccupancyMaxActiveClusters(cluster step)");
+    n = 0;
+  }
+  std::lock_guard<std::mutex> lock(g_cluster_mutex);
+  g_max_clusters[dev] = n;
+}
+
+#ifdef MIE_STEP_STAMPS
+extern "C" int mie_debug_cstep_stamps(unsigned long long* host, int64_t count) {
+  return cudaMemcpyFromSymbol(host, g_cstep_stamps, sizeof(unsigned long long) * (size_t)count) == cudaSuccess
+             ? MIE_OK
+             : MIE_ERR_CUDA;
+}
+#endif
+
+}  // namespace mie

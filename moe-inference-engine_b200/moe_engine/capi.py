@@ -18,6 +18,7 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "_native", "libmie.so")
 
 MIE_OK, MIE_ERR_INVALID, MIE_ERR_UNSUPPORTED, MIE_ERR_CUDA, MIE_ERR_TIMEOUT, MIE_ERR_RANGE, MIE_ERR_SCRATCH_LIMIT = range(7)
+MIE_STEP_AUTO, MIE_STEP_FLAT, MIE_STEP_CLUSTER = range(3)
 MIE_F32, MIE_BF16 = 0, 1
 MIE_NORM_NONE, MIE_NORM_RMS, MIE_NORM_LAYER = 0, 1, 2
 MIE_ACT_GELU, MIE_ACT_SWIGLU = 0, 1
@@ -104,7 +105,7 @@ class StepDesc(ctypes.Structure):
         ("logits", _p), ("status", _p), ("attn_splits", _i), ("max_splits", _i), ("lm_grid", _i),
         ("use_pdl", _i), ("step_scratch", _p), ("step_scratch_bytes", _i64), ("sample_temperature", _f),
         ("sample_top_k", _i), ("sample_seed", _p), ("step_limit", _p), ("wait_limit_ns", _i64),
-        ("start_gate", _p),
+        ("start_gate", _p), ("step_kernel", _i),
     ]
 
 
@@ -170,6 +171,7 @@ SYMBOLS = {
     "mie_decode_layer": ([ctypes.POINTER(StepDesc), _i, _p], ctypes.c_int),
     "mie_decode_head": ([ctypes.POINTER(StepDesc), _p], ctypes.c_int),
     "mie_step_scratch_bytes": ([ctypes.POINTER(StepDesc)], ctypes.c_int64),
+    "mie_step_kernel_of": ([ctypes.POINTER(StepDesc)], ctypes.c_int),
     "mie_gemm": ([ctypes.POINTER(GemmArgs), _p], ctypes.c_int),
     "mie_prefill_norm": ([ctypes.POINTER(PrefillNormArgs), _p], ctypes.c_int),
     "mie_prefill_rope_kv": ([ctypes.POINTER(PrefillRopeArgs), _p], ctypes.c_int),

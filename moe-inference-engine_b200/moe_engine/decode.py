@@ -119,6 +119,9 @@ class DecodeRunner:
         # step waits for before it reads its input).
         self.wait_limit_ns = 0
         self.start_gate = None
+        # which persistent kernel: capi.MIE_STEP_AUTO (the cluster step when it
+        # takes the shapes), MIE_STEP_FLAT or MIE_STEP_CLUSTER
+        self.step_kernel = int(os.environ.get("MIE_STEP_KERNEL", "0"))
 
     # ---- descriptors --------------------------------------------------------
     def param_signature(self):
@@ -231,6 +234,7 @@ class DecodeRunner:
         d.step_scratch_bytes = 0
         d.wait_limit_ns = int(self.wait_limit_ns)
         d.start_gate = capi.ptr(self.start_gate)
+        d.step_kernel = int(self.step_kernel)
         if self.persistent:
             with torch.cuda.device(self.device):
                 need = int(self.lib.mie_step_scratch_bytes(ctypes.byref(d)))
@@ -246,6 +250,18 @@ class DecodeRunner:
         _, _, _, _, bs, _, _ = cache_geometry(cache, 0)
         desc, _ = self.make_desc(cache, logits=False, graph=True, splits=self.splits_for(bs, bs))
         return bool(desc.step_scratch)
+
+    def step_kernel_for(self, cache) -> int:
+        """capi.MIE_STEP_CLUSTER or MIE_STEP_FLAT: the persistent kernel that
+        runs decode steps for ``cache`` (0 when steps run as the per-op
+        launch sequence)."""
+        _, _, _, _, bs, _, _ = cache_geometry(cache, 0)
+        desc, _ = self.make_desc(cache, logits=False, graph=True, splits=self.splits_for(bs, bs))
+        if not desc.step_scratch:
+            return 0
+        with torch.cuda.device(self.device):
+            k = int(self.lib.mie_step_kernel_of(ctypes.byref(desc)))
+        return max(k, 0)
 
     def steps_per_graph(self, cache) -> int:
         """Decode steps one graph of :meth:`graph_for` may hold for ``cache``:
@@ -304,7 +320,7 @@ class DecodeRunner:
         k0 = cache_geometry(cache, 0)[0]
         table = getattr(cache, "block_table_device", None)
         key = (k0.data_ptr(), None if table is None else table.data_ptr(), splits, self.use_pdl,
-               self.persistent, self.param_signature(), tuple(sample), steps)
+               self.persistent, self.step_kernel, self.param_signature(), tuple(sample), steps)
         hit = self._graphs.get(key)
         if hit is not None:
             return hit[0]

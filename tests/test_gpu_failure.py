@@ -26,19 +26,24 @@ pytestmark = pytest.mark.gpu
 DEV = "cuda"
 
 
-def prefilled():
+KERNELS = [capi.MIE_STEP_FLAT, capi.MIE_STEP_CLUSTER]
+
+
+def prefilled(kernel):
     m, _, _ = baseline_bf16_model(max_seq=256, num_layers=2)
+    m.decode_runner().step_kernel = kernel
     cache = shuffled_paged_cache(m, 256)
     prompt = torch.randint(0, 50304, (20,), generator=torch.Generator().manual_seed(12))
     with torch.no_grad():
         logits = m(prompt[None].to(DEV), cache)
     runner = m.decode_runner()
-    assert runner.uses_persistent(cache)
+    assert runner.step_kernel_for(cache) == kernel
     return m, runner, cache, int(logits[0, -1].float().argmax())
 
 
-def test_closed_start_gate_times_out_and_changes_nothing():
-    m, runner, cache, tok = prefilled()
+@pytest.mark.parametrize("kernel", KERNELS)
+def test_closed_start_gate_times_out_and_changes_nothing(kernel):
+    m, runner, cache, tok = prefilled(kernel)
     p = cache.position
     t = torch.tensor([[tok]], device=DEV)
     ref_logits = runner.forward_step(t, cache).clone()
@@ -70,8 +75,9 @@ def test_closed_start_gate_times_out_and_changes_nothing():
     assert int(runner.token.item()) == ref_token
 
 
-def test_gate_opened_from_another_stream_lets_the_step_run():
-    m, runner, cache, tok = prefilled()
+@pytest.mark.parametrize("kernel", KERNELS)
+def test_gate_opened_from_another_stream_lets_the_step_run(kernel):
+    m, runner, cache, tok = prefilled(kernel)
     p = cache.position
     t = torch.tensor([[tok]], device=DEV)
     ref_logits = runner.forward_step(t, cache).clone()

@@ -29,6 +29,7 @@ import pytest
 import torch
 
 import oracle
+from moe_engine import capi
 from oracle import minimoe as om
 from tests.helpers import baseline_bf16_model, engine_state_dict, shuffled_paged_cache
 
@@ -76,7 +77,9 @@ def step_both_paths(runner, cache, tok: int):
     logits_persistent, token_persistent)."""
     p = cache.position
     t = torch.tensor([[tok]], device=DEV)
-    assert runner.persistent and runner.uses_persistent(cache)
+    assert runner.persistent and runner.step_kernel_for(cache) in (runner.step_kernel, capi.MIE_STEP_FLAT)
+    if runner.step_kernel:
+        assert runner.step_kernel_for(cache) == runner.step_kernel
     la = runner.forward_step(t, cache)
     xa, ta = runner.x.clone(), int(runner.token.item())
     cache.position = p
@@ -127,17 +130,27 @@ def run_checkpoints(m, P, arch, prompt_len, checkpoints, max_seq, prompt_seed):
     return report
 
 
-def test_bench_config_step_vs_per_op_and_oracle():
+# both persistent kernels: one CTA per SM, and clusters of six CTAs
+KERNELS = [capi.MIE_STEP_FLAT, capi.MIE_STEP_CLUSTER]
+
+
+@pytest.mark.parametrize("kernel", KERNELS)
+def test_bench_config_step_vs_per_op_and_oracle(kernel):
     """config[3] geometry: 512-token prompt, graph decode to context 1536."""
     m, P, arch = model_and_params()
+    m.decode_runner().step_kernel = kernel
     report = run_checkpoints(m, P, arch, 512, [520, 1000, 1535], 1536, prompt_seed=3)
     assert sum(1 for r in report if r[4] >= 1e-3) >= 2  # at least two positions checked against the oracle
 
 
-def test_long_context_multi_chunk_step():
-    """max_seq_length 4096: at context 2000 and 3800 every split holds 166 /
-    316 old tokens, i.e. two / three 128-token chunks of the attention core."""
+@pytest.mark.parametrize("kernel", KERNELS)
+def test_long_context_multi_chunk_step(kernel):
+    """max_seq_length 4096: at context 2000 and 3800 every split of the flat
+    step holds 166 / 316 old tokens, i.e. two / three 128-token chunks of its
+    attention core (the cluster step: 333 / 633 tokens, two / three chunks of
+    256)."""
     m, P, arch = model_and_params(max_seq=4096)
+    m.decode_runner().step_kernel = kernel
     report = run_checkpoints(m, P, arch, 2000, [2000, 3800], 4096, prompt_seed=4)
     assert sum(1 for r in report if r[4] >= 1e-3) >= 1
 
@@ -151,7 +164,8 @@ def _higher_index_topk(logits, k):
     return vals, logits.shape[-1] - 1 - ids
 
 
-def test_router_ties_pick_lower_expert_ids(monkeypatch):
+@pytest.mark.parametrize("kernel", KERNELS)
+def test_router_ties_pick_lower_expert_ids(monkeypatch, kernel):
     """Layer 0: router rows 3 and 6 equal r, row 5 = 2r, the others zero --
     whatever the sign of r.x, the second place (or both places) is a tie.
     Layer 1: all eight rows equal, so experts 0 and 1 must be chosen."""
@@ -172,7 +186,8 @@ def test_router_ties_pick_lower_expert_ids(monkeypatch):
         logits = m(prompt[None].to(DEV), cache)
     dec.forward(prompt[None])
     runner = m.decode_runner()
-    assert runner.uses_persistent(cache)
+    runner.step_kernel = kernel
+    assert runner.step_kernel_for(cache) == kernel
     tok = int(logits[0, -1].float().argmax())
     got, wrong = [], []
     for _ in range(6):
@@ -196,14 +211,18 @@ def test_router_ties_pick_lower_expert_ids(monkeypatch):
     assert min(wrong) > 5e-2, wrong  # the test tells the two rules apart
 
 
-@pytest.mark.parametrize("persistent", [True, False])
-def test_lm_head_ties_emit_lower_token(persistent):
+@pytest.mark.parametrize("kernel", KERNELS + [None])
+def test_lm_head_ties_emit_lower_token(kernel):
     """Two embedding rows (the tied LM head) set equal and dominant: the step
     must emit the lower token id, whether the rows lie in different CTAs'
-    vocab ranges (5 and 50300) or next to each other (1000, 1001)."""
+    vocab ranges (5 and 50300) or next to each other (1000, 1001).  Kernel
+    None: the per-op launch sequence."""
+    persistent = kernel is not None
     m, P, arch = model_and_params(num_layers=2, max_seq=256)
     runner = m.decode_runner()
     runner.persistent = persistent
+    if persistent:
+        runner.step_kernel = kernel
     cache = paged_cache(m, 256)
     prompt = torch.randint(0, 4000, (8,), generator=torch.Generator().manual_seed(10)) + 2000
     with torch.no_grad():
@@ -211,7 +230,7 @@ def test_lm_head_ties_emit_lower_token(persistent):
     p = cache.position
     t = torch.tensor([[2500]], device=DEV)
     runner.forward_step(t, cache)
-    assert runner.uses_persistent(cache) == persistent
+    assert runner.step_kernel_for(cache) == (kernel or 0)
     x = runner.x.clone()
     g = m.final_norm.weight.float()
     xn = x * torch.rsqrt(x.pow(2).mean() + 1e-5) * g
