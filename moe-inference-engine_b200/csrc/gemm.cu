@@ -258,9 +258,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 }
 
 // ---- host: tensor maps ----
-using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+}  // namespace
 
 EncodeTiledFn encode_fn() {
   static EncodeTiledFn fn = nullptr;
@@ -273,6 +271,8 @@ EncodeTiledFn encode_fn() {
   }
   return fn;
 }
+
+namespace {
 
 // 2-D bf16 tensor [rows, cols] (row stride ld elements), box box_rows x 64,
 // 128-byte swizzle; reads past `rows` return zeros.

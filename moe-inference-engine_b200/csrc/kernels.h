@@ -1,6 +1,7 @@
 // Internal host-side interface between the kernel files and the C ABI layer.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <stdint.h>
@@ -94,17 +95,19 @@ struct CGeom {
   int G, NC;      // CTAs, clusters (G = NC * kStepCluster)
   int chunk_tok;  // K/V tokens per shared-memory chunk
   int np_max, nv_max;  // RoPE pairs / v rows of one split (upper bounds)
-  int orows;      // out_proj rows of one split (upper bound)
+  int orows;      // out_proj rows of one split (upper bound; the tile height)
   int nu_max, nr_max;  // up units / down rows of one CTA (upper bounds)
   int head_rows, head_stages;  // LM-head ring
   // staging regions: A (q/k/v rows, then the selected experts' gate/up rows),
-  // K (K then V chunk), O (out_proj tile), D (down rows), R (router + norms)
+  // K (K then V chunk), O (out_proj tile), D (down rows), R (router + norms);
+  // [sm_k, sm_fn) is the LM-head ring after the last layer
   uint32_t sm_a, sm_k, sm_o, sm_d, sm_r;
   // fp32 vectors: x, normalised x, x_mid [2][D], x_mid square sums [2][CS],
   // gathered q / k_new / v_new [2][3][hd], merge partials [2][CS][hd + 4],
   // own q/k/v GEMV results, scores, scratch, expert hidden [2 Hx], received
   // partials [H + 1][orows], merged o [hd]
   uint32_t sm_x, sm_xn, sm_xm, sm_ss, sm_g, sm_mg, sm_qkv, sm_sc, sm_ab, sm_h, sm_pr, sm_ov;
+  uint32_t sm_fn;  // final norm weights
   uint32_t smem;
 };
 
@@ -112,6 +115,7 @@ struct CStepParams {
   mie_step_desc d;  // d.layers is not used on the device
   CGeom g;
   mie_layer_desc layers[kMaxStepLayers];
+  CUtensorMap omap[kMaxStepLayers];  // per layer: out_proj [D, D] bf16, box hd x orows
 };
 
 // Allow the largest dynamic shared memory the device permits next to the
@@ -182,6 +186,11 @@ void step_set_attributes();
 int cstep_geometry(const mie_step_desc& d, CGeom* g);
 int cstep_launch(const mie_step_desc& d, const CGeom& g, uint64_t* scratch, cudaStream_t st);
 void cstep_set_attributes();
+// gemm.cu: cuTensorMapEncodeTiled through the runtime's driver entry point
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn encode_fn();
 // step_wide.cu (the wide variant of the persistent step, its own translation unit)
 int step_launch_wide(const StepParams& p, cudaStream_t st);
 void step_set_attributes_wide();

@@ -80,6 +80,9 @@ namespace {
 using bf16 = __nv_bfloat16;
 constexpr int kT = kStepThreads;      // 512 threads
 constexpr int kW = kT / 32;           // 16 warps
+constexpr int kCT = kT - 32;          // consumer threads: warps 0..14
+constexpr int kCW = kCT / 32;         // consumer warps
+constexpr int kProd = kCT;            // first thread of the producer warp (warp 15)
 constexpr int kCS = kStepCluster;     // CTAs per cluster
 constexpr int kHd = kClusterHeadDim;  // head_dim
 constexpr int kPV = 8;                // bf16 elements per 16-byte vector
@@ -87,11 +90,17 @@ constexpr int kMg = kHd + 4;          // merge partial: acc [hd], m, l (padded)
 
 constexpr int kHdrStep = 0, kHdrAbort = 1;  // scratch header words
 
-// mbarriers: A (q/k/v rows, then the selected experts' gate/up rows), K (K/V
-// chunk), O (out_proj tile), R (router + norm weights), D (down rows), then
-// the LM-head ring stages
-constexpr int kBA = 0, kBK = 1, kBO = 2, kBR = 3, kBD = 4, kBH = 5;
-constexpr int kNB = kBH + kStepHeadStagesMax;
+// "Full" mbarriers (a staged region landed), each filled by one side:
+// the producer warp (count 32) -- q/k/v rows (region A), the first K/V chunk
+// (K), the out_proj tile (O), router + norm weights (R), the LM-head ring
+// stages -- or the consumers (count kCT) -- the selected experts' gate/up rows
+// (A) and down rows (D), further K/V chunks (K).  "Empty" mbarriers (count 1,
+// arrived by consumer thread 0): a region the producer refills was read for
+// the last time.
+constexpr int kFQ = 0, kFK = 1, kFK2 = 2, kFO = 3, kFR = 4, kFE = 5, kFD = 6, kFH = 7;
+constexpr int kNF = kFH + kStepHeadStagesMax;  // full barriers
+constexpr int kEK = kNF, kEO = kNF + 1, kER = kNF + 2, kEA = kNF + 3, kED = kNF + 4, kEH = kNF + 5;
+constexpr int kNB = kEH + kStepHeadStagesMax;
 constexpr int kBlkCache = 64;  // block ids of a split cached per step
 
 #ifdef MIE_STEP_STAMPS
@@ -153,6 +162,33 @@ __device__ __forceinline__ bool better(float v, int i, float bv, int bi) { retur
 __device__ __forceinline__ void raise_abort() {
   atomicExch(reinterpret_cast<unsigned long long*>(ps.g.ll + kHdrAbort), 1ull);
 }
+// Barrier over the consumer warps (named barrier 1); the producer warp never
+// takes it.
+__device__ __forceinline__ void csync() { asm volatile("bar.sync 1, %0;" ::"n"(kCT) : "memory"); }
+__device__ __forceinline__ int csync_or(int v) {
+  uint32_t any;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 q, %1, 0;\n\tbarrier.red.or.pred p, 1, %2, q;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(any)
+      : "r"(v), "n"(kCT)
+      : "memory");
+  return (int)any;
+}
+__device__ __forceinline__ void mbar_arrive1(int b) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&bars_s[b])) : "memory");
+}
+// Consumer thread 0, after the consumer barrier that follows the last read of
+// a region: tell the producer the region is free.
+__device__ __forceinline__ void region_free(int b) {
+  if (threadIdx.x == 0) mbar_arrive1(b);
+}
+// Cluster barrier in two halves (the producer warp arrives early and waits
+// late, so the consumers never wait for it).
+__device__ __forceinline__ void cluster_arrive() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
 __device__ __forceinline__ void layer_fetch(const CStepParams& P, int l, int first) {
   constexpr int kWords = (int)(sizeof(mie_layer_desc) / 8);
   const int i = (int)threadIdx.x - first;
@@ -181,19 +217,19 @@ __device__ __noinline__ bool give_up(unsigned long long* t0) {
 }
 
 // Poll n exchange words: dst[i] = value of buf[src(i)] once its tag equals
-// `tag`.  Thread t owns words t, t + kT, ... in groups of four polled
-// together.  1 when this thread gave up.
+// `tag`.  Consumer thread t owns words t, t + kCT, ... in groups of four
+// polled together.  1 when this thread gave up.
 template <typename Src>
 __device__ __forceinline__ int poll(const uint64_t* buf, int n, uint32_t tag, float* dst, Src src) {
   unsigned long long t0 = 0;
 #pragma unroll 1
-  for (int i0 = threadIdx.x; i0 < n; i0 += 4 * kT) {
+  for (int i0 = threadIdx.x; i0 < n; i0 += 4 * kCT) {
     uint64_t w[4];
     int a[4];
     unsigned need = 0;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      const int i = i0 + j * kT;
+      const int i = i0 + j * kCT;
       a[j] = i < n ? src(i) : 0;
       if (i < n) {
         w[j] = ll_ld(buf + a[j]);
@@ -205,7 +241,7 @@ __device__ __forceinline__ int poll(const uint64_t* buf, int n, uint32_t tag, fl
 #pragma unroll
       for (int j = 0; j < 4; ++j)
         if ((need >> j & 1u) && ll_tag(w[j]) == tag) {
-          dst[i0 + j * kT] = ll_val(w[j]);
+          dst[i0 + j * kCT] = ll_val(w[j]);
           need &= ~(1u << j);
         }
       if (!need) break;
@@ -221,25 +257,38 @@ struct Ident {
   __device__ __forceinline__ int operator()(int i) const { return i; }
 };
 
-// Every thread: wait (bounded) for the oldest armed phase of mbarrier b.
+// Every consumer thread: wait (bounded) for the oldest armed phase of full
+// barrier b.
 __device__ __noinline__ bool bwait(bool ok, int b) {
   bool mine = true;
   if (ok) {
     mine = mbar_wait(&bars_s[b], done_s[b] & 1u, ps.d.status, lim_s);
     if (!mine) raise_abort();
   }
-  const int bad = __syncthreads_or(!mine);
+  const int bad = csync_or(!mine);
   if (ok && mine && threadIdx.x == 0) done_s[b] += 1;  // the phase completed
   return ok && !bad;
 }
 
+// Producer warp: wait (bounded) for the next phase of empty barrier b.
+__device__ __noinline__ bool pwait(bool ok, int b) {
+  if (!ok) return false;
+  const bool mine = mbar_wait(&bars_s[b], done_s[b] & 1u, ps.d.status, lim_s);
+  if (!mine) raise_abort();
+  const bool all = __all_sync(0xffffffffu, mine);
+  __syncwarp();
+  if (all && (threadIdx.x & 31) == 0) done_s[b] += 1;
+  __syncwarp();
+  return all;
+}
+
 // Before leaving: wait (bounded) for every armed copy not waited for, so no
-// bulk copy lands in shared memory after the CTA left.
+// copy lands in shared memory after the CTA left.
 __device__ __noinline__ void drain_copies() {
   __syncthreads();
   if (threadIdx.x != 0) return;
 #pragma unroll 1
-  for (int b = 0; b < kNB; ++b)
+  for (int b = 0; b < kNF; ++b)
     while (done_s[b] < armed_s[b]) {
       mbar_wait(&bars_s[b], done_s[b] & 1u, nullptr);
       done_s[b] += 1;
@@ -247,29 +296,32 @@ __device__ __noinline__ void drain_copies() {
 }
 
 // ---------------------------------------------------------------------------
-// Staging.  Every region is filled by ALL threads of the CTA with 16-byte
-// cp.async copies (thread t copies chunks t, t + kT, ...), each thread then
-// arrives on the region's mbarrier (count kT) once its own copies have
-// landed (cp.async.mbarrier.arrive.noinc).  Issuing costs every thread a few
-// instructions; a bulk (TMA) copy instead holds its issuing thread for about
-// 0.4 us when every SM issues at once, which put the copy issue on the
-// critical path.  Called under CTA-uniform conditions only: every thread
-// must arrive exactly once per phase.
+// Consumer staging: right after routing the consumer warps, which would
+// otherwise only wait, fill the expert regions themselves with 16-byte
+// cp.async copies (chunk j by consumer thread j mod kCT); every consumer
+// thread then arrives on the region's full barrier once its own copies landed
+// (cp.async.mbarrier.arrive.noinc).  Spread over 15 warps, the issue keeps
+// enough bytes in flight; the same copies from one warp would not.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void cp16(void* dst, const void* src, uint64_t pol) {
   asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src),
                "l"(pol)
                : "memory");
 }
-// Every thread: `bytes` (a multiple of 16) from src to dst, chunk j by thread j mod kT.
-__device__ __forceinline__ void stage(void* dst, const void* src, uint32_t bytes, uint64_t pol) {
+// Staging side of the calling thread: (index, count).
+struct Side {
+  int i, n;
+};
+__device__ __forceinline__ Side cons_side() { return Side{(int)threadIdx.x, kCT}; }
+// `bytes` (a multiple of 16) from src to dst.
+__device__ __forceinline__ void stage(Side sd, void* dst, const void* src, uint32_t bytes, uint64_t pol) {
 #pragma unroll 1
-  for (uint32_t o = threadIdx.x * 16u; o < bytes; o += kT * 16u)
+  for (uint32_t o = (uint32_t)sd.i * 16u; o < bytes; o += (uint32_t)sd.n * 16u)
     cp16(static_cast<uint8_t*>(dst) + o, static_cast<const uint8_t*>(src) + o, pol);
 }
-// Every thread, after its copies of one phase of barrier b: arrive when they land.
-__device__ __forceinline__ void stage_done(int b) {
-  if (threadIdx.x == 0) armed_s[b] += 1;
+// After this side's copies of one phase of full barrier b: arrive when they land.
+__device__ __forceinline__ void stage_done(Side sd, int b) {
+  if (sd.i == 0) armed_s[b] += 1;
   asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(&bars_s[b])) : "memory");
 }
 
@@ -295,65 +347,10 @@ __device__ __forceinline__ Split split_of(int pos) {
   return a;
 }
 
-// Layer l's q/k/v rows of this split -> region A: q pair first halves, second
-// halves, k pair first halves, second halves, v rows.
-__device__ __noinline__ void issue_qkv(int l) {
-  const mie_step_desc& d = ps.d;
-  const Split a = split_of(cx.pos);
-  const int D = d.hidden_dim;
-  const uint32_t rb = (uint32_t)D * 2u;
-  const uint8_t* w = static_cast<const uint8_t*>(layer_at(l).qkv_w);
-  uint8_t* dst = at<uint8_t>(ps.g.sm_a);
-  const int64_t base = (int64_t)a.h * kHd;
-  const uint64_t pol = policy_evict_first();
-#pragma unroll 1
-  for (int k = 0; k < 4; ++k) {
-    const int64_t row = (k >= 2 ? D : 0) + base + (k & 1) * (kHd / 2) + a.p0;
-    stage(dst + (size_t)k * a.np * rb, w + row * rb, (uint32_t)a.np * rb, pol);
-  }
-  stage(dst + (size_t)4 * a.np * rb, w + (2 * (int64_t)D + base + a.v0) * rb, (uint32_t)a.nv * rb, pol);
-  stage_done(kBA);
-}
-
-// Layer l's out_proj tile of this split -> region O: rows [r0, r0 + nr),
-// the hd columns of head h (row r of the tile at r * hd elements).
-__device__ __noinline__ void issue_otile(int l) {
-  const Split a = split_of(cx.pos);
-  const int D = ps.d.hidden_dim;
-  const bf16* w = static_cast<const bf16*>(layer_at(l).out_w) + (int64_t)a.r0 * D + a.h * kHd;
-  bf16* dst = at<bf16>(ps.g.sm_o);
-  const uint64_t pol = policy_evict_first();
-  constexpr int kPieces = kHd / kPV;  // 16-byte pieces per tile row
-#pragma unroll 1
-  for (int j = threadIdx.x; j < a.nr * kPieces; j += kT) {
-    const int r = j / kPieces, q = j - r * kPieces;
-    cp16(dst + (size_t)r * kHd + q * kPV, w + (int64_t)r * D + q * kPV, pol);
-  }
-  stage_done(kBO);
-}
-
-// Layer l's router rows and both norm weights -> region R, or for l ==
-// num_layers the final norm weights.
-__device__ __noinline__ void issue_side(int l) {
-  const mie_step_desc& d = ps.d;
-  const uint32_t rb = (uint32_t)d.hidden_dim * 2u;
-  uint8_t* dst = at<uint8_t>(ps.g.sm_r);
-  const uint64_t pol = policy_evict_first();
-  if (l == d.num_layers) {
-    stage(dst + (size_t)d.num_experts * rb, d.final_norm_w, rb, pol);
-  } else {
-    const mie_layer_desc& ly = layer_at(l);
-    stage(dst, ly.router_w, (uint32_t)d.num_experts * rb, pol);
-    stage(dst + (size_t)d.num_experts * rb, ly.attn_norm_w, rb, pol);
-    stage(dst + (size_t)(d.num_experts + 1) * rb, ly.moe_norm_w, rb, pol);
-  }
-  stage_done(kBR);
-}
-
 // K/V of tokens [ta, ta + n) of head h, layer l -> region K (K rows, then V
 // rows at chunk_tok): 16-byte piece j of the n K rows then of the n V rows,
 // each through the block table.
-__device__ __noinline__ void issue_kv(int l, int h, int ta, int n) {
+__device__ __noinline__ void issue_kv(Side sd, int b, int l, int h, int ta, int n) {
   const mie_step_desc& d = ps.d;
   const mie_layer_desc& ly = layer_at(l);
   const int bs = d.block_size;
@@ -362,7 +359,7 @@ __device__ __noinline__ void issue_kv(int l, int h, int ta, int n) {
   const uint64_t pol = policy_evict_first();
   const int total = 2 * n * kPieces;
 #pragma unroll 1
-  for (int j = threadIdx.x; j < total; j += kT) {
+  for (int j = sd.i; j < total; j += sd.n) {
     const int v = j >= n * kPieces;
     const int jj = j - v * n * kPieces, t = jj / kPieces, q = jj - t * kPieces;
     const int tok = ta + t, bi = tok / bs;
@@ -378,13 +375,13 @@ __device__ __noinline__ void issue_kv(int l, int h, int ta, int n) {
     cp16(dst + (size_t)v * ps.g.chunk_tok * kHd + (size_t)t * kHd + q * kPV,
          static_cast<const bf16*>(v ? ly.v_cache : ly.k_cache) + off, pol);
   }
-  stage_done(kBK);
+  stage_done(sd, b);
 }
 
 // The selected experts' rows of this CTA: gate rows then up rows of its units
 // -> region A (barrier A), down rows of its output rows, slot 0 then slot 1 ->
 // region D (barrier D).
-__device__ __noinline__ void issue_experts(int l, int sel0, int sel1) {
+__device__ __noinline__ void issue_experts(Side sd, int l, int sel0, int sel1) {
   const mie_step_desc& d = ps.d;
   const CGeom& g = ps.g;
   const mie_layer_desc& ly = layer_at(l);
@@ -402,36 +399,158 @@ __device__ __noinline__ void issue_experts(int l, int sel0, int sel1) {
     for (int k = 0; k < 2; ++k) {
       const int ua = max(u0, k * Hx), ub = min(u1, (k + 1) * Hx);
       if (ub > ua)
-        stage(at<uint8_t>(g.sm_a) + (size_t)(m * nu + ua - u0) * rbD,
+        stage(sd, at<uint8_t>(g.sm_a) + (size_t)(m * nu + ua - u0) * rbD,
               w + ((size_t)(k ? sel1 : sel0) * Hx + ua - k * Hx) * rbD, (uint32_t)(ub - ua) * rbD, pol);
     }
   }
-  stage_done(kBA);
+  stage_done(sd, kFE);
 #pragma unroll 1
   for (int k = 0; k < 2; ++k)
-    stage(at<uint8_t>(g.sm_d) + (size_t)k * nr * rbH,
+    stage(sd, at<uint8_t>(g.sm_d) + (size_t)k * nr * rbH,
           static_cast<const uint8_t*>(ly.w2) + ((size_t)(k ? sel1 : sel0) * D + r0) * rbH, (uint32_t)nr * rbH, pol);
-  stage_done(kBD);
+  stage_done(sd, kFD);
+}
+
+// ---------------------------------------------------------------------------
+// Producer staging: bulk (TMA) copies issued by the producer warp, counted in
+// bytes on the region's full barrier (armed by one lane with expect_tx).  One
+// thread issues a large copy and the copy engine moves the bytes, while a
+// warp issuing 16-byte cp.async copies keeps only a few kilobytes in flight.
+// Issuing holds the producer warp for 0.1-0.4 us per copy, off the
+// consumers' path.  Each copy follows a proxy fence: the consumers read the
+// region with ordinary loads before the empty barrier released it.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void bar_arm(int b, uint32_t bytes) {
+  armed_s[b] += 1;
+  mbar_arrive_expect_tx(&bars_s[b], bytes);
+}
+__device__ __noinline__ void bulk_copy(void* dst, const void* src, uint32_t bytes, int b, bool keep = false) {
+  const uint64_t pol = keep ? policy_evict_last() : policy_evict_first();
+#pragma unroll 1
+  for (uint32_t o = 0; o < bytes; o += kBulkMax)
+    bulk_g2s_stream(static_cast<uint8_t*>(dst) + o, static_cast<const uint8_t*>(src) + o, min(kBulkMax, bytes - o),
+                    &bars_s[b], pol);
+}
+
+// Layer l's q/k/v rows of this split -> region A (producer warp: lane 0 arms,
+// lanes 0-4 issue one copy each: q pair first halves, second halves, k pair
+// first halves, second halves, v rows).
+__device__ __noinline__ void tma_qkv(int l) {
+  const mie_step_desc& d = ps.d;
+  const Split a = split_of(cx.pos);
+  const int lane = threadIdx.x & 31, D = d.hidden_dim;
+  const uint32_t rb = (uint32_t)D * 2u;
+  if (lane == 0) {
+    fence_proxy_async_smem();
+    bar_arm(kFQ, (uint32_t)(4 * a.np + a.nv) * rb);
+  }
+  __syncwarp();
+  if (lane > 4) return;
+  fence_proxy_async_smem();
+  const uint8_t* w = static_cast<const uint8_t*>(layer_at(l).qkv_w);
+  uint8_t* dst = at<uint8_t>(ps.g.sm_a);
+  const int64_t base = (int64_t)a.h * kHd;
+  int64_t row;
+  int n, slot;
+  if (lane < 4) {
+    row = (lane >= 2 ? D : 0) + base + (lane & 1) * (kHd / 2) + a.p0;
+    n = a.np;
+    slot = lane * a.np;
+  } else {
+    row = 2 * (int64_t)D + base + a.v0;
+    n = a.nv;
+    slot = 4 * a.np;
+  }
+  if (n > 0) bulk_copy(dst + (size_t)slot * rb, w + row * rb, (uint32_t)n * rb, kFQ);
+}
+
+// Layer l's out_proj tile of this split (rows [r0, r0 + orows), the hd
+// columns of head h; row r of the tile at r * hd elements) -> region O: one
+// 2-D tensor copy (producer lane 0).
+__device__ __noinline__ void tma_otile(const CStepParams& P, int l) {
+  if ((threadIdx.x & 31) != 0) return;
+  const Split a = split_of(cx.pos);
+  fence_proxy_async_smem();
+  bar_arm(kFO, (uint32_t)ps.g.orows * kHd * 2u);
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(at<uint8_t>(ps.g.sm_o))),
+      "l"(&P.omap[l]), "r"(a.h * kHd), "r"(a.r0), "r"(smem_u32(&bars_s[kFO])), "l"(policy_evict_first())
+      : "memory");
+}
+
+// Layer l's router rows and both norm weights -> region R, or for l ==
+// num_layers the final norm weights (producer lane 0).
+__device__ __noinline__ void tma_side(int l) {
+  if ((threadIdx.x & 31) != 0) return;
+  const mie_step_desc& d = ps.d;
+  const uint32_t rb = (uint32_t)d.hidden_dim * 2u;
+  uint8_t* dst = at<uint8_t>(ps.g.sm_r);
+  fence_proxy_async_smem();
+  if (l == d.num_layers) {
+    bar_arm(kFR, rb);
+    bulk_copy(at<uint8_t>(ps.g.sm_fn), d.final_norm_w, rb, kFR);
+    return;
+  }
+  const mie_layer_desc& ly = layer_at(l);
+  bar_arm(kFR, (uint32_t)(d.num_experts + 2) * rb);
+  bulk_copy(dst, ly.router_w, (uint32_t)d.num_experts * rb, kFR);
+  bulk_copy(dst + (size_t)d.num_experts * rb, ly.attn_norm_w, rb, kFR);
+  bulk_copy(dst + (size_t)(d.num_experts + 1) * rb, ly.moe_norm_w, rb, kFR);
+}
+
+// K/V of tokens [ta, ta + n) of head h, layer l -> region K (K rows, then V
+// rows at chunk_tok), counted on barrier K (producer warp: lane 0 arms, the
+// lanes issue one copy per (block, K or V) segment).
+__device__ __noinline__ void tma_kv(int l, int h, int ta, int n) {
+  const mie_step_desc& d = ps.d;
+  const mie_layer_desc& ly = layer_at(l);
+  const int lane = threadIdx.x & 31, bs = d.block_size;
+  if (lane == 0) {
+    fence_proxy_async_smem();
+    bar_arm(kFK, (uint32_t)(2 * n * kHd * 2));
+  }
+  __syncwarp();
+  fence_proxy_async_smem();
+  bf16* dst = at<bf16>(ps.g.sm_k);
+  const int b0 = ta / bs, b1 = (ta + n - 1) / bs;
+#pragma unroll 1
+  for (int bi = b0 + lane; bi <= b1; bi += 32) {
+    const int tb = max(ta, bi * bs), te = min(ta + n, (bi + 1) * bs);
+    int64_t blk = bi;
+    if (d.block_table) {
+      const int k = bi - cx.blk0;
+      const int pb = (k >= 0 && k < kBlkCache) ? blk_s[k] : __ldg(d.block_table + bi);
+      if (pb < 0 || pb >= d.num_blocks) set_status(d.status, MIE_ERR_RANGE);
+      blk = (pb < 0 || pb >= d.num_blocks) ? 0 : pb;
+    }
+    const int64_t off = blk * d.kv_stride_block + (int64_t)h * d.kv_stride_head + (int64_t)(tb % bs) * d.kv_stride_tok;
+    const uint32_t bytes = (uint32_t)((te - tb) * kHd * 2);
+    bulk_copy(dst + (size_t)(tb - ta) * kHd, static_cast<const bf16*>(ly.k_cache) + off, bytes, kFK);
+    bulk_copy(dst + (size_t)ps.g.chunk_tok * kHd + (size_t)(tb - ta) * kHd, static_cast<const bf16*>(ly.v_cache) + off,
+              bytes, kFK);
+  }
 }
 
 // LM-head stages [first, first + count) of this CTA's vocab rows into the
-// ring over regions A..D; the rows stay in L2 preferentially (evict-last),
-// since every step reads them again.
-__device__ __noinline__ void issue_head(int first, int count) {
+// ring over regions A..D (producer lane 0); the rows stay in L2
+// preferentially (evict-last), since every step reads them again.
+__device__ __noinline__ void tma_head(int first, int count) {
+  if ((threadIdx.x & 31) != 0) return;
   const mie_step_desc& d = ps.d;
   const CGeom& g = ps.g;
   int v0, v1;
   split32(d.vocab, blockIdx.x, g.G, &v0, &v1);
   const uint32_t rb = (uint32_t)d.hidden_dim * 2u;
   const int nst = (v1 - v0 + g.head_rows - 1) / g.head_rows;
-  const uint64_t pol = policy_evict_last();
+  fence_proxy_async_smem();
 #pragma unroll 1
   for (int i = first; i < first + count && i < nst; ++i) {
     const int slot = i % g.head_stages;
     const int r0 = v0 + i * g.head_rows, n = min(g.head_rows, v1 - r0);
-    stage(at<uint8_t>(g.sm_a) + (size_t)slot * g.head_rows * rb,
-          static_cast<const uint8_t*>(d.embedding) + (size_t)r0 * rb, (uint32_t)n * rb, pol);
-    stage_done(kBH + slot);
+    bar_arm(kFH + slot, (uint32_t)n * rb);
+    bulk_copy(at<uint8_t>(g.sm_k) + (size_t)slot * g.head_rows * rb,
+              static_cast<const uint8_t*>(d.embedding) + (size_t)r0 * rb, (uint32_t)n * rb, kFH + slot, true);
   }
 }
 
@@ -440,7 +559,7 @@ __device__ __noinline__ void issue_head(int first, int count) {
 // ---------------------------------------------------------------------------
 // out[r] = rows[r] . x for r < n: bf16 rows of nvec 16-byte vectors (<= 96)
 // staged in shared memory, x fp32 in shared memory (rows [split, n) dot x1
-// when x1 is set).  Warp w forms rows w, w + kW, ...: R rows per iteration,
+// when x1 is set).  Consumer warp w forms rows w, w + kCW, ...: R rows per iteration,
 // one partial sum per 16-byte vector and row.  No barrier.
 template <int R>
 __device__ __forceinline__ void gemv_rows(const uint4* rows, int n, int nvec, const float* xr, const float* xr1,
@@ -449,11 +568,11 @@ __device__ __forceinline__ void gemv_rows(const uint4* rows, int n, int nvec, co
   const int lane = threadIdx.x & 31;
   const uint4 z = make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll 1
-  for (int r = threadIdx.x >> 5; r < n; r += R * kW) {
+  for (int r = threadIdx.x >> 5; r < n; r += R * kCW) {
     uint4 w[R][NV];
 #pragma unroll
     for (int k = 0; k < R; ++k) {
-      const int rk = r + k * kW < n ? r + k * kW : r;
+      const int rk = r + k * kCW < n ? r + k * kCW : r;
       const uint4* rp = rows + (size_t)rk * nvec;
 #pragma unroll
       for (int j = 0; j < NV; ++j) {
@@ -464,7 +583,7 @@ __device__ __forceinline__ void gemv_rows(const uint4* rows, int n, int nvec, co
     float sum[R];
 #pragma unroll
     for (int k = 0; k < R; ++k) {
-      const float* x = (xr1 && r + k * kW >= split) ? xr1 : xr;
+      const float* x = (xr1 && r + k * kCW >= split) ? xr1 : xr;
       sum[k] = 0.f;
 #pragma unroll
       for (int j = 0; j < NV; ++j) sum[k] += dot_vec(w[k][j], x + j * kPV, 0.f, (const bf16*)nullptr);
@@ -477,7 +596,7 @@ __device__ __forceinline__ void gemv_rows(const uint4* rows, int n, int nvec, co
     if (lane == 0) {
 #pragma unroll
       for (int k = 0; k < R; ++k)
-        if (r + k * kW < n) out[r + k * kW] = sum[k];
+        if (r + k * kCW < n) out[r + k * kCW] = sum[k];
     }
   }
 }
@@ -487,13 +606,18 @@ __device__ __noinline__ void gemv(const uint4* rows, int n, int nvec, const floa
   constexpr int NV = Seg<bf16>::kNV;
   if ((int)(threadIdx.x >> 5) >= n) return;
   float xr[NV * kPV];
-  load_x_regs<bf16>(xr, x, nvec);
   if (x1) {
-    float xr1[NV * kPV];
-    load_x_regs<bf16>(xr1, x1, nvec);
-    gemv_rows<2>(rows, n, nvec, xr, xr1, split, out);
-  } else if (n > 2 * kW) {
-    gemv_rows<3>(rows, n, nvec, xr, nullptr, 0, out);  // up to 48 rows in one pass
+    // rows [split, n) dot x1 (n <= kCW: one row per warp, so each warp loads
+    // the one vector its row needs)
+    load_x_regs<bf16>(xr, (int)(threadIdx.x >> 5) >= split ? x1 : x, nvec);
+    gemv_rows<1>(rows, n, nvec, xr, nullptr, 0, out);
+    return;
+  }
+  load_x_regs<bf16>(xr, x, nvec);
+  if (n > 3 * kCW) {
+    gemv_rows<4>(rows, n, nvec, xr, nullptr, 0, out);  // LM-head stages: up to 60 rows in one pass
+  } else if (n > 2 * kCW) {
+    gemv_rows<3>(rows, n, nvec, xr, nullptr, 0, out);  // up to 45 rows in one pass
   } else {
     gemv_rows<2>(rows, n, nvec, xr, nullptr, 0, out);
   }
@@ -504,17 +628,17 @@ __device__ __noinline__ void gemv(const uint4* rows, int n, int nvec, const floa
 __device__ __noinline__ void rms_norm(float* out, const float* in, int D, float eps, const bf16* w) {
   float s2 = 0.f;
 #pragma unroll 1
-  for (int i = threadIdx.x; i < D; i += kT) s2 = fmaf(in[i], in[i], s2);
+  for (int i = threadIdx.x; i < D; i += kCT) s2 = fmaf(in[i], in[i], s2);
   s2 = warp_sum(s2);
   if ((threadIdx.x & 31) == 0) red_s[threadIdx.x >> 5] = s2;
-  __syncthreads();
+  csync();
   float t = 0.f;
 #pragma unroll
-  for (int i = 0; i < kW; ++i) t += red_s[i];
+  for (int i = 0; i < kCW; ++i) t += red_s[i];
   const float rs = rsqrtf(t / (float)D + eps);
 #pragma unroll 1
-  for (int i = threadIdx.x; i < D; i += kT) out[i] = (in[i] * rs) * __bfloat162float(w[i]);
-  __syncthreads();
+  for (int i = threadIdx.x; i < D; i += kCT) out[i] = (in[i] * rs) * __bfloat162float(w[i]);
+  csync();
 }
 
 // Online softmax of q over this split's old tokens [t0, t1) in chunks of
@@ -525,7 +649,7 @@ __device__ __noinline__ bool att_core(bool ok, int l, int h, int t0, int t1, con
   const CGeom& g = ps.g;
   const int tid = threadIdx.x, chunk = g.chunk_tok;
   constexpr int VPH = kHd / kPV;           // 16-byte pieces per K row
-  constexpr int Gp = kT / kHd;             // PV groups
+  constexpr int Gp = kCT / kHd;            // PV groups (threads past Gp * hd idle)
   const int gi = tid / kHd, dc = tid % kHd;
   const bf16* ks = at<const bf16>(g.sm_k);
   const bf16* vs = ks + (size_t)chunk * kHd;
@@ -538,15 +662,15 @@ __device__ __noinline__ bool att_core(bool ok, int l, int h, int t0, int t1, con
   for (int ci = 0; ci < nch; ++ci) {
     const int ta = t0 + ci * chunk, n = min(chunk, t1 - ta);
     if (ci > 0) {
-      __syncthreads();  // the previous chunk is no longer read
-      if (ok) issue_kv(l, h, ta, n);
+      csync();  // the previous chunk is no longer read
+      if (ok) issue_kv(cons_side(), kFK2, l, h, ta, n);
     }
-    ok = bwait(ok, kBK);
+    ok = bwait(ok, ci == 0 ? kFK : kFK2);
     CSTAMP(l, 16);
     float mloc = -INFINITY;
     if (ok) {
 #pragma unroll 1
-      for (int t = tid; t < n; t += kT) {
+      for (int t = tid; t < n; t += kCT) {
         const uint4* kr = reinterpret_cast<const uint4*>(ks + (size_t)t * kHd);
         // the start piece rotates with t: the threads of a warp read distinct banks
         float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
@@ -566,17 +690,17 @@ __device__ __noinline__ bool att_core(bool ok, int l, int h, int t0, int t1, con
     }
     mloc = warp_max(mloc);
     if ((tid & 31) == 0) red_s[tid >> 5] = mloc;
-    __syncthreads();
+    csync();
     float bmax = -INFINITY;
 #pragma unroll
-    for (int i = 0; i < kW; ++i) bmax = fmaxf(bmax, red_s[i]);
+    for (int i = 0; i < kCW; ++i) bmax = fmaxf(bmax, red_s[i]);
     const float mn = fmaxf(m_run, bmax);
     CSTAMP(l, 17);
     const float alpha = m_run == -INFINITY ? 0.f : expf(m_run - mn);
     float ls = 0.f;
     if (ok) {
 #pragma unroll 1
-      for (int t = tid; t < n; t += kT) {
+      for (int t = tid; t < n; t += kCT) {
         const float p = expf(sc[t] - mn);
         sc[t] = p;
         ls += p;
@@ -584,15 +708,23 @@ __device__ __noinline__ bool att_core(bool ok, int l, int h, int t0, int t1, con
     }
     ls = warp_sum(ls);
     if ((tid & 31) == 0) red2_s[tid >> 5] = ls;
-    __syncthreads();  // also orders the probabilities before the PV reads
+    csync();  // also orders the probabilities before the PV reads
     float bsum = 0.f;
 #pragma unroll
-    for (int i = 0; i < kW; ++i) bsum += red2_s[i];
+    for (int i = 0; i < kCW; ++i) bsum += red2_s[i];
     l_run = l_run * alpha + bsum;
     m_run = mn;
     CSTAMP(l, 18);
     float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-    if (ok) {
+    if (ci == 0 && gi == Gp) {
+      // the warp past the PV groups: scale * q . k_new (q, k_new gathered before
+      // the core), for the merge
+      const int lane = tid & 31;
+      float p = q[lane] * q[kHd + lane] + q[lane + 32] * q[kHd + lane + 32];
+      p = warp_sum(p);
+      if (lane == 0) cx.snew = p * scale;
+    }
+    if (ok && gi < Gp) {
       int t = gi;
 #pragma unroll 1
       for (; t + 3 * Gp < n; t += 4 * Gp) {
@@ -607,9 +739,15 @@ __device__ __noinline__ bool att_core(bool ok, int l, int h, int t0, int t1, con
     acc = fmaf(acc, alpha, (a0 + a1) + (a2 + a3));
     CSTAMP(l, 19);
   }
-  __syncthreads();  // every chunk read (the K/V region may be restaged), scores scratch free
-  pv[gi * kHd + dc] = acc;
-  __syncthreads();
+  if (nch == 0 && gi == Gp) {
+    const int lane = tid & 31;
+    float p = q[lane] * q[kHd + lane] + q[lane + 32] * q[kHd + lane + 32];
+    p = warp_sum(p);
+    if (lane == 0) cx.snew = p * scale;
+  }
+  csync();  // every chunk read (the K/V region may be restaged), scores scratch free
+  if (gi < Gp) pv[gi * kHd + dc] = acc;
+  csync();
   if (tid < kHd) {
     float s = 0.f;
 #pragma unroll
@@ -619,7 +757,7 @@ __device__ __noinline__ bool att_core(bool ok, int l, int h, int t0, int t1, con
     res[kHd] = m_run;
     res[kHd + 1] = l_run;
   }
-  __syncthreads();
+  csync();
   return ok;
 }
 
@@ -636,30 +774,29 @@ __device__ __noinline__ bool att_phase(const CStepParams& P, int l, bool ok) {
   const Split a = split_of(pos);
   float* xs = at<float>(g.sm_x);
   float* xn = at<float>(g.sm_xn);
-  const uint32_t rbD = (uint32_t)D * 2u;
   CSTAMP(l, 0);
   // ---- x: the token embedding (layer 0) or exchange X ----
   if (l == 0) {
     const bf16* e = static_cast<const bf16*>(d.embedding) + cx.tok * D;
 #pragma unroll 1
-    for (int i = tid; i < D; i += kT) xs[i] = __bfloat162float(e[i]);
-    __syncthreads();
+    for (int i = tid; i < D; i += kCT) xs[i] = __bfloat162float(e[i]);
+    csync();
   } else {
     int bad = 0;
     if (ok) bad = poll(g.ll + g.off_x[par], D, tag, xs, Ident{});
-    ok = !__syncthreads_or(bad) && ok;
+    ok = !csync_or(bad) && ok;
   }
   CSTAMP(l, 1);
-  ok = bwait(ok, kBR);  // the layer's norm weights (and router)
+  ok = bwait(ok, kFR);  // the layer's norm weights (and router)
   CSTAMP(l, 12);
   rms_norm(xn, xs, D, d.eps, at<const bf16>(g.sm_r) + (size_t)d.num_experts * D);
   // ---- this split's q, k, v rows ----
-  ok = bwait(ok, kBA);
+  ok = bwait(ok, kFQ);
   CSTAMP(l, 14);
   float* qo = at<float>(g.sm_qkv);
   const int nrows = 4 * a.np + a.nv;
   if (ok) gemv(at<const uint4>(g.sm_a), nrows, nvD, xn, qo);
-  __syncthreads();
+  csync();
   CSTAMP(l, 2);
   // ---- RoPE, cache store, send q / k_new / v_new to every CTA of the cluster ----
   float* gq = at<float>(g.sm_g) + (size_t)par * 3 * kHd;  // [q | k | v] of this layer parity
@@ -707,23 +844,13 @@ __device__ __noinline__ bool att_phase(const CStepParams& P, int l, bool ok) {
   cluster_sync_all();  // cluster barrier 1: q, k_new, v_new of the head complete in every CTA
 
   CSTAMP(l, 3);
-  // scale * q . k_new (warp 15, beside the attention core's first loads)
-  if (tid >= kT - 32) {
-    const int lane = tid & 31;
-    float p = gq[lane] * gq[kHd + lane] + gq[lane + 32] * gq[kHd + lane + 32];
-    p = warp_sum(p);
-    if (lane == 0) cx.snew = p * d.attn_scale;
-  }
   // ---- attention over the old tokens ----
   float* mg = at<float>(g.sm_mg) + (size_t)par * kCS * kMg;  // [CS][acc, m, l]
   float* mine = at<float>(g.sm_ov);                          // this split's result, then o
   ok = att_core(ok, l, a.h, a.t0, a.t1, gq, mine);
   CSTAMP(l, 4);
-  // the next layer's first K/V chunk (region K is free)
-  if (ok && l + 1 < d.num_layers) {
-    const int n0 = min(g.chunk_tok, a.t1 - a.t0);
-    if (n0 > 0) issue_kv(l + 1, a.h, a.t0, n0);
-  }
+  // region K is free: the producer stages the next layer's first K/V chunk
+  if (l + 1 < d.num_layers) region_free(kEK);
   CSTAMP(l, 21);
   if (ok && tid < kHd + 2) {
     const float v = mine[tid];
@@ -752,10 +879,10 @@ __device__ __noinline__ bool att_phase(const CStepParams& P, int l, bool ok) {
     }
     ov[tid] = num / den;
   }
-  __syncthreads();
+  csync();
   CSTAMP(l, 23);
   // ---- out_proj partial of head h: rows [r0, r0 + nr) . o_h -> exchange P[h] ----
-  ok = bwait(ok, kBO);
+  ok = bwait(ok, kFO);
   CSTAMP(l, 24);
   if (ok) {
     // 8 lanes per row (8 bf16 each), 4 rows per warp per pass
@@ -767,7 +894,7 @@ __device__ __noinline__ bool att_phase(const CStepParams& P, int l, bool ok) {
     uint64_t* pw = g.ll + g.off_p[par] + (int64_t)a.h * D + a.r0;
     // every lane of a warp takes the same number of passes (the shuffles)
 #pragma unroll 1
-    for (int rw = (tid >> 5) * 4; rw < a.nr; rw += kW * 4) {
+    for (int rw = (tid >> 5) * 4; rw < a.nr; rw += kCW * 4) {
       const int r = rw + sub;
       float s = r < a.nr ? dot_vec(tile[r * (kHd / kPV) + e], o8, 0.f, (const bf16*)nullptr) : 0.f;
       s += __shfl_xor_sync(0xffffffffu, s, 4);
@@ -776,9 +903,9 @@ __device__ __noinline__ bool att_phase(const CStepParams& P, int l, bool ok) {
       if (e == 0 && r < a.nr) ll_put(pw + r, s, tag);
     }
   }
-  __syncthreads();  // the tile is no longer read
+  csync();  // the tile is no longer read
   CSTAMP(l, 25);
-  if (ok && l + 1 < d.num_layers) issue_otile(l + 1);
+  if (l + 1 < d.num_layers) region_free(kEO);
   CSTAMP(l, 6);
   return ok;
 }
@@ -818,9 +945,9 @@ __device__ __noinline__ bool moe_phase(const CStepParams& P, int l, bool ok, boo
       });
     if (!att && l == 0) {
       const bf16* e = static_cast<const bf16*>(d.embedding) + cx.tok * D;
-      for (int i = tid; i < nr; i += kT) pr[H * nr + i] = __bfloat162float(e[r0 + i]);
+      for (int i = tid; i < nr; i += kCT) pr[H * nr + i] = __bfloat162float(e[r0 + i]);
     }
-    ok = !__syncthreads_or(bad) && ok;
+    ok = !csync_or(bad) && ok;
   }
   CSTAMP(l, 26);
   // ---- x_mid rows and their square sum -> every CTA of the cluster ----
@@ -832,23 +959,23 @@ __device__ __noinline__ bool moe_phase(const CStepParams& P, int l, bool ok, boo
   }
   float s2 = warp_sum(v * v);  // rows beyond nr contribute 0
   if ((tid & 31) == 0) red_s[tid >> 5] = s2;
-  __syncthreads();
+  csync();
   if (ok) {
     if (tid < nr) {
 #pragma unroll 1
       for (int r = 0; r < kCS; ++r) dsmem_st(dsmem_addr(xm + r0 + tid, (uint32_t)r), v);
-    } else if (tid >= kT - 32 && tid - (kT - 32) < kCS) {
+    } else if (tid >= kCT - 32 && tid - (kCT - 32) < kCS) {
       float t = 0.f;
 #pragma unroll
-      for (int i = 0; i < kW; ++i) t += red_s[i];
-      dsmem_st(dsmem_addr(ssb + a.s, (uint32_t)(tid - (kT - 32))), t);
+      for (int i = 0; i < kCW; ++i) t += red_s[i];
+      dsmem_st(dsmem_addr(ssb + a.s, (uint32_t)(tid - (kCT - 32))), t);
     }
   }
   CSTAMP(l, 27);
   cluster_sync_all();  // cluster barrier 3: x_mid complete in every CTA
   CSTAMP(l, 7);
   // ---- RMSNorm (square sums of the cluster's shares, in rank order), router, top-2 ----
-  if (!att) ok = bwait(ok, kBR);
+  if (!att) ok = bwait(ok, kFR);
   const bf16* rw = at<const bf16>(g.sm_r);
   {
     float t = 0.f;
@@ -857,12 +984,12 @@ __device__ __noinline__ bool moe_phase(const CStepParams& P, int l, bool ok, boo
     const float rs = rsqrtf(t / (float)D + d.eps);
     const bf16* nw = rw + (size_t)(E + 1) * D;
 #pragma unroll 1
-    for (int i = tid; i < D; i += kT) xn[i] = (xm[i] * rs) * __bfloat162float(nw[i]);
+    for (int i = tid; i < D; i += kCT) xn[i] = (xm[i] * rs) * __bfloat162float(nw[i]);
   }
-  __syncthreads();
+  csync();
   CSTAMP(l, 28);
   if (ok) gemv(reinterpret_cast<const uint4*>(rw), E, nvD, xn, ab);
-  __syncthreads();
+  csync();
   CSTAMP(l, 29);
   // top-2 in registers, every thread: scanning ascending ids with strict
   // comparisons keeps the lower id on ties -- the repeated argmax of the
@@ -890,43 +1017,47 @@ __device__ __noinline__ bool moe_phase(const CStepParams& P, int l, bool ok, boo
   }
   const float e1 = expf(cv - bv);
   const float wt0 = 1.0f / (1.0f + e1), wt1 = e1 / (1.0f + e1);
-  __syncthreads();  // router rows and norm weights read: region R may be restaged
   CSTAMP(l, 30);
-  if (ok) {
-    issue_experts(l, sel0, sel1);
-    issue_side(l + 1);  // the next layer's router + norms, or the final norm
-  }
+  if (ok) issue_experts(cons_side(), l, sel0, sel1);
+  csync();  // router rows and norm weights read: region R may be restaged
+  region_free(kER);  // the producer stages the next layer's router + norms, or the final norm
   CSTAMP(l, 8);
   // ---- up units: silu(gate) * up -> exchange H ----
   int u0, u1, q0, q1;
   split32(2 * Hx, blockIdx.x, g.G, &u0, &u1);
   split32(D, blockIdx.x, g.G, &q0, &q1);
   const int nu = u1 - u0, nq = q1 - q0;
-  ok = bwait(ok, kBA);
+  ok = bwait(ok, kFE);
   CSTAMP(l, 31);
   if (ok) gemv(at<const uint4>(g.sm_a), 2 * nu, nvD, xn, ab);
-  __syncthreads();  // region A no longer read
+  csync();  // region A no longer read
   if (ok && tid < nu) ll_put(g.ll + g.off_h[par] + u0 + tid, silu(ab[tid]) * ab[nu + tid], tag);
-  if (ok && att && l + 1 < d.num_layers) issue_qkv(l + 1);  // the next layer's q/k/v rows
+  if (att && l + 1 < d.num_layers) region_free(kEA);  // the producer stages the next layer's q/k/v rows
   CSTAMP(l, 9);
   // ---- down rows of both slots . h + residual -> exchange X of layer l + 1 ----
   {
     int bad = 0;
     if (ok) bad = poll(g.ll + g.off_h[par], 2 * Hx, tag, hb, Ident{});
-    ok = !__syncthreads_or(bad) && ok;
+    ok = !csync_or(bad) && ok;
   }
   CSTAMP(l, 10);
-  ok = bwait(ok, kBD);
+  ok = bwait(ok, kFD);
+  CSTAMP(l, 13);
   if (ok) gemv(at<const uint4>(g.sm_d), 2 * nq, nvH, hb, ab, hb + Hx, nq);
-  __syncthreads();  // region D no longer read
+  csync();  // region D no longer read
+  CSTAMP(l, 20);
   if (ok && tid < nq) {
     const int r = q0 + tid;
     const float y = fmaf(wt1, ab[nq + tid], fmaf(wt0, ab[tid], xm[r]));
     ll_put(g.ll + g.off_x[(l + 1) & 1] + r, y, tag_of(l + 1));
     if (l == d.num_layers - 1) d.x[r] = y;
   }
-  // after the last layer every staging region but R is free: the first LM-head stages
-  if (ok && l == d.num_layers - 1) issue_head(0, g.head_stages);
+  // after the last layer the ring area is free (x_mid, read just above, lies
+  // in it too): the producer starts the LM-head ring
+  if (l == d.num_layers - 1) {
+    csync();
+    region_free(kED);
+  }
   if (tid == 0) {
     cx.sel0 = sel0;
     cx.sel1 = sel1;
@@ -969,10 +1100,10 @@ __device__ __noinline__ bool head_phase(bool ok) {
   {
     int bad = 0;
     if (ok) bad = poll(g.ll + g.off_x[L & 1], D, tag_of(L), xs, Ident{});
-    ok = !__syncthreads_or(bad) && ok;
+    ok = !csync_or(bad) && ok;
   }
-  ok = bwait(ok, kBR);  // the final norm weights
-  rms_norm(xn, xs, D, d.eps, at<const bf16>(g.sm_r) + (size_t)d.num_experts * D);
+  ok = bwait(ok, kFR);  // the final norm weights
+  rms_norm(xn, xs, D, d.eps, at<const bf16>(g.sm_fn));
   CSTAMP(L, 1);
   int v0, v1;
   split32(d.vocab, c, G, &v0, &v1);
@@ -982,11 +1113,11 @@ __device__ __noinline__ bool head_phase(bool ok) {
 #pragma unroll 1
   for (int i = 0; i < nst; ++i) {
     const int slot = i % g.head_stages;
-    ok = bwait(ok, kBH + slot);
+    ok = bwait(ok, kFH + slot);
     const int r0 = v0 + i * g.head_rows, n = min(g.head_rows, v1 - r0);
-    if (ok) gemv(at<const uint4>(g.sm_a) + (size_t)slot * g.head_rows * nvD, n, nvD, xn, ab);
-    __syncthreads();  // stage no longer read, ab complete
-    if (ok && i + g.head_stages < nst) issue_head(i + g.head_stages, 1);
+    if (ok) gemv(at<const uint4>(g.sm_k) + (size_t)slot * g.head_rows * nvD, n, nvD, xn, ab);
+    csync();  // stage no longer read, ab complete
+    if (i + g.head_stages < nst) region_free(kEH + slot);  // the producer refills the slot
     if (tid < n) {
       const float v = ab[tid];
       const int row = r0 + tid;
@@ -1013,12 +1144,12 @@ __device__ __noinline__ bool head_phase(bool ok) {
     bestv_s[warp] = best_v;
     besti_s[warp] = best_i;
   }
-  __syncthreads();
+  csync();
   if (tid == 0) {
     float bv = -INFINITY;
     int bi = 0x7fffffff;
 #pragma unroll 1
-    for (int w = 0; w < kW; ++w)
+    for (int w = 0; w < kCW; ++w)
       if (better(bestv_s[w], besti_s[w], bv, bi)) {
         bv = bestv_s[w];
         bi = besti_s[w];
@@ -1027,7 +1158,7 @@ __device__ __noinline__ bool head_phase(bool ok) {
     d.lm_partial_idx[c] = bi;
     cx.last = atom_add_acq_rel_gpu(d.lm_counter, 1u) == (uint32_t)(G - 1);
   }
-  __syncthreads();
+  csync();
   if (!cx.last || warp != 0) return true;
   __threadfence();
   float bv = -INFINITY;
@@ -1073,6 +1204,80 @@ __device__ __noinline__ bool gate_open(const int32_t* gate, unsigned long long l
   return true;
 }
 
+// During the last layer: this CTA's LM-head rows (its vocab share of the tied
+// embedding) are prefetched into L2 (producer lane 0), so the LM-head ring
+// after the last layer reads them from L2 instead of HBM.  The rows do not
+// depend on the step; HBM is mostly idle while the layer's dependent phases
+// run.
+__device__ __noinline__ void head_prefetch_l2() {
+  if ((threadIdx.x & 31) != 0) return;
+  const mie_step_desc& d = ps.d;
+  int v0, v1;
+  split32(d.vocab, blockIdx.x, ps.g.G, &v0, &v1);
+  const uint32_t rb = (uint32_t)d.hidden_dim * 2u;
+  const uint8_t* src = static_cast<const uint8_t*>(d.embedding) + (size_t)v0 * rb;
+  const uint32_t nb = (uint32_t)(v1 - v0) * rb;
+#pragma unroll 1
+  for (uint32_t o = 0; o < nb; o += kBulkMax) bulk_prefetch_l2(src + o, min(kBulkMax, nb - o));
+}
+
+// The producer warp's program: it stages, one layer ahead, everything that
+// does not depend on the layer's routing -- the next layer's first K/V chunk,
+// out_proj tile, router + norm weights and q/k/v rows, each once the
+// consumers have read the region for the last time -- then the LM-head ring.
+// It arrives at every cluster barrier as soon as it may (and waits on it
+// late), so the consumers never wait for it; after a failed wait it keeps
+// taking the cluster barriers without staging.
+__device__ __noinline__ void producer(const CStepParams& P, bool att, bool ok) {
+  const mie_step_desc& d = ps.d;
+  const CGeom& g = ps.g;
+  const int L = d.num_layers;
+  const Split a = split_of(cx.pos);
+  const int n0 = min(g.chunk_tok, a.t1 - a.t0);
+  if (ok && att && n0 > 0) tma_kv(0, a.h, a.t0, n0);
+#pragma unroll 1
+  for (int l = 0; l < L; ++l) {
+    if (l + 2 < L && l + 2 >= kLaySlots) layer_fetch(P, l + 2, kProd);  // into the slot of layer l - 2
+    if (l == L - 1 && ok) head_prefetch_l2();
+    if (att) {
+      cluster_arrive();  // barrier 1 (q, k_new, v_new)
+      cluster_wait();
+      cluster_arrive();  // barrier 2 (split results)
+      cluster_wait();
+      cluster_arrive();  // barrier 3 (x_mid), waited for after this layer's staging
+      if (l + 1 < L) {
+        ok = pwait(ok, kEK);
+        if (ok && n0 > 0) tma_kv(l + 1, a.h, a.t0, n0);
+        ok = pwait(ok, kEO);
+        if (ok) tma_otile(P, l + 1);
+      }
+      ok = pwait(ok, kER);
+      if (ok) tma_side(l + 1);
+      if (l + 1 < L) {
+        ok = pwait(ok, kEA);
+        if (ok) tma_qkv(l + 1);
+      }
+      cluster_wait();
+    } else {
+      cluster_arrive();  // barrier 3 (x_mid)
+      ok = pwait(ok, kER);
+      if (ok) tma_side(l + 1);
+      cluster_wait();
+    }
+  }
+  // the LM-head ring over regions A..D, free after the last down projection
+  ok = pwait(ok, kED);
+  if (ok) tma_head(0, g.head_stages);
+  int v0, v1;
+  split32(d.vocab, blockIdx.x, g.G, &v0, &v1);
+  const int nst = (v1 - v0 + g.head_rows - 1) / g.head_rows;
+#pragma unroll 1
+  for (int i = 0; i + g.head_stages < nst; ++i) {
+    ok = pwait(ok, kEH + i % g.head_stages);
+    if (ok) tma_head(i + g.head_stages, 1);
+  }
+}
+
 __global__ void __launch_bounds__(kT, 1) cstep_kernel(const __grid_constant__ CStepParams P) {
   CSTAMP(P.d.num_layers, 3);
   // under programmatic dependent launch the next step's CTAs may take the SMs
@@ -1094,7 +1299,11 @@ __global__ void __launch_bounds__(kT, 1) cstep_kernel(const __grid_constant__ CS
       cx.pos = 0;
 #pragma unroll 1
       for (int b = 0; b < kNB; ++b) {
-        mbar_init(&bars_s[b], kT);  // every thread arrives once per phase
+        // full barriers: one arrival per thread of the filling side; empty: one
+        // full barriers filled by the consumers' cp.async: one arrival per
+        // consumer thread; by the producer's bulk copies, and empty barriers: one
+        const bool cons = b == kFK2 || b == kFE || b == kFD;
+        mbar_init(&bars_s[b], cons ? (uint32_t)kCT : 1u);
         armed_s[b] = done_s[b] = 0;
       }
       fence_barrier_init();
@@ -1104,12 +1313,14 @@ __global__ void __launch_bounds__(kT, 1) cstep_kernel(const __grid_constant__ CS
   const mie_step_desc& d = ps.d;
   const bool att = (int)(blockIdx.x / kCS) < d.num_heads;
   // layer 0's q/k/v rows, out_proj tile, router and norm weights depend on the
-  // CTA alone: staged before the wait (the row splits do not depend on pos)
-  if (att) {
-    issue_qkv(0);
-    issue_otile(0);
+  // CTA alone: the producer warp stages them before the wait
+  if (threadIdx.x >= kProd) {
+    if (att) {
+      tma_qkv(0);
+      tma_otile(P, 0);
+    }
+    tma_side(0);
   }
-  issue_side(0);
   // the previous step's writes are visible from here on
   pdl_wait();
   bool ok = true;
@@ -1175,18 +1386,16 @@ __global__ void __launch_bounds__(kT, 1) cstep_kernel(const __grid_constant__ CS
     ok = gate_ok != 0;
   }
   CSTAMP(d.num_layers, 4);
-  if (ok && att) {
-    const Split a = split_of(cx.pos);
-    const int n0 = min(ps.g.chunk_tok, a.t1 - a.t0);
-    if (n0 > 0) issue_kv(0, a.h, a.t0, n0);
-  }
+  if (threadIdx.x >= kProd) {
+    producer(P, att, ok);
+  } else {
 #pragma unroll 1
-  for (int l = 0; l < d.num_layers; ++l) {
-    if (threadIdx.x >= 448 && l + 2 < d.num_layers && l + 2 >= kLaySlots) layer_fetch(P, l + 2, 448);
-    if (att) ok = att_phase(P, l, ok);
-    ok = moe_phase(P, l, ok, att);
+    for (int l = 0; l < d.num_layers; ++l) {
+      if (att) ok = att_phase(P, l, ok);
+      ok = moe_phase(P, l, ok, att);
+    }
+    head_phase(ok);
   }
-  head_phase(ok);
   drain_copies();
 }
 
@@ -1197,8 +1406,7 @@ int g_max_clusters[64] = {0};  // per device: clusters of the kernel that fit at
 }  // namespace
 
 int cstep_geometry(const mie_step_desc& d, CGeom* out) {
-  // MIE_STEP_AUTO selects the one-CTA-per-SM step while it is the faster one
-  if (d.step_kernel != MIE_STEP_CLUSTER) return MIE_ERR_UNSUPPORTED;
+  if (d.step_kernel == MIE_STEP_FLAT) return MIE_ERR_UNSUPPORTED;
   if (d.dtype != MIE_BF16 || d.kv_dtype != MIE_BF16) return MIE_ERR_UNSUPPORTED;
   if (d.norm != MIE_NORM_RMS || d.act != MIE_ACT_SWIGLU || d.top_k != 2) return MIE_ERR_UNSUPPORTED;
   if (d.head_dim != kHd || d.num_heads * kHd != d.hidden_dim) return MIE_ERR_UNSUPPORTED;
@@ -1246,30 +1454,39 @@ int cstep_geometry(const mie_step_desc& d, CGeom* out) {
   if (d.lm_grid < g.G) return MIE_ERR_INVALID;
   g.nu_max = (2 * Hx + g.G - 1) / g.G;
   g.nr_max = (D + g.G - 1) / g.G;
-  if (2 * g.nu_max > kT || g.nu_max > kT || (H + 1) * g.orows > 6 * kT) return MIE_ERR_UNSUPPORTED;
+  // per-thread epilogues: one up unit / out_proj row / down row per consumer thread
+  if (2 * g.nu_max > kCT || g.orows > kCT || g.nr_max > kCT) return MIE_ERR_UNSUPPORTED;
+  if (2 * g.nr_max > kCW) return MIE_ERR_UNSUPPORTED;  // the down GEMV: one row per consumer warp
   const uint32_t a_bytes = (uint32_t)max(4 * g.np_max + g.nv_max, 2 * g.nu_max) * rbD;
-  g.sm_a = stake(a_bytes);
+  // everything the LM head does not use comes first: after the last layer it
+  // is one contiguous ring of LM-head stages
   g.sm_k = stake((uint32_t)(2 * g.chunk_tok * kHd * 2));
   g.sm_o = stake((uint32_t)(g.orows * kHd * 2));
+  g.sm_a = stake(a_bytes);
   g.sm_d = stake(2u * (uint32_t)g.nr_max * rbH);
   g.sm_r = stake((uint32_t)(E + 2) * rbD);
-  g.sm_x = stake(4u * D);
-  g.sm_xn = stake(4u * D);
   g.sm_xm = stake(8u * D);
-  g.sm_ss = stake(8u * kCS);
   g.sm_g = stake(2u * 3u * kHd * 4u);
   g.sm_mg = stake(2u * kCS * kMg * 4u);
   g.sm_qkv = stake((uint32_t)(4 * g.np_max + g.nv_max) * 4u);
   g.sm_sc = stake((uint32_t)g.chunk_tok * 4u);
-  g.sm_ab = stake(4u * (uint32_t)max(kT, max(E, 2 * g.nu_max)));
   g.sm_h = stake(8u * Hx);
   g.sm_pr = stake((uint32_t)(H + 1) * g.orows * 4u);
   g.sm_ov = stake((kHd + 4) * 4u);
+  // the LM head's vectors and the final norm weights after the ring
+  const uint32_t tail = 4u * D * 2u + 2u * D + 4u * (uint32_t)max(kT, max(E, 2 * g.nu_max)) + 8u * kCS + 5u * 128u;
+  if (so + tail > kStepMaxSmem) return MIE_ERR_UNSUPPORTED;
+  so = kStepMaxSmem - tail;  // the ring takes whatever shared memory is left
+  g.sm_fn = stake(2u * D);
+  g.sm_x = stake(4u * D);
+  g.sm_xn = stake(4u * D);
+  g.sm_ab = stake(4u * (uint32_t)max(kT, max(E, 2 * g.nu_max)));
+  g.sm_ss = stake(8u * kCS);
   g.smem = (so + 127) & ~127u;
   if (g.smem > kStepMaxSmem) return MIE_ERR_UNSUPPORTED;
-  // LM-head ring over regions A..D: stages of 32 rows (two per warp)
-  g.head_rows = 2 * kW;
-  const uint32_t ring = g.sm_r - g.sm_a;
+  // LM-head ring over [sm_k, sm_fn): stages of four rows per consumer warp
+  g.head_rows = 4 * kCW;
+  const uint32_t ring = g.sm_fn - g.sm_k;
   g.head_stages = (int)(ring / ((uint32_t)g.head_rows * rbD));
   if (g.head_stages > kStepHeadStagesMax) g.head_stages = kStepHeadStagesMax;
   if (g.head_stages < 2) return MIE_ERR_UNSUPPORTED;
@@ -1296,7 +1513,21 @@ int cstep_launch(const mie_step_desc& d, const CGeom& g, uint64_t* scratch, cuda
   p.d = d;
   p.g = g;
   p.g.ll = scratch;
-  for (int l = 0; l < d.num_layers; ++l) p.layers[l] = d.layers[l];
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return MIE_ERR_CUDA;
+  const int D = d.hidden_dim;
+  for (int l = 0; l < d.num_layers; ++l) {
+    p.layers[l] = d.layers[l];
+    // out_proj [D rows, D columns] bf16; a tile = hd columns (one head) x orows rows
+    const cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)D};
+    const cuuint64_t strides[1] = {(cuuint64_t)D * 2u};
+    const cuuint32_t box[2] = {(cuuint32_t)kHd, (cuuint32_t)g.orows};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = fn(&p.omap[l], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(d.layers[l].out_w), dims,
+                          strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return MIE_ERR_INVALID;
+  }
   p.d.layers = nullptr;
 #ifdef MIE_STEP_STAMPS
   if (d.num_layers + 1 > kStampLayers || g.G > 160) return MIE_ERR_UNSUPPORTED;
