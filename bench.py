@@ -146,48 +146,111 @@ def time_graph_calls(fn, calls: int, reps: int = 5):
     return e0.elapsed_time(e1) / 1e3 / (reps * calls)
 
 
-def kernel_rooflines(model, cache, hbm_peak):
-    """Isolated per-kernel device times (graphs of back-to-back launches)."""
-    from moe_engine import fused_moe, paged_attention
+def moe_microbench(model, hbm_peak):
+    """config[1]: the isolated fused top-2 MoE layer (``fused_moe.decode``,
+    bf16), the 12 layers' weights cycled (340 MB > L2): graphs of 240
+    back-to-back calls, x ~ N(0, 1) per layer (seed 1)."""
+    from moe_engine import fused_moe
 
     dev = model.token_embedding.weight.device
-    out = {}
-    # MoE: the 12 layers' experts cycled (working set 340 MB > L2)
-    ws = []
-    xs = torch.randn(12, 768, device=dev, dtype=torch.bfloat16)
-    for blk in model.MoEBlocks:
-        moe = blk.moe
-        s = moe._expert_storage
-        ws.append((moe, s))
+    layers = [(blk.moe, blk.moe._expert_storage) for blk in model.MoEBlocks]
+    L = len(layers)
+    xs = torch.randn(L, 768, generator=torch.Generator().manual_seed(1)).to(dev, torch.bfloat16)
     state = {"i": 0}
 
-    def moe_call():
-        i = state["i"] % 12
+    def timed_call():
+        i = state["i"] % L
         state["i"] += 1
-        moe, s = ws[i]
+        moe, s = layers[i]
         fused_moe.decode(xs[i].view(1, 1, 768), moe.router.weight, s["w1"], None, s["w2"], None,
                          router_logits=moe._router_logits, expert_ids=moe._expert_ids,
                          route_weights=moe._route_weights, hidden=moe._expert_hidden, out=moe._direct_out,
                          w3_base=s["w3"], sync=moe._sync)
 
-    t = time_graph_calls(moe_call, 240)
-    out["moe_decode"] = {"us": t * 1e6, "bytes": MOE_LAYER_BYTES, "gbs": MOE_LAYER_BYTES / t / 1e9}
-    # attention at ctx 1024 (12 layers cycled, paged bf16)
-    q = torch.randn(1, 12, 1, 64, device=dev, dtype=torch.bfloat16)
-    ctx = 1024
-    st2 = {"i": 0}
+    t = time_graph_calls(timed_call, 240)
+    return {"us": t * 1e6, "bytes": MOE_LAYER_BYTES, "gbs": MOE_LAYER_BYTES / t / 1e9,
+            "frac": MOE_LAYER_BYTES / t / 1e9 / hbm_peak, "calls_per_graph": 240}
 
-    def attn_call():
-        i = st2["i"] % 12
-        st2["i"] += 1
-        paged_attention.decode(q, cache, i, ctx)
 
-    if len(cache.block_table) * cache.allocator.block_size >= ctx:
-        t = time_graph_calls(attn_call, 120)
-        b = ctx * 12 * 64 * 2 * 2
-        out["attn_decode_ctx1024"] = {"us": t * 1e6, "bytes": b, "gbs": b / t / 1e9}
-    for v in out.values():
-        v["frac"] = v["gbs"] / hbm_peak
+def attn_microbench(device, hbm_peak, contexts=(128, 512, 2048, 8192)):
+    """config[2]: one query [12 heads, 64] bf16 over a paged cache (block 16,
+    K/V ~ N(0, 1) bf16, shuffled block tables), through the C ABI entry point
+    ``mie_attn_decode`` with the operator's split choice.  Per context, graphs
+    of back-to-back calls: "cold" rotates among R disjoint block tables of one
+    pool of >= 256 MB (twice L2), so no call finds its K/V in L2; "hot" reuses
+    one table (the K/V of every call in L2)."""
+    import ctypes
+    import math
+
+    from moe_engine import capi, paged_attention
+
+    lib = capi.ensure_init(device)
+    stream = capi.stream_handle(device)
+    H, hd, bs = 12, 64, 16
+    out = {}
+    for ctx in contexts:
+        nb = -(-ctx // bs)
+        per_table = nb * H * bs * hd * 2 * 2
+        R = max(8, -(-256 * 2**20 // per_table))
+        nblocks = R * nb
+        gen = torch.Generator().manual_seed(2)
+        k = torch.randn(nblocks, H, bs, hd, generator=gen).to(device, torch.bfloat16)
+        v = torch.randn(nblocks, H, bs, hd, generator=gen).to(device, torch.bfloat16)
+        tables = torch.randperm(nblocks, generator=gen).view(R, nb).to(torch.int32).to(device)
+        q = torch.randn(H, hd, generator=gen).to(device, torch.bfloat16)
+        o = torch.empty(H, hd, dtype=torch.bfloat16, device=device)
+        splits = paged_attention.choose_splits(H, nb, lib.mie_num_sms(device.index or 0))
+        partials = torch.zeros(H * paged_attention.MAX_SPLITS * (hd + 2), dtype=torch.float32, device=device)
+        counters = torch.zeros(H, dtype=torch.int32, device=device)
+
+        def args_for(r):
+            a = capi.AttnArgs()
+            a.kv_dtype = a.q_dtype = a.out_dtype = capi.dtype_code(torch.bfloat16)
+            a.num_heads, a.head_dim = H, hd
+            a.q, a.k, a.v = q.data_ptr(), k.data_ptr(), v.data_ptr()
+            a.block_table = tables[r].data_ptr()
+            a.num_blocks, a.block_size = nblocks, bs
+            a.stride_block, a.stride_head, a.stride_tok = H * bs * hd, bs * hd, hd
+            a.ctx_len, a.max_ctx = ctx, nb * bs
+            a.scale = 1.0 / math.sqrt(hd)
+            a.out = o.data_ptr()
+            a.partials, a.counters = partials.data_ptr(), counters.data_ptr()
+            a.splits, a.max_splits = splits, paged_attention.MAX_SPLITS
+            return a
+
+        cold_args = [args_for(r) for r in range(R)]
+        hot_args = [args_for(0)] * R
+        res = {"splits": splits, "ctx": ctx, "bytes": ctx * H * hd * 2 * 2}
+        for name, arglist in (("cold", cold_args), ("hot", hot_args)):
+            for a in arglist[:3]:
+                capi.check(lib.mie_attn_decode(ctypes.byref(a), stream), "mie_attn_decode")
+            torch.cuda.synchronize()
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr):
+                st = capi.stream_handle(device)
+                for a in arglist:
+                    capi.check(lib.mie_attn_decode(ctypes.byref(a), st), "mie_attn_decode")
+            gr.replay()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(3):
+                gr.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            t = e0.elapsed_time(e1) / 1e3 / (3 * R)
+            res[name] = {"us": t * 1e6, "gbs": res["bytes"] / t / 1e9, "frac": res["bytes"] / t / 1e9 / hbm_peak,
+                         "calls_per_graph": R}
+            del gr
+        out[f"attn_decode_ctx{ctx}"] = res
+        del k, v
+    return out
+
+
+def kernel_rooflines(model, hbm_peak):
+    """Isolated per-op kernels: config[1] (MoE) and config[2] (attention)."""
+    out = {"moe_decode": moe_microbench(model, hbm_peak)}
+    out.update(attn_microbench(model.token_embedding.weight.device, hbm_peak))
     return out
 
 
@@ -253,6 +316,7 @@ def run_b200(args, rank, world, device):
         elapsed = float(t)
         torch.distributed.barrier()
     runner.check_status()
+    single_tokens = runner.tokens_log[:NEW_TOKENS].tolist()  # this replica's greedy tokens
     tokens = args.steps * NEW_TOKENS * world
     value = tokens / elapsed
 
@@ -297,7 +361,7 @@ def run_b200(args, rank, world, device):
     weights_bytes = 2 * ACTIVE_PARAMS
     mean_ctx = PROMPT_LEN + NEW_TOKENS / 2
     kv_bytes = KV_BYTES_PER_CTX * mean_ctx
-    k_roof = kernel_rooflines(model, cache, hbm_peak) if rank == 0 else {}
+    k_roof = kernel_rooflines(model, hbm_peak) if rank == 0 else {}
     persistent = launches_per_token == 1
     # dominant kernel: the persistent step kernel (one launch per token) or,
     # on the per-op path, the fused MoE kernel timed in isolation
@@ -381,61 +445,106 @@ def run_b200(args, rank, world, device):
         },
         "gpu_launches": args.steps * NEW_TOKENS * launches_per_token,
     }
+    if world > 1:
+        # independent replicas: each stream decodes at value / world
+        result["per_stream_tok_s"] = value / world
+        result["per_stream_e2e_tok_s"] = e2e_value / world
+        # config[4b] on the same group: one request, experts split over the ranks
+        eps = {}
+        if model.config.num_experts % world == 0:
+            want = [int(t) for t in single_tokens] if rank == 0 else None
+            for payload in ("fp32", "bf16"):
+                eps[payload] = measure_expert_parallel(model, alloc, device, world, max(1, min(args.steps, 2)), 1,
+                                                       payload, want)
+        result["expert_parallel"] = {
+            "n_gpus": world,
+            "experts_per_rank": model.config.num_experts // world,
+            "note": "one request; aggregate = per-stream tok/s; the all-reduce of the [768] MoE partial per layer "
+                    "is captured in a CUDA graph with the step's kernels (layer-by-layer kernels, not the "
+                    "persistent step); tokens compared with rank 0's single-GPU greedy tokens of the same prompt",
+            **{f"{k}_tok_s": v["tok_s"] for k, v in eps.items()},
+            **{f"{k}_tokens": {kk: vv for kk, vv in v.items() if kk not in ("tok_s",)} for k, v in eps.items()},
+        }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(seconds=args.cpu_seconds)
     return result
 
 
-def cpu_baseline(seconds: float = 15.0):
-    """The reference path (--moe reference, contiguous fp32 KV) on the host cores.
+class CpuWindows:
+    """The reference algorithm's CPU decode path (``--moe reference`` with a
+    contiguous fp32 KV cache, restated by the oracle -- the reference engine
+    cannot run BASELINE's architecture unmodified) at three points of the
+    bench's context range: prefixes of 512, 1024 and 1480 tokens are prefilled
+    once (untimed), then timed greedy decode steps continue from each, so the
+    sample covers contexts 513-1536 like the GPU run."""
 
-    Restated by the oracle (the reference engine cannot run BASELINE's
-    architecture unmodified).  Sample: the config[3] 512-token prompt prefill
-    (untimed) then greedy decode steps at context 513+, timed until `seconds`
-    elapse.
-    """
-    import oracle
+    STARTS = (PROMPT_LEN, 1024, 1480)
 
-    ncores = len(os.sched_getaffinity(0))
-    torch.set_num_threads(ncores)
-    P = oracle.init_params(oracle.BASELINE_ARCH, seed=0)
-    dec = oracle.Decoder(P, oracle.BASELINE_ARCH)
-    prompt = torch.randint(0, 50304, (1, PROMPT_LEN), generator=torch.Generator().manual_seed(3))
-    with torch.no_grad():
-        logits = dec.forward(prompt)
-        tok = logits[0, -1].argmax().view(1, 1)
+    def __init__(self):
+        import oracle
+
+        self.cores = len(os.sched_getaffinity(0))
+        torch.set_num_threads(self.cores)
+        P = oracle.init_params(oracle.BASELINE_ARCH, seed=0)
+        ids = torch.randint(0, 50304, (1, max(self.STARTS)), generator=torch.Generator().manual_seed(3))
+        self.windows = []
+        with torch.no_grad():
+            for start in self.STARTS:
+                dec = oracle.Decoder(P, oracle.BASELINE_ARCH)
+                logits = dec.forward(ids[:, :start])
+                self.windows.append([dec, logits[0, -1].argmax().view(1, 1)])
+        self.ctx_seen = [[None, None] for _ in self.STARTS]
+
+    def sample(self, seconds: float):
+        """Decode steps for about `seconds`, a third in each window; returns
+        the per-step times."""
         times = []
-        t_end = time.perf_counter() + seconds
-        while time.perf_counter() < t_end and len(times) < 256:
-            t0 = time.perf_counter()
-            logits = dec.forward(tok)
-            tok = logits[0, -1].argmax().view(1, 1)
-            times.append(time.perf_counter() - t0)
-    times.sort()
-    return {
-        "value": len(times) / sum(times),
-        "unit": "tok/s",
-        "cores": ncores,
-        "kind": "port",
-        "sample": f"BASELINE arch fp32, {PROMPT_LEN}-token prompt, {len(times)} greedy decode steps "
-                  f"(p50 {times[len(times) // 2] * 1e3:.1f} ms/token)",
-    }
+        with torch.no_grad():
+            for wi, w in enumerate(self.windows):
+                dec, tok = w
+                t_end = time.perf_counter() + seconds / len(self.windows)
+                while time.perf_counter() < t_end and dec.position < dec.max_seq:
+                    ctx = dec.position + 1
+                    t0 = time.perf_counter()
+                    logits = dec.forward(tok)
+                    tok = logits[0, -1].argmax().view(1, 1)
+                    times.append(time.perf_counter() - t0)
+                    lo, hi = self.ctx_seen[wi]
+                    self.ctx_seen[wi] = [ctx if lo is None else lo, ctx]
+                w[1] = tok
+        return times
+
+    def describe(self, times) -> str:
+        ranges = ", ".join(f"{lo}-{hi}" for lo, hi in self.ctx_seen if lo is not None)
+        times = sorted(times)
+        return (f"BASELINE arch fp32, {len(times)} greedy decode steps at contexts {ranges} after prefills of "
+                f"{', '.join(map(str, self.STARTS))} tokens (p50 {times[len(times) // 2] * 1e3:.1f} ms/token)")
+
+
+def cpu_baseline(seconds: float = 15.0):
+    """The reference path on the host cores (see CpuWindows); bounded sample."""
+    w = CpuWindows()
+    times = w.sample(seconds)
+    return {"value": len(times) / sum(times), "unit": "tok/s", "cores": w.cores, "kind": "port",
+            "sample": w.describe(times)}
 
 
 def run_reference(args):
-    """--impl reference: the reference algorithm's CPU path (oracle port)."""
+    """--impl reference: the reference algorithm's CPU path (oracle port), each
+    step a bounded sample spread over the bench's context range."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return None
-    steps_t = []
-    cb = None
+    w = CpuWindows()
     for _ in range(args.warmup):
-        cpu_baseline(seconds=2.0)
+        w.sample(1.0)
+    steps_t, all_times = [], []
     for _ in range(args.steps):
-        cb = cpu_baseline(seconds=args.cpu_seconds / max(1, args.steps))
-        steps_t.append(cb["value"])
+        t = w.sample(args.cpu_seconds / max(1, args.steps))
+        all_times += t
+        steps_t.append(len(t) / sum(t))
     value = statistics.median(steps_t)
-    cb["value"] = value
+    cb = {"value": value, "unit": "tok/s", "cores": w.cores, "kind": "port", "sample": w.describe(all_times)}
     return {
         "metric": METRIC,
         "value": value,
@@ -449,44 +558,63 @@ def run_reference(args):
         "dtype": "f32",
         "data": "synthetic",
         "impl": "reference",
-        "config": {"workload": "config[3]-shaped decode, bounded CPU sample (see cpu_baseline.sample)"},
+        "config": {"workload": "config[3]-shaped decode on the host cores: greedy decode steps at contexts spread "
+                               "over 513-1536 (see cpu_baseline.sample)"},
         "cpu_baseline": cb,
         "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
 
 
-def run_expert_parallel(args, rank, world, device):
-    """config[4b]: one request decoded with the 8 experts of every layer split
-    8/N over the N ranks and an NCCL all-reduce of the MoE partial per layer.
-    ``value`` = decode tok/s of the single stream (= aggregate: all ranks serve
-    the same request); device time, CUDA events, max over ranks."""
+def measure_expert_parallel(model, alloc, device, world, steps: int, warmup: int, payload: str, want=None):
+    """config[4b] on the job's process group: one request (the seed-3 prompt
+    of rank 0's replica) decoded with the experts of every layer split 8/N
+    over the ranks and an NCCL all-reduce of the [768] MoE partial per layer,
+    the steps graph-captured with their all-reduces.  Returns tok/s (device
+    time, CUDA events, max over ranks) and, when ``want`` holds the
+    single-GPU tokens of the same prompt, how many leading tokens agree."""
     from moe_engine.expert_parallel import ExpertParallelDecoder
 
-    model = build_model(device, torch.bfloat16)
     prompt = torch.randint(0, 50304, (PROMPT_LEN,), generator=torch.Generator().manual_seed(3))
-    max_blocks = -(-(PROMPT_LEN + NEW_TOKENS) // 16)
-    alloc = model.new_block_allocator(num_blocks=max_blocks + 8, block_size=16, attention_mode="direct")
-    ep = ExpertParallelDecoder(model)
-    times = []
-    produced = 0
-    for it in range(args.warmup + args.steps):
-        cache = alloc.new_cache()
-        _, first = ep.prefill(prompt, cache)
-        torch.distributed.barrier()
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        new = ep.decode(first, NEW_TOKENS, cache)
-        e1.record()
-        torch.cuda.synchronize()
-        cache.free()
-        if it >= args.warmup:
-            times.append(e0.elapsed_time(e1) / 1e3)
-            produced += int(new.numel())
+    ep = ExpertParallelDecoder(model, payload=payload)
+    times, new = [], None
+    try:
+        for it in range(warmup + steps):
+            cache = alloc.new_cache()
+            _, first = ep.prefill(prompt, cache)
+            torch.distributed.barrier()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            new = ep.decode(first, NEW_TOKENS, cache)
+            e1.record()
+            torch.cuda.synchronize()
+            cache.free()
+            if it >= warmup:
+                times.append(e0.elapsed_time(e1) / 1e3)
+    finally:
+        ep.release_graphs()  # NCCL work in graphs: released before the group goes
     t = torch.tensor([sum(times)], device=device)
     torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-    elapsed = float(t)
-    value = produced / elapsed
+    out = {"payload": payload, "tok_s": steps * NEW_TOKENS / float(t), "tokens": int(new.numel())}
+    if want is not None:
+        got = new.tolist()
+        agree = 0
+        for a, b in zip(got, want):
+            if a != b:
+                break
+            agree += 1
+        out["tokens_equal_single_gpu"] = agree == len(want) == len(got)
+        out["leading_tokens_equal"] = agree
+    return out
+
+
+def run_expert_parallel(args, rank, world, device):
+    """--mode ep: the expert-parallel measurement alone, as its own JSON line."""
+    model = build_model(device, torch.bfloat16)
+    max_blocks = -(-(PROMPT_LEN + NEW_TOKENS) // 16)
+    alloc = model.new_block_allocator(num_blocks=max_blocks + 8, block_size=16, attention_mode="direct")
+    res = measure_expert_parallel(model, alloc, device, world, args.steps, args.warmup, "fp32")
+    value = res["tok_s"]
     return {
         "metric": METRIC + " -- expert parallel",
         "value": value,
@@ -494,14 +622,14 @@ def run_expert_parallel(args, rank, world, device):
         "n_gpus": world,
         "steps": args.steps,
         "warmup": args.warmup,
-        "ms_per_step": elapsed / args.steps * 1e3,
+        "ms_per_step": NEW_TOKENS / value * 1e3,
         "higher_is_better": True,
         "scaling": "strong",
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic (random-init weights N(0,0.02), seeded random prompt ids)",
         "config": {"workload": "config[4b] expert parallel: config[3] request, experts split %d/%d per rank, "
-                               "NCCL all-reduce of the fp32 [768] MoE partial per layer, layer-by-layer launches"
+                               "NCCL all-reduce of the fp32 [768] MoE partial per layer, steps graph-captured"
                                % (model.config.num_experts // world, model.config.num_experts),
                    "parallelism": f"ep{world}"},
         "per_stream_tok_s": value,

@@ -235,20 +235,40 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const mie_attn_ar
   __syncthreads();
   if (!last_s) return;
   __threadfence();
-  // log-sum-exp merge of the S partials of this head
+  // log-sum-exp merge of the S partials of this head.  The partials are first
+  // copied into shared memory (the K/V buffers are free) with every thread's
+  // loads in flight together -- loaded one after another from L2 inside the
+  // merge loops they made the merge a chain of dependent L2 round trips.
   const float* hp = a.partials + (size_t)h * a.max_splits * (HD + 2);
+  float* ps = reinterpret_cast<float*>(kvbuf);  // [S][HD + 2]
+  const int np = S * (HD + 2);
+#pragma unroll 1
+  for (int i0 = tid; i0 < np; i0 += 8 * kThreads) {
+    float v[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int i = i0 + k * kThreads;
+      v[k] = i < np ? __ldcg(hp + i) : 0.f;
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int i = i0 + k * kThreads;
+      if (i < np) ps[i] = v[k];
+    }
+  }
+  __syncthreads();
   float M = -INFINITY;
-  for (int j = 0; j < S; ++j) M = fmaxf(M, __ldcg(hp + (size_t)j * (HD + 2)));
+  for (int j = 0; j < S; ++j) M = fmaxf(M, ps[j * (HD + 2)]);
   float Lsum = 0.f;
   for (int j = 0; j < S; ++j) {
-    const float mj = __ldcg(hp + (size_t)j * (HD + 2));
-    if (mj != -INFINITY) Lsum += __ldcg(hp + (size_t)j * (HD + 2) + 1) * expf(mj - M);
+    const float mj = ps[j * (HD + 2)];
+    if (mj != -INFINITY) Lsum += ps[j * (HD + 2) + 1] * expf(mj - M);
   }
   for (int d = tid; d < HD; d += kThreads) {
     float o = 0.f;
     for (int j = 0; j < S; ++j) {
-      const float mj = __ldcg(hp + (size_t)j * (HD + 2));
-      if (mj != -INFINITY) o += __ldcg(hp + (size_t)j * (HD + 2) + 2 + d) * expf(mj - M);
+      const float mj = ps[j * (HD + 2)];
+      if (mj != -INFINITY) o += ps[j * (HD + 2) + 2 + d] * expf(mj - M);
     }
     store_any(a.out, a.out_dtype, (int64_t)h * HD + d, o / Lsum);
   }

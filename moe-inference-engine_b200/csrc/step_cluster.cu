@@ -145,6 +145,7 @@ __shared__ float bestv_s[kW];
 __shared__ int besti_s[kW];
 __shared__ __align__(8) uint64_t bars_s[kNB];
 __shared__ uint32_t armed_s[kNB], done_s[kNB];
+__shared__ uint32_t wdone_s[kCW][kNF];  // full-barrier phases each consumer warp has waited for
 extern __shared__ __align__(128) uint8_t sm[];
 
 template <typename T>
@@ -257,17 +258,21 @@ struct Ident {
   __device__ __forceinline__ int operator()(int i) const { return i; }
 };
 
-// Every consumer thread: wait (bounded) for the oldest armed phase of full
-// barrier b.
+// A consumer warp: wait (bounded) for the next phase of full barrier b.
+// Every thread observes the phase itself (which also makes the staged bytes
+// visible to it), so no barrier is needed; the verdict is warp-uniform and
+// becomes CTA-uniform at the next consumer barrier that carries it.
 __device__ __noinline__ bool bwait(bool ok, int b) {
-  bool mine = true;
-  if (ok) {
-    mine = mbar_wait(&bars_s[b], done_s[b] & 1u, ps.d.status, lim_s);
-    if (!mine) raise_abort();
-  }
-  const int bad = csync_or(!mine);
-  if (ok && mine && threadIdx.x == 0) done_s[b] += 1;  // the phase completed
-  return ok && !bad;
+  if (!ok) return false;
+  const int w = threadIdx.x >> 5;
+  const uint32_t k = wdone_s[w][b];
+  const bool mine = mbar_wait(&bars_s[b], k & 1u, ps.d.status, lim_s);
+  if (!mine) raise_abort();
+  const bool all = __all_sync(0xffffffffu, mine);
+  __syncwarp();
+  if (all && (threadIdx.x & 31) == 0) wdone_s[w][b] = k + 1;
+  __syncwarp();
+  return all;
 }
 
 // Producer warp: wait (bounded) for the next phase of empty barrier b.
@@ -288,11 +293,13 @@ __device__ __noinline__ void drain_copies() {
   __syncthreads();
   if (threadIdx.x != 0) return;
 #pragma unroll 1
-  for (int b = 0; b < kNF; ++b)
-    while (done_s[b] < armed_s[b]) {
-      mbar_wait(&bars_s[b], done_s[b] & 1u, nullptr);
-      done_s[b] += 1;
+  for (int b = 0; b < kNF; ++b) {
+    uint32_t k = wdone_s[0][b];  // phases consumer warp 0 waited for
+    while (k < armed_s[b]) {
+      mbar_wait(&bars_s[b], k & 1u, nullptr);
+      ++k;
     }
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -690,7 +697,7 @@ __device__ __noinline__ bool att_core(bool ok, int l, int h, int t0, int t1, con
     }
     mloc = warp_max(mloc);
     if ((tid & 31) == 0) red_s[tid >> 5] = mloc;
-    csync();
+    ok = !csync_or(!ok);  // CTA-uniform: the next chunk's copies need every consumer thread
     float bmax = -INFINITY;
 #pragma unroll
     for (int i = 0; i < kCW; ++i) bmax = fmaxf(bmax, red_s[i]);
@@ -784,7 +791,7 @@ __device__ __noinline__ bool att_phase(const CStepParams& P, int l, bool ok) {
   } else {
     int bad = 0;
     if (ok) bad = poll(g.ll + g.off_x[par], D, tag, xs, Ident{});
-    ok = !csync_or(bad) && ok;
+    ok = !csync_or(bad || !ok);
   }
   CSTAMP(l, 1);
   ok = bwait(ok, kFR);  // the layer's norm weights (and router)
@@ -947,7 +954,7 @@ __device__ __noinline__ bool moe_phase(const CStepParams& P, int l, bool ok, boo
       const bf16* e = static_cast<const bf16*>(d.embedding) + cx.tok * D;
       for (int i = tid; i < nr; i += kCT) pr[H * nr + i] = __bfloat162float(e[r0 + i]);
     }
-    ok = !csync_or(bad) && ok;
+    ok = !csync_or(bad || !ok);
   }
   CSTAMP(l, 26);
   // ---- x_mid rows and their square sum -> every CTA of the cluster ----
@@ -1038,7 +1045,7 @@ __device__ __noinline__ bool moe_phase(const CStepParams& P, int l, bool ok, boo
   {
     int bad = 0;
     if (ok) bad = poll(g.ll + g.off_h[par], 2 * Hx, tag, hb, Ident{});
-    ok = !csync_or(bad) && ok;
+    ok = !csync_or(bad || !ok);
   }
   CSTAMP(l, 10);
   ok = bwait(ok, kFD);
@@ -1100,7 +1107,7 @@ __device__ __noinline__ bool head_phase(bool ok) {
   {
     int bad = 0;
     if (ok) bad = poll(g.ll + g.off_x[L & 1], D, tag_of(L), xs, Ident{});
-    ok = !csync_or(bad) && ok;
+    ok = !csync_or(bad || !ok);
   }
   ok = bwait(ok, kFR);  // the final norm weights
   rms_norm(xn, xs, D, d.eps, at<const bf16>(g.sm_fn));
@@ -1129,6 +1136,7 @@ __device__ __noinline__ bool head_phase(bool ok) {
     }
   }
   CSTAMP(L, 2);
+  ok = !csync_or(!ok);  // CTA-uniform before the CTA argmax and its barriers
   if (!ok) return false;
   // CTA argmax: (value, lower index) is a total order
 #pragma unroll
@@ -1305,6 +1313,8 @@ __global__ void __launch_bounds__(kT, 1) cstep_kernel(const __grid_constant__ CS
         const bool cons = b == kFK2 || b == kFE || b == kFD;
         mbar_init(&bars_s[b], cons ? (uint32_t)kCT : 1u);
         armed_s[b] = done_s[b] = 0;
+        if (b < kNF)
+          for (int w = 0; w < kCW; ++w) wdone_s[w][b] = 0;
       }
       fence_barrier_init();
     }

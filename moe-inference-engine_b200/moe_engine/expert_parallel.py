@@ -17,6 +17,12 @@ sum_k w_k E_k(x) = sum_ranks sum_{k local} w_k E_k(x).
 
 Each step is launched layer by layer (``mie_decode_layer``, the all-reduce,
 ``mie_decode_head``); the single-GPU persistent step kernel is not used here.
+``decode`` captures whole steps -- every layer's kernels and its NCCL
+all-reduce -- in a CUDA graph and replays it, so the host issues one graph
+launch per ``GRAPH_STEPS`` tokens instead of about fifty launches per token.
+The partial travels as fp32 by default; ``payload="bf16"`` sends it as bf16
+(half the bytes, the residual stream then differs from the single-GPU one by
+the bf16 rounding of each layer's MoE output).
 """
 
 from __future__ import annotations
@@ -41,34 +47,89 @@ def expert_shard(num_experts: int, rank: int, world: int) -> tuple[int, int]:
     return rank * count, count
 
 
+GRAPH_STEPS = 8  # decode steps per captured graph
+
+
 class ExpertParallelDecoder:
     """Greedy decode of one request with the experts split over ``group``.
 
     ``model`` is the full model on this rank's GPU (all ranks identical); only
     the experts [base, base + count) of every layer are read by this rank.
+    ``payload`` is the all-reduced partial's type: "fp32" or "bf16".
     """
 
-    def __init__(self, model, group=None):
+    def __init__(self, model, group=None, payload: str = "fp32", use_graph: bool = True):
+        if payload not in ("fp32", "bf16"):
+            raise ValueError(f"payload must be fp32 or bf16, not {payload!r}")
         self.model = model
         self.group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
+        self.payload = payload
+        self.use_graph = use_graph
         cfg = model.config
         self.expert_base, self.expert_count = expert_shard(cfg.num_experts, self.rank, self.world)
         self.runner = DecodeRunner(model, expert_base=self.expert_base, expert_count=self.expert_count,
                                    moe_partial=True)
+        self._wire = (torch.zeros(cfg.hidden_dim, dtype=torch.bfloat16, device=self.runner.device)
+                      if payload == "bf16" else None)
+        self._graphs: dict = {}
 
     def _desc(self, cache, max_ctx: int):
         _, _, _, _, bs, _, _ = cache_geometry(cache, 0)
         return self.runner.make_desc(cache, logits=False, graph=True,
                                      splits=self.runner.splits_for(max_ctx, bs))
 
+    def _all_reduce(self) -> None:
+        r = self.runner
+        if self._wire is None:
+            dist.all_reduce(r.moe_partial, op=dist.ReduceOp.SUM, group=self.group)
+        else:
+            self._wire.copy_(r.moe_partial)
+            dist.all_reduce(self._wire, op=dist.ReduceOp.SUM, group=self.group)
+            r.moe_partial.copy_(self._wire)
+
     def _step(self, desc, stream) -> None:
-        lib, r = self.runner.lib, self.runner
+        lib = self.runner.lib
         for layer in range(self.model.config.num_layers):
             capi.check(lib.mie_decode_layer(ctypes.byref(desc), layer, stream), "mie_decode_layer")
-            dist.all_reduce(r.moe_partial, op=dist.ReduceOp.SUM, group=self.group)
+            self._all_reduce()
         capi.check(lib.mie_decode_head(ctypes.byref(desc), stream), "mie_decode_head")
+
+    def _graph(self, cache, max_ctx: int):
+        """A CUDA graph of GRAPH_STEPS decode steps (kernels and all-reduces),
+        captured on first use for this cache; every rank captures in the same
+        order.  Steps after EOS change nothing (the kernels see the device
+        flag), so replays past the requested count are harmless."""
+        _, _, _, _, bs, _, _ = cache_geometry(cache, 0)
+        k0 = cache_geometry(cache, 0)[0]
+        table = getattr(cache, "block_table_device", None)
+        key = (k0.data_ptr(), None if table is None else table.data_ptr(), self.runner.splits_for(max_ctx, bs))
+        hit = self._graphs.get(key)
+        if hit is not None:
+            return hit[0]
+        desc, layers = self._desc(cache, max_ctx)
+        r = self.runner
+        # warm-up outside the capture (modules, NCCL communicator) with the
+        # kernels skipping (done = 1), then capture on a side stream
+        r.done.fill_(1)
+        stream = torch.cuda.Stream(device=r.device)
+        stream.wait_stream(torch.cuda.current_stream(r.device))
+        with torch.cuda.stream(stream):
+            self._step(desc, capi.stream_handle(r.device))
+        torch.cuda.current_stream(r.device).wait_stream(stream)
+        torch.cuda.synchronize(r.device)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for _ in range(GRAPH_STEPS):
+                self._step(desc, capi.stream_handle(r.device))
+        self._graphs[key] = (g, desc, layers)
+        return g
+
+    def release_graphs(self) -> None:
+        """Drop the captured graphs (they hold NCCL work: release them before
+        the process group is destroyed)."""
+        self._graphs.clear()
 
     @torch.no_grad()
     def prefill(self, token_ids: torch.Tensor, cache):
@@ -88,14 +149,19 @@ class ExpertParallelDecoder:
         P = cache.position
         if hasattr(cache, "allocator"):
             cache.reserve(P + steps)
+        graph = self._graph(cache, P + steps) if self.use_graph and steps % GRAPH_STEPS == 0 else None
         desc, layers = self._desc(cache, P + steps)
         r.token.fill_(first)
         r.pos.fill_(P)
         r.done.zero_()
         r.log_count.zero_()
-        stream = capi.stream_handle(r.device)
-        for _ in range(steps):
-            self._step(desc, stream)
+        if graph is not None:
+            for _ in range(steps // GRAPH_STEPS):
+                graph.replay()
+        else:
+            stream = capi.stream_handle(r.device)
+            for _ in range(steps):
+                self._step(desc, stream)
         del layers
         r.check_status()
         count = int(r.log_count.item())

@@ -39,10 +39,15 @@ def is_supported(x: torch.Tensor) -> bool:
     return HAS_KERNELS and x.is_cuda and x.dtype in (torch.float32, torch.bfloat16)
 
 
+MIN_BLOCKS_PER_SPLIT = 8  # 128 tokens of bf16 K+V at head_dim 64: one 32 KB stage per CTA
+
+
 def choose_splits(num_heads: int, num_kv_blocks: int, num_sms: int) -> int:
-    """KV splits per head: about two CTAs per SM, at least two blocks per split."""
+    """KV splits per head: at most about two CTAs per SM, and at least
+    MIN_BLOCKS_PER_SPLIT blocks per split, so a CTA streams a whole stage of
+    K/V instead of a few kilobytes between its launch and its merge."""
     want = max(1, -(-2 * num_sms // num_heads))
-    return max(1, min(want, -(-num_kv_blocks // 2), MAX_SPLITS))
+    return max(1, min(want, -(-num_kv_blocks // MIN_BLOCKS_PER_SPLIT), MAX_SPLITS))
 
 
 class _Workspace:
