@@ -664,6 +664,56 @@ def run_profile(steps: int):
     print(json.dumps({"profile_steps": steps, "tokens": int(runner.log_count.item())}), flush=True)
 
 
+def run_profile_ops(reps: int):
+    """Profiling workload (``--profile-ops N``): N calls of the per-op fused MoE
+    kernel (config[1] shapes, the 12 layers cycled) and N calls of the per-op
+    attention kernel (config[2], context 8192, rotating block tables of a
+    256 MB pool); no timing."""
+    import ctypes
+    import math
+
+    from moe_engine import capi, fused_moe, paged_attention
+
+    device = torch.device("cuda", 0)
+    model = build_model(device, torch.bfloat16)
+    layers = [(blk.moe, blk.moe._expert_storage) for blk in model.MoEBlocks]
+    xs = torch.randn(len(layers), 768, generator=torch.Generator().manual_seed(1)).to(device, torch.bfloat16)
+    for i in range(reps):
+        moe, s = layers[i % len(layers)]
+        fused_moe.decode(xs[i % len(layers)].view(1, 1, 768), moe.router.weight, s["w1"], None, s["w2"], None,
+                         router_logits=moe._router_logits, expert_ids=moe._expert_ids,
+                         route_weights=moe._route_weights, hidden=moe._expert_hidden, out=moe._direct_out,
+                         w3_base=s["w3"], sync=moe._sync)
+    lib = capi.ensure_init(device)
+    H, hd, bs, ctx = 12, 64, 16, 8192
+    nb = ctx // bs
+    R = 11
+    gen = torch.Generator().manual_seed(2)
+    k = torch.randn(R * nb, H, bs, hd, generator=gen).to(device, torch.bfloat16)
+    v = torch.randn(R * nb, H, bs, hd, generator=gen).to(device, torch.bfloat16)
+    tables = torch.randperm(R * nb, generator=gen).view(R, nb).to(torch.int32).to(device)
+    q = torch.randn(H, hd, generator=gen).to(device, torch.bfloat16)
+    o = torch.empty(H, hd, dtype=torch.bfloat16, device=device)
+    partials = torch.zeros(H * paged_attention.MAX_SPLITS * (hd + 2), dtype=torch.float32, device=device)
+    counters = torch.zeros(H, dtype=torch.int32, device=device)
+    for i in range(reps):
+        a = capi.AttnArgs()
+        a.kv_dtype = a.q_dtype = a.out_dtype = capi.dtype_code(torch.bfloat16)
+        a.num_heads, a.head_dim = H, hd
+        a.q, a.k, a.v = q.data_ptr(), k.data_ptr(), v.data_ptr()
+        a.block_table = tables[i % R].data_ptr()
+        a.num_blocks, a.block_size = R * nb, bs
+        a.stride_block, a.stride_head, a.stride_tok = H * bs * hd, bs * hd, hd
+        a.ctx_len, a.max_ctx = ctx, nb * bs
+        a.scale = 1.0 / math.sqrt(hd)
+        a.out, a.partials, a.counters = o.data_ptr(), partials.data_ptr(), counters.data_ptr()
+        a.splits = paged_attention.choose_splits(H, nb, lib.mie_num_sms(0))
+        a.max_splits = paged_attention.MAX_SPLITS
+        capi.check(lib.mie_attn_decode(ctypes.byref(a), capi.stream_handle(device)), "mie_attn_decode")
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_ops": reps}), flush=True)
+
+
 def run_profile_prefill(reps: int):
     """Profiling workload (``--profile-prefill N``): the bench's model and
     512-token prompt prefilled N times into fresh paged caches (tensor-core
@@ -695,12 +745,17 @@ def main():
                     help="profiling workload: N decode steps after the prompt, no timing")
     ap.add_argument("--profile-prefill", type=int, default=0, metavar="N",
                     help="profiling workload: N prefills of the 512-token prompt, no timing")
+    ap.add_argument("--profile-ops", type=int, default=0, metavar="N",
+                    help="profiling workload: N calls each of the per-op MoE and attention kernels, no timing")
     args = ap.parse_args()
     if args.profile:
         run_profile(args.profile)
         return
     if args.profile_prefill:
         run_profile_prefill(args.profile_prefill)
+        return
+    if args.profile_ops:
+        run_profile_ops(args.profile_ops)
         return
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
