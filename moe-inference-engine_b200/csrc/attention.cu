@@ -275,6 +275,232 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const mie_attn_ar
   if (tid == 0) a.counters[h] = 0u;  // ready for the next launch
 }
 
+// ---------------------------------------------------------------------------
+// The cp.async kernel (rows of whole 16-byte pieces; the kernel above keeps
+// the narrow rows).  256 threads; the split's physical block ids are read into
+// shared memory first (one round trip instead of one per piece), then every
+// thread issues 16-byte cp.async copies of the split's K and V rows into two
+// chunk buffers of up to 48 KB each -- a split of up to two chunks has its
+// whole range in flight at once -- and the chunks are reduced in order, a
+// chunk's buffer refilled with the chunk after next once it is read.  Chunks
+// holding only old tokens are issued before the programmatic-dependent wait.
+// ---------------------------------------------------------------------------
+constexpr int kFastThreads = 256;
+constexpr uint32_t kFastChunkBytes = 48 * 1024;  // K + V of one chunk buffer
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+template <typename KV, int HD>
+__global__ void __launch_bounds__(kFastThreads) attn_fast_kernel(const mie_attn_args a, AttnLayout L) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  constexpr int T = kFastThreads;
+  constexpr int VPT = 16 / (int)sizeof(KV), VPH = HD / VPT;  // 16-byte pieces per row
+  constexpr int G = T / HD;                                   // PV token groups
+  const int h = blockIdx.y, s = blockIdx.x, S = gridDim.x, tid = threadIdx.x;
+  const int bs = a.block_size, chunk = L.chunk_tok;
+  int* blk_s = reinterpret_cast<int*>(smem + L.off_blk);
+  KV* kvb = reinterpret_cast<KV*>(smem + L.off_kv);  // [2 buffers][K | V][chunk][HD]
+  float* q_s = reinterpret_cast<float*>(smem + L.off_q);
+  float* sc = reinterpret_cast<float*>(smem + L.off_p);
+  float* pv = reinterpret_cast<float*>(smem + L.off_acc);
+  __shared__ float red[T / 32];
+  __shared__ int last_s;
+
+  // context length (see the kernel above: the device position may be read
+  // before the dependency wait; out-of-range values are clamped, reported later)
+  int ctx = a.ctx_dev ? (__ldcg(a.ctx_dev) + a.ctx_dev_offset) : a.ctx_len;
+  const bool bad_ctx = ctx < 1 || ctx > a.max_ctx;
+  if (bad_ctx) ctx = ctx < 1 ? 1 : a.max_ctx;
+  const int nblk = (ctx + bs - 1) / bs;
+  int b0, b1;
+  split_range(nblk, s, S, &b0, &b1);
+  const int tok0 = b0 * bs, tok1 = min(b1 * bs, ctx), ntok = max(0, tok1 - tok0);
+  const int nch = (ntok + chunk - 1) / chunk;
+  for (int i = tid; i < b1 - b0 && i < L.cap_blocks; i += T) {
+    int p = b0 + i;  // contiguous cache: the identity block map
+    if (a.block_table) {
+      p = __ldg(a.block_table + b0 + i);
+      if (p < 0 || p >= a.num_blocks) {
+        set_status(a.status, MIE_ERR_RANGE);
+        p = 0;
+      }
+    }
+    blk_s[i] = p;
+  }
+  __syncthreads();
+  auto issue = [&](int c) {  // chunk c -> buffer c & 1 (every thread; one commit group)
+    const int t0 = tok0 + c * chunk, n = min(chunk, tok1 - t0);
+    KV* kd = kvb + (size_t)(c & 1) * 2 * chunk * HD;
+    KV* vd = kd + (size_t)chunk * HD;
+    for (int j = tid; j < 2 * n * VPH; j += T) {
+      const int v = j >= n * VPH, jj = j - v * n * VPH, t = jj / VPH, pc = jj - t * VPH;
+      const int tok = t0 + t;
+      const int64_t blk = blk_s[min(tok / bs - b0, L.cap_blocks - 1)];
+      const KV* src = static_cast<const KV*>(v ? a.v : a.k) + blk * a.stride_block + (int64_t)h * a.stride_head +
+                      (int64_t)(tok % bs) * a.stride_tok + pc * VPT;
+      cp_async16((v ? vd : kd) + (size_t)t * HD + pc * VPT, src);
+    }
+    cp_async_commit();
+  };
+  // the split's last chunk holds the newest token when the producer grid
+  // writes it: issued only after the wait
+  const int nch_pre = (a.new_token_last && b1 == nblk && nch > 0) ? nch - 1 : nch;
+  int issued = 0;
+  for (; issued < min(2, nch_pre); ++issued) issue(issued);
+
+  pdl_wait();
+  if (skip_requested(a.skip)) {
+    cp_async_wait<0>();  // nothing lands after the CTA left
+    pdl_trigger();
+    return;
+  }
+  pdl_trigger();
+  if (bad_ctx && tid == 0 && s == 0) set_status(a.status, MIE_ERR_RANGE);
+  for (; issued < min(2, nch); ++issued) issue(issued);
+  for (int d = tid; d < HD; d += T) q_s[d] = load_any(a.q, a.q_dtype, (int64_t)h * HD + d);
+
+  const float scale = a.scale;
+  const int g = tid / HD, dcol = tid % HD;
+  float acc = 0.f, m_run = -INFINITY, l_run = 0.f;
+  for (int c = 0; c < nch; ++c) {
+    if (issued - c - 1 >= 1)
+      cp_async_wait<1>();
+    else
+      cp_async_wait<0>();
+    __syncthreads();  // chunk c visible to every thread (and q_s)
+    const int n = min(chunk, tok1 - (tok0 + c * chunk));
+    const KV* kst = kvb + (size_t)(c & 1) * 2 * chunk * HD;
+    const KV* vst = kst + (size_t)chunk * HD;
+    float mloc = -INFINITY;
+    for (int t = tid; t < n; t += T) {
+      const uint4* kr = reinterpret_cast<const uint4*>(kst + (size_t)t * HD);
+      float dot = 0.f;
+#pragma unroll
+      for (int j = 0; j < VPH; ++j) {
+        const int v = (j + t) % VPH;  // rotate the start piece: spreads banks
+        dot = dot_vec(kr[v], q_s + v * VPT, dot, (const KV*)nullptr);
+      }
+      const float scv = dot * scale;
+      sc[t] = scv;
+      mloc = fmaxf(mloc, scv);
+    }
+    const float m_new = fmaxf(m_run, block_max(mloc, red));
+    const float alpha = (m_run == -INFINITY) ? 0.f : expf(m_run - m_new);
+    float lsum = 0.f;
+    for (int t = tid; t < n; t += T) {
+      const float p = expf(sc[t] - m_new);
+      sc[t] = p;
+      lsum += p;
+    }
+    l_run = l_run * alpha + block_sum(lsum, red);  // ends with sc visible to all
+    m_run = m_new;
+    float a0 = 0.f, a1 = 0.f;
+    int t = g;
+    for (; t + G < n; t += 2 * G) {
+      a0 = fmaf(sc[t], Elem<KV>::to_f(vst[(size_t)t * HD + dcol]), a0);
+      a1 = fmaf(sc[t + G], Elem<KV>::to_f(vst[(size_t)(t + G) * HD + dcol]), a1);
+    }
+    if (t < n) a0 = fmaf(sc[t], Elem<KV>::to_f(vst[(size_t)t * HD + dcol]), a0);
+    acc = fmaf(acc, alpha, a0 + a1);
+    __syncthreads();  // buffer c & 1 and the scores are no longer read
+    if (issued < nch) {
+      issue(issued);
+      ++issued;
+    }
+  }
+
+  // combine the PV token groups
+  pv[g * HD + dcol] = acc;
+  __syncthreads();
+  const bool direct_out = (S == 1 && !a.defer_merge);
+  float* part = a.partials + ((size_t)h * a.max_splits + s) * (HD + 2);
+  for (int d = tid; d < HD; d += T) {
+    float v = 0.f;
+#pragma unroll
+    for (int gg = 0; gg < G; ++gg) v += pv[gg * HD + d];
+    if (direct_out)
+      store_any(a.out, a.out_dtype, (int64_t)h * HD + d, ntok > 0 ? v / l_run : 0.f);
+    else
+      part[2 + d] = v;
+  }
+  if (direct_out) return;
+  if (tid == 0) {
+    part[0] = m_run;
+    part[1] = l_run;
+  }
+  if (a.defer_merge) return;
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) last_s = (atom_add_acq_rel_gpu(a.counters + h, 1u) == (uint32_t)(S - 1));
+  __syncthreads();
+  if (!last_s) return;
+  __threadfence();
+  // log-sum-exp merge of the S partials of this head, staged in shared memory
+  // (the chunk buffers are free) with every thread's loads in flight together
+  const float* hp = a.partials + (size_t)h * a.max_splits * (HD + 2);
+  float* ps = reinterpret_cast<float*>(kvb);  // [S][HD + 2]
+  const int np = S * (HD + 2);
+  for (int i0 = tid; i0 < np; i0 += 8 * T) {
+    float v[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int i = i0 + k * T;
+      v[k] = i < np ? __ldcg(hp + i) : 0.f;
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int i = i0 + k * T;
+      if (i < np) ps[i] = v[k];
+    }
+  }
+  __syncthreads();
+  float M = -INFINITY;
+  for (int j = 0; j < S; ++j) M = fmaxf(M, ps[j * (HD + 2)]);
+  float Lsum = 0.f;
+  for (int j = 0; j < S; ++j) {
+    const float mj = ps[j * (HD + 2)];
+    if (mj != -INFINITY) Lsum += ps[j * (HD + 2) + 1] * expf(mj - M);
+  }
+  for (int d = tid; d < HD; d += T) {
+    float o = 0.f;
+    for (int j = 0; j < S; ++j) {
+      const float mj = ps[j * (HD + 2)];
+      if (mj != -INFINITY) o += ps[j * (HD + 2) + 2 + d] * expf(mj - M);
+    }
+    store_any(a.out, a.out_dtype, (int64_t)h * HD + d, o / Lsum);
+  }
+  if (tid == 0) a.counters[h] = 0u;  // ready for the next launch
+}
+
+// The cp.async kernel exists for rows of whole 16-byte pieces only.
+template <typename KV, int HD>
+void* fast_kernel_or_null() {
+  if constexpr ((HD * sizeof(KV)) % 16 == 0)
+    return (void*)attn_fast_kernel<KV, HD>;
+  else
+    return nullptr;
+}
+template <typename KV>
+void* pick_fast(int hd) {
+  switch (hd) {
+    case 4: return fast_kernel_or_null<KV, 4>();
+    case 8: return fast_kernel_or_null<KV, 8>();
+    case 16: return fast_kernel_or_null<KV, 16>();
+    case 32: return fast_kernel_or_null<KV, 32>();
+    case 64: return fast_kernel_or_null<KV, 64>();
+    case 96: return fast_kernel_or_null<KV, 96>();
+    case 128: return fast_kernel_or_null<KV, 128>();
+    default: return nullptr;
+  }
+}
+
 template <typename KV>
 void* pick(int hd) {
   switch (hd) {
@@ -318,20 +544,47 @@ AttnLayout attn_layout(const mie_attn_args& a) {
   L.smem = (uint32_t)((off + 127) & ~size_t(127));
   // One block of K+V must fit the per-thread register staging (16-byte rows).
   if ((a.head_dim * esz) % 16 == 0 && per_tok * st > budget) L.smem = 0xffffffffu;  // -> unsupported
+  // 16-byte rows run the cp.async kernel: two chunk buffers of up to 48 KB of
+  // K + V each (whole blocks), the split's block ids, q, scores, PV partials
+  if ((a.head_dim * esz) % 16 == 0 && a.splits > 0) {
+    AttnLayout F{};
+    F.fast = 1;
+    int ct = (int)(kFastChunkBytes / (uint32_t)per_tok) / a.block_size * a.block_size;
+    if (ct < a.block_size) ct = a.block_size;
+    F.chunk_tok = ct;
+    const int max_blk = (a.max_ctx + a.block_size - 1) / a.block_size;
+    F.cap_blocks = (max_blk + a.splits - 1) / a.splits;
+    if (F.cap_blocks < 1) F.cap_blocks = 1;
+    off = 0;
+    F.off_kv = take((size_t)2 * per_tok * ct);
+    F.off_blk = take(sizeof(int) * (size_t)F.cap_blocks);
+    F.off_q = take(sizeof(float) * a.head_dim);
+    F.off_p = take(sizeof(float) * ct);
+    F.off_acc = take(sizeof(float) * kFastThreads);
+    F.smem = (uint32_t)((off + 127) & ~size_t(127));
+    // the merge stages every split's partial in the chunk buffers
+    if ((size_t)a.splits * (a.head_dim + 2) * 4 <= (size_t)2 * per_tok * ct && F.smem <= (uint32_t)kMaxDynSmem)
+      return F;
+  }
   return L;
 }
 
 int attn_decode_launch(const mie_attn_args& a, const AttnLayout& L, cudaStream_t st, bool pdl) {
-  void* k = a.kv_dtype == MIE_BF16 ? pick<__nv_bfloat16>(a.head_dim) : pick<float>(a.head_dim);
+  void* k = L.fast ? (a.kv_dtype == MIE_BF16 ? pick_fast<__nv_bfloat16>(a.head_dim) : pick_fast<float>(a.head_dim))
+                   : (a.kv_dtype == MIE_BF16 ? pick<__nv_bfloat16>(a.head_dim) : pick<float>(a.head_dim));
   if (!k) return MIE_ERR_UNSUPPORTED;
   using K = void (*)(const mie_attn_args, AttnLayout);
-  return launch(reinterpret_cast<K>(k), dim3(a.splits, a.num_heads), dim3(kThreads), L.smem, st, pdl, a, L);
+  return launch(reinterpret_cast<K>(k), dim3(a.splits, a.num_heads), dim3(L.fast ? kFastThreads : kThreads), L.smem,
+                st, pdl, a, L);
 }
 
 void attn_set_attributes() {
   for (int hd : {4, 8, 16, 32, 64, 96, 128}) {
     set_max_smem(pick<float>(hd));
     set_max_smem(pick<__nv_bfloat16>(hd));
+    if (void* f = pick_fast<float>(hd)) set_max_smem(reinterpret_cast<void (*)(const mie_attn_args, AttnLayout)>(f));
+    if (void* f = pick_fast<__nv_bfloat16>(hd))
+      set_max_smem(reinterpret_cast<void (*)(const mie_attn_args, AttnLayout)>(f));
   }
 }
 

@@ -33,6 +33,10 @@ struct AttnLayout {
   uint32_t off_bar, off_kv, off_q, off_p, off_acc, smem;
   int nstage;
   int stage_tokens;  // tokens per stage (a multiple of block_size)
+  // the cp.async kernel (16-byte K/V rows): tokens per chunk buffer, block
+  // ids of one split cached in shared memory, their offset
+  int fast, chunk_tok, cap_blocks;
+  uint32_t off_blk;
 };
 
 // Dynamic shared memory any layout here may use (under the 227 KB opt-in

@@ -43,10 +43,11 @@ MIN_BLOCKS_PER_SPLIT = 8  # 128 tokens of bf16 K+V at head_dim 64: one 32 KB sta
 
 
 def choose_splits(num_heads: int, num_kv_blocks: int, num_sms: int) -> int:
-    """KV splits per head: at most about two CTAs per SM, and at least
+    """KV splits per head: at most two CTAs per SM (the kernel's shared memory
+    holds two at once, so a third would run in a second wave), and at least
     MIN_BLOCKS_PER_SPLIT blocks per split, so a CTA streams a whole stage of
     K/V instead of a few kilobytes between its launch and its merge."""
-    want = max(1, -(-2 * num_sms // num_heads))
+    want = max(1, 2 * num_sms // num_heads)
     return max(1, min(want, -(-num_kv_blocks // MIN_BLOCKS_PER_SPLIT), MAX_SPLITS))
 
 

@@ -313,7 +313,7 @@ def test_split_choice_bounds():
     assert paged_attention.MIN_BLOCKS_PER_SPLIT == 8
     assert paged_attention.choose_splits(12, 96, 148) == 12   # ctx 1536: 8 blocks (128 tokens) per split
     assert paged_attention.choose_splits(12, 8, 148) == 1     # ctx 128: one split per head
-    assert paged_attention.choose_splits(12, 512, 148) == 25  # ctx 8192: ~2 CTAs per SM
+    assert paged_attention.choose_splits(12, 512, 148) == 24  # ctx 8192: two CTAs per SM, one wave
     assert paged_attention.choose_splits(12, 1, 148) == 1
     assert paged_attention.choose_splits(8, 512, 148) == 37
     assert paged_attention.choose_splits(1, 10_000, 148) == paged_attention.MAX_SPLITS
