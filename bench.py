@@ -357,6 +357,29 @@ def run_b200(args, rank, world, device):
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MIN)
         e2e_value = float(t) * world
 
+    # the prompt prefill alone (graph-replayed after its first run): GPU time
+    # (CUDA events) and wall time of model(prompt) into a fresh cache
+    pf_gpu, pf_wall = [], []
+    dprompt = prompt[None].to(device)
+    for it in range(4):
+        c = alloc.new_cache()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        e0p, e1p = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0p.record()
+        with torch.no_grad():
+            model(dprompt, c)
+        e1p.record()
+        torch.cuda.synchronize()
+        t1 = time.perf_counter()
+        c.free()
+        if it > 0:
+            pf_gpu.append(e0p.elapsed_time(e1p))
+            pf_wall.append((t1 - t0) * 1e3)
+    prefill = {"tokens": PROMPT_LEN, "gpu_ms": statistics.median(pf_gpu), "wall_ms": statistics.median(pf_wall),
+               "note": "model(prompt) into a fresh paged cache: tcgen05 GEMMs, the causal attention kernel and "
+                       "the per-token kernels, replayed from the captured prefill graph"}
+
     # rooflines
     step_s = elapsed / (args.steps * NEW_TOKENS)  # seconds per token on each replica
     weights_bytes = 2 * ACTIVE_PARAMS
@@ -436,6 +459,7 @@ def run_b200(args, rank, world, device):
             "note": roof_note,
         },
         "kernels": k_roof,
+        "prefill": prefill,
         "clocks": clocks.summary(),
         "e2e": {
             "value": e2e_value,

@@ -446,6 +446,22 @@ typedef struct mie_prefill_combine_args {
   const int32_t* rows;       /* [tokens, 2] */
 } mie_prefill_combine_args;
 
+/* Causal self-attention of the prompt prefill (replaces the reference's
+ * F.scaled_dot_product_attention(q, k, v, is_causal=True) of the prefill fast
+ * path, src/moe_engine/model.py:252-256): o[t, h hd + d] = sum_{s <= t}
+ * softmax_s(scale q_h[t] . k_h[s]) v_h[s][d], fp32 accumulation. */
+typedef struct mie_prefill_attn_args {
+  int tokens;
+  int num_heads;
+  int head_dim;              /* 64, 96 or 128 */
+  float scale;               /* normally 1 / sqrt(head_dim) */
+  const void* q;             /* bf16 [num_heads, tokens, head_dim] */
+  const void* k;
+  const void* v;
+  void* out;                 /* bf16 [tokens, ld_out] */
+  int64_t ld_out;            /* >= num_heads * head_dim */
+} mie_prefill_attn_args;
+
 /* Library management */
 int mie_version(void);
 int mie_init(int device);                 /* set kernel attributes; call before any capture */
@@ -512,6 +528,7 @@ int mie_prefill_norm(const mie_prefill_norm_args* a, void* stream);
 int mie_prefill_rope_kv(const mie_prefill_rope_args* a, void* stream);
 int mie_prefill_route(const mie_prefill_route_args* a, void* stream);
 int mie_prefill_combine(const mie_prefill_combine_args* a, void* stream);
+int mie_prefill_attention(const mie_prefill_attn_args* a, void* stream);
 
 #ifdef __cplusplus
 }

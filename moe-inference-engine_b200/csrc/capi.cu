@@ -481,6 +481,9 @@ int mie_prefill_route(const mie_prefill_route_args* a, void* stream) {
 int mie_prefill_combine(const mie_prefill_combine_args* a, void* stream) {
   return a ? prefill_combine(*a, static_cast<cudaStream_t>(stream)) : MIE_ERR_INVALID;
 }
+int mie_prefill_attention(const mie_prefill_attn_args* a, void* stream) {
+  return a ? prefill_attention(*a, static_cast<cudaStream_t>(stream)) : MIE_ERR_INVALID;
+}
 
 int mie_decode_layer(const mie_step_desc* d, int l, void* stream) {
   if (!d || l < 0 || l >= d->num_layers) return MIE_ERR_INVALID;

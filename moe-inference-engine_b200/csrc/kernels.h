@@ -227,6 +227,7 @@ int prefill_norm(const mie_prefill_norm_args& a, cudaStream_t st);
 int prefill_rope_kv(const mie_prefill_rope_args& a, cudaStream_t st);
 int prefill_route(const mie_prefill_route_args& a, cudaStream_t st);
 int prefill_combine(const mie_prefill_combine_args& a, cudaStream_t st);
+int prefill_attention(const mie_prefill_attn_args& a, cudaStream_t st);
 
 int num_sms();
 

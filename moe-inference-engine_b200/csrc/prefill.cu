@@ -260,7 +260,190 @@ __global__ void __launch_bounds__(kPfThreads) prefill_combine_kernel(const mie_p
 
 unsigned grid_for(int items) { return (unsigned)((items + kPfWarps - 1) / kPfWarps); }
 
+// ---------------------------------------------------------------------------
+// Causal attention of the prompt: one CTA per (64-query tile, head), 256
+// threads.  Key tiles of 64 up to the diagonal are staged in shared memory as
+// fp32 (K transposed, V as rows); thread (ty, tx) holds the scores of queries
+// 4 ty .. 4 ty + 3 against keys 4 tx .. 4 tx + 3 and the outputs of those
+// queries in dims tx, tx + 16, ...; the online softmax keeps a running max and
+// sum per query, reduced over the 16 threads of a query row with shuffles.
+// At prompt lengths of hundreds of tokens the whole attention is a few hundred
+// MFLOP spread over ~100 CTAs: the kernel is latency bound whatever unit does
+// the arithmetic, and plain fp32 FMAs keep the reference's fp32 accumulation.
+// ---------------------------------------------------------------------------
+constexpr int kAtQ = 64, kAtK = 64, kAtThreads = 256;
+
+template <int HD>
+__global__ void __launch_bounds__(kAtThreads) prefill_attention_kernel(const mie_prefill_attn_args a) {
+  constexpr int DPT = HD / 16;  // output dims per thread
+  extern __shared__ __align__(16) float at_sm[];
+  float* qt = at_sm;                 // [HD][kAtQ]   q transposed
+  float* kt = qt + HD * kAtQ;        // [HD][kAtK]   k transposed
+  float* vs = kt + HD * kAtK;        // [kAtK][HD]
+  float* pt = vs + kAtK * HD;        // [kAtK][kAtQ] probabilities transposed
+  const int h = blockIdx.y, q0 = blockIdx.x * kAtQ, T = a.tokens, tid = threadIdx.x;
+  const int ty = tid >> 4, tx = tid & 15;
+  const __nv_bfloat16* qh = static_cast<const __nv_bfloat16*>(a.q) + (int64_t)h * T * HD;
+  const __nv_bfloat16* kh = static_cast<const __nv_bfloat16*>(a.k) + (int64_t)h * T * HD;
+  const __nv_bfloat16* vh = static_cast<const __nv_bfloat16*>(a.v) + (int64_t)h * T * HD;
+  // a tile of 64 rows as 16-byte vectors (8 bf16 of one row each): every
+  // thread's loads are issued before any is converted and stored
+  constexpr int kVecRow = HD / 8, kVecs = kAtK * kVecRow, kPer = (kVecs + kAtThreads - 1) / kAtThreads;
+  auto load_tile = [&](const __nv_bfloat16* base, int r0, uint4* v) {
+#pragma unroll
+    for (int u = 0; u < kPer; ++u) {
+      const int i = tid + u * kAtThreads, r = i / kVecRow, c = i - r * kVecRow;
+      v[u] = (i < kVecs && r0 + r < T) ? __ldg(reinterpret_cast<const uint4*>(base + (int64_t)(r0 + r) * HD) + c)
+                                       : make_uint4(0u, 0u, 0u, 0u);
+    }
+  };
+  auto unpack = [](uint4 v, float* f) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      f[2 * e] = __uint_as_float(w[e] << 16);
+      f[2 * e + 1] = __uint_as_float(w[e] & 0xffff0000u);
+    }
+  };
+  {
+    uint4 qv[kPer];
+    load_tile(qh, q0, qv);
+#pragma unroll
+    for (int u = 0; u < kPer; ++u) {
+      const int i = tid + u * kAtThreads, r = i / kVecRow, c = i - r * kVecRow;
+      if (i >= kVecs) continue;
+      float f[8];
+      unpack(qv[u], f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) qt[(c * 8 + e) * kAtQ + r] = f[e] * a.scale;
+    }
+  }
+  float m[4], l[4], o[4][DPT];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    m[i] = -INFINITY;
+    l[i] = 0.f;
+#pragma unroll
+    for (int j = 0; j < DPT; ++j) o[i][j] = 0.f;
+  }
+  const int qlast = min(q0 + kAtQ, T) - 1;  // the last query of the tile sees keys up to qlast
+  for (int k0 = 0; k0 <= qlast; k0 += kAtK) {
+    {
+      uint4 kv4[kPer], vv4[kPer];
+      load_tile(kh, k0, kv4);  // in flight while the previous tile is finished with
+      load_tile(vh, k0, vv4);
+      __syncthreads();  // previous tile's k, v, p no longer read (and q staged)
+#pragma unroll
+      for (int u = 0; u < kPer; ++u) {
+        const int i = tid + u * kAtThreads, r = i / kVecRow, c = i - r * kVecRow;
+        if (i >= kVecs) continue;
+        float f[8], g[8];
+        unpack(kv4[u], f);
+        unpack(vv4[u], g);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          kt[(c * 8 + e) * kAtK + r] = f[e];
+          vs[r * HD + c * 8 + e] = g[e];
+        }
+      }
+    }
+    __syncthreads();
+    float sc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) sc[i][j] = 0.f;
+#pragma unroll 4
+    for (int d = 0; d < HD; ++d) {
+      const float4 qa = *reinterpret_cast<const float4*>(qt + d * kAtQ + 4 * ty);
+      const float4 kb = *reinterpret_cast<const float4*>(kt + d * kAtK + 4 * tx);
+      const float qv[4] = {qa.x, qa.y, qa.z, qa.w}, kv[4] = {kb.x, kb.y, kb.z, kb.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) sc[i][j] = fmaf(qv[i], kv[j], sc[i][j]);
+    }
+    // causal mask and the online softmax of each of this thread's four queries
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int qi = q0 + 4 * ty + i;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int kj = k0 + 4 * tx + j;
+        if (kj > qi || kj >= T) sc[i][j] = -INFINITY;
+        mx = fmaxf(mx, sc[i][j]);
+      }
+#pragma unroll
+      for (int off = 8; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+      const float mn = fmaxf(m[i], mx);
+      const float alpha = m[i] == -INFINITY ? 0.f : expf(m[i] - mn);
+      float rs = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float p = mn == -INFINITY ? 0.f : expf(sc[i][j] - mn);
+        sc[i][j] = p;
+        rs += p;
+      }
+#pragma unroll
+      for (int off = 8; off > 0; off >>= 1) rs += __shfl_xor_sync(0xffffffffu, rs, off);
+      l[i] = l[i] * alpha + rs;
+      m[i] = mn;
+#pragma unroll
+      for (int j = 0; j < DPT; ++j) o[i][j] *= alpha;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) pt[(4 * tx + j) * kAtQ + 4 * ty + i] = sc[i][j];
+    }
+    __syncthreads();
+    // o += p . v over the tile's keys
+#pragma unroll 2
+    for (int kj = 0; kj < kAtK; ++kj) {
+      const float4 pa = *reinterpret_cast<const float4*>(pt + kj * kAtQ + 4 * ty);
+      const float pv[4] = {pa.x, pa.y, pa.z, pa.w};
+#pragma unroll
+      for (int j = 0; j < DPT; ++j) {
+        const float vv = vs[kj * HD + tx + 16 * j];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) o[i][j] = fmaf(pv[i], vv, o[i][j]);
+      }
+    }
+  }
+  __nv_bfloat16* out = static_cast<__nv_bfloat16*>(a.out);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int qi = q0 + 4 * ty + i;
+    if (qi >= T) continue;
+    const float inv = 1.0f / l[i];
+#pragma unroll
+    for (int j = 0; j < DPT; ++j)
+      out[(int64_t)qi * a.ld_out + (int64_t)h * HD + tx + 16 * j] = __float2bfloat16_rn(o[i][j] * inv);
+  }
+}
+
+template <int HD>
+int prefill_attention_launch(const mie_prefill_attn_args& a, cudaStream_t st) {
+  const uint32_t smem = (uint32_t)sizeof(float) * (2 * HD * kAtQ + kAtK * HD + kAtK * kAtQ);
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(prefill_attention_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    attr = true;
+  }
+  return launch(prefill_attention_kernel<HD>, dim3((unsigned)((a.tokens + kAtQ - 1) / kAtQ), (unsigned)a.num_heads),
+                dim3(kAtThreads), smem, st, false, a);
+}
+
 }  // namespace
+
+int prefill_attention(const mie_prefill_attn_args& a, cudaStream_t st) {
+  if (a.tokens <= 0 || a.num_heads <= 0 || !a.q || !a.k || !a.v || !a.out || a.ld_out < (int64_t)a.num_heads * a.head_dim)
+    return MIE_ERR_INVALID;
+  switch (a.head_dim) {
+    case 64: return prefill_attention_launch<64>(a, st);
+    case 96: return prefill_attention_launch<96>(a, st);
+    case 128: return prefill_attention_launch<128>(a, st);
+    default: return MIE_ERR_UNSUPPORTED;
+  }
+}
 
 int prefill_norm(const mie_prefill_norm_args& a, cudaStream_t st) {
   if (a.tokens <= 0 || a.hidden_dim <= 0 || a.hidden_dim % 32 || a.hidden_dim > kPfMaxDim || !a.x || !a.w ||

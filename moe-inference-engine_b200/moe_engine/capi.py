@@ -128,6 +128,13 @@ class PrefillNormArgs(ctypes.Structure):
     ]
 
 
+class PrefillAttnArgs(ctypes.Structure):
+    _fields_ = [
+        ("tokens", _i), ("num_heads", _i), ("head_dim", _i), ("scale", _f), ("q", _p), ("k", _p), ("v", _p),
+        ("out", _p), ("ld_out", _i64),
+    ]
+
+
 class PrefillRopeArgs(ctypes.Structure):
     _fields_ = [
         ("tokens", _i), ("num_heads", _i), ("head_dim", _i), ("pos0", _i), ("qkv", _p), ("rope_cos", _p),
@@ -172,6 +179,7 @@ SYMBOLS = {
     "mie_decode_head": ([ctypes.POINTER(StepDesc), _p], ctypes.c_int),
     "mie_step_scratch_bytes": ([ctypes.POINTER(StepDesc)], ctypes.c_int64),
     "mie_step_kernel_of": ([ctypes.POINTER(StepDesc)], ctypes.c_int),
+    "mie_prefill_attention": ([ctypes.POINTER(PrefillAttnArgs), _p], ctypes.c_int),
     "mie_gemm": ([ctypes.POINTER(GemmArgs), _p], ctypes.c_int),
     "mie_prefill_norm": ([ctypes.POINTER(PrefillNormArgs), _p], ctypes.c_int),
     "mie_prefill_rope_kv": ([ctypes.POINTER(PrefillRopeArgs), _p], ctypes.c_int),

@@ -23,6 +23,7 @@ STRUCTS = {
     "mie_lmhead_args": capi.LmHeadArgs,
     "mie_layer_desc": capi.LayerDesc,
     "mie_step_desc": capi.StepDesc,
+    "mie_prefill_attn_args": capi.PrefillAttnArgs,
 }
 
 

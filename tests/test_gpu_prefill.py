@@ -1,6 +1,12 @@
 """Prompt prefill on the sm_100a kernels (moe_engine/prefill.py: tcgen05 GEMMs,
-per-token norm / RoPE / routing / combine kernels, SDPA for the causal
-attention) against the CPU oracle and against the PyTorch module path.
+per-token norm / RoPE / routing / combine kernels, the causal attention kernel
+mie_prefill_attention, the whole prefill replayed from a CUDA graph) against
+the CPU oracle and against the PyTorch module path.
+
+* mie_prefill_attention alone against a plain fp32 causal attention on the
+  same bf16 q / k / v (head_dim 64, 96, 128; prompt lengths around the 64-token
+  tile edges): within 1e-2;
+* a second prefill of the same length (a graph replay) equals the first;
 
 * logits of the prompt positions against the oracle run on the same
   bf16-rounded weights with a bf16 K/V cache (relative error, Frobenius over
@@ -107,3 +113,50 @@ def test_gather_attention_keeps_module_path(model):
     p = prompt(16)
     cache = model.new_cache(attention_mode="gather")
     assert not model.prefill_supported(cache, p[None].to(DEV))
+
+
+@pytest.mark.parametrize("hd", [64, 96, 128])
+@pytest.mark.parametrize("T", [1, 7, 63, 64, 65, 200, 512])
+def test_prefill_attention_kernel_matches_fp32_attention(T, hd):
+    import ctypes
+    import math
+
+    from moe_engine import capi
+
+    H = 12 if hd == 64 else 8
+    g = torch.Generator().manual_seed(T * 7 + hd)
+    q, k, v = (torch.randn(H, T, hd, generator=g).to(torch.bfloat16) for _ in range(3))
+    want = oracle.attention(q.float(), k.float(), v.float(), causal=True)  # [H, T, hd] fp32
+    out = torch.full((T, H * hd), float("nan"), dtype=torch.bfloat16, device=DEV)
+    qd, kd, vd = q.to(DEV), k.to(DEV), v.to(DEV)
+    lib = capi.ensure_init(torch.device(DEV))
+    a = capi.PrefillAttnArgs(tokens=T, num_heads=H, head_dim=hd, scale=1.0 / math.sqrt(hd), q=qd.data_ptr(),
+                             k=kd.data_ptr(), v=vd.data_ptr(), out=out.data_ptr(), ld_out=out.stride(0))
+    capi.check(lib.mie_prefill_attention(ctypes.byref(a), capi.stream_handle(torch.device(DEV))),
+               "mie_prefill_attention")
+    got = out.float().cpu().view(T, H, hd).transpose(0, 1)
+    torch.testing.assert_close(got, want, atol=1e-2, rtol=1e-2)
+
+
+def test_prefill_graph_replay_equals_first_run(model):
+    """The first prefill of a length captures the graph (after one eager run);
+    later prefills of that length into other caches of the same pool replay
+    it, through a copy of each cache's block table."""
+    prompt = torch.randint(0, 50304, (1, 96), generator=torch.Generator().manual_seed(21))
+    alloc = model.new_block_allocator(num_blocks=32, block_size=16, attention_mode="direct")
+    free = list(alloc.free_blocks)
+    __import__("random").Random(4).shuffle(free)
+    alloc.free_blocks = free
+    outs, keep = [], []
+    for _ in range(3):
+        cache = alloc.new_cache()
+        with torch.no_grad():
+            lg = model(prompt.to(DEV), cache).float().cpu()
+        kp = alloc.k_pool[:, torch.tensor(cache.block_table)].clone().cpu()  # this cache's blocks, in order
+        outs.append((lg, kp))
+        keep.append(cache)  # distinct block tables for every prefill
+    runner = model.prefill_runner()
+    assert any(g is not None for _, g in runner._graphs.values())
+    assert keep[0].block_table != keep[1].block_table
+    for lg, kp in outs[1:]:
+        assert torch.equal(lg, outs[0][0]) and torch.equal(kp, outs[0][1])
