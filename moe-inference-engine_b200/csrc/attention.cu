@@ -5,7 +5,10 @@
 // SDPA decode at src/moe_engine/model.py:261-266.
 //
 // Here the context of every head is split over `splits` CTAs (grid = splits x
-// heads) so all SMs stream K/V.  A CTA walks its token range in stages of up
+// heads) so all SMs stream K/V.  Rows of whole 16-byte pieces run the
+// pipelined kernel further down (bulk copies of whole blocks into a ring of
+// stages, one online softmax per warp).  The kernel below keeps the rest (and
+// is the layout's fallback): a CTA walks its token range in stages of up
 // to 32 KB of K+V: every thread loads its 16-byte pieces of the stage with
 // plain read-only loads into registers (a block of one head is bs*hd
 // contiguous elements in the [nb, H, bs, hd] pool; the contiguous [H, S, hd]
@@ -276,42 +279,52 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const mie_attn_ar
 }
 
 // ---------------------------------------------------------------------------
-// The cp.async kernel (rows of whole 16-byte pieces; the kernel above keeps
-// the narrow rows).  256 threads; the split's physical block ids are read into
-// shared memory first (one round trip instead of one per piece), then every
-// thread issues 16-byte cp.async copies of the split's K and V rows into two
-// chunk buffers of up to 48 KB each -- a split of up to two chunks has its
-// whole range in flight at once -- and the chunks are reduced in order, a
-// chunk's buffer refilled with the chunk after next once it is read.  Chunks
-// holding only old tokens are issued before the programmatic-dependent wait.
+// The pipelined kernel (rows of whole 16-byte pieces; the kernel above keeps
+// the narrow rows).  256 threads = 8 warps.  The split's token range is cut
+// into stages of whole blocks (~16 KB of K + V each) held in a ring of up to
+// kFastStages slots.  The split's physical block ids are read into shared
+// memory first; then warp 0 issues one bulk copy per block for K and one for
+// V (a block's K, and its V, is one contiguous run), each stage counted in
+// bytes on the mbarrier of its slot, the whole ring in flight at once.  Every
+// warp runs its own online softmax (running max and normaliser, HD/32 output
+// dims per lane) over its share of each stage as soon as that stage lands --
+// no block barrier per stage -- and the eight warp states are merged once at
+// the end.  A slot is refilled by warp 0 once every warp arrived on its empty
+// barrier.  Stages holding only old tokens are issued before the
+// programmatic-dependent wait.
 // ---------------------------------------------------------------------------
 constexpr int kFastThreads = 256;
-constexpr uint32_t kFastChunkBytes = 48 * 1024;  // K + V of one chunk buffer
+constexpr int kFastWarps = kFastThreads / 32;
+constexpr int kFastStages = 8;                   // ring slots (at most)
+constexpr uint32_t kFastStageBytes = 16 * 1024;  // K + V of one stage (at least one block)
+constexpr uint32_t kFastRingBytes = 96 * 1024;   // two CTAs per SM
 
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+// two adjacent elements (4- or 8-byte aligned) as floats
+__device__ __forceinline__ float2 load2(const __nv_bfloat16* p) {
+  return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(p));
 }
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
+__device__ __forceinline__ float2 load2(const float* p) { return *reinterpret_cast<const float2*>(p); }
 
 template <typename KV, int HD>
 __global__ void __launch_bounds__(kFastThreads) attn_fast_kernel(const mie_attn_args a, AttnLayout L) {
   extern __shared__ __align__(128) uint8_t smem[];
-  constexpr int T = kFastThreads;
+  constexpr unsigned kAll = 0xffffffffu;
   constexpr int VPT = 16 / (int)sizeof(KV), VPH = HD / VPT;  // 16-byte pieces per row
-  constexpr int G = T / HD;                                   // PV token groups
+  // lanes per token in the score pass (VPH rounded up to a power of two),
+  // tokens per pass, output dims per lane
+  constexpr int LG = VPH <= 1 ? 1 : VPH <= 2 ? 2 : VPH <= 4 ? 4 : VPH <= 8 ? 8 : VPH <= 16 ? 16 : 32;
+  constexpr int TPP = 32 / LG;
+  constexpr int DPL = (HD + 31) / 32;
+  constexpr int P = 2;  // passes per iteration
+  constexpr uint32_t kRow = HD * sizeof(KV);
   const int h = blockIdx.y, s = blockIdx.x, S = gridDim.x, tid = threadIdx.x;
-  const int bs = a.block_size, chunk = L.chunk_tok;
+  const int warp = tid >> 5, lane = tid & 31;
+  const int bs = a.block_size, stok = L.chunk_tok, NS = L.nstage;
   int* blk_s = reinterpret_cast<int*>(smem + L.off_blk);
-  KV* kvb = reinterpret_cast<KV*>(smem + L.off_kv);  // [2 buffers][K | V][chunk][HD]
-  float* q_s = reinterpret_cast<float*>(smem + L.off_q);
-  float* sc = reinterpret_cast<float*>(smem + L.off_p);
-  float* pv = reinterpret_cast<float*>(smem + L.off_acc);
-  __shared__ float red[T / 32];
+  KV* ring = reinterpret_cast<KV*>(smem + L.off_kv);       // [NS][K | V][stok][HD]
+  float* pw = reinterpret_cast<float*>(smem + L.off_acc);  // [warps][HD + 2]: acc, m, l
   __shared__ int last_s;
+  __shared__ __align__(8) uint64_t full_s[kFastStages], empty_s[kFastStages];
 
   // context length (see the kernel above: the device position may be read
   // before the dependency wait; out-of-range values are clamped, reported later)
@@ -322,8 +335,15 @@ __global__ void __launch_bounds__(kFastThreads) attn_fast_kernel(const mie_attn_
   int b0, b1;
   split_range(nblk, s, S, &b0, &b1);
   const int tok0 = b0 * bs, tok1 = min(b1 * bs, ctx), ntok = max(0, tok1 - tok0);
-  const int nch = (ntok + chunk - 1) / chunk;
-  for (int i = tid; i < b1 - b0 && i < L.cap_blocks; i += T) {
+  const int nst = (ntok + stok - 1) / stok;
+  if (tid == 0) {
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(&full_s[i], 1u);
+      mbar_init(&empty_s[i], (uint32_t)kFastWarps);
+    }
+    fence_barrier_init();
+  }
+  for (int i = tid; i < b1 - b0 && i < L.cap_blocks; i += kFastThreads) {
     int p = b0 + i;  // contiguous cache: the identity block map
     if (a.block_table) {
       p = __ldg(a.block_table + b0 + i);
@@ -335,118 +355,211 @@ __global__ void __launch_bounds__(kFastThreads) attn_fast_kernel(const mie_attn_
     blk_s[i] = p;
   }
   __syncthreads();
-  auto issue = [&](int c) {  // chunk c -> buffer c & 1 (every thread; one commit group)
-    const int t0 = tok0 + c * chunk, n = min(chunk, tok1 - t0);
-    KV* kd = kvb + (size_t)(c & 1) * 2 * chunk * HD;
-    KV* vd = kd + (size_t)chunk * HD;
-    for (int j = tid; j < 2 * n * VPH; j += T) {
-      const int v = j >= n * VPH, jj = j - v * n * VPH, t = jj / VPH, pc = jj - t * VPH;
-      const int tok = t0 + t;
-      const int64_t blk = blk_s[min(tok / bs - b0, L.cap_blocks - 1)];
-      const KV* src = static_cast<const KV*>(v ? a.v : a.k) + blk * a.stride_block + (int64_t)h * a.stride_head +
-                      (int64_t)(tok % bs) * a.stride_tok + pc * VPT;
-      cp_async16((v ? vd : kd) + (size_t)t * HD + pc * VPT, src);
+  // Stage i -> slot i % NS (warp 0).  Lane 0 arms the slot's barrier with the
+  // stage's bytes, then one lane per block issues its K and V copies (16-byte
+  // aligned runs of whole rows: checked on the host).  Stages start on block
+  // boundaries (stok is a multiple of bs).
+  const int blk_per_stage = stok / bs;
+  auto issue = [&](int i) {
+    const int t0 = tok0 + i * stok, n = min(stok, tok1 - t0);
+    KV* kd = ring + (size_t)(i % NS) * 2 * stok * HD;
+    KV* vd = kd + (size_t)stok * HD;
+    const int nb = (n + bs - 1) / bs;
+    if (lane == 0) {
+      fence_proxy_async_smem();  // the slot's earlier reads (ordered by its empty barrier) before the copies
+      mbar_arrive_expect_tx(&full_s[i % NS], 2u * (uint32_t)n * kRow);
     }
-    cp_async_commit();
+    __syncwarp();
+#pragma unroll 1
+    for (int ib = lane; ib < nb; ib += 32) {
+      const int64_t blk = blk_s[min(i * blk_per_stage + ib, L.cap_blocks - 1)];
+      const uint32_t bytes = (uint32_t)min(bs, n - ib * bs) * kRow;
+      const int64_t base = blk * a.stride_block + (int64_t)h * a.stride_head;
+      bulk_g2s(kd + (size_t)ib * bs * HD, static_cast<const KV*>(a.k) + base, bytes, &full_s[i % NS]);
+      bulk_g2s(vd + (size_t)ib * bs * HD, static_cast<const KV*>(a.v) + base, bytes, &full_s[i % NS]);
+    }
   };
-  // the split's last chunk holds the newest token when the producer grid
-  // writes it: issued only after the wait
-  const int nch_pre = (a.new_token_last && b1 == nblk && nch > 0) ? nch - 1 : nch;
+  auto landed = [&](int i) { return mbar_wait(&full_s[i % NS], (uint32_t)((i / NS) & 1), a.status); };
+  // the split's last stage holds the newest token when the producer grid
+  // writes it: issued only after the wait.  `issued` is CTA-uniform until the
+  // stage loop, then kept by warp 0 alone.
+  const int nst_pre = (a.new_token_last && b1 == nblk && nst > 0) ? nst - 1 : nst;
   int issued = 0;
-  for (; issued < min(2, nch_pre); ++issued) issue(issued);
+  for (; issued < min(NS, nst_pre); ++issued)
+    if (warp == 0) issue(issued);
+  // every issued stage has landed before the CTA leaves (bounded waits)
+  auto drain = [&]() {
+    for (int i = max(0, issued - NS); i < issued; ++i) landed(i);
+  };
 
   pdl_wait();
   if (skip_requested(a.skip)) {
-    cp_async_wait<0>();  // nothing lands after the CTA left
+    drain();
     pdl_trigger();
     return;
   }
   pdl_trigger();
   if (bad_ctx && tid == 0 && s == 0) set_status(a.status, MIE_ERR_RANGE);
-  for (; issued < min(2, nch); ++issued) issue(issued);
-  for (int d = tid; d < HD; d += T) q_s[d] = load_any(a.q, a.q_dtype, (int64_t)h * HD + d);
+  for (; issued < min(NS, nst); ++issued)
+    if (warp == 0) issue(issued);
 
-  const float scale = a.scale;
-  const int g = tid / HD, dcol = tid % HD;
-  float acc = 0.f, m_run = -INFINITY, l_run = 0.f;
-  for (int c = 0; c < nch; ++c) {
-    if (issued - c - 1 >= 1)
-      cp_async_wait<1>();
-    else
-      cp_async_wait<0>();
-    __syncthreads();  // chunk c visible to every thread (and q_s)
-    const int n = min(chunk, tok1 - (tok0 + c * chunk));
-    const KV* kst = kvb + (size_t)(c & 1) * 2 * chunk * HD;
-    const KV* vst = kst + (size_t)chunk * HD;
-    float mloc = -INFINITY;
-    for (int t = tid; t < n; t += T) {
-      const uint4* kr = reinterpret_cast<const uint4*>(kst + (size_t)t * HD);
-      float dot = 0.f;
+  // this lane's piece of q (score pass: LG lanes per token, lane pc holds
+  // elements [pc * VPT, pc * VPT + VPT) of the row)
+  const int pc = lane % LG, grp = lane / LG;
+  const bool has_piece = pc < VPH;
+  float qr[VPT];
 #pragma unroll
-      for (int j = 0; j < VPH; ++j) {
-        const int v = (j + t) % VPH;  // rotate the start piece: spreads banks
-        dot = dot_vec(kr[v], q_s + v * VPT, dot, (const KV*)nullptr);
+  for (int j = 0; j < VPT; ++j) qr[j] = has_piece ? load_any(a.q, a.q_dtype, (int64_t)h * HD + pc * VPT + j) : 0.f;
+  const float scale = a.scale;
+  float m = -INFINITY, l = 0.f, acc[DPL];
+#pragma unroll
+  for (int d = 0; d < DPL; ++d) acc[d] = 0.f;
+  bool lost = false;  // a wait of this warp ran out (status set)
+#pragma unroll 1
+  for (int i = 0; i < nst; ++i) {
+    if (!__all_sync(kAll, landed(i))) {
+      lost = true;
+      break;
+    }
+    const int n = min(stok, tok1 - (tok0 + i * stok));
+    const KV* kst = ring + (size_t)(i % NS) * 2 * stok * HD;
+    const KV* vst = kst + (size_t)stok * HD;
+    // this warp's tokens [wa, wb) of the stage, TPP per pass
+    const int wa = n * warp / kFastWarps, wb = n * (warp + 1) / kFastWarps;
+    // P passes of TPP tokens per iteration: their dot products, shuffle
+    // reductions and exps are independent chains, one max / sum reduction
+    // and one rescale for all of them
+#pragma unroll 1
+    for (int t = wa; t < wb; t += P * TPP) {
+      float sv[P];
+#pragma unroll
+      for (int u = 0; u < P; ++u) {
+        const int tt = t + u * TPP + grp;
+        sv[u] = (tt < wb && has_piece)
+                    ? dot_vec(reinterpret_cast<const uint4*>(kst + (size_t)tt * HD)[pc], qr, 0.f, (const KV*)nullptr)
+                    : 0.f;
       }
-      const float scv = dot * scale;
-      sc[t] = scv;
-      mloc = fmaxf(mloc, scv);
+#pragma unroll
+      for (int o = 1; o < LG; o <<= 1)
+#pragma unroll
+        for (int u = 0; u < P; ++u) sv[u] += __shfl_xor_sync(kAll, sv[u], o);
+      float mx = -INFINITY;
+#pragma unroll
+      for (int u = 0; u < P; ++u) {
+        sv[u] = (t + u * TPP + grp < wb) ? sv[u] * scale : -INFINITY;
+        mx = fmaxf(mx, sv[u]);
+      }
+#pragma unroll
+      for (int o = LG; o < 32; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(kAll, mx, o));
+      const float mn = fmaxf(m, mx);  // finite: token t is live
+      const float alpha = expf(m - mn);
+      float pr[P], ps = 0.f;
+#pragma unroll
+      for (int u = 0; u < P; ++u) {
+        pr[u] = sv[u] == -INFINITY ? 0.f : expf(sv[u] - mn);
+        ps += pr[u];
+      }
+#pragma unroll
+      for (int o = LG; o < 32; o <<= 1) ps += __shfl_xor_sync(kAll, ps, o);
+      l = fmaf(l, alpha, ps);
+      m = mn;
+      float ac[2][DPL];
+#pragma unroll
+      for (int d = 0; d < DPL; ++d) {
+        ac[0][d] = acc[d] * alpha;
+        ac[1][d] = 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < P; ++u) {
+#pragma unroll
+        for (int k = 0; k < TPP; ++k) {
+          const float pk = __shfl_sync(kAll, pr[u], k * LG);
+          const int tk = t + u * TPP + k;
+          float* av = ac[(u * TPP + k) & 1];
+          if (tk < wb) {
+            const KV* vr = vst + (size_t)tk * HD;
+            if constexpr (DPL == 2 && HD == 64) {
+              const float2 v2 = load2(vr + 2 * lane);
+              av[0] = fmaf(pk, v2.x, av[0]);
+              av[1] = fmaf(pk, v2.y, av[1]);
+            } else {
+#pragma unroll
+              for (int d = 0; d < DPL; ++d) {
+                const int dd = lane * DPL + d;
+                if (dd < HD) av[d] = fmaf(pk, Elem<KV>::to_f(vr[dd]), av[d]);
+              }
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int d = 0; d < DPL; ++d) acc[d] = ac[0][d] + ac[1][d];
     }
-    const float m_new = fmaxf(m_run, block_max(mloc, red));
-    const float alpha = (m_run == -INFINITY) ? 0.f : expf(m_run - m_new);
-    float lsum = 0.f;
-    for (int t = tid; t < n; t += T) {
-      const float p = expf(sc[t] - m_new);
-      sc[t] = p;
-      lsum += p;
-    }
-    l_run = l_run * alpha + block_sum(lsum, red);  // ends with sc visible to all
-    m_run = m_new;
-    float a0 = 0.f, a1 = 0.f;
-    int t = g;
-    for (; t + G < n; t += 2 * G) {
-      a0 = fmaf(sc[t], Elem<KV>::to_f(vst[(size_t)t * HD + dcol]), a0);
-      a1 = fmaf(sc[t + G], Elem<KV>::to_f(vst[(size_t)(t + G) * HD + dcol]), a1);
-    }
-    if (t < n) a0 = fmaf(sc[t], Elem<KV>::to_f(vst[(size_t)t * HD + dcol]), a0);
-    acc = fmaf(acc, alpha, a0 + a1);
-    __syncthreads();  // buffer c & 1 and the scores are no longer read
-    if (issued < nch) {
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty_s[i % NS]);  // this warp no longer reads the slot
+    if (warp == 0 && issued < nst) {
+      // refill slot i % NS with stage issued == i + NS once every warp left it
+      if (!__all_sync(kAll, mbar_wait(&empty_s[i % NS], (uint32_t)((i / NS) & 1), a.status))) {
+        lost = true;
+        break;
+      }
       issue(issued);
       ++issued;
     }
   }
 
-  // combine the PV token groups
-  pv[g * HD + dcol] = acc;
-  __syncthreads();
+  // ---- merge the warps: (acc, m, l) of every warp -> the CTA's partial ----
+#pragma unroll
+  for (int d = 0; d < DPL; ++d) {
+    const int dd = lane * DPL + d;
+    if (dd < HD) pw[warp * (HD + 2) + dd] = acc[d];
+  }
+  if (lane == 0) {
+    pw[warp * (HD + 2) + HD] = m;
+    pw[warp * (HD + 2) + HD + 1] = l;
+  }
+  if (__syncthreads_or(lost) && warp == 0) drain();
+  float M = -INFINITY;
+#pragma unroll
+  for (int w = 0; w < kFastWarps; ++w) M = fmaxf(M, pw[w * (HD + 2) + HD]);
+  float lsum = 0.f, o = 0.f;
+#pragma unroll
+  for (int w = 0; w < kFastWarps; ++w) {
+    const float mw = pw[w * (HD + 2) + HD];
+    if (mw != -INFINITY) {
+      const float e = expf(mw - M);
+      lsum = fmaf(e, pw[w * (HD + 2) + HD + 1], lsum);
+      if (tid < HD) o = fmaf(e, pw[w * (HD + 2) + tid], o);
+    }
+  }
   const bool direct_out = (S == 1 && !a.defer_merge);
   float* part = a.partials + ((size_t)h * a.max_splits + s) * (HD + 2);
-  for (int d = tid; d < HD; d += T) {
-    float v = 0.f;
-#pragma unroll
-    for (int gg = 0; gg < G; ++gg) v += pv[gg * HD + d];
+  if (tid < HD) {
     if (direct_out)
-      store_any(a.out, a.out_dtype, (int64_t)h * HD + d, ntok > 0 ? v / l_run : 0.f);
+      store_any(a.out, a.out_dtype, (int64_t)h * HD + tid, lsum > 0.f ? o / lsum : 0.f);
     else
-      part[2 + d] = v;
+      part[2 + tid] = o;
   }
   if (direct_out) return;
   if (tid == 0) {
-    part[0] = m_run;
-    part[1] = l_run;
+    part[0] = M;
+    part[1] = lsum;
   }
   if (a.defer_merge) return;
-  __threadfence();
+  // arrival: the block barrier orders every thread's partial stores before
+  // thread 0's release (gpu scope) on the head's counter; the last arrival's
+  // acquire, then the barrier, orders the other splits' partials before this
+  // CTA's loads
   __syncthreads();
   if (tid == 0) last_s = (atom_add_acq_rel_gpu(a.counters + h, 1u) == (uint32_t)(S - 1));
   __syncthreads();
   if (!last_s) return;
-  __threadfence();
   // log-sum-exp merge of the S partials of this head, staged in shared memory
-  // (the chunk buffers are free) with every thread's loads in flight together
+  // (the ring is free) with every thread's loads in flight together
   const float* hp = a.partials + (size_t)h * a.max_splits * (HD + 2);
-  float* ps = reinterpret_cast<float*>(kvb);  // [S][HD + 2]
+  float* ps = reinterpret_cast<float*>(ring);  // [S][HD + 2]
   const int np = S * (HD + 2);
+  constexpr int T = kFastThreads;
   for (int i0 = tid; i0 < np; i0 += 8 * T) {
     float v[8];
 #pragma unroll
@@ -461,25 +574,44 @@ __global__ void __launch_bounds__(kFastThreads) attn_fast_kernel(const mie_attn_
     }
   }
   __syncthreads();
-  float M = -INFINITY;
-  for (int j = 0; j < S; ++j) M = fmaxf(M, ps[j * (HD + 2)]);
-  float Lsum = 0.f;
-  for (int j = 0; j < S; ++j) {
-    const float mj = ps[j * (HD + 2)];
-    if (mj != -INFINITY) Lsum += ps[j * (HD + 2) + 1] * expf(mj - M);
-  }
-  for (int d = tid; d < HD; d += T) {
-    float o = 0.f;
-    for (int j = 0; j < S; ++j) {
+  // per-split weights e^(m_j - M) and the normaliser once (warp 0), then
+  // Q subsets of the splits per output dim, summed at the end
+  float* wts = ps + np;  // [S]
+  float* osum = wts + S;  // [Q][HD]
+  __shared__ float lsum_s;
+  if (warp == 0) {
+    float mloc = -INFINITY;
+    for (int j = lane; j < S; j += 32) mloc = fmaxf(mloc, ps[j * (HD + 2)]);
+    const float Mh = warp_max(mloc);
+    float lw = 0.f;
+    for (int j = lane; j < S; j += 32) {
       const float mj = ps[j * (HD + 2)];
-      if (mj != -INFINITY) o += ps[j * (HD + 2) + 2 + d] * expf(mj - M);
+      const float w = mj == -INFINITY ? 0.f : expf(mj - Mh);
+      wts[j] = w;
+      lw = fmaf(w, ps[j * (HD + 2) + 1], lw);
     }
-    store_any(a.out, a.out_dtype, (int64_t)h * HD + d, o / Lsum);
+    lw = warp_sum(lw);
+    if (lane == 0) lsum_s = lw;
+  }
+  __syncthreads();
+  constexpr int Q = T / HD;
+  if (tid < Q * HD) {
+    const int d = tid % HD, qq = tid / HD;
+    float o2 = 0.f;
+    for (int j = qq; j < S; j += Q) o2 = fmaf(wts[j], ps[j * (HD + 2) + 2 + d], o2);
+    osum[qq * HD + d] = o2;
+  }
+  __syncthreads();
+  for (int d = tid; d < HD; d += T) {
+    float o2 = 0.f;
+#pragma unroll
+    for (int qq = 0; qq < Q; ++qq) o2 += osum[qq * HD + d];
+    store_any(a.out, a.out_dtype, (int64_t)h * HD + d, o2 / lsum_s);
   }
   if (tid == 0) a.counters[h] = 0u;  // ready for the next launch
 }
 
-// The cp.async kernel exists for rows of whole 16-byte pieces only.
+// The pipelined kernel exists for rows of whole 16-byte pieces only.
 template <typename KV, int HD>
 void* fast_kernel_or_null() {
   if constexpr ((HD * sizeof(KV)) % 16 == 0)
@@ -544,26 +676,28 @@ AttnLayout attn_layout(const mie_attn_args& a) {
   L.smem = (uint32_t)((off + 127) & ~size_t(127));
   // One block of K+V must fit the per-thread register staging (16-byte rows).
   if ((a.head_dim * esz) % 16 == 0 && per_tok * st > budget) L.smem = 0xffffffffu;  // -> unsupported
-  // 16-byte rows run the cp.async kernel: two chunk buffers of up to 48 KB of
-  // K + V each (whole blocks), the split's block ids, q, scores, PV partials
+  // 16-byte rows run the pipelined kernel: a ring of stages of whole blocks
+  // (~16 KB of K + V each, up to 96 KB), the split's block ids, per-warp
+  // partial states
   if ((a.head_dim * esz) % 16 == 0 && a.splits > 0) {
     AttnLayout F{};
     F.fast = 1;
-    int ct = (int)(kFastChunkBytes / (uint32_t)per_tok) / a.block_size * a.block_size;
+    int ct = (int)(kFastStageBytes / (uint32_t)per_tok) / a.block_size * a.block_size;
     if (ct < a.block_size) ct = a.block_size;
     F.chunk_tok = ct;
+    int ns = (int)(kFastRingBytes / ((uint32_t)per_tok * (uint32_t)ct));
+    F.nstage = ns < 1 ? 1 : (ns > kFastStages ? kFastStages : ns);
     const int max_blk = (a.max_ctx + a.block_size - 1) / a.block_size;
     F.cap_blocks = (max_blk + a.splits - 1) / a.splits;
     if (F.cap_blocks < 1) F.cap_blocks = 1;
     off = 0;
-    F.off_kv = take((size_t)2 * per_tok * ct);
+    F.off_kv = take((size_t)F.nstage * per_tok * ct);
     F.off_blk = take(sizeof(int) * (size_t)F.cap_blocks);
-    F.off_q = take(sizeof(float) * a.head_dim);
-    F.off_p = take(sizeof(float) * ct);
-    F.off_acc = take(sizeof(float) * kFastThreads);
+    F.off_acc = take(sizeof(float) * kFastWarps * (size_t)(a.head_dim + 2));
     F.smem = (uint32_t)((off + 127) & ~size_t(127));
-    // the merge stages every split's partial in the chunk buffers
-    if ((size_t)a.splits * (a.head_dim + 2) * 4 <= (size_t)2 * per_tok * ct && F.smem <= (uint32_t)kMaxDynSmem)
+    // the merge stages every split's partial, its weight and the dim sums in the ring
+    if (((size_t)a.splits * (a.head_dim + 3) + kFastThreads) * 4 <= (size_t)F.nstage * per_tok * ct &&
+        F.smem <= (uint32_t)kMaxDynSmem)
       return F;
   }
   return L;

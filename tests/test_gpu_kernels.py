@@ -288,3 +288,43 @@ def test_attention_reuses_workspace_across_calls():
     for _ in range(50):
         got = paged_attention.decode(qd, cache, 0, 700)
     torch.testing.assert_close(got.view(H, hd).cpu(), want, atol=2e-5, rtol=1e-5)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("splits", [1, 3, 7])
+def test_attention_long_splits_refill_the_stage_ring(dtype, splits):
+    """Few splits over a long context: every split's range is many stages
+    longer than the kernel's ring of stage slots, so slots are refilled while
+    the other warps still read; the merge of 1 (direct output), 3 and 7
+    partials.  C entry point, 12 x 64 heads, block 16, ctx 2000 (a partial
+    last block)."""
+    import ctypes
+    import math
+
+    from moe_engine import capi
+
+    H, hd, bs, ctx = 12, 64, 16, 2000
+    cache, k, v, q = filled_paged_cache(H, hd, bs, ctx, 2048, 21, True, dtype)
+    lib = capi.ensure_init(torch.device(DEV))
+    kp, vp = cache.allocator.k_pool[0], cache.allocator.v_pool[0]
+    qd = q.to(DEV, dtype)[0, :, 0].contiguous()
+    out = torch.full((H, hd), float("nan"), dtype=dtype, device=DEV)
+    partials = torch.zeros(H * paged_attention.MAX_SPLITS * (hd + 2), dtype=torch.float32, device=DEV)
+    counters = torch.zeros(H, dtype=torch.int32, device=DEV)
+    a = capi.AttnArgs()
+    a.kv_dtype = a.q_dtype = a.out_dtype = capi.dtype_code(dtype)
+    a.num_heads, a.head_dim = H, hd
+    a.q, a.k, a.v = qd.data_ptr(), kp.data_ptr(), vp.data_ptr()
+    a.block_table = cache.block_table_device.data_ptr()
+    a.num_blocks, a.block_size = kp.shape[0], bs
+    a.stride_block, a.stride_head, a.stride_tok = H * bs * hd, bs * hd, hd
+    a.ctx_len, a.max_ctx = ctx, len(cache.block_table) * bs
+    a.scale = 1.0 / math.sqrt(hd)
+    a.out, a.partials, a.counters = out.data_ptr(), partials.data_ptr(), counters.data_ptr()
+    a.splits, a.max_splits = splits, paged_attention.MAX_SPLITS
+    for _ in range(3):  # the counters reset themselves between calls
+        capi.check(lib.mie_attn_decode(ctypes.byref(a), capi.stream_handle(torch.device(DEV))), "mie_attn_decode")
+    torch.cuda.synchronize()
+    want = oracle.attention_decode(q[0, :, 0].to(dtype).float(), k[0].to(dtype).float(), v[0].to(dtype).float())
+    tol = 1e-2 if dtype == torch.bfloat16 else 2e-5
+    torch.testing.assert_close(out.float().cpu(), want, atol=tol, rtol=tol if dtype == torch.bfloat16 else 1e-5)
