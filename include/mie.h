@@ -449,7 +449,10 @@ typedef struct mie_prefill_combine_args {
 /* Causal self-attention of the prompt prefill (replaces the reference's
  * F.scaled_dot_product_attention(q, k, v, is_causal=True) of the prefill fast
  * path, src/moe_engine/model.py:252-256): o[t, h hd + d] = sum_{s <= t}
- * softmax_s(scale q_h[t] . k_h[s]) v_h[s][d], fp32 accumulation. */
+ * softmax_s(scale q_h[t] . k_h[s]) v_h[s][d], fp32 accumulation.  head_dim
+ * 64 with 16-byte aligned q / k / v / out and ld_out a multiple of 8 runs on
+ * the tensor cores (the probabilities rounded to bf16 for the P V product, as
+ * flash attention does); other shapes on CUDA cores in fp32. */
 typedef struct mie_prefill_attn_args {
   int tokens;
   int num_heads;
@@ -460,6 +463,8 @@ typedef struct mie_prefill_attn_args {
   const void* v;
   void* out;                 /* bf16 [tokens, ld_out] */
   int64_t ld_out;            /* >= num_heads * head_dim */
+  int32_t* status;           /* optional: MIE_ERR_TIMEOUT when a bounded wait of the
+                                tensor-core kernel ran out (that launch wrote no rows) */
 } mie_prefill_attn_args;
 
 /* Library management */

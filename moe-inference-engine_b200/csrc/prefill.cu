@@ -17,6 +17,7 @@
 //   prefill_combine   x[t] += w0 y[row0] + w1 y[row1] in that order (model.py:453-461)
 #include "common.cuh"
 #include "kernels.h"
+#include "tcgen05.cuh"
 
 namespace mie {
 namespace {
@@ -420,6 +421,212 @@ __global__ void __launch_bounds__(kAtThreads) prefill_attention_kernel(const mie
   }
 }
 
+// ---------------------------------------------------------------------------
+// Causal attention of the prompt on the tensor cores (head_dim 64, bf16): one
+// CTA of 128 threads per (128-query tile, head); thread r owns query row r,
+// which is TMEM lane r.  For each 64-key tile up to the diagonal:
+//   S = Q K^T      tcgen05.mma (M 128, N 64, K 64) into TMEM columns [0, 64);
+//   softmax        thread r reads its 64 scores (tcgen05.ld), masks the keys
+//                  past its query, updates its running max and sum and writes
+//                  its row of P (bf16) to shared memory;
+//   O_t = P V      tcgen05.mma (M 128, N 64, K = the tile's 64 keys) into TMEM
+//                  columns [64, 128), read back and added to the register O
+//                  after the rescale of the running max.
+// Operands are K-major tiles in the 128-byte-swizzled layout, written by the
+// threads: Q [128 x 64] once, K [64 keys x 64] and V transposed [64 dims x 64
+// keys] per tile, double buffered (the next tile's rows are loaded into
+// registers while the current tile is reduced).  P is rounded to bf16 for the
+// second product, as in flash attention; scores, sums and O stay fp32.
+// ---------------------------------------------------------------------------
+constexpr int kTcQ = 128, kTcK = 64, kTcThreads = 128, kTcHD = 64;
+constexpr uint32_t kTcQBytes = kTcQ * 128u;  // 16 KB: 128 rows of 64 bf16
+constexpr uint32_t kTcKBytes = kTcK * 128u;  // 8 KB
+constexpr uint32_t kTcVBytes = kTcHD * 128u;  // 8 KB: 64 dims x 64 keys
+constexpr uint32_t kTcPBytes = kTcQ * 128u;  // 16 KB
+constexpr uint32_t kTcSmem = kTcQBytes + 2 * kTcKBytes + 2 * kTcVBytes + kTcPBytes + 1024u;  // + alignment
+constexpr uint32_t kTcCols = 128;  // TMEM: S [0, 64), O_t [64, 128)
+
+// Byte offset of 16-byte chunk c of row r in a K-major 128-byte-swizzled tile
+// (rows of 128 bytes; chunk c of row r sits at chunk c ^ (r mod 8)).
+__device__ __forceinline__ uint32_t sw128_off(int r, int c) {
+  return (uint32_t)r * 128u + ((uint32_t)(c ^ (r & 7)) << 4);
+}
+
+__global__ void __launch_bounds__(kTcThreads, 1) prefill_attention_tc_kernel(const mie_prefill_attn_args a) {
+  extern __shared__ uint8_t tc_raw[];
+  uint8_t* sq = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tc_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* skv = sq + kTcQBytes;  // [2][K | V^T]
+  uint8_t* sp = skv + 2 * (kTcKBytes + kTcVBytes);
+  __shared__ __align__(8) uint64_t bar_s, bar_o;
+  __shared__ uint32_t tmem_s;
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int h = blockIdx.y, q0 = blockIdx.x * kTcQ, T = a.tokens;
+  const __nv_bfloat16* qh = static_cast<const __nv_bfloat16*>(a.q) + (int64_t)h * T * kTcHD;
+  const __nv_bfloat16* kh = static_cast<const __nv_bfloat16*>(a.k) + (int64_t)h * T * kTcHD;
+  const __nv_bfloat16* vh = static_cast<const __nv_bfloat16*>(a.v) + (int64_t)h * T * kTcHD;
+  const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
+  if (tid == 0) {
+    mbar_init(&bar_s, 1u);
+    mbar_init(&bar_o, 1u);
+    fence_barrier_init();
+  }
+  if (warp == 0) tmem_alloc(&tmem_s, kTcCols);
+  // Q tile (rows past T are zero)
+#pragma unroll
+  for (int u = 0; u < kTcQ * 8 / kTcThreads; ++u) {
+    const int i = tid + u * kTcThreads, r = i >> 3, c = i & 7;
+    const uint4 v = q0 + r < T ? __ldg(reinterpret_cast<const uint4*>(qh + (int64_t)(q0 + r) * kTcHD) + c) : zero;
+    *reinterpret_cast<uint4*>(sq + sw128_off(r, c)) = v;
+  }
+  // K rows: chunk (key i >> 3, piece i & 7), four per thread; V rows: thread
+  // t holds dims [32 (t >> 6), + 32) of key t & 63 (the transposed store of a
+  // warp then writes 32 consecutive keys of one row: no bank conflict)
+  uint4 kr[4], vr[4];
+  const int vkey = tid & 63, vd0 = (tid >> 6) * 32;
+  auto load_kv = [&](int k0) {
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int i = tid + u * kTcThreads, r = i >> 3, c = i & 7;
+      kr[u] = k0 + r < T ? __ldg(reinterpret_cast<const uint4*>(kh + (int64_t)(k0 + r) * kTcHD) + c) : zero;
+      vr[u] = k0 + vkey < T
+                  ? __ldg(reinterpret_cast<const uint4*>(vh + (int64_t)(k0 + vkey) * kTcHD + vd0) + u)
+                  : zero;
+    }
+  };
+  auto store_kv = [&](int buf) {
+    uint8_t* sk = skv + (uint32_t)buf * (kTcKBytes + kTcVBytes);
+    uint8_t* sv = sk + kTcKBytes;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int i = tid + u * kTcThreads, r = i >> 3, c = i & 7;
+      *reinterpret_cast<uint4*>(sk + sw128_off(r, c)) = kr[u];
+      const uint32_t w[4] = {vr[u].x, vr[u].y, vr[u].z, vr[u].w};
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int d = vd0 + 8 * u + e;  // row of V^T
+        const uint16_t bits = (uint16_t)(e & 1 ? w[e >> 1] >> 16 : w[e >> 1] & 0xffffu);
+        *reinterpret_cast<uint16_t*>(sv + sw128_off(d, vkey >> 3) + (vkey & 7) * 2) = bits;
+      }
+    }
+  };
+  const int qi = q0 + tid;  // this thread's query
+  const int klast = min(q0 + kTcQ, T) - 1;  // the tile's last query sees keys up to klast
+  const int nkt = klast / kTcK + 1;
+  load_kv(0);
+  store_kv(0);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_s;
+  const uint32_t tlane = tmem + ((uint32_t)(warp * 32) << 16);
+  constexpr uint32_t idesc = idesc_bf16(kTcK, kTcQ);  // both products: M 128, N 64
+  const float scale = a.scale;
+  float o[kTcHD], m = -INFINITY, l = 0.f;
+#pragma unroll
+  for (int d = 0; d < kTcHD; ++d) o[d] = 0.f;
+  // `ok` (every wait succeeded) is made CTA-uniform at each block barrier, so
+  // every thread leaves the loop at the same barrier
+  bool ok = true;
+#pragma unroll 1
+  for (int j = 0; j < nkt; ++j) {
+    const int k0 = j * kTcK, buf = j & 1;
+    const uint8_t* sk = skv + (uint32_t)buf * (kTcKBytes + kTcVBytes);
+    const uint8_t* sv = sk + kTcKBytes;
+    // the tile's K / V^T (and Q) stores by every thread, then the MMAs
+    fence_proxy_async_smem();
+    tc_fence_before();
+    ok = __syncthreads_and(ok) != 0;
+    tc_fence_after();
+    if (!ok) break;
+    if (tid == 0) {
+#pragma unroll
+      for (int kk = 0; kk < kTcHD / 16; ++kk)
+        tc_mma(tmem, sw128_desc(sq, 32u * kk), sw128_desc(sk, 32u * kk), idesc, kk ? 1u : 0u);
+      tc_commit(&bar_s);
+    }
+    if (j + 1 < nkt) load_kv(k0 + kTcK);  // the next tile's rows in flight during this one
+    ok = mbar_wait(&bar_s, (uint32_t)(j & 1), a.status);
+    tc_fence_after();
+    float s[kTcK];
+    tmem_ld32(tlane, s);
+    tmem_ld32(tlane + 32, s + 32);
+    // causal mask, online softmax of this thread's row, P row (bf16) to shared memory
+    float mx = -INFINITY;
+#pragma unroll
+    for (int c = 0; c < kTcK; ++c) {
+      s[c] = (k0 + c <= qi && k0 + c < T) ? s[c] * scale : -INFINITY;
+      mx = fmaxf(mx, s[c]);
+    }
+    const float mn = fmaxf(m, mx);
+    const float alpha = m == -INFINITY ? 0.f : expf(m - mn);
+    float rs = 0.f;
+#pragma unroll
+    for (int c = 0; c < kTcK; c += 8) {
+      uint32_t w[4];
+#pragma unroll
+      for (int e = 0; e < 8; e += 2) {
+        const float p0 = mn == -INFINITY ? 0.f : expf(s[c + e] - mn);
+        const float p1 = mn == -INFINITY ? 0.f : expf(s[c + e + 1] - mn);
+        rs += p0 + p1;
+        const __nv_bfloat162 pb = __floats2bfloat162_rn(p0, p1);
+        w[e >> 1] = *reinterpret_cast<const uint32_t*>(&pb);
+      }
+      *reinterpret_cast<uint4*>(sp + sw128_off(tid, c >> 3)) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+    l = fmaf(l, alpha, rs);
+    m = mn;
+    if (j + 1 < nkt) store_kv(buf ^ 1);  // the other buffer: its MMAs completed last iteration
+    fence_proxy_async_smem();
+    tc_fence_before();
+    ok = __syncthreads_and(ok) != 0;
+    tc_fence_after();
+    if (!ok) break;
+    if (tid == 0) {
+#pragma unroll
+      for (int kk = 0; kk < kTcK / 16; ++kk)
+        tc_mma(tmem + kTcK, sw128_desc(sp, 32u * kk), sw128_desc(sv, 32u * kk), idesc, kk ? 1u : 0u);
+      tc_commit(&bar_o);
+    }
+    ok = mbar_wait(&bar_o, (uint32_t)(j & 1), a.status);
+    tc_fence_after();
+    float pv[kTcHD];
+    tmem_ld32(tlane + kTcK, pv);
+    tmem_ld32(tlane + kTcK + 32, pv + 32);
+#pragma unroll
+    for (int d = 0; d < kTcHD; ++d) o[d] = fmaf(o[d], alpha, pv[d]);
+  }
+  if (ok && qi < T) {
+    const float inv = 1.0f / l;
+    __nv_bfloat16* out = static_cast<__nv_bfloat16*>(a.out) + (int64_t)qi * a.ld_out + (int64_t)h * kTcHD;
+#pragma unroll
+    for (int d = 0; d < kTcHD; d += 8) {
+      uint32_t w[4];
+#pragma unroll
+      for (int e = 0; e < 8; e += 2) {
+        const __nv_bfloat162 ob = __floats2bfloat162_rn(o[d + e] * inv, o[d + e + 1] * inv);
+        w[e >> 1] = *reinterpret_cast<const uint32_t*>(&ob);
+      }
+      *reinterpret_cast<uint4*>(out + d) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_free(tmem, kTcCols);
+  }
+}
+
+int prefill_attention_tc_launch(const mie_prefill_attn_args& a, cudaStream_t st) {
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(prefill_attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmem);
+    attr = true;
+  }
+  return launch(prefill_attention_tc_kernel, dim3((unsigned)((a.tokens + kTcQ - 1) / kTcQ), (unsigned)a.num_heads),
+                dim3(kTcThreads), kTcSmem, st, false, a);
+}
+
 template <int HD>
 int prefill_attention_launch(const mie_prefill_attn_args& a, cudaStream_t st) {
   const uint32_t smem = (uint32_t)sizeof(float) * (2 * HD * kAtQ + kAtK * HD + kAtK * kAtQ);
@@ -437,6 +644,11 @@ int prefill_attention_launch(const mie_prefill_attn_args& a, cudaStream_t st) {
 int prefill_attention(const mie_prefill_attn_args& a, cudaStream_t st) {
   if (a.tokens <= 0 || a.num_heads <= 0 || !a.q || !a.k || !a.v || !a.out || a.ld_out < (int64_t)a.num_heads * a.head_dim)
     return MIE_ERR_INVALID;
+  // head_dim 64 with 16-byte aligned rows: the tensor-core kernel
+  const bool rows16 = ((reinterpret_cast<uintptr_t>(a.q) | reinterpret_cast<uintptr_t>(a.k) |
+                        reinterpret_cast<uintptr_t>(a.v) | reinterpret_cast<uintptr_t>(a.out)) % 16 == 0) &&
+                      a.ld_out % 8 == 0;
+  if (a.head_dim == kTcHD && rows16) return prefill_attention_tc_launch(a, st);
   switch (a.head_dim) {
     case 64: return prefill_attention_launch<64>(a, st);
     case 96: return prefill_attention_launch<96>(a, st);

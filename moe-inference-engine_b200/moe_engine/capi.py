@@ -131,7 +131,7 @@ class PrefillNormArgs(ctypes.Structure):
 class PrefillAttnArgs(ctypes.Structure):
     _fields_ = [
         ("tokens", _i), ("num_heads", _i), ("head_dim", _i), ("scale", _f), ("q", _p), ("k", _p), ("v", _p),
-        ("out", _p), ("ld_out", _i64),
+        ("out", _p), ("ld_out", _i64), ("status", _p),
     ]
 
 

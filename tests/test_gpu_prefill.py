@@ -115,9 +115,12 @@ def test_gather_attention_keeps_module_path(model):
     assert not model.prefill_supported(cache, p[None].to(DEV))
 
 
-@pytest.mark.parametrize("hd", [64, 96, 128])
-@pytest.mark.parametrize("T", [1, 7, 63, 64, 65, 200, 512])
-def test_prefill_attention_kernel_matches_fp32_attention(T, hd):
+@pytest.mark.parametrize("hd,pad", [(64, 0), (64, 4), (96, 0), (128, 0)])
+@pytest.mark.parametrize("T", [1, 7, 63, 64, 65, 127, 128, 129, 200, 512, 1000])
+def test_prefill_attention_kernel_matches_fp32_attention(T, hd, pad):
+    """hd 64 runs the tensor-core kernel (128-query tiles, 64-key tiles); an
+    output row stride that is not a multiple of 8 (pad 4) and hd 96 / 128 run
+    the CUDA-core kernel."""
     import ctypes
     import math
 
@@ -127,14 +130,17 @@ def test_prefill_attention_kernel_matches_fp32_attention(T, hd):
     g = torch.Generator().manual_seed(T * 7 + hd)
     q, k, v = (torch.randn(H, T, hd, generator=g).to(torch.bfloat16) for _ in range(3))
     want = oracle.attention(q.float(), k.float(), v.float(), causal=True)  # [H, T, hd] fp32
-    out = torch.full((T, H * hd), float("nan"), dtype=torch.bfloat16, device=DEV)
+    out = torch.full((T, H * hd + pad), float("nan"), dtype=torch.bfloat16, device=DEV)[:, :H * hd]
     qd, kd, vd = q.to(DEV), k.to(DEV), v.to(DEV)
     lib = capi.ensure_init(torch.device(DEV))
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
     a = capi.PrefillAttnArgs(tokens=T, num_heads=H, head_dim=hd, scale=1.0 / math.sqrt(hd), q=qd.data_ptr(),
-                             k=kd.data_ptr(), v=vd.data_ptr(), out=out.data_ptr(), ld_out=out.stride(0))
+                             k=kd.data_ptr(), v=vd.data_ptr(), out=out.data_ptr(), ld_out=out.stride(0),
+                             status=status.data_ptr())
     capi.check(lib.mie_prefill_attention(ctypes.byref(a), capi.stream_handle(torch.device(DEV))),
                "mie_prefill_attention")
-    got = out.float().cpu().view(T, H, hd).transpose(0, 1)
+    assert int(status.item()) == 0
+    got = out.float().cpu().reshape(T, H, hd).transpose(0, 1)
     torch.testing.assert_close(got, want, atol=1e-2, rtol=1e-2)
 
 
