@@ -173,6 +173,43 @@ def moe_microbench(model, hbm_peak):
             "frac": MOE_LAYER_BYTES / t / 1e9 / hbm_peak, "calls_per_graph": 240}
 
 
+def moe_q_microbench(model, hbm_peak, bits: int, group: int = 128):
+    """config[1] with quantized experts (``fused_moe.quantize_experts``, int8
+    or int4 in groups of 128): the 12 layers' experts quantized, copies added
+    until the working set is >= 256 MB (twice L2), cycled in graphs of 240
+    back-to-back calls.  Algorithmic bytes per call: the bf16 router plus two
+    experts' quantized rows and fp32 group scales."""
+    from moe_engine import fused_moe
+
+    dev = model.token_embedding.weight.device
+    base = []
+    for blk in model.MoEBlocks:
+        s = blk.moe._expert_storage
+        base.append((blk.moe, {k: fused_moe.quantize_experts(s[k], bits, group) for k in ("w1", "w3", "w2")}))
+    per_layer = sum(q.nbytes() for q in base[0][1].values())
+    copies = max(1, -(-256 * 2**20 // (per_layer * len(base))))
+    layers = [(moe, {k: fused_moe.QuantizedExperts(q.q.clone(), q.scale.clone(), q.bits, q.group_size, q.shape)
+                     for k, q in qs.items()}) for _ in range(copies) for moe, qs in base]
+    L = len(layers)
+    xs = torch.randn(len(base), 768, generator=torch.Generator().manual_seed(1)).to(dev, torch.bfloat16)
+    state = {"i": 0}
+
+    def timed_call():
+        i = state["i"] % L
+        state["i"] += 1
+        moe, q = layers[i]
+        fused_moe.decode(xs[i % len(base)].view(1, 1, 768), moe.router.weight, q["w1"], None, q["w2"], None,
+                         router_logits=moe._router_logits, expert_ids=moe._expert_ids,
+                         route_weights=moe._route_weights, hidden=moe._expert_hidden, out=moe._direct_out,
+                         w3_base=q["w3"], sync=moe._sync)
+
+    t = time_graph_calls(timed_call, 240)
+    E = model.config.num_experts
+    nbytes = 12288 + 2 * per_layer // E
+    return {"us": t * 1e6, "bytes": nbytes, "gbs": nbytes / t / 1e9, "frac": nbytes / t / 1e9 / hbm_peak,
+            "calls_per_graph": 240, "bits": bits, "group": group, "working_set_mb": round(per_layer * L / 2**20)}
+
+
 def attn_microbench(device, hbm_peak, contexts=(128, 512, 2048, 8192)):
     """config[2]: one query [12 heads, 64] bf16 over a paged cache (block 16,
     K/V ~ N(0, 1) bf16, shuffled block tables), through the C ABI entry point
@@ -251,6 +288,8 @@ def attn_microbench(device, hbm_peak, contexts=(128, 512, 2048, 8192)):
 def kernel_rooflines(model, hbm_peak):
     """Isolated per-op kernels: config[1] (MoE) and config[2] (attention)."""
     out = {"moe_decode": moe_microbench(model, hbm_peak)}
+    for bits in (8, 4):
+        out[f"moe_decode_int{bits}"] = moe_q_microbench(model, hbm_peak, bits)
     out.update(attn_microbench(model.token_embedding.weight.device, hbm_peak))
     return out
 
@@ -481,9 +520,12 @@ def run_b200(args, rank, world, device):
             for payload in ("fp32", "bf16"):
                 eps[payload] = measure_expert_parallel(model, alloc, device, world, max(1, min(args.steps, 2)), 1,
                                                        payload, want)
+        allreduce = {f"allreduce_us_{pl}": measure_allreduce(device, pl, model.config.hidden_dim)
+                     for pl in ("fp32", "bf16")}
         result["expert_parallel"] = {
             "n_gpus": world,
             "experts_per_rank": model.config.num_experts // world,
+            **allreduce,
             "note": "one request; aggregate = per-stream tok/s; the all-reduce of the [768] MoE partial per layer "
                     "is captured in a CUDA graph with the step's kernels (layer-by-layer kernels, not the "
                     "persistent step); tokens compared with rank 0's single-GPU greedy tokens of the same prompt",
@@ -588,6 +630,39 @@ def run_reference(args):
         "cpu_baseline": cb,
         "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+
+
+def measure_allreduce(device, payload: str, n: int, calls: int = 96, reps: int = 5) -> float:
+    """The expert-parallel step's collective alone: device time of one NCCL
+    all-reduce (sum) of the [n] MoE partial, fp32 or bf16, from a CUDA graph of
+    ``calls`` back-to-back all-reduces (max over ranks), in us."""
+    import torch.distributed as dist
+
+    buf = torch.ones(n, device=device, dtype=torch.float32 if payload == "fp32" else torch.bfloat16)
+    s = torch.cuda.Stream(device=device)
+    s.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(s):
+        for _ in range(3):
+            dist.all_reduce(buf)
+    torch.cuda.current_stream(device).wait_stream(s)
+    torch.cuda.synchronize(device)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        for _ in range(calls):
+            dist.all_reduce(buf)
+    g.replay()
+    torch.cuda.synchronize(device)
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize(device)
+    t = torch.tensor([e0.elapsed_time(e1) * 1e3 / (reps * calls)], device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    del g  # NCCL work in the graph: released before the group goes
+    return float(t)
 
 
 def measure_expert_parallel(model, alloc, device, world, steps: int, warmup: int, payload: str, want=None):

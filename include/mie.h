@@ -94,6 +94,18 @@ typedef struct mie_moe_args {
   int grid;               /* CTAs; 0 = one per SM */
   int expert_base;        /* expert parallel: weights hold experts [base, base+count) */
   int expert_count;       /* 0 = all experts local */
+  /* Quantized experts (no counterpart in the reference; its roadmap item
+   * moe-inference-engine.md:36).  0: w1 / w3 / w2 hold `dtype` values.  8 or 4:
+   * they hold int8 values, or int4 values two per byte (the even element in
+   * the low nibble), of rows quantized in groups of group_size consecutive
+   * elements along the row (symmetric: w = scale * q, |q| <= 127 or 7); the
+   * router, biases and activations stay in `dtype`.  Rows must be multiples
+   * of 16 bytes and of group_size (a multiple of 32). */
+  int expert_bits;
+  int group_size;
+  const float* w1_scale;  /* [E', Hx, D / group_size] */
+  const float* w3_scale;  /* [E', Hx, D / group_size] (SwiGLU) */
+  const float* w2_scale;  /* [E', D, Hx / group_size] */
 } mie_moe_args;
 
 /* Single-query attention over a paged ([nb, H, bs, hd] per layer) or

@@ -45,6 +45,15 @@ int check_moe(const mie_moe_args& a, bool route_only) {
   if (a.norm != MIE_NORM_NONE && !a.norm_w) return MIE_ERR_INVALID;
   if (route_only) return MIE_OK;
   if (a.act != MIE_ACT_GELU && a.act != MIE_ACT_SWIGLU) return MIE_ERR_UNSUPPORTED;
+  if (a.expert_bits != 0) {
+    // quantized experts: int8 / int4 rows of whole 16-byte pieces and groups
+    if (a.expert_bits != 8 && a.expert_bits != 4) return MIE_ERR_UNSUPPORTED;
+    const int g = a.group_size;
+    if (g <= 0 || g % 32 || a.hidden_dim % g || a.expert_hidden_dim % g) return MIE_ERR_UNSUPPORTED;
+    if (((int64_t)a.hidden_dim * a.expert_bits / 8) % 16 || ((int64_t)a.expert_hidden_dim * a.expert_bits / 8) % 16)
+      return MIE_ERR_UNSUPPORTED;
+    if (!a.w1_scale || !a.w2_scale || (a.act == MIE_ACT_SWIGLU && !a.w3_scale)) return MIE_ERR_INVALID;
+  }
   if (!a.w1 || !a.w2 || !aligned16(a.w1) || !aligned16(a.w2)) return MIE_ERR_INVALID;
   if (a.act == MIE_ACT_SWIGLU && (!a.w3 || !aligned16(a.w3))) return MIE_ERR_INVALID;
   if (!a.hidden || !a.out || !a.sync) return MIE_ERR_INVALID;
@@ -62,6 +71,7 @@ int run_moe(const mie_moe_args& a, cudaStream_t st, bool pdl, bool route_only) {
   MoeLayout L = moe_layout(a, grid, 0, 0);
   L.route_only = route_only ? 1 : 0;
   if (L.smem > (uint32_t)kMaxDynSmem) return MIE_ERR_UNSUPPORTED;
+  if (a.expert_bits != 0 && !route_only) return moe_decode_q_launch(a, L, grid, st, pdl);
   return moe_decode_launch(a, L, grid, st, pdl);
 }
 
@@ -405,6 +415,7 @@ int mie_init(int device) {
   }
   g_last_error[0] = 0;
   moe_set_attributes();
+  moe_q_set_attributes();
   attn_set_attributes();
   gemv_set_attributes();
   step_set_attributes();

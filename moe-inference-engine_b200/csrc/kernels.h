@@ -166,6 +166,8 @@ inline int launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, uint32_t smem
 MoeLayout moe_layout(const mie_moe_args& a, int grid, int slot_bytes, int nslot);
 int moe_decode_launch(const mie_moe_args& a, const MoeLayout& L, int grid, cudaStream_t st, bool pdl);
 void moe_set_attributes();
+int moe_decode_q_launch(const mie_moe_args& a, const MoeLayout& L, int grid, cudaStream_t st, bool pdl);
+void moe_q_set_attributes();
 
 // attention.cu
 AttnLayout attn_layout(const mie_attn_args& a);

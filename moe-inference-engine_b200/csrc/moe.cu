@@ -85,21 +85,10 @@ __global__ void __launch_bounds__(kThreads) moe_decode_kernel(const mie_moe_args
   }
   __syncthreads();
   if (tid == 0) {
-    // Repeated argmax: strict '>' while scanning ascending ids keeps the lower
-    // id on ties (fused_moe.py:146-150).
-    int i0 = 0;
-    for (int e = 1; e < E; ++e)
-      if (logits_s[e] > logits_s[i0]) i0 = e;
-    int i1 = (i0 == 0) ? 1 : 0;
-    for (int e = 0; e < E; ++e)
-      if (e != i0 && logits_s[e] > logits_s[i1]) i1 = e;
-    const float l0 = logits_s[i0], l1 = logits_s[i1];
-    const float e1 = expf(l1 - l0);  // l0 >= l1: stable 2-way softmax
-    const float den = 1.0f + e1;
+    int i0, i1;
+    top2_route(logits_s, E, &i0, &i1, &wts_s[0], &wts_s[1]);
     ids_s[0] = i0;
     ids_s[1] = i1;
-    wts_s[0] = 1.0f / den;
-    wts_s[1] = e1 / den;
     if (c == 0) {
       if (a.router_logits)
         for (int e = 0; e < E; ++e) a.router_logits[e] = logits_s[e];

@@ -59,6 +59,9 @@ __global__ void __launch_bounds__(kPfThreads) prefill_norm_kernel(const mie_pref
   const __nv_bfloat16* w = static_cast<const __nv_bfloat16*>(a.w);
   const __nv_bfloat16* b = static_cast<const __nv_bfloat16*>(a.b);
   __nv_bfloat16* out = static_cast<__nv_bfloat16*>(a.out) + (int64_t)t * D;
+  float wv[kPer];  // the weights, requested before the reduction
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) wv[j] = j < per ? bf(w, lane + 32 * j) : 0.f;
   float mean = 0.f, q = 0.f;
   if (a.norm == MIE_NORM_LAYER) {
     float sm = 0.f;
@@ -79,7 +82,7 @@ __global__ void __launch_bounds__(kPfThreads) prefill_norm_kernel(const mie_pref
   for (int j = 0; j < kPer; ++j) {
     if (j < per) {
       const int i = lane + 32 * j;
-      float y = (v[j] - mean) * rs * bf(w, i);
+      float y = (v[j] - mean) * rs * wv[j];
       if (b) y += bf(b, i);
       out[i] = __float2bfloat16_rn(y);
     }
@@ -176,17 +179,29 @@ __global__ void __launch_bounds__(kPfThreads) prefill_route_kernel(const mie_pre
       }
     }
   }
-  // lane e ends up holding logit e (E <= 32)
+  // lane e ends up holding logit e (E <= 32); eight experts at a time, their
+  // weight loads and reductions independent of one another
   float mine = -INFINITY;
 #pragma unroll 1
-  for (int e = 0; e < E; ++e) {
-    const __nv_bfloat16* we = rw + (int64_t)e * D + lane;
-    float s = 0.f;
+  for (int e0 = 0; e0 < E; e0 += 8) {
+    float s[8];
 #pragma unroll
-    for (int j = 0; j < kPer; ++j)
-      if (j < per) s = fmaf(xv[j], bf(we, 32 * j), s);
-    s = warp_sum(s);
-    if (lane == e) mine = s;
+    for (int u = 0; u < 8; ++u) {
+      s[u] = 0.f;
+      if (e0 + u < E) {
+        const __nv_bfloat16* we = rw + (int64_t)(e0 + u) * D + lane;
+#pragma unroll
+        for (int j = 0; j < kPer; ++j)
+          if (j < per) s[u] = fmaf(xv[j], bf(we, 32 * j), s[u]);
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+      for (int u = 0; u < 8; ++u) s[u] += __shfl_xor_sync(0xffffffffu, s[u], o);
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      if (lane == e0 + u) mine = s[u];
   }
   if (a.logits && lane < E) a.logits[(int64_t)t * E + lane] = mine;
   float bv = lane < E ? mine : -INFINITY;
@@ -229,11 +244,21 @@ __global__ void __launch_bounds__(kPfThreads) prefill_route_kernel(const mie_pre
   r1 = __shfl_sync(0xffffffffu, r1, 0);
   __nv_bfloat16* g0 = static_cast<__nv_bfloat16*>(a.gathered) + (int64_t)r0 * D;
   __nv_bfloat16* g1 = static_cast<__nv_bfloat16*>(a.gathered) + (int64_t)r1 * D;
+  if (((reinterpret_cast<uintptr_t>(xr) | reinterpret_cast<uintptr_t>(g0) | reinterpret_cast<uintptr_t>(g1)) & 15) == 0) {
+    // the row in 16-byte pieces (D is a multiple of 32)
+    const uint4* src = reinterpret_cast<const uint4*>(xr);
+    for (int i = lane; i < D / 8; i += 32) {
+      const uint4 v = src[i];
+      reinterpret_cast<uint4*>(g0)[i] = v;
+      reinterpret_cast<uint4*>(g1)[i] = v;
+    }
+  } else {
 #pragma unroll 4
-  for (int j = 0; j < per; ++j) {
-    const int i = lane + 32 * j;
-    g0[i] = xr[i];
-    g1[i] = xr[i];
+    for (int j = 0; j < per; ++j) {
+      const int i = lane + 32 * j;
+      g0[i] = xr[i];
+      g1[i] = xr[i];
+    }
   }
 }
 

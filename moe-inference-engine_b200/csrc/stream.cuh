@@ -163,6 +163,24 @@ __device__ __forceinline__ void load_and_norm(float* xs, const void* x, int x_dt
   __syncthreads();
 }
 
+// Top-2 of E logits by repeated argmax -- a strict '>' while scanning
+// ascending ids keeps the lower id on ties (fused_moe.py:146-150) -- and the
+// stable 2-way softmax of the pair (l0 >= l1).
+__device__ __forceinline__ void top2_route(const float* logits, int E, int* id0, int* id1, float* w0, float* w1) {
+  int i0 = 0;
+  for (int e = 1; e < E; ++e)
+    if (logits[e] > logits[i0]) i0 = e;
+  int i1 = (i0 == 0) ? 1 : 0;
+  for (int e = 0; e < E; ++e)
+    if (e != i0 && logits[e] > logits[i1]) i1 = e;
+  const float e1 = expf(logits[i1] - logits[i0]);
+  const float den = 1.0f + e1;
+  *id0 = i0;
+  *id1 = i1;
+  *w0 = 1.0f / den;
+  *w1 = e1 / den;
+}
+
 // Contiguous share of `total` items for CTA `c` of `g`: [begin, end).
 __device__ __forceinline__ void split_range(int total, int c, int g, int* begin, int* end) {
   *begin = (int)(((int64_t)total * c) / g);

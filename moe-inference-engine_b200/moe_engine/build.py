@@ -19,7 +19,7 @@ CSRC = os.path.join(ROOT, "csrc")
 INCLUDE = os.path.join(os.path.dirname(ROOT), "include")
 OUT_DIR = os.path.join(PKG, "_native")
 OUT = os.path.join(OUT_DIR, "libmie.so")
-SOURCES = ["capi.cu", "moe.cu", "attention.cu", "gemv.cu", "step.cu", "step_wide.cu", "step_cluster.cu", "gemm.cu",
+SOURCES = ["capi.cu", "moe.cu", "moe_q.cu", "attention.cu", "gemv.cu", "step.cu", "step_wide.cu", "step_cluster.cu", "gemm.cu",
            "prefill.cu"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

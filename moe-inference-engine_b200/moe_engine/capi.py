@@ -35,6 +35,7 @@ class MoeArgs(ctypes.Structure):
         ("router_logits", _p), ("expert_ids", _p), ("route_weights", _p), ("hidden", _p),
         ("out", _p), ("residual", _i), ("sync", _p), ("status", _p), ("skip", _p),
         ("grid", _i), ("expert_base", _i), ("expert_count", _i),
+        ("expert_bits", _i), ("group_size", _i), ("w1_scale", _p), ("w3_scale", _p), ("w2_scale", _p),
     ]
 
 

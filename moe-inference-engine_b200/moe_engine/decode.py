@@ -70,6 +70,8 @@ class DecodeRunner:
         for block in model.MoEBlocks:
             if block.moe.mode == "reference" or not block.moe.direct_configuration_supported(1):
                 return False
+            if block.moe.quantized:  # the step descriptors carry bf16 / fp32 experts only
+                return False
         return all(p.dtype == w.dtype and p.device == w.device for p in model.parameters())
 
     def __init__(self, model, expert_base: int = 0, expert_count: int = 0, moe_partial: bool = False):

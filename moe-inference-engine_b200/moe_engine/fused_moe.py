@@ -16,7 +16,14 @@ Differences from the reference, all widening what is supported:
 * SwiGLU experts: pass ``w3_base`` (the "up" projection) and the kernel
   computes ``down(silu(w1 x) * (w3 x))``; without it the expert is the
   reference's ``Linear -> GELU(erf) -> Linear`` with optional biases;
-* top-2 ties resolve to the lower expert id.
+* top-2 ties resolve to the lower expert id;
+* quantized experts (the reference's roadmap item, moe-inference-engine.md:36,
+  which has no code there): ``quantize_experts`` turns a stacked [E, rows,
+  cols] weight into int8 or int4 values with one fp32 scale per group of
+  ``group_size`` consecutive elements of a row, and ``decode`` takes such
+  ``QuantizedExperts`` for ``w1_base`` / ``w2_base`` / ``w3_base``
+  (``mie_moe_decode`` with ``expert_bits`` 8 or 4: half or a quarter of the
+  bf16 expert bytes are read).
 """
 
 from __future__ import annotations
@@ -152,6 +159,74 @@ def _sync_words(device: torch.device) -> torch.Tensor:
     return t
 
 
+class QuantizedExperts:
+    """Stacked expert weights [E, rows, cols] quantized in groups of
+    ``group_size`` consecutive elements of each row, symmetric:
+    ``w[e, r, i] ~ scale[e, r, i // group_size] * q[e, r, i]`` with
+    ``|q| <= 127`` (``bits`` 8, ``q`` int8 [E, rows, cols]) or ``|q| <= 7``
+    (``bits`` 4, ``q`` uint8 [E, rows, cols / 2] holding two values per byte,
+    the even element in the low nibble)."""
+
+    def __init__(self, q: torch.Tensor, scale: torch.Tensor, bits: int, group_size: int, shape):
+        self.q, self.scale, self.bits, self.group_size = q, scale, bits, group_size
+        self.shape = torch.Size(shape)
+
+    @property
+    def device(self):
+        return self.q.device
+
+    @property
+    def is_cuda(self):
+        return self.q.is_cuda
+
+    def to(self, device) -> "QuantizedExperts":
+        return QuantizedExperts(self.q.to(device), self.scale.to(device), self.bits, self.group_size, self.shape)
+
+    def nbytes(self) -> int:
+        return self.q.numel() * self.q.element_size() + self.scale.numel() * 4
+
+
+def quantize_experts(w: torch.Tensor, bits: int = 8, group_size: int = 128) -> QuantizedExperts:
+    """Groupwise symmetric absmax quantization of a stacked [E, rows, cols]
+    weight: per group, ``scale = max|w| / qmax`` (fp32, qmax 127 or 7) and
+    ``q = clamp(round_half_even(w / scale), -qmax, qmax)`` (0 where the group
+    is all zero)."""
+    if bits not in (8, 4):
+        raise ValueError(f"expert weights quantize to 8 or 4 bits, not {bits}")
+    if w.dim() != 3:
+        raise ValueError("quantize_experts needs a stacked [E, rows, cols] weight")
+    E, R, C = w.shape
+    if group_size <= 0 or group_size % 32 or C % group_size:
+        raise ValueError(f"group_size must be a multiple of 32 dividing the row length {C}")
+    qmax = 127 if bits == 8 else 7
+    g = w.detach().float().reshape(E, R, C // group_size, group_size)
+    amax = g.abs().amax(-1)
+    # tensor / tensor: a correctly rounded division on every device (a CUDA
+    # division by a Python scalar multiplies by its reciprocal instead)
+    scale = amax / torch.full_like(amax, float(qmax))
+    safe = torch.where(scale > 0, scale, torch.ones_like(scale))
+    q = torch.clamp(torch.round(g / safe.unsqueeze(-1)), -qmax, qmax).to(torch.int8).reshape(E, R, C)
+    if bits == 4:
+        u = (q.to(torch.int16) & 0xF).to(torch.uint8)
+        q = u[..., 0::2] | (u[..., 1::2] << 4)
+    return QuantizedExperts(q.contiguous(), scale.contiguous(), bits, group_size, (E, R, C))
+
+
+def dequantize_experts(qe: QuantizedExperts) -> torch.Tensor:
+    """The fp32 weights a QuantizedExperts stands for: scale * q."""
+    E, R, C = qe.shape
+    if qe.bits == 4:
+        lo = (qe.q & 0xF).to(torch.int16)
+        hi = ((qe.q >> 4) & 0xF).to(torch.int16)
+        lo = torch.where(lo >= 8, lo - 16, lo)
+        hi = torch.where(hi >= 8, hi - 16, hi)
+        q = torch.stack((lo, hi), dim=-1).reshape(E, R, C)
+    else:
+        q = qe.q
+    g = q.float().reshape(E, R, C // qe.group_size, qe.group_size)
+    return (g * qe.scale.unsqueeze(-1)).reshape(E, R, C)
+
+
 def _args(x, router_weight, w1, b1, w2, b2, w3, router_logits, expert_ids, route_weights, hidden, out, sync):
     E, D = router_weight.shape
     a = capi.MoeArgs()
@@ -238,6 +313,9 @@ def decode(
     barrier words (a per-device default is used when omitted).  Returns
     ``out.view(1, 1, D)``.
     """
+    if isinstance(w1_base, QuantizedExperts):
+        return _decode_quantized(x, router_weight, w1_base, b1_base, w2_base, b2_base, router_logits, expert_ids,
+                                 route_weights, hidden, out, w3_base, sync)
     tensors = [x, router_weight, w1_base, w2_base, router_logits, route_weights, hidden, out]
     tensors += [t for t in (b1_base, b2_base, w3_base) if t is not None]
     _require_cuda(*tensors)
@@ -254,5 +332,52 @@ def decode(
     lib = capi.ensure_init(x.device)
     a = _args(x, router_weight, w1_base, b1_base, w2_base, b2_base, w3_base, router_logits, expert_ids,
               route_weights, hidden, out, sync)
+    capi.check(lib.mie_moe_decode(ctypes.byref(a), capi.stream_handle(x.device)), "mie_moe_decode")
+    return out.view(1, 1, D)
+
+
+def _decode_quantized(x, router_weight, w1, b1, w2, b2, router_logits, expert_ids, route_weights, hidden, out, w3,
+                      sync):
+    """``decode`` with QuantizedExperts for w1 / w2 (/ w3): the same launch
+    with ``expert_bits`` and the group scales set."""
+    quant = [w1, w2] + ([w3] if w3 is not None else [])
+    if not all(isinstance(q, QuantizedExperts) for q in quant):
+        raise ValueError("quantized MoE needs QuantizedExperts for w1, w2 (and w3)")
+    if len({(q.bits, q.group_size) for q in quant}) != 1:
+        raise ValueError("quantized MoE weights must share bits and group size")
+    tensors = [x, router_weight, router_logits, route_weights, hidden, out]
+    tensors += [t for t in (b1, b2) if t is not None]
+    _require_cuda(*tensors)
+    if any(q.device != x.device for q in quant):
+        raise ValueError("direct MoE tensors must be on the same CUDA device")
+    if router_weight.dim() != 2:
+        raise ValueError("direct MoE router weight must be [E, D]")
+    E, D = router_weight.shape
+    Hx = w1.shape[1]
+    rows = [(w1, (E, Hx, D)), (w2, (E, D, Hx))] + ([(w3, (E, Hx, D))] if w3 is not None else [])
+    wdt = router_weight.dtype
+    ok = all(q.shape == shape and q.q.is_contiguous() and q.scale.is_contiguous() and q.scale.dtype == torch.float32
+             for q, shape in rows)
+    ok = ok and router_weight.is_contiguous() and all(
+        t is None or (t.is_contiguous() and t.dtype == wdt and t.shape == shape)
+        for t, shape in ((b1, (E, Hx)), (b2, (E, D))))
+    ok = ok and (router_logits.shape == (E,) and router_logits.dtype == torch.float32
+                 and route_weights.shape == (TOP_K,) and route_weights.dtype == torch.float32
+                 and hidden.shape == (TOP_K, Hx) and hidden.dtype == torch.float32 and hidden.is_contiguous()
+                 and expert_ids.shape == (TOP_K,) and expert_ids.dtype == torch.int32
+                 and out.numel() == D and out.dtype == wdt and out.is_contiguous())
+    if not ok:
+        raise ValueError("direct MoE weights and workspaces must use canonical layouts")
+    if x.numel() != D or not x.is_contiguous():
+        raise ValueError("direct MoE needs one contiguous token x of the router's width")
+    if sync is None:
+        sync = _sync_words(x.device)
+    lib = capi.ensure_init(x.device)
+    a = _args(x, router_weight, w1.q, b1, w2.q, b2, w3.q if w3 is not None else None, router_logits, expert_ids,
+              route_weights, hidden, out, sync)
+    a.expert_hidden_dim = Hx
+    a.expert_bits, a.group_size = w1.bits, w1.group_size
+    a.w1_scale, a.w2_scale = w1.scale.data_ptr(), w2.scale.data_ptr()
+    a.w3_scale = w3.scale.data_ptr() if w3 is not None else None
     capi.check(lib.mie_moe_decode(ctypes.byref(a), capi.stream_handle(x.device)), "mie_moe_decode")
     return out.view(1, 1, D)

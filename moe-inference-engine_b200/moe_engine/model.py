@@ -474,13 +474,34 @@ class MoEFeedForward(nn.Module):
 
     def _repack_after_load(self, _module, _incompatible_keys) -> None:
         self._pack_expert_parameters()
+        self._quant = None  # loaded weights replace any quantized copy
 
     def _apply(self, fn, recurse=True):
         result = super()._apply(fn, recurse=recurse)
         self._pack_expert_parameters()
         w = self.router.weight
         self._make_workspaces(w.device, w.dtype)
+        if getattr(self, "_quant", None):
+            self._quant = {name: q.to(w.device) for name, q in self._quant.items()}
         return result
+
+    def quantize_experts(self, bits: int = 8, group_size: int = 128) -> None:
+        """Quantize the expert weights groupwise (int8 or int4, see
+        ``fused_moe.quantize_experts``).  The decode kernel then reads the
+        quantized values; the expert parameters are overwritten with the
+        weights those values stand for, so the prefill, the reference mode and
+        the decode all compute with the same effective weights."""
+        s = self._expert_storage
+        quant = {name: fused_moe.quantize_experts(s[name], bits, group_size) for name in ("w1", "w3", "w2")
+                 if name in s}
+        with torch.no_grad():
+            for name, q in quant.items():
+                s[name].copy_(fused_moe.dequantize_experts(q).to(s[name].dtype))
+        self._quant = quant
+
+    @property
+    def quantized(self) -> bool:
+        return bool(getattr(self, "_quant", None))
 
     def set_mode(self, mode: str) -> None:
         if mode not in ("auto", "direct", "reference"):
@@ -560,7 +581,9 @@ class MoEFeedForward(nn.Module):
         return out.reshape(batch, seq_len, dim)
 
     def _forward_direct(self, x: torch.Tensor) -> torch.Tensor:
-        s = self._expert_storage
+        s = dict(self._expert_storage)
+        if self.quantized:
+            s.update(self._quant)
         return fused_moe.decode(
             x,
             self.router.weight,
@@ -666,6 +689,16 @@ class Model(nn.Module):
         """Set reference, forced-direct, or automatic MoE dispatch on all layers."""
         for block in self.MoEBlocks:
             block.moe.set_mode(mode)
+        return self
+
+    def quantize_experts(self, bits: int = 8, group_size: int = 128) -> "Model":
+        """Groupwise int8 / int4 expert weights on every layer (the reference's
+        roadmap item, moe-inference-engine.md:36).  Decode steps then run the
+        per-layer operators with the quantized MoE kernel (the persistent step
+        kernels take bf16 / fp32 experts only); the prefill computes with the
+        weights the quantized values stand for."""
+        for block in self.MoEBlocks:
+            block.moe.quantize_experts(bits, group_size)
         return self
 
     def new_block_allocator(self, num_blocks: int, block_size: int = 16, attention_mode: str = "auto") -> BlockAllocator:
