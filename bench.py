@@ -766,7 +766,8 @@ def run_profile(steps: int):
 
 def run_profile_ops(reps: int):
     """Profiling workload (``--profile-ops N``): N calls of the per-op fused MoE
-    kernel (config[1] shapes, the 12 layers cycled) and N calls of the per-op
+    kernel (config[1] shapes, the 12 layers cycled; then N with int8 and N with
+    int4 experts, groups of 128) and N calls of the per-op
     attention kernel (config[2], context 8192, rotating block tables of a
     256 MB pool); no timing."""
     import ctypes
@@ -784,6 +785,17 @@ def run_profile_ops(reps: int):
                          router_logits=moe._router_logits, expert_ids=moe._expert_ids,
                          route_weights=moe._route_weights, hidden=moe._expert_hidden, out=moe._direct_out,
                          w3_base=s["w3"], sync=moe._sync)
+    # the same calls with int8, then int4 experts (groups of 128)
+    for bits in (8, 4):
+        qs = [{k: fused_moe.quantize_experts(s[k], bits, 128) for k in ("w1", "w3", "w2")} for _, s in layers]
+        for i in range(reps):
+            moe, _ = layers[i % len(layers)]
+            q = qs[i % len(layers)]
+            fused_moe.decode(xs[i % len(layers)].view(1, 1, 768), moe.router.weight, q["w1"], None, q["w2"], None,
+                             router_logits=moe._router_logits, expert_ids=moe._expert_ids,
+                             route_weights=moe._route_weights, hidden=moe._expert_hidden, out=moe._direct_out,
+                             w3_base=q["w3"], sync=moe._sync)
+        del qs
     lib = capi.ensure_init(device)
     H, hd, bs, ctx = 12, 64, 16, 8192
     nb = ctx // bs

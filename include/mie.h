@@ -100,7 +100,7 @@ typedef struct mie_moe_args {
    * the low nibble), of rows quantized in groups of group_size consecutive
    * elements along the row (symmetric: w = scale * q, |q| <= 127 or 7); the
    * router, biases and activations stay in `dtype`.  Rows must be multiples
-   * of 16 bytes and of group_size (a multiple of 32). */
+   * of 16 bytes and of group_size (a power of two, at least 32). */
   int expert_bits;
   int group_size;
   const float* w1_scale;  /* [E', Hx, D / group_size] */

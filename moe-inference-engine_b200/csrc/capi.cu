@@ -49,7 +49,7 @@ int check_moe(const mie_moe_args& a, bool route_only) {
     // quantized experts: int8 / int4 rows of whole 16-byte pieces and groups
     if (a.expert_bits != 8 && a.expert_bits != 4) return MIE_ERR_UNSUPPORTED;
     const int g = a.group_size;
-    if (g <= 0 || g % 32 || a.hidden_dim % g || a.expert_hidden_dim % g) return MIE_ERR_UNSUPPORTED;
+    if (g < 32 || (g & (g - 1)) || a.hidden_dim % g || a.expert_hidden_dim % g) return MIE_ERR_UNSUPPORTED;
     if (((int64_t)a.hidden_dim * a.expert_bits / 8) % 16 || ((int64_t)a.expert_hidden_dim * a.expert_bits / 8) % 16)
       return MIE_ERR_UNSUPPORTED;
     if (!a.w1_scale || !a.w2_scale || (a.act == MIE_ACT_SWIGLU && !a.w3_scale)) return MIE_ERR_INVALID;

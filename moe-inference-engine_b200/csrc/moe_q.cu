@@ -28,7 +28,7 @@ namespace {
 
 constexpr int kQThreads = 512;
 constexpr int kQWarps = kQThreads / 32;
-constexpr int kQSegWords = 8;  // words per lane held in registers per row segment
+constexpr int kQSegWords = 6;  // words per lane held in registers per row segment (a 768-element int8 row)
 
 __device__ __forceinline__ float q_gelu(float v) { return 0.5f * v * (1.0f + erff(v * 0.7071067811865476f)); }
 __device__ __forceinline__ float q_silu(float v) { return v / (1.0f + expf(-v)); }
@@ -45,18 +45,30 @@ struct QSeg {
   float s[kQSegWords];
 };
 
+// gsh = log2(group): the group of element i is i >> gsh (group a power of two)
 template <int BITS>
-__device__ __forceinline__ void qseg_load(QSeg<BITS>& r, const uint32_t* row, const float* scale, int nw,
-                                          int group, int seg) {
+__device__ __forceinline__ void qseg_load(QSeg<BITS>& r, const uint32_t* row, const float* scale, int nw, int gsh,
+                                          int seg) {
   const int lane = threadIdx.x & 31;
 #pragma unroll
   for (int k = 0; k < kQSegWords; ++k) {
     const int w = seg * 32 * kQSegWords + lane + 32 * k;
     if (w < nw) {
       r.q[k] = __ldg(row + w);
-      r.s[k] = __ldg(scale + (w * kEpw<BITS>) / group);
+      r.s[k] = __ldg(scale + ((w * kEpw<BITS>) >> gsh));
     }
   }
+}
+
+// Small integers to float without I2F: with the bit pattern 0x4B000000 | u
+// (u < 2^23) a float holds exactly 2^23 + u, so subtracting 2^23 + bias
+// leaves u - bias.  The values are stored offset to unsigned (q + 128 for
+// int8, q + 8 for int4) by flipping their sign bits.
+__device__ __forceinline__ float byte_to_f(uint32_t u_flipped, uint32_t sel) {
+  return __int_as_float(__byte_perm(u_flipped, 0x4B000000u, sel)) - 8388736.0f;  // 2^23 + 128
+}
+__device__ __forceinline__ float nibble_to_f(uint32_t u_flipped, int b) {
+  return __int_as_float(0x4B000000u | ((u_flipped >> (4 * b)) & 0xFu)) - 8388616.0f;  // 2^23 + 8
 }
 
 // sum over the segment's words of scale x (q . x); x fp32 in shared memory
@@ -67,24 +79,23 @@ __device__ __forceinline__ float qseg_dot(const QSeg<BITS>& r, const float* xs, 
   for (int k = 0; k < kQSegWords; ++k) {
     const int w = seg * 32 * kQSegWords + lane + 32 * k;
     if (w < nw) {
-      const uint32_t q = r.q[k];
       float part;
       if constexpr (BITS == 8) {
+        const uint32_t u = r.q[k] ^ 0x80808080u;
         const float4 x = *reinterpret_cast<const float4*>(xs + 4 * w);
-        part = (float)(int)(int8_t)(q & 0xffu) * x.x;
-        part = fmaf((float)(int)(int8_t)((q >> 8) & 0xffu), x.y, part);
-        part = fmaf((float)(int)(int8_t)((q >> 16) & 0xffu), x.z, part);
-        part = fmaf((float)(int)(int8_t)(q >> 24), x.w, part);
+        // byte b to the low byte, zeros, 0x4B on top
+        part = byte_to_f(u, 0x7440u) * x.x;
+        part = fmaf(byte_to_f(u, 0x7441u), x.y, part);
+        part = fmaf(byte_to_f(u, 0x7442u), x.z, part);
+        part = fmaf(byte_to_f(u, 0x7443u), x.w, part);
       } else {
+        const uint32_t u = r.q[k] ^ 0x88888888u;
         const float4 x0 = *reinterpret_cast<const float4*>(xs + 8 * w);
         const float4 x1 = *reinterpret_cast<const float4*>(xs + 8 * w + 4);
         const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
         part = 0.f;
 #pragma unroll
-        for (int b = 0; b < 8; ++b) {
-          const int v = (int)(q << (28 - 4 * b)) >> 28;  // sign-extended nibble b
-          part = fmaf((float)v, xv[b], part);
-        }
+        for (int b = 0; b < 8; ++b) part = fmaf(nibble_to_f(u, b), xv[b], part);
       }
       acc = fmaf(r.s[k], part, acc);
     }
@@ -94,14 +105,13 @@ __device__ __forceinline__ float qseg_dot(const QSeg<BITS>& r, const float* xs, 
 
 // Full dot of one quantized row of n elements with xs (segment by segment).
 template <int BITS>
-__device__ __forceinline__ float qrow_dot(const uint32_t* row, const float* scale, const float* xs, int n,
-                                          int group) {
+__device__ __forceinline__ float qrow_dot(const uint32_t* row, const float* scale, const float* xs, int n, int gsh) {
   const int nw = n / kEpw<BITS>;
   const int nseg = (nw + 32 * kQSegWords - 1) / (32 * kQSegWords);
   float acc = 0.f;
   for (int sg = 0; sg < nseg; ++sg) {
     QSeg<BITS> r;
-    qseg_load<BITS>(r, row, scale, nw, group, sg);
+    qseg_load<BITS>(r, row, scale, nw, gsh, sg);
     acc = qseg_dot<BITS>(r, xs, nw, sg, acc);
   }
   return warp_sum(acc);
@@ -111,6 +121,7 @@ template <typename X, int BITS>
 __global__ void __launch_bounds__(kQThreads) moe_decode_q_kernel(const mie_moe_args a, MoeLayout L) {
   extern __shared__ __align__(16) float smem_q[];
   const int D = a.hidden_dim, Hx = a.expert_hidden_dim, E = a.num_experts, grp = a.group_size;
+  const int gsh = __ffs(grp) - 1;  // group_size is a power of two (checked on the host)
   const int G = gridDim.x, c = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const bool swiglu = a.act == MIE_ACT_SWIGLU;
   float* xs = smem_q;            // [D] normalised input
@@ -123,6 +134,21 @@ __global__ void __launch_bounds__(kQThreads) moe_decode_q_kernel(const mie_moe_a
   __shared__ uint64_t target_s;
   uint64_t* ctr = reinterpret_cast<uint64_t*>(a.sync);
   if (tid == 0) target_s = grid_sync_target(ctr, (uint32_t)G);
+  // Router rows (in the activation type) are static: requested into registers
+  // before waiting on the producer grid, dotted as the bf16 kernel does (the
+  // same logits, so the same routing)
+  constexpr int PV = Elem<X>::kPerVec;
+  const int nvec_d = D / PV;
+  const int64_t rb_d = (int64_t)D * sizeof(X);
+  const bool r_regs = nvec_d <= Seg<X>::kVecs;
+  auto router_row = [&](int e) {
+    return reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(a.router_w) + e * rb_d);
+  };
+  RowRegs<X> rr[2];
+  if (r_regs) {
+    for (int k = 0; k < 2; ++k)
+      if (warp + kQWarps * k < E) row_load<X>(rr[k], router_row(warp + kQWarps * k), nvec_d, 0);
+  }
 
   pdl_wait();
   if (skip_requested(a.skip)) {
@@ -130,13 +156,16 @@ __global__ void __launch_bounds__(kQThreads) moe_decode_q_kernel(const mie_moe_a
     return;
   }
 
-  // ---- prologue: norm + router (in the activation type) + top-2, every CTA ----
+  // ---- prologue: norm + router + top-2, every CTA ----
   load_and_norm(xs, a.x, a.x_dtype, nullptr, D, a.norm, a.eps, a.norm_w, a.norm_b, a.dtype, red);
-  const int64_t rb_d = (int64_t)D * sizeof(X);
-  for (int e = warp; e < E; e += kQWarps) {
-    const float v = warp_row_dot<X>(
-        reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(a.router_w) + e * rb_d), D / Elem<X>::kPerVec, xs);
-    if (lane == 0) logits_s[e] = v;
+  float xr[Seg<X>::kNV * PV];
+  if (r_regs) load_x_regs<X>(xr, xs, nvec_d);
+  for (int k = 0; k < 2; ++k) {
+    const int e = warp + kQWarps * k;
+    if (e < E) {
+      const float v = r_regs ? warp_sum(row_dot_regs<X>(rr[k], xr)) : warp_row_dot<X>(router_row(e), nvec_d, xs);
+      if (lane == 0) logits_s[e] = v;
+    }
   }
   __syncthreads();
   if (tid == 0) {
@@ -183,7 +212,7 @@ __global__ void __launch_bounds__(kQThreads) moe_decode_q_kernel(const mie_moe_a
   QSeg<BITS> wd;
   if (dn_regs && warp < np && local[warp / nr]) {
     const int64_t row = (int64_t)le[warp / nr] * D + r0 + warp % nr;
-    qseg_load<BITS>(wd, q2 + row * wpr_h, a.w2_scale + row * spr_h, wpr_h, grp, 0);
+    qseg_load<BITS>(wd, q2 + row * wpr_h, a.w2_scale + row * spr_h, wpr_h, gsh, 0);
   }
 
   // ---- up phase: unit k -> slot r = u / Hx, hidden index j ----
@@ -194,13 +223,13 @@ __global__ void __launch_bounds__(kQThreads) moe_decode_q_kernel(const mie_moe_a
     float g, uv = 0.f;
     if (up_regs) {
       QSeg<BITS> ga, ua;
-      qseg_load<BITS>(ga, q1 + row * wpr_d, a.w1_scale + row * spr_d, wpr_d, grp, 0);
-      if (swiglu) qseg_load<BITS>(ua, q3 + row * wpr_d, a.w3_scale + row * spr_d, wpr_d, grp, 0);
+      qseg_load<BITS>(ga, q1 + row * wpr_d, a.w1_scale + row * spr_d, wpr_d, gsh, 0);
+      if (swiglu) qseg_load<BITS>(ua, q3 + row * wpr_d, a.w3_scale + row * spr_d, wpr_d, gsh, 0);
       g = warp_sum(qseg_dot<BITS>(ga, xs, wpr_d, 0, 0.f));
       if (swiglu) uv = warp_sum(qseg_dot<BITS>(ua, xs, wpr_d, 0, 0.f));
     } else {
-      g = qrow_dot<BITS>(q1 + row * wpr_d, a.w1_scale + row * spr_d, xs, D, grp);
-      if (swiglu) uv = qrow_dot<BITS>(q3 + row * wpr_d, a.w3_scale + row * spr_d, xs, D, grp);
+      g = qrow_dot<BITS>(q1 + row * wpr_d, a.w1_scale + row * spr_d, xs, D, gsh);
+      if (swiglu) uv = qrow_dot<BITS>(q3 + row * wpr_d, a.w3_scale + row * spr_d, xs, D, gsh);
     }
     if (lane == 0) {
       if (a.b1) g += load_any(a.b1, a.dtype, row);
@@ -222,10 +251,10 @@ __global__ void __launch_bounds__(kQThreads) moe_decode_q_kernel(const mie_moe_a
     const int64_t row = (int64_t)le[r] * D + rowi;
     float v;
     if (dn_regs) {
-      if (p != warp) qseg_load<BITS>(wd, q2 + row * wpr_h, a.w2_scale + row * spr_h, wpr_h, grp, 0);
+      if (p != warp) qseg_load<BITS>(wd, q2 + row * wpr_h, a.w2_scale + row * spr_h, wpr_h, gsh, 0);
       v = warp_sum(qseg_dot<BITS>(wd, hs + (size_t)r * Hx, wpr_h, 0, 0.f));
     } else {
-      v = qrow_dot<BITS>(q2 + row * wpr_h, a.w2_scale + row * spr_h, hs + (size_t)r * Hx, Hx, grp);
+      v = qrow_dot<BITS>(q2 + row * wpr_h, a.w2_scale + row * spr_h, hs + (size_t)r * Hx, Hx, gsh);
     }
     if (lane == 0) resD[p] = v;
   }

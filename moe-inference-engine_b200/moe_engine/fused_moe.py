@@ -196,8 +196,8 @@ def quantize_experts(w: torch.Tensor, bits: int = 8, group_size: int = 128) -> Q
     if w.dim() != 3:
         raise ValueError("quantize_experts needs a stacked [E, rows, cols] weight")
     E, R, C = w.shape
-    if group_size <= 0 or group_size % 32 or C % group_size:
-        raise ValueError(f"group_size must be a multiple of 32 dividing the row length {C}")
+    if group_size < 32 or group_size & (group_size - 1) or C % group_size:
+        raise ValueError(f"group_size must be a power of two >= 32 dividing the row length {C}")
     qmax = 127 if bits == 8 else 7
     g = w.detach().float().reshape(E, R, C // group_size, group_size)
     amax = g.abs().amax(-1)

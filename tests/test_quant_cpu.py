@@ -76,6 +76,8 @@ def test_quantizer_rejects_bad_shapes():
     with pytest.raises(ValueError):
         fused_moe.quantize_experts(w, 8, 64)  # does not divide 96
     with pytest.raises(ValueError):
+        fused_moe.quantize_experts(torch.zeros(2, 4, 192), 8, 96)  # not a power of two
+    with pytest.raises(ValueError):
         fused_moe.quantize_experts(w[0], 8, 32)  # not stacked
 
 
