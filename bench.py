@@ -430,7 +430,11 @@ def run_b200(args, rank, world, device):
     # on the per-op path, the fused MoE kernel timed in isolation
     traffic = None
     if persistent:
-        dominant = "step_kernel (persistent decode step, one launch per token)"
+        from moe_engine import capi as _capi
+
+        dominant = ("cstep_kernel (persistent decode step on thread-block clusters, one launch per token)"
+                    if runner.step_kernel_for(cache) == _capi.MIE_STEP_CLUSTER
+                    else "step_kernel (persistent decode step, one CTA per SM, one launch per token)")
         step_bytes = weights_bytes + kv_bytes
         kr = {"us": step_s * 1e6, "gbs": step_bytes / step_s / 1e9, "bytes": step_bytes}
         kr["frac"] = kr["gbs"] / hbm_peak
