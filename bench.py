@@ -521,18 +521,21 @@ def run_b200(args, rank, world, device):
         eps = {}
         if model.config.num_experts % world == 0:
             want = [int(t) for t in single_tokens] if rank == 0 else None
-            for payload in ("fp32", "bf16"):
-                eps[payload] = measure_expert_parallel(model, alloc, device, world, max(1, min(args.steps, 2)), 1,
-                                                       payload, want)
-        allreduce = {f"allreduce_us_{pl}": measure_allreduce(device, pl, model.config.hidden_dim)
+            for key, payload, coll in (("peer", "fp32", "peer"), ("fp32", "fp32", "nccl"), ("bf16", "bf16", "nccl")):
+                eps[key] = measure_expert_parallel(model, alloc, device, world, max(1, min(args.steps, 2)), 1,
+                                                   payload, want, collective=coll)
+        allreduce = {f"allreduce_us_nccl_{pl}": measure_allreduce(device, pl, model.config.hidden_dim)
                      for pl in ("fp32", "bf16")}
+        allreduce["allreduce_us_peer_fp32"] = measure_peer_allreduce(device, model.config.hidden_dim)
         result["expert_parallel"] = {
             "n_gpus": world,
             "experts_per_rank": model.config.num_experts // world,
             **allreduce,
             "note": "one request; aggregate = per-stream tok/s; the all-reduce of the [768] MoE partial per layer "
-                    "is captured in a CUDA graph with the step's kernels (layer-by-layer kernels, not the "
-                    "persistent step); tokens compared with rank 0's single-GPU greedy tokens of the same prompt",
+                    "(peer: this repository's kernel over the ranks' memory; fp32 / bf16: NCCL with that "
+                    "payload) is captured in a CUDA graph with the step's kernels (layer-by-layer kernels, not "
+                    "the persistent step); tokens compared with rank 0's single-GPU greedy tokens of the same "
+                    "prompt; allreduce_us_*: the collective alone",
             **{f"{k}_tok_s": v["tok_s"] for k, v in eps.items()},
             **{f"{k}_tokens": {kk: vv for kk, vv in v.items() if kk not in ("tok_s",)} for k, v in eps.items()},
         }
@@ -669,7 +672,46 @@ def measure_allreduce(device, payload: str, n: int, calls: int = 96, reps: int =
     return float(t)
 
 
-def measure_expert_parallel(model, alloc, device, world, steps: int, warmup: int, payload: str, want=None):
+def measure_peer_allreduce(device, n: int, calls: int = 96, reps: int = 5) -> float:
+    """``mie_peer_reduce`` alone (this repository's all-reduce over peer
+    memory): device time of one call of the [n] fp32 partial from a CUDA graph
+    of ``calls`` back-to-back calls, max over ranks, in us."""
+    import torch.distributed as dist
+
+    from moe_engine.expert_parallel import PeerReducer
+
+    red = PeerReducer(n, None, device)
+    try:
+        buf = torch.ones(n, device=device)
+        for _ in range(3):
+            red(buf, buf)
+        torch.cuda.synchronize(device)
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream(device=device)
+        with torch.cuda.graph(g, stream=s):
+            for _ in range(calls):
+                red(buf, buf)
+        g.replay()
+        torch.cuda.synchronize(device)
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize(device)
+        t = torch.tensor([e0.elapsed_time(e1) * 1e3 / (reps * calls)], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        del g
+        if int(red.status.item()):
+            raise RuntimeError("mie_peer_reduce reported a timeout")
+        return float(t)
+    finally:
+        red.close()
+
+
+def measure_expert_parallel(model, alloc, device, world, steps: int, warmup: int, payload: str, want=None,
+                            collective: str = "nccl"):
     """config[4b] on the job's process group: one request (the seed-3 prompt
     of rank 0's replica) decoded with the experts of every layer split 8/N
     over the ranks and an NCCL all-reduce of the [768] MoE partial per layer,
@@ -679,7 +721,7 @@ def measure_expert_parallel(model, alloc, device, world, steps: int, warmup: int
     from moe_engine.expert_parallel import ExpertParallelDecoder
 
     prompt = torch.randint(0, 50304, (PROMPT_LEN,), generator=torch.Generator().manual_seed(3))
-    ep = ExpertParallelDecoder(model, payload=payload)
+    ep = ExpertParallelDecoder(model, payload=payload, collective=collective)
     times, new = [], None
     try:
         for it in range(warmup + steps):
@@ -696,10 +738,11 @@ def measure_expert_parallel(model, alloc, device, world, steps: int, warmup: int
             if it >= warmup:
                 times.append(e0.elapsed_time(e1) / 1e3)
     finally:
-        ep.release_graphs()  # NCCL work in graphs: released before the group goes
+        ep.close()  # graphs (NCCL work) and peer buffers released before the group goes
     t = torch.tensor([sum(times)], device=device)
     torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-    out = {"payload": payload, "tok_s": steps * NEW_TOKENS / float(t), "tokens": int(new.numel())}
+    out = {"payload": payload, "collective": collective, "tok_s": steps * NEW_TOKENS / float(t),
+           "tokens": int(new.numel())}
     if want is not None:
         got = new.tolist()
         agree = 0
@@ -717,7 +760,7 @@ def run_expert_parallel(args, rank, world, device):
     model = build_model(device, torch.bfloat16)
     max_blocks = -(-(PROMPT_LEN + NEW_TOKENS) // 16)
     alloc = model.new_block_allocator(num_blocks=max_blocks + 8, block_size=16, attention_mode="direct")
-    res = measure_expert_parallel(model, alloc, device, world, args.steps, args.warmup, "fp32")
+    res = measure_expert_parallel(model, alloc, device, world, args.steps, args.warmup, "fp32", collective="peer")
     value = res["tok_s"]
     return {
         "metric": METRIC + " -- expert parallel",

@@ -31,6 +31,11 @@
  *   mie_prefill_route    <- model.py:443-452 (fp32 router, top-2, softmax) plus
  *                           the per-expert token selection of the loop
  *   mie_prefill_combine  <- model.py:453-461 (weighted index_add_ of expert outputs)
+ *   mie_prefill_attention <- model.py:252-256 (causal SDPA of the prefill fast path)
+ * No counterpart in the reference (it is a single-GPU engine without quantized
+ * weights): mie_peer_reduce (the expert-parallel all-reduce over peer memory),
+ * the quantized-expert fields of mie_moe_args (its roadmap item,
+ * moe-inference-engine.md:36), mie_attn_decode_fixed_scratch.
  */
 #ifndef MIE_H
 #define MIE_H
@@ -479,6 +484,33 @@ typedef struct mie_prefill_attn_args {
                                 tensor-core kernel ran out (that launch wrote no rows) */
 } mie_prefill_attn_args;
 
+/* Expert-parallel all-reduce over peer memory.  No counterpart in the
+ * reference (a single-GPU engine): it replaces the NCCL all-reduce of the
+ * per-layer MoE partial in the expert-parallel decode (BASELINE config[4b]),
+ *   out[i] = sum over ranks r = 0 .. world - 1, in rank order, of in_r[i].
+ * Every rank writes its partial as tagged 64-bit words {f32 value, u32 call
+ * number} into its slot of every rank's receive buffer (a peer's through a
+ * CUDA IPC mapping, plain stores over NVLink) and polls its own buffer until
+ * every rank's words carry this call's number; the sum order is the same on
+ * every rank, so every rank holds the same bits.  The call number comes from
+ * `seq` (device, zeroed once, advanced by each call), so the launch can be
+ * captured in a CUDA graph.  All ranks make the same calls in the same order,
+ * as with an NCCL collective.  Two buffer halves alternate by call number: a
+ * rank cannot overwrite words a slower rank has yet to read. */
+#define MIE_PEER_MAX_RANKS 8
+typedef struct mie_peer_reduce_args {
+  int n;                     /* fp32 elements, 1 .. 1024 */
+  int rank;
+  int world;                 /* 1 .. MIE_PEER_MAX_RANKS */
+  const float* in;           /* [n] this rank's partial */
+  float* out;                /* [n] the sum (may be `in`) */
+  uint64_t* bufs[MIE_PEER_MAX_RANKS];  /* every rank's receive buffer as this process maps it
+                                          (its own at [rank]), mie_peer_buffer_bytes(n, world) each */
+  uint32_t* seq;             /* this group's device call counter, zeroed once */
+  int32_t* status;           /* optional: MIE_ERR_TIMEOUT when a rank's words did not arrive */
+  int64_t wait_limit_ns;     /* 0: 200 ms */
+} mie_peer_reduce_args;
+
 /* Library management */
 int mie_version(void);
 int mie_init(int device);                 /* set kernel attributes; call before any capture */
@@ -546,6 +578,17 @@ int mie_prefill_rope_kv(const mie_prefill_rope_args* a, void* stream);
 int mie_prefill_route(const mie_prefill_route_args* a, void* stream);
 int mie_prefill_combine(const mie_prefill_combine_args* a, void* stream);
 int mie_prefill_attention(const mie_prefill_attn_args* a, void* stream);
+
+/* Expert-parallel all-reduce over peer memory (see mie_peer_reduce_args) and
+ * the CUDA IPC plumbing of its receive buffers; the caller exchanges the
+ * 64-byte handles between its processes (e.g. torch.distributed). */
+int64_t mie_peer_buffer_bytes(int n, int world);
+int mie_peer_reduce(const mie_peer_reduce_args* a, void* stream);
+int mie_peer_alloc(int64_t bytes, void** ptr);         /* zeroed device memory, its own allocation */
+int mie_peer_free(void* ptr);
+int mie_peer_handle(const void* ptr, void* handle64);  /* cudaIpcGetMemHandle of an mie_peer_alloc buffer */
+int mie_peer_open(const void* handle64, void** ptr);   /* cudaIpcOpenMemHandle (another process's buffer) */
+int mie_peer_close(void* ptr);
 
 #ifdef __cplusplus
 }

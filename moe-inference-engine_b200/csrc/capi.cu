@@ -1,6 +1,7 @@
 // extern "C" entry points of libmie.so (declared in include/mie.h): argument
 // validation, launch geometry, and the decode-step launch sequence.
 #include <cstdio>
+#include <cstring>
 
 #include "kernels.h"
 
@@ -494,6 +495,71 @@ int mie_prefill_combine(const mie_prefill_combine_args* a, void* stream) {
 }
 int mie_prefill_attention(const mie_prefill_attn_args* a, void* stream) {
   return a ? prefill_attention(*a, static_cast<cudaStream_t>(stream)) : MIE_ERR_INVALID;
+}
+
+// ---- expert-parallel all-reduce over peer memory ----
+int64_t mie_peer_buffer_bytes(int n, int world) {
+  return (n < 1 || world < 1 || world > MIE_PEER_MAX_RANKS) ? 0 : peer_buffer_bytes(n, world);
+}
+
+int mie_peer_reduce(const mie_peer_reduce_args* a, void* stream) {
+  return a ? peer_reduce(*a, static_cast<cudaStream_t>(stream)) : MIE_ERR_INVALID;
+}
+
+int mie_peer_alloc(int64_t bytes, void** ptr) {
+  if (!ptr || bytes <= 0) return MIE_ERR_INVALID;
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, (size_t)bytes);
+  if (e == cudaSuccess) e = cudaMemset(p, 0, (size_t)bytes);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();  // zeroed before any stream uses it (one-time set-up)
+  if (e != cudaSuccess) {
+    note_cuda_error(e, "mie_peer_alloc");
+    if (p) cudaFree(p);
+    return MIE_ERR_CUDA;
+  }
+  *ptr = p;
+  return MIE_OK;
+}
+
+int mie_peer_free(void* ptr) {
+  if (!ptr) return MIE_ERR_INVALID;
+  const cudaError_t e = cudaFree(ptr);
+  if (e != cudaSuccess) note_cuda_error(e, "mie_peer_free");
+  return e == cudaSuccess ? MIE_OK : MIE_ERR_CUDA;
+}
+
+int mie_peer_handle(const void* ptr, void* handle64) {
+  if (!ptr || !handle64) return MIE_ERR_INVALID;
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "64-byte IPC handle");
+  cudaIpcMemHandle_t h;
+  const cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void*>(ptr));
+  if (e != cudaSuccess) {
+    note_cuda_error(e, "mie_peer_handle");
+    return MIE_ERR_CUDA;
+  }
+  memcpy(handle64, &h, sizeof(h));
+  return MIE_OK;
+}
+
+int mie_peer_open(const void* handle64, void** ptr) {
+  if (!handle64 || !ptr) return MIE_ERR_INVALID;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle64, sizeof(h));
+  void* p = nullptr;
+  const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) {
+    note_cuda_error(e, "mie_peer_open");
+    return MIE_ERR_CUDA;
+  }
+  *ptr = p;
+  return MIE_OK;
+}
+
+int mie_peer_close(void* ptr) {
+  if (!ptr) return MIE_ERR_INVALID;
+  const cudaError_t e = cudaIpcCloseMemHandle(ptr);
+  if (e != cudaSuccess) note_cuda_error(e, "mie_peer_close");
+  return e == cudaSuccess ? MIE_OK : MIE_ERR_CUDA;
 }
 
 int mie_decode_layer(const mie_step_desc* d, int l, void* stream) {

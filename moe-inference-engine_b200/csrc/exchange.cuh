@@ -25,6 +25,17 @@ __device__ __forceinline__ uint64_t ll_ld(const uint64_t* p) {
   asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
+// The same words across GPUs (system scope): a store into a peer's memory
+// through an IPC mapping, and the poll of this GPU's own copy.
+__device__ __forceinline__ void ll_put_sys(uint64_t* p, float v, uint32_t tag) {
+  const uint64_t w = ((uint64_t)tag << 32) | (uint64_t)__float_as_uint(v);
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ uint64_t ll_ld_sys(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
 __device__ __forceinline__ uint32_t ll_tag(uint64_t w) { return (uint32_t)(w >> 32); }
 __device__ __forceinline__ float ll_val(uint64_t w) { return __uint_as_float((uint32_t)w); }
 

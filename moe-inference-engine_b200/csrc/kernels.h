@@ -168,6 +168,8 @@ int moe_decode_launch(const mie_moe_args& a, const MoeLayout& L, int grid, cudaS
 void moe_set_attributes();
 int moe_decode_q_launch(const mie_moe_args& a, const MoeLayout& L, int grid, cudaStream_t st, bool pdl);
 void moe_q_set_attributes();
+int64_t peer_buffer_bytes(int n, int world);
+int peer_reduce(const mie_peer_reduce_args& a, cudaStream_t st);
 
 // attention.cu
 AttnLayout attn_layout(const mie_attn_args& a);

@@ -20,7 +20,7 @@ INCLUDE = os.path.join(os.path.dirname(ROOT), "include")
 OUT_DIR = os.path.join(PKG, "_native")
 OUT = os.path.join(OUT_DIR, "libmie.so")
 SOURCES = ["capi.cu", "moe.cu", "moe_q.cu", "attention.cu", "gemv.cu", "step.cu", "step_wide.cu", "step_cluster.cu", "gemm.cu",
-           "prefill.cu"]
+           "prefill.cu", "peer.cu"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -136,6 +136,16 @@ class PrefillAttnArgs(ctypes.Structure):
     ]
 
 
+MIE_PEER_MAX_RANKS = 8
+
+
+class PeerReduceArgs(ctypes.Structure):
+    _fields_ = [
+        ("n", _i), ("rank", _i), ("world", _i), ("in_", _p), ("out", _p), ("bufs", _p * MIE_PEER_MAX_RANKS),
+        ("seq", _p), ("status", _p), ("wait_limit_ns", _i64),
+    ]
+
+
 class PrefillRopeArgs(ctypes.Structure):
     _fields_ = [
         ("tokens", _i), ("num_heads", _i), ("head_dim", _i), ("pos0", _i), ("qkv", _p), ("rope_cos", _p),
@@ -181,6 +191,13 @@ SYMBOLS = {
     "mie_step_scratch_bytes": ([ctypes.POINTER(StepDesc)], ctypes.c_int64),
     "mie_step_kernel_of": ([ctypes.POINTER(StepDesc)], ctypes.c_int),
     "mie_prefill_attention": ([ctypes.POINTER(PrefillAttnArgs), _p], ctypes.c_int),
+    "mie_peer_buffer_bytes": ([ctypes.c_int, ctypes.c_int], ctypes.c_int64),
+    "mie_peer_reduce": ([ctypes.POINTER(PeerReduceArgs), _p], ctypes.c_int),
+    "mie_peer_alloc": ([ctypes.c_int64, ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),
+    "mie_peer_free": ([_p], ctypes.c_int),
+    "mie_peer_handle": ([_p, _p], ctypes.c_int),
+    "mie_peer_open": ([_p, ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),
+    "mie_peer_close": ([_p], ctypes.c_int),
     "mie_gemm": ([ctypes.POINTER(GemmArgs), _p], ctypes.c_int),
     "mie_prefill_norm": ([ctypes.POINTER(PrefillNormArgs), _p], ctypes.c_int),
     "mie_prefill_rope_kv": ([ctypes.POINTER(PrefillRopeArgs), _p], ctypes.c_int),

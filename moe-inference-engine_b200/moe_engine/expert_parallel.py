@@ -17,12 +17,15 @@ sum_k w_k E_k(x) = sum_ranks sum_{k local} w_k E_k(x).
 
 Each step is launched layer by layer (``mie_decode_layer``, the all-reduce,
 ``mie_decode_head``); the single-GPU persistent step kernel is not used here.
-``decode`` captures whole steps -- every layer's kernels and its NCCL
+``decode`` captures whole steps -- every layer's kernels and its
 all-reduce -- in a CUDA graph and replays it, so the host issues one graph
 launch per ``GRAPH_STEPS`` tokens instead of about fifty launches per token.
-The partial travels as fp32 by default; ``payload="bf16"`` sends it as bf16
-(half the bytes, the residual stream then differs from the single-GPU one by
-the bf16 rounding of each layer's MoE output).
+The partial is summed by ``mie_peer_reduce`` by default (``collective="peer"``:
+this repository's all-reduce kernel over the ranks' memory, tagged fp32 words
+stored over NVLink into every rank's receive buffer) or by an NCCL all-reduce
+(``collective="nccl"``), whose partial travels as fp32 or, with
+``payload="bf16"``, as bf16 (half the bytes; the residual stream then differs
+from the single-GPU one by the bf16 rounding of each layer's MoE output).
 """
 
 from __future__ import annotations
@@ -35,6 +38,71 @@ import torch.distributed as dist
 from . import capi
 from .decode import EOS_TOKEN_ID, DecodeRunner
 from .paged_attention import cache_geometry
+
+
+class PeerReducer:
+    """All-reduce (sum, rank order) of an fp32 [n] vector over the ranks of
+    ``group`` with ``mie_peer_reduce``: every rank stores its words into every
+    rank's receive buffer (CUDA IPC mappings; the handles travel through the
+    process group once) and polls its own.  Every rank must make the same
+    calls in the same order; ``close`` (a collective too) unmaps and frees."""
+
+    def __init__(self, n: int, group=None, device=None, status=None, wait_limit_ns: int = 0):
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        if self.world > capi.MIE_PEER_MAX_RANKS:
+            raise ValueError(f"the peer all-reduce takes at most {capi.MIE_PEER_MAX_RANKS} ranks")
+        self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else device
+        self.lib = capi.ensure_init(self.device)
+        self.n = n
+        self.local = ctypes.c_void_p()
+        nbytes = self.lib.mie_peer_buffer_bytes(n, self.world)
+        if nbytes <= 0:
+            raise ValueError(f"no peer buffer for n = {n}, world = {self.world}")
+        capi.check(self.lib.mie_peer_alloc(nbytes, ctypes.byref(self.local)), "mie_peer_alloc")
+        handle = (ctypes.c_char * 64)()
+        capi.check(self.lib.mie_peer_handle(self.local, handle), "mie_peer_handle")
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self.opened = []
+        bufs = []
+        for r, hb in enumerate(handles):
+            if r == self.rank:
+                bufs.append(self.local.value)
+                continue
+            p = ctypes.c_void_p()
+            capi.check(self.lib.mie_peer_open((ctypes.c_char * 64).from_buffer_copy(hb), ctypes.byref(p)),
+                       "mie_peer_open")
+            self.opened.append(p)
+            bufs.append(p.value)
+        self.seq = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.status = status if status is not None else torch.zeros(1, dtype=torch.int32, device=self.device)
+        self._args = capi.PeerReduceArgs()
+        a = self._args
+        a.n, a.rank, a.world = n, self.rank, self.world
+        for r, b in enumerate(bufs):
+            a.bufs[r] = b
+        a.seq, a.status, a.wait_limit_ns = self.seq.data_ptr(), self.status.data_ptr(), int(wait_limit_ns)
+        dist.barrier(group)  # every rank's buffer zeroed and mapped before the first call
+
+    def __call__(self, inp: torch.Tensor, out: torch.Tensor, stream=None) -> None:
+        a = self._args
+        a.in_, a.out = inp.data_ptr(), out.data_ptr()
+        capi.check(self.lib.mie_peer_reduce(ctypes.byref(a), stream if stream is not None
+                                            else capi.stream_handle(self.device)), "mie_peer_reduce")
+
+    def close(self) -> None:
+        if self.local is None:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(self.group)  # no rank still writes into a buffer about to go
+        for p in self.opened:
+            self.lib.mie_peer_close(p)
+        self.opened = []
+        dist.barrier(self.group)
+        self.lib.mie_peer_free(self.local)
+        self.local = None
 
 
 def expert_shard(num_experts: int, rank: int, world: int) -> tuple[int, int]:
@@ -58,14 +126,20 @@ class ExpertParallelDecoder:
     ``payload`` is the all-reduced partial's type: "fp32" or "bf16".
     """
 
-    def __init__(self, model, group=None, payload: str = "fp32", use_graph: bool = True):
+    def __init__(self, model, group=None, payload: str = "fp32", use_graph: bool = True,
+                 collective: str = "peer"):
         if payload not in ("fp32", "bf16"):
             raise ValueError(f"payload must be fp32 or bf16, not {payload!r}")
+        if collective not in ("peer", "nccl"):
+            raise ValueError(f"collective must be peer or nccl, not {collective!r}")
+        if collective == "peer" and payload != "fp32":
+            raise ValueError("the peer all-reduce carries fp32 partials")
         self.model = model
         self.group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
         self.payload = payload
+        self.collective = collective
         self.use_graph = use_graph
         cfg = model.config
         self.expert_base, self.expert_count = expert_shard(cfg.num_experts, self.rank, self.world)
@@ -73,6 +147,9 @@ class ExpertParallelDecoder:
                                    moe_partial=True)
         self._wire = (torch.zeros(cfg.hidden_dim, dtype=torch.bfloat16, device=self.runner.device)
                       if payload == "bf16" else None)
+        self._peer = (PeerReducer(cfg.hidden_dim, group, self.runner.device, status=self.runner.status,
+                                  wait_limit_ns=getattr(self.runner, "wait_limit_ns", 0))
+                      if collective == "peer" else None)
         self._graphs: dict = {}
 
     def _desc(self, cache, max_ctx: int):
@@ -82,7 +159,9 @@ class ExpertParallelDecoder:
 
     def _all_reduce(self) -> None:
         r = self.runner
-        if self._wire is None:
+        if self._peer is not None:
+            self._peer(r.moe_partial, r.moe_partial)
+        elif self._wire is None:
             dist.all_reduce(r.moe_partial, op=dist.ReduceOp.SUM, group=self.group)
         else:
             self._wire.copy_(r.moe_partial)
@@ -130,6 +209,14 @@ class ExpertParallelDecoder:
         """Drop the captured graphs (they hold NCCL work: release them before
         the process group is destroyed)."""
         self._graphs.clear()
+
+    def close(self) -> None:
+        """Release the graphs and the peer all-reduce's buffers (every rank
+        calls it: it synchronises the group)."""
+        self.release_graphs()
+        if self._peer is not None:
+            self._peer.close()
+            self._peer = None
 
     @torch.no_grad()
     def prefill(self, token_ids: torch.Tensor, cache):

@@ -24,6 +24,7 @@ STRUCTS = {
     "mie_layer_desc": capi.LayerDesc,
     "mie_step_desc": capi.StepDesc,
     "mie_prefill_attn_args": capi.PrefillAttnArgs,
+    "mie_peer_reduce_args": capi.PeerReduceArgs,
 }
 
 
@@ -36,7 +37,7 @@ def c_field_names(struct_name):
     text = open(HEADER).read()
     body = re.search(r"typedef struct %s \{(.*?)\} %s;" % (struct_name, struct_name), text, re.S).group(1)
     body = re.sub(r"/\*.*?\*/", "", body, flags=re.S)
-    return re.findall(r"(\w+)\s*;", body)
+    return re.findall(r"(\w+)\s*(?:\[[^\]]*\])?\s*;", body)
 
 
 @pytest.fixture(scope="module")

@@ -4,9 +4,10 @@ output completed by an all-reduce of per-rank partials.
 * CPU (gloo, 2 and 4 ranks): the decomposition the product relies on -- each
   rank's weighted sum over the selected experts it owns, summed over ranks,
   equals the full MoE output of the oracle; and the expert shard arithmetic.
-* GPU (NCCL, 2 ranks, needs 2 GPUs): expert-parallel greedy decode of the
+* GPU (2 ranks, needs 2 GPUs): expert-parallel greedy decode of the
   BASELINE model in fp32 gives the same tokens as the oracle and as the
-  single-GPU path.
+  single-GPU path, with the peer all-reduce kernel and with NCCL; the peer
+  all-reduce alone is bitwise the rank-order sum, eager and in a CUDA graph.
 """
 
 import os
@@ -93,9 +94,15 @@ def _ep_gpu_worker(rank, world, port, out):
         m.load_state_dict(engine_state_dict(P))
         m = m.to(dev, torch.float32)
         prompt = torch.randint(0, 50304, (16,), generator=torch.Generator().manual_seed(0))
-        alloc = m.new_block_allocator(num_blocks=8, block_size=16, attention_mode="direct")
-        ep = ExpertParallelDecoder(m)
-        got = ep.generate(prompt, 24, alloc.new_cache())[0].tolist()
+        alloc = m.new_block_allocator(num_blocks=16, block_size=16, attention_mode="direct")
+        got = {}
+        for collective in ("peer", "nccl"):
+            ep = ExpertParallelDecoder(m, collective=collective)
+            try:
+                got[collective] = ep.generate(prompt, 24, alloc.new_cache())[0].tolist()
+                ep.runner.check_status()
+            finally:
+                ep.close()
         single = m.generate(prompt, max_new_tokens=24, temperature=0)[0].tolist() if rank == 0 else None
         if rank == 0:
             out.put((got, single, oracle.generate_greedy(P, oracle.BASELINE_ARCH, prompt, 24)))
@@ -117,5 +124,73 @@ def test_expert_parallel_greedy_matches_oracle_and_single_gpu():
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
-    assert got == want
-    assert got == single
+    for collective in ("peer", "nccl"):
+        assert got[collective] == want, collective
+        assert got[collective] == single, collective
+
+
+def _peer_reduce_worker(rank, world, port, out):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    import datetime
+
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=dev)
+    try:
+        from moe_engine.expert_parallel import PeerReducer
+
+        n = 768
+        red = PeerReducer(n, None, dev)
+        try:
+            errs = 0
+            # eager calls, then a graph of 10 calls replayed 3 times: the call counter and the two
+            # buffer halves advance on the device
+            for call in range(6):
+                ins = [torch.randn(n, generator=torch.Generator().manual_seed(100 * call + r)) for r in range(world)]
+                x = ins[rank].to(dev)
+                red(x, x)  # in place
+                want = ins[0].clone()
+                for r in range(1, world):
+                    want += ins[r]
+                errs += int(not torch.equal(x.cpu(), want))
+            buf = torch.full((n,), float(rank + 1), device=dev)
+            g = torch.cuda.CUDAGraph()
+            s = torch.cuda.Stream(device=dev)
+            with torch.cuda.graph(g, stream=s):
+                for _ in range(10):
+                    red(buf, buf)
+            for _ in range(3):
+                buf.fill_(float(rank + 1))
+                g.replay()
+                torch.cuda.synchronize(dev)
+                total = float(sum(r + 1 for r in range(world)))
+                # each call sums the previous sums of every rank: total * world^(calls - 1)
+                errs += int(not torch.equal(buf.cpu(), torch.full((n,), total * world ** 9)))
+            del g
+            status = int(red.status.item())
+        finally:
+            red.close()
+        if rank == 0:
+            out.put((errs, status))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="the peer all-reduce needs 2 GPUs")
+def test_peer_all_reduce_sums_in_rank_order_eager_and_in_a_graph():
+    """mie_peer_reduce on 2 GPUs: bitwise the rank-order fp32 sum, in place,
+    over eager calls and CUDA-graph replays; no timeout recorded."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    procs = [ctx.Process(target=_peer_reduce_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    errs, status = q.get(timeout=300)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert errs == 0 and status == 0
