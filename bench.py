@@ -521,7 +521,8 @@ def run_b200(args, rank, world, device):
         eps = {}
         if model.config.num_experts % world == 0:
             want = [int(t) for t in single_tokens] if rank == 0 else None
-            for key, payload, coll in (("peer", "fp32", "peer"), ("fp32", "fp32", "nccl"), ("bf16", "bf16", "nccl")):
+            for key, payload, coll in (("fused", "fp32", "fused"), ("peer", "fp32", "peer"), ("fp32", "fp32", "nccl"),
+                                       ("bf16", "bf16", "nccl")):
                 eps[key] = measure_expert_parallel(model, alloc, device, world, max(1, min(args.steps, 2)), 1,
                                                    payload, want, collective=coll)
         allreduce = {f"allreduce_us_nccl_{pl}": measure_allreduce(device, pl, model.config.hidden_dim)
@@ -532,8 +533,8 @@ def run_b200(args, rank, world, device):
             "experts_per_rank": model.config.num_experts // world,
             **allreduce,
             "note": "one request; aggregate = per-stream tok/s; the all-reduce of the [768] MoE partial per layer "
-                    "(peer: this repository's kernel over the ranks' memory; fp32 / bf16: NCCL with that "
-                    "payload) is captured in a CUDA graph with the step's kernels (layer-by-layer kernels, not "
+                    "(fused: completed inside the MoE kernel over the ranks' memory; peer: the same exchange as "
+                    "a kernel of its own; fp32 / bf16: NCCL with that payload) is captured in a CUDA graph with the step's kernels (layer-by-layer kernels, not "
                     "the persistent step); tokens compared with rank 0's single-GPU greedy tokens of the same "
                     "prompt; allreduce_us_*: the collective alone",
             **{f"{k}_tok_s": v["tok_s"] for k, v in eps.items()},
@@ -760,7 +761,7 @@ def run_expert_parallel(args, rank, world, device):
     model = build_model(device, torch.bfloat16)
     max_blocks = -(-(PROMPT_LEN + NEW_TOKENS) // 16)
     alloc = model.new_block_allocator(num_blocks=max_blocks + 8, block_size=16, attention_mode="direct")
-    res = measure_expert_parallel(model, alloc, device, world, args.steps, args.warmup, "fp32", collective="peer")
+    res = measure_expert_parallel(model, alloc, device, world, args.steps, args.warmup, "fp32", collective="fused")
     value = res["tok_s"]
     return {
         "metric": METRIC + " -- expert parallel",

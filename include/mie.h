@@ -59,6 +59,8 @@ enum {
 
 /* element types */
 enum { MIE_F32 = 0, MIE_BF16 = 1 };
+/* ranks of an expert-parallel group served by the all-reduce over peer memory */
+#define MIE_PEER_MAX_RANKS 8
 /* normalisation applied in a kernel prologue */
 enum { MIE_NORM_NONE = 0, MIE_NORM_RMS = 1, MIE_NORM_LAYER = 2 };
 /* expert activation */
@@ -111,6 +113,17 @@ typedef struct mie_moe_args {
   const float* w1_scale;  /* [E', Hx, D / group_size] */
   const float* w3_scale;  /* [E', Hx, D / group_size] (SwiGLU) */
   const float* w2_scale;  /* [E', D, Hx / group_size] */
+  /* Expert parallel with the all-reduce fused in (peer_world > 1; no
+   * counterpart in the reference): each CTA stores its output rows' partial
+   * -- its local experts' weighted sum -- as tagged words into every rank's
+   * receive buffer (the layout, call counter and call-order rules of
+   * mie_peer_reduce, n = hidden_dim), polls its own buffer for the same rows
+   * and writes out = (residual ? x : 0) + the rank-order sum. */
+  int peer_rank;
+  int peer_world;                          /* 0 or 1: no exchange */
+  uint32_t* peer_seq;
+  uint64_t* peer_bufs[MIE_PEER_MAX_RANKS];
+  int64_t peer_wait_limit_ns;              /* 0: 200 ms */
 } mie_moe_args;
 
 /* Single-query attention over a paged ([nb, H, bs, hd] per layer) or
@@ -354,6 +367,11 @@ typedef struct mie_step_desc {
    * one-CTA-per-SM kernel; the other two force one (MIE_ERR_UNSUPPORTED when
    * the forced kernel cannot take the shapes). */
   int step_kernel;
+  /* Expert parallel, per-layer launch sequence: when non-NULL (a host
+   * pointer, read at launch), each layer's MoE kernel completes the
+   * all-reduce of its partial itself over these peer buffers (see the peer_*
+   * fields of mie_moe_args), so moe_partial receives the sum over ranks. */
+  const struct mie_peer_reduce_args* moe_peer;
 } mie_step_desc;
 
 enum { MIE_STEP_AUTO = 0, MIE_STEP_FLAT = 1, MIE_STEP_CLUSTER = 2 };
@@ -497,7 +515,6 @@ typedef struct mie_prefill_attn_args {
  * captured in a CUDA graph.  All ranks make the same calls in the same order,
  * as with an NCCL collective.  Two buffer halves alternate by call number: a
  * rank cannot overwrite words a slower rank has yet to read. */
-#define MIE_PEER_MAX_RANKS 8
 typedef struct mie_peer_reduce_args {
   int n;                     /* fp32 elements, 1 .. 1024 */
   int rank;

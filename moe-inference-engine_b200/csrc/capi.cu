@@ -60,6 +60,13 @@ int check_moe(const mie_moe_args& a, bool route_only) {
   if (!a.hidden || !a.out || !a.sync) return MIE_ERR_INVALID;
   if (a.expert_count < 0 || a.expert_base < 0 || a.expert_base + a.expert_count > a.num_experts)
     return MIE_ERR_INVALID;
+  if (a.peer_world > 1) {
+    // the fused expert-parallel all-reduce (one word per row per rank)
+    if (a.peer_world > MIE_PEER_MAX_RANKS || a.peer_rank < 0 || a.peer_rank >= a.peer_world || !a.peer_seq)
+      return MIE_ERR_INVALID;
+    for (int r = 0; r < a.peer_world; ++r)
+      if (!a.peer_bufs[r] || (reinterpret_cast<uintptr_t>(a.peer_bufs[r]) & 7u)) return MIE_ERR_INVALID;
+  }
   return MIE_OK;
 }
 
@@ -288,6 +295,14 @@ mie_moe_args step_moe(const mie_step_desc& d, int l) {
   a.skip = d.done;
   a.expert_base = d.expert_base;
   a.expert_count = d.expert_count;
+  if (d.moe_peer) {  // expert parallel: the MoE kernel completes the all-reduce of its partial
+    const mie_peer_reduce_args& p = *d.moe_peer;
+    a.peer_rank = p.rank;
+    a.peer_world = p.world;
+    a.peer_seq = p.seq;
+    for (int r = 0; r < MIE_PEER_MAX_RANKS; ++r) a.peer_bufs[r] = r < p.world ? p.bufs[r] : nullptr;
+    a.peer_wait_limit_ns = p.wait_limit_ns;
+  }
   return a;
 }
 

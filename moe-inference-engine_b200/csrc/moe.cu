@@ -70,6 +70,10 @@ __global__ void __launch_bounds__(kThreads) moe_decode_kernel(const mie_moe_args
     pdl_trigger();
     return;
   }
+  // expert parallel with the all-reduce fused in: this launch's call number
+  __shared__ uint32_t ptag_s;
+  const bool peer = a.peer_world > 1 && !L.route_only;
+  if (peer && tid == 0) ptag_s = peer_tag(a);
 
   // ---- prologue: norm + router + top-2 (identical in every CTA) ----
   load_and_norm(xs, a.x, a.x_dtype, nullptr, D, a.norm, a.eps, a.norm_w, a.norm_b, a.dtype, red);
@@ -204,9 +208,12 @@ __global__ void __launch_bounds__(kThreads) moe_decode_kernel(const mie_moe_args
       if (a.b2) v += load_any(a.b2, a.dtype, (int64_t)le[r] * D + row);
       y = fmaf(wts_s[r], v, y);
     }
+    if (peer) y = peer_row_sum(a, D, row, y, ptag_s);  // every rank's partial of this row
     if (a.residual) y += load_any(a.x, a.x_dtype, row);
     store_any(a.out, a.out_dtype, row, y);
   }
+  // every CTA read the counter before the grid barrier
+  if (peer && c == 0 && tid == 0) *reinterpret_cast<volatile uint32_t*>(a.peer_seq) = ptag_s;
 }
 
 }  // namespace

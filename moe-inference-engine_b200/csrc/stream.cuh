@@ -17,6 +17,7 @@
 #include <cstdio>
 
 #include "common.cuh"
+#include "exchange.cuh"
 
 namespace mie {
 
@@ -179,6 +180,39 @@ __device__ __forceinline__ void top2_route(const float* logits, int E, int* id0,
   *id1 = i1;
   *w0 = 1.0f / den;
   *w1 = e1 / den;
+}
+
+// Expert parallel with the all-reduce fused into the MoE kernels (the
+// peer_* fields of mie_moe_args; the exchange of mie_peer_reduce, done by the
+// CTA that owns the rows).  peer_tag: this launch's call number, read after
+// the dependency wait and before the grid barrier (CTA 0 advances the counter
+// after it).  peer_row_sum: row `row` of this rank's partial y into every
+// rank's receive buffer, then the rank-order sum of that row over the ranks;
+// a wait that runs out records MIE_ERR_TIMEOUT and returns y.
+__device__ __forceinline__ uint32_t peer_tag(const mie_moe_args& a) {
+  return *reinterpret_cast<volatile const uint32_t*>(a.peer_seq) + 1u;
+}
+__device__ __forceinline__ float peer_row_sum(const mie_moe_args& a, int D, int row, float y, uint32_t tag) {
+  const size_t half = (size_t)(tag & 1u) * (size_t)a.peer_world * D;
+  for (int r = 0; r < a.peer_world; ++r) ll_put_sys(a.peer_bufs[r] + half + (size_t)a.peer_rank * D + row, y, tag);
+  const uint64_t* mine = a.peer_bufs[a.peer_rank] + half + row;
+  const unsigned long long limit = a.peer_wait_limit_ns > 0 ? (unsigned long long)a.peer_wait_limit_ns : kWaitLimitNs;
+  float sum = 0.f;
+  for (int r = 0; r < a.peer_world; ++r) {
+    const uint64_t* p = mine + (size_t)r * D;
+    uint64_t w = ll_ld_sys(p);
+    if (ll_tag(w) != tag) {
+      const unsigned long long t0 = global_ns();
+      while (ll_tag(w = ll_ld_sys(p)) != tag) {
+        if (global_ns() - t0 > limit) {
+          set_status(a.status, MIE_ERR_TIMEOUT);
+          return y;
+        }
+      }
+    }
+    sum += ll_val(w);
+  }
+  return sum;
 }
 
 // Contiguous share of `total` items for CTA `c` of `g`: [begin, end).

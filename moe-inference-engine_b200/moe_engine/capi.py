@@ -36,6 +36,8 @@ class MoeArgs(ctypes.Structure):
         ("out", _p), ("residual", _i), ("sync", _p), ("status", _p), ("skip", _p),
         ("grid", _i), ("expert_base", _i), ("expert_count", _i),
         ("expert_bits", _i), ("group_size", _i), ("w1_scale", _p), ("w3_scale", _p), ("w2_scale", _p),
+        ("peer_rank", _i), ("peer_world", _i), ("peer_seq", _p), ("peer_bufs", _p * 8),
+        ("peer_wait_limit_ns", _i64),
     ]
 
 
@@ -106,7 +108,7 @@ class StepDesc(ctypes.Structure):
         ("logits", _p), ("status", _p), ("attn_splits", _i), ("max_splits", _i), ("lm_grid", _i),
         ("use_pdl", _i), ("step_scratch", _p), ("step_scratch_bytes", _i64), ("sample_temperature", _f),
         ("sample_top_k", _i), ("sample_seed", _p), ("step_limit", _p), ("wait_limit_ns", _i64),
-        ("start_gate", _p), ("step_kernel", _i),
+        ("start_gate", _p), ("step_kernel", _i), ("moe_peer", _p),
     ]
 
 

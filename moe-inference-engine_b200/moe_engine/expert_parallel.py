@@ -20,10 +20,13 @@ Each step is launched layer by layer (``mie_decode_layer``, the all-reduce,
 ``decode`` captures whole steps -- every layer's kernels and its
 all-reduce -- in a CUDA graph and replays it, so the host issues one graph
 launch per ``GRAPH_STEPS`` tokens instead of about fifty launches per token.
-The partial is summed by ``mie_peer_reduce`` by default (``collective="peer"``:
-this repository's all-reduce kernel over the ranks' memory, tagged fp32 words
-stored over NVLink into every rank's receive buffer) or by an NCCL all-reduce
-(``collective="nccl"``), whose partial travels as fp32 or, with
+By default (``collective="fused"``) each layer's MoE kernel completes the
+all-reduce of its partial itself: every CTA stores its output rows' partial as
+tagged fp32 words over NVLink into every rank's receive buffer, polls its own
+for the same rows and sums them in rank order.  ``collective="peer"`` runs the
+same exchange as a kernel of its own after the MoE kernel
+(``mie_peer_reduce``); ``collective="nccl"`` uses an NCCL all-reduce, whose
+partial travels as fp32 or, with
 ``payload="bf16"``, as bf16 (half the bytes; the residual stream then differs
 from the single-GPU one by the bf16 rounding of each layer's MoE output).
 """
@@ -127,12 +130,12 @@ class ExpertParallelDecoder:
     """
 
     def __init__(self, model, group=None, payload: str = "fp32", use_graph: bool = True,
-                 collective: str = "peer"):
+                 collective: str = "fused"):
         if payload not in ("fp32", "bf16"):
             raise ValueError(f"payload must be fp32 or bf16, not {payload!r}")
-        if collective not in ("peer", "nccl"):
-            raise ValueError(f"collective must be peer or nccl, not {collective!r}")
-        if collective == "peer" and payload != "fp32":
+        if collective not in ("fused", "peer", "nccl"):
+            raise ValueError(f"collective must be fused, peer or nccl, not {collective!r}")
+        if collective != "nccl" and payload != "fp32":
             raise ValueError("the peer all-reduce carries fp32 partials")
         self.model = model
         self.group = group
@@ -149,16 +152,22 @@ class ExpertParallelDecoder:
                       if payload == "bf16" else None)
         self._peer = (PeerReducer(cfg.hidden_dim, group, self.runner.device, status=self.runner.status,
                                   wait_limit_ns=getattr(self.runner, "wait_limit_ns", 0))
-                      if collective == "peer" else None)
+                      if collective in ("fused", "peer") else None)
         self._graphs: dict = {}
 
     def _desc(self, cache, max_ctx: int):
         _, _, _, _, bs, _, _ = cache_geometry(cache, 0)
-        return self.runner.make_desc(cache, logits=False, graph=True,
-                                     splits=self.runner.splits_for(max_ctx, bs))
+        desc, layers = self.runner.make_desc(cache, logits=False, graph=True,
+                                             splits=self.runner.splits_for(max_ctx, bs))
+        if self.collective == "fused":
+            # each layer's MoE kernel completes the all-reduce of its partial itself
+            desc.moe_peer = ctypes.addressof(self._peer._args)
+        return desc, layers
 
     def _all_reduce(self) -> None:
         r = self.runner
+        if self.collective == "fused":
+            return  # done inside the MoE kernel
         if self._peer is not None:
             self._peer(r.moe_partial, r.moe_partial)
         elif self._wire is None:

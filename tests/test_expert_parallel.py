@@ -6,8 +6,9 @@ output completed by an all-reduce of per-rank partials.
   equals the full MoE output of the oracle; and the expert shard arithmetic.
 * GPU (2 ranks, needs 2 GPUs): expert-parallel greedy decode of the
   BASELINE model in fp32 gives the same tokens as the oracle and as the
-  single-GPU path, with the peer all-reduce kernel and with NCCL; the peer
-  all-reduce alone is bitwise the rank-order sum, eager and in a CUDA graph.
+  single-GPU path with each collective -- the all-reduce fused into the MoE
+  kernel, the peer all-reduce kernel, NCCL; the peer all-reduce alone is
+  bitwise the rank-order sum, eager and in a CUDA graph.
 """
 
 import os
@@ -96,7 +97,7 @@ def _ep_gpu_worker(rank, world, port, out):
         prompt = torch.randint(0, 50304, (16,), generator=torch.Generator().manual_seed(0))
         alloc = m.new_block_allocator(num_blocks=16, block_size=16, attention_mode="direct")
         got = {}
-        for collective in ("peer", "nccl"):
+        for collective in ("fused", "peer", "nccl"):
             ep = ExpertParallelDecoder(m, collective=collective)
             try:
                 got[collective] = ep.generate(prompt, 24, alloc.new_cache())[0].tolist()
@@ -124,7 +125,7 @@ def test_expert_parallel_greedy_matches_oracle_and_single_gpu():
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
-    for collective in ("peer", "nccl"):
+    for collective in ("fused", "peer", "nccl"):
         assert got[collective] == want, collective
         assert got[collective] == single, collective
 
