@@ -98,3 +98,49 @@ def test_gate_opened_from_another_stream_lets_the_step_run(kernel):
     runner.check_status()
     runner.start_gate, runner.wait_limit_ns = None, 0
     assert torch.equal(logits, ref_logits)
+
+
+def test_peer_exchange_wait_runs_out_then_completes():
+    """The expert-parallel exchange (mie_peer_reduce) on one GPU with two
+    rank slots in local buffers, as sequential launches (no launch waits on a
+    concurrently running one).  Rank 0 alone: its wait for rank 1's words runs
+    out after 1 ms and it records MIE_ERR_TIMEOUT.  Rank 1 then: rank 0's words
+    of the same call are already there, so it completes with the rank-order
+    sum and no error."""
+    import ctypes
+
+    lib = capi.ensure_init(torch.device(DEV))
+    n, world = 768, 2
+    nbytes = lib.mie_peer_buffer_bytes(n, world)
+    assert nbytes == 2 * world * n * 8
+    bufs = [torch.zeros(nbytes // 8, dtype=torch.int64, device=DEV) for _ in range(world)]
+    seqs = [torch.zeros(1, dtype=torch.int32, device=DEV) for _ in range(world)]
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    g = torch.Generator().manual_seed(5)
+    ins = [torch.randn(n, generator=g).to(DEV) for _ in range(world)]
+    outs = [torch.full((n,), float("nan"), device=DEV) for _ in range(world)]
+
+    def call(rank, limit_ns):
+        a = capi.PeerReduceArgs()
+        a.n, a.rank, a.world = n, rank, world
+        a.in_, a.out = ins[rank].data_ptr(), outs[rank].data_ptr()
+        for r in range(world):
+            a.bufs[r] = bufs[r].data_ptr()
+        a.seq, a.status, a.wait_limit_ns = seqs[rank].data_ptr(), status.data_ptr(), limit_ns
+        capi.check(lib.mie_peer_reduce(ctypes.byref(a), capi.stream_handle(torch.device(DEV))), "mie_peer_reduce")
+
+    t0 = time.perf_counter()
+    call(0, 1_000_000)
+    torch.cuda.synchronize()
+    assert time.perf_counter() - t0 < 5.0
+    assert int(status.item()) == capi.MIE_ERR_TIMEOUT
+    assert int(seqs[0].item()) == 1  # the call is counted all the same
+    status.zero_()
+    call(1, 1_000_000)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    assert torch.equal(outs[1], ins[0] + ins[1])
+    # invalid requests are refused on the host
+    a = capi.PeerReduceArgs()
+    a.n, a.rank, a.world = n, 2, world
+    assert lib.mie_peer_reduce(ctypes.byref(a), None) == capi.MIE_ERR_INVALID
