@@ -198,7 +198,7 @@ __device__ __forceinline__ void layer_fetch(const CStepParams& P, int l, int fir
 }
 
 // ---------------------------------------------------------------------------
-// Bounded waits.  Each returns a CTA-uniform verdict: true when `ok` was
+// Bounded waits.  Each returns a CTA-uniform result: true when `ok` was
 // true and every thread's wait succeeded; a CTA that is no longer ok skips
 // the wait (but still takes the block barrier).
 // ---------------------------------------------------------------------------
@@ -260,7 +260,7 @@ struct Ident {
 
 // A consumer warp: wait (bounded) for the next phase of full barrier b.
 // Every thread observes the phase itself (which also makes the staged bytes
-// visible to it), so no barrier is needed; the verdict is warp-uniform and
+// visible to it), so no barrier is needed; the result is warp-uniform and
 // becomes CTA-uniform at the next consumer barrier that carries it.
 __device__ __noinline__ bool bwait(bool ok, int b) {
   if (!ok) return false;

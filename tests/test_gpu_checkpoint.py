@@ -1,5 +1,5 @@
 """The reference architecture at production size through a checkpoint in the
-reference's format (survey row (f)2, "real-checkpoint path"): LayerNorm,
+reference's format (the real-checkpoint path): LayerNorm,
 learned positions, 8 heads x 96, biased GELU(erf) experts with hidden 3072,
 biased QKV / out / LM-head projections, 6 layers, vocab 50304.  The real
 checkpoint is not available offline, so a seeded random one is written in its
