@@ -281,7 +281,7 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const mie_attn_ar
 // ---------------------------------------------------------------------------
 // The pipelined kernel (rows of whole 16-byte pieces; the kernel above keeps
 // the narrow rows).  256 threads = 8 warps.  The split's token range is cut
-// into stages of whole blocks (~16 KB of K + V each) held in a ring of up to
+// into stages of whole blocks (~32 KB of K + V each) held in a ring of up to
 // kFastStages slots.  The split's physical block ids are read into shared
 // memory first; then warp 0 issues one bulk copy per block for K and one for
 // V (a block's K, and its V, is one contiguous run), each stage counted in
@@ -296,7 +296,7 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const mie_attn_ar
 constexpr int kFastThreads = 256;
 constexpr int kFastWarps = kFastThreads / 32;
 constexpr int kFastStages = 8;                   // ring slots (at most)
-constexpr uint32_t kFastStageBytes = 16 * 1024;  // K + V of one stage (at least one block)
+constexpr uint32_t kFastStageBytes = 32 * 1024;  // K + V of one stage (at least one block)
 constexpr uint32_t kFastRingBytes = 96 * 1024;   // two CTAs per SM
 
 // two adjacent elements (4- or 8-byte aligned) as floats
@@ -315,7 +315,7 @@ __global__ void __launch_bounds__(kFastThreads) attn_fast_kernel(const mie_attn_
   constexpr int LG = VPH <= 1 ? 1 : VPH <= 2 ? 2 : VPH <= 4 ? 4 : VPH <= 8 ? 8 : VPH <= 16 ? 16 : 32;
   constexpr int TPP = 32 / LG;
   constexpr int DPL = (HD + 31) / 32;
-  constexpr int P = 2;  // passes per iteration
+  constexpr int P = 4;  // passes per iteration (16 tokens of a warp at hd 64 bf16: one 32 KB stage)
   constexpr uint32_t kRow = HD * sizeof(KV);
   const int h = blockIdx.y, s = blockIdx.x, S = gridDim.x, tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
@@ -677,7 +677,7 @@ AttnLayout attn_layout(const mie_attn_args& a) {
   // One block of K+V must fit the per-thread register staging (16-byte rows).
   if ((a.head_dim * esz) % 16 == 0 && per_tok * st > budget) L.smem = 0xffffffffu;  // -> unsupported
   // 16-byte rows run the pipelined kernel: a ring of stages of whole blocks
-  // (~16 KB of K + V each, up to 96 KB), the split's block ids, per-warp
+  // (~32 KB of K + V each, up to 96 KB), the split's block ids, per-warp
   // partial states
   if ((a.head_dim * esz) % 16 == 0 && a.splits > 0) {
     AttnLayout F{};
