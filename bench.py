@@ -521,8 +521,8 @@ def run_b200(args, rank, world, device):
         eps = {}
         if model.config.num_experts % world == 0:
             want = [int(t) for t in single_tokens] if rank == 0 else None
-            for key, payload, coll in (("fused", "fp32", "fused"), ("peer", "fp32", "peer"), ("fp32", "fp32", "nccl"),
-                                       ("bf16", "bf16", "nccl")):
+            for key, payload, coll in (("step", "fp32", "step"), ("fused", "fp32", "fused"), ("peer", "fp32", "peer"),
+                                       ("fp32", "fp32", "nccl"), ("bf16", "bf16", "nccl")):
                 eps[key] = measure_expert_parallel(model, alloc, device, world, max(1, min(args.steps, 2)), 1,
                                                    payload, want, collective=coll)
         allreduce = {f"allreduce_us_nccl_{pl}": measure_allreduce(device, pl, model.config.hidden_dim)
@@ -532,11 +532,13 @@ def run_b200(args, rank, world, device):
             "n_gpus": world,
             "experts_per_rank": model.config.num_experts // world,
             **allreduce,
-            "note": "one request; aggregate = per-stream tok/s; the all-reduce of the [768] MoE partial per layer "
-                    "(fused: completed inside the MoE kernel over the ranks' memory; peer: the same exchange as "
-                    "a kernel of its own; fp32 / bf16: NCCL with that payload) is captured in a CUDA graph with the step's kernels (layer-by-layer kernels, not "
-                    "the persistent step); tokens compared with rank 0's single-GPU greedy tokens of the same "
-                    "prompt; allreduce_us_*: the collective alone",
+            "note": "one request; aggregate = per-stream tok/s; the all-reduce of the [768] MoE partial per layer: "
+                    "step: inside the single-launch persistent cluster step (tagged words over NVLink into every "
+                    "rank's memory, summed in rank order by every reader); fused: completed inside each layer's "
+                    "MoE kernel (layer-by-layer kernels); peer: the same exchange as a kernel of its own; "
+                    "fp32 / bf16: NCCL with that payload; every variant's steps captured in CUDA graphs; tokens "
+                    "compared with rank 0's single-GPU greedy tokens of the same prompt; allreduce_us_*: the "
+                    "collective alone",
             **{f"{k}_tok_s": v["tok_s"] for k, v in eps.items()},
             **{f"{k}_tokens": {kk: vv for kk, vv in v.items() if kk not in ("tok_s",)} for k, v in eps.items()},
         }
@@ -742,7 +744,7 @@ def measure_expert_parallel(model, alloc, device, world, steps: int, warmup: int
         ep.close()  # graphs (NCCL work) and peer buffers released before the group goes
     t = torch.tensor([sum(times)], device=device)
     torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-    out = {"payload": payload, "collective": collective, "tok_s": steps * NEW_TOKENS / float(t),
+    out = {"payload": payload, "collective": ep.active, "tok_s": steps * NEW_TOKENS / float(t),
            "tokens": int(new.numel())}
     if want is not None:
         got = new.tolist()
@@ -761,7 +763,7 @@ def run_expert_parallel(args, rank, world, device):
     model = build_model(device, torch.bfloat16)
     max_blocks = -(-(PROMPT_LEN + NEW_TOKENS) // 16)
     alloc = model.new_block_allocator(num_blocks=max_blocks + 8, block_size=16, attention_mode="direct")
-    res = measure_expert_parallel(model, alloc, device, world, args.steps, args.warmup, "fp32", collective="fused")
+    res = measure_expert_parallel(model, alloc, device, world, args.steps, args.warmup, "fp32", collective="auto")
     value = res["tok_s"]
     return {
         "metric": METRIC + " -- expert parallel",

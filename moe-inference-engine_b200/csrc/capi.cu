@@ -360,8 +360,8 @@ int persistent_geometry(const mie_step_desc& d, StepPlan* plan) {
     rc = cstep_geometry(d, &plan->cg);
     if (rc == MIE_OK)
       plan->cluster = 1;
-    else if (d.step_kernel == MIE_STEP_CLUSTER)
-      return rc;
+    else if (d.step_kernel == MIE_STEP_CLUSTER || (d.moe_peer && d.moe_peer->world > 1))
+      return rc;  // expert parallel: no other persistent kernel takes it
   }
   if (!plan->cluster) rc = step_geometry(d, num_sms(), &plan->g);
   if (rc) return rc;

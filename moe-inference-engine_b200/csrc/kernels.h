@@ -113,6 +113,12 @@ struct CGeom {
   uint32_t sm_x, sm_xn, sm_xm, sm_ss, sm_g, sm_mg, sm_qkv, sm_sc, sm_ab, sm_h, sm_pr, sm_ov;
   uint32_t sm_fn;  // final norm weights
   uint32_t smem;
+  // expert parallel (peer_world > 1): this rank, every rank's exchange buffer
+  // as this process maps it ([2 layer parities][world][D] tagged words) and
+  // the group's device step counter, whose value + 1 keys the step's tags
+  int peer_rank, peer_world;
+  uint64_t* peer_bufs[MIE_PEER_MAX_RANKS];
+  uint32_t* peer_seq;
 };
 
 struct CStepParams {

@@ -1714,8 +1714,9 @@ int step_geometry(const mie_step_desc& d, int grid, StepGeom* g) {
   bool wide = (vph & (vph - 1)) != 0 || kStepThreads % hd != 0 || Hx > 768;
   if (d.top_k != 2 || E < 2 || E > 32) return MIE_ERR_UNSUPPORTED;
   if (d.act != MIE_ACT_GELU && d.act != MIE_ACT_SWIGLU) return MIE_ERR_UNSUPPORTED;
-  if (d.moe_partial || (d.expert_count && d.expert_count != E) || d.expert_base)
-    return MIE_ERR_UNSUPPORTED;  // expert parallel runs layer by layer
+  if (d.moe_partial || (d.expert_count && d.expert_count != E) || d.expert_base ||
+      (d.moe_peer && d.moe_peer->world > 1))
+    return MIE_ERR_UNSUPPORTED;  // expert parallel: the cluster step or layer by layer
   if (d.kv_stride_tok != hd || (d.kv_stride_block * kvsz) % 16 || (d.kv_stride_head * kvsz) % 16)
     return MIE_ERR_UNSUPPORTED;
   if (grid < H || grid < 2) return MIE_ERR_UNSUPPORTED;

@@ -129,6 +129,7 @@ struct CCtx {
   int sel0, sel1; // the layer's experts
   float wt0, wt1; // and their weights
   float snew;     // scale * q . k_new
+  uint32_t pstep; // expert parallel: the group's step number (tags of the cross-GPU exchange)
 };
 __shared__ CCtx cx;
 __shared__ unsigned long long lim_s;  // limit of every wait (ns)
@@ -154,6 +155,11 @@ __device__ __forceinline__ T* at(uint32_t off) {
 }
 __device__ __forceinline__ const mie_layer_desc& layer_at(int l) { return lay_s[l & (kLaySlots - 1)]; }
 __device__ __forceinline__ uint32_t tag_of(int l) { return (cx.step << 8) | (uint32_t)l; }
+// Tags of the cross-GPU exchange (expert parallel): the top bit keeps them
+// apart from the per-layer MoE kernels' call numbers in the same buffers.
+__device__ __forceinline__ uint32_t ptag_of(int l) {
+  return 0x80000000u | ((cx.pstep & 0x7fffffu) << 8) | (uint32_t)l;
+}
 __device__ __forceinline__ void split32(int total, int c, int g, int* b, int* e) {
   *b = (int)(((uint32_t)total * (uint32_t)c) / (uint32_t)g);
   *e = (int)(((uint32_t)total * (uint32_t)(c + 1)) / (uint32_t)g);
@@ -257,6 +263,73 @@ __device__ __forceinline__ int poll(const uint64_t* buf, int n, uint32_t tag, fl
 struct Ident {
   __device__ __forceinline__ int operator()(int i) const { return i; }
 };
+
+// ---------------------------------------------------------------------------
+// Expert parallel: exchange X across GPUs.  Every rank's down-row owners store
+// their rows of the rank's MoE partial (the contribution of the selected
+// experts it holds, 0 for the others) into slot [layer parity][rank] of every
+// rank's buffer; a reader sums the ranks' words of a row in rank order and
+// adds x_mid -- the combine of the per-layer expert-parallel path, so every
+// rank computes the same bits of x (and the same routing).
+//
+// Slot reuse: the layer outputs of all steps form one sequence (index
+// seq * L + l, seq the group's step counter before the step) and alternate
+// between the two slots along it, across step boundaries too.  Every rank
+// writes every row of every layer output, and a rank writes output n + 2 only
+// after it read output n + 1 completely -- whose words every other rank wrote
+// after all its CTAs had read output n (it needed their expert units).  So a
+// slot is rewritten only after every rank read it.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t pslot(int l) {
+  return ((cx.pstep - 1u) * (uint32_t)ps.d.num_layers + (uint32_t)l) & 1u;
+}
+__device__ __forceinline__ void peer_put(int l, int r, float y) {
+  const CGeom& g = ps.g;
+  const size_t o = ((size_t)pslot(l) * g.peer_world + g.peer_rank) * ps.d.hidden_dim + r;
+  const uint32_t t = ptag_of(l);
+#pragma unroll 1
+  for (int k = 0; k < g.peer_world; ++k) ll_put_sys(g.peer_bufs[k] + o, y, t);
+}
+
+// Rows a0 + i, i < n, of layer l's X from this GPU's buffer: dst[i] =
+// base[a0 + i] + (sum over ranks in rank order of the rank's word).  dst may
+// be base.  1 when this thread gave up.
+__device__ __noinline__ int poll_ranks(int l, int n, const float* base, float* dst, int a0) {
+  const CGeom& g = ps.g;
+  const int D = ps.d.hidden_dim, W = g.peer_world;
+  const uint64_t* buf = g.peer_bufs[g.peer_rank] + (size_t)pslot(l) * W * D;
+  const uint32_t tag = ptag_of(l);
+  unsigned long long t0 = 0;
+#pragma unroll 1
+  for (int i = threadIdx.x; i < n; i += kCT) {
+    const int a = a0 + i;
+    uint64_t w[MIE_PEER_MAX_RANKS];
+    unsigned need = 0;
+#pragma unroll
+    for (int k = 0; k < MIE_PEER_MAX_RANKS; ++k)
+      if (k < W) {
+        w[k] = ll_ld_sys(buf + (size_t)k * D + a);
+        need |= 1u << k;
+      }
+#pragma unroll 1
+    for (int it = 1;; ++it) {
+#pragma unroll
+      for (int k = 0; k < MIE_PEER_MAX_RANKS; ++k)
+        if ((need >> k & 1u) && ll_tag(w[k]) == tag) need &= ~(1u << k);
+      if (!need) break;
+#pragma unroll
+      for (int k = 0; k < MIE_PEER_MAX_RANKS; ++k)
+        if (need >> k & 1u) w[k] = ll_ld_sys(buf + (size_t)k * D + a);
+      if ((it & 63) == 0 && give_up(&t0)) return 1;
+    }
+    float s = 0.f;
+#pragma unroll
+    for (int k = 0; k < MIE_PEER_MAX_RANKS; ++k)
+      if (k < W) s += ll_val(w[k]);
+    dst[i] = base[a] + s;
+  }
+  return 0;
+}
 
 // A consumer warp: wait (bounded) for the next phase of full barrier b.
 // Every thread observes the phase itself (which also makes the staged bytes
@@ -387,8 +460,11 @@ __device__ __noinline__ void issue_kv(Side sd, int b, int l, int h, int ta, int 
 
 // The selected experts' rows of this CTA: gate rows then up rows of its units
 // -> region A (barrier A), down rows of its output rows, slot 0 then slot 1 ->
-// region D (barrier D).
-__device__ __noinline__ void issue_experts(Side sd, int l, int sel0, int sel1) {
+// region D (barrier D).  e0, e1: the slots' experts in this rank's weight
+// stack; with EP (expert parallel) -1 marks a slot held by another rank,
+// which stages nothing.
+template <bool EP>
+__device__ __noinline__ void issue_experts(Side sd, int l, int e0, int e1) {
   const mie_step_desc& d = ps.d;
   const CGeom& g = ps.g;
   const mie_layer_desc& ly = layer_at(l);
@@ -404,17 +480,18 @@ __device__ __noinline__ void issue_experts(Side sd, int l, int sel0, int sel1) {
     const uint8_t* w = static_cast<const uint8_t*>(m ? ly.w3 : ly.w1);
 #pragma unroll 1
     for (int k = 0; k < 2; ++k) {
-      const int ua = max(u0, k * Hx), ub = min(u1, (k + 1) * Hx);
-      if (ub > ua)
+      const int ua = max(u0, k * Hx), ub = min(u1, (k + 1) * Hx), e = k ? e1 : e0;
+      if (ub > ua && (!EP || e >= 0))
         stage(sd, at<uint8_t>(g.sm_a) + (size_t)(m * nu + ua - u0) * rbD,
-              w + ((size_t)(k ? sel1 : sel0) * Hx + ua - k * Hx) * rbD, (uint32_t)(ub - ua) * rbD, pol);
+              w + ((size_t)e * Hx + ua - k * Hx) * rbD, (uint32_t)(ub - ua) * rbD, pol);
     }
   }
   stage_done(sd, kFE);
 #pragma unroll 1
   for (int k = 0; k < 2; ++k)
-    stage(sd, at<uint8_t>(g.sm_d) + (size_t)k * nr * rbH,
-          static_cast<const uint8_t*>(ly.w2) + ((size_t)(k ? sel1 : sel0) * D + r0) * rbH, (uint32_t)nr * rbH, pol);
+    if (!EP || (k ? e1 : e0) >= 0)
+      stage(sd, at<uint8_t>(g.sm_d) + (size_t)k * nr * rbH,
+            static_cast<const uint8_t*>(ly.w2) + ((size_t)(k ? e1 : e0) * D + r0) * rbH, (uint32_t)nr * rbH, pol);
   stage_done(sd, kFD);
 }
 
@@ -771,6 +848,7 @@ __device__ __noinline__ bool att_core(bool ok, int l, int h, int t0, int t1, con
 // ---------------------------------------------------------------------------
 // ATT: attention of layer l for the attention clusters (see the file comment)
 // ---------------------------------------------------------------------------
+template <bool EP>
 __device__ __noinline__ bool att_phase(const CStepParams& P, int l, bool ok) {
   const mie_step_desc& d = ps.d;
   const CGeom& g = ps.g;
@@ -790,7 +868,9 @@ __device__ __noinline__ bool att_phase(const CStepParams& P, int l, bool ok) {
     csync();
   } else {
     int bad = 0;
-    if (ok) bad = poll(g.ll + g.off_x[par], D, tag, xs, Ident{});
+    if (ok)
+      bad = EP ? poll_ranks(l, D, at<const float>(g.sm_xm) + (size_t)((l - 1) & 1) * D, xs, 0)
+               : poll(g.ll + g.off_x[par], D, tag, xs, Ident{});
     ok = !csync_or(bad || !ok);
   }
   CSTAMP(l, 1);
@@ -920,6 +1000,7 @@ __device__ __noinline__ bool att_phase(const CStepParams& P, int l, bool ok) {
 // ---------------------------------------------------------------------------
 // MOE: x_mid, routing, the two selected experts, x of layer l + 1
 // ---------------------------------------------------------------------------
+template <bool EP>
 __device__ __noinline__ bool moe_phase(const CStepParams& P, int l, bool ok, bool att) {
   const mie_step_desc& d = ps.d;
   const CGeom& g = ps.g;
@@ -937,8 +1018,10 @@ __device__ __noinline__ bool moe_phase(const CStepParams& P, int l, bool ok, boo
   // ---- receive rows [r0, r0 + nr) of every head's partial (and of x) ----
   const int nr = a.nr, r0 = a.r0;
   const bool need_x = !att && l > 0;
+  constexpr bool ep = EP;
   {
-    const int n = H * nr + (need_x ? nr : 0);
+    // expert parallel: x's rows come from the cross-GPU exchange below
+    const int n = H * nr + (need_x && !ep ? nr : 0);
     const uint64_t* pb = g.ll + g.off_p[par];
     const int64_t xoff = g.off_x[par] - g.off_p[par];
     int bad = 0;
@@ -950,6 +1033,8 @@ __device__ __noinline__ bool moe_phase(const CStepParams& P, int l, bool ok, boo
         }
         return (int)xoff + r0 + (i - H * nr);
       });
+    if (ok && need_x && ep && !bad)
+      bad = poll_ranks(l, nr, at<const float>(g.sm_xm) + (size_t)((l - 1) & 1) * D, pr + (size_t)H * nr, r0);
     if (!att && l == 0) {
       const bf16* e = static_cast<const bf16*>(d.embedding) + cx.tok * D;
       for (int i = tid; i < nr; i += kCT) pr[H * nr + i] = __bfloat162float(e[r0 + i]);
@@ -1025,7 +1110,15 @@ __device__ __noinline__ bool moe_phase(const CStepParams& P, int l, bool ok, boo
   const float e1 = expf(cv - bv);
   const float wt0 = 1.0f / (1.0f + e1), wt1 = e1 / (1.0f + e1);
   CSTAMP(l, 30);
-  if (ok) issue_experts(cons_side(), l, sel0, sel1);
+  // the slots' experts in this rank's weight stack (expert parallel: -1 for
+  // a slot held by another rank)
+  int le0 = sel0, le1 = sel1;
+  if (EP) {
+    le0 = (unsigned)(sel0 - d.expert_base) < (unsigned)d.expert_count ? sel0 - d.expert_base : -1;
+    le1 = (unsigned)(sel1 - d.expert_base) < (unsigned)d.expert_count ? sel1 - d.expert_base : -1;
+  }
+  if (ok) issue_experts<EP>(cons_side(), l, le0, le1);
+  const unsigned held = EP ? (le0 >= 0 ? 1u : 0u) | (le1 >= 0 ? 2u : 0u) : 3u;  // the slots this rank computes
   csync();  // router rows and norm weights read: region R may be restaged
   region_free(kER);  // the producer stages the next layer's router + norms, or the final norm
   CSTAMP(l, 8);
@@ -1038,7 +1131,12 @@ __device__ __noinline__ bool moe_phase(const CStepParams& P, int l, bool ok, boo
   CSTAMP(l, 31);
   if (ok) gemv(at<const uint4>(g.sm_a), 2 * nu, nvD, xn, ab);
   csync();  // region A no longer read
-  if (ok && tid < nu) ll_put(g.ll + g.off_h[par] + u0 + tid, silu(ab[tid]) * ab[nu + tid], tag);
+  if (ok && tid < nu) {
+    float h = silu(ab[tid]) * ab[nu + tid];
+    // a slot held by another rank: its rows were not staged, its units are 0
+    if (EP && !(held >> (u0 + tid < Hx ? 0 : 1) & 1u)) h = 0.f;
+    ll_put(g.ll + g.off_h[par] + u0 + tid, h, tag);
+  }
   if (att && l + 1 < d.num_layers) region_free(kEA);  // the producer stages the next layer's q/k/v rows
   CSTAMP(l, 9);
   // ---- down rows of both slots . h + residual -> exchange X of layer l + 1 ----
@@ -1055,13 +1153,27 @@ __device__ __noinline__ bool moe_phase(const CStepParams& P, int l, bool ok, boo
   CSTAMP(l, 20);
   if (ok && tid < nq) {
     const int r = q0 + tid;
-    const float y = fmaf(wt1, ab[nq + tid], fmaf(wt0, ab[tid], xm[r]));
-    ll_put(g.ll + g.off_x[(l + 1) & 1] + r, y, tag_of(l + 1));
-    if (l == d.num_layers - 1) d.x[r] = y;
+    if constexpr (EP) {
+      // this rank's partial: its slots in slot order (the per-layer kernels'
+      // combine); the readers add x_mid
+      float y = 0.f;
+      if (held & 1u) y = fmaf(wt0, ab[tid], y);
+      if (held & 2u) y = fmaf(wt1, ab[nq + tid], y);
+      peer_put(l + 1, r, y);
+    } else {
+      const float y = fmaf(wt1, ab[nq + tid], fmaf(wt0, ab[tid], xm[r]));
+      ll_put(g.ll + g.off_x[(l + 1) & 1] + r, y, tag_of(l + 1));
+      if (l == d.num_layers - 1) d.x[r] = y;
+    }
   }
   // after the last layer the ring area is free (x_mid, read just above, lies
   // in it too): the producer starts the LM-head ring
   if (l == d.num_layers - 1) {
+    if (EP) {  // the head adds the ranks' partials to x_mid: keep it outside the ring
+      float* xs = at<float>(g.sm_x);
+#pragma unroll 1
+      for (int i = tid; i < D; i += kCT) xs[i] = xm[i];
+    }
     csync();
     region_free(kED);
   }
@@ -1091,10 +1203,12 @@ __device__ __noinline__ void head_finish(int bi) {
   }
   if (d.done && bi == d.eos_id) *d.done = 1;
   *d.lm_counter = 0u;
+  if (ps.g.peer_world > 1) *reinterpret_cast<volatile uint32_t*>(ps.g.peer_seq) = cx.pstep;
   __threadfence();
   asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(ps.g.ll + kHdrStep), "l"((uint64_t)cx.step) : "memory");
 }
 
+template <bool EP>
 __device__ __noinline__ bool head_phase(bool ok) {
   const mie_step_desc& d = ps.d;
   const CGeom& g = ps.g;
@@ -1106,8 +1220,12 @@ __device__ __noinline__ bool head_phase(bool ok) {
   CSTAMP(L, 0);
   {
     int bad = 0;
-    if (ok) bad = poll(g.ll + g.off_x[L & 1], D, tag_of(L), xs, Ident{});
+    if (ok) bad = EP ? poll_ranks(L, D, xs, xs, 0) : poll(g.ll + g.off_x[L & 1], D, tag_of(L), xs, Ident{});
     ok = !csync_or(bad || !ok);
+    if (EP && ok && c == 0) {  // x after the last layer (the row owners hold only their partials)
+#pragma unroll 1
+      for (int i = tid; i < D; i += kCT) d.x[i] = xs[i];
+    }
   }
   ok = bwait(ok, kFR);  // the final norm weights
   rms_norm(xn, xs, D, d.eps, at<const bf16>(g.sm_fn));
@@ -1286,6 +1404,9 @@ __device__ __noinline__ void producer(const CStepParams& P, bool att, bool ok) {
   }
 }
 
+// EP: expert parallel (ps.g.peer_world > 1), a separate instantiation so the
+// single-GPU step carries none of its code.
+template <bool EP>
 __global__ void __launch_bounds__(kT, 1) cstep_kernel(const __grid_constant__ CStepParams P) {
   CSTAMP(P.d.num_layers, 3);
   // under programmatic dependent launch the next step's CTAs may take the SMs
@@ -1344,6 +1465,7 @@ __global__ void __launch_bounds__(kT, 1) cstep_kernel(const __grid_constant__ CS
     int stop = done_v || (d.step_limit && d.log_count && lc >= lim);
     lim_s = d.wait_limit_ns > 0 ? (unsigned long long)d.wait_limit_ns : kWaitLimitNs;
     cx.step = (uint32_t)hstep + 1u;
+    cx.pstep = EP ? *reinterpret_cast<volatile const uint32_t*>(ps.g.peer_seq) + 1u : 0u;
     cx.log_k = lc;
     if (!stop && (p < 0 || p >= d.max_pos || t < 0 || t >= d.vocab)) {
       if (blockIdx.x == 0) set_status(d.status, MIE_ERR_RANGE);
@@ -1401,10 +1523,10 @@ __global__ void __launch_bounds__(kT, 1) cstep_kernel(const __grid_constant__ CS
   } else {
 #pragma unroll 1
     for (int l = 0; l < d.num_layers; ++l) {
-      if (att) ok = att_phase(P, l, ok);
-      ok = moe_phase(P, l, ok, att);
+      if (att) ok = att_phase<EP>(P, l, ok);
+      ok = moe_phase<EP>(P, l, ok, att);
     }
-    head_phase(ok);
+    head_phase<EP>(ok);
   }
   drain_copies();
 }
@@ -1425,7 +1547,20 @@ int cstep_geometry(const mie_step_desc& d, CGeom* out) {
   if (d.num_layers <= 0 || d.num_layers > kMaxStepLayers) return MIE_ERR_UNSUPPORTED;
   if (!d.rope_cos || !d.rope_sin || d.pos_embedding || d.lm_bias || d.final_norm_b) return MIE_ERR_UNSUPPORTED;
   if (d.sample_temperature > 0.f) return MIE_ERR_UNSUPPORTED;  // the device sampler runs on the flat step
-  if (d.moe_partial || (d.expert_count && d.expert_count != E) || d.expert_base) return MIE_ERR_UNSUPPORTED;
+  // expert parallel: the ranks' partials travel inside the step (moe_peer),
+  // never through moe_partial
+  const mie_peer_reduce_args* pr = d.moe_peer;
+  const bool ep = pr && pr->world > 1;
+  if (d.moe_partial) return MIE_ERR_UNSUPPORTED;
+  if (ep) {
+    if (pr->world > MIE_PEER_MAX_RANKS || pr->rank < 0 || pr->rank >= pr->world || pr->n != D || !pr->seq)
+      return MIE_ERR_INVALID;
+    for (int r = 0; r < pr->world; ++r)
+      if (!pr->bufs[r] || reinterpret_cast<uintptr_t>(pr->bufs[r]) % 8) return MIE_ERR_INVALID;
+    if (d.expert_count <= 0 || d.expert_base < 0 || d.expert_base + d.expert_count > E) return MIE_ERR_INVALID;
+  } else if ((d.expert_count && d.expert_count != E) || d.expert_base) {
+    return MIE_ERR_UNSUPPORTED;
+  }
   if (d.kv_stride_tok != kHd || (d.kv_stride_block * 2) % 16 || (d.kv_stride_head * 2) % 16)
     return MIE_ERR_UNSUPPORTED;
   for (int l = 0; l < d.num_layers; ++l) {
@@ -1513,6 +1648,13 @@ int cstep_geometry(const mie_step_desc& d, CGeom* out) {
     g.off_h[p] = take(2 * (int64_t)Hx);
   }
   g.words = off;
+  g.peer_world = 1;
+  if (ep) {
+    g.peer_rank = pr->rank;
+    g.peer_world = pr->world;
+    for (int r = 0; r < pr->world; ++r) g.peer_bufs[r] = pr->bufs[r];
+    g.peer_seq = pr->seq;
+  }
   return MIE_OK;
 }
 
@@ -1556,7 +1698,7 @@ int cstep_launch(const mie_step_desc& d, const CGeom& g, uint64_t* scratch, cuda
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = d.use_pdl ? 2 : 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, cstep_kernel, p);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, g.peer_world > 1 ? cstep_kernel<true> : cstep_kernel<false>, p);
   if (e != cudaSuccess) {
     note_cuda_error(e, "cudaLaunchKernelEx(cluster step)");
     return MIE_ERR_CUDA;
@@ -1568,7 +1710,8 @@ int cstep_launch(const mie_step_desc& d, const CGeom& g, uint64_t* scratch, cuda
 // clusters of the kernel the device holds at once with its largest shared
 // memory footprint.
 void cstep_set_attributes() {
-  set_max_smem(cstep_kernel);
+  set_max_smem(cstep_kernel<false>);
+  set_max_smem(cstep_kernel<true>);
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return;
   cudaLaunchConfig_t cfg = {};
@@ -1582,12 +1725,15 @@ void cstep_set_attributes() {
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  int n = 0;
-  const cudaError_t e = cudaOccupancyMaxActiveClusters(&n, cstep_kernel, &cfg);
+  // both instantiations must fit the grid: the smaller count of the two
+  int n = 0, n_ep = 0;
+  cudaError_t e = cudaOccupancyMaxActiveClusters(&n, cstep_kernel<false>, &cfg);
+  if (e == cudaSuccess) e = cudaOccupancyMaxActiveClusters(&n_ep, cstep_kernel<true>, &cfg);
   if (e != cudaSuccess) {
     note_cuda_error(e, "cudaOccupancyMaxActiveClusters(cluster step)");
     n = 0;
   }
+  if (n_ep < n) n = n_ep;
   std::lock_guard<std::mutex> lock(g_cluster_mutex);
   g_max_clusters[dev] = n;
 }

@@ -162,10 +162,14 @@ class DecodeRunner:
             L.k_cache, L.v_cache = k.data_ptr(), v.data_ptr()
         return arr
 
-    def make_desc(self, cache, *, logits: bool, graph: bool, splits: int, sample=(0.0, 0), limit: bool = False):
+    def make_desc(self, cache, *, logits: bool, graph: bool, splits: int, sample=(0.0, 0), limit: bool = False,
+                  moe_peer=None):
         """Step descriptor; ``sample`` = (temperature, top_k) selects the device
         sampler (persistent step only) instead of the greedy argmax; ``limit``
-        makes steps stop once ``log_count`` reaches ``step_limit``."""
+        makes steps stop once ``log_count`` reaches ``step_limit``;
+        ``moe_peer`` (the address of a ``capi.PeerReduceArgs``) makes the
+        persistent step expert parallel, its ranks' MoE partials summed inside
+        the step (``moe_partial`` is then not used)."""
         cfg, m = self.config, self.model
         w = m.token_embedding.weight
         d = capi.StepDesc()
@@ -213,7 +217,8 @@ class DecodeRunner:
         d.q = self.q.data_ptr()
         d.attn_out = self.attn_out.data_ptr()
         d.moe_hidden = self.moe_hidden.data_ptr()
-        d.moe_partial = capi.ptr(self.moe_partial)
+        d.moe_partial = None if moe_peer else capi.ptr(self.moe_partial)
+        d.moe_peer = moe_peer
         d.expert_base = self.expert_base
         d.expert_count = self.expert_count
         d.attn_partials = self.attn_partials.data_ptr()

@@ -15,20 +15,32 @@ those of the single-GPU path (src/moe_engine/model.py:543-565 with the MoE of
 src/moe_engine/fused_moe.py:312-380), with the expert sum split across ranks:
 sum_k w_k E_k(x) = sum_ranks sum_{k local} w_k E_k(x).
 
-Each step is launched layer by layer (``mie_decode_layer``, the all-reduce,
-``mie_decode_head``); the single-GPU persistent step kernel is not used here.
-``decode`` captures whole steps -- every layer's kernels and its
-all-reduce -- in a CUDA graph and replays it, so the host issues one graph
-launch per ``GRAPH_STEPS`` tokens instead of about fifty launches per token.
-By default (``collective="fused"``) each layer's MoE kernel completes the
-all-reduce of its partial itself: every CTA stores its output rows' partial as
-tagged fp32 words over NVLink into every rank's receive buffer, polls its own
-for the same rows and sums them in rank order.  ``collective="peer"`` runs the
-same exchange as a kernel of its own after the MoE kernel
-(``mie_peer_reduce``); ``collective="nccl"`` uses an NCCL all-reduce, whose
-partial travels as fp32 or, with
-``payload="bf16"``, as bf16 (half the bytes; the residual stream then differs
-from the single-GPU one by the bf16 rounding of each layer's MoE output).
+Collectives:
+
+* ``"step"``: each decode step is ONE launch of the persistent cluster step
+  kernel on every rank, which completes each layer's all-reduce inside the
+  kernel: the CTAs that own a layer's output rows store the rank's partial of
+  those rows as tagged fp32 words over NVLink into every rank's receive buffer,
+  and every CTA that reads the layer's output polls its own buffer and sums
+  the ranks' words in rank order onto x_mid.  Shapes of the cluster step only
+  (bf16, head_dim 64, RMSNorm, SwiGLU, no biases).
+* ``"fused"``: each step is launched layer by layer (``mie_decode_layer``,
+  ``mie_decode_head``) and each layer's MoE kernel completes the all-reduce of
+  its partial itself, with the same tagged words.
+* ``"peer"``: layer by layer, the same exchange as a kernel of its own after
+  the MoE kernel (``mie_peer_reduce``).
+* ``"nccl"``: layer by layer, an NCCL all-reduce, whose partial travels as fp32
+  or, with ``payload="bf16"``, as bf16 (half the bytes; the residual stream
+  then differs from the single-GPU one by the bf16 rounding of each layer's
+  MoE output).
+* ``"auto"`` (default): ``"step"`` when the cluster step takes the model's
+  shapes, else ``"fused"``.
+
+``decode`` captures the steps in CUDA graphs (``GRAPH_STEPS`` steps per graph)
+and replays them, so the host issues one graph launch per ``GRAPH_STEPS``
+tokens.  Every rank must make the same calls in the same order.  After a
+device failure (``KernelError``) the ranks' exchange state may disagree:
+``close`` the decoder on every rank and make a new one.
 """
 
 from __future__ import annotations
@@ -129,12 +141,14 @@ class ExpertParallelDecoder:
     ``payload`` is the all-reduced partial's type: "fp32" or "bf16".
     """
 
+    COLLECTIVES = ("auto", "step", "fused", "peer", "nccl")
+
     def __init__(self, model, group=None, payload: str = "fp32", use_graph: bool = True,
-                 collective: str = "fused"):
+                 collective: str = "auto"):
         if payload not in ("fp32", "bf16"):
             raise ValueError(f"payload must be fp32 or bf16, not {payload!r}")
-        if collective not in ("fused", "peer", "nccl"):
-            raise ValueError(f"collective must be fused, peer or nccl, not {collective!r}")
+        if collective not in self.COLLECTIVES:
+            raise ValueError(f"collective must be one of {', '.join(self.COLLECTIVES)}, not {collective!r}")
         if collective != "nccl" and payload != "fp32":
             raise ValueError("the peer all-reduce carries fp32 partials")
         self.model = model
@@ -152,8 +166,32 @@ class ExpertParallelDecoder:
                       if payload == "bf16" else None)
         self._peer = (PeerReducer(cfg.hidden_dim, group, self.runner.device, status=self.runner.status,
                                   wait_limit_ns=getattr(self.runner, "wait_limit_ns", 0))
-                      if collective in ("fused", "peer") else None)
+                      if collective != "nccl" else None)
         self._graphs: dict = {}
+        self.active = None  # the collective the last decode ran
+
+    def _step_desc(self, cache, max_ctx: int):
+        """Descriptor of the expert-parallel persistent step for ``cache``, or
+        (None, None) when the cluster step does not take the shapes."""
+        r = self.runner
+        if not r.persistent:
+            return None, None
+        _, _, _, _, bs, _, _ = cache_geometry(cache, 0)
+        desc, layers = r.make_desc(cache, logits=False, graph=True, splits=r.splits_for(max_ctx, bs), limit=True,
+                                   moe_peer=ctypes.addressof(self._peer._args))
+        if not desc.step_scratch:
+            return None, None
+        return desc, layers
+
+    def collective_for(self, cache, max_ctx: int) -> str:
+        """The collective ``decode`` runs for ``cache`` ("auto" resolved)."""
+        if self.collective in ("auto", "step"):
+            if self._step_desc(cache, max_ctx)[0] is not None:
+                return "step"
+            if self.collective == "step":
+                raise ValueError("the persistent cluster step does not take this model's shapes")
+            return "fused"
+        return self.collective
 
     def _desc(self, cache, max_ctx: int):
         _, _, _, _, bs, _, _ = cache_geometry(cache, 0)
@@ -183,6 +221,31 @@ class ExpertParallelDecoder:
             capi.check(lib.mie_decode_layer(ctypes.byref(desc), layer, stream), "mie_decode_layer")
             self._all_reduce()
         capi.check(lib.mie_decode_head(ctypes.byref(desc), stream), "mie_decode_head")
+
+    def _step_graph(self, cache, max_ctx: int):
+        """A CUDA graph of GRAPH_STEPS launches of the expert-parallel
+        persistent step (each stops once ``log_count`` reaches ``step_limit``),
+        captured on first use for this cache."""
+        _, _, _, _, bs, _, _ = cache_geometry(cache, 0)
+        k0 = cache_geometry(cache, 0)[0]
+        table = getattr(cache, "block_table_device", None)
+        key = ("step", k0.data_ptr(), None if table is None else table.data_ptr(), self.runner.splits_for(max_ctx, bs))
+        hit = self._graphs.get(key)
+        if hit is not None:
+            return hit[0]
+        desc, layers = self._step_desc(cache, max_ctx)
+        r = self.runner
+        r.done.fill_(1)  # warm-up: every CTA skips the step, no rank exchanges anything
+        r.pos.zero_()
+        r.launch_step(desc)
+        torch.cuda.synchronize(r.device)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for _ in range(GRAPH_STEPS):
+                capi.check(r.lib.mie_decode_step(ctypes.byref(desc), capi.stream_handle(r.device)),
+                           "mie_decode_step (capture)")
+        self._graphs[key] = (g, desc, layers)
+        return g
 
     def _graph(self, cache, max_ctx: int):
         """A CUDA graph of GRAPH_STEPS decode steps (kernels and all-reduces),
@@ -245,13 +308,31 @@ class ExpertParallelDecoder:
         P = cache.position
         if hasattr(cache, "allocator"):
             cache.reserve(P + steps)
-        graph = self._graph(cache, P + steps) if self.use_graph and steps % GRAPH_STEPS == 0 else None
-        desc, layers = self._desc(cache, P + steps)
+        active = self.collective_for(cache, P + steps)
+        if self.active is not None and active != self.active:
+            # the collectives share the receive buffers: no rank may still
+            # read words of the previous one
+            dist.barrier(self.group)
+        self.active = active
+        if self.active == "step":
+            graph = self._step_graph(cache, P + steps) if self.use_graph else None
+            desc, layers = self._step_desc(cache, P + steps)
+        else:
+            graph = self._graph(cache, P + steps) if self.use_graph and steps % GRAPH_STEPS == 0 else None
+            desc, layers = self._desc(cache, P + steps)
         r.token.fill_(first)
         r.pos.fill_(P)
         r.done.zero_()
         r.log_count.zero_()
-        if graph is not None:
+        r.step_limit.fill_(steps)
+        if self.active == "step":
+            if graph is not None:
+                for _ in range(-(-steps // GRAPH_STEPS)):
+                    graph.replay()
+            else:
+                for _ in range(steps):
+                    r.launch_step(desc)
+        elif graph is not None:
             for _ in range(steps // GRAPH_STEPS):
                 graph.replay()
         else:

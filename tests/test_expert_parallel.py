@@ -9,6 +9,11 @@ output completed by an all-reduce of per-rank partials.
   single-GPU path with each collective -- the all-reduce fused into the MoE
   kernel, the peer all-reduce kernel, NCCL; the peer all-reduce alone is
   bitwise the rank-order sum, eager and in a CUDA graph.
+* GPU (2 ranks): the expert-parallel persistent step (collective "step", the
+  all-reduce inside the single-launch cluster step) on the BASELINE model in
+  bf16 gives the single-GPU persistent step's greedy tokens for two requests
+  on one decoder (graphs of several steps, a step limit that ends mid-graph),
+  and hidden states equal to rounding.
 """
 
 import os
@@ -195,3 +200,68 @@ def test_peer_all_reduce_sums_in_rank_order_eager_and_in_a_graph():
         p.join(timeout=120)
         assert p.exitcode == 0
     assert errs == 0 and status == 0
+
+
+def _ep_step_worker(rank, world, port, out):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    import datetime
+
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=dev)
+    try:
+        from moe_engine.expert_parallel import ExpertParallelDecoder
+        from tests.helpers import baseline_bf16_model
+
+        m, _, _ = baseline_bf16_model(max_seq=1024, device=dev)
+        alloc = m.new_block_allocator(num_blocks=80, block_size=16, attention_mode="direct")
+        prompts = [torch.randint(0, 50304, (n,), generator=torch.Generator().manual_seed(40 + n)) for n in (24, 300)]
+        lengths = (40, 33)  # 33: the last graph of 8 steps ends after one step
+        got, xs = [], []
+        ep = ExpertParallelDecoder(m)  # "auto": the persistent step takes these shapes
+        try:
+            for prompt, n in zip(prompts, lengths):
+                cache = alloc.new_cache()
+                got.append(ep.generate(prompt, n, cache)[0].tolist())
+                ep.runner.check_status()
+                xs.append(ep.runner.x.cpu())
+                cache.free()
+            active = ep.active
+            seq = int(ep._peer.seq.item())
+        finally:
+            ep.close()
+        if rank == 0:
+            single, xs1 = [], []
+            for prompt, n in zip(prompts, lengths):
+                single.append(m.generate(prompt, max_new_tokens=n, temperature=0)[0].tolist())
+                xs1.append(m.decode_runner().x.cpu())
+            out.put((active, seq, got, single, xs, xs1, m.decode_runner().step_kernel_for(alloc.new_cache())))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="expert parallel needs 2 GPUs")
+def test_expert_parallel_persistent_step_matches_single_gpu_step():
+    from moe_engine import capi
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    procs = [ctx.Process(target=_ep_step_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    active, seq, got, single, xs, xs1, kernel = q.get(timeout=600)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert kernel == capi.MIE_STEP_CLUSTER
+    assert active == "step"
+    # one advance of the group's step counter per decoded token after the first
+    assert seq == (40 - 1) + (33 - 1)
+    for g, s, a, b in zip(got, single, xs, xs1):
+        assert g == s
+        rel = float((a - b).norm() / b.norm())
+        assert rel < 1e-3, rel
