@@ -367,10 +367,22 @@ typedef struct mie_step_desc {
    * one-CTA-per-SM kernel; the other two force one (MIE_ERR_UNSUPPORTED when
    * the forced kernel cannot take the shapes). */
   int step_kernel;
-  /* Expert parallel, per-layer launch sequence: when non-NULL (a host
-   * pointer, read at launch), each layer's MoE kernel completes the
-   * all-reduce of its partial itself over these peer buffers (see the peer_*
-   * fields of mie_moe_args), so moe_partial receives the sum over ranks. */
+  /* Expert parallel over the ranks of mie_peer_reduce_args (a host pointer,
+   * read at launch; n = hidden_dim; in, out and status unused):
+   * - per-layer launch sequence (moe_partial set): each layer's MoE kernel
+   *   completes the all-reduce of its partial itself over these peer
+   *   buffers (see the peer_* fields of mie_moe_args), so moe_partial
+   *   receives the sum over ranks;
+   * - persistent step (step_scratch set, moe_partial NULL, world > 1; the
+   *   cluster kernel only): the layers' weights hold experts
+   *   [expert_base, expert_base + expert_count); the step computes the
+   *   selected experts among them and completes every layer's all-reduce
+   *   inside the kernel -- the rank's partial of each output row is stored
+   *   into every rank's buffer, every reader sums the ranks' words in rank
+   *   order onto x_mid.  Every rank runs the same steps on the same token;
+   *   *seq advances once per step.  A wait for a peer's words gives up after
+   *   wait_limit_ns (MIE_ERR_TIMEOUT); the ranks' exchange state then
+   *   differs, so the group makes new buffers and a new counter. */
   const struct mie_peer_reduce_args* moe_peer;
 } mie_step_desc;
 

@@ -308,12 +308,7 @@ class ExpertParallelDecoder:
         P = cache.position
         if hasattr(cache, "allocator"):
             cache.reserve(P + steps)
-        active = self.collective_for(cache, P + steps)
-        if self.active is not None and active != self.active:
-            # the collectives share the receive buffers: no rank may still
-            # read words of the previous one
-            dist.barrier(self.group)
-        self.active = active
+        self.active = self.collective_for(cache, P + steps)
         if self.active == "step":
             graph = self._step_graph(cache, P + steps) if self.use_graph else None
             desc, layers = self._step_desc(cache, P + steps)
@@ -325,6 +320,11 @@ class ExpertParallelDecoder:
         r.done.zero_()
         r.log_count.zero_()
         r.step_limit.fill_(steps)
+        # Every rank's steps start together: a rank still capturing or
+        # allocating would otherwise keep the others' first bounded waits on
+        # its words running, and no rank still reads words of an earlier
+        # decode (the collectives share the receive buffers).
+        dist.barrier(self.group)
         if self.active == "step":
             if graph is not None:
                 for _ in range(-(-steps // GRAPH_STEPS)):
