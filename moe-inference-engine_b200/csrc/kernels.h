@@ -109,8 +109,8 @@ struct CGeom {
   // fp32 vectors: x, normalised x, x_mid [2][D], x_mid square sums [2][CS],
   // gathered q / k_new / v_new [2][3][hd], merge partials [2][CS][hd + 4],
   // own q/k/v GEMV results, scores, scratch, expert hidden [2 Hx], received
-  // partials [H + 1][orows], merged o [hd]
-  uint32_t sm_x, sm_xn, sm_xm, sm_ss, sm_g, sm_mg, sm_qkv, sm_sc, sm_ab, sm_h, sm_pr, sm_ov;
+  // partials [H + 1][orows], merged o [hd], router partials [2][CS][E]
+  uint32_t sm_x, sm_xn, sm_xm, sm_ss, sm_g, sm_mg, sm_qkv, sm_sc, sm_ab, sm_h, sm_pr, sm_ov, sm_rp;
   uint32_t sm_fn;  // final norm weights
   uint32_t smem;
   // expert parallel (peer_world > 1): this rank, every rank's exchange buffer

@@ -1012,6 +1012,7 @@ __device__ __noinline__ bool moe_phase(const CStepParams& P, int l, bool ok, boo
   float* xn = at<float>(g.sm_xn);
   float* xm = at<float>(g.sm_xm) + (size_t)par * D;
   float* ssb = at<float>(g.sm_ss) + (size_t)par * kCS;
+  float* rps = at<float>(g.sm_rp) + (size_t)par * kCS * E;  // [CS][E] router partials
   float* pr = at<float>(g.sm_pr);  // [H][nr] partials, then [nr] x rows (non-attention CTAs)
   float* ab = at<float>(g.sm_ab);
   float* hb = at<float>(g.sm_h);
@@ -1042,17 +1043,25 @@ __device__ __noinline__ bool moe_phase(const CStepParams& P, int l, bool ok, boo
     ok = !csync_or(bad || !ok);
   }
   CSTAMP(l, 26);
-  // ---- x_mid rows and their square sum -> every CTA of the cluster ----
+  // ---- x_mid rows, their square sum and their router partials -> every CTA of the cluster ----
+  // The router logit of expert e is rs * sum_i (x_mid_i * nw_i) * w_e,i with
+  // rs the RMSNorm scale: each CTA sends the partial dots of its rows, and
+  // routing right after the cluster barrier needs no pass over D.
+  if (!att) ok = bwait(ok, kFR);  // router rows + norm weights (the attention CTAs waited already)
+  const bf16* rw = at<const bf16>(g.sm_r);
+  const bf16* nw = rw + (size_t)(E + 1) * D;
   float v = 0.f;
   if (tid < nr) {
     v = att ? xs[r0 + tid] : pr[H * nr + tid];
 #pragma unroll 1
     for (int h = 0; h < H; ++h) v += pr[h * nr + tid];
+    ab[tid] = v * __bfloat162float(nw[r0 + tid]);
   }
   float s2 = warp_sum(v * v);  // rows beyond nr contribute 0
   if ((tid & 31) == 0) red_s[tid >> 5] = s2;
   csync();
   if (ok) {
+    const int warp = tid >> 5, lane = tid & 31;
     if (tid < nr) {
 #pragma unroll 1
       for (int r = 0; r < kCS; ++r) dsmem_st(dsmem_addr(xm + r0 + tid, (uint32_t)r), v);
@@ -1062,26 +1071,30 @@ __device__ __noinline__ bool moe_phase(const CStepParams& P, int l, bool ok, boo
       for (int i = 0; i < kCW; ++i) t += red_s[i];
       dsmem_st(dsmem_addr(ssb + a.s, (uint32_t)(tid - (kCT - 32))), t);
     }
+    // router partials of this CTA's rows: expert e on warp kCW - 1 - e (mod
+    // kCW), away from the row senders of the low warps
+#pragma unroll 1
+    for (int e = kCW - 1 - warp; e < E; e += kCW) {
+      const bf16* we = rw + (size_t)e * D + r0;
+      float p = 0.f;
+#pragma unroll 1
+      for (int i = lane; i < nr; i += 32) p = fmaf(ab[i], __bfloat162float(we[i]), p);
+      p = warp_sum(p);
+      if (lane < kCS) dsmem_st(dsmem_addr(rps + a.s * E + e, (uint32_t)lane), p);
+    }
   }
   CSTAMP(l, 27);
-  cluster_sync_all();  // cluster barrier 3: x_mid complete in every CTA
+  cluster_sync_all();  // cluster barrier 3: x_mid and the router partials complete in every CTA
   CSTAMP(l, 7);
-  // ---- RMSNorm (square sums of the cluster's shares, in rank order), router, top-2 ----
-  if (!att) ok = bwait(ok, kFR);
-  const bf16* rw = at<const bf16>(g.sm_r);
+  // ---- routing: RMSNorm scale and logits from the cluster's shares, in rank order; top-2 ----
+  float rs;
   {
     float t = 0.f;
 #pragma unroll
     for (int s = 0; s < kCS; ++s) t += ssb[s];
-    const float rs = rsqrtf(t / (float)D + d.eps);
-    const bf16* nw = rw + (size_t)(E + 1) * D;
-#pragma unroll 1
-    for (int i = tid; i < D; i += kCT) xn[i] = (xm[i] * rs) * __bfloat162float(nw[i]);
+    rs = rsqrtf(t / (float)D + d.eps);
   }
-  csync();
   CSTAMP(l, 28);
-  if (ok) gemv(reinterpret_cast<const uint4*>(rw), E, nvD, xn, ab);
-  csync();
   CSTAMP(l, 29);
   // top-2 in registers, every thread: scanning ascending ids with strict
   // comparisons keeps the lower id on ties -- the repeated argmax of the
@@ -1090,8 +1103,14 @@ __device__ __noinline__ bool moe_phase(const CStepParams& P, int l, bool ok, boo
   float bv = -INFINITY, cv = -INFINITY;
 #pragma unroll 1
   for (int e0 = 0; e0 < E; e0 += 4) {
-    const float4 q4 = *reinterpret_cast<const float4*>(ab + e0);
-    const float v4[4] = {q4.x, q4.y, q4.z, q4.w};
+    float v4[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float q = 0.f;
+#pragma unroll
+      for (int s = 0; s < kCS; ++s) q += rps[s * E + min(e0 + j, E - 1)];
+      v4[j] = rs * q;
+    }
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int e = e0 + j;
@@ -1119,7 +1138,10 @@ __device__ __noinline__ bool moe_phase(const CStepParams& P, int l, bool ok, boo
   }
   if (ok) issue_experts<EP>(cons_side(), l, le0, le1);
   const unsigned held = EP ? (le0 >= 0 ? 1u : 0u) | (le1 >= 0 ? 2u : 0u) : 3u;  // the slots this rank computes
-  csync();  // router rows and norm weights read: region R may be restaged
+  // the normalised x_mid for the up GEMV, while the expert rows are in flight
+#pragma unroll 1
+  for (int i = tid; i < D; i += kCT) xn[i] = (xm[i] * rs) * __bfloat162float(nw[i]);
+  csync();  // router rows and norm weights read: region R may be restaged; xn complete
   region_free(kER);  // the producer stages the next layer's router + norms, or the final norm
   CSTAMP(l, 8);
   // ---- up units: silu(gate) * up -> exchange H ----
@@ -1619,7 +1641,8 @@ int cstep_geometry(const mie_step_desc& d, CGeom* out) {
   g.sm_pr = stake((uint32_t)(H + 1) * g.orows * 4u);
   g.sm_ov = stake((kHd + 4) * 4u);
   // the LM head's vectors and the final norm weights after the ring
-  const uint32_t tail = 4u * D * 2u + 2u * D + 4u * (uint32_t)max(kT, max(E, 2 * g.nu_max)) + 8u * kCS + 5u * 128u;
+  const uint32_t tail = 4u * D * 2u + 2u * D + 4u * (uint32_t)max(kT, max(E, 2 * g.nu_max)) + 8u * kCS +
+                        8u * kCS * (uint32_t)E + 6u * 128u;
   if (so + tail > kStepMaxSmem) return MIE_ERR_UNSUPPORTED;
   so = kStepMaxSmem - tail;  // the ring takes whatever shared memory is left
   g.sm_fn = stake(2u * D);
@@ -1627,6 +1650,7 @@ int cstep_geometry(const mie_step_desc& d, CGeom* out) {
   g.sm_xn = stake(4u * D);
   g.sm_ab = stake(4u * (uint32_t)max(kT, max(E, 2 * g.nu_max)));
   g.sm_ss = stake(8u * kCS);
+  g.sm_rp = stake(8u * kCS * (uint32_t)E);
   g.smem = (so + 127) & ~127u;
   if (g.smem > kStepMaxSmem) return MIE_ERR_UNSUPPORTED;
   // LM-head ring over [sm_k, sm_fn): stages of four rows per consumer warp
