@@ -707,24 +707,6 @@ __device__ __noinline__ void gemv(const uint4* rows, int n, int nvec, const floa
   }
 }
 
-// RMSNorm of D fp32 values: out = in * rsqrt(mean(in^2) + eps) * w (w bf16 in
-// shared memory); the sum of squares in a fixed order.  Ends with a barrier.
-__device__ __noinline__ void rms_norm(float* out, const float* in, int D, float eps, const bf16* w) {
-  float s2 = 0.f;
-#pragma unroll 1
-  for (int i = threadIdx.x; i < D; i += kCT) s2 = fmaf(in[i], in[i], s2);
-  s2 = warp_sum(s2);
-  if ((threadIdx.x & 31) == 0) red_s[threadIdx.x >> 5] = s2;
-  csync();
-  float t = 0.f;
-#pragma unroll
-  for (int i = 0; i < kCW; ++i) t += red_s[i];
-  const float rs = rsqrtf(t / (float)D + eps);
-#pragma unroll 1
-  for (int i = threadIdx.x; i < D; i += kCT) out[i] = (in[i] * rs) * __bfloat162float(w[i]);
-  csync();
-}
-
 // Online softmax of q over this split's old tokens [t0, t1) in chunks of
 // chunk_tok (the first chunk was staged ahead).  Leaves (acc [hd], m, l) at
 // `res` (acc, then m, l).  q fp32 in shared memory.
@@ -860,23 +842,43 @@ __device__ __noinline__ bool att_phase(const CStepParams& P, int l, bool ok) {
   float* xs = at<float>(g.sm_x);
   float* xn = at<float>(g.sm_xn);
   CSTAMP(l, 0);
+  ok = bwait(ok, kFR);  // the layer's norm weights (and router)
+  CSTAMP(l, 12);
   // ---- x: the token embedding (layer 0) or exchange X ----
+  // RMSNorm folded in: the thread that received element i forms x_i * nw_i
+  // and its share of the square sum (the poll gives thread t the elements
+  // t, t + kCT, ...), so the block sum needs no barrier of its own; the
+  // q/k/v GEMV runs on x * nw and its results are scaled by rs.
+  int bad = 0;
   if (l == 0) {
     const bf16* e = static_cast<const bf16*>(d.embedding) + cx.tok * D;
 #pragma unroll 1
     for (int i = tid; i < D; i += kCT) xs[i] = __bfloat162float(e[i]);
-    csync();
-  } else {
-    int bad = 0;
-    if (ok)
-      bad = EP ? poll_ranks(l, D, at<const float>(g.sm_xm) + (size_t)((l - 1) & 1) * D, xs, 0)
-               : poll(g.ll + g.off_x[par], D, tag, xs, Ident{});
-    ok = !csync_or(bad || !ok);
+  } else if (ok) {
+    bad = EP ? poll_ranks(l, D, at<const float>(g.sm_xm) + (size_t)((l - 1) & 1) * D, xs, 0)
+             : poll(g.ll + g.off_x[par], D, tag, xs, Ident{});
+  }
+  {
+    const bf16* nw = at<const bf16>(g.sm_r) + (size_t)d.num_experts * D;
+    float s2 = 0.f;
+#pragma unroll 1
+    for (int i = tid; i < D; i += kCT) {
+      const float x = xs[i];
+      s2 = fmaf(x, x, s2);
+      xn[i] = x * __bfloat162float(nw[i]);
+    }
+    s2 = warp_sum(s2);
+    if ((tid & 31) == 0) red_s[tid >> 5] = s2;
+  }
+  ok = !csync_or(bad || !ok);
+  float rs;
+  {
+    float t = 0.f;
+#pragma unroll
+    for (int i = 0; i < kCW; ++i) t += red_s[i];
+    rs = rsqrtf(t / (float)D + d.eps);
   }
   CSTAMP(l, 1);
-  ok = bwait(ok, kFR);  // the layer's norm weights (and router)
-  CSTAMP(l, 12);
-  rms_norm(xn, xs, D, d.eps, at<const bf16>(g.sm_r) + (size_t)d.num_experts * D);
   // ---- this split's q, k, v rows ----
   ok = bwait(ok, kFQ);
   CSTAMP(l, 14);
@@ -895,14 +897,14 @@ __device__ __noinline__ bool att_phase(const CStepParams& P, int l, bool ok) {
     float v1 = 0.f, v2 = 0.f;
     if (tid < a.np) {  // q pair
       const int i = a.p0 + tid;
-      const float x1 = qo[tid], x2 = qo[a.np + tid];
+      const float x1 = qo[tid] * rs, x2 = qo[a.np + tid] * rs;
       v1 = x1 * cs[i] - x2 * sn[i];
       v2 = x2 * cs[i] + x1 * sn[i];
       dim = i;
       dim2 = i + kHd / 2;
     } else if (tid >= 64 && tid < 64 + a.np) {  // k pair: rounded to the cache type, stored
       const int k = tid - 64, i = a.p0 + k;
-      const float x1 = qo[2 * a.np + k], x2 = qo[3 * a.np + k];
+      const float x1 = qo[2 * a.np + k] * rs, x2 = qo[3 * a.np + k] * rs;
       const bf16 k1 = __float2bfloat16_rn(x1 * cs[i] - x2 * sn[i]);
       const bf16 k2 = __float2bfloat16_rn(x2 * cs[i] + x1 * sn[i]);
       bf16* kc = static_cast<bf16*>(ly.k_cache);
@@ -914,7 +916,7 @@ __device__ __noinline__ bool att_phase(const CStepParams& P, int l, bool ok) {
       dim2 = kHd + i + kHd / 2;
     } else if (tid >= 128 && tid < 128 + a.nv) {  // v row
       const int k = tid - 128, i = a.v0 + k;
-      const bf16 vv = __float2bfloat16_rn(qo[4 * a.np + k]);
+      const bf16 vv = __float2bfloat16_rn(qo[4 * a.np + k] * rs);
       static_cast<bf16*>(ly.v_cache)[slot + i] = vv;
       v1 = __bfloat162float(vv);
       dim = 2 * kHd + i;
@@ -1240,17 +1242,33 @@ __device__ __noinline__ bool head_phase(bool ok) {
   float* xn = at<float>(g.sm_xn);
   float* ab = at<float>(g.sm_ab);
   CSTAMP(L, 0);
+  ok = bwait(ok, kFR);  // the final norm weights
+  // the final RMSNorm folded into the receive as in the attention phase: the
+  // LM-head GEMV runs on x * w, its logits are scaled by rs
+  float rs;
   {
     int bad = 0;
     if (ok) bad = EP ? poll_ranks(L, D, xs, xs, 0) : poll(g.ll + g.off_x[L & 1], D, tag_of(L), xs, Ident{});
+    const bf16* fw = at<const bf16>(g.sm_fn);
+    float s2 = 0.f;
+#pragma unroll 1
+    for (int i = tid; i < D; i += kCT) {
+      const float x = xs[i];
+      s2 = fmaf(x, x, s2);
+      xn[i] = x * __bfloat162float(fw[i]);
+    }
+    s2 = warp_sum(s2);
+    if ((tid & 31) == 0) red_s[tid >> 5] = s2;
     ok = !csync_or(bad || !ok);
     if (EP && ok && c == 0) {  // x after the last layer (the row owners hold only their partials)
 #pragma unroll 1
       for (int i = tid; i < D; i += kCT) d.x[i] = xs[i];
     }
+    float t = 0.f;
+#pragma unroll
+    for (int i = 0; i < kCW; ++i) t += red_s[i];
+    rs = rsqrtf(t / (float)D + d.eps);
   }
-  ok = bwait(ok, kFR);  // the final norm weights
-  rms_norm(xn, xs, D, d.eps, at<const bf16>(g.sm_fn));
   CSTAMP(L, 1);
   int v0, v1;
   split32(d.vocab, c, G, &v0, &v1);
@@ -1266,7 +1284,7 @@ __device__ __noinline__ bool head_phase(bool ok) {
     csync();  // stage no longer read, ab complete
     if (i + g.head_stages < nst) region_free(kEH + slot);  // the producer refills the slot
     if (tid < n) {
-      const float v = ab[tid];
+      const float v = ab[tid] * rs;
       const int row = r0 + tid;
       if (d.logits) d.logits[row] = v;
       if (better(v, row, best_v, best_i)) {
