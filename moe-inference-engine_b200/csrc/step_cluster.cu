@@ -1097,34 +1097,44 @@ __device__ __noinline__ bool moe_phase(const CStepParams& P, int l, bool ok, boo
     rs = rsqrtf(t / (float)D + d.eps);
   }
   CSTAMP(l, 28);
-  CSTAMP(l, 29);
-  // top-2 in registers, every thread: scanning ascending ids with strict
-  // comparisons keeps the lower id on ties -- the repeated argmax of the
-  // reference's router (src/moe_engine/fused_moe.py:143-150)
-  int sel0 = 0, sel1 = 1;
-  float bv = -INFINITY, cv = -INFINITY;
-#pragma unroll 1
-  for (int e0 = 0; e0 < E; e0 += 4) {
-    float v4[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
+  // top-2 in every warp, one expert per lane (E <= 32): lane e holds expert
+  // e's logit (the cluster's partials summed in rank order, times rs; NaN
+  // ranks as -inf).  (value, lower id) is a total order, so the butterfly
+  // gives every lane the same answer: the maximum with ties to the lower id,
+  // then the maximum of the others with ties to the lower id -- the repeated
+  // argmax of the reference's router (src/moe_engine/fused_moe.py:143-150).
+  int sel0, sel1;
+  float bv, cv;
+  {
+    const int lane = tid & 31;
+    float lv = -INFINITY;
+    if (lane < E) {
       float q = 0.f;
 #pragma unroll
-      for (int s = 0; s < kCS; ++s) q += rps[s * E + min(e0 + j, E - 1)];
-      v4[j] = rs * q;
+      for (int s = 0; s < kCS; ++s) q += rps[s * E + lane];
+      lv = rs * q;
+      if (lv != lv) lv = -INFINITY;
     }
+    bv = lv;
+    sel0 = lane;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int e = e0 + j;
-      const float x = e < E ? v4[j] : -INFINITY;
-      if (x > bv) {
-        cv = bv;
-        sel1 = sel0;
-        bv = x;
-        sel0 = e;
-      } else if (x > cv) {
-        cv = x;
-        sel1 = e;
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, sel0, o);
+      if (better(ov, oi, bv, sel0)) {
+        bv = ov;
+        sel0 = oi;
+      }
+    }
+    cv = lane == sel0 ? -INFINITY : lv;
+    sel1 = lane == sel0 ? 64 : lane;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, cv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, sel1, o);
+      if (better(ov, oi, cv, sel1)) {
+        cv = ov;
+        sel1 = oi;
       }
     }
   }
