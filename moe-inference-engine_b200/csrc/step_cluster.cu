@@ -31,13 +31,19 @@
 //       of out_proj . o)
 //   MOE (every cluster)
 //     CTA s receives rows share s of P (every head) and of x, sums them
-//       (x_mid = x + sum_h P[h]) and sends its rows and their square sum to
-//       every CTA of the cluster -- cluster barrier 3
-//     RMSNorm -> router -> top-2 (ties to the lower id) -> 2-way softmax
-//     the selected experts' gate/up rows of this CTA's units and down rows of
-//       its output rows are bulk-copied into shared memory
+//       (x_mid = x + sum_h P[h]) and sends its rows, their square sum and
+//       their router partial dots (x_mid * norm w) . router row e to every
+//       CTA of the cluster -- cluster barrier 3
+//     routing from the cluster's shares: RMSNorm scale, logits, top-2 (ties
+//       to the lower id), 2-way softmax -- computed by every consumer warp
+//       and by the producer warp, which bulk-copies the selected experts'
+//       gate/up rows of this CTA's units and down rows of its output rows
+//       into shared memory while the consumers normalise x_mid
 //     up units: silu(gate) * up -> exchange H
 //     down rows of both slots . h + residual -> exchange X of layer l + 1
+//
+// The RMSNorms before the q/k/v rows and the LM head are folded into the
+// receive of x: the GEMVs run on x * w and their results are scaled by rs.
 //
 // HEAD: x_L -> final norm -> this CTA's tied LM-head rows (a ring of bulk
 // copies) -> argmax -> the last CTA reduces the CTA results and does the
@@ -91,10 +97,11 @@ constexpr int kMg = kHd + 4;          // merge partial: acc [hd], m, l (padded)
 constexpr int kHdrStep = 0, kHdrAbort = 1;  // scratch header words
 
 // "Full" mbarriers (a staged region landed), each filled by one side:
-// the producer warp (count 32) -- q/k/v rows (region A), the first K/V chunk
-// (K), the out_proj tile (O), router + norm weights (R), the LM-head ring
-// stages -- or the consumers (count kCT) -- the selected experts' gate/up rows
-// (A) and down rows (D), further K/V chunks (K).  "Empty" mbarriers (count 1,
+// the producer warp (count 1: lane 0 arrives with the bytes expected) --
+// q/k/v rows (region A), the first K/V chunk (K), the out_proj tile (O),
+// router + norm weights (R), the selected experts' gate/up rows (A) and down
+// rows (D), the LM-head ring stages -- or the consumers (count kCT) --
+// further K/V chunks (K).  "Empty" mbarriers (count 1,
 // arrived by consumer thread 0): a region the producer refills was read for
 // the last time.
 constexpr int kFQ = 0, kFK = 1, kFK2 = 2, kFO = 3, kFR = 4, kFE = 5, kFD = 6, kFH = 7;
@@ -393,12 +400,6 @@ struct Side {
   int i, n;
 };
 __device__ __forceinline__ Side cons_side() { return Side{(int)threadIdx.x, kCT}; }
-// `bytes` (a multiple of 16) from src to dst.
-__device__ __forceinline__ void stage(Side sd, void* dst, const void* src, uint32_t bytes, uint64_t pol) {
-#pragma unroll 1
-  for (uint32_t o = (uint32_t)sd.i * 16u; o < bytes; o += (uint32_t)sd.n * 16u)
-    cp16(static_cast<uint8_t*>(dst) + o, static_cast<const uint8_t*>(src) + o, pol);
-}
 // After this side's copies of one phase of full barrier b: arrive when they land.
 __device__ __forceinline__ void stage_done(Side sd, int b) {
   if (sd.i == 0) armed_s[b] += 1;
@@ -456,43 +457,6 @@ __device__ __noinline__ void issue_kv(Side sd, int b, int l, int h, int ta, int 
          static_cast<const bf16*>(v ? ly.v_cache : ly.k_cache) + off, pol);
   }
   stage_done(sd, b);
-}
-
-// The selected experts' rows of this CTA: gate rows then up rows of its units
-// -> region A (barrier A), down rows of its output rows, slot 0 then slot 1 ->
-// region D (barrier D).  e0, e1: the slots' experts in this rank's weight
-// stack; with EP (expert parallel) -1 marks a slot held by another rank,
-// which stages nothing.
-template <bool EP>
-__device__ __noinline__ void issue_experts(Side sd, int l, int e0, int e1) {
-  const mie_step_desc& d = ps.d;
-  const CGeom& g = ps.g;
-  const mie_layer_desc& ly = layer_at(l);
-  const int D = d.hidden_dim, Hx = d.expert_hidden_dim;
-  const uint32_t rbD = (uint32_t)D * 2u, rbH = (uint32_t)Hx * 2u;
-  int u0, u1, r0, r1;
-  split32(2 * Hx, blockIdx.x, g.G, &u0, &u1);
-  split32(D, blockIdx.x, g.G, &r0, &r1);
-  const int nu = u1 - u0, nr = r1 - r0;
-  const uint64_t pol = policy_evict_first();
-#pragma unroll 1
-  for (int m = 0; m < 2; ++m) {
-    const uint8_t* w = static_cast<const uint8_t*>(m ? ly.w3 : ly.w1);
-#pragma unroll 1
-    for (int k = 0; k < 2; ++k) {
-      const int ua = max(u0, k * Hx), ub = min(u1, (k + 1) * Hx), e = k ? e1 : e0;
-      if (ub > ua && (!EP || e >= 0))
-        stage(sd, at<uint8_t>(g.sm_a) + (size_t)(m * nu + ua - u0) * rbD,
-              w + ((size_t)e * Hx + ua - k * Hx) * rbD, (uint32_t)(ub - ua) * rbD, pol);
-    }
-  }
-  stage_done(sd, kFE);
-#pragma unroll 1
-  for (int k = 0; k < 2; ++k)
-    if (!EP || (k ? e1 : e0) >= 0)
-      stage(sd, at<uint8_t>(g.sm_d) + (size_t)k * nr * rbH,
-            static_cast<const uint8_t*>(ly.w2) + ((size_t)(k ? e1 : e0) * D + r0) * rbH, (uint32_t)nr * rbH, pol);
-  stage_done(sd, kFD);
 }
 
 // ---------------------------------------------------------------------------
@@ -581,6 +545,54 @@ __device__ __noinline__ void tma_side(int l) {
   bulk_copy(dst, ly.router_w, (uint32_t)d.num_experts * rb, kFR);
   bulk_copy(dst + (size_t)d.num_experts * rb, ly.attn_norm_w, rb, kFR);
   bulk_copy(dst + (size_t)(d.num_experts + 1) * rb, ly.moe_norm_w, rb, kFR);
+}
+
+// The selected experts' rows of this CTA (producer lane 0): gate rows then up
+// rows of its units -> region A (barrier A), down rows of its output rows,
+// slot 0 then slot 1 -> region D (barrier D); at most six bulk copies.  e0,
+// e1: the slots' experts in this rank's weight stack; with EP (expert
+// parallel) -1 marks a slot held by another rank, which stages nothing (its
+// barrier phase still completes).  Regions A and D were last read before
+// cluster barrier 3 of this layer, which the caller has passed.
+template <bool EP>
+__device__ __noinline__ void tma_experts(int l, int e0, int e1) {
+  if ((threadIdx.x & 31) != 0) return;
+  const mie_step_desc& d = ps.d;
+  const CGeom& g = ps.g;
+  const mie_layer_desc& ly = layer_at(l);
+  const int D = d.hidden_dim, Hx = d.expert_hidden_dim;
+  const uint32_t rbD = (uint32_t)D * 2u, rbH = (uint32_t)Hx * 2u;
+  int u0, u1, r0, r1;
+  split32(2 * Hx, blockIdx.x, g.G, &u0, &u1);
+  split32(D, blockIdx.x, g.G, &r0, &r1);
+  const int nu = u1 - u0, nr = r1 - r0;
+  fence_proxy_async_smem();
+  uint32_t bytes = 0;
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const int ua = max(u0, k * Hx), ub = min(u1, (k + 1) * Hx);
+    if (ub > ua && (!EP || (k ? e1 : e0) >= 0)) bytes += 2u * (uint32_t)(ub - ua) * rbD;
+  }
+  bar_arm(kFE, bytes);
+#pragma unroll 1
+  for (int m = 0; m < 2; ++m) {
+    const uint8_t* w = static_cast<const uint8_t*>(m ? ly.w3 : ly.w1);
+#pragma unroll 1
+    for (int k = 0; k < 2; ++k) {
+      const int ua = max(u0, k * Hx), ub = min(u1, (k + 1) * Hx), e = k ? e1 : e0;
+      if (ub > ua && (!EP || e >= 0))
+        bulk_copy(at<uint8_t>(g.sm_a) + (size_t)(m * nu + ua - u0) * rbD,
+                  w + ((size_t)e * Hx + ua - k * Hx) * rbD, (uint32_t)(ub - ua) * rbD, kFE);
+    }
+  }
+  bar_arm(kFD, (uint32_t)((!EP || e0 >= 0) + (!EP || e1 >= 0)) * (uint32_t)nr * rbH);
+#pragma unroll 1
+  for (int k = 0; k < 2; ++k) {
+    const int e = k ? e1 : e0;
+    if (!EP || e >= 0)
+      bulk_copy(at<uint8_t>(g.sm_d) + (size_t)k * nr * rbH,
+                static_cast<const uint8_t*>(ly.w2) + ((size_t)e * D + r0) * rbH, (uint32_t)nr * rbH, kFD);
+  }
 }
 
 // K/V of tokens [ta, ta + n) of head h, layer l -> region K (K rows, then V
@@ -999,6 +1011,75 @@ __device__ __noinline__ bool att_phase(const CStepParams& P, int l, bool ok) {
   return ok;
 }
 
+// Routing of layer l after cluster barrier 3, by one full warp (every
+// consumer warp and the producer warp compute the same bits): the RMSNorm
+// scale rs of x_mid from the cluster's square sums and the top-2 experts from
+// the cluster's router partials, both summed in rank order.  One expert per
+// lane (E <= 32): lane e holds expert e's logit (its partials' sum times rs;
+// NaN ranks as -inf).  (value, lower id) is a total order, so the butterfly
+// gives every lane the same answer: the maximum with ties to the lower id,
+// then the maximum of the others with ties to the lower id -- the repeated
+// argmax of the reference's router (src/moe_engine/fused_moe.py:143-150).
+struct Route {
+  float rs;        // RMSNorm scale of x_mid
+  int sel0, sel1;  // the experts
+  float bv, cv;    // and their logits
+};
+__device__ __forceinline__ Route route_top2(int l) {
+  const mie_step_desc& d = ps.d;
+  const int E = d.num_experts, par = l & 1, lane = threadIdx.x & 31;
+  const float* ssb = at<const float>(ps.g.sm_ss) + (size_t)par * kCS;
+  const float* rps = at<const float>(ps.g.sm_rp) + (size_t)par * kCS * E;
+  Route r;
+  float t = 0.f;
+#pragma unroll
+  for (int s = 0; s < kCS; ++s) t += ssb[s];
+  r.rs = rsqrtf(t / (float)d.hidden_dim + d.eps);
+  float lv = -INFINITY;
+  if (lane < E) {
+    float q = 0.f;
+#pragma unroll
+    for (int s = 0; s < kCS; ++s) q += rps[s * E + lane];
+    lv = r.rs * q;
+    if (lv != lv) lv = -INFINITY;
+  }
+  r.bv = lv;
+  r.sel0 = lane;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, r.bv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, r.sel0, o);
+    if (better(ov, oi, r.bv, r.sel0)) {
+      r.bv = ov;
+      r.sel0 = oi;
+    }
+  }
+  r.cv = lane == r.sel0 ? -INFINITY : lv;
+  r.sel1 = lane == r.sel0 ? 64 : lane;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, r.cv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, r.sel1, o);
+    if (better(ov, oi, r.cv, r.sel1)) {
+      r.cv = ov;
+      r.sel1 = oi;
+    }
+  }
+  return r;
+}
+// The slots' experts in this rank's weight stack (expert parallel: -1 for a
+// slot held by another rank).
+template <bool EP>
+__device__ __forceinline__ void local_experts(int sel0, int sel1, int* le0, int* le1) {
+  *le0 = sel0;
+  *le1 = sel1;
+  if (EP) {
+    const mie_step_desc& d = ps.d;
+    *le0 = (unsigned)(sel0 - d.expert_base) < (unsigned)d.expert_count ? sel0 - d.expert_base : -1;
+    *le1 = (unsigned)(sel1 - d.expert_base) < (unsigned)d.expert_count ? sel1 - d.expert_base : -1;
+  }
+}
+
 // ---------------------------------------------------------------------------
 // MOE: x_mid, routing, the two selected experts, x of layer l + 1
 // ---------------------------------------------------------------------------
@@ -1088,67 +1169,16 @@ __device__ __noinline__ bool moe_phase(const CStepParams& P, int l, bool ok, boo
   CSTAMP(l, 27);
   cluster_sync_all();  // cluster barrier 3: x_mid and the router partials complete in every CTA
   CSTAMP(l, 7);
-  // ---- routing: RMSNorm scale and logits from the cluster's shares, in rank order; top-2 ----
-  float rs;
-  {
-    float t = 0.f;
-#pragma unroll
-    for (int s = 0; s < kCS; ++s) t += ssb[s];
-    rs = rsqrtf(t / (float)D + d.eps);
-  }
+  // ---- routing (the producer warp computes the same and stages the selected experts' rows) ----
+  const Route rt = route_top2(l);
+  const float rs = rt.rs;
+  const int sel0 = rt.sel0, sel1 = rt.sel1;
   CSTAMP(l, 28);
-  // top-2 in every warp, one expert per lane (E <= 32): lane e holds expert
-  // e's logit (the cluster's partials summed in rank order, times rs; NaN
-  // ranks as -inf).  (value, lower id) is a total order, so the butterfly
-  // gives every lane the same answer: the maximum with ties to the lower id,
-  // then the maximum of the others with ties to the lower id -- the repeated
-  // argmax of the reference's router (src/moe_engine/fused_moe.py:143-150).
-  int sel0, sel1;
-  float bv, cv;
-  {
-    const int lane = tid & 31;
-    float lv = -INFINITY;
-    if (lane < E) {
-      float q = 0.f;
-#pragma unroll
-      for (int s = 0; s < kCS; ++s) q += rps[s * E + lane];
-      lv = rs * q;
-      if (lv != lv) lv = -INFINITY;
-    }
-    bv = lv;
-    sel0 = lane;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, sel0, o);
-      if (better(ov, oi, bv, sel0)) {
-        bv = ov;
-        sel0 = oi;
-      }
-    }
-    cv = lane == sel0 ? -INFINITY : lv;
-    sel1 = lane == sel0 ? 64 : lane;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, cv, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, sel1, o);
-      if (better(ov, oi, cv, sel1)) {
-        cv = ov;
-        sel1 = oi;
-      }
-    }
-  }
-  const float e1 = expf(cv - bv);
+  const float e1 = expf(rt.cv - rt.bv);
   const float wt0 = 1.0f / (1.0f + e1), wt1 = e1 / (1.0f + e1);
   CSTAMP(l, 30);
-  // the slots' experts in this rank's weight stack (expert parallel: -1 for
-  // a slot held by another rank)
-  int le0 = sel0, le1 = sel1;
-  if (EP) {
-    le0 = (unsigned)(sel0 - d.expert_base) < (unsigned)d.expert_count ? sel0 - d.expert_base : -1;
-    le1 = (unsigned)(sel1 - d.expert_base) < (unsigned)d.expert_count ? sel1 - d.expert_base : -1;
-  }
-  if (ok) issue_experts<EP>(cons_side(), l, le0, le1);
+  int le0, le1;
+  local_experts<EP>(sel0, sel1, &le0, &le1);
   const unsigned held = EP ? (le0 >= 0 ? 1u : 0u) | (le1 >= 0 ? 2u : 0u) : 3u;  // the slots this rank computes
   // the normalised x_mid for the up GEMV, while the expert rows are in flight
 #pragma unroll 1
@@ -1397,13 +1427,25 @@ __device__ __noinline__ void head_prefetch_l2() {
   for (uint32_t o = 0; o < nb; o += kBulkMax) bulk_prefetch_l2(src + o, min(kBulkMax, nb - o));
 }
 
+// After cluster barrier 3 of layer l (producer warp): the routing the
+// consumers compute, then the selected experts' rows of this CTA.
+template <bool EP>
+__device__ __forceinline__ void producer_experts(int l, bool ok) {
+  const Route rt = route_top2(l);
+  int le0, le1;
+  local_experts<EP>(rt.sel0, rt.sel1, &le0, &le1);
+  if (ok) tma_experts<EP>(l, le0, le1);
+}
+
 // The producer warp's program: it stages, one layer ahead, everything that
 // does not depend on the layer's routing -- the next layer's first K/V chunk,
 // out_proj tile, router + norm weights and q/k/v rows, each once the
-// consumers have read the region for the last time -- then the LM-head ring.
-// It arrives at every cluster barrier as soon as it may (and waits on it
-// late), so the consumers never wait for it; after a failed wait it keeps
-// taking the cluster barriers without staging.
+// consumers have read the region for the last time -- and, right after
+// cluster barrier 3, the rows of the experts this layer selected; then the
+// LM-head ring.  It arrives at every cluster barrier as soon as it may, so
+// the consumers never wait for it; after a failed wait it keeps taking the
+// cluster barriers without staging.
+template <bool EP>
 __device__ __noinline__ void producer(const CStepParams& P, bool att, bool ok) {
   const mie_step_desc& d = ps.d;
   const CGeom& g = ps.g;
@@ -1420,25 +1462,27 @@ __device__ __noinline__ void producer(const CStepParams& P, bool att, bool ok) {
       cluster_wait();
       cluster_arrive();  // barrier 2 (split results)
       cluster_wait();
-      cluster_arrive();  // barrier 3 (x_mid), waited for after this layer's staging
+      cluster_arrive();  // barrier 3 (x_mid, router partials)
       if (l + 1 < L) {
         ok = pwait(ok, kEK);
         if (ok && n0 > 0) tma_kv(l + 1, a.h, a.t0, n0);
         ok = pwait(ok, kEO);
         if (ok) tma_otile(P, l + 1);
       }
+      cluster_wait();
+      producer_experts<EP>(l, ok);
       ok = pwait(ok, kER);
       if (ok) tma_side(l + 1);
       if (l + 1 < L) {
         ok = pwait(ok, kEA);
         if (ok) tma_qkv(l + 1);
       }
-      cluster_wait();
     } else {
-      cluster_arrive();  // barrier 3 (x_mid)
+      cluster_arrive();  // barrier 3 (x_mid, router partials)
+      cluster_wait();
+      producer_experts<EP>(l, ok);
       ok = pwait(ok, kER);
       if (ok) tma_side(l + 1);
-      cluster_wait();
     }
   }
   // the LM-head ring over regions A..D, free after the last down projection
@@ -1481,7 +1525,7 @@ __global__ void __launch_bounds__(kT, 1) cstep_kernel(const __grid_constant__ CS
         // full barriers: one arrival per thread of the filling side; empty: one
         // full barriers filled by the consumers' cp.async: one arrival per
         // consumer thread; by the producer's bulk copies, and empty barriers: one
-        const bool cons = b == kFK2 || b == kFE || b == kFD;
+        const bool cons = b == kFK2;
         mbar_init(&bars_s[b], cons ? (uint32_t)kCT : 1u);
         armed_s[b] = done_s[b] = 0;
         if (b < kNF)
@@ -1569,7 +1613,7 @@ __global__ void __launch_bounds__(kT, 1) cstep_kernel(const __grid_constant__ CS
   }
   CSTAMP(d.num_layers, 4);
   if (threadIdx.x >= kProd) {
-    producer(P, att, ok);
+    producer<EP>(P, att, ok);
   } else {
 #pragma unroll 1
     for (int l = 0; l < d.num_layers; ++l) {
