@@ -1025,16 +1025,20 @@ struct Route {
   int sel0, sel1;  // the experts
   float bv, cv;    // and their logits
 };
-__device__ __forceinline__ Route route_top2(int l) {
-  const mie_step_desc& d = ps.d;
-  const int E = d.num_experts, par = l & 1, lane = threadIdx.x & 31;
-  const float* ssb = at<const float>(ps.g.sm_ss) + (size_t)par * kCS;
-  const float* rps = at<const float>(ps.g.sm_rp) + (size_t)par * kCS * E;
-  Route r;
+// RMSNorm scale of layer l's x_mid from the cluster's square sums.
+__device__ __forceinline__ float xmid_scale(int l) {
+  const float* ssb = at<const float>(ps.g.sm_ss) + (size_t)(l & 1) * kCS;
   float t = 0.f;
 #pragma unroll
   for (int s = 0; s < kCS; ++s) t += ssb[s];
-  r.rs = rsqrtf(t / (float)d.hidden_dim + d.eps);
+  return rsqrtf(t / (float)ps.d.hidden_dim + ps.d.eps);
+}
+__device__ __forceinline__ Route route_top2(int l) {
+  const mie_step_desc& d = ps.d;
+  const int E = d.num_experts, par = l & 1, lane = threadIdx.x & 31;
+  const float* rps = at<const float>(ps.g.sm_rp) + (size_t)par * kCS * E;
+  Route r;
+  r.rs = xmid_scale(l);
   float lv = -INFINITY;
   if (lane < E) {
     float q = 0.f;
@@ -1169,17 +1173,26 @@ __device__ __noinline__ bool moe_phase(const CStepParams& P, int l, bool ok, boo
   CSTAMP(l, 27);
   cluster_sync_all();  // cluster barrier 3: x_mid and the router partials complete in every CTA
   CSTAMP(l, 7);
-  // ---- routing (the producer warp computes the same and stages the selected experts' rows) ----
-  const Route rt = route_top2(l);
-  const float rs = rt.rs;
-  const int sel0 = rt.sel0, sel1 = rt.sel1;
+  // ---- routing: the producer warp computes it at once and stages the
+  // selected experts' rows.  The consumers need the RMSNorm scale now and the
+  // routing weights only for the combine, so they route while the expert
+  // hidden units are exchanged -- except with expert parallelism, where the
+  // up units need to know which slots this rank holds. ----
+  Route rt;
+  unsigned held = 3u;  // the slots this rank computes
+  if constexpr (EP) {
+    rt = route_top2(l);
+    int le0, le1;
+    local_experts<EP>(rt.sel0, rt.sel1, &le0, &le1);
+    held = (le0 >= 0 ? 1u : 0u) | (le1 >= 0 ? 2u : 0u);
+  }
+  float rs;
+  if constexpr (EP)
+    rs = rt.rs;
+  else
+    rs = xmid_scale(l);
   CSTAMP(l, 28);
-  const float e1 = expf(rt.cv - rt.bv);
-  const float wt0 = 1.0f / (1.0f + e1), wt1 = e1 / (1.0f + e1);
   CSTAMP(l, 30);
-  int le0, le1;
-  local_experts<EP>(sel0, sel1, &le0, &le1);
-  const unsigned held = EP ? (le0 >= 0 ? 1u : 0u) | (le1 >= 0 ? 2u : 0u) : 3u;  // the slots this rank computes
   // the normalised x_mid for the up GEMV, while the expert rows are in flight
 #pragma unroll 1
   for (int i = tid; i < D; i += kCT) xn[i] = (xm[i] * rs) * __bfloat162float(nw[i]);
@@ -1202,6 +1215,9 @@ __device__ __noinline__ bool moe_phase(const CStepParams& P, int l, bool ok, boo
     ll_put(g.ll + g.off_h[par] + u0 + tid, h, tag);
   }
   if (att && l + 1 < d.num_layers) region_free(kEA);  // the producer stages the next layer's q/k/v rows
+  if constexpr (!EP) rt = route_top2(l);
+  const float e1 = expf(rt.cv - rt.bv);
+  const float wt0 = 1.0f / (1.0f + e1), wt1 = e1 / (1.0f + e1);
   CSTAMP(l, 9);
   // ---- down rows of both slots . h + residual -> exchange X of layer l + 1 ----
   {
@@ -1242,8 +1258,8 @@ __device__ __noinline__ bool moe_phase(const CStepParams& P, int l, bool ok, boo
     region_free(kED);
   }
   if (tid == 0) {
-    cx.sel0 = sel0;
-    cx.sel1 = sel1;
+    cx.sel0 = rt.sel0;
+    cx.sel1 = rt.sel1;
   }
   CSTAMP(l, 11);
   return ok;
