@@ -548,14 +548,14 @@ __device__ __noinline__ void tma_side(int l) {
 }
 
 // The selected experts' rows of this CTA (producer lane 0): gate rows then up
-// rows of its units -> region A (barrier A), down rows of its output rows,
-// slot 0 then slot 1 -> region D (barrier D); at most six bulk copies.  e0,
-// e1: the slots' experts in this rank's weight stack; with EP (expert
-// parallel) -1 marks a slot held by another rank, which stages nothing (its
-// barrier phase still completes).  Regions A and D were last read before
-// cluster barrier 3 of this layer, which the caller has passed.
+// rows of its units -> region A (barrier A), or (down) the down rows of its
+// output rows, slot 0 then slot 1 -> region D (barrier D); at most four / two
+// bulk copies.  e0, e1: the slots' experts in this rank's weight stack; with
+// EP (expert parallel) -1 marks a slot held by another rank, which stages
+// nothing (its barrier phase still completes).  Regions A and D were last read
+// before cluster barrier 3 of this layer, which the caller has passed.
 template <bool EP>
-__device__ __noinline__ void tma_experts(int l, int e0, int e1) {
+__device__ __noinline__ void tma_experts(int l, int e0, int e1, bool down) {
   if ((threadIdx.x & 31) != 0) return;
   const mie_step_desc& d = ps.d;
   const CGeom& g = ps.g;
@@ -567,6 +567,17 @@ __device__ __noinline__ void tma_experts(int l, int e0, int e1) {
   split32(D, blockIdx.x, g.G, &r0, &r1);
   const int nu = u1 - u0, nr = r1 - r0;
   fence_proxy_async_smem();
+  if (down) {
+    bar_arm(kFD, (uint32_t)((!EP || e0 >= 0) + (!EP || e1 >= 0)) * (uint32_t)nr * rbH);
+#pragma unroll 1
+    for (int k = 0; k < 2; ++k) {
+      const int e = k ? e1 : e0;
+      if (!EP || e >= 0)
+        bulk_copy(at<uint8_t>(g.sm_d) + (size_t)k * nr * rbH,
+                  static_cast<const uint8_t*>(ly.w2) + ((size_t)e * D + r0) * rbH, (uint32_t)nr * rbH, kFD);
+    }
+    return;
+  }
   uint32_t bytes = 0;
 #pragma unroll
   for (int k = 0; k < 2; ++k) {
@@ -584,14 +595,6 @@ __device__ __noinline__ void tma_experts(int l, int e0, int e1) {
         bulk_copy(at<uint8_t>(g.sm_a) + (size_t)(m * nu + ua - u0) * rbD,
                   w + ((size_t)e * Hx + ua - k * Hx) * rbD, (uint32_t)(ub - ua) * rbD, kFE);
     }
-  }
-  bar_arm(kFD, (uint32_t)((!EP || e0 >= 0) + (!EP || e1 >= 0)) * (uint32_t)nr * rbH);
-#pragma unroll 1
-  for (int k = 0; k < 2; ++k) {
-    const int e = k ? e1 : e0;
-    if (!EP || e >= 0)
-      bulk_copy(at<uint8_t>(g.sm_d) + (size_t)k * nr * rbH,
-                static_cast<const uint8_t*>(ly.w2) + ((size_t)e * D + r0) * rbH, (uint32_t)nr * rbH, kFD);
   }
 }
 
@@ -1444,13 +1447,23 @@ __device__ __noinline__ void head_prefetch_l2() {
 }
 
 // After cluster barrier 3 of layer l (producer warp): the routing the
-// consumers compute, then the selected experts' rows of this CTA.
+// consumers compute, then the selected experts' gate/up rows of this CTA and,
+// once those landed, its down rows -- needed only after the up units and the
+// hidden exchange, they would otherwise share the SM's bandwidth with the
+// gate/up rows the consumers wait for.
 template <bool EP>
-__device__ __forceinline__ void producer_experts(int l, bool ok) {
+__device__ __forceinline__ bool producer_experts(int l, bool ok) {
   const Route rt = route_top2(l);
   int le0, le1;
   local_experts<EP>(rt.sel0, rt.sel1, &le0, &le1);
-  if (ok) tma_experts<EP>(l, le0, le1);
+  if (!ok) return false;
+  tma_experts<EP>(l, le0, le1, false);
+  __syncwarp();
+  const bool mine = mbar_wait(&bars_s[kFE], (armed_s[kFE] - 1u) & 1u, ps.d.status, lim_s);
+  if (!mine) raise_abort();
+  if (!__all_sync(0xffffffffu, mine)) return false;
+  tma_experts<EP>(l, le0, le1, true);
+  return true;
 }
 
 // The producer warp's program: it stages, one layer ahead, everything that
@@ -1486,7 +1499,7 @@ __device__ __noinline__ void producer(const CStepParams& P, bool att, bool ok) {
         if (ok) tma_otile(P, l + 1);
       }
       cluster_wait();
-      producer_experts<EP>(l, ok);
+      ok = producer_experts<EP>(l, ok);
       ok = pwait(ok, kER);
       if (ok) tma_side(l + 1);
       if (l + 1 < L) {
@@ -1496,7 +1509,7 @@ __device__ __noinline__ void producer(const CStepParams& P, bool att, bool ok) {
     } else {
       cluster_arrive();  // barrier 3 (x_mid, router partials)
       cluster_wait();
-      producer_experts<EP>(l, ok);
+      ok = producer_experts<EP>(l, ok);
       ok = pwait(ok, kER);
       if (ok) tma_side(l + 1);
     }
