@@ -1429,22 +1429,6 @@ __device__ __noinline__ bool gate_open(const int32_t* gate, unsigned long long l
   return true;
 }
 
-// During the last layer: this CTA's LM-head rows (its vocab share of the tied
-// embedding) are prefetched into L2 (producer lane 0), so the LM-head ring
-// after the last layer reads them from L2 instead of HBM.  The rows do not
-// depend on the step; HBM is mostly idle while the layer's dependent phases
-// run.
-__device__ __noinline__ void head_prefetch_l2() {
-  if ((threadIdx.x & 31) != 0) return;
-  const mie_step_desc& d = ps.d;
-  int v0, v1;
-  split32(d.vocab, blockIdx.x, ps.g.G, &v0, &v1);
-  const uint32_t rb = (uint32_t)d.hidden_dim * 2u;
-  const uint8_t* src = static_cast<const uint8_t*>(d.embedding) + (size_t)v0 * rb;
-  const uint32_t nb = (uint32_t)(v1 - v0) * rb;
-#pragma unroll 1
-  for (uint32_t o = 0; o < nb; o += kBulkMax) bulk_prefetch_l2(src + o, min(kBulkMax, nb - o));
-}
 
 // After cluster barrier 3 of layer l (producer warp): the routing the
 // consumers compute, then the selected experts' gate/up rows of this CTA and,
@@ -1485,7 +1469,6 @@ __device__ __noinline__ void producer(const CStepParams& P, bool att, bool ok) {
 #pragma unroll 1
   for (int l = 0; l < L; ++l) {
     if (l + 2 < L && l + 2 >= kLaySlots) layer_fetch(P, l + 2, kProd);  // into the slot of layer l - 2
-    if (l == L - 1 && ok) head_prefetch_l2();
     if (att) {
       cluster_arrive();  // barrier 1 (q, k_new, v_new)
       cluster_wait();
