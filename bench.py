@@ -39,9 +39,9 @@ sys.path.insert(0, REPO)
 
 METRIC = "batch-1 decode tok/s (bf16, config[3]: 512-token prompt + 1024 greedy tokens)"
 # ncu capture of one persistent step launch of the cluster step kernel
-# (--profile 12, 7th step, context 518): dram__bytes_read.sum +
-# dram__bytes_write.sum
-STEP_CAPTURE_DRAM_BYTES = 238.82368e6 + 4.129536e6
+# (--profile 12, 7th step, context 518; 224.8 us under ncu):
+# dram__bytes_read.sum + dram__bytes_write.sum
+STEP_CAPTURE_DRAM_BYTES = 238.445312e6 + 3.497216e6
 STEP_CAPTURE_CTX = 518
 PROMPT_LEN = 512
 NEW_TOKENS = 1024
