@@ -270,6 +270,12 @@ typedef struct mie_layer_desc {
   const void* b2;
   void* k_cache;
   void* v_cache;
+  /* quantized experts (mie_step_desc.expert_bits set): w1 / w3 / w2 hold the
+   * int8 values or packed int4 pairs, these their fp32 group scales
+   * ([experts, rows, cols / group_size], as mie_moe_args) */
+  const float* w1_scale;
+  const float* w3_scale;
+  const float* w2_scale;
 } mie_layer_desc;
 
 /* One whole decode step (all layers + LM head) for one token. */
@@ -384,6 +390,13 @@ typedef struct mie_step_desc {
    *   wait_limit_ns (MIE_ERR_TIMEOUT); the ranks' exchange state then
    *   differs, so the group makes new buffers and a new counter. */
   const struct mie_peer_reduce_args* moe_peer;
+  /* Quantized experts (0: the layers' experts are in `dtype`): 8 or 4 with
+   * group_size as in mie_moe_args, scales in the layer descriptors.  The
+   * cluster step takes int8 (bf16 model, group_size a power of two >= 32
+   * dividing hidden_dim and expert_hidden_dim); int4, and int8 on other
+   * shapes, run the per-layer launch sequence. */
+  int expert_bits;
+  int group_size;
 } mie_step_desc;
 
 enum { MIE_STEP_AUTO = 0, MIE_STEP_FLAT = 1, MIE_STEP_CLUSTER = 2 };

@@ -295,6 +295,13 @@ mie_moe_args step_moe(const mie_step_desc& d, int l) {
   a.skip = d.done;
   a.expert_base = d.expert_base;
   a.expert_count = d.expert_count;
+  if (d.expert_bits) {  // quantized experts: the grouped kernel
+    a.expert_bits = d.expert_bits;
+    a.group_size = d.group_size;
+    a.w1_scale = ly.w1_scale;
+    a.w3_scale = ly.w3_scale;
+    a.w2_scale = ly.w2_scale;
+  }
   if (d.moe_peer) {  // expert parallel: the MoE kernel completes the all-reduce of its partial
     const mie_peer_reduce_args& p = *d.moe_peer;
     a.peer_rank = p.rank;

@@ -119,6 +119,10 @@ struct CGeom {
   int peer_rank, peer_world;
   uint64_t* peer_bufs[MIE_PEER_MAX_RANKS];
   uint32_t* peer_seq;
+  // int8 experts (qbits 8; 0: bf16): log2 of the group size, and where the
+  // staged rows' fp32 group scales start in regions A and D (bytes)
+  int qbits, qgsh;
+  uint32_t q_a_scale, q_d_scale;
 };
 
 struct CStepParams {

@@ -60,16 +60,6 @@ __device__ __forceinline__ void qseg_load(QSeg<BITS>& r, const uint32_t* row, co
   }
 }
 
-// Small integers to float without I2F: with the bit pattern 0x4B000000 | u
-// (u < 2^23) a float holds exactly 2^23 + u, so subtracting 2^23 + bias
-// leaves u - bias.  The values are stored offset to unsigned (q + 128 for
-// int8, q + 8 for int4) by flipping their sign bits.
-__device__ __forceinline__ float byte_to_f(uint32_t u_flipped, uint32_t sel) {
-  return __int_as_float(__byte_perm(u_flipped, 0x4B000000u, sel)) - 8388736.0f;  // 2^23 + 128
-}
-__device__ __forceinline__ float nibble_to_f(uint32_t u_flipped, int b) {
-  return __int_as_float(0x4B000000u | ((u_flipped >> (4 * b)) & 0xFu)) - 8388616.0f;  // 2^23 + 8
-}
 
 // sum over the segment's words of scale x (q . x); x fp32 in shared memory
 template <int BITS>

@@ -1715,7 +1715,7 @@ int step_geometry(const mie_step_desc& d, int grid, StepGeom* g) {
   if (d.top_k != 2 || E < 2 || E > 32) return MIE_ERR_UNSUPPORTED;
   if (d.act != MIE_ACT_GELU && d.act != MIE_ACT_SWIGLU) return MIE_ERR_UNSUPPORTED;
   if (d.moe_partial || (d.expert_count && d.expert_count != E) || d.expert_base ||
-      (d.moe_peer && d.moe_peer->world > 1))
+      (d.moe_peer && d.moe_peer->world > 1) || d.expert_bits)
     return MIE_ERR_UNSUPPORTED;  // expert parallel: the cluster step or layer by layer
   if (d.kv_stride_tok != hd || (d.kv_stride_block * kvsz) % 16 || (d.kv_stride_head * kvsz) % 16)
     return MIE_ERR_UNSUPPORTED;

@@ -547,54 +547,120 @@ __device__ __noinline__ void tma_side(int l) {
   bulk_copy(dst + (size_t)(d.num_experts + 1) * rb, ly.moe_norm_w, rb, kFR);
 }
 
-// The selected experts' rows of this CTA (producer lane 0): gate rows then up
+// The selected experts' rows of this CTA (producer warp): gate rows then up
 // rows of its units -> region A (barrier A), or (down) the down rows of its
-// output rows, slot 0 then slot 1 -> region D (barrier D); at most four / two
-// bulk copies.  e0, e1: the slots' experts in this rank's weight stack; with
-// EP (expert parallel) -1 marks a slot held by another rank, which stages
-// nothing (its barrier phase still completes).  Regions A and D were last read
+// output rows, slot 0 then slot 1 -> region D (barrier D); lane 0 issues at
+// most four / two bulk copies.  e0, e1: the slots' experts in this rank's
+// weight stack; with EP (expert parallel) -1 marks a slot held by another
+// rank, which stages nothing (its barrier phase still completes).  With Q8
+// (int8 experts) the rows are int8 and the warp also loads their fp32 group
+// scales into the region (after the rows, at q_a_scale / q_d_scale); the
+// barrier's one arrival follows those stores, so its phase completes once the
+// rows landed and the scales are in place.  Regions A and D were last read
 // before cluster barrier 3 of this layer, which the caller has passed.
-template <bool EP>
+template <bool EP, bool Q8>
 __device__ __noinline__ void tma_experts(int l, int e0, int e1, bool down) {
-  if ((threadIdx.x & 31) != 0) return;
+  static_assert(!(EP && Q8), "int8 experts run without expert parallelism in this kernel");
+  const int lane = threadIdx.x & 31;
+  if (!Q8 && lane != 0) return;
   const mie_step_desc& d = ps.d;
   const CGeom& g = ps.g;
   const mie_layer_desc& ly = layer_at(l);
   const int D = d.hidden_dim, Hx = d.expert_hidden_dim;
-  const uint32_t rbD = (uint32_t)D * 2u, rbH = (uint32_t)Hx * 2u;
+  const uint32_t eb = Q8 ? 1u : 2u;  // bytes per weight
+  const uint32_t rbD = (uint32_t)D * eb, rbH = (uint32_t)Hx * eb;
   int u0, u1, r0, r1;
   split32(2 * Hx, blockIdx.x, g.G, &u0, &u1);
   split32(D, blockIdx.x, g.G, &r0, &r1);
   const int nu = u1 - u0, nr = r1 - r0;
-  fence_proxy_async_smem();
-  if (down) {
-    bar_arm(kFD, (uint32_t)((!EP || e0 >= 0) + (!EP || e1 >= 0)) * (uint32_t)nr * rbH);
-#pragma unroll 1
-    for (int k = 0; k < 2; ++k) {
-      const int e = k ? e1 : e0;
-      if (!EP || e >= 0)
-        bulk_copy(at<uint8_t>(g.sm_d) + (size_t)k * nr * rbH,
-                  static_cast<const uint8_t*>(ly.w2) + ((size_t)e * D + r0) * rbH, (uint32_t)nr * rbH, kFD);
-    }
-    return;
-  }
-  uint32_t bytes = 0;
+  const int b = down ? kFD : kFE;
+  if (lane == 0) {
+    fence_proxy_async_smem();
+    uint32_t bytes = 0;
+    if (down) {
+      bytes = (uint32_t)((!EP || e0 >= 0) + (!EP || e1 >= 0)) * (uint32_t)nr * rbH;
+    } else {
 #pragma unroll
-  for (int k = 0; k < 2; ++k) {
-    const int ua = max(u0, k * Hx), ub = min(u1, (k + 1) * Hx);
-    if (ub > ua && (!EP || (k ? e1 : e0) >= 0)) bytes += 2u * (uint32_t)(ub - ua) * rbD;
-  }
-  bar_arm(kFE, bytes);
-#pragma unroll 1
-  for (int m = 0; m < 2; ++m) {
-    const uint8_t* w = static_cast<const uint8_t*>(m ? ly.w3 : ly.w1);
-#pragma unroll 1
-    for (int k = 0; k < 2; ++k) {
-      const int ua = max(u0, k * Hx), ub = min(u1, (k + 1) * Hx), e = k ? e1 : e0;
-      if (ub > ua && (!EP || e >= 0))
-        bulk_copy(at<uint8_t>(g.sm_a) + (size_t)(m * nu + ua - u0) * rbD,
-                  w + ((size_t)e * Hx + ua - k * Hx) * rbD, (uint32_t)(ub - ua) * rbD, kFE);
+      for (int k = 0; k < 2; ++k) {
+        const int ua = max(u0, k * Hx), ub = min(u1, (k + 1) * Hx);
+        if (ub > ua && (!EP || (k ? e1 : e0) >= 0)) bytes += 2u * (uint32_t)(ub - ua) * rbD;
+      }
     }
+    if (Q8) {  // the arrival comes after the scales
+      armed_s[b] += 1;
+      mbar_expect_tx(&bars_s[b], bytes);
+    } else {
+      bar_arm(b, bytes);
+    }
+    if (down) {
+#pragma unroll 1
+      for (int k = 0; k < 2; ++k) {
+        const int e = k ? e1 : e0;
+        if (!EP || e >= 0)
+          bulk_copy(at<uint8_t>(g.sm_d) + (size_t)k * nr * rbH,
+                    static_cast<const uint8_t*>(ly.w2) + ((size_t)e * D + r0) * rbH, (uint32_t)nr * rbH, kFD);
+      }
+    } else {
+#pragma unroll 1
+      for (int m = 0; m < 2; ++m) {
+        const uint8_t* w = static_cast<const uint8_t*>(m ? ly.w3 : ly.w1);
+#pragma unroll 1
+        for (int k = 0; k < 2; ++k) {
+          const int ua = max(u0, k * Hx), ub = min(u1, (k + 1) * Hx), e = k ? e1 : e0;
+          if (ub > ua && (!EP || e >= 0))
+            bulk_copy(at<uint8_t>(g.sm_a) + (size_t)(m * nu + ua - u0) * rbD,
+                      w + ((size_t)e * Hx + ua - k * Hx) * rbD, (uint32_t)(ub - ua) * rbD, kFE);
+        }
+      }
+    }
+  }
+  if constexpr (Q8) {
+    // the scales in batches of eight independent loads per lane
+    constexpr int kB = 8;
+    if (down) {
+      // scales of the down rows: [slot k][row i][group c]
+      const int ng = Hx >> g.qgsh, cnt = 2 * nr * ng;
+      float* dst = at<float>(g.sm_d + g.q_d_scale);
+#pragma unroll 1
+      for (int i0 = lane; i0 < cnt; i0 += 32 * kB) {
+        float v[kB];
+#pragma unroll
+        for (int t = 0; t < kB; ++t) {
+          const int i = i0 + 32 * t;
+          v[t] = 0.f;
+          if (i < cnt) {
+            const int k = i / (nr * ng), rem = i - k * nr * ng, row = rem / ng, c = rem - row * ng;
+            v[t] = __ldg(ly.w2_scale + ((size_t)(k ? e1 : e0) * D + r0 + row) * ng + c);
+          }
+        }
+#pragma unroll
+        for (int t = 0; t < kB; ++t)
+          if (i0 + 32 * t < cnt) dst[i0 + 32 * t] = v[t];
+      }
+    } else {
+      // scales of the gate then up rows: [m][unit j][group c], unit u0 + j of slot (u0 + j) / Hx
+      const int ng = D >> g.qgsh, cnt = 2 * nu * ng;
+      float* dst = at<float>(g.sm_a + g.q_a_scale);
+#pragma unroll 1
+      for (int i0 = lane; i0 < cnt; i0 += 32 * kB) {
+        float v[kB];
+#pragma unroll
+        for (int t = 0; t < kB; ++t) {
+          const int i = i0 + 32 * t;
+          v[t] = 0.f;
+          if (i < cnt) {
+            const int m = i / (nu * ng), rem = i - m * nu * ng, j = rem / ng, c = rem - j * ng;
+            const int u = u0 + j, k = u >= Hx ? 1 : 0;
+            v[t] = __ldg((m ? ly.w3_scale : ly.w1_scale) + ((size_t)(k ? e1 : e0) * Hx + u - k * Hx) * ng + c);
+          }
+        }
+#pragma unroll
+        for (int t = 0; t < kB; ++t)
+          if (i0 + 32 * t < cnt) dst[i0 + 32 * t] = v[t];
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive1(b);
   }
 }
 
@@ -699,6 +765,89 @@ __device__ __forceinline__ void gemv_rows(const uint4* rows, int n, int nvec, co
     }
   }
 }
+// int8 rows staged in shared memory (nw 32-bit words of four values each,
+// the values' fp32 group scales [row][ngr] at sc, group = 1 << gsh): out[r] =
+// sum over the row's words of scale x (q . x), x fp32 in registers (lane l
+// holds x of its words l, l + 32, ... : xr[4k + j] = x[4 (l + 32 k) + j]).
+// Consumer warp w forms rows w, w + kCW, ...: R rows per iteration.  Rows
+// [split, n) use xr1.  The values are two's complement; flipping the sign
+// bits offsets them to unsigned for byte_to_f.
+constexpr int kQ8Words = 6;  // words per lane of a row of <= 768 int8 values
+template <int R>
+__device__ __forceinline__ void gemv_q8_rows(const uint32_t* rows, const float* sc, int n, int nw, int ngr, int gsh,
+                                             const float* xr, const float* xr1, int split, float* out) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll 1
+  for (int r = threadIdx.x >> 5; r < n; r += R * kCW) {
+    uint32_t w[R][kQ8Words];
+    float s[R][kQ8Words];
+#pragma unroll
+    for (int k = 0; k < R; ++k) {
+      const int rk = r + k * kCW < n ? r + k * kCW : r;
+#pragma unroll
+      for (int j = 0; j < kQ8Words; ++j) {
+        const int wi = lane + 32 * j;
+        w[k][j] = wi < nw ? rows[(size_t)rk * nw + wi] ^ 0x80808080u : 0x80808080u;  // 0x80808080: four zeros
+        s[k][j] = wi < nw ? sc[(size_t)rk * ngr + ((4 * wi) >> gsh)] : 0.f;
+      }
+    }
+    float sum[R];
+#pragma unroll
+    for (int k = 0; k < R; ++k) {
+      const float* x = (xr1 && r + k * kCW >= split) ? xr1 : xr;
+      sum[k] = 0.f;
+#pragma unroll
+      for (int j = 0; j < kQ8Words; ++j) {
+        float part = byte_to_f(w[k][j], 0x7440u) * x[4 * j];
+        part = fmaf(byte_to_f(w[k][j], 0x7441u), x[4 * j + 1], part);
+        part = fmaf(byte_to_f(w[k][j], 0x7442u), x[4 * j + 2], part);
+        part = fmaf(byte_to_f(w[k][j], 0x7443u), x[4 * j + 3], part);
+        sum[k] = fmaf(part, s[k][j], sum[k]);
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+      for (int k = 0; k < R; ++k) sum[k] += __shfl_xor_sync(0xffffffffu, sum[k], o);
+    }
+    if (lane == 0) {
+#pragma unroll
+      for (int k = 0; k < R; ++k)
+        if (r + k * kCW < n) out[r + k * kCW] = sum[k];
+    }
+  }
+}
+__device__ __forceinline__ void load_xq_regs(float* xr, const float* x, int nw) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int j = 0; j < kQ8Words; ++j) {
+    const int wi = lane + 32 * j;
+    const float4 v = wi < nw ? *reinterpret_cast<const float4*>(x + 4 * wi) : make_float4(0.f, 0.f, 0.f, 0.f);
+    xr[4 * j] = v.x;
+    xr[4 * j + 1] = v.y;
+    xr[4 * j + 2] = v.z;
+    xr[4 * j + 3] = v.w;
+  }
+}
+// GEMV of n staged int8 rows (rows [split, n) dot x1 when x1 is set).
+__device__ __noinline__ void gemv_q8(const uint32_t* rows, const float* sc, int n, int nw, int ngr, int gsh,
+                                     const float* x, float* out, const float* x1 = nullptr, int split = 0) {
+  if ((int)(threadIdx.x >> 5) >= n) return;
+  float xr[4 * kQ8Words];
+  if (x1) {
+    // rows [split, n) dot x1 (n <= kCW: one row per warp)
+    load_xq_regs(xr, (int)(threadIdx.x >> 5) >= split ? x1 : x, nw);
+    gemv_q8_rows<1>(rows, sc, n, nw, ngr, gsh, xr, nullptr, 0, out);
+    return;
+  }
+  load_xq_regs(xr, x, nw);
+  if (n > 2 * kCW) {
+    gemv_q8_rows<3>(rows, sc, n, nw, ngr, gsh, xr, nullptr, 0, out);
+  } else {
+    gemv_q8_rows<2>(rows, sc, n, nw, ngr, gsh, xr, nullptr, 0, out);
+  }
+}
+
 // GEMV of n staged rows (rows [split, n) dot x1 when x1 is set).
 __device__ __noinline__ void gemv(const uint4* rows, int n, int nvec, const float* x, float* out,
                                   const float* x1 = nullptr, int split = 0) {
@@ -1090,7 +1239,7 @@ __device__ __forceinline__ void local_experts(int sel0, int sel1, int* le0, int*
 // ---------------------------------------------------------------------------
 // MOE: x_mid, routing, the two selected experts, x of layer l + 1
 // ---------------------------------------------------------------------------
-template <bool EP>
+template <bool EP, bool Q8>
 __device__ __noinline__ bool moe_phase(const CStepParams& P, int l, bool ok, bool att) {
   const mie_step_desc& d = ps.d;
   const CGeom& g = ps.g;
@@ -1209,7 +1358,13 @@ __device__ __noinline__ bool moe_phase(const CStepParams& P, int l, bool ok, boo
   const int nu = u1 - u0, nq = q1 - q0;
   ok = bwait(ok, kFE);
   CSTAMP(l, 31);
-  if (ok) gemv(at<const uint4>(g.sm_a), 2 * nu, nvD, xn, ab);
+  if (ok) {
+    if constexpr (Q8)
+      gemv_q8(at<const uint32_t>(g.sm_a), at<const float>(g.sm_a + g.q_a_scale), 2 * nu, D / 4, D >> g.qgsh,
+              g.qgsh, xn, ab);
+    else
+      gemv(at<const uint4>(g.sm_a), 2 * nu, nvD, xn, ab);
+  }
   csync();  // region A no longer read
   if (ok && tid < nu) {
     float h = silu(ab[tid]) * ab[nu + tid];
@@ -1231,7 +1386,13 @@ __device__ __noinline__ bool moe_phase(const CStepParams& P, int l, bool ok, boo
   CSTAMP(l, 10);
   ok = bwait(ok, kFD);
   CSTAMP(l, 13);
-  if (ok) gemv(at<const uint4>(g.sm_d), 2 * nq, nvH, hb, ab, hb + Hx, nq);
+  if (ok) {
+    if constexpr (Q8)
+      gemv_q8(at<const uint32_t>(g.sm_d), at<const float>(g.sm_d + g.q_d_scale), 2 * nq, Hx / 4, Hx >> g.qgsh,
+              g.qgsh, hb, ab, hb + Hx, nq);
+    else
+      gemv(at<const uint4>(g.sm_d), 2 * nq, nvH, hb, ab, hb + Hx, nq);
+  }
   csync();  // region D no longer read
   CSTAMP(l, 20);
   if (ok && tid < nq) {
@@ -1435,18 +1596,18 @@ __device__ __noinline__ bool gate_open(const int32_t* gate, unsigned long long l
 // once those landed, its down rows -- needed only after the up units and the
 // hidden exchange, they would otherwise share the SM's bandwidth with the
 // gate/up rows the consumers wait for.
-template <bool EP>
+template <bool EP, bool Q8>
 __device__ __forceinline__ bool producer_experts(int l, bool ok) {
   const Route rt = route_top2(l);
   int le0, le1;
   local_experts<EP>(rt.sel0, rt.sel1, &le0, &le1);
   if (!ok) return false;
-  tma_experts<EP>(l, le0, le1, false);
+  tma_experts<EP, Q8>(l, le0, le1, false);
   __syncwarp();
   const bool mine = mbar_wait(&bars_s[kFE], (armed_s[kFE] - 1u) & 1u, ps.d.status, lim_s);
   if (!mine) raise_abort();
   if (!__all_sync(0xffffffffu, mine)) return false;
-  tma_experts<EP>(l, le0, le1, true);
+  tma_experts<EP, Q8>(l, le0, le1, true);
   return true;
 }
 
@@ -1458,7 +1619,7 @@ __device__ __forceinline__ bool producer_experts(int l, bool ok) {
 // LM-head ring.  It arrives at every cluster barrier as soon as it may, so
 // the consumers never wait for it; after a failed wait it keeps taking the
 // cluster barriers without staging.
-template <bool EP>
+template <bool EP, bool Q8>
 __device__ __noinline__ void producer(const CStepParams& P, bool att, bool ok) {
   const mie_step_desc& d = ps.d;
   const CGeom& g = ps.g;
@@ -1482,7 +1643,7 @@ __device__ __noinline__ void producer(const CStepParams& P, bool att, bool ok) {
         if (ok) tma_otile(P, l + 1);
       }
       cluster_wait();
-      ok = producer_experts<EP>(l, ok);
+      ok = producer_experts<EP, Q8>(l, ok);
       ok = pwait(ok, kER);
       if (ok) tma_side(l + 1);
       if (l + 1 < L) {
@@ -1492,7 +1653,7 @@ __device__ __noinline__ void producer(const CStepParams& P, bool att, bool ok) {
     } else {
       cluster_arrive();  // barrier 3 (x_mid, router partials)
       cluster_wait();
-      ok = producer_experts<EP>(l, ok);
+      ok = producer_experts<EP, Q8>(l, ok);
       ok = pwait(ok, kER);
       if (ok) tma_side(l + 1);
     }
@@ -1510,9 +1671,10 @@ __device__ __noinline__ void producer(const CStepParams& P, bool att, bool ok) {
   }
 }
 
-// EP: expert parallel (ps.g.peer_world > 1), a separate instantiation so the
-// single-GPU step carries none of its code.
-template <bool EP>
+// EP: expert parallel (ps.g.peer_world > 1); Q8: int8 experts (ps.g.qbits
+// 8).  Separate instantiations, so the bf16 single-GPU step carries none of
+// their code.
+template <bool EP, bool Q8>
 __global__ void __launch_bounds__(kT, 1) cstep_kernel(const __grid_constant__ CStepParams P) {
   CSTAMP(P.d.num_layers, 3);
   // under programmatic dependent launch the next step's CTAs may take the SMs
@@ -1625,12 +1787,12 @@ __global__ void __launch_bounds__(kT, 1) cstep_kernel(const __grid_constant__ CS
   }
   CSTAMP(d.num_layers, 4);
   if (threadIdx.x >= kProd) {
-    producer<EP>(P, att, ok);
+    producer<EP, Q8>(P, att, ok);
   } else {
 #pragma unroll 1
     for (int l = 0; l < d.num_layers; ++l) {
       if (att) ok = att_phase<EP>(P, l, ok);
-      ok = moe_phase<EP>(P, l, ok, att);
+      ok = moe_phase<EP, Q8>(P, l, ok, att);
     }
     head_phase<EP>(ok);
   }
@@ -1666,6 +1828,21 @@ int cstep_geometry(const mie_step_desc& d, CGeom* out) {
     if (d.expert_count <= 0 || d.expert_base < 0 || d.expert_base + d.expert_count > E) return MIE_ERR_INVALID;
   } else if ((d.expert_count && d.expert_count != E) || d.expert_base) {
     return MIE_ERR_UNSUPPORTED;
+  }
+  // int8 experts: groups of a power of two >= 32 along rows of 16-byte
+  // multiples; int4, or int8 with expert parallelism, run layer by layer
+  int qgsh = 0;
+  if (d.expert_bits) {
+    const int gs = d.group_size;
+    if (d.expert_bits != 8 || ep) return MIE_ERR_UNSUPPORTED;
+    if (gs < 32 || (gs & (gs - 1)) || D % gs || Hx % gs || D % 16 || Hx % 16) return MIE_ERR_UNSUPPORTED;
+    while ((1 << qgsh) < gs) ++qgsh;
+    for (int l = 0; l < d.num_layers; ++l) {
+      const mie_layer_desc& y = d.layers[l];
+      if (!y.w1_scale || !y.w3_scale || !y.w2_scale) return MIE_ERR_INVALID;
+      if ((reinterpret_cast<uintptr_t>(y.w1) | reinterpret_cast<uintptr_t>(y.w3) | reinterpret_cast<uintptr_t>(y.w2)) & 15u)
+        return MIE_ERR_INVALID;
+    }
   }
   if (d.kv_stride_tok != kHd || (d.kv_stride_block * 2) % 16 || (d.kv_stride_head * 2) % 16)
     return MIE_ERR_UNSUPPORTED;
@@ -1756,6 +1933,16 @@ int cstep_geometry(const mie_step_desc& d, CGeom* out) {
     g.off_h[p] = take(2 * (int64_t)Hx);
   }
   g.words = off;
+  if (d.expert_bits) {
+    // int8 rows first, their scales after them, inside regions A and D
+    g.qbits = 8;
+    g.qgsh = qgsh;
+    g.q_a_scale = ((uint32_t)(2 * g.nu_max * D) + 15u) & ~15u;
+    g.q_d_scale = ((uint32_t)(2 * g.nr_max * Hx) + 15u) & ~15u;
+    if (g.q_a_scale + (uint32_t)(2 * g.nu_max * (D >> qgsh)) * 4u > a_bytes ||
+        g.q_d_scale + (uint32_t)(2 * g.nr_max * (Hx >> qgsh)) * 4u > 2u * (uint32_t)g.nr_max * rbH)
+      return MIE_ERR_UNSUPPORTED;
+  }
   g.peer_world = 1;
   if (ep) {
     g.peer_rank = pr->rank;
@@ -1806,7 +1993,9 @@ int cstep_launch(const mie_step_desc& d, const CGeom& g, uint64_t* scratch, cuda
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = d.use_pdl ? 2 : 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, g.peer_world > 1 ? cstep_kernel<true> : cstep_kernel<false>, p);
+  const cudaError_t e = cudaLaunchKernelEx(
+      &cfg, g.peer_world > 1 ? cstep_kernel<true, false> : g.qbits ? cstep_kernel<false, true> : cstep_kernel<false, false>,
+      p);
   if (e != cudaSuccess) {
     note_cuda_error(e, "cudaLaunchKernelEx(cluster step)");
     return MIE_ERR_CUDA;
@@ -1818,8 +2007,9 @@ int cstep_launch(const mie_step_desc& d, const CGeom& g, uint64_t* scratch, cuda
 // clusters of the kernel the device holds at once with its largest shared
 // memory footprint.
 void cstep_set_attributes() {
-  set_max_smem(cstep_kernel<false>);
-  set_max_smem(cstep_kernel<true>);
+  set_max_smem(cstep_kernel<false, false>);
+  set_max_smem(cstep_kernel<true, false>);
+  set_max_smem(cstep_kernel<false, true>);
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return;
   cudaLaunchConfig_t cfg = {};
@@ -1833,15 +2023,16 @@ void cstep_set_attributes() {
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  // both instantiations must fit the grid: the smaller count of the two
-  int n = 0, n_ep = 0;
-  cudaError_t e = cudaOccupancyMaxActiveClusters(&n, cstep_kernel<false>, &cfg);
-  if (e == cudaSuccess) e = cudaOccupancyMaxActiveClusters(&n_ep, cstep_kernel<true>, &cfg);
+  // every instantiation must fit the grid: the smallest count
+  int n = 0, n_ep = 0, n_q8 = 0;
+  cudaError_t e = cudaOccupancyMaxActiveClusters(&n, cstep_kernel<false, false>, &cfg);
+  if (e == cudaSuccess) e = cudaOccupancyMaxActiveClusters(&n_ep, cstep_kernel<true, false>, &cfg);
+  if (e == cudaSuccess) e = cudaOccupancyMaxActiveClusters(&n_q8, cstep_kernel<false, true>, &cfg);
   if (e != cudaSuccess) {
     note_cuda_error(e, "cudaOccupancyMaxActiveClusters(cluster step)");
     n = 0;
   }
-  if (n_ep < n) n = n_ep;
+  n = min(n, min(n_ep, n_q8));
   std::lock_guard<std::mutex> lock(g_cluster_mutex);
   g_max_clusters[dev] = n;
 }

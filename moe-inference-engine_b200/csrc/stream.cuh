@@ -215,6 +215,17 @@ __device__ __forceinline__ float peer_row_sum(const mie_moe_args& a, int D, int 
   return sum;
 }
 
+// Small integers to float without I2F: with the bit pattern 0x4B000000 | u
+// (u < 2^23) a float holds exactly 2^23 + u, so subtracting 2^23 + bias
+// leaves u - bias.  Quantized expert values are offset to unsigned (q + 128
+// for int8, q + 8 for int4) by flipping their sign bits when loaded.
+__device__ __forceinline__ float byte_to_f(uint32_t u_flipped, uint32_t sel) {
+  return __int_as_float(__byte_perm(u_flipped, 0x4B000000u, sel)) - 8388736.0f;  // 2^23 + 128
+}
+__device__ __forceinline__ float nibble_to_f(uint32_t u_flipped, int b) {
+  return __int_as_float(0x4B000000u | ((u_flipped >> (4 * b)) & 0xFu)) - 8388616.0f;  // 2^23 + 8
+}
+
 // Contiguous share of `total` items for CTA `c` of `g`: [begin, end).
 __device__ __forceinline__ void split_range(int total, int c, int g, int* begin, int* end) {
   *begin = (int)(((int64_t)total * c) / g);

@@ -89,6 +89,7 @@ class LayerDesc(ctypes.Structure):
         ("attn_norm_w", _p), ("attn_norm_b", _p), ("qkv_w", _p), ("qkv_b", _p), ("out_w", _p),
         ("out_b", _p), ("moe_norm_w", _p), ("moe_norm_b", _p), ("router_w", _p), ("w1", _p),
         ("b1", _p), ("w3", _p), ("w2", _p), ("b2", _p), ("k_cache", _p), ("v_cache", _p),
+        ("w1_scale", _p), ("w3_scale", _p), ("w2_scale", _p),
     ]
 
 
@@ -108,7 +109,7 @@ class StepDesc(ctypes.Structure):
         ("logits", _p), ("status", _p), ("attn_splits", _i), ("max_splits", _i), ("lm_grid", _i),
         ("use_pdl", _i), ("step_scratch", _p), ("step_scratch_bytes", _i64), ("sample_temperature", _f),
         ("sample_top_k", _i), ("sample_seed", _p), ("step_limit", _p), ("wait_limit_ns", _i64),
-        ("start_gate", _p), ("step_kernel", _i), ("moe_peer", _p),
+        ("start_gate", _p), ("step_kernel", _i), ("moe_peer", _p), ("expert_bits", _i), ("group_size", _i),
     ]
 
 

@@ -70,9 +70,25 @@ class DecodeRunner:
         for block in model.MoEBlocks:
             if block.moe.mode == "reference" or not block.moe.direct_configuration_supported(1):
                 return False
-            if block.moe.quantized:  # the step descriptors carry bf16 / fp32 experts only
-                return False
+        if DecodeRunner._quant_format(model) is None:  # quantized layers must share bits and groups
+            return False
         return all(p.dtype == w.dtype and p.device == w.device for p in model.parameters())
+
+    @staticmethod
+    def _quant_format(model):
+        """(bits, group size) of the model's quantized experts, (0, 0) when none
+        is quantized, None when the layers disagree (or only some are)."""
+        fmts = set()
+        for block in model.MoEBlocks:
+            q = getattr(block.moe, "_quant", None)
+            if not q:
+                fmts.add((0, 0))
+                continue
+            f = {(qe.bits, qe.group_size) for qe in q.values()}
+            if len(f) != 1 or set(q) != ({"w1", "w2", "w3"} & set(block.moe._expert_storage)):
+                return None
+            fmts.add(f.pop())
+        return fmts.pop() if len(fmts) == 1 else None
 
     def __init__(self, model, expert_base: int = 0, expert_count: int = 0, moe_partial: bool = False):
         cfg = model.config
@@ -127,7 +143,8 @@ class DecodeRunner:
 
     # ---- descriptors --------------------------------------------------------
     def param_signature(self):
-        return tuple(p.data_ptr() for p in self.model.parameters())
+        quant = tuple(qe.q.data_ptr() for b in self.model.MoEBlocks for qe in (getattr(b.moe, "_quant", None) or {}).values())
+        return tuple(p.data_ptr() for p in self.model.parameters()) + quant
 
     def splits_for(self, max_ctx: int, block_size: int) -> int:
         nblk = -(-max_ctx // block_size)
@@ -158,6 +175,11 @@ class DecodeRunner:
                     return p(t)
                 return t[eb].data_ptr()
             L.w1, L.b1, L.w3, L.w2, L.b2 = (view(s.get(k)) for k in ("w1", "b1", "w3", "w2", "b2"))
+            quant = getattr(moe, "_quant", None)
+            if quant:  # the quantized values and their group scales replace the expert weights
+                L.w1, L.w3, L.w2 = (view(quant[k].q) if k in quant else None for k in ("w1", "w3", "w2"))
+                L.w1_scale, L.w3_scale, L.w2_scale = (view(quant[k].scale) if k in quant else None
+                                                      for k in ("w1", "w3", "w2"))
             k, v, *_ = cache_geometry(cache, i)
             L.k_cache, L.v_cache = k.data_ptr(), v.data_ptr()
         return arr
@@ -219,6 +241,7 @@ class DecodeRunner:
         d.moe_hidden = self.moe_hidden.data_ptr()
         d.moe_partial = None if moe_peer else capi.ptr(self.moe_partial)
         d.moe_peer = moe_peer
+        d.expert_bits, d.group_size = self._quant_format(m) or (0, 0)
         d.expert_base = self.expert_base
         d.expert_count = self.expert_count
         d.attn_partials = self.attn_partials.data_ptr()

@@ -12,8 +12,12 @@ Tolerances:
   error): relative Frobenius error below 2e-2 for int8 and 3e-1 for int4 at
   group 128 on N(0, 0.02) weights (measured: ~0.2 for int4, the cost of 15
   levels per group through two projections);
-* model level: fp32 greedy tokens of the int8 model identical to the oracle's
-  on the dequantized weights.
+* model level: fp32 greedy tokens of the int8 and int4 models (the per-layer
+  launch sequence with the quantized MoE kernel) identical to the oracle's on
+  the dequantized weights; the bf16 model with int8 experts through the
+  persistent cluster step agrees with the per-layer launch sequence on the
+  same quantized weights (hidden states within 5e-3, the bar between the two
+  paths in bf16; greedy tokens identical).
 """
 
 import numpy as np
@@ -148,23 +152,26 @@ def test_quantized_decode_rejects_mixed_or_bad_weights():
         fused_moe.decode(x, r, q8["w1"], None, four, None, w3_base=q8["w3"], **ws)
 
 
-def test_model_int8_experts_fp32_tokens_identical_to_oracle():
-    """A 2-layer BASELINE-architecture model (vocab 512) in fp32 with int8
-    experts: 24 greedy tokens through Model.generate (the per-layer operators
-    with the quantized MoE kernel) equal the oracle's on the dequantized
-    weights."""
+@pytest.mark.parametrize("bits", [8, 4])
+def test_model_quantized_experts_fp32_tokens_identical_to_oracle(bits):
+    """A 2-layer BASELINE-architecture model (vocab 512) in fp32 with int8 or
+    int4 experts: 24 greedy tokens through Model.generate (the per-layer launch
+    sequence with the quantized MoE kernel) equal the oracle's on the
+    dequantized weights."""
     arch = oracle.BASELINE_ARCH.with_(num_layers=2, vocab_size=512)
     P = oracle.init_params(arch, seed=5)
     m = Model(baseline_config(num_layers=2, vocab_size=512)).eval()
     m.load_state_dict(engine_state_dict(P))
-    m = m.to(DEV, torch.float32).quantize_experts(8, 128)
-    assert not m.fused_decode_supported(m.new_cache(), 1)  # quantized: the per-layer operators
+    m = m.to(DEV, torch.float32).quantize_experts(bits, 128)
+    cache = m.new_cache()
+    assert m.fused_decode_supported(cache, 1)
+    assert not m.decode_runner().uses_persistent(cache)  # fp32: the per-layer launch sequence
     Pq = dict(P)
     for i in range(arch.num_layers):
         for name in ("gate", "up", "down"):
             keys = [f"MoEBlocks.{i}.moe.experts.{e}.{name}.weight" for e in range(arch.num_experts)]
             st = torch.stack([P[k] for k in keys]).numpy()
-            q, s = oq.quantize(st, 8, 128)
+            q, s = oq.quantize(st, bits, 128)
             deq = torch.from_numpy(oq.dequantize(q, s, 128))
             for e, k in enumerate(keys):
                 Pq[k] = deq[e]
@@ -174,4 +181,50 @@ def test_model_int8_experts_fp32_tokens_identical_to_oracle():
     assert got == want
     assert np.array_equal(m.MoEBlocks[0].moe._quant["w1"].scale.cpu().numpy(),
                           oq.quantize(torch.stack([P[f"MoEBlocks.0.moe.experts.{e}.gate.weight"]
-                                                   for e in range(arch.num_experts)]).numpy(), 8, 128)[1])
+                                                   for e in range(arch.num_experts)]).numpy(), bits, 128)[1])
+
+
+@pytest.mark.parametrize("group", [128, 32])
+def test_bf16_int8_persistent_step_agrees_with_launch_sequence(group):
+    """The BASELINE model in bf16 with int8 experts: decode steps run the
+    persistent cluster step (int8 rows and their group scales staged by the
+    producer warp) and agree with the per-layer launch sequence (the quantized
+    MoE kernel) on the same weights: hidden states within 5e-3 over 6 steps,
+    40 greedy tokens identical.  int4 experts run the launch sequence."""
+    from moe_engine import capi
+    from tests.helpers import baseline_bf16_model
+
+    m, _, _ = baseline_bf16_model(max_seq=512)
+    m.quantize_experts(8, group)
+    runner = m.decode_runner()
+    assert runner.step_kernel_for(m.new_cache()) == capi.MIE_STEP_CLUSTER
+    prompt = torch.randint(0, 50304, (24,), generator=torch.Generator().manual_seed(9))
+    xs = {}
+    for persistent in (True, False):
+        runner.persistent = persistent
+        cache = m.new_block_allocator(num_blocks=40, block_size=16, attention_mode="direct").new_cache()
+        hs = []
+        with torch.no_grad():
+            m(prompt[None].to(DEV), cache)
+            tok = torch.tensor([[17]], device=DEV)
+            for _ in range(6):
+                logits = m(tok, cache)
+                hs.append(runner.x.clone())
+                tok = logits[0, -1].float().argmax().view(1, 1)
+        xs[persistent] = torch.stack(hs)
+        runner.check_status()
+    runner.persistent = True
+    rel = (xs[True] - xs[False]).norm() / xs[False].norm()
+    assert rel < 5e-3, float(rel)
+    gen = {}
+    for persistent in (True, False):
+        runner.persistent = persistent
+        gen[persistent] = m.generate(prompt, max_new_tokens=40, temperature=0)
+    runner.persistent = True
+    assert torch.equal(gen[True], gen[False])
+    runner.check_status()
+
+    m4, _, _ = baseline_bf16_model(max_seq=512, num_layers=2)
+    m4.quantize_experts(4, group)
+    assert m4.fused_decode_supported(m4.new_cache(), 1)
+    assert m4.decode_runner().step_kernel_for(m4.new_cache()) == 0
