@@ -100,3 +100,21 @@ def test_model_quantize_experts_rewrites_expert_parameters(bits):
         # the per-expert parameters are views of the storage
         e0 = moe.experts[0]
         assert e0.gate.weight.data_ptr() == moe._expert_storage["w1"][0].data_ptr()
+
+
+def test_decode_descriptor_quant_format():
+    """The step descriptors carry one (bits, group) for the whole model: (0, 0)
+    without quantized experts, the shared format when every layer is quantized
+    alike, and no fused decode (None) when layers differ."""
+    from moe_engine.decode import DecodeRunner
+
+    cfg = baseline_config()
+    cfg.num_layers = 2
+    m = Model(cfg).eval()
+    assert DecodeRunner._quant_format(m) == (0, 0)
+    m.quantize_experts(8, 64)
+    assert DecodeRunner._quant_format(m) == (8, 64)
+    m.MoEBlocks[1].moe.quantize_experts(4, 64)
+    assert DecodeRunner._quant_format(m) is None
+    m.MoEBlocks[1].moe._quant = None
+    assert DecodeRunner._quant_format(m) is None
