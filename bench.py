@@ -523,8 +523,12 @@ def run_b200(args, rank, world, device):
             want = [int(t) for t in single_tokens] if rank == 0 else None
             for key, payload, coll in (("step", "fp32", "step"), ("fused", "fp32", "fused"), ("peer", "fp32", "peer"),
                                        ("fp32", "fp32", "nccl"), ("bf16", "bf16", "nccl")):
-                eps[key] = measure_expert_parallel(model, alloc, device, world, max(1, min(args.steps, 2)), 1,
-                                                   payload, want, collective=coll)
+                try:
+                    eps[key] = measure_expert_parallel(model, alloc, device, world, max(1, min(args.steps, 2)), 1,
+                                                       payload, want, collective=coll)
+                except Exception as e:  # one variant's failure is recorded, the replica line stands
+                    eps[key] = {"payload": payload, "collective": coll, "tok_s": None,
+                                "error": f"{type(e).__name__}: {e}"[:300]}
         allreduce = {f"allreduce_us_nccl_{pl}": measure_allreduce(device, pl, model.config.hidden_dim)
                      for pl in ("fp32", "bf16")}
         allreduce["allreduce_us_peer_fp32"] = measure_peer_allreduce(device, model.config.hidden_dim)
